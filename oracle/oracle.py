@@ -1,0 +1,549 @@
+"""ctypes front end of the CPU oracle (test infrastructure only).
+
+The oracle restates the xvec search hot path on the CPU (see
+``oracle/xvec_oracle.cpp``); only ``tests/``, ``__graft_entry__.smoke()`` and
+the CPU-baseline leg of ``bench.py`` import this module, always as the checker
+or the reported baseline, never as a code path of the shipped library.
+
+``ReferenceFloats`` loads the reference's own AVX-512/AVX kernels
+(``internal/floats/src/floats_avx512.c`` and ``floats_avx.c``), compiled in
+place by ``make -C oracle ref`` into ``oracle/_ref/``.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "_build", "libxvec_oracle.so")
+REF_PATH = os.path.join(HERE, "_ref", "libxvec_floats_ref.so")
+
+L2, IP, COSINE, MIPSL2 = 1, 2, 3, 4
+OK, INVALID_ARGUMENT, NON_FINITE, OVERFLOW = 0, 1, 7, 8
+
+_f32p = ctypes.POINTER(ctypes.c_float)
+_f64p = ctypes.POINTER(ctypes.c_double)
+_u64p = ctypes.POINTER(ctypes.c_uint64)
+_i64p = ctypes.POINTER(ctypes.c_int64)
+_i32p = ctypes.POINTER(ctypes.c_int32)
+_u32p = ctypes.POINTER(ctypes.c_uint32)
+_u8p = ctypes.POINTER(ctypes.c_uint8)
+_i8p = ctypes.POINTER(ctypes.c_int8)
+
+
+class SQParams(ctypes.Structure):
+    _fields_ = [("inverse_scale", ctypes.c_float), ("offset", ctypes.c_float),
+                ("code_sum", ctypes.c_double), ("code_square", ctypes.c_double)]
+
+
+SQ_PARAMS_DTYPE = np.dtype([("inverse_scale", "<f4"), ("offset", "<f4"),
+                            ("code_sum", "<f8"), ("code_square", "<f8")])
+
+
+class RaBitQFactors(ctypes.Structure):
+    _fields_ = [("cluster", ctypes.c_int32), ("pad_", ctypes.c_int32),
+                ("coarse_add", ctypes.c_double), ("coarse_rescale", ctypes.c_double),
+                ("coarse_error", ctypes.c_double), ("full_add", ctypes.c_double),
+                ("full_rescale", ctypes.c_double)]
+
+
+RABITQ_FACTORS_DTYPE = np.dtype([("cluster", "<i4"), ("pad_", "<i4"), ("coarse_add", "<f8"),
+                                 ("coarse_rescale", "<f8"), ("coarse_error", "<f8"),
+                                 ("full_add", "<f8"), ("full_rescale", "<f8")])
+
+
+def build(reference: bool = True) -> None:
+    """Compile the restatement and, when the reference checkout exists, its C kernels."""
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    if reference and os.path.isdir(os.environ.get("XVEC_REFERENCE", "/root/reference")):
+        subprocess.run(["make", "-s", "-C", HERE, "ref",
+                        "REFERENCE=" + os.environ.get("XVEC_REFERENCE", "/root/reference")],
+                       check=True)
+
+
+def _ptr(a: np.ndarray | None, typ):
+    if a is None:
+        return None
+    return a.ctypes.data_as(typ)
+
+
+def _c(a, dtype):
+    return np.ascontiguousarray(a, dtype=dtype)
+
+
+class Oracle:
+    def __init__(self, path: str = LIB_PATH):
+        if not os.path.exists(path):
+            build(reference=False)
+        lib = ctypes.CDLL(path)
+        self.lib = lib
+        lib.xo_l2_squared.restype = ctypes.c_float
+        lib.xo_l2_squared.argtypes = [_f32p, _f32p, ctypes.c_int64]
+        lib.xo_inner_product.restype = ctypes.c_float
+        lib.xo_inner_product.argtypes = [_f32p, _f32p, ctypes.c_int64]
+        lib.xo_dot_norms.argtypes = [_f32p, _f32p, ctypes.c_int64, _f32p, _f32p, _f32p]
+        lib.xo_metric_compute.argtypes = [ctypes.c_int, _f32p, _f32p, ctypes.c_int64, _f32p]
+        lib.xo_f32_to_f16.restype = ctypes.c_uint16
+        lib.xo_f32_to_f16.argtypes = [ctypes.c_float]
+        lib.xo_f16_to_f32.restype = ctypes.c_float
+        lib.xo_f16_to_f32.argtypes = [ctypes.c_uint16]
+        search_tail = [_i32p, _u64p, _f32p, _i32p, _i32p]
+        lib.xo_flat_search.argtypes = [ctypes.c_int, _f32p, _u64p, ctypes.c_int64, ctypes.c_int32,
+                                       _f32p, ctypes.c_int32, ctypes.c_int32, ctypes.c_float,
+                                       _u32p, ctypes.c_int32, _u64p, _f32p, _i32p, _i32p]
+        lib.xo_merge_results.restype = ctypes.c_int32
+        lib.xo_merge_results.argtypes = [ctypes.c_int, ctypes.c_int32, _u64p, _f32p,
+                                         ctypes.c_int64, _u64p, _f32p]
+        lib.xo_quantize_int8.argtypes = [_f32p, ctypes.c_int32, _i8p, ctypes.POINTER(SQParams)]
+        lib.xo_quantize_int4.argtypes = [_f32p, ctypes.c_int32, _u8p, ctypes.POINTER(SQParams)]
+        lib.xo_quantized_distance_int8.argtypes = [ctypes.c_int, _i8p, ctypes.POINTER(SQParams),
+                                                   _i8p, ctypes.POINTER(SQParams),
+                                                   ctypes.c_int32, _f32p]
+        lib.xo_refinement_candidate_count.argtypes = [ctypes.c_int32, ctypes.c_float, _i32p]
+        lib.xo_sq8_search.argtypes = [ctypes.c_int, _i8p, ctypes.c_void_p, _f32p, _u64p,
+                                      ctypes.c_int64, ctypes.c_int32, _f32p, ctypes.c_int32,
+                                      ctypes.c_int32, ctypes.c_float, ctypes.c_float, _u32p,
+                                      ctypes.c_int32, _u64p, _f32p, _i32p, _i32p]
+        lib.xo_splitmix64_next.restype = ctypes.c_uint64
+        lib.xo_splitmix64_next.argtypes = [_u64p]
+        lib.xo_kmeans_reservoir.argtypes = [ctypes.c_int64, ctypes.c_int32, ctypes.c_uint64, _i64p]
+        lib.xo_kmeans_assign.argtypes = [ctypes.c_int, _f32p, ctypes.c_int64, _f32p,
+                                         ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _i32p,
+                                         _f32p]
+        lib.xo_kmeans_train.argtypes = [ctypes.c_int, _f32p, ctypes.c_int64, ctypes.c_int32,
+                                        ctypes.c_int32, ctypes.c_int32, ctypes.c_double,
+                                        ctypes.c_uint64, ctypes.c_int32, _f32p, _i32p, _i32p]
+        lib.xo_ivf_probe.restype = ctypes.c_int32
+        lib.xo_ivf_probe.argtypes = [ctypes.c_int, _f32p, ctypes.c_int32, ctypes.c_int32, _f32p,
+                                     ctypes.c_int32, _i32p]
+        lib.xo_ivf_flat_search.argtypes = [ctypes.c_int, _f32p, _u64p, ctypes.c_int64,
+                                           ctypes.c_int32, _f32p, ctypes.c_int32, _i64p, _i64p,
+                                           _f32p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                           ctypes.c_float, _u32p, ctypes.c_int32, _u64p, _f32p,
+                                           _i32p, _i32p]
+        lib.xo_pq_chunk_offsets.argtypes = [ctypes.c_int32, ctypes.c_int32, _i32p]
+        lib.xo_pq_encode.argtypes = [ctypes.c_int, _f32p, _i32p, ctypes.c_int32, ctypes.c_int32,
+                                     _f32p, _u8p]
+        lib.xo_pq_distance_table.argtypes = [ctypes.c_int, _f32p, _i32p, ctypes.c_int32,
+                                             ctypes.c_int32, _f32p, _f32p]
+        lib.xo_pq_lookup.argtypes = [_f32p, ctypes.c_int32, _u8p, _f32p]
+        lib.xo_ivfpq_search.argtypes = [ctypes.c_int, _f32p, ctypes.c_int32, ctypes.c_int32,
+                                        _f32p, _i32p, ctypes.c_int32, _u8p, _u64p, _i64p, _i64p,
+                                        _f32p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                        ctypes.c_float, _u32p, ctypes.c_int32, _u64p, _f32p,
+                                        _i32p, _i32p]
+        lib.xo_fht_rotate.argtypes = [ctypes.c_int32, _u8p, _f32p, _f32p]
+        lib.xo_rabitq_padded_dimension.restype = ctypes.c_int32
+        lib.xo_rabitq_padded_dimension.argtypes = [ctypes.c_int32]
+        lib.xo_rabitq_rotate.argtypes = [ctypes.c_int32, _u8p, _f32p, _f32p]
+        lib.xo_rabitq_quantize.argtypes = [_f32p, _f32p, ctypes.c_int32, ctypes.c_int32,
+                                           ctypes.c_int32, ctypes.c_double, ctypes.c_int32,
+                                           _u8p, _u8p, ctypes.POINTER(RaBitQFactors)]
+        lib.xo_rabitq_encode1.argtypes = [ctypes.c_int, ctypes.c_int32, _f32p, ctypes.c_int32,
+                                          _u8p, _f32p, _u8p, ctypes.POINTER(RaBitQFactors)]
+        lib.xo_rabitq_prepare_query.argtypes = [ctypes.c_int, ctypes.c_int32, _f32p,
+                                                ctypes.c_int32, _u8p, _f32p, _f32p, _f64p, _f64p,
+                                                _f64p]
+        lib.xo_rabitq_estimate_coarse.argtypes = [_f32p, ctypes.c_int32, ctypes.c_double, _f64p,
+                                                  _u8p, ctypes.POINTER(RaBitQFactors), _f32p]
+        lib.xo_rabitq_search.argtypes = [ctypes.c_int, ctypes.c_int32, _f32p, ctypes.c_int32,
+                                         _u8p, _u8p, ctypes.c_void_p, _f32p, _u64p,
+                                         ctypes.c_int64, _f32p, ctypes.c_int32, ctypes.c_int32,
+                                         ctypes.c_int32, ctypes.c_float, _u32p, ctypes.c_int32,
+                                         _u64p, _f32p, _i32p, _i32p]
+        del search_tail
+
+    # ---- distances ---------------------------------------------------------
+    def l2_squared(self, a, b) -> float:
+        a, b = _c(a, np.float32), _c(b, np.float32)
+        return float(np.float32(self.lib.xo_l2_squared(_ptr(a, _f32p), _ptr(b, _f32p), a.size)))
+
+    def inner_product(self, a, b) -> float:
+        a, b = _c(a, np.float32), _c(b, np.float32)
+        return float(np.float32(self.lib.xo_inner_product(_ptr(a, _f32p), _ptr(b, _f32p), a.size)))
+
+    def dot_norms(self, a, b):
+        a, b = _c(a, np.float32), _c(b, np.float32)
+        out = np.zeros(3, np.float32)
+        self.lib.xo_dot_norms(_ptr(a, _f32p), _ptr(b, _f32p), a.size, _ptr(out[0:1], _f32p),
+                              _ptr(out[1:2], _f32p), _ptr(out[2:3], _f32p))
+        return out
+
+    def metric_compute(self, metric: int, a, b):
+        """Returns (status, score) like metric.Compute."""
+        a, b = _c(a, np.float32), _c(b, np.float32)
+        out = np.zeros(1, np.float32)
+        st = self.lib.xo_metric_compute(metric, _ptr(a, _f32p), _ptr(b, _f32p), a.size,
+                                        _ptr(out, _f32p))
+        return st, np.float32(out[0])
+
+    def f32_to_f16(self, values) -> np.ndarray:
+        v = np.asarray(values, np.float32).ravel()
+        return np.array([self.lib.xo_f32_to_f16(float(x)) for x in v], np.uint16)
+
+    def f16_to_f32(self, bits) -> np.ndarray:
+        b = np.asarray(bits, np.uint16).ravel()
+        return np.array([self.lib.xo_f16_to_f32(int(x)) for x in b], np.float32)
+
+    # ---- searches ------------------------------------------------------------
+    @staticmethod
+    def _outs(nq, k):
+        return (np.zeros(nq * k, np.uint64), np.zeros(nq * k, np.float32),
+                np.zeros(nq, np.int32), np.zeros(nq, np.int32))
+
+    def flat_search(self, metric, rows, keys, queries, k, radius=0.0, bitmap=None, threads=0):
+        rows = _c(rows, np.float32)
+        queries = _c(queries, np.float32)
+        keys = _c(keys, np.uint64)
+        n, d = rows.shape
+        nq = queries.shape[0]
+        ok, os_, oc, ost = self._outs(nq, k)
+        bm = None if bitmap is None else _c(bitmap, np.uint32)
+        st = self.lib.xo_flat_search(metric, _ptr(rows, _f32p), _ptr(keys, _u64p), n, d,
+                                     _ptr(queries, _f32p), nq, k, radius, _ptr(bm, _u32p),
+                                     threads or os.cpu_count(), _ptr(ok, _u64p),
+                                     _ptr(os_, _f32p), _ptr(oc, _i32p), _ptr(ost, _i32p))
+        return st, ok.reshape(nq, k), os_.reshape(nq, k), oc, ost
+
+    def merge_results(self, metric, k, keys, scores):
+        keys = _c(keys, np.uint64)
+        scores = _c(scores, np.float32)
+        ok = np.zeros(max(k, 1), np.uint64)
+        os_ = np.zeros(max(k, 1), np.float32)
+        c = self.lib.xo_merge_results(metric, k, _ptr(keys, _u64p), _ptr(scores, _f32p),
+                                      keys.size, _ptr(ok, _u64p), _ptr(os_, _f32p))
+        return ok[:c], os_[:c]
+
+    def quantize_int8(self, v):
+        v = _c(v, np.float32)
+        codes = np.zeros(v.size, np.int8)
+        p = SQParams()
+        st = self.lib.xo_quantize_int8(_ptr(v, _f32p), v.size, _ptr(codes, _i8p), ctypes.byref(p))
+        return st, codes, p
+
+    def quantize_int8_batch(self, rows):
+        rows = _c(rows, np.float32)
+        n, d = rows.shape
+        codes = np.zeros((n, d), np.int8)
+        params = np.zeros(n, SQ_PARAMS_DTYPE)
+        for i in range(n):
+            p = SQParams()
+            st = self.lib.xo_quantize_int8(_ptr(rows[i], _f32p), d, _ptr(codes[i], _i8p),
+                                           ctypes.byref(p))
+            if st != OK:
+                raise ValueError(f"quantize row {i}: status {st}")
+            params[i] = (p.inverse_scale, p.offset, p.code_sum, p.code_square)
+        return codes, params
+
+    def quantize_int4(self, v):
+        v = _c(v, np.float32)
+        packed = np.zeros(v.size // 2, np.uint8)
+        p = SQParams()
+        st = self.lib.xo_quantize_int4(_ptr(v, _f32p), v.size, _ptr(packed, _u8p), ctypes.byref(p))
+        return st, packed, p
+
+    def quantized_distance_int8(self, metric, lcodes, lp, rcodes, rp):
+        lcodes, rcodes = _c(lcodes, np.int8), _c(rcodes, np.int8)
+        out = np.zeros(1, np.float32)
+        st = self.lib.xo_quantized_distance_int8(metric, _ptr(lcodes, _i8p), ctypes.byref(lp),
+                                                 _ptr(rcodes, _i8p), ctypes.byref(rp),
+                                                 lcodes.size, _ptr(out, _f32p))
+        return st, np.float32(out[0])
+
+    def refinement_candidate_count(self, k, scale):
+        out = np.zeros(1, np.int32)
+        st = self.lib.xo_refinement_candidate_count(k, scale, _ptr(out, _i32p))
+        return st, int(out[0])
+
+    def sq8_search(self, metric, codes, params, originals, keys, queries, k, radius=0.0,
+                   refine_scale=0.0, bitmap=None, threads=0):
+        codes = _c(codes, np.int8)
+        params = np.ascontiguousarray(params, SQ_PARAMS_DTYPE)
+        originals = _c(originals, np.float32)
+        keys = _c(keys, np.uint64)
+        queries = _c(queries, np.float32)
+        n, d = codes.shape
+        nq = queries.shape[0]
+        ok, os_, oc, ost = self._outs(nq, k)
+        bm = None if bitmap is None else _c(bitmap, np.uint32)
+        st = self.lib.xo_sq8_search(metric, _ptr(codes, _i8p), params.ctypes.data,
+                                    _ptr(originals, _f32p), _ptr(keys, _u64p), n, d,
+                                    _ptr(queries, _f32p), nq, k, radius, refine_scale,
+                                    _ptr(bm, _u32p), threads or os.cpu_count(), _ptr(ok, _u64p),
+                                    _ptr(os_, _f32p), _ptr(oc, _i32p), _ptr(ost, _i32p))
+        return st, ok.reshape(nq, k), os_.reshape(nq, k), oc, ost
+
+    def splitmix64(self, seed: int, count: int) -> np.ndarray:
+        state = np.array([seed], np.uint64)
+        return np.array([self.lib.xo_splitmix64_next(_ptr(state, _u64p)) for _ in range(count)],
+                        np.uint64)
+
+    def kmeans_reservoir(self, n, clusters, seed):
+        out = np.zeros(clusters, np.int64)
+        self.lib.xo_kmeans_reservoir(n, clusters, seed, _ptr(out, _i64p))
+        return out
+
+    def kmeans_assign(self, metric, vectors, centroids, threads=0):
+        vectors = _c(vectors, np.float32)
+        centroids = _c(centroids, np.float32)
+        n, d = vectors.shape
+        labels = np.zeros(n, np.int32)
+        scores = np.zeros(n, np.float32)
+        st = self.lib.xo_kmeans_assign(metric, _ptr(vectors, _f32p), n, _ptr(centroids, _f32p),
+                                       centroids.shape[0], d, threads or os.cpu_count(),
+                                       _ptr(labels, _i32p), _ptr(scores, _f32p))
+        return st, labels, scores
+
+    def kmeans_train(self, metric, vectors, clusters, iterations=10,
+                     tolerance=1.1920928955078125e-7, seed=0, threads=0):
+        vectors = _c(vectors, np.float32)
+        n, d = vectors.shape
+        cents = np.zeros((clusters, d), np.float32)
+        kc = np.zeros(1, np.int32)
+        labels = np.zeros(n, np.int32)
+        st = self.lib.xo_kmeans_train(metric, _ptr(vectors, _f32p), n, d, clusters, iterations,
+                                      tolerance, seed, threads or os.cpu_count(),
+                                      _ptr(cents, _f32p), _ptr(kc, _i32p), _ptr(labels, _i32p))
+        return st, cents[: int(kc[0])], labels
+
+    def ivf_probe(self, metric, centroids, query, nprobe):
+        centroids = _c(centroids, np.float32)
+        query = _c(query, np.float32)
+        lists = np.zeros(min(nprobe, centroids.shape[0]), np.int32)
+        c = self.lib.xo_ivf_probe(metric, _ptr(centroids, _f32p), centroids.shape[0],
+                                  centroids.shape[1], _ptr(query, _f32p), nprobe,
+                                  _ptr(lists, _i32p))
+        return lists[:c]
+
+    def ivf_flat_search(self, metric, rows, keys, centroids, list_offsets, list_positions,
+                        queries, k, nprobe, radius=0.0, bitmap=None, threads=0):
+        rows = _c(rows, np.float32)
+        keys = _c(keys, np.uint64)
+        centroids = _c(centroids, np.float32)
+        lo = _c(list_offsets, np.int64)
+        lp = _c(list_positions, np.int64)
+        queries = _c(queries, np.float32)
+        n, d = rows.shape
+        nq = queries.shape[0]
+        ok, os_, oc, ost = self._outs(nq, k)
+        bm = None if bitmap is None else _c(bitmap, np.uint32)
+        st = self.lib.xo_ivf_flat_search(metric, _ptr(rows, _f32p), _ptr(keys, _u64p), n, d,
+                                         _ptr(centroids, _f32p), centroids.shape[0],
+                                         _ptr(lo, _i64p), _ptr(lp, _i64p), _ptr(queries, _f32p),
+                                         nq, k, nprobe, radius, _ptr(bm, _u32p),
+                                         threads or os.cpu_count(), _ptr(ok, _u64p),
+                                         _ptr(os_, _f32p), _ptr(oc, _i32p), _ptr(ost, _i32p))
+        return st, ok.reshape(nq, k), os_.reshape(nq, k), oc, ost
+
+    def pq_chunk_offsets(self, d, chunks):
+        out = np.zeros(chunks + 1, np.int32)
+        self.lib.xo_pq_chunk_offsets(d, chunks, _ptr(out, _i32p))
+        return out
+
+    def pq_encode(self, metric, pivots, offsets, v):
+        pivots = _c(pivots, np.float32)
+        offsets = _c(offsets, np.int32)
+        v = _c(v, np.float32)
+        chunks = offsets.size - 1
+        code = np.zeros(chunks, np.uint8)
+        st = self.lib.xo_pq_encode(metric, _ptr(pivots, _f32p), _ptr(offsets, _i32p), chunks,
+                                   v.size, _ptr(v, _f32p), _ptr(code, _u8p))
+        return st, code
+
+    def pq_distance_table(self, metric, pivots, offsets, query):
+        pivots = _c(pivots, np.float32)
+        offsets = _c(offsets, np.int32)
+        query = _c(query, np.float32)
+        chunks = offsets.size - 1
+        table = np.zeros(chunks * 256, np.float32)
+        st = self.lib.xo_pq_distance_table(metric, _ptr(pivots, _f32p), _ptr(offsets, _i32p),
+                                           chunks, query.size, _ptr(query, _f32p),
+                                           _ptr(table, _f32p))
+        return st, table
+
+    def pq_lookup(self, table, code):
+        table = _c(table, np.float32)
+        code = _c(code, np.uint8)
+        out = np.zeros(1, np.float32)
+        st = self.lib.xo_pq_lookup(_ptr(table, _f32p), code.size, _ptr(code, _u8p),
+                                   _ptr(out, _f32p))
+        return st, np.float32(out[0])
+
+    def ivfpq_search(self, metric, centroids, pivots, offsets, codes, keys, list_offsets,
+                     list_positions, queries, k, nprobe, radius=0.0, bitmap=None, threads=0):
+        centroids = _c(centroids, np.float32)
+        pivots = _c(pivots, np.float32)
+        offsets = _c(offsets, np.int32)
+        codes = _c(codes, np.uint8)
+        keys = _c(keys, np.uint64)
+        lo = _c(list_offsets, np.int64)
+        lp = _c(list_positions, np.int64)
+        queries = _c(queries, np.float32)
+        nq, d = queries.shape
+        ok, os_, oc, ost = self._outs(nq, k)
+        bm = None if bitmap is None else _c(bitmap, np.uint32)
+        st = self.lib.xo_ivfpq_search(metric, _ptr(centroids, _f32p), centroids.shape[0], d,
+                                      _ptr(pivots, _f32p), _ptr(offsets, _i32p), offsets.size - 1,
+                                      _ptr(codes, _u8p), _ptr(keys, _u64p), _ptr(lo, _i64p),
+                                      _ptr(lp, _i64p), _ptr(queries, _f32p), nq, k, nprobe,
+                                      radius, _ptr(bm, _u32p), threads or os.cpu_count(),
+                                      _ptr(ok, _u64p), _ptr(os_, _f32p), _ptr(oc, _i32p),
+                                      _ptr(ost, _i32p))
+        return st, ok.reshape(nq, k), os_.reshape(nq, k), oc, ost
+
+    def fht_rotate(self, signs, v):
+        signs = _c(signs, np.uint8)
+        v = _c(v, np.float32)
+        out = np.zeros_like(v)
+        st = self.lib.xo_fht_rotate(v.size, _ptr(signs, _u8p), _ptr(v, _f32p), _ptr(out, _f32p))
+        return st, out
+
+    def rabitq_padded_dimension(self, d):
+        return int(self.lib.xo_rabitq_padded_dimension(d))
+
+    def rabitq_rotate(self, d, signs, v):
+        signs = _c(signs, np.uint8)
+        v = _c(v, np.float32)
+        out = np.zeros(self.rabitq_padded_dimension(d), np.float32)
+        st = self.lib.xo_rabitq_rotate(d, _ptr(signs, _u8p), _ptr(v, _f32p), _ptr(out, _f32p))
+        return st, out
+
+    def rabitq_quantize(self, rotated, rotated_centroid, cluster, total_bits, extra_scale, ip):
+        rotated = _c(rotated, np.float32)
+        rc = _c(rotated_centroid, np.float32)
+        padded = rotated.size
+        binary = np.zeros(padded // 8, np.uint8)
+        extra = np.zeros(max(1, (padded * (total_bits - 1) + 7) // 8), np.uint8)
+        f = RaBitQFactors()
+        st = self.lib.xo_rabitq_quantize(_ptr(rotated, _f32p), _ptr(rc, _f32p), padded, cluster,
+                                         total_bits, extra_scale, int(ip), _ptr(binary, _u8p),
+                                         _ptr(extra, _u8p), ctypes.byref(f))
+        return st, binary, extra[: (padded * (total_bits - 1) + 7) // 8], f
+
+    def rabitq_encode1_batch(self, metric, centroids, signs, rows):
+        centroids = _c(centroids, np.float32)
+        signs = _c(signs, np.uint8)
+        rows = _c(rows, np.float32)
+        n, d = rows.shape
+        padded = self.rabitq_padded_dimension(d)
+        codes = np.zeros((n, padded // 8), np.uint8)
+        factors = np.zeros(n, RABITQ_FACTORS_DTYPE)
+        for i in range(n):
+            f = RaBitQFactors()
+            st = self.lib.xo_rabitq_encode1(metric, d, _ptr(centroids, _f32p), centroids.shape[0],
+                                            _ptr(signs, _u8p), _ptr(rows[i], _f32p),
+                                            _ptr(codes[i], _u8p), ctypes.byref(f))
+            if st != OK:
+                raise ValueError(f"encode row {i}: status {st}")
+            factors[i] = (f.cluster, 0, f.coarse_add, f.coarse_rescale, f.coarse_error,
+                          f.full_add, f.full_rescale)
+        return codes, factors
+
+    def rabitq_prepare_query(self, metric, centroids, signs, query):
+        centroids = _c(centroids, np.float32)
+        signs = _c(signs, np.uint8)
+        query = _c(query, np.float32)
+        d = query.size
+        nc = centroids.shape[0]
+        rot = np.zeros(self.rabitq_padded_dimension(d), np.float32)
+        s = np.zeros(1, np.float64)
+        gadd = np.zeros(nc, np.float64)
+        gerr = np.zeros(nc, np.float64)
+        st = self.lib.xo_rabitq_prepare_query(metric, d, _ptr(centroids, _f32p), nc,
+                                              _ptr(signs, _u8p), _ptr(query, _f32p),
+                                              _ptr(rot, _f32p), _ptr(s, _f64p),
+                                              _ptr(gadd, _f64p), _ptr(gerr, _f64p))
+        return st, rot, float(s[0]), gadd, gerr
+
+    def rabitq_estimate_coarse(self, rotated, qsum, gadd, code, factors_row):
+        rotated = _c(rotated, np.float32)
+        gadd = _c(gadd, np.float64)
+        code = _c(code, np.uint8)
+        f = RaBitQFactors(int(factors_row["cluster"]), 0, float(factors_row["coarse_add"]),
+                          float(factors_row["coarse_rescale"]), float(factors_row["coarse_error"]),
+                          float(factors_row["full_add"]), float(factors_row["full_rescale"]))
+        out = np.zeros(1, np.float32)
+        st = self.lib.xo_rabitq_estimate_coarse(_ptr(rotated, _f32p), rotated.size, qsum,
+                                                _ptr(gadd, _f64p), _ptr(code, _u8p),
+                                                ctypes.byref(f), _ptr(out, _f32p))
+        return st, np.float32(out[0])
+
+    def rabitq_search(self, metric, centroids, signs, codes, factors, originals, keys, queries,
+                      k, candidate_count, radius=0.0, bitmap=None, threads=0):
+        centroids = _c(centroids, np.float32)
+        signs = _c(signs, np.uint8)
+        codes = _c(codes, np.uint8)
+        factors = np.ascontiguousarray(factors, RABITQ_FACTORS_DTYPE)
+        originals = _c(originals, np.float32)
+        keys = _c(keys, np.uint64)
+        queries = _c(queries, np.float32)
+        n, d = originals.shape
+        nq = queries.shape[0]
+        ok, os_, oc, ost = self._outs(nq, k)
+        bm = None if bitmap is None else _c(bitmap, np.uint32)
+        st = self.lib.xo_rabitq_search(metric, d, _ptr(centroids, _f32p), centroids.shape[0],
+                                       _ptr(signs, _u8p), _ptr(codes, _u8p), factors.ctypes.data,
+                                       _ptr(originals, _f32p), _ptr(keys, _u64p), n,
+                                       _ptr(queries, _f32p), nq, k, candidate_count, radius,
+                                       _ptr(bm, _u32p), threads or os.cpu_count(),
+                                       _ptr(ok, _u64p), _ptr(os_, _f32p), _ptr(oc, _i32p),
+                                       _ptr(ost, _i32p))
+        return st, ok.reshape(nq, k), os_.reshape(nq, k), oc, ost
+
+
+class ReferenceFloats:
+    """The reference's own float kernels (floats_avx512.c / floats_avx.c) from oracle/_ref."""
+
+    def __init__(self, path: str = REF_PATH):
+        lib = ctypes.CDLL(path)
+        self.lib = lib
+        for name in ("xvec_avx512_l2_squared", "xvec_avx512_inner_product",
+                     "xvec_avx_l2_squared", "xvec_avx_inner_product"):
+            getattr(lib, name).argtypes = [_f32p, _f32p, ctypes.c_int64, _f32p]
+        for name in ("xvec_avx512_dot_norms", "xvec_avx_dot_norms"):
+            getattr(lib, name).argtypes = [_f32p, _f32p, ctypes.c_int64, _f32p, _f32p, _f32p]
+
+    @staticmethod
+    def available() -> bool:
+        if not os.path.exists(REF_PATH):
+            return False
+        try:
+            with open("/proc/cpuinfo") as f:
+                flags = f.read()
+        except OSError:
+            return False
+        return "avx512f" in flags and " fma" in flags
+
+    def _binary(self, name, a, b):
+        a, b = _c(a, np.float32), _c(b, np.float32)
+        out = np.zeros(1, np.float32)
+        getattr(self.lib, name)(_ptr(a, _f32p), _ptr(b, _f32p), a.size, _ptr(out, _f32p))
+        return np.float32(out[0])
+
+    def l2_squared(self, a, b):
+        """Go dispatch (floats_amd64.go:59-91) over the reference kernels."""
+        a = np.asarray(a, np.float32)
+        if a.size >= 16:
+            return self._binary("xvec_avx512_l2_squared", a, b)
+        if a.size >= 8:
+            return self._binary("xvec_avx_l2_squared", a, b)
+        return None
+
+    def inner_product(self, a, b):
+        a = np.asarray(a, np.float32)
+        if a.size >= 16:
+            return self._binary("xvec_avx512_inner_product", a, b)
+        if a.size >= 8:
+            return self._binary("xvec_avx_inner_product", a, b)
+        return None
+
+    def dot_norms(self, a, b):
+        a, b = _c(a, np.float32), _c(b, np.float32)
+        name = "xvec_avx512_dot_norms" if a.size >= 16 else "xvec_avx_dot_norms"
+        out = np.zeros(3, np.float32)
+        getattr(self.lib, name)(_ptr(a, _f32p), _ptr(b, _f32p), a.size, _ptr(out[0:1], _f32p),
+                                _ptr(out[1:2], _f32p), _ptr(out[2:3], _f32p))
+        return out
