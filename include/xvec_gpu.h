@@ -1,0 +1,211 @@
+/*
+ * xvec_gpu.h — C ABI of the B200 (sm_100a) search library for xvec.
+ *
+ * This is the boundary a cgo shim binds.  It takes plain
+ * pointers and sizes only.  Each entry point names the reference interface it
+ * replaces, by file:line in the gorse-io/xvec module.
+ *
+ * Conventions
+ *   - Keys are uint64 (internal/core/topk.go:47-50, Result.Key); scores are
+ *     float32 (Result.Score).  Results are best-first; ties are broken by the
+ *     ascending key (resultBetter, internal/core/topk.go:271-276).
+ *   - Metric values equal core.Metric (internal/core/metric/metric.go:26-31).
+ *   - "host" entry points take host memory and copy it themselves; the
+ *     *_device variants take device memory on the index's device and enqueue
+ *     on the caller's stream.  The library never keeps a caller pointer after
+ *     a call returns.
+ *   - Every entry point returns an xvec_gpu_status; xvec_gpu_last_error()
+ *     returns the message of the calling thread's last failure.  Nothing in
+ *     the library aborts or exits the process.
+ *   - Batched searches fill every query they can: out_counts[q] >= 0 is the
+ *     number of results of query q, out_counts[q] < 0 is -(status) of a query
+ *     that failed on its own (for example a non-finite query vector, like the
+ *     per-query error of core.BatchTopK, internal/core/topk.go:257-262); the
+ *     call then returns the first failing query's status.
+ */
+#ifndef XVEC_GPU_H
+#define XVEC_GPU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define XVEC_GPU_ABI_VERSION 1
+
+typedef enum {
+  XVEC_GPU_OK = 0,
+  XVEC_GPU_INVALID_ARGUMENT = 1, /* ErrInvalidTopK, ErrInvalidRadius, ErrInvalidDimension, ... */
+  XVEC_GPU_OUT_OF_MEMORY = 2,
+  XVEC_GPU_CANCELLED = 3,        /* the caller's cancel flag was set (ctx.Err()) */
+  XVEC_GPU_TIMEOUT = 4,          /* a bounded device-side wait gave up */
+  XVEC_GPU_CUDA_ERROR = 5,
+  XVEC_GPU_NCCL_ERROR = 6,
+  XVEC_GPU_NON_FINITE = 7,       /* mathutil.ErrNonFiniteVector */
+  XVEC_GPU_OVERFLOW = 8,         /* ErrQuantizationOverflow / ErrPQScoreOverflow */
+  XVEC_GPU_NOT_FOUND = 9,        /* ErrMissingRefineVector */
+  XVEC_GPU_DUPLICATE_KEY = 10,   /* ErrDuplicateKey */
+  XVEC_GPU_UNSUPPORTED = 11      /* no sm_100a device / feature not available */
+} xvec_gpu_status;
+
+typedef enum {
+  XVEC_METRIC_L2 = 1,
+  XVEC_METRIC_IP = 2,
+  XVEC_METRIC_COSINE = 3,
+  XVEC_METRIC_MIPSL2 = 4
+} xvec_gpu_metric;
+
+typedef enum {
+  /* Dense Flat exact search: core.DenseFlatIndex (internal/core/flat.go:70-196). */
+  XVEC_INDEX_FLAT = 1,
+  /* INT8 scalar-quantized Flat: core.ScalarQuantizedFlatIndex
+   * (internal/core/quantized_index.go:28-120, quantization.go:267-321). */
+  XVEC_INDEX_SQ8_FLAT = 2,
+  /* IVF list scan over 8-bit PQ codes: probedListsLocked (internal/core/ivf.go:524-561)
+   * + PQDistanceTable.Lookup (internal/core/pq.go:549-595). */
+  XVEC_INDEX_IVF_PQ = 3,
+  /* One-bit RaBitQ linear scan + exact refine (internal/core/hnsw_rabitq.go:539-642,
+   * 780-801; internal/core/rabitq.go:372-430). */
+  XVEC_INDEX_RABITQ = 4
+} xvec_gpu_index_kind;
+
+typedef enum {
+  XVEC_STORAGE_FP32 = 1, /* rows and queries are float32 */
+  XVEC_STORAGE_FP16 = 2  /* rows and queries are IEEE binary16 bit patterns (uint16);
+                            the arithmetic is float32 on the decoded values, as for a
+                            VectorFP16 field (collection.go:4607-4613) or QuantizationFP16
+                            (quantization.go:187-191) */
+} xvec_gpu_storage;
+
+typedef struct xvec_gpu_index xvec_gpu_index;
+
+typedef struct {
+  int32_t kind;      /* xvec_gpu_index_kind */
+  int32_t dimension; /* > 0 (ErrInvalidDimension, flat.go:84-86) */
+  int32_t metric;    /* xvec_gpu_metric; IVF_PQ: L2 or IP (pq.go:67-70); RABITQ: L2/IP/COSINE */
+  int32_t storage;   /* FLAT only: xvec_gpu_storage; others use float32 input */
+  int32_t device;    /* CUDA device ordinal */
+  int32_t reserved[3];
+} xvec_gpu_index_desc;
+
+typedef struct {
+  int32_t top_k;            /* SearchOptions.TopK, > 0 (query.go:47-55) */
+  float radius;             /* SearchOptions.Radius, 0 = off (query.go:193-201) */
+  int32_t nprobe;           /* IVFSearchOptions.NProbe (ivf.go:387-400); IVF_PQ only */
+  float refine_scale;       /* > 0: UseRefiner with QueryParams.ScaleFactor
+                               (collection.go:1606-1631, refiner.go:112-129).
+                               SQ8_FLAT: exact fp32 rerank of floor(top_k*scale) codes.
+                               RABITQ: number of estimates refined = floor(top_k*scale)
+                               (>= top_k). */
+  const uint32_t* filter_bitmap; /* NULL = no filter.  Bit p (word p/32, bit p%32) set =
+                                    the row at insertion position p passes
+                                    CandidateFilter (query.go:35); evaluated before
+                                    scoring.  Host memory for xvec_gpu_index_search,
+                                    device memory for the _device variant. */
+  int64_t filter_words;     /* number of uint32 words in filter_bitmap */
+  void* stream;             /* cudaStream_t for the _device variants; NULL = the
+                               legacy default stream */
+  const volatile int32_t* cancel_flag; /* optional host flag, polled between kernel
+                                          launches; non-zero => XVEC_GPU_CANCELLED */
+} xvec_gpu_search_opts;
+
+/* Library ------------------------------------------------------------------ */
+int32_t xvec_gpu_abi_version(void);
+/* Copies the calling thread's last error message; returns its full length. */
+size_t xvec_gpu_last_error(char* buffer, size_t length);
+/* Number of CUDA devices the library can use (compute capability 10.0). */
+int32_t xvec_gpu_device_count(void);
+
+/* Index lifecycle ------------------------------------------------------------
+ * Replaces core.NewDenseFlatIndex (flat.go:79-93), NewScalarQuantizedFlatIndex
+ * (quantized_index.go:33-60), NewIVFBuilder (ivf.go:95-107) and
+ * RestoreRaBitQModel (rabitq.go:189-241) at the collection's index
+ * construction (collection.go:657-818). */
+xvec_gpu_status xvec_gpu_index_create(const xvec_gpu_index_desc* desc, xvec_gpu_index** out);
+xvec_gpu_status xvec_gpu_index_destroy(xvec_gpu_index* index);
+int64_t xvec_gpu_index_len(const xvec_gpu_index* index);
+
+/* Appends n rows at positions len..len+n-1 (DenseFlatIndex.Add, flat.go:122-153;
+ * batch form).  rows: n*dimension float32, or uint16 for FP16 storage.  Keys
+ * must be unique (XVEC_GPU_DUPLICATE_KEY); rows must be finite
+ * (XVEC_GPU_NON_FINITE).  SQ8_FLAT quantizes each row per vector with the
+ * reference INT8 rule and keeps the float32 row for refinement; IVF_PQ
+ * assigns each row to its best list and PQ-encodes it (requires the model);
+ * RABITQ encodes each row with the one-bit quantizer (requires the model). */
+xvec_gpu_status xvec_gpu_index_add(xvec_gpu_index* index, const uint64_t* keys, const void* rows,
+                                   int64_t n);
+xvec_gpu_status xvec_gpu_index_add_device(xvec_gpu_index* index, const uint64_t* d_keys,
+                                          const void* d_rows, int64_t n, void* stream);
+
+/* IVF-PQ model: IVF centroids [nlist*dimension] (KMeansModel centroids,
+ * ivf.go:193-201) and the PQ codebook in PQModelState layout (pq.go:86-94):
+ * pivots [256*dimension], centroid-major, split into `chunks` contiguous chunks
+ * by pqChunkOffsets (pq.go:395-406). */
+xvec_gpu_status xvec_gpu_ivfpq_set_model(xvec_gpu_index* index, const float* centroids,
+                                         int32_t nlist, const float* pivots, int32_t chunks);
+
+/* RaBitQ model (RaBitQModelState, rabitq.go:96-103) with TotalBits = 1:
+ * centroids [nclusters*dimension] and rotation signs
+ * [4 * roundUp64(dimension) / 8] bytes. */
+xvec_gpu_status xvec_gpu_rabitq_set_model(xvec_gpu_index* index, const float* centroids,
+                                          int32_t nclusters, const uint8_t* rotation_signs);
+
+/* Batched search: queries [nq*dimension] (float32, or uint16 for FP16 storage).
+ * out_keys / out_scores: nq*top_k (slots past out_counts[q] are unspecified).
+ * Replaces DenseQuerySearcher.SearchWithOptions (query.go:58-61) per query,
+ * batched like core.BatchTopK (topk.go:242-269): FLAT → flat.go:175-196;
+ * SQ8_FLAT → quantized_index.go:113-120 (+ OriginalVectorRefiner.Refine,
+ * refiner.go:66-108, when refine_scale > 0); IVF_PQ → the IVF SearchIVF flow
+ * (ivf.go:423-493) scoring PQ codes; RABITQ → hnsw_rabitq.go:539-586 with a
+ * linear scan and Refine. */
+xvec_gpu_status xvec_gpu_index_search(xvec_gpu_index* index, const void* queries, int32_t nq,
+                                      const xvec_gpu_search_opts* opts, uint64_t* out_keys,
+                                      float* out_scores, int32_t* out_counts);
+xvec_gpu_status xvec_gpu_index_search_device(xvec_gpu_index* index, const void* d_queries,
+                                             int32_t nq, const xvec_gpu_search_opts* opts,
+                                             uint64_t* d_out_keys, float* d_out_scores,
+                                             int32_t* d_out_counts);
+
+/* k-means assignment: assignKMeans / assignKMeansCosine (kmeans.go:382-479):
+ * for each vector the metric-best centroid (lower index wins ties) and its
+ * score.  vectors [n*dim], centroids [nc*dim]; labels/scores [n]. */
+xvec_gpu_status xvec_gpu_kmeans_assign(int32_t device, int32_t metric, const float* vectors,
+                                       int64_t n, const float* centroids, int32_t nc, int32_t dim,
+                                       int32_t* labels, float* scores);
+xvec_gpu_status xvec_gpu_kmeans_assign_device(int32_t device, int32_t metric,
+                                              const float* d_vectors, int64_t n,
+                                              const float* d_centroids, int32_t nc, int32_t dim,
+                                              int32_t* d_labels, float* d_scores, void* stream);
+
+/* Cross-shard merge: MergeSearchResults (query.go:154-191) of `parts` result
+ * lists per query, as produced by xvec_gpu_index_search_device on each shard
+ * (layout [parts][nq][top_k] keys/scores and [parts][nq] counts, all device
+ * memory).  Writes the best top_k per query.  Used after the NCCL allgather of
+ * the multi-GPU search. */
+xvec_gpu_status xvec_gpu_merge_results_device(int32_t device, int32_t metric, int32_t top_k,
+                                              int32_t nq, int32_t parts, const uint64_t* d_keys,
+                                              const float* d_scores, const int32_t* d_counts,
+                                              uint64_t* d_out_keys, float* d_out_scores,
+                                              int32_t* d_out_counts, void* stream);
+
+/* Counters (the reference's RuntimeStats role, collection.go:5185-5315, for
+ * the device path).  Device-time fields are filled only while timing is
+ * enabled, because timing adds an event pair around each scan launch. */
+typedef struct {
+  int64_t searches;        /* search calls completed */
+  int64_t queries;         /* queries answered */
+  int64_t kernel_launches; /* kernels launched by this library (all devices) */
+  int64_t exact_queries;   /* queries answered through the exact (reference-order) scan */
+  double scan_ms;          /* device time of the candidate scan kernels */
+  double search_ms;        /* device time of whole search calls */
+} xvec_gpu_stats;
+void xvec_gpu_stats_enable_timing(int32_t enabled);
+void xvec_gpu_get_stats(xvec_gpu_stats* out);
+void xvec_gpu_reset_stats(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* XVEC_GPU_H */

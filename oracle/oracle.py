@@ -155,6 +155,20 @@ class Oracle:
                                          ctypes.c_int32, ctypes.c_float, _u32p, ctypes.c_int32,
                                          _u64p, _f32p, _i32p, _i32p]
         del search_tail
+        lib.xo_use_reference_kernels.argtypes = [ctypes.c_void_p] * 6
+        self.kernels = "restated"
+
+    def use_reference_kernels(self, ref: "ReferenceFloats | None") -> None:
+        """Dispatch the distance kernels to the reference's compiled C (or back)."""
+        if ref is None:
+            self.lib.xo_use_reference_kernels(None, None, None, None, None, None)
+            self.kernels = "restated"
+            return
+        names = ("xvec_avx512_l2_squared", "xvec_avx512_inner_product", "xvec_avx512_dot_norms",
+                 "xvec_avx_l2_squared", "xvec_avx_inner_product", "xvec_avx_dot_norms")
+        ptrs = [ctypes.cast(getattr(ref.lib, n), ctypes.c_void_p).value for n in names]
+        self.lib.xo_use_reference_kernels(*ptrs)
+        self.kernels = "reference"
 
     # ---- distances ---------------------------------------------------------
     def l2_squared(self, a, b) -> float:

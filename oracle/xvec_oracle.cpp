@@ -157,24 +157,64 @@ void dn_avx512(const float* a, const float* b, int64_t n, float* dot, float* ln,
   *rn = r;
 }
 
+// Optional: the reference's own compiled kernels (oracle/_ref), installed by
+// xo_use_reference_kernels; they produce the same bits as the restatement
+// above (tests/test_oracle_golden.py checks it) and are what the CPU
+// baseline times.
+typedef void (*binary_kernel)(float*, float*, int64_t, float*);
+typedef void (*products_kernel)(float*, float*, int64_t, float*, float*, float*);
+binary_kernel g_ref_l2_512 = nullptr, g_ref_ip_512 = nullptr, g_ref_l2_256 = nullptr,
+              g_ref_ip_256 = nullptr;
+products_kernel g_ref_dn_512 = nullptr, g_ref_dn_256 = nullptr;
+
 }  // namespace
+
+extern "C" void xo_use_reference_kernels(void* l2_512, void* ip_512, void* dn_512, void* l2_256,
+                                         void* ip_256, void* dn_256) {
+  g_ref_l2_512 = (binary_kernel)l2_512;
+  g_ref_ip_512 = (binary_kernel)ip_512;
+  g_ref_dn_512 = (products_kernel)dn_512;
+  g_ref_l2_256 = (binary_kernel)l2_256;
+  g_ref_ip_256 = (binary_kernel)ip_256;
+  g_ref_dn_256 = (products_kernel)dn_256;
+}
 
 // floats_amd64.go:27-91 on an AVX-512F+FMA host: >=16 → AVX-512 kernel,
 // >=8 → AVX kernel, otherwise the scalar Go loop.
 extern "C" float xo_l2_squared(const float* a, const float* b, int64_t n) {
-  if (n >= 16) return l2_avx512(a, b, n);
-  if (n >= 8) return l2_avx(a, b, n);
+  float r;
+  if (n >= 16) {
+    if (g_ref_l2_512) return g_ref_l2_512((float*)a, (float*)b, n, &r), r;
+    return l2_avx512(a, b, n);
+  }
+  if (n >= 8) {
+    if (g_ref_l2_256) return g_ref_l2_256((float*)a, (float*)b, n, &r), r;
+    return l2_avx(a, b, n);
+  }
   return l2_scalar(a, b, n);
 }
 extern "C" float xo_inner_product(const float* a, const float* b, int64_t n) {
-  if (n >= 16) return ip_avx512(a, b, n);
-  if (n >= 8) return ip_avx(a, b, n);
+  float r;
+  if (n >= 16) {
+    if (g_ref_ip_512) return g_ref_ip_512((float*)a, (float*)b, n, &r), r;
+    return ip_avx512(a, b, n);
+  }
+  if (n >= 8) {
+    if (g_ref_ip_256) return g_ref_ip_256((float*)a, (float*)b, n, &r), r;
+    return ip_avx(a, b, n);
+  }
   return ip_scalar(a, b, n);
 }
 extern "C" void xo_dot_norms(const float* a, const float* b, int64_t n, float* dot, float* ln,
                              float* rn) {
-  if (n >= 16) return dn_avx512(a, b, n, dot, ln, rn);
-  if (n >= 8) return dn_avx(a, b, n, dot, ln, rn);
+  if (n >= 16) {
+    if (g_ref_dn_512) return g_ref_dn_512((float*)a, (float*)b, n, dot, ln, rn);
+    return dn_avx512(a, b, n, dot, ln, rn);
+  }
+  if (n >= 8) {
+    if (g_ref_dn_256) return g_ref_dn_256((float*)a, (float*)b, n, dot, ln, rn);
+    return dn_avx(a, b, n, dot, ln, rn);
+  }
   return dn_scalar(a, b, n, dot, ln, rn);
 }
 

@@ -10,7 +10,7 @@
  * Parity pin: the restatement is checked against (a) the reference's own
  * known-answer tests (tests/golden/) and (b) the reference's AVX-512/AVX C
  * kernels (internal/floats/src/floats_avx512.c, floats_avx.c) compiled in
- * place into oracle/_ref/ by oracle/build_ref.sh.
+ * place into oracle/_ref/ by `make -C oracle ref`.
  */
 #ifndef XVEC_ORACLE_H
 #define XVEC_ORACLE_H
@@ -35,6 +35,11 @@ enum {
 enum { XO_L2 = 1, XO_IP = 2, XO_COSINE = 3, XO_MIPSL2 = 4 };
 
 /* ---- internal/floats: dispatch of floats_amd64.go:27-91 ---------------- */
+/* Routes the >=16 (AVX-512) and >=8 (AVX) cases to the reference's own
+ * compiled kernels (function pointers from oracle/_ref); NULLs restore the
+ * restatement. */
+void xo_use_reference_kernels(void* l2_512, void* ip_512, void* dn_512, void* l2_256,
+                              void* ip_256, void* dn_256);
 float xo_l2_squared(const float* left, const float* right, int64_t n);
 float xo_inner_product(const float* left, const float* right, int64_t n);
 void xo_dot_norms(const float* left, const float* right, int64_t n, float* dot,

@@ -238,3 +238,20 @@ def test_merge_results_order_independent(oracle):
     perm = rng.permutation(200)
     b = oracle.merge_results(L2, 15, keys[perm], scores[perm])
     assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1])
+
+
+@pytest.mark.skipif(not ReferenceFloats.available(), reason="reference kernels not built or no AVX-512")
+def test_flat_search_same_with_reference_kernels():
+    from oracle.oracle import Oracle
+    ora = Oracle()
+    rng = np.random.default_rng(8)
+    rows = rng.standard_normal((800, 96)).astype(np.float32)
+    keys = np.arange(800, dtype=np.uint64)
+    q = rng.standard_normal((5, 96)).astype(np.float32)
+    a = ora.flat_search(COSINE, rows, keys, q, 10)
+    ora.use_reference_kernels(ReferenceFloats())
+    try:
+        b = ora.flat_search(COSINE, rows, keys, q, 10)
+    finally:
+        ora.use_reference_kernels(None)
+    assert np.array_equal(a[1], b[1]) and np.array_equal(a[2], b[2])

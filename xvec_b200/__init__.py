@@ -1,0 +1,330 @@
+"""xvec_b200 — Python host binding of the B200 (sm_100a) xvec search library.
+
+The compute lives in ``libxvec_gpu.so`` (CUDA kernels + the C ABI declared in
+``include/xvec_gpu.h``).  This module mirrors the reference's Go interfaces for
+the search path so that tests read like the reference's own:
+
+  reference (gorse-io/xvec)                      here
+  ---------------------------------------------  --------------------------------
+  core.NewDenseFlatIndex / Add / SearchWithOptions  DenseFlatIndex (flat.go:79-196)
+  core.NewScalarQuantizedFlatIndex (INT8)        ScalarQuantizedFlatIndex
+                                                 (quantized_index.go:33-120)
+  IVF SearchIVF over PQ codes                    IVFPQIndex (ivf.go:423-493, pq.go:549-595)
+  HNSW-RaBitQ linear scan + Refine               RaBitQIndex (hnsw_rabitq.go:539-642)
+  core.SearchOptions {TopK, Radius, Filter}      SearchOptions (query.go:39-55)
+  core.Result {Key, Score}                       Result / ndarray pairs (topk.go:47-50)
+  assignKMeans                                   kmeans_assign (kmeans.go:382-479)
+  core.MergeSearchResults                        merge_results_device (query.go:154-191)
+
+There is no CPU fallback: importing this module fails if the shared library is
+missing, and every search runs on a CUDA device.
+"""
+from __future__ import annotations
+
+import ctypes
+import dataclasses
+import os
+from typing import Callable, Iterable, Optional, Sequence
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libxvec_gpu.so")
+
+METRIC_L2, METRIC_IP, METRIC_COSINE, METRIC_MIPSL2 = 1, 2, 3, 4
+INDEX_FLAT, INDEX_SQ8_FLAT, INDEX_IVF_PQ, INDEX_RABITQ = 1, 2, 3, 4
+STORAGE_FP32, STORAGE_FP16 = 1, 2
+
+STATUS_NAMES = {
+    0: "OK", 1: "INVALID_ARGUMENT", 2: "OUT_OF_MEMORY", 3: "CANCELLED", 4: "TIMEOUT",
+    5: "CUDA_ERROR", 6: "NCCL_ERROR", 7: "NON_FINITE", 8: "OVERFLOW", 9: "NOT_FOUND",
+    10: "DUPLICATE_KEY", 11: "UNSUPPORTED",
+}
+OK, INVALID_ARGUMENT, NON_FINITE, DUPLICATE_KEY, UNSUPPORTED, CANCELLED = 0, 1, 7, 10, 11, 3
+
+# Entry points of include/xvec_gpu.h (checked by the CPU test suite).
+EXPORTED_SYMBOLS = (
+    "xvec_gpu_abi_version", "xvec_gpu_last_error", "xvec_gpu_device_count",
+    "xvec_gpu_index_create", "xvec_gpu_index_destroy", "xvec_gpu_index_len",
+    "xvec_gpu_index_add", "xvec_gpu_index_add_device", "xvec_gpu_ivfpq_set_model",
+    "xvec_gpu_rabitq_set_model", "xvec_gpu_index_search", "xvec_gpu_index_search_device",
+    "xvec_gpu_kmeans_assign", "xvec_gpu_kmeans_assign_device", "xvec_gpu_merge_results_device",
+    "xvec_gpu_stats_enable_timing", "xvec_gpu_get_stats", "xvec_gpu_reset_stats",
+)
+
+
+class XvecGPUError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{STATUS_NAMES.get(status, status)}: {message}")
+        self.status = status
+
+
+class IndexDesc(ctypes.Structure):
+    _fields_ = [("kind", ctypes.c_int32), ("dimension", ctypes.c_int32),
+                ("metric", ctypes.c_int32), ("storage", ctypes.c_int32),
+                ("device", ctypes.c_int32), ("reserved", ctypes.c_int32 * 3)]
+
+
+class SearchOpts(ctypes.Structure):
+    _fields_ = [("top_k", ctypes.c_int32), ("radius", ctypes.c_float),
+                ("nprobe", ctypes.c_int32), ("refine_scale", ctypes.c_float),
+                ("filter_bitmap", ctypes.c_void_p), ("filter_words", ctypes.c_int64),
+                ("stream", ctypes.c_void_p), ("cancel_flag", ctypes.c_void_p)]
+
+
+class Stats(ctypes.Structure):
+    _fields_ = [("searches", ctypes.c_int64), ("queries", ctypes.c_int64),
+                ("kernel_launches", ctypes.c_int64), ("exact_queries", ctypes.c_int64),
+                ("scan_ms", ctypes.c_double), ("search_ms", ctypes.c_double)]
+
+
+def _load() -> ctypes.CDLL:
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"{LIB_PATH} is missing: run `python -m xvec_b200.build` "
+                          "(or __graft_entry__.build()) first")
+    lib = ctypes.CDLL(LIB_PATH)
+    vp, i32, i64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64
+    lib.xvec_gpu_abi_version.restype = i32
+    lib.xvec_gpu_last_error.restype = ctypes.c_size_t
+    lib.xvec_gpu_last_error.argtypes = [ctypes.c_char_p, ctypes.c_size_t]
+    lib.xvec_gpu_device_count.restype = i32
+    lib.xvec_gpu_index_create.argtypes = [ctypes.POINTER(IndexDesc), ctypes.POINTER(vp)]
+    lib.xvec_gpu_index_destroy.argtypes = [vp]
+    lib.xvec_gpu_index_len.restype = i64
+    lib.xvec_gpu_index_len.argtypes = [vp]
+    lib.xvec_gpu_index_add.argtypes = [vp, vp, vp, i64]
+    lib.xvec_gpu_index_add_device.argtypes = [vp, vp, vp, i64, vp]
+    lib.xvec_gpu_ivfpq_set_model.argtypes = [vp, vp, i32, vp, i32]
+    lib.xvec_gpu_rabitq_set_model.argtypes = [vp, vp, i32, vp]
+    lib.xvec_gpu_index_search.argtypes = [vp, vp, i32, ctypes.POINTER(SearchOpts), vp, vp, vp]
+    lib.xvec_gpu_index_search_device.argtypes = [vp, vp, i32, ctypes.POINTER(SearchOpts), vp,
+                                                 vp, vp]
+    lib.xvec_gpu_kmeans_assign.argtypes = [i32, i32, vp, i64, vp, i32, i32, vp, vp]
+    lib.xvec_gpu_kmeans_assign_device.argtypes = [i32, i32, vp, i64, vp, i32, i32, vp, vp, vp]
+    lib.xvec_gpu_merge_results_device.argtypes = [i32, i32, i32, i32, i32, vp, vp, vp, vp, vp,
+                                                  vp, vp]
+    lib.xvec_gpu_stats_enable_timing.argtypes = [i32]
+    lib.xvec_gpu_get_stats.argtypes = [ctypes.POINTER(Stats)]
+    for name in EXPORTED_SYMBOLS:
+        if not hasattr(lib, name):
+            raise ImportError(f"{LIB_PATH} does not export {name}")
+    return lib
+
+
+_lib = _load()
+
+
+def library() -> ctypes.CDLL:
+    return _lib
+
+
+def last_error() -> str:
+    buf = ctypes.create_string_buffer(1024)
+    _lib.xvec_gpu_last_error(buf, 1024)
+    return buf.value.decode(errors="replace")
+
+
+def _check(status: int) -> None:
+    if status != OK:
+        raise XvecGPUError(status, last_error())
+
+
+def stats() -> dict:
+    """xvec_gpu_get_stats as a dict (kernel launches, queries, device ms)."""
+    st = Stats()
+    _lib.xvec_gpu_get_stats(ctypes.byref(st))
+    return {name: getattr(st, name) for name, _ in Stats._fields_}
+
+
+def reset_stats() -> None:
+    _lib.xvec_gpu_reset_stats()
+
+
+def enable_timing(on: bool = True) -> None:
+    _lib.xvec_gpu_stats_enable_timing(1 if on else 0)
+
+
+def device_count() -> int:
+    return int(_lib.xvec_gpu_device_count())
+
+
+def _ptr(a: Optional[np.ndarray]):
+    return None if a is None else a.ctypes.data
+
+
+@dataclasses.dataclass
+class SearchOptions:
+    """core.SearchOptions (internal/core/query.go:39-55) plus the IVF/refine knobs."""
+    top_k: int
+    radius: float = 0.0
+    filter: Optional[np.ndarray] = None  # uint32 bitmap over insertion positions
+    nprobe: int = 10                     # DefaultIVFNProbe (ivf.go:380)
+    refine_scale: float = 0.0            # > 0: UseRefiner with this ScaleFactor
+
+
+def bitmap_from_predicate(n: int, keys: Sequence[int], predicate: Callable[[int], bool]) -> np.ndarray:
+    """Materialises a CandidateFilter (query.go:35) as the position bitmap the ABI takes."""
+    words = np.zeros(max(1, (n + 31) // 32), np.uint32)
+    for pos in range(n):
+        if predicate(int(keys[pos])):
+            words[pos >> 5] |= np.uint32(1 << (pos & 31))
+    return words
+
+
+@dataclasses.dataclass
+class SearchResults:
+    keys: np.ndarray    # [nq, k] uint64
+    scores: np.ndarray  # [nq, k] float32
+    counts: np.ndarray  # [nq] int32; negative = -(status) of a failed query
+
+    def query(self, q: int):
+        c = int(self.counts[q])
+        return [(int(self.keys[q, i]), float(self.scores[q, i])) for i in range(max(c, 0))]
+
+
+class _Index:
+    kind = 0
+
+    def __init__(self, dimension: int, metric: int, storage: int = STORAGE_FP32, device: int = 0):
+        desc = IndexDesc(self.kind, dimension, metric, storage, device)
+        handle = ctypes.c_void_p()
+        _check(_lib.xvec_gpu_index_create(ctypes.byref(desc), ctypes.byref(handle)))
+        self._h = handle
+        self.dimension = dimension
+        self.metric = metric
+        self.storage = storage
+        self.device = device
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            _lib.xvec_gpu_index_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __len__(self) -> int:
+        return int(_lib.xvec_gpu_index_len(self._h))
+
+    def _row_dtype(self):
+        return np.uint16 if self.storage == STORAGE_FP16 else np.float32
+
+    def add(self, keys, vectors) -> None:
+        """Batch form of DenseFlatIndex.Add (flat.go:122-153)."""
+        keys = np.ascontiguousarray(keys, np.uint64)
+        vectors = np.ascontiguousarray(vectors, self._row_dtype())
+        if vectors.ndim != 2 or vectors.shape[1] != self.dimension or vectors.shape[0] != keys.size:
+            raise XvecGPUError(INVALID_ARGUMENT, "core: invalid vector dimension")
+        _check(_lib.xvec_gpu_index_add(self._h, _ptr(keys), _ptr(vectors), keys.size))
+
+    def add_device(self, keys_ptr: int, rows_ptr: int, n: int, stream: int = 0) -> None:
+        _check(_lib.xvec_gpu_index_add_device(self._h, keys_ptr, rows_ptr, n, stream or None))
+
+    def _opts(self, options: SearchOptions, stream=None, device_filter_ptr=None,
+              cancel_flag=None) -> SearchOpts:
+        o = SearchOpts()
+        o.top_k = options.top_k
+        o.radius = options.radius
+        o.nprobe = options.nprobe
+        o.refine_scale = options.refine_scale
+        if device_filter_ptr is not None:
+            o.filter_bitmap = device_filter_ptr
+            o.filter_words = (len(self) + 31) // 32
+        elif options.filter is not None:
+            f = np.ascontiguousarray(options.filter, np.uint32)
+            self._keep_filter = f
+            o.filter_bitmap = f.ctypes.data
+            o.filter_words = f.size
+        o.stream = stream
+        o.cancel_flag = cancel_flag
+        return o
+
+    def search_with_options(self, queries, options: SearchOptions, raise_on_error: bool = True,
+                            cancel_flag: Optional[np.ndarray] = None) -> SearchResults:
+        """Batched DenseQuerySearcher.SearchWithOptions (query.go:58-61)."""
+        queries = np.ascontiguousarray(queries, self._row_dtype())
+        if queries.ndim == 1:
+            queries = queries[None, :]
+        if queries.shape[1] != self.dimension:
+            raise XvecGPUError(INVALID_ARGUMENT, "core: invalid vector dimension")
+        nq, k = queries.shape[0], options.top_k
+        keys = np.zeros((nq, max(k, 1)), np.uint64)
+        scores = np.zeros((nq, max(k, 1)), np.float32)
+        counts = np.zeros(nq, np.int32)
+        o = self._opts(options, cancel_flag=None if cancel_flag is None else cancel_flag.ctypes.data)
+        st = _lib.xvec_gpu_index_search(self._h, _ptr(queries), nq, ctypes.byref(o), _ptr(keys),
+                                        _ptr(scores), _ptr(counts))
+        if st != OK and (raise_on_error or st not in (NON_FINITE,) or not (counts < 0).any()):
+            raise XvecGPUError(st, last_error())
+        return SearchResults(keys[:, :k], scores[:, :k], counts)
+
+    def search(self, queries, k: int) -> SearchResults:
+        return self.search_with_options(queries, SearchOptions(top_k=k))
+
+    def search_device(self, queries_ptr: int, nq: int, options: SearchOptions, out_keys_ptr: int,
+                      out_scores_ptr: int, out_counts_ptr: int, stream: int = 0,
+                      filter_ptr: Optional[int] = None) -> None:
+        """Device-memory variant (xvec_gpu_index_search_device)."""
+        o = self._opts(options, stream=stream or None, device_filter_ptr=filter_ptr)
+        _check(_lib.xvec_gpu_index_search_device(self._h, queries_ptr, nq, ctypes.byref(o),
+                                                 out_keys_ptr, out_scores_ptr, out_counts_ptr))
+
+
+class DenseFlatIndex(_Index):
+    """core.DenseFlatIndex (internal/core/flat.go:70-196) on one B200.
+
+    storage=STORAGE_FP16 keeps rows as binary16 bit patterns (uint16) and takes
+    binary16 queries; the arithmetic is float32 on the decoded values, like a
+    VectorFP16 field (collection.go:4607-4613)."""
+    kind = INDEX_FLAT
+
+
+class ScalarQuantizedFlatIndex(_Index):
+    """core.ScalarQuantizedFlatIndex with QuantizationInt8 (quantized_index.go:28-120)."""
+    kind = INDEX_SQ8_FLAT
+
+
+class IVFPQIndex(_Index):
+    """IVF list scan over 8-bit PQ codes (composition of ivf.go:524-561 and pq.go:549-595)."""
+    kind = INDEX_IVF_PQ
+
+    def set_model(self, centroids, pivots, chunks: int) -> None:
+        centroids = np.ascontiguousarray(centroids, np.float32)
+        pivots = np.ascontiguousarray(pivots, np.float32)
+        _check(_lib.xvec_gpu_ivfpq_set_model(self._h, _ptr(centroids), centroids.shape[0],
+                                             _ptr(pivots), chunks))
+
+
+class RaBitQIndex(_Index):
+    """One-bit RaBitQ linear scan with exact refinement (hnsw_rabitq.go:539-642, 780-801)."""
+    kind = INDEX_RABITQ
+
+    def set_model(self, centroids, rotation_signs) -> None:
+        centroids = np.ascontiguousarray(centroids, np.float32)
+        signs = np.ascontiguousarray(rotation_signs, np.uint8)
+        _check(_lib.xvec_gpu_rabitq_set_model(self._h, _ptr(centroids), centroids.shape[0],
+                                              _ptr(signs)))
+
+
+def kmeans_assign(metric: int, vectors, centroids, device: int = 0):
+    """assignKMeans / assignKMeansCosine (kmeans.go:382-479) on the GPU."""
+    vectors = np.ascontiguousarray(vectors, np.float32)
+    centroids = np.ascontiguousarray(centroids, np.float32)
+    n, d = vectors.shape
+    labels = np.zeros(n, np.int32)
+    scores = np.zeros(n, np.float32)
+    _check(_lib.xvec_gpu_kmeans_assign(device, metric, _ptr(vectors), n, _ptr(centroids),
+                                       centroids.shape[0], d, _ptr(labels), _ptr(scores)))
+    return labels, scores
+
+
+def merge_results_device(device: int, metric: int, top_k: int, nq: int, parts: int, keys_ptr: int,
+                         scores_ptr: int, counts_ptr: int, out_keys_ptr: int,
+                         out_scores_ptr: int, out_counts_ptr: int, stream: int = 0) -> None:
+    """MergeSearchResults (query.go:154-191) over per-shard lists in device memory."""
+    _check(_lib.xvec_gpu_merge_results_device(device, metric, top_k, nq, parts, keys_ptr,
+                                              scores_ptr, counts_ptr, out_keys_ptr,
+                                              out_scores_ptr, out_counts_ptr, stream or None))

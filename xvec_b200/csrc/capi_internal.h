@@ -1,0 +1,111 @@
+// capi_internal.h — host-side internals shared by the C-ABI translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <mutex>
+#include <shared_mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/xvec_gpu.h"
+
+namespace xvec {
+
+// Per-thread last error (xvec_gpu_last_error).
+void set_error(const char* fmt, ...);
+
+// Library counters (xvec_gpu_get_stats).
+void count_launches(int64_t n);
+void count_search(int64_t queries, int64_t exact_queries, double scan_ms, double search_ms);
+bool timing_enabled();
+#define XVEC_LAUNCHED() ::xvec::count_launches(1)
+
+#define XVEC_CUDA(expr)                                                                       \
+  do {                                                                                        \
+    cudaError_t err__ = (expr);                                                               \
+    if (err__ != cudaSuccess) {                                                               \
+      ::xvec::set_error("%s:%d %s: %s", __FILE__, __LINE__, #expr, cudaGetErrorString(err__)); \
+      return err__ == cudaErrorMemoryAllocation ? XVEC_GPU_OUT_OF_MEMORY                      \
+                                                : XVEC_GPU_CUDA_ERROR;                        \
+    }                                                                                         \
+  } while (0)
+
+// Growable device array.
+struct DeviceBuffer {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+  ~DeviceBuffer() {
+    if (ptr) cudaFree(ptr);
+  }
+  // Grows to at least `need` bytes keeping the first `keep` bytes.
+  xvec_gpu_status reserve(size_t need, size_t keep, cudaStream_t stream);
+  template <typename T>
+  T* as() const {
+    return static_cast<T*>(ptr);
+  }
+};
+
+// Stream-ordered scratch allocation that frees itself.
+struct Scratch {
+  void* ptr = nullptr;
+  cudaStream_t stream = nullptr;
+  Scratch() = default;
+  Scratch(const Scratch&) = delete;
+  Scratch& operator=(const Scratch&) = delete;
+  ~Scratch() {
+    if (ptr) cudaFreeAsync(ptr, stream);
+  }
+  xvec_gpu_status alloc(size_t bytes, cudaStream_t s);
+  template <typename T>
+  T* as() const {
+    return static_cast<T*>(ptr);
+  }
+};
+
+}  // namespace xvec
+
+struct xvec_gpu_index {
+  xvec_gpu_index_desc desc{};
+  int device = 0;
+  std::shared_mutex mu;  // search: shared, add/set_model: exclusive (flat.go:70-77)
+  int64_t n = 0;
+  int64_t capacity = 0;
+  size_t row_bytes = 0;  // bytes of one stored row
+
+  // Common per-row state.
+  xvec::DeviceBuffer rows;       // FLAT: float/half rows; SQ8/RABITQ/IVF_PQ: float32 originals
+  xvec::DeviceBuffer keys;       // uint64
+  xvec::DeviceBuffer row_n2;     // float reference-order ||x||^2
+  xvec::DeviceBuffer keyrank;    // uint32: position -> rank of its key
+  xvec::DeviceBuffer pos_of_kr;  // uint32: key rank -> position
+  xvec::DeviceBuffer max_n2;     // unsigned (ordered float) max ||x||^2
+
+  // SQ8.
+  xvec::DeviceBuffer sq_codes;   // int8 [n][d]
+  xvec::DeviceBuffer sq_params;  // {float inv_scale, float offset, double sum, double square}
+
+  // IVF-PQ.
+  int32_t nlist = 0, chunks = 0;
+  bool has_model = false;
+  xvec::DeviceBuffer centroids;     // float [nlist][d]
+  xvec::DeviceBuffer centroid_n2;   // float [nlist]
+  xvec::DeviceBuffer pivots;        // float [256][d]
+  xvec::DeviceBuffer chunk_offsets; // int [chunks+1]
+  xvec::DeviceBuffer pq_codes;      // uint8 [n][chunks]
+  xvec::DeviceBuffer row_list;      // int32 [n] list of each row
+  xvec::DeviceBuffer list_offsets;  // int64 [nlist+1] CSR over positions
+  xvec::DeviceBuffer list_rows;     // uint32 [n] positions grouped by list (insertion order)
+  bool lists_dirty = true;
+
+  // RaBitQ (one-bit).
+  int32_t rq_clusters = 0, padded = 0;
+  xvec::DeviceBuffer rq_centroids;          // float [c][d]
+  xvec::DeviceBuffer rq_rot_centroids;      // float [c][padded]
+  xvec::DeviceBuffer rq_signs;              // uint8 [4*padded/8]
+  xvec::DeviceBuffer rq_codes;              // uint8 [n][padded/8]
+  xvec::DeviceBuffer rq_factors;            // double [n][3] + int cluster -> struct
+};

@@ -1,0 +1,46 @@
+// flat_kernels.cuh — launchers of the Flat search kernels (flat_kernels.cu).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace xvec {
+
+template <typename QT>
+void launch_prep_queries(const QT* q, int nq, int d, int metric, float* qf, float* q_n2,
+                         int* q_status, cudaStream_t stream);
+
+template <typename RowT>
+void launch_row_norms(const RowT* rows, int64_t n, int d, float* n2, unsigned* max_n2,
+                      int* nonfinite, cudaStream_t stream);
+
+// Capacity of the per-query accumulator buffers for a retained-list size kp.
+int simt_cap_for(int kp);
+int exact_cap_for(int kp);
+
+template <typename RowT>
+cudaError_t launch_flat_scan_simt(const RowT* rows, int64_t n, int d, const float* row_n2,
+                                  const uint32_t* keyrank, const float* qf, const float* q_n2,
+                                  int nq, const uint32_t* bitmap, int metric, int num_parts,
+                                  int kp, uint64_t* part_keys, int* part_counts,
+                                  uint64_t* part_sat, int* q_flags, cudaStream_t stream);
+
+template <typename RowT>
+cudaError_t launch_flat_scan_exact(const RowT* rows, int64_t n, int d, const uint32_t* keyrank,
+                                   const float* qf, const int* query_ids, int nlist,
+                                   const uint32_t* bitmap, int metric, int num_parts, int kp,
+                                   uint64_t* part_keys, int* part_counts, uint64_t* part_sat,
+                                   int* q_flags, cudaStream_t stream);
+
+template <typename RowT>
+cudaError_t launch_flat_merge_rescore(const RowT* rows, int d, const uint32_t* pos_of_keyrank,
+                                      const uint64_t* keys, const float* qf, const float* q_n2,
+                                      const unsigned* max_n2, const int* query_ids, int nlist,
+                                      int metric, int k, float radius, int exact_mode,
+                                      const uint64_t* part_keys, const int* part_counts,
+                                      const uint64_t* part_sat, int num_parts, int kp,
+                                      uint64_t* out_keys, float* out_scores, int* out_counts,
+                                      int* q_flags, cudaStream_t stream);
+
+}  // namespace xvec

@@ -1,0 +1,30 @@
+// index_kernels.cuh — per-index-kind hooks used by capi.cu.
+#pragma once
+
+#include <vector>
+
+#include "capi_internal.h"
+
+namespace xvec {
+
+// Extra per-row storage for the quantized index kinds (grown with capacity).
+xvec_gpu_status extra_reserve(xvec_gpu_index* idx, int64_t capacity, cudaStream_t s);
+// Checks that rows [old_n, old_n + m) can be committed (models present, ...).
+xvec_gpu_status extra_validate(xvec_gpu_index* idx, int64_t old_n, int64_t m, cudaStream_t s);
+// Encodes rows [old_n, old_n + m) (quantize / assign / PQ-encode / RaBitQ).
+xvec_gpu_status extra_commit(xvec_gpu_index* idx, int64_t old_n, int64_t m, cudaStream_t s);
+
+xvec_gpu_status sq8_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
+                                const xvec_gpu_search_opts& o, const uint32_t* d_bitmap,
+                                uint64_t* d_keys, float* d_scores, int* d_counts, cudaStream_t s,
+                                std::vector<int>* statuses);
+xvec_gpu_status ivfpq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
+                                  const xvec_gpu_search_opts& o, const uint32_t* d_bitmap,
+                                  uint64_t* d_keys, float* d_scores, int* d_counts,
+                                  cudaStream_t s, std::vector<int>* statuses);
+xvec_gpu_status rabitq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
+                                   const xvec_gpu_search_opts& o, const uint32_t* d_bitmap,
+                                   uint64_t* d_keys, float* d_scores, int* d_counts,
+                                   cudaStream_t s, std::vector<int>* statuses);
+
+}  // namespace xvec

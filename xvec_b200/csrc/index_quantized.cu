@@ -1,0 +1,48 @@
+// index_quantized.cu — SQ8, IVF-PQ and RaBitQ index kinds.
+#include "index_kernels.cuh"
+
+namespace xvec {
+
+xvec_gpu_status extra_reserve(xvec_gpu_index*, int64_t, cudaStream_t) { return XVEC_GPU_OK; }
+xvec_gpu_status extra_validate(xvec_gpu_index* idx, int64_t, int64_t, cudaStream_t) {
+  if (idx->desc.kind != XVEC_INDEX_FLAT)
+    return set_error("index kind not available yet"), XVEC_GPU_UNSUPPORTED;
+  return XVEC_GPU_OK;
+}
+xvec_gpu_status extra_commit(xvec_gpu_index*, int64_t, int64_t, cudaStream_t) { return XVEC_GPU_OK; }
+xvec_gpu_status sq8_search_impl(xvec_gpu_index*, const float*, int, const xvec_gpu_search_opts&,
+                                const uint32_t*, uint64_t*, float*, int*, cudaStream_t,
+                                std::vector<int>*) {
+  return set_error("index kind not available yet"), XVEC_GPU_UNSUPPORTED;
+}
+xvec_gpu_status ivfpq_search_impl(xvec_gpu_index*, const float*, int, const xvec_gpu_search_opts&,
+                                  const uint32_t*, uint64_t*, float*, int*, cudaStream_t,
+                                  std::vector<int>*) {
+  return set_error("index kind not available yet"), XVEC_GPU_UNSUPPORTED;
+}
+xvec_gpu_status rabitq_search_impl(xvec_gpu_index*, const float*, int, const xvec_gpu_search_opts&,
+                                   const uint32_t*, uint64_t*, float*, int*, cudaStream_t,
+                                   std::vector<int>*) {
+  return set_error("index kind not available yet"), XVEC_GPU_UNSUPPORTED;
+}
+
+}  // namespace xvec
+
+extern "C" xvec_gpu_status xvec_gpu_ivfpq_set_model(xvec_gpu_index*, const float*, int32_t,
+                                                    const float*, int32_t) {
+  return XVEC_GPU_UNSUPPORTED;
+}
+extern "C" xvec_gpu_status xvec_gpu_rabitq_set_model(xvec_gpu_index*, const float*, int32_t,
+                                                     const uint8_t*) {
+  return XVEC_GPU_UNSUPPORTED;
+}
+extern "C" xvec_gpu_status xvec_gpu_kmeans_assign(int32_t, int32_t, const float*, int64_t,
+                                                  const float*, int32_t, int32_t, int32_t*,
+                                                  float*) {
+  return XVEC_GPU_UNSUPPORTED;
+}
+extern "C" xvec_gpu_status xvec_gpu_kmeans_assign_device(int32_t, int32_t, const float*, int64_t,
+                                                         const float*, int32_t, int32_t, int32_t*,
+                                                         float*, void*) {
+  return XVEC_GPU_UNSUPPORTED;
+}

@@ -1,0 +1,59 @@
+"""Sharded search over the GPUs of one node (one process per GPU).
+
+The reference fans a query out over segments and merges the per-segment
+top-k with MergeSearchResults (collection.go:4043-4066, query.go:154-191).
+Here each rank holds one shard of the rows (its own index on its own GPU,
+keys globally unique), searches it, the per-shard lists are exchanged with
+one NCCL all-gather, and every rank merges them on its GPU with the same
+ordering rule.  torch.distributed is the plumbing; the search and the merge
+are this library's kernels.
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from . import SearchOptions, SearchResults, _Index, merge_results_device
+
+
+class ShardedSearch:
+    def __init__(self, index: _Index, group=None):
+        self.index = index
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.device = torch.device("cuda", index.device)
+
+    def search_device(self, queries: torch.Tensor, options: SearchOptions):
+        """queries: device tensor [nq, d] (float32, or int16/uint16 bits for FP16 storage).
+        Returns merged (keys int64 [nq,k], scores float32 [nq,k], counts int32 [nq])."""
+        nq, k = queries.shape[0], options.top_k
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        keys = torch.empty((nq, k), dtype=torch.int64, device=self.device)
+        scores = torch.empty((nq, k), dtype=torch.float32, device=self.device)
+        counts = torch.empty((nq,), dtype=torch.int32, device=self.device)
+        self.index.search_device(queries.data_ptr(), nq, options, keys.data_ptr(),
+                                 scores.data_ptr(), counts.data_ptr(), stream=stream)
+        if self.world == 1:
+            return keys, scores, counts
+        all_keys = torch.empty((self.world, nq, k), dtype=torch.int64, device=self.device)
+        all_scores = torch.empty((self.world, nq, k), dtype=torch.float32, device=self.device)
+        all_counts = torch.empty((self.world, nq), dtype=torch.int32, device=self.device)
+        dist.all_gather_into_tensor(all_keys, keys, group=self.group)
+        dist.all_gather_into_tensor(all_scores, scores, group=self.group)
+        dist.all_gather_into_tensor(all_counts, counts, group=self.group)
+        out_keys = torch.empty_like(keys)
+        out_scores = torch.empty_like(scores)
+        out_counts = torch.empty_like(counts)
+        merge_results_device(self.index.device, self.index.metric, k, nq, self.world,
+                             all_keys.data_ptr(), all_scores.data_ptr(), all_counts.data_ptr(),
+                             out_keys.data_ptr(), out_scores.data_ptr(), out_counts.data_ptr(),
+                             stream=stream)
+        return out_keys, out_scores, out_counts
+
+    def search(self, queries_host: torch.Tensor, options: SearchOptions) -> SearchResults:
+        """End-to-end form: host (pinned) queries in, host results out on every rank."""
+        q = queries_host.to(self.device, non_blocking=True)
+        keys, scores, counts = self.search_device(q, options)
+        return SearchResults(keys.cpu().numpy().view(np.uint64), scores.cpu().numpy(),
+                             counts.cpu().numpy())
