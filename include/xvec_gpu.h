@@ -200,6 +200,7 @@ typedef struct {
   int64_t exact_queries;   /* queries answered through the exact (reference-order) scan */
   double scan_ms;          /* device time of the candidate scan kernels */
   double search_ms;        /* device time of whole search calls */
+  int64_t tensor_scans;    /* scans that ran on the tensor cores (tcgen05) */
 } xvec_gpu_stats;
 void xvec_gpu_stats_enable_timing(int32_t enabled);
 void xvec_gpu_get_stats(xvec_gpu_stats* out);

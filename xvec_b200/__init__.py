@@ -75,7 +75,8 @@ class SearchOpts(ctypes.Structure):
 class Stats(ctypes.Structure):
     _fields_ = [("searches", ctypes.c_int64), ("queries", ctypes.c_int64),
                 ("kernel_launches", ctypes.c_int64), ("exact_queries", ctypes.c_int64),
-                ("scan_ms", ctypes.c_double), ("search_ms", ctypes.c_double)]
+                ("scan_ms", ctypes.c_double), ("search_ms", ctypes.c_double),
+                ("tensor_scans", ctypes.c_int64)]
 
 
 def _load() -> ctypes.CDLL:

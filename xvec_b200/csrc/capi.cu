@@ -3,12 +3,14 @@
 #include <cub/device/device_radix_sort.cuh>
 
 #include <algorithm>
+#include <type_traits>
 #include <cmath>
 #include <cstring>
 
 #include "capi_internal.h"
 #include "common.cuh"
 #include "flat_kernels.cuh"
+#include "flat_tc.cuh"
 #include "index_kernels.cuh"
 
 namespace xvec {
@@ -194,23 +196,71 @@ xvec_gpu_status flat_search_impl(xvec_gpu_index* idx, const void* d_q, int nq,
   const int64_t n = idx->n;
   const RowT* rows = idx->rows.as<RowT>();
   xvec_gpu_status st;
-  Scratch qf, qn2, qstatus, qflags;
+  Scratch qf, qn2, qaux, qstatus, qflags, kstatus;
   if ((st = qf.alloc((size_t)nq * d * 4, s)) || (st = qn2.alloc((size_t)nq * 4, s)) ||
-      (st = qstatus.alloc((size_t)nq * 4, s)) || (st = qflags.alloc((size_t)nq * 4, s)))
+      (st = qaux.alloc((size_t)nq * 4, s)) || (st = qstatus.alloc((size_t)nq * 4, s)) ||
+      (st = qflags.alloc((size_t)nq * 4, s)) || (st = kstatus.alloc(4, s)))
     return st;
+  XVEC_CUDA(cudaMemsetAsync(kstatus.ptr, 0, 4, s));
   EventTimer timer(s);
   timer.mark(0);
   XVEC_CUDA(cudaMemsetAsync(qflags.ptr, 0, (size_t)nq * 4, s));
   launch_prep_queries<RowT>(static_cast<const RowT*>(d_q), nq, d, metric, qf.as<float>(),
-                            qn2.as<float>(), qstatus.as<int>(), s);
+                            qn2.as<float>(), qaux.as<float>(), qstatus.as<int>(), s);
   XVEC_LAUNCHED();
   XVEC_CUDA(cudaGetLastError());
   XVEC_CUDA(cudaMemsetAsync(d_counts_out, 0, (size_t)nq * 4, s));
 
   std::vector<int> h_status(nq), h_flags(nq);
   const int kp = choose_kp(k);
-  const bool fast = simt_cap_for(kp) <= 512 && n > 0;
-  if (fast) {
+  const bool use_tc = std::is_same<RowT, __half>::value && n > 0 && n < (1ll << 31) - 256 &&
+                      kp + 32 <= flat_tc_cap() && flat_tc_supported(d, rows, d_q);
+  const bool fast = use_tc || (simt_cap_for(kp) <= 512 && n > 0);
+  if (use_tc) {
+    if (is_cancelled(o)) return set_error("cancelled"), XVEC_GPU_CANCELLED;
+    // Parts: pick the row split whose CTA count best fills whole waves of
+    // one CTA per SM, keeping at least 16 tiles of 256 rows per part.
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, idx->device);
+    const int qblocks = (nq + 127) / 128;
+    const int64_t max_parts = std::max<int64_t>(1, std::min<int64_t>(64, n / (256 * 16)));
+    int parts = 1;
+    double best = -1;
+    for (int p = 1; p <= max_parts; ++p) {
+      const int64_t ctas = (int64_t)qblocks * p;
+      const int64_t waves = (ctas + sms - 1) / sms;
+      const double eff = (double)ctas / (double)(waves * sms);
+      if (eff > best + 1e-9) {
+        best = eff;
+        parts = p;
+      }
+    }
+    const int cap = flat_tc_cap();
+    Scratch pkeys, pcounts, psat;
+    if ((st = pkeys.alloc((size_t)nq * parts * cap * 8, s)) ||
+        (st = pcounts.alloc((size_t)nq * parts * 4, s)) ||
+        (st = psat.alloc((size_t)nq * parts * 8, s)))
+      return st;
+    const float* row_aux =
+        metric == XVEC_METRIC_COSINE ? idx->row_inv.as<float>() : idx->row_n2.as<float>();
+    timer.mark(1);
+    XVEC_CUDA(launch_flat_scan_tc(metric, static_cast<const __half*>(d_q), nq,
+                                  reinterpret_cast<const __half*>(rows), n, d, d, row_aux,
+                                  idx->keyrank.as<uint32_t>(), qaux.as<float>(), qn2.as<float>(),
+                                  nullptr, d_bitmap, parts, kp, pkeys.as<uint64_t>(),
+                                  pcounts.as<int>(), psat.as<uint64_t>(), qflags.as<int>(),
+                                  kstatus.as<int>(), s));
+    timer.mark(2);
+    XVEC_LAUNCHED();
+    count_tensor_scan();
+    if (is_cancelled(o)) return set_error("cancelled"), XVEC_GPU_CANCELLED;
+    XVEC_CUDA(launch_flat_merge_rescore<RowT>(
+        rows, d, idx->pos_of_kr.as<uint32_t>(), idx->keys.as<uint64_t>(), qf.as<float>(),
+        qn2.as<float>(), idx->max_n2.as<unsigned>(), nullptr, nq, metric, k, o.radius, 0,
+        pkeys.as<uint64_t>(), pcounts.as<int>(), psat.as<uint64_t>(), parts, cap, d_keys_out,
+        d_scores_out, d_counts_out, qflags.as<int>(), s));
+    XVEC_LAUNCHED();
+  } else if (fast) {
     if (is_cancelled(o)) return set_error("cancelled"), XVEC_GPU_CANCELLED;
     const int qtiles = (nq + 31) / 32;
     int parts = (int)std::max<int64_t>(
@@ -229,6 +279,7 @@ xvec_gpu_status flat_search_impl(xvec_gpu_index* idx, const void* d_q, int nq,
                                           psat.as<uint64_t>(), qflags.as<int>(), s));
     timer.mark(2);
     XVEC_LAUNCHED();
+    count_tensor_scan();
     if (is_cancelled(o)) return set_error("cancelled"), XVEC_GPU_CANCELLED;
     XVEC_CUDA(launch_flat_merge_rescore<RowT>(
         rows, d, idx->pos_of_kr.as<uint32_t>(), idx->keys.as<uint64_t>(), qf.as<float>(),
@@ -241,7 +292,12 @@ xvec_gpu_status flat_search_impl(xvec_gpu_index* idx, const void* d_q, int nq,
                             s));
   XVEC_CUDA(cudaMemcpyAsync(h_flags.data(), qflags.ptr, (size_t)nq * 4, cudaMemcpyDeviceToHost,
                             s));
+  int h_kstatus = 0;
+  XVEC_CUDA(cudaMemcpyAsync(&h_kstatus, kstatus.ptr, 4, cudaMemcpyDeviceToHost, s));
   XVEC_CUDA(cudaStreamSynchronize(s));
+  if (h_kstatus != 0)
+    return set_error("tensor-core scan: a bounded device wait expired (code %d)", h_kstatus),
+           XVEC_GPU_TIMEOUT;
   // Exact path: queries whose candidate set was not provably complete (or
   // that saw a non-finite fast rank), and every query when k is large.
   std::vector<int> exact_list;
@@ -354,6 +410,7 @@ xvec_gpu_status add_device_locked(xvec_gpu_index* idx, const uint64_t* d_keys, c
     if ((st = idx->rows.reserve((size_t)cap * in_row_bytes, (size_t)old_n * in_row_bytes, s)) ||
         (st = idx->keys.reserve((size_t)cap * 8, (size_t)old_n * 8, s)) ||
         (st = idx->row_n2.reserve((size_t)cap * 4, (size_t)old_n * 4, s)) ||
+        (st = idx->row_inv.reserve((size_t)cap * 4, (size_t)old_n * 4, s)) ||
         (st = idx->keyrank.reserve((size_t)cap * 4, (size_t)old_n * 4, s)) ||
         (st = idx->pos_of_kr.reserve((size_t)cap * 4, (size_t)old_n * 4, s)))
       return st;
@@ -381,12 +438,12 @@ xvec_gpu_status add_device_locked(xvec_gpu_index* idx, const uint64_t* d_keys, c
   XVEC_CUDA(cudaMemcpyAsync(max_new.ptr, idx->max_n2.ptr, 4, cudaMemcpyDeviceToDevice, s));
   if (idx->desc.kind == XVEC_INDEX_FLAT && idx->desc.storage == XVEC_STORAGE_FP16)
     launch_row_norms<__half>(idx->rows.as<__half>() + (size_t)old_n * d, m, d,
-                             idx->row_n2.as<float>() + old_n, max_new.as<unsigned>(),
-                             nonfinite.as<int>(), s);
+                             idx->row_n2.as<float>() + old_n, idx->row_inv.as<float>() + old_n,
+                             max_new.as<unsigned>(), nonfinite.as<int>(), s);
   else
     launch_row_norms<float>(idx->rows.as<float>() + (size_t)old_n * d, m, d,
-                            idx->row_n2.as<float>() + old_n, max_new.as<unsigned>(),
-                            nonfinite.as<int>(), s);
+                            idx->row_n2.as<float>() + old_n, idx->row_inv.as<float>() + old_n,
+                            max_new.as<unsigned>(), nonfinite.as<int>(), s);
   XVEC_CUDA(cudaGetLastError());
   int h_nonfinite = 0;
   XVEC_CUDA(cudaMemcpyAsync(&h_nonfinite, nonfinite.ptr, 4, cudaMemcpyDeviceToHost, s));

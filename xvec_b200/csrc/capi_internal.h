@@ -20,6 +20,7 @@ void set_error(const char* fmt, ...);
 
 // Library counters (xvec_gpu_get_stats).
 void count_launches(int64_t n);
+void count_tensor_scan();
 void count_search(int64_t queries, int64_t exact_queries, double scan_ms, double search_ms);
 bool timing_enabled();
 #define XVEC_LAUNCHED() ::xvec::count_launches(1)
@@ -80,6 +81,7 @@ struct xvec_gpu_index {
   xvec::DeviceBuffer rows;       // FLAT: float/half rows; SQ8/RABITQ/IVF_PQ: float32 originals
   xvec::DeviceBuffer keys;       // uint64
   xvec::DeviceBuffer row_n2;     // float reference-order ||x||^2
+  xvec::DeviceBuffer row_inv;    // float 1/||x|| (0 for a zero row), tensor-core epilogue
   xvec::DeviceBuffer keyrank;    // uint32: position -> rank of its key
   xvec::DeviceBuffer pos_of_kr;  // uint32: key rank -> position
   xvec::DeviceBuffer max_n2;     // unsigned (ordered float) max ||x||^2

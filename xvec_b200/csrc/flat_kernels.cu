@@ -27,7 +27,7 @@ namespace xvec {
 template <typename QT>
 __global__ void prep_queries_kernel(const QT* __restrict__ q_in, int nq, int d, int metric,
                                     float* __restrict__ qf, float* __restrict__ q_n2,
-                                    int* __restrict__ q_status) {
+                                    float* __restrict__ q_aux, int* __restrict__ q_status) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= nq) return;
@@ -45,6 +45,8 @@ __global__ void prep_queries_kernel(const QT* __restrict__ q_in, int nq, int d, 
   warp_reference_sums<1>(dst, dst, d, &s0, &s1, &s2);  // InnerProduct(q, q)
   if (lane == 0) {
     q_n2[warp] = s0;
+    // Tensor-core epilogue operand: 1/||q|| for cosine, ||q||^2 otherwise.
+    q_aux[warp] = metric == kMetricCosine ? (s0 > 0.f ? rsqrtf(s0) : 0.f) : s0;
     // metric.Compute(q, q): L2 is always 0 for finite input; IP, cosine and
     // MIPS become non-finite exactly when ||q||^2 overflows.
     int st = 0;
@@ -58,7 +60,8 @@ __global__ void prep_queries_kernel(const QT* __restrict__ q_in, int nq, int d, 
 // fast L2 / cosine / MIPS ranks and the error bounds.
 template <typename RowT>
 __global__ void row_norms_kernel(const RowT* __restrict__ rows, int64_t n, int d,
-                                 float* __restrict__ n2, unsigned* __restrict__ max_n2_ordered,
+                                 float* __restrict__ n2, float* __restrict__ inv_mag,
+                                 unsigned* __restrict__ max_n2_ordered,
                                  int* __restrict__ nonfinite) {
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -102,6 +105,7 @@ __global__ void row_norms_kernel(const RowT* __restrict__ rows, int64_t n, int d
   }
   if (lane == 0) {
     n2[warp] = s0;
+    inv_mag[warp] = s0 > 0.f ? rsqrtf(s0) : 0.f;
     if (!finite) atomicExch(nonfinite, 1);
     else if (finite_f(s0)) atomicMax(max_n2_ordered, float_to_ordered(s0));
     else atomicMax(max_n2_ordered, float_to_ordered(3.0e38f));
@@ -340,7 +344,7 @@ __global__ void __launch_bounds__(256) flat_merge_rescore_kernel(
     const float* __restrict__ q_n2, const unsigned* __restrict__ max_n2_ordered,
     const int* __restrict__ query_ids, int metric, int k, float radius, int exact_mode,
     const uint64_t* __restrict__ part_keys, const int* __restrict__ part_counts,
-    const uint64_t* __restrict__ part_sat, int num_parts, int kp,
+    const uint64_t* __restrict__ part_sat, int num_parts, int stride,
     uint64_t* __restrict__ out_keys, float* __restrict__ out_scores, int* __restrict__ out_counts,
     int* __restrict__ q_flags) {
   __shared__ int hist[256];
@@ -361,16 +365,12 @@ __global__ void __launch_bounds__(256) flat_merge_rescore_kernel(
   __syncthreads();
   const int total = s_total;
   // Entry i of the union: walk parts (each list is dense from 0).
-  auto get = [&](int i) -> uint64_t {
-    // Parts have a fixed stride kp; map i by scanning counts lazily would be
-    // slow, so the union is addressed as [part][kp] with empty slots skipped
-    // by the callers below.
-    return part_keys[pbase * kp + i];
-  };
-  const int span = num_parts * kp;  // addressable slots (empty ones hold garbage)
+  // The union is addressed as [part][stride]; slots past a part's count
+  // are skipped.
+  const int span = num_parts * stride;
   auto get_valid = [&](int i) -> uint64_t {
-    const int p = i / kp, j = i - p * kp;
-    return j < part_counts[pbase + p] ? get(i) : kEmptyKey;
+    const int p = i / stride, j = i - p * stride;
+    return j < part_counts[pbase + p] ? part_keys[pbase * stride + i] : kEmptyKey;
   };
 
   if (total == 0) {
@@ -445,30 +445,30 @@ __global__ void __launch_bounds__(256) flat_merge_rescore_kernel(
 // ---------------------------------------------------------------------------
 template <typename QT>
 void launch_prep_queries(const QT* q, int nq, int d, int metric, float* qf, float* q_n2,
-                         int* q_status, cudaStream_t stream) {
+                         float* q_aux, int* q_status, cudaStream_t stream) {
   const int warps_per_block = 8;
   const int blocks = (nq + warps_per_block - 1) / warps_per_block;
   if (blocks > 0)
     prep_queries_kernel<QT><<<blocks, warps_per_block * 32, 0, stream>>>(q, nq, d, metric, qf,
-                                                                         q_n2, q_status);
+                                                                         q_n2, q_aux, q_status);
 }
-template void launch_prep_queries<float>(const float*, int, int, int, float*, float*, int*,
-                                         cudaStream_t);
-template void launch_prep_queries<__half>(const __half*, int, int, int, float*, float*, int*,
-                                          cudaStream_t);
+template void launch_prep_queries<float>(const float*, int, int, int, float*, float*, float*,
+                                         int*, cudaStream_t);
+template void launch_prep_queries<__half>(const __half*, int, int, int, float*, float*, float*,
+                                          int*, cudaStream_t);
 
 template <typename RowT>
-void launch_row_norms(const RowT* rows, int64_t n, int d, float* n2, unsigned* max_n2,
-                      int* nonfinite, cudaStream_t stream) {
+void launch_row_norms(const RowT* rows, int64_t n, int d, float* n2, float* inv_mag,
+                      unsigned* max_n2, int* nonfinite, cudaStream_t stream) {
   const int64_t blocks = (n + 7) / 8;
   if (blocks > 0)
-    row_norms_kernel<RowT><<<(unsigned)blocks, 256, 0, stream>>>(rows, n, d, n2, max_n2,
+    row_norms_kernel<RowT><<<(unsigned)blocks, 256, 0, stream>>>(rows, n, d, n2, inv_mag, max_n2,
                                                                  nonfinite);
 }
-template void launch_row_norms<float>(const float*, int64_t, int, float*, unsigned*, int*,
-                                      cudaStream_t);
-template void launch_row_norms<__half>(const __half*, int64_t, int, float*, unsigned*, int*,
-                                       cudaStream_t);
+template void launch_row_norms<float>(const float*, int64_t, int, float*, float*, unsigned*,
+                                      int*, cudaStream_t);
+template void launch_row_norms<__half>(const __half*, int64_t, int, float*, float*, unsigned*,
+                                       int*, cudaStream_t);
 
 int simt_cap_for(int kp) {
   // CAP must hold KP retained entries plus two tiles of appends.
@@ -565,13 +565,14 @@ cudaError_t launch_flat_merge_rescore(const RowT* rows, int d, const uint32_t* p
                                       const unsigned* max_n2, const int* query_ids, int nlist,
                                       int metric, int k, float radius, int exact_mode,
                                       const uint64_t* part_keys, const int* part_counts,
-                                      const uint64_t* part_sat, int num_parts, int kp,
+                                      const uint64_t* part_sat, int num_parts, int stride,
                                       uint64_t* out_keys, float* out_scores, int* out_counts,
                                       int* q_flags, cudaStream_t stream) {
   if (nlist <= 0) return cudaSuccess;
   flat_merge_rescore_kernel<RowT><<<nlist, 256, 0, stream>>>(
       rows, d, pos_of_keyrank, keys, qf, q_n2, max_n2, query_ids, metric, k, radius, exact_mode,
-      part_keys, part_counts, part_sat, num_parts, kp, out_keys, out_scores, out_counts, q_flags);
+      part_keys, part_counts, part_sat, num_parts, stride, out_keys, out_scores, out_counts,
+      q_flags);
   return cudaGetLastError();
 }
 template cudaError_t launch_flat_merge_rescore<float>(const float*, int, const uint32_t*,

@@ -9,11 +9,11 @@ namespace xvec {
 
 template <typename QT>
 void launch_prep_queries(const QT* q, int nq, int d, int metric, float* qf, float* q_n2,
-                         int* q_status, cudaStream_t stream);
+                         float* q_aux, int* q_status, cudaStream_t stream);
 
 template <typename RowT>
-void launch_row_norms(const RowT* rows, int64_t n, int d, float* n2, unsigned* max_n2,
-                      int* nonfinite, cudaStream_t stream);
+void launch_row_norms(const RowT* rows, int64_t n, int d, float* n2, float* inv_mag,
+                      unsigned* max_n2, int* nonfinite, cudaStream_t stream);
 
 // Capacity of the per-query accumulator buffers for a retained-list size kp.
 int simt_cap_for(int kp);
@@ -39,7 +39,7 @@ cudaError_t launch_flat_merge_rescore(const RowT* rows, int d, const uint32_t* p
                                       const unsigned* max_n2, const int* query_ids, int nlist,
                                       int metric, int k, float radius, int exact_mode,
                                       const uint64_t* part_keys, const int* part_counts,
-                                      const uint64_t* part_sat, int num_parts, int kp,
+                                      const uint64_t* part_sat, int num_parts, int stride,
                                       uint64_t* out_keys, float* out_scores, int* out_counts,
                                       int* q_flags, cudaStream_t stream);
 

@@ -12,13 +12,14 @@
 namespace xvec {
 
 namespace {
-std::atomic<int64_t> g_searches{0}, g_queries{0}, g_launches{0}, g_exact{0};
+std::atomic<int64_t> g_searches{0}, g_queries{0}, g_launches{0}, g_exact{0}, g_tensor{0};
 std::mutex g_ms_mu;
 double g_scan_ms = 0, g_search_ms = 0;
 std::atomic<int> g_timing{0};
 }  // namespace
 
 void count_launches(int64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+void count_tensor_scan() { g_tensor.fetch_add(1); }
 void count_search(int64_t queries, int64_t exact_queries, double scan_ms, double search_ms) {
   g_searches.fetch_add(1);
   g_queries.fetch_add(queries);
@@ -102,6 +103,7 @@ extern "C" void xvec_gpu_get_stats(xvec_gpu_stats* out) {
   out->queries = g_queries.load();
   out->kernel_launches = g_launches.load();
   out->exact_queries = g_exact.load();
+  out->tensor_scans = g_tensor.load();
   std::lock_guard<std::mutex> lock(g_ms_mu);
   out->scan_ms = g_scan_ms;
   out->search_ms = g_search_ms;
@@ -112,6 +114,7 @@ extern "C" void xvec_gpu_reset_stats(void) {
   g_queries = 0;
   g_launches = 0;
   g_exact = 0;
+  g_tensor = 0;
   std::lock_guard<std::mutex> lock(g_ms_mu);
   g_scan_ms = 0;
   g_search_ms = 0;
