@@ -80,6 +80,10 @@ __global__ void adjacent_equal_kernel(const uint64_t* sorted, int64_t n, int* fl
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i + 1 < n && sorted[i] == sorted[i + 1]) atomicExch(flag, 1);
 }
+__global__ void clear_flags_kernel(const int* ids, int n, int* q_flags, int mask) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) q_flags[ids[i]] &= ~mask;
+}
 __global__ void apply_status_kernel(const int* q_status, const int* q_flags, int nq,
                                     int* out_counts) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -214,7 +218,7 @@ xvec_gpu_status flat_search_impl(xvec_gpu_index* idx, const void* d_q, int nq,
   std::vector<int> h_status(nq), h_flags(nq);
   const int kp = choose_kp(k);
   const bool use_tc = std::is_same<RowT, __half>::value && n > 0 && n < (1ll << 31) - 256 &&
-                      kp + 32 <= flat_tc_cap() && flat_tc_supported(d, rows, d_q);
+                      kp + 128 <= flat_tc_cap() && flat_tc_supported(d, rows, d_q);
   const bool fast = use_tc || (simt_cap_for(kp) <= 512 && n > 0);
   if (use_tc) {
     if (is_cancelled(o)) return set_error("cancelled"), XVEC_GPU_CANCELLED;
@@ -223,7 +227,10 @@ xvec_gpu_status flat_search_impl(xvec_gpu_index* idx, const void* d_q, int nq,
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, idx->device);
     const int qblocks = (nq + 127) / 128;
-    const int64_t max_parts = std::max<int64_t>(1, std::min<int64_t>(64, n / (256 * 16)));
+    // The merge gathers every list of a query in shared memory.
+    const int64_t merge_cap = flat_merge_capacity() / (kp * flat_tc_lists_per_part());
+    const int64_t max_parts =
+        std::max<int64_t>(1, std::min<int64_t>(std::min<int64_t>(64, merge_cap), n / (256 * 16)));
     int parts = 1;
     double best = -1;
     for (int p = 1; p <= max_parts; ++p) {
@@ -236,18 +243,21 @@ xvec_gpu_status flat_search_impl(xvec_gpu_index* idx, const void* d_q, int nq,
       }
     }
     const int cap = flat_tc_cap();
-    Scratch pkeys, pcounts, psat;
-    if ((st = pkeys.alloc((size_t)nq * parts * cap * 8, s)) ||
-        (st = pcounts.alloc((size_t)nq * parts * 4, s)) ||
-        (st = psat.alloc((size_t)nq * parts * 8, s)))
+    const int lists = parts * flat_tc_lists_per_part();
+    Scratch pkeys, pcounts, psat, gthr;
+    if ((st = pkeys.alloc((size_t)nq * lists * cap * 8, s)) ||
+        (st = pcounts.alloc((size_t)nq * lists * 4, s)) ||
+        (st = psat.alloc((size_t)nq * lists * 8, s)) || (st = gthr.alloc((size_t)nq * 8, s)))
       return st;
+    XVEC_CUDA(cudaMemsetAsync(gthr.ptr, 0xff, (size_t)nq * 8, s));
     const float* row_aux =
         metric == XVEC_METRIC_COSINE ? idx->row_inv.as<float>() : idx->row_n2.as<float>();
     timer.mark(1);
     XVEC_CUDA(launch_flat_scan_tc(metric, static_cast<const __half*>(d_q), nq,
                                   reinterpret_cast<const __half*>(rows), n, d, d, row_aux,
                                   idx->keyrank.as<uint32_t>(), qaux.as<float>(), qn2.as<float>(),
-                                  nullptr, d_bitmap, parts, kp, pkeys.as<uint64_t>(),
+                                  gthr.as<unsigned long long>(), d_bitmap, parts, kp,
+                                  pkeys.as<uint64_t>(),
                                   pcounts.as<int>(), psat.as<uint64_t>(), qflags.as<int>(),
                                   kstatus.as<int>(), s));
     timer.mark(2);
@@ -257,7 +267,7 @@ xvec_gpu_status flat_search_impl(xvec_gpu_index* idx, const void* d_q, int nq,
     XVEC_CUDA(launch_flat_merge_rescore<RowT>(
         rows, d, idx->pos_of_kr.as<uint32_t>(), idx->keys.as<uint64_t>(), qf.as<float>(),
         qn2.as<float>(), idx->max_n2.as<unsigned>(), nullptr, nq, metric, k, o.radius, 0,
-        pkeys.as<uint64_t>(), pcounts.as<int>(), psat.as<uint64_t>(), parts, cap, d_keys_out,
+        pkeys.as<uint64_t>(), pcounts.as<int>(), psat.as<uint64_t>(), lists, cap, d_keys_out,
         d_scores_out, d_counts_out, qflags.as<int>(), s));
     XVEC_LAUNCHED();
   } else if (fast) {
@@ -265,7 +275,7 @@ xvec_gpu_status flat_search_impl(xvec_gpu_index* idx, const void* d_q, int nq,
     const int qtiles = (nq + 31) / 32;
     int parts = (int)std::max<int64_t>(
         1, std::min<int64_t>((592 + qtiles - 1) / qtiles, (n + 1023) / 1024));
-    parts = std::min(parts, 65535);
+    parts = std::min(parts, std::max(1, flat_merge_capacity() / kp));
     Scratch pkeys, pcounts, psat;
     if ((st = pkeys.alloc((size_t)nq * parts * kp * 8, s)) ||
         (st = pcounts.alloc((size_t)nq * parts * 4, s)) ||
@@ -312,13 +322,16 @@ xvec_gpu_status flat_search_impl(xvec_gpu_index* idx, const void* d_q, int nq,
       return XVEC_GPU_INVALID_ARGUMENT;
     }
     int parts = (int)std::max<int64_t>(1, std::min<int64_t>((592 + nl - 1) / nl, (n + 1023) / 1024));
-    parts = std::min(parts, 65535);
+    parts = std::min(parts, std::max(1, flat_merge_capacity() / kp));
     Scratch ids, pkeys, pcounts, psat;
     if ((st = ids.alloc((size_t)nl * 4, s)) || (st = pkeys.alloc((size_t)nl * parts * kp * 8, s)) ||
         (st = pcounts.alloc((size_t)nl * parts * 4, s)) ||
         (st = psat.alloc((size_t)nl * parts * 8, s)))
       return st;
     XVEC_CUDA(cudaMemcpyAsync(ids.ptr, exact_list.data(), (size_t)nl * 4, cudaMemcpyHostToDevice, s));
+    // The fast pass's coverage bit does not apply to the exact pass.
+    clear_flags_kernel<<<blocks_for(nl), 256, 0, s>>>(ids.as<int>(), nl, qflags.as<int>(), 3);
+    XVEC_LAUNCHED();
     XVEC_CUDA(launch_flat_scan_exact<RowT>(rows, n, d, idx->keyrank.as<uint32_t>(), qf.as<float>(),
                                            ids.as<int>(), nl, d_bitmap, metric, parts, kp,
                                            pkeys.as<uint64_t>(), pcounts.as<int>(),
@@ -331,6 +344,15 @@ xvec_gpu_status flat_search_impl(xvec_gpu_index* idx, const void* d_q, int nq,
     count_launches(2);
     XVEC_CUDA(cudaMemcpyAsync(h_flags.data(), qflags.ptr, (size_t)nq * 4, cudaMemcpyDeviceToHost,
                               s));
+    XVEC_CUDA(cudaStreamSynchronize(s));
+    // The exact path selects exactly k keys per part and never fails its
+    // coverage check; a failure here is an internal error, not a result.
+    for (int q : exact_list) {
+      if (h_flags[q] & 2) {
+        set_error("exact scan could not complete query %d", q);
+        return XVEC_GPU_CUDA_ERROR;
+      }
+    }
   }
   apply_status_kernel<<<blocks_for(nq), 256, 0, s>>>(qstatus.as<int>(), qflags.as<int>(), nq,
                                                      d_counts_out);

@@ -336,6 +336,43 @@ __global__ void __launch_bounds__(256) flat_scan_exact_kernel(
 // exactly the k best keys.
 // ---------------------------------------------------------------------------
 constexpr int kMaxCandidates = 1024;
+constexpr int kMergeSmemEntries = 12288;  // union entries gathered in shared memory
+
+// Radix select over keys[0, m) in shared memory: the kth smallest (1-based)
+// considering bits [low_bit, 64) only; returns those high bits (low bits 0).
+__device__ uint64_t smem_radix_select(const uint64_t* keys, int m, int kth, int low_bit,
+                                      int* hist) {
+  __shared__ uint64_t s_prefix;
+  __shared__ int s_kth;
+  if (threadIdx.x == 0) {
+    s_prefix = 0;
+    s_kth = kth;
+  }
+  __syncthreads();
+#pragma unroll 1
+  for (int shift = 56; shift >= low_bit; shift -= 8) {
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+    const uint64_t prefix = s_prefix;
+    const uint64_t mask = (shift == 56) ? 0ull : (~0ull << (shift + 8));
+    for (int i = threadIdx.x; i < m; i += blockDim.x) {
+      const uint64_t key = keys[i];
+      if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 0xff], 1);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int remaining = s_kth, digit = 0;
+      for (; digit < 255; ++digit) {
+        if (remaining <= hist[digit]) break;
+        remaining -= hist[digit];
+      }
+      s_kth = remaining;
+      s_prefix = prefix | ((uint64_t)digit << shift);
+    }
+    __syncthreads();
+  }
+  return s_prefix;
+}
 
 template <typename RowT>
 __global__ void __launch_bounds__(256) flat_merge_rescore_kernel(
@@ -347,56 +384,70 @@ __global__ void __launch_bounds__(256) flat_merge_rescore_kernel(
     const uint64_t* __restrict__ part_sat, int num_parts, int stride,
     uint64_t* __restrict__ out_keys, float* __restrict__ out_scores, int* __restrict__ out_counts,
     int* __restrict__ q_flags) {
+  extern __shared__ __align__(16) unsigned char merge_smem[];
+  uint64_t* ukeys = reinterpret_cast<uint64_t*>(merge_smem);  // [kMergeSmemEntries]
   __shared__ int hist[256];
   __shared__ uint64_t cand[kMaxCandidates];
-  __shared__ float cand_score[kMaxCandidates];
-  __shared__ int s_total, s_ncand, s_fail;
+  __shared__ int s_offsets[1025];
+  __shared__ int s_ncand, s_fail;
   const int slot_q = blockIdx.x;
   const int qi = query_ids ? query_ids[blockIdx.x] : blockIdx.x;
   const int64_t pbase = (int64_t)slot_q * num_parts;
 
+  // Prefix sums of the list counts (num_parts <= 1024).
   if (threadIdx.x == 0) {
     int total = 0;
-    for (int p = 0; p < num_parts; ++p) total += part_counts[pbase + p];
-    s_total = total;
+    for (int p = 0; p < num_parts; ++p) {
+      s_offsets[p] = total;
+      total += part_counts[pbase + p];
+    }
+    s_offsets[num_parts] = total;
     s_ncand = 0;
     s_fail = 0;
   }
   __syncthreads();
-  const int total = s_total;
-  // Entry i of the union: walk parts (each list is dense from 0).
-  // The union is addressed as [part][stride]; slots past a part's count
-  // are skipped.
-  const int span = num_parts * stride;
-  auto get_valid = [&](int i) -> uint64_t {
-    const int p = i / stride, j = i - p * stride;
-    return j < part_counts[pbase + p] ? part_keys[pbase * stride + i] : kEmptyKey;
-  };
-
+  const int total = s_offsets[num_parts];
   if (total == 0) {
     if (threadIdx.x == 0) out_counts[qi] = 0;
     return;
   }
+  if (total > kMergeSmemEntries) {
+    // Cannot happen with the list sizes the scans produce; route to the
+    // exact path rather than read past the shared buffer.
+    if (threadIdx.x == 0) {
+      atomicOr(&q_flags[qi], 2);
+      out_counts[qi] = 0;
+    }
+    return;
+  }
+  // Gather the union (one warp per list).
+  {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int p = warp; p < num_parts; p += blockDim.x >> 5) {
+      const int off = s_offsets[p], c = s_offsets[p + 1] - off;
+      const uint64_t* src = part_keys + (pbase + p) * stride;
+      for (int j = lane; j < c; j += 32) ukeys[off + j] = src[j];
+    }
+  }
+  __syncthreads();
   const int kth = min(k, total);
-  const uint64_t kkey = block_radix_select(get_valid, span, kth, hist, nullptr);
-
-  // Candidate threshold on packed keys.
   uint64_t limit;
   if (exact_mode) {
-    limit = kkey;
+    limit = smem_radix_select(ukeys, total, kth, 0, hist);
   } else {
+    const uint64_t kr = smem_radix_select(ukeys, total, kth, 32, hist);
     const float eps = fast_eps(metric, d, q_n2[qi], ordered_to_float(*max_n2_ordered));
-    const float t = __fadd_ru(rank_of(kkey), 2.f * eps);
+    const float t = __fadd_ru(rank_of(kr), 2.f * eps);
     limit = ((uint64_t)float_to_ordered(t) << 32) | 0xffffffffull;
-    // Coverage: every dropped key of a saturated part is > its saturation key.
+    // Coverage: a list dropped only keys above its saturation key.
     for (int p = threadIdx.x; p < num_parts; p += blockDim.x) {
       const uint64_t sat = part_sat[pbase + p];
       if (sat != kEmptyKey && sat <= limit) atomicExch(&s_fail, 1);
     }
   }
-  for (int i = threadIdx.x; i < span; i += blockDim.x) {
-    const uint64_t key = get_valid(i);
-    if (key <= limit && key != kEmptyKey) {
+  for (int i = threadIdx.x; i < total; i += blockDim.x) {
+    const uint64_t key = ukeys[i];
+    if (key <= limit) {
       const int slot = atomicAdd(&s_ncand, 1);
       if (slot < kMaxCandidates) cand[slot] = key;
     }
@@ -419,24 +470,34 @@ __global__ void __launch_bounds__(256) flat_merge_rescore_kernel(
     const float s = warp_reference_score(metric, rows + (int64_t)pos * d, q, d);
     if (lane == 0) {
       if (!finite_f(s)) atomicOr(&q_flags[qi], 4);
-      cand_score[c] = s;
       cand[c] = pack_rank(rank_from_score(metric, s), kr);
     }
   }
   __syncthreads();
   block_sort_u64<kMaxCandidates>(cand, ncand);
   // Final top-k (radius is monotone in the sorted order).
-  if (threadIdx.x == 0) {
+  if (threadIdx.x < 32) {
+    // Count the prefix within radius with a warp scan over chunks.
     int count = 0;
-    for (int i = 0; i < ncand && count < k; ++i) {
-      const float s = score_from_rank(metric, rank_of(cand[i]));
-      if (!within_radius(metric, s, radius)) break;
-      const uint32_t pos = pos_of_keyrank[pos_of(cand[i])];
-      out_keys[(int64_t)qi * k + count] = keys[pos];
-      out_scores[(int64_t)qi * k + count] = s;
-      ++count;
+    for (int base = 0; base < ncand && count < k; base += 32) {
+      const int i = base + lane;
+      bool in = i < ncand;
+      float s = 0.f;
+      if (in) {
+        s = score_from_rank(metric, rank_of(cand[i]));
+        in = within_radius(metric, s, radius);
+      }
+      const unsigned m = __ballot_sync(kFullMask, in);
+      const int run = (m == kFullMask) ? 32 : __ffs(~m) - 1;  // leading in-radius run
+      if (lane < run && count + lane < k) {
+        const uint32_t pos = pos_of_keyrank[pos_of(cand[i])];
+        out_keys[(int64_t)qi * k + count + lane] = keys[pos];
+        out_scores[(int64_t)qi * k + count + lane] = s;
+      }
+      count = min(k, count + run);
+      if (run < 32) break;
     }
-    out_counts[qi] = count;
+    if (lane == 0) out_counts[qi] = count;
   }
 }
 
@@ -469,6 +530,8 @@ template void launch_row_norms<float>(const float*, int64_t, int, float*, float*
                                       int*, cudaStream_t);
 template void launch_row_norms<__half>(const __half*, int64_t, int, float*, float*, unsigned*,
                                        int*, cudaStream_t);
+
+int flat_merge_capacity() { return kMergeSmemEntries; }
 
 int simt_cap_for(int kp) {
   // CAP must hold KP retained entries plus two tiles of appends.
@@ -569,7 +632,11 @@ cudaError_t launch_flat_merge_rescore(const RowT* rows, int d, const uint32_t* p
                                       uint64_t* out_keys, float* out_scores, int* out_counts,
                                       int* q_flags, cudaStream_t stream) {
   if (nlist <= 0) return cudaSuccess;
-  flat_merge_rescore_kernel<RowT><<<nlist, 256, 0, stream>>>(
+  if (num_parts > 1024) return cudaErrorInvalidValue;
+  const int smem = kMergeSmemEntries * 8;
+  cudaFuncSetAttribute(flat_merge_rescore_kernel<RowT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       smem);
+  flat_merge_rescore_kernel<RowT><<<nlist, 256, smem, stream>>>(
       rows, d, pos_of_keyrank, keys, qf, q_n2, max_n2, query_ids, metric, k, radius, exact_mode,
       part_keys, part_counts, part_sat, num_parts, stride, out_keys, out_scores, out_counts,
       q_flags);

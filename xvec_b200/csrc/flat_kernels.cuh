@@ -17,6 +17,8 @@ void launch_row_norms(const RowT* rows, int64_t n, int d, float* n2, float* inv_
 
 // Capacity of the per-query accumulator buffers for a retained-list size kp.
 int simt_cap_for(int kp);
+// Union entries per query the merge kernel can hold (parts x kp must fit).
+int flat_merge_capacity();
 int exact_cap_for(int kp);
 
 template <typename RowT>

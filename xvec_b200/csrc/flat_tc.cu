@@ -38,12 +38,15 @@ constexpr int kBM = 128;   // queries per CTA (TMEM lanes)
 constexpr int kBN = 256;   // rows per tile (TMEM columns per accumulator)
 constexpr int kBK = 64;    // k-step: 64 fp16 = 128 bytes (one swizzle row)
 constexpr int kStages = 4;
-constexpr int kCap = 256;  // candidate buffer entries per (query, part)
-constexpr int kThreads = 192;
+constexpr int kCap = 512;  // candidate list entries per (query, part, column half)
+constexpr int kEpiWarps = 8;  // two warps per TMEM lane quarter, one per column half
+constexpr int kThreads = 64 + kEpiWarps * 32;
 constexpr uint32_t kTileABytes = kBM * kBK * 2;  // 16 KB
 constexpr uint32_t kTileBBytes = kBN * kBK * 2;  // 32 KB
 constexpr uint32_t kStageBytes = kTileABytes + kTileBBytes;
-constexpr uint32_t kSmemBytes = kStages * kStageBytes + 4 * kCap * 8 + 1024 /*align*/ + 256;
+// Per epilogue warp: radix histogram (1 KB) + the current tile's row
+// metadata for its 128 columns (aux floats + key ranks, 1 KB).
+constexpr uint32_t kSmemBytes = kStages * kStageBytes + kEpiWarps * 256 * 4 * 2 + 1024 + 256;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // a wait gives up after 2 s
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -140,6 +143,8 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
         "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]),
         "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
       : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
@@ -158,18 +163,102 @@ __device__ __forceinline__ float tc_rank(float dot, float aux, float qa, float q
   return 2.f - 2.f * dot / den;
 }
 
-// Compacts lane `who`'s candidate buffer (global) to its KP best keys.
-__device__ __noinline__ void warp_compact_global(uint64_t* gbuf, uint64_t* scratch, int cnt,
-                                                 int kp, uint64_t* thr_out) {
+// The common path tests a per-row "score" s against a per-query bound Tq
+// derived from the list threshold T (rank domain): s >= Tq must hold for
+// every row whose fast rank is <= T.  Tq is lowered by a relative slack so
+// rounding can only send extra rows to the exact check of the rare path.
+//   IP:     s = dot,             rank = -dot            -> Tq = -T
+//   cosine: s = dot * (1/|x|),   rank = 1 - s/|q|       -> Tq = (1 - T) |q|
+//   L2:     s = dot - |x|^2/2,   rank = |x|^2+|q|^2-2dot -> Tq = (|q|^2 - T) / 2
+//   MIPS:   s = -rank                                   -> Tq = -T
+template <int METRIC>
+__device__ __forceinline__ float score_bound(float T, float qa, float qn2) {
+  if (!(T == T)) return -INFINITY;  // list not full yet: take everything
+  float b;
+  if (METRIC == kMetricIP || METRIC == kMetricMIPS) {
+    b = -T;
+  } else if (METRIC == kMetricCosine) {
+    if (qa == 0.f) return -INFINITY;  // zero query: ranks are 0/1, check exactly
+    b = (1.f - T) / qa;
+  } else {
+    b = 0.5f * (qn2 - T);
+  }
+  return b - fabsf(b) * 6.1035156e-5f - 1e-30f;  // 2^-14 relative slack
+}
+
+// Keeps the kp smallest keys of a candidate list (global memory, unsorted)
+// and returns the kp-th smallest.  The warp loads the list once into
+// registers (kCap/32 keys per lane, all loads in flight together), runs a
+// radix select over the 64-bit keys (8 passes of 8 bits, histogram in
+// shared memory) and writes the kept keys back in order.  Keys are unique,
+// so exactly kp remain.
+__device__ __forceinline__ uint64_t warp_select_compact(uint64_t* gbuf, int cnt, int kp,
+                                                     int* hist) {
+  constexpr int kPer = kCap / 32;
   const int lane = threadIdx.x & 31;
   __syncwarp();  // the owning lane's appends are visible to the warp
-  for (int i = lane; i < kCap; i += 32) scratch[i] = i < cnt ? gbuf[i] : kEmptyKey;
+  uint64_t keys[kPer];
+#pragma unroll
+  for (int e = 0; e < kPer; ++e) {
+    const int i = e * 32 + lane;
+    keys[e] = i < cnt ? gbuf[i] : kEmptyKey;
+  }
+  uint64_t prefix = 0;
+  int kth = kp;
+#pragma unroll 1
+  for (int shift = 56; shift >= 0; shift -= 8) {
+    for (int b = lane; b < 256; b += 32) hist[b] = 0;
+    __syncwarp();
+    const uint64_t mask = shift == 56 ? 0ull : (~0ull << (shift + 8));
+#pragma unroll
+    for (int e = 0; e < kPer; ++e)
+      if (e * 32 + lane < cnt && (keys[e] & mask) == prefix)
+        atomicAdd(&hist[(keys[e] >> shift) & 0xff], 1);
+    __syncwarp();
+    // Lane l owns bins 8l..8l+7: find the bin where the running count
+    // reaches kth.
+    int local[8], sum = 0;
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+      local[b] = hist[lane * 8 + b];
+      sum += local[b];
+    }
+    int incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(kFullMask, incl, o);
+      if (lane >= o) incl += v;
+    }
+    const int excl = incl - sum;
+    const unsigned owner = __ballot_sync(kFullMask, excl < kth && kth <= incl);
+    const int src = __ffs(owner) - 1;
+    int digit = 0, rem = kth - excl;
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+      if (rem > 0 && rem <= local[b]) {
+        digit = lane * 8 + b;
+        rem = -rem;  // found: stop matching further bins
+      } else if (rem > 0) {
+        rem -= local[b];
+      }
+    }
+    digit = __shfl_sync(kFullMask, digit, src);
+    kth = -__shfl_sync(kFullMask, rem, src);
+    prefix |= (uint64_t)digit << shift;
+    __syncwarp();
+  }
+  // prefix is the kp-th smallest key; keep every key <= prefix, in order of
+  // their slots.
+  int out = 0;
+#pragma unroll
+  for (int e = 0; e < kPer; ++e) {
+    const bool keep = e * 32 + lane < cnt && keys[e] <= prefix;
+    const unsigned m = __ballot_sync(kFullMask, keep);
+    if (keep) gbuf[out + __popc(m & ((1u << lane) - 1))] = keys[e];
+    out += __popc(m);
+  }
   __syncwarp();
-  warp_sort_u64<kCap>(scratch);
-  const int keep = min(cnt, kp);
-  for (int i = lane; i < keep; i += 32) gbuf[i] = scratch[i];
-  __syncwarp();
-  if (cnt >= kp) *thr_out = scratch[kp - 1];
+  return prefix;
 }
 
 template <int METRIC>
@@ -177,14 +266,15 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
     const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap rmap, int nq,
     int64_t n, int d, const float* __restrict__ row_aux, const uint32_t* __restrict__ keyrank,
     const float* __restrict__ q_aux, const float* __restrict__ q_n2,
-    const uint64_t* __restrict__ q_seed, const uint32_t* __restrict__ bitmap,
+    unsigned long long* __restrict__ gthr, const uint32_t* __restrict__ bitmap,
     int64_t rows_per_part, int kp, uint64_t* __restrict__ cand, int* __restrict__ part_counts,
     uint64_t* __restrict__ part_sat, int* __restrict__ q_flags, int* __restrict__ status) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   unsigned char* tiles = smem;  // kStages x (A | B)
-  uint64_t* scratch = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);  // 4 x kCap
-  uint64_t* bars = scratch + 4 * kCap;
+  int* hist_all = reinterpret_cast<int*>(smem + kStages * kStageBytes);  // kEpiWarps x 256
+  uint32_t* meta_all = reinterpret_cast<uint32_t*>(hist_all + kEpiWarps * 256);  // x 256
+  uint64_t* bars = reinterpret_cast<uint64_t*>(meta_all + kEpiWarps * 256);
   uint64_t* full = bars;               // [kStages]
   uint64_t* empty = bars + kStages;    // [kStages]
   uint64_t* tfull = bars + 2 * kStages;   // [2]
@@ -209,7 +299,7 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 128);
+      mbar_init(&tempty[a], kEpiWarps * 32);
     }
     mbar_init(mdone, 1);
     *s_abort = 0;
@@ -303,89 +393,163 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
     }
   } else {
     // ---------------- epilogue ----------------
-    const int quarter = warp & 3;  // TMEM lanes this warp may access
-    const int ew = warp - 2;       // epilogue warp index for scratch
+    const int quarter = warp & 3;            // TMEM lanes this warp may access
+    const int ew = warp - 2;                 // 0..7
+    const int half = ew >> 2;                // column half of each tile
     const int qlocal = quarter * 32 + lane;
     const int qi = qblock * kBM + qlocal;
     const bool qvalid = qi < nq;
     const float qa = qvalid ? q_aux[qi] : 0.f;
     const float qn2 = qvalid ? q_n2[qi] : 0.f;
-    uint64_t thr = (qvalid && q_seed) ? q_seed[qi] : kEmptyKey;
-    uint32_t thr_hi = (uint32_t)(thr >> 32);
+    // Per-query thresholds are shared by every list of the query (gthr,
+    // lowered with atomicMin after each compaction): a list may drop any key
+    // above another list's kp-th key, so only the first lists of a query pay
+    // for filling up.
+    uint64_t thr = qvalid ? (uint64_t)*(volatile unsigned long long*)&gthr[qi] : kEmptyKey;
+    float thr_f = rank_of(thr);  // NaN while the list is not full: accept all
+    float tq = score_bound<METRIC>(thr_f, qa, qn2);
     int cnt = 0;
     int nonfinite = 0;
-    uint64_t* gbuf = cand + ((int64_t)(qvalid ? qi : 0) * num_parts + part) * kCap;
-    uint64_t* wscratch = scratch + ew * kCap;
+    const int list = part * 2 + half;
+    const int num_lists = num_parts * 2;
+    uint64_t* gbuf = cand + ((int64_t)(qvalid ? qi : 0) * num_lists + list) * kCap;
+    int* hist = hist_all + ew * 256;
+    float* meta_aux = reinterpret_cast<float*>(meta_all + ew * 256);  // [128]
+    uint32_t* meta_kr = meta_all + ew * 256 + 128;                     // [128]
+    // Row metadata (aux, key rank, filter) of this warp's 128 columns is
+    // loaded one tile ahead into registers and staged in shared memory, so
+    // neither the scoring loop nor the append path waits on global memory.
+    float pf_aux[4];
+    uint32_t pf_kr[4], pf_vm[4];
+    auto prefetch = [&](int t) {
+      const int64_t base = row_begin + (int64_t)t * kBN + half * 128;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int64_t row = base + c * 32 + lane;
+        const bool ok = t < num_tiles && row < row_end && bitmap_pass(bitmap, row);
+        const float ra = (ok && METRIC != kMetricIP) ? row_aux[row] : 0.f;
+        pf_aux[c] = METRIC == kMetricL2 ? -0.5f * ra : ra;
+        pf_kr[c] = ok ? keyrank[row] : 0u;
+        pf_vm[c] = __ballot_sync(kFullMask, ok);
+      }
+    };
+    prefetch(0);
     for (int t = 0; t < num_tiles; ++t) {
       const int acc = t & 1;
       const uint32_t acc_phase = (t >> 1) & 1;
+      uint32_t vm[4];
+      __syncwarp();
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        meta_aux[c * 32 + lane] = pf_aux[c];
+        meta_kr[c * 32 + lane] = pf_kr[c];
+        vm[c] = pf_vm[c];
+      }
+      __syncwarp();
+      prefetch(t + 1);
+      if (qvalid) {
+        const uint64_t g = *(volatile unsigned long long*)&gthr[qi];
+        if (g < thr) {
+          thr = g;
+          thr_f = rank_of(thr);
+          tq = score_bound<METRIC>(thr_f, qa, qn2);
+        }
+      }
       if (!mbar_wait(&tfull[acc], acc_phase, s_abort)) {
         atomicExch(status, 4);
         *s_abort = 1;
         break;
       }
       tmem_fence_after();
-      const int64_t tile_row = row_begin + (int64_t)t * kBN;
-#pragma unroll 1
-      for (int c = 0; c < kBN / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * kBN + c * 32, v);
-        const int64_t row0 = tile_row + c * 32;
-        const int64_t my_row = row0 + lane;
-        const bool rvalid = my_row < row_end && bitmap_pass(bitmap, my_row);
-        const float aux = rvalid ? (METRIC == kMetricIP ? 0.f : row_aux[my_row]) : 0.f;
-        const uint32_t kr = rvalid ? keyrank[my_row] : 0u;
-        const uint32_t vmask = __ballot_sync(kFullMask, rvalid);
-        if (vmask != 0) {
+      const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * kBN + half * 128;
+      uint32_t va[32], vb[32];
+      tmem_ld32(taddr, va);
+      tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float a = __shfl_sync(kFullMask, aux, j);
-            const uint32_t krj = __shfl_sync(kFullMask, kr, j);
-            if (!qvalid || !((vmask >> j) & 1u)) continue;
-            const float r = tc_rank<METRIC>(__uint_as_float(v[j]), a, qa, qn2);
-            const uint32_t hi = float_to_ordered(r);
-            if (hi <= thr_hi || hi >= 0xff800000u) {
-              if (!isfinite(r)) {
-                nonfinite = 1;
-              } else {
-                const uint64_t key = ((uint64_t)hi << 32) | krj;
-                if (key < thr) gbuf[cnt++] = key;
-              }
-            }
+      for (int c = 0; c < 4; ++c) {
+        uint32_t(&cur)[32] = (c & 1) ? vb : va;
+        uint32_t(&nxt)[32] = (c & 1) ? va : vb;
+        if (c + 1 < 4) tmem_ld32(taddr + (c + 1) * 32, nxt);
+        const uint32_t vmask = qvalid ? vm[c] : 0u;
+        // Rare path: the exact fast rank and key of column j, appended when
+        // below the list threshold.
+        auto rare = [&](int j, float a) {
+          const float ra = METRIC == kMetricL2 ? -2.f * a : a;
+          const float r = tc_rank<METRIC>(__uint_as_float(cur[j]), ra, qa, qn2);
+          if (!isfinite(r)) {
+            nonfinite = 1;
+          } else {
+            const uint64_t key = pack_rank(r, meta_kr[c * 32 + j]);
+            if (key < thr) gbuf[cnt++] = key;
+          }
+        };
+        auto score = [&](int j, float a) -> float {
+          const float dot = __uint_as_float(cur[j]);
+          if (METRIC == kMetricIP) return dot;
+          if (METRIC == kMetricCosine) return dot * a;
+          if (METRIC == kMetricL2) return dot + a;
+          return -tc_rank<METRIC>(dot, a, qa, qn2);
+        };
+        const float4* a4 = reinterpret_cast<const float4*>(meta_aux + c * 32);
+        if (vmask == kFullMask) {
+#pragma unroll
+          for (int g = 0; g < 8; ++g) {
+            const float4 av = a4[g];
+            const float aa[4] = {av.x, av.y, av.z, av.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              if (score(g * 4 + e, aa[e]) >= tq) rare(g * 4 + e, aa[e]);
+          }
+        } else if (vmask != 0u) {
+#pragma unroll
+          for (int g = 0; g < 8; ++g) {
+            const float4 av = a4[g];
+            const float aa[4] = {av.x, av.y, av.z, av.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              if (((vmask >> (g * 4 + e)) & 1u) && score(g * 4 + e, aa[e]) >= tq)
+                rare(g * 4 + e, aa[e]);
           }
         }
-        // Make room for the next 32 appends.
-        uint32_t need = __ballot_sync(kFullMask, cnt > kCap - 32);
-        while (need) {
-          const int who = __ffs(need) - 1;
-          need &= need - 1;
-          const int wcnt = __shfl_sync(kFullMask, cnt, who);
-          uint64_t* wbuf = cand + ((int64_t)(qblock * kBM + quarter * 32 + who) * num_parts + part) * kCap;
-          uint64_t new_thr = __shfl_sync(kFullMask, thr, who);
-          warp_compact_global(wbuf, wscratch, wcnt, kp, &new_thr);
-          new_thr = __shfl_sync(kFullMask, new_thr, 0);
-          if (lane == who) {
-            thr = new_thr;
-            thr_hi = (uint32_t)(thr >> 32);
-            cnt = min(cnt, kp);
-          }
-        }
+        if (c + 1 < 4) tmem_wait_ld();
       }
+      // Release the accumulator to the MMA warp before any compaction.
       tmem_fence_before();
       mbar_arrive(&tempty[acc]);
+      // Keep room for the next tile's appends (at most 128 per list).
+      uint32_t need = __ballot_sync(kFullMask, cnt > kCap - 128);
+      while (need) {
+        const int who = __ffs(need) - 1;
+        need &= need - 1;
+        const int wcnt = __shfl_sync(kFullMask, cnt, who);
+        uint64_t* wbuf =
+            cand + ((int64_t)(qblock * kBM + quarter * 32 + who) * num_lists + list) * kCap;
+        const uint64_t new_thr = warp_select_compact(wbuf, wcnt, kp, hist);
+        if (lane == who) {
+          if (new_thr < thr) {
+            thr = new_thr;
+            thr_f = rank_of(thr);
+            tq = score_bound<METRIC>(thr_f, qa, qn2);
+            atomicMin(&gthr[qi], (unsigned long long)thr);
+          }
+          cnt = kp;
+        }
+      }
     }
-    // Final compaction of every query of the warp, then publish the part.
+    // Publish each list: at most kp keys (unsorted) and its saturation key.
     for (int who = 0; who < 32; ++who) {
-      const int wcnt = __shfl_sync(kFullMask, cnt, who);
       const int wq = qblock * kBM + quarter * 32 + who;
       if (wq >= nq) continue;
-      uint64_t* wbuf = cand + ((int64_t)wq * num_parts + part) * kCap;
-      uint64_t new_thr = __shfl_sync(kFullMask, thr, who);
-      warp_compact_global(wbuf, wscratch, wcnt, kp, &new_thr);
-      new_thr = __shfl_sync(kFullMask, new_thr, 0);
+      const int wcnt = __shfl_sync(kFullMask, cnt, who);
+      uint64_t wthr = __shfl_sync(kFullMask, thr, who);
+      uint64_t* wbuf = cand + ((int64_t)wq * num_lists + list) * kCap;
+      if (wcnt > kp) {
+        const uint64_t c = warp_select_compact(wbuf, wcnt, kp, hist);
+        wthr = c < wthr ? c : wthr;
+      }
       if (lane == 0) {
-        part_counts[(int64_t)wq * num_parts + part] = min(wcnt, kp);
-        part_sat[(int64_t)wq * num_parts + part] = new_thr;
+        part_counts[(int64_t)wq * num_lists + list] = min(wcnt, kp);
+        part_sat[(int64_t)wq * num_lists + list] = wthr;
       }
     }
     if (qvalid && nonfinite) atomicOr(&q_flags[qi], 1);
@@ -441,11 +605,12 @@ bool flat_tc_supported(int d, const void* rows, const void* queries) {
 }
 
 int flat_tc_cap() { return tc::kCap; }
+int flat_tc_lists_per_part() { return 2; }
 
 cudaError_t launch_flat_scan_tc(int metric, const __half* queries, int nq, const __half* rows,
                                 int64_t n, int d, int64_t row_stride_elems, const float* row_aux,
                                 const uint32_t* keyrank, const float* q_aux, const float* q_n2,
-                                const uint64_t* q_seed, const uint32_t* bitmap, int num_parts,
+                                unsigned long long* gthr, const uint32_t* bitmap, int num_parts,
                                 int kp, uint64_t* cand, int* part_counts, uint64_t* part_sat,
                                 int* q_flags, int* status, cudaStream_t stream) {
   CUtensorMap qmap, rmap;
@@ -460,7 +625,7 @@ cudaError_t launch_flat_scan_tc(int metric, const __half* queries, int nq, const
     auto kern = tc::flat_scan_tc_kernel<M>;                                                 \
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);         \
     kern<<<grid, tc::kThreads, smem, stream>>>(qmap, rmap, nq, n, d, row_aux, keyrank, q_aux, \
-                                               q_n2, q_seed, bitmap, rows_per_part, kp, cand, \
+                                               q_n2, gthr, bitmap, rows_per_part, kp, cand,   \
                                                part_counts, part_sat, q_flags, status);      \
     break;                                                                                  \
   }

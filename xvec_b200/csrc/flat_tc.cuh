@@ -10,18 +10,21 @@ namespace xvec {
 // True when the TMA/UMMA path can take this layout (d % 8 == 0, d >= 64,
 // 16-byte aligned operands, driver entry point available).
 bool flat_tc_supported(int d, const void* rows, const void* queries);
-// Candidate buffer entries per (query, part); parts are stored with this stride.
+// Candidate list entries per (query, list); lists are stored with this stride.
 int flat_tc_cap();
+// Candidate lists per row part (one per column half of the tile).
+int flat_tc_lists_per_part();
 
 // Scans rows [0, n) (row i at rows + i * row_stride_elems) against nq queries.
 // row_aux: 1/||x|| for cosine, ||x||^2 for L2 / MIPS (unused for IP);
-// q_aux: 1/||q|| for cosine, ||q||^2 otherwise.  q_seed (optional): initial
-// per-query key threshold.  status != 0 after the launch = a bounded wait
-// expired (the results are then invalid).
+// q_aux: 1/||q|| for cosine, ||q||^2 otherwise.  gthr: per-query key
+// thresholds shared by all lists of a query (initialise to all ones).
+// status != 0 after the launch = a bounded wait expired (the results are
+// then invalid).
 cudaError_t launch_flat_scan_tc(int metric, const __half* queries, int nq, const __half* rows,
                                 int64_t n, int d, int64_t row_stride_elems, const float* row_aux,
                                 const uint32_t* keyrank, const float* q_aux, const float* q_n2,
-                                const uint64_t* q_seed, const uint32_t* bitmap, int num_parts,
+                                unsigned long long* gthr, const uint32_t* bitmap, int num_parts,
                                 int kp, uint64_t* cand, int* part_counts, uint64_t* part_sat,
                                 int* q_flags, int* status, cudaStream_t stream);
 
