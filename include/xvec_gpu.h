@@ -190,6 +190,26 @@ xvec_gpu_status xvec_gpu_merge_results_device(int32_t device, int32_t metric, in
                                               uint64_t* d_out_keys, float* d_out_scores,
                                               int32_t* d_out_counts, void* stream);
 
+/* Flat search that allocates no device memory during the call (no
+ * counterpart in the reference).  For callers that cannot allocate while they
+ * search: a process that plans a fixed device-memory budget up front, or a
+ * latency-critical caller that must not enter the CUDA allocator (which can
+ * block or synchronise the device).  Same inputs, outputs and results as
+ * xvec_gpu_index_search_device on a Flat index; the per-call scratch comes
+ * from one 32 MiB device array that every GPU loading the library holds until
+ * exit.  Limits: at most 4096 queries, top-k <= 100, no filter bitmap, and
+ * the scratch the batch needs must fit in 32 MiB (otherwise
+ * XVEC_GPU_INVALID_ARGUMENT).  All calls share the array: calls whose GPU
+ * work overlaps race (the library serialises calls from one process and each
+ * call waits for its GPU work).  The first call on a device looks up the
+ * array's device address (which also makes the CUDA runtime load the
+ * library's device code there, reserving the array); make that first call
+ * before any stream capture. */
+xvec_gpu_status xvec_gpu_index_search_noalloc(xvec_gpu_index* index, const void* d_queries,
+                                              int32_t nq, const xvec_gpu_search_opts* opts,
+                                              uint64_t* d_out_keys, float* d_out_scores,
+                                              int32_t* d_out_counts);
+
 /* Counters (the reference's RuntimeStats role, collection.go:5185-5315, for
  * the device path).  Device-time fields are filled only while timing is
  * enabled, because timing adds an event pair around each scan launch. */

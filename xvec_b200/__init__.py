@@ -50,6 +50,7 @@ EXPORTED_SYMBOLS = (
     "xvec_gpu_rabitq_set_model", "xvec_gpu_index_search", "xvec_gpu_index_search_device",
     "xvec_gpu_kmeans_assign", "xvec_gpu_kmeans_assign_device", "xvec_gpu_merge_results_device",
     "xvec_gpu_stats_enable_timing", "xvec_gpu_get_stats", "xvec_gpu_reset_stats",
+    "xvec_gpu_index_search_noalloc",
 )
 
 
@@ -103,6 +104,8 @@ def _load() -> ctypes.CDLL:
     lib.xvec_gpu_kmeans_assign.argtypes = [i32, i32, vp, i64, vp, i32, i32, vp, vp]
     lib.xvec_gpu_kmeans_assign_device.argtypes = [i32, i32, vp, i64, vp, i32, i32, vp, vp, vp]
     lib.xvec_gpu_merge_results_device.argtypes = [i32, i32, i32, i32, i32, vp, vp, vp, vp, vp,
+                                                  vp, vp]
+    lib.xvec_gpu_index_search_noalloc.argtypes = [vp, vp, i32, ctypes.POINTER(SearchOpts), vp,
                                                   vp, vp]
     lib.xvec_gpu_stats_enable_timing.argtypes = [i32]
     lib.xvec_gpu_get_stats.argtypes = [ctypes.POINTER(Stats)]
@@ -274,7 +277,18 @@ class _Index:
                                                  out_keys_ptr, out_scores_ptr, out_counts_ptr))
 
 
-class DenseFlatIndex(_Index):
+class _NoAllocMixin:
+    def search_device_noalloc(self, queries_ptr: int, nq: int, options: SearchOptions,
+                              out_keys_ptr: int, out_scores_ptr: int, out_counts_ptr: int,
+                              stream: int = 0) -> None:
+        """xvec_gpu_index_search_noalloc: the Flat search without device allocations,
+        for callers that cannot allocate while searching (see include/xvec_gpu.h)."""
+        o = self._opts(options, stream=stream or None)
+        _check(_lib.xvec_gpu_index_search_noalloc(self._h, queries_ptr, nq, ctypes.byref(o),
+                                                  out_keys_ptr, out_scores_ptr, out_counts_ptr))
+
+
+class DenseFlatIndex(_NoAllocMixin, _Index):
     """core.DenseFlatIndex (internal/core/flat.go:70-196) on one B200.
 
     storage=STORAGE_FP16 keeps rows as binary16 bit patterns (uint16) and takes
