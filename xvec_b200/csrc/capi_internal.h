@@ -89,6 +89,8 @@ struct xvec_gpu_index {
   // SQ8.
   xvec::DeviceBuffer sq_codes;   // int8 [n][d]
   xvec::DeviceBuffer sq_params;  // {float inv_scale, float offset, double sum, double square}
+  xvec::DeviceBuffer sq_fast;    // float4 {inv_scale, offset, code sum, ||decoded||^2}
+  xvec::DeviceBuffer sq_bounds;  // 4 ordered floats: error-bound maxima over rows
 
   // IVF-PQ.
   int32_t nlist = 0, chunks = 0;

@@ -73,6 +73,7 @@ constexpr uint64_t kEmptyKey = 0xffffffffffffffffull;
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float load_elem(const float* p, int64_t i) { return p[i]; }
 __device__ __forceinline__ float load_elem(const __half* p, int64_t i) { return __half2float(p[i]); }
+__device__ __forceinline__ float load_elem(const int8_t* p, int64_t i) { return (float)p[i]; }
 
 // Go's min/max built-ins on floats propagate NaN.
 __device__ __forceinline__ float go_minf(float a, float b) {
@@ -92,6 +93,13 @@ __device__ __forceinline__ double go_maxd(double a, double b) {
   return a > b ? a : b;
 }
 __device__ __forceinline__ bool finite_f(float v) { return isfinite(v); }
+// Go's min/max on float32 also order the zeros: min(-0, +0) = -0, max = +0.
+__device__ __forceinline__ float go_min_zero(float a, float b) {
+  return (a < b || (a == b && signbit(a))) ? a : b;
+}
+__device__ __forceinline__ float go_max_zero(float a, float b) {
+  return (a > b || (a == b && !signbit(a))) ? a : b;
+}
 
 // ---------------------------------------------------------------------------
 // Reference-order accumulation, evaluated by one warp (all 32 lanes call it;

@@ -3,17 +3,18 @@
 
 namespace xvec {
 
-xvec_gpu_status extra_reserve(xvec_gpu_index*, int64_t, cudaStream_t) { return XVEC_GPU_OK; }
+xvec_gpu_status extra_reserve(xvec_gpu_index* idx, int64_t cap, cudaStream_t s) {
+  if (idx->desc.kind == XVEC_INDEX_SQ8_FLAT) return sq8_reserve(idx, cap, s);
+  return XVEC_GPU_OK;
+}
 xvec_gpu_status extra_validate(xvec_gpu_index* idx, int64_t, int64_t, cudaStream_t) {
-  if (idx->desc.kind != XVEC_INDEX_FLAT)
+  if (idx->desc.kind == XVEC_INDEX_IVF_PQ || idx->desc.kind == XVEC_INDEX_RABITQ)
     return set_error("index kind not available yet"), XVEC_GPU_UNSUPPORTED;
   return XVEC_GPU_OK;
 }
-xvec_gpu_status extra_commit(xvec_gpu_index*, int64_t, int64_t, cudaStream_t) { return XVEC_GPU_OK; }
-xvec_gpu_status sq8_search_impl(xvec_gpu_index*, const float*, int, const xvec_gpu_search_opts&,
-                                const uint32_t*, uint64_t*, float*, int*, cudaStream_t,
-                                std::vector<int>*) {
-  return set_error("index kind not available yet"), XVEC_GPU_UNSUPPORTED;
+xvec_gpu_status extra_commit(xvec_gpu_index* idx, int64_t old_n, int64_t m, cudaStream_t s) {
+  if (idx->desc.kind == XVEC_INDEX_SQ8_FLAT) return sq8_commit(idx, old_n, m, s);
+  return XVEC_GPU_OK;
 }
 xvec_gpu_status ivfpq_search_impl(xvec_gpu_index*, const float*, int, const xvec_gpu_search_opts&,
                                   const uint32_t*, uint64_t*, float*, int*, cudaStream_t,

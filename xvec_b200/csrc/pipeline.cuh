@@ -1,0 +1,455 @@
+// pipeline.cuh — the candidate pipeline shared by every index kind.
+//
+//   scan (fast)   : a Ranker turns a dot product into a fast rank; each
+//                   (query, row part) keeps its KP best packed keys.
+//   scan (exact)  : a Scorer gives the reference score of one (query, row);
+//                   the same per-part selection, used when the fast pass
+//                   cannot prove its candidate set complete.
+//   merge_rescore : per query, the k-th best key over all parts, the
+//                   candidates within the Scorer's error bound, their
+//                   reference scores, the final (score, key) order, radius
+//                   and top-k (optionally the row positions as well).
+//
+// Ranker:  struct RowInfo; struct QueryInfo;
+//          QueryInfo query(int qi); RowInfo row(int64_t row);
+//          float rank(float dot, const RowInfo&, const QueryInfo&);
+// Scorer:  int metric (ordering and radius rule);
+//          float score(int qi, int64_t row)  -- called by a whole warp;
+//          float eps(int qi)                  -- bound on |fast - reference|;
+//          int error_flag(float s)            -- flag bit for a non-finite score.
+#pragma once
+
+#include "common.cuh"
+#include "select.cuh"
+
+namespace xvec {
+
+// ---------------------------------------------------------------------------
+// Fast FFMA scan: block = 256 threads, tile = 64 rows x 32 queries, k-step 32.
+// Thread (ty, tx) owns rows ty*4..ty*4+3 and queries tx*2, tx*2+1.
+// ---------------------------------------------------------------------------
+constexpr int kSimtQT = 32;
+constexpr int kSimtRT = 64;
+constexpr int kSimtKT = 32;
+
+template <typename RowT, int CAP, typename Ranker>
+__global__ void __launch_bounds__(256) scan_simt_kernel(
+    const RowT* __restrict__ rows, int64_t n, int d, const uint32_t* __restrict__ keyrank,
+    const float* __restrict__ qf, int nq, const uint32_t* __restrict__ bitmap, Ranker rk,
+    int64_t rows_per_part, int kp, uint64_t* __restrict__ part_keys,
+    int* __restrict__ part_counts, uint64_t* __restrict__ part_sat, int* __restrict__ q_flags) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  uint64_t* buf = reinterpret_cast<uint64_t*>(smem_raw);                       // [QT][CAP]
+  float* xs = reinterpret_cast<float*>(buf + kSimtQT * CAP);                    // [KT][RT+4]
+  float* qs = xs + kSimtKT * (kSimtRT + 4);                                     // [KT][QT+4]
+  __shared__ AccumState st[kSimtQT];
+
+  const int tid = threadIdx.x;
+  const int tx = tid & 15, ty = tid >> 4;
+  const int q0 = blockIdx.x * kSimtQT;
+  const int part = blockIdx.y;
+  const int num_parts = gridDim.y;
+  const int64_t row_begin = (int64_t)part * rows_per_part;
+  const int64_t row_end = min(n, row_begin + rows_per_part);
+
+  if (tid < kSimtQT) {
+    st[tid].count = 0;
+    st[tid].saturated = 0;
+    st[tid].thr = kEmptyKey;
+  }
+  typename Ranker::QueryInfo qinfo[2];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int qi = q0 + tx * 2 + j;
+    qinfo[j] = rk.query(qi < nq ? qi : 0);
+  }
+  __syncthreads();
+
+  for (int64_t tile = row_begin; tile < row_end; tile += kSimtRT) {
+    float acc[4][2];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[i][0] = acc[i][1] = 0.f;
+    for (int k0 = 0; k0 < d; k0 += kSimtKT) {
+      __syncthreads();
+      for (int e = tid; e < kSimtRT * kSimtKT; e += 256) {
+        const int r = e / kSimtKT, kk = e % kSimtKT;
+        const int64_t row = tile + r;
+        const int k = k0 + kk;
+        xs[kk * (kSimtRT + 4) + r] = (row < row_end && k < d) ? load_elem(rows, row * d + k) : 0.f;
+      }
+      for (int e = tid; e < kSimtQT * kSimtKT; e += 256) {
+        const int qq = e / kSimtKT, kk = e % kSimtKT;
+        const int qi = q0 + qq;
+        const int k = k0 + kk;
+        qs[kk * (kSimtQT + 4) + qq] = (qi < nq && k < d) ? qf[(int64_t)qi * d + k] : 0.f;
+      }
+      __syncthreads();
+#pragma unroll 8
+      for (int kk = 0; kk < kSimtKT; ++kk) {
+        const float4 a = *reinterpret_cast<const float4*>(&xs[kk * (kSimtRT + 4) + ty * 4]);
+        const float2 b = *reinterpret_cast<const float2*>(&qs[kk * (kSimtQT + 4) + tx * 2]);
+        acc[0][0] = fmaf(a.x, b.x, acc[0][0]);
+        acc[0][1] = fmaf(a.x, b.y, acc[0][1]);
+        acc[1][0] = fmaf(a.y, b.x, acc[1][0]);
+        acc[1][1] = fmaf(a.y, b.y, acc[1][1]);
+        acc[2][0] = fmaf(a.z, b.x, acc[2][0]);
+        acc[2][1] = fmaf(a.z, b.y, acc[2][1]);
+        acc[3][0] = fmaf(a.w, b.x, acc[3][0]);
+        acc[3][1] = fmaf(a.w, b.y, acc[3][1]);
+      }
+    }
+    // Epilogue: rank, filter, append.
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int64_t row = tile + ty * 4 + i;
+      if (row >= row_end || !bitmap_pass(bitmap, row)) continue;
+      const typename Ranker::RowInfo rinfo = rk.row(row);
+      const uint32_t kr = keyrank[row];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int ql = tx * 2 + j;
+        const int qi = q0 + ql;
+        if (qi >= nq) continue;
+        const float r = rk.rank(acc[i][j], rinfo, qinfo[j]);
+        if (!finite_f(r)) {
+          atomicOr(&q_flags[qi], 1);
+          continue;
+        }
+        const uint64_t key = pack_rank(r, kr);
+        if (key < st[ql].thr) {
+          const int slot = atomicAdd(&st[ql].count, 1);
+          buf[ql * CAP + slot] = key;
+        }
+      }
+    }
+    __syncthreads();
+    // Keep room for one more tile of appends per query.
+    const int warp = tid >> 5;
+    for (int ql = warp; ql < kSimtQT; ql += 8)
+      if (st[ql].count > CAP - kSimtRT) warp_compact<CAP>(buf + ql * CAP, &st[ql], kp);
+    __syncthreads();
+  }
+  // Final compaction and write-out of this part's sorted list.
+  const int warp = tid >> 5, lane = tid & 31;
+  for (int ql = warp; ql < kSimtQT; ql += 8) {
+    const int qi = q0 + ql;
+    if (qi >= nq) continue;
+    warp_compact<CAP>(buf + ql * CAP, &st[ql], kp);
+    // warp_compact only trims when count >= kp; sort happened regardless.
+    const int cnt = min(st[ql].count, kp);
+    const int64_t base = ((int64_t)qi * num_parts + part) * kp;
+    for (int i = lane; i < cnt; i += 32) part_keys[base + i] = buf[ql * CAP + i];
+    if (lane == 0) {
+      part_counts[(int64_t)qi * num_parts + part] = cnt;
+      part_sat[(int64_t)qi * num_parts + part] = st[ql].thr;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Exact scan: reference-order scores for one query per block (8 warps, each
+// scoring rows in turn).  Used when the fast candidate set cannot be proven
+// complete, and for top-k beyond the fast scan's capacity.
+// ---------------------------------------------------------------------------
+template <int CAP, typename Scorer>
+__global__ void __launch_bounds__(256) scan_exact_kernel(
+    Scorer sc, int64_t n, const uint32_t* __restrict__ keyrank, const int* __restrict__ query_ids,
+    const uint32_t* __restrict__ bitmap, int64_t rows_per_part, int kp,
+    uint64_t* __restrict__ part_keys, int* __restrict__ part_counts,
+    uint64_t* __restrict__ part_sat, int* __restrict__ q_flags) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  uint64_t* buf = reinterpret_cast<uint64_t*>(smem_raw);
+  __shared__ AccumState st;
+  constexpr int kRowsPerRound = 8 * 16;
+  const int qi = query_ids[blockIdx.x];
+  const int slot_q = blockIdx.x;  // part buffers are indexed by list slot
+  const int part = blockIdx.y, num_parts = gridDim.y;
+  const int64_t row_begin = (int64_t)part * rows_per_part;
+  const int64_t row_end = min(n, row_begin + rows_per_part);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    st.count = 0;
+    st.saturated = 0;
+    st.thr = kEmptyKey;
+  }
+  __syncthreads();
+  for (int64_t round = row_begin; round < row_end; round += kRowsPerRound) {
+    for (int j = 0; j < 16; ++j) {
+      const int64_t row = round + j * 8 + warp;
+      if (row >= row_end || !bitmap_pass(bitmap, row)) continue;
+      const float s = sc.score(qi, row);
+      if (lane == 0) {
+        if (!finite_f(s)) {
+          atomicOr(&q_flags[qi], sc.error_flag(s));
+        } else {
+          const uint64_t key = pack_rank(rank_from_score(sc.metric, s), keyrank[row]);
+          if (key < st.thr) {
+            const int slot = atomicAdd(&st.count, 1);
+            buf[slot] = key;
+          }
+        }
+      }
+    }
+    __syncthreads();
+    if (warp == 0 && st.count > CAP - kRowsPerRound) warp_compact<CAP>(buf, &st, kp);
+    __syncthreads();
+  }
+  if (warp == 0) {
+    warp_compact<CAP>(buf, &st, kp);
+    const int cnt = min(st.count, kp);
+    const int64_t base = ((int64_t)slot_q * num_parts + part) * kp;
+    for (int i = lane; i < cnt; i += 32) part_keys[base + i] = buf[i];
+    if (lane == 0) {
+      part_counts[(int64_t)slot_q * num_parts + part] = cnt;
+      part_sat[(int64_t)slot_q * num_parts + part] = st.thr;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Merge + reference rescoring.  One block (256 threads) per query.
+// exact_mode: the part keys already hold reference ranks; the candidates are
+// exactly the k best keys.
+// ---------------------------------------------------------------------------
+constexpr int kMaxCandidates = 1024;
+constexpr int kMergeSmemEntries = 12288;  // union entries gathered in shared memory
+
+// Radix select over keys[0, m) in shared memory: the kth smallest (1-based)
+// considering bits [low_bit, 64) only; returns those high bits (low bits 0).
+static __device__ uint64_t smem_radix_select(const uint64_t* keys, int m, int kth, int low_bit,
+                                      int* hist) {
+  __shared__ uint64_t s_prefix;
+  __shared__ int s_kth;
+  if (threadIdx.x == 0) {
+    s_prefix = 0;
+    s_kth = kth;
+  }
+  __syncthreads();
+#pragma unroll 1
+  for (int shift = 56; shift >= low_bit; shift -= 8) {
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+    const uint64_t prefix = s_prefix;
+    const uint64_t mask = (shift == 56) ? 0ull : (~0ull << (shift + 8));
+    for (int i = threadIdx.x; i < m; i += blockDim.x) {
+      const uint64_t key = keys[i];
+      if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 0xff], 1);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int remaining = s_kth, digit = 0;
+      for (; digit < 255; ++digit) {
+        if (remaining <= hist[digit]) break;
+        remaining -= hist[digit];
+      }
+      s_kth = remaining;
+      s_prefix = prefix | ((uint64_t)digit << shift);
+    }
+    __syncthreads();
+  }
+  return s_prefix;
+}
+
+template <typename Scorer>
+__global__ void __launch_bounds__(256) merge_rescore_kernel(
+    Scorer sc, const uint32_t* __restrict__ pos_of_keyrank, const uint64_t* __restrict__ keys,
+    const int* __restrict__ query_ids, int k, float radius, int exact_mode,
+    const uint64_t* __restrict__ part_keys, const int* __restrict__ part_counts,
+    const uint64_t* __restrict__ part_sat, int num_parts, int stride,
+    uint64_t* __restrict__ out_keys, float* __restrict__ out_scores, int* __restrict__ out_counts,
+    uint32_t* __restrict__ out_pos, int* __restrict__ q_flags) {
+  const int metric = sc.metric;
+  extern __shared__ __align__(16) unsigned char merge_smem[];
+  uint64_t* ukeys = reinterpret_cast<uint64_t*>(merge_smem);  // [kMergeSmemEntries]
+  __shared__ int hist[256];
+  __shared__ uint64_t cand[kMaxCandidates];
+  __shared__ int s_offsets[1025];
+  __shared__ int s_ncand, s_fail;
+  const int slot_q = blockIdx.x;
+  const int qi = query_ids ? query_ids[blockIdx.x] : blockIdx.x;
+  const int64_t pbase = (int64_t)slot_q * num_parts;
+
+  // Prefix sums of the list counts (num_parts <= 1024).
+  if (threadIdx.x == 0) {
+    int total = 0;
+    for (int p = 0; p < num_parts; ++p) {
+      s_offsets[p] = total;
+      total += part_counts[pbase + p];
+    }
+    s_offsets[num_parts] = total;
+    s_ncand = 0;
+    s_fail = 0;
+  }
+  __syncthreads();
+  const int total = s_offsets[num_parts];
+  if (total == 0) {
+    if (threadIdx.x == 0) out_counts[qi] = 0;
+    return;
+  }
+  if (total > kMergeSmemEntries) {
+    // Cannot happen with the list sizes the scans produce; route to the
+    // exact path rather than read past the shared buffer.
+    if (threadIdx.x == 0) {
+      atomicOr(&q_flags[qi], 2);
+      out_counts[qi] = 0;
+    }
+    return;
+  }
+  // Gather the union (one warp per list).
+  {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int p = warp; p < num_parts; p += blockDim.x >> 5) {
+      const int off = s_offsets[p], c = s_offsets[p + 1] - off;
+      const uint64_t* src = part_keys + (pbase + p) * stride;
+      for (int j = lane; j < c; j += 32) ukeys[off + j] = src[j];
+    }
+  }
+  __syncthreads();
+  const int kth = min(k, total);
+  uint64_t limit;
+  if (exact_mode) {
+    limit = smem_radix_select(ukeys, total, kth, 0, hist);
+  } else {
+    const uint64_t kr = smem_radix_select(ukeys, total, kth, 32, hist);
+    const float eps = sc.eps(qi);
+    const float t = __fadd_ru(rank_of(kr), 2.f * eps);
+    limit = ((uint64_t)float_to_ordered(t) << 32) | 0xffffffffull;
+    // Coverage: a list dropped only keys above its saturation key.
+    for (int p = threadIdx.x; p < num_parts; p += blockDim.x) {
+      const uint64_t sat = part_sat[pbase + p];
+      if (sat != kEmptyKey && sat <= limit) atomicExch(&s_fail, 1);
+    }
+  }
+  for (int i = threadIdx.x; i < total; i += blockDim.x) {
+    const uint64_t key = ukeys[i];
+    if (key <= limit) {
+      const int slot = atomicAdd(&s_ncand, 1);
+      if (slot < kMaxCandidates) cand[slot] = key;
+    }
+  }
+  __syncthreads();
+  if (s_fail || s_ncand > kMaxCandidates) {
+    if (threadIdx.x == 0) {
+      atomicOr(&q_flags[qi], 2);
+      out_counts[qi] = 0;
+    }
+    return;
+  }
+  const int ncand = s_ncand;
+  // Reference rescoring: one warp per candidate.
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int c = warp; c < ncand; c += blockDim.x >> 5) {
+    const uint32_t kr = pos_of(cand[c]);
+    const uint32_t pos = pos_of_keyrank[kr];
+    const float s = sc.score(qi, pos);
+    if (lane == 0) {
+      if (!finite_f(s)) atomicOr(&q_flags[qi], sc.error_flag(s));
+      cand[c] = pack_rank(rank_from_score(metric, s), kr);
+    }
+  }
+  __syncthreads();
+  block_sort_u64<kMaxCandidates>(cand, ncand);
+  // Final top-k (radius is monotone in the sorted order).
+  if (threadIdx.x < 32) {
+    // Count the prefix within radius with a warp scan over chunks.
+    int count = 0;
+    for (int base = 0; base < ncand && count < k; base += 32) {
+      const int i = base + lane;
+      bool in = i < ncand;
+      float s = 0.f;
+      if (in) {
+        s = score_from_rank(metric, rank_of(cand[i]));
+        in = within_radius(metric, s, radius);
+      }
+      const unsigned m = __ballot_sync(kFullMask, in);
+      const int run = (m == kFullMask) ? 32 : __ffs(~m) - 1;  // leading in-radius run
+      if (lane < run && count + lane < k) {
+        const uint32_t pos = pos_of_keyrank[pos_of(cand[i])];
+        out_keys[(int64_t)qi * k + count + lane] = keys[pos];
+        out_scores[(int64_t)qi * k + count + lane] = s;
+        if (out_pos) out_pos[(int64_t)qi * k + count + lane] = pos;
+      }
+      count = min(k, count + run);
+      if (run < 32) break;
+    }
+    if (lane == 0) out_counts[qi] = count;
+  }
+}
+
+
+template <typename RowT, typename Ranker>
+cudaError_t launch_scan_simt(const RowT* rows, int64_t n, int d, const uint32_t* keyrank,
+                             const float* qf, int nq, const uint32_t* bitmap, const Ranker& rk,
+                             int num_parts, int kp, uint64_t* part_keys, int* part_counts,
+                             uint64_t* part_sat, int* q_flags, cudaStream_t stream) {
+  int need = kp + 2 * kSimtRT, cap = 256;
+  while (cap < need) cap <<= 1;
+  const int64_t rows_per_part =
+      ((n + num_parts - 1) / num_parts + kSimtRT - 1) / kSimtRT * kSimtRT;
+  dim3 grid((nq + kSimtQT - 1) / kSimtQT, num_parts);
+  const size_t tiles = (size_t)(kSimtKT * (kSimtRT + 4) + kSimtKT * (kSimtQT + 4)) * sizeof(float);
+  if (cap == 256) {
+    const size_t smem = (size_t)kSimtQT * 256 * 8 + tiles;
+    auto kern = scan_simt_kernel<RowT, 256, Ranker>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    kern<<<grid, 256, smem, stream>>>(rows, n, d, keyrank, qf, nq, bitmap, rk, rows_per_part,
+                                      kp, part_keys, part_counts, part_sat, q_flags);
+  } else if (cap == 512) {
+    const size_t smem = (size_t)kSimtQT * 512 * 8 + tiles;
+    auto kern = scan_simt_kernel<RowT, 512, Ranker>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    kern<<<grid, 256, smem, stream>>>(rows, n, d, keyrank, qf, nq, bitmap, rk, rows_per_part,
+                                      kp, part_keys, part_counts, part_sat, q_flags);
+  } else {
+    return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+template <typename Scorer>
+cudaError_t launch_scan_exact(const Scorer& sc, int64_t n, const uint32_t* keyrank,
+                              const int* query_ids, int nlist, const uint32_t* bitmap,
+                              int num_parts, int kp, uint64_t* part_keys, int* part_counts,
+                              uint64_t* part_sat, int* q_flags, cudaStream_t stream) {
+  int need = kp + 2 * 128, cap = 512;
+  while (cap < need) cap <<= 1;
+  const int64_t rows_per_part = (n + num_parts - 1) / num_parts;
+  dim3 grid(nlist, num_parts);
+  const size_t smem = (size_t)cap * 8;
+#define XVEC_EXACT_CASE(C)                                                                   \
+  if (cap == C) {                                                                            \
+    auto kern = scan_exact_kernel<C, Scorer>;                                                \
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);      \
+    kern<<<grid, 256, smem, stream>>>(sc, n, keyrank, query_ids, bitmap, rows_per_part, kp,  \
+                                      part_keys, part_counts, part_sat, q_flags);           \
+    return cudaGetLastError();                                                               \
+  }
+  XVEC_EXACT_CASE(512)
+  XVEC_EXACT_CASE(1024)
+  XVEC_EXACT_CASE(2048)
+  XVEC_EXACT_CASE(4096)
+  XVEC_EXACT_CASE(8192)
+#undef XVEC_EXACT_CASE
+  return cudaErrorInvalidValue;
+}
+
+template <typename Scorer>
+cudaError_t launch_merge_rescore(const Scorer& sc, const uint32_t* pos_of_keyrank,
+                                 const uint64_t* keys, const int* query_ids, int nlist, int k,
+                                 float radius, int exact_mode, const uint64_t* part_keys,
+                                 const int* part_counts, const uint64_t* part_sat, int num_parts,
+                                 int stride, uint64_t* out_keys, float* out_scores,
+                                 int* out_counts, uint32_t* out_pos, int* q_flags,
+                                 cudaStream_t stream) {
+  if (nlist <= 0) return cudaSuccess;
+  if (num_parts > 1024) return cudaErrorInvalidValue;
+  const int smem = kMergeSmemEntries * 8;
+  cudaFuncSetAttribute(merge_rescore_kernel<Scorer>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       smem);
+  merge_rescore_kernel<Scorer><<<nlist, 256, smem, stream>>>(
+      sc, pos_of_keyrank, keys, query_ids, k, radius, exact_mode, part_keys, part_counts,
+      part_sat, num_parts, stride, out_keys, out_scores, out_counts, out_pos, q_flags);
+  return cudaGetLastError();
+}
+
+}  // namespace xvec

@@ -1,0 +1,71 @@
+// refine.cuh — exact float32 re-ranking of a small candidate list per query.
+//
+// OriginalVectorRefiner.Refine (internal/core/refiner.go:66-108): the
+// candidates of the approximate stage (distinct keys, already filtered) are
+// rescored with metric.Compute on the original float32 rows, then the k best
+// under (score by metric, ties by ascending key) within the radius are kept.
+// Used by the SQ8 refine stage and the RaBitQ refine stage.
+#pragma once
+
+#include "common.cuh"
+#include "select.cuh"
+
+namespace xvec {
+
+constexpr int kRefineMax = 1024;  // candidates per query
+
+// One block (256 threads) per query.  stage_pos/stage_counts: per query the
+// positions of the approximate stage's results (stride `stage_k`).
+__global__ void __launch_bounds__(256) refine_kernel(
+    const float* __restrict__ rows, int d, int metric, const float* __restrict__ queries,
+    const uint32_t* __restrict__ stage_pos, const int* __restrict__ stage_counts, int stage_k,
+    const uint32_t* __restrict__ keyrank, const uint32_t* __restrict__ pos_of_keyrank,
+    const uint64_t* __restrict__ keys, int k, float radius,
+    uint64_t* __restrict__ out_keys, float* __restrict__ out_scores, int* __restrict__ out_counts,
+    int* __restrict__ q_flags) {
+  __shared__ uint64_t cand[kRefineMax];
+  const int qi = blockIdx.x;
+  const int c = stage_counts[qi];
+  if (c <= 0) {
+    if (threadIdx.x == 0 && c == 0) out_counts[qi] = 0;
+    return;
+  }
+  const int n = min(c, kRefineMax);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float* q = queries + (int64_t)qi * d;
+  for (int i = warp; i < n; i += blockDim.x >> 5) {
+    const uint32_t pos = stage_pos[(int64_t)qi * stage_k + i];
+    const float s = warp_reference_score(metric, rows + (int64_t)pos * d, q, d);
+    if (lane == 0) {
+      if (!finite_f(s)) atomicOr(&q_flags[qi], 4);
+      cand[i] = pack_rank(rank_from_score(metric, s), keyrank[pos]);
+    }
+  }
+  __syncthreads();
+  // (rank, key rank) ascending is the reference order.
+  block_sort_u64<kRefineMax>(cand, n);
+  if (threadIdx.x < 32) {
+    int count = 0;
+    for (int base = 0; base < n && count < k; base += 32) {
+      const int i = base + lane;
+      bool in = i < n;
+      float s = 0.f;
+      if (in) {
+        s = score_from_rank(metric, rank_of(cand[i]));
+        in = within_radius(metric, s, radius);
+      }
+      const unsigned m = __ballot_sync(kFullMask, in);
+      const int run = (m == kFullMask) ? 32 : __ffs(~m) - 1;
+      if (lane < run && count + lane < k) {
+        const uint32_t pos = pos_of_keyrank[pos_of(cand[i])];
+        out_keys[(int64_t)qi * k + count + lane] = keys[pos];
+        out_scores[(int64_t)qi * k + count + lane] = s;
+      }
+      count = min(k, count + run);
+      if (run < 32) break;
+    }
+    if (lane == 0) out_counts[qi] = count;
+  }
+}
+
+}  // namespace xvec

@@ -1,0 +1,478 @@
+// sq8.cu — INT8 scalar-quantized Flat search (+ exact float32 refinement).
+//
+// Reference: ScalarQuantizedFlatIndex (internal/core/quantized_index.go:28-120,
+// 182-335) with QuantizationInt8 (quantization.go:79-105, 267-321),
+// QuantizedDistance (quantization.go:171-235) and, when a refine scale is
+// given, the collection's refinement (collection.go:1606-1631,
+// refiner.go:66-129).
+//
+// Per row the index keeps the float32 original, the int8 codes and the
+// quantization parameters (inverse scale, offset, code sum and code sum of
+// squares).  A search quantizes each query with the same rule, scans the
+// int8 codes with the shared FFMA tile kernel (the int8 dot products are
+// exact in float32 for d <= 1040), ranks in float32 within a bound eps of the
+// reference's float64 formula, rescores the candidates exactly (integer dot,
+// float64 formula in the reference's operation order with explicit
+// round-to-nearest intrinsics) and selects the k (or refine-count) best.
+#include <algorithm>
+#include <cmath>
+
+#include "capi_internal.h"
+#include "common.cuh"
+#include "flat_kernels.cuh"
+#include "index_kernels.cuh"
+#include "pipeline.cuh"
+#include "refine.cuh"
+
+namespace xvec {
+
+struct SQParams {
+  float inv_scale;
+  float offset;
+  double code_sum;
+  double code_square;
+};
+
+namespace {
+
+constexpr float kU = 5.9604645e-8f;  // 2^-24
+
+// quantizeInteger (quantization.go:267-321) for INT8, one warp per vector.
+// Returns false on ErrQuantizationOverflow.  Writes codes and params.
+__device__ bool warp_quantize_int8(const float* v, int d, int8_t* codes, SQParams* p) {
+  const int lane = threadIdx.x & 31;
+  float mn = v[0], mx = v[0];
+  for (int i = lane; i < d; i += 32) {
+    mn = go_min_zero(mn, v[i]);
+    mx = go_max_zero(mx, v[i]);
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    mn = go_min_zero(mn, __shfl_xor_sync(kFullMask, mn, o));
+    mx = go_max_zero(mx, __shfl_xor_sync(kFullMask, mx, o));
+  }
+  if (mn == mx) {
+    for (int i = lane; i < d; i += 32) codes[i] = 0;
+    if (lane == 0) *p = SQParams{0.f, mn, 0.0, 0.0};
+    return true;
+  }
+  const float eps32 = 1.1920928955078125e-7f;
+  const float span = __fsub_rn(mx, mn);
+  const float scale = __fdiv_rn(254.f, go_maxf(span, eps32));
+  const float bias = __fadd_rn(__fmul_rn(-mn, scale), -127.f);
+  const float inv = __fdiv_rn(1.f, scale);
+  const float off = __fdiv_rn(-bias, scale);
+  if (!finite_f(inv) || !finite_f(off)) return false;
+  long long sum = 0, sq = 0;
+  for (int i = lane; i < d; i += 32) {
+    const float t = __fadd_rn(__fmul_rn(v[i], scale), bias);
+    int c = (int)round((double)t);
+    c = min(127, max(-127, c));
+    codes[i] = (int8_t)c;
+    sum += c;
+    sq += c * c;
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    sum += __shfl_xor_sync(kFullMask, sum, o);
+    sq += __shfl_xor_sync(kFullMask, sq, o);
+  }
+  if (lane == 0) *p = SQParams{inv, off, (double)sum, (double)sq};
+  return true;
+}
+
+// The squared norm of the decoded vector, float64 in the reference order
+// (leftNorm / rightNorm of quantization.go:205-208).
+__device__ __forceinline__ double sq_norm64(const SQParams& p, int d) {
+  const double s = (double)p.inv_scale, o = (double)p.offset;
+  return __dadd_rn(__dadd_rn(__dmul_rn(__dmul_rn(s, s), p.code_square),
+                             __dmul_rn(__dmul_rn(__dmul_rn(2.0, s), o), p.code_sum)),
+                   __dmul_rn(__dmul_rn((double)d, o), o));
+}
+
+// QuantizedDistance (quantization.go:196-235) from the exact integer code dot;
+// left = stored row, right = query.
+__device__ float sq_reference_score(int metric, double dot, const SQParams& l, const SQParams& r,
+                                    int d) {
+  const double ls = (double)l.inv_scale, rs = (double)r.inv_scale;
+  const double lo = (double)l.offset, ro = (double)r.offset;
+  const double dim = (double)d;
+  const double inner =
+      __dadd_rn(__dadd_rn(__dadd_rn(__dmul_rn(__dmul_rn(ls, rs), dot),
+                                    __dmul_rn(__dmul_rn(lo, rs), r.code_sum)),
+                          __dmul_rn(__dmul_rn(ro, ls), l.code_sum)),
+                __dmul_rn(__dmul_rn(dim, lo), ro));
+  const double ln = sq_norm64(l, d), rn = sq_norm64(r, d);
+  double s;
+  if (metric == kMetricL2) {
+    s = __dsub_rn(__dadd_rn(ln, rn), __dmul_rn(2.0, inner));
+    if (s < 0 && s > __dmul_rn(-1e-6, go_maxd(1.0, __dadd_rn(ln, rn)))) s = 0;
+  } else if (metric == kMetricIP) {
+    s = inner;
+  } else if (metric == kMetricCosine) {
+    if (ln == 0 && rn == 0) {
+      s = 0;
+    } else if (ln == 0 || rn == 0) {
+      s = 1;
+    } else {
+      double c = __ddiv_rn(inner, __dsqrt_rn(__dmul_rn(ln, rn)));
+      c = go_mind(1.0, go_maxd(-1.0, c));
+      s = __dsub_rn(1.0, c);
+    }
+  } else {
+    const double den = go_maxd(ln, rn);
+    s = den == 0 ? 0.0 : __dsub_rn(2.0, __ddiv_rn(__dmul_rn(2.0, inner), den));
+  }
+  // finiteQuantizedScore (quantization.go:387-393)
+  const float f = __double2float_rn(s);
+  if (isnan(s) || isinf(s) || !finite_f(f)) return __int_as_float(0x7fc00000);
+  return f;
+}
+
+// Rows: quantize, fast-rank terms and the index-wide error-bound maxima.
+__global__ void sq8_encode_rows_kernel(const float* __restrict__ rows, int64_t n, int d,
+                                       int8_t* __restrict__ codes, SQParams* __restrict__ params,
+                                       float4* __restrict__ fast, unsigned* __restrict__ bounds,
+                                       int* __restrict__ err) {
+  const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= n) return;
+  SQParams p;
+  __shared__ SQParams sp[8];
+  const int wl = threadIdx.x >> 5;
+  if (!warp_quantize_int8(rows + w * d, d, codes + w * d, &sp[wl])) {
+    if (lane == 0) atomicExch(err, XVEC_GPU_OVERFLOW);
+    return;
+  }
+  __syncwarp();
+  p = sp[wl];
+  if (lane == 0) {
+    params[w] = p;
+    const float ln = __double2float_rn(sq_norm64(p, d));
+    fast[w] = make_float4(p.inv_scale, p.offset, (float)p.code_sum, ln);
+    const float U = fabsf(p.inv_scale) * sqrtf((float)p.code_square);
+    const float V = fabsf(p.inv_scale * (float)p.code_sum);
+    const float W = fabsf(p.offset);
+    atomicMax(&bounds[0], float_to_ordered(U));
+    atomicMax(&bounds[1], float_to_ordered(V));
+    atomicMax(&bounds[2], float_to_ordered(W));
+    atomicMax(&bounds[3], float_to_ordered(ln));
+  }
+}
+
+// Queries: validation (metric.Compute(q, q), quantized_index.go:264-272),
+// quantization, the float codes for the scan, the fast-rank constants and
+// eps (bound on |fast rank - reference rank|, see sq8.cu header).
+__global__ void sq8_prep_queries_kernel(const float* __restrict__ q, int nq, int d, int metric,
+                                        const unsigned* __restrict__ bounds,
+                                        int8_t* __restrict__ qcodes, SQParams* __restrict__ qparams,
+                                        float* __restrict__ qf, float4* __restrict__ qinfo,
+                                        float* __restrict__ q_eps, int* __restrict__ q_status) {
+  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= nq) return;
+  const float* v = q + (int64_t)w * d;
+  bool finite = true;
+  for (int i = lane; i < d; i += 32) finite &= finite_f(v[i]);
+  finite = __all_sync(kFullMask, finite);
+  float s0, s1, s2;
+  warp_reference_sums<1>(v, v, d, &s0, &s1, &s2);
+  int st = 0;
+  if (!finite || (metric != kMetricL2 && !finite_f(s0))) st = XVEC_GPU_NON_FINITE;
+  __shared__ SQParams sp[8];
+  const int wl = threadIdx.x >> 5;
+  if (st == 0 && !warp_quantize_int8(v, d, qcodes + (int64_t)w * d, &sp[wl]))
+    st = XVEC_GPU_OVERFLOW;
+  __syncwarp();
+  if (st != 0) {
+    if (lane == 0) q_status[w] = st;
+    for (int i = lane; i < d; i += 32) qf[(int64_t)w * d + i] = 0.f;
+    return;
+  }
+  for (int i = lane; i < d; i += 32) qf[(int64_t)w * d + i] = (float)qcodes[(int64_t)w * d + i];
+  if (lane == 0) {
+    const SQParams p = sp[wl];
+    qparams[w] = p;
+    const double rs = p.inv_scale, ro = p.offset;
+    const float A = p.inv_scale, B = p.offset;
+    const float C = __double2float_rn(rs * p.code_sum + (double)d * ro);
+    const double rn64 = sq_norm64(p, d);
+    const float rn = __double2float_rn(rn64);
+    qinfo[w] = make_float4(A, B, C, rn);
+    const float maxU = ordered_to_float(bounds[0]), maxV = ordered_to_float(bounds[1]);
+    const float maxW = ordered_to_float(bounds[2]), maxLn = ordered_to_float(bounds[3]);
+    const float a = fabsf(A) * sqrtf((float)p.code_square);
+    const float b = fabsf(A * (float)p.code_sum);
+    const float c = fabsf(B);
+    const float e = (float)d * fabsf(B);
+    float ei = 8.f * kU * (a * maxU + c * maxV + (b + e) * maxW) + kU * sqrtf(maxLn * rn);
+    float eps;
+    if (metric == kMetricL2)
+      eps = 2.f * ei + 5.f * kU * (maxLn + rn);
+    else
+      eps = ei;
+    q_eps[w] = 1.25f * eps + 1e-30f;
+    q_status[w] = 0;
+  }
+}
+
+struct SQ8Ranker {
+  int metric;
+  const float4* row_fast;
+  const float4* q_info;
+  using RowInfo = float4;
+  using QueryInfo = float4;
+  __device__ QueryInfo query(int qi) const { return q_info[qi]; }
+  __device__ RowInfo row(int64_t r) const { return row_fast[r]; }
+  // inner ~ ls * (rs*dot + ro*sum_l) + lo * (rs*sum_r + d*ro)
+  __device__ float rank(float dot, const RowInfo& r, const QueryInfo& q) const {
+    const float t = fmaf(q.x, dot, q.y * r.z);
+    const float inner = fmaf(r.x, t, r.y * q.z);
+    if (metric == kMetricIP) return -inner;
+    return (r.w + q.w) - 2.f * inner;  // L2
+  }
+};
+
+struct SQ8Scorer {
+  int metric;
+  const int8_t* codes;
+  const SQParams* params;
+  const int8_t* qcodes;
+  const SQParams* qparams;
+  const float* q_eps;
+  int d;
+  __device__ float score(int qi, int64_t row) const {
+    const int lane = threadIdx.x & 31;
+    const int8_t* a = codes + row * d;
+    const int8_t* b = qcodes + (int64_t)qi * d;
+    int dot = 0;
+    for (int i = lane; i < d; i += 32) dot += (int)a[i] * (int)b[i];
+    for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(kFullMask, dot, o);
+    return sq_reference_score(metric, (double)dot, params[row], qparams[qi], d);
+  }
+  __device__ float eps(int qi) const { return q_eps[qi]; }
+  __device__ int error_flag(float) const { return 4; }
+};
+
+__global__ void sq8_status_kernel(const int* q_status, const int* q_flags, int nq,
+                                  int* out_counts) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= nq) return;
+  int st = q_status[i];
+  if (st == 0 && (q_flags[i] & 4)) st = XVEC_GPU_NON_FINITE;
+  if (st != 0) out_counts[i] = -st;
+}
+
+__global__ void sq8_clear_flags(const int* ids, int n, int* q_flags) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) q_flags[ids[i]] &= ~3;
+}
+
+inline unsigned blocks_of(int64_t n, int t = 256) { return (unsigned)((n + t - 1) / t); }
+
+int sq8_kp(int k) {
+  int want = k + std::max(8, k / 4);
+  int kp = 32;
+  while (kp < want) kp <<= 1;
+  return kp;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// Insertion hooks.
+// ---------------------------------------------------------------------------
+xvec_gpu_status sq8_reserve(xvec_gpu_index* idx, int64_t cap, cudaStream_t s) {
+  const int d = idx->desc.dimension;
+  const int64_t n = idx->n;
+  xvec_gpu_status st;
+  if ((st = idx->sq_codes.reserve((size_t)cap * d, (size_t)n * d, s)) ||
+      (st = idx->sq_params.reserve((size_t)cap * sizeof(SQParams), (size_t)n * sizeof(SQParams), s)) ||
+      (st = idx->sq_fast.reserve((size_t)cap * 16, (size_t)n * 16, s)))
+    return st;
+  if (!idx->sq_bounds.ptr) {
+    if ((st = idx->sq_bounds.reserve(16, 0, s))) return st;
+    XVEC_CUDA(cudaMemsetAsync(idx->sq_bounds.ptr, 0, 16, s));
+  }
+  return XVEC_GPU_OK;
+}
+
+xvec_gpu_status sq8_commit(xvec_gpu_index* idx, int64_t old_n, int64_t m, cudaStream_t s) {
+  const int d = idx->desc.dimension;
+  // metric.Compute(vector, vector) must be finite (quantized_index.go:233-235).
+  if (idx->desc.metric != XVEC_METRIC_L2) {
+    std::vector<float> n2(m);
+    XVEC_CUDA(cudaMemcpyAsync(n2.data(), idx->row_n2.as<float>() + old_n, (size_t)m * 4,
+                              cudaMemcpyDeviceToHost, s));
+    XVEC_CUDA(cudaStreamSynchronize(s));
+    for (int64_t i = 0; i < m; ++i)
+      if (!std::isfinite(n2[i]))
+        return set_error("core: validate scalar-quantized vector %lld: non-finite",
+                         (long long)(old_n + i)),
+               XVEC_GPU_NON_FINITE;
+  }
+  Scratch err, bounds;
+  xvec_gpu_status st;
+  if ((st = err.alloc(4, s)) || (st = bounds.alloc(16, s))) return st;
+  XVEC_CUDA(cudaMemsetAsync(err.ptr, 0, 4, s));
+  XVEC_CUDA(cudaMemcpyAsync(bounds.ptr, idx->sq_bounds.ptr, 16, cudaMemcpyDeviceToDevice, s));
+  sq8_encode_rows_kernel<<<blocks_of(m * 32), 256, 0, s>>>(
+      idx->rows.as<float>() + old_n * d, m, d, idx->sq_codes.as<int8_t>() + old_n * d,
+      idx->sq_params.as<SQParams>() + old_n, idx->sq_fast.as<float4>() + old_n,
+      bounds.as<unsigned>(), err.as<int>());
+  XVEC_LAUNCHED();
+  XVEC_CUDA(cudaGetLastError());
+  int h_err = 0;
+  XVEC_CUDA(cudaMemcpyAsync(&h_err, err.ptr, 4, cudaMemcpyDeviceToHost, s));
+  XVEC_CUDA(cudaStreamSynchronize(s));
+  if (h_err) return set_error("core: value overflows quantized representation"), XVEC_GPU_OVERFLOW;
+  XVEC_CUDA(cudaMemcpyAsync(idx->sq_bounds.ptr, bounds.ptr, 16, cudaMemcpyDeviceToDevice, s));
+  return XVEC_GPU_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Search.
+// ---------------------------------------------------------------------------
+xvec_gpu_status sq8_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
+                                const xvec_gpu_search_opts& o, const uint32_t* d_bitmap,
+                                uint64_t* d_keys, float* d_scores, int* d_counts, cudaStream_t s,
+                                std::vector<int>* statuses) {
+  const int d = idx->desc.dimension, metric = idx->desc.metric;
+  const int64_t n = idx->n;
+  const bool refine = o.refine_scale > 0;
+  int stage_k = o.top_k;
+  if (refine) {
+    if (!(o.refine_scale > 0) || std::isinf(o.refine_scale))
+      return set_error("core: refiner scale factor must be finite and positive"),
+             XVEC_GPU_INVALID_ARGUMENT;
+    const double product = (double)o.top_k * (double)o.refine_scale;
+    if (product >= 1024.0 + 1.0)
+      return set_error("refinement candidate count %.0f exceeds 1024", std::floor(product)),
+             XVEC_GPU_INVALID_ARGUMENT;
+    stage_k = std::max(1, (int)std::floor(product));  // RefinementCandidateCount (refiner.go:112-129)
+  }
+  const float stage_radius = refine ? 0.f : o.radius;  // collection.go:1623
+  const int kp = sq8_kp(stage_k);
+  xvec_gpu_status st;
+  Scratch qcodes, qparams, qf, qinfo, qeps, qstatus, qflags;
+  if ((st = qcodes.alloc((size_t)nq * d, s)) ||
+      (st = qparams.alloc((size_t)nq * sizeof(SQParams), s)) ||
+      (st = qf.alloc((size_t)nq * d * 4, s)) || (st = qinfo.alloc((size_t)nq * 16, s)) ||
+      (st = qeps.alloc((size_t)nq * 4, s)) || (st = qstatus.alloc((size_t)nq * 4, s)) ||
+      (st = qflags.alloc((size_t)nq * 4, s)))
+    return st;
+  XVEC_CUDA(cudaMemsetAsync(qflags.ptr, 0, (size_t)nq * 4, s));
+  XVEC_CUDA(cudaMemsetAsync(qstatus.ptr, 0, (size_t)nq * 4, s));
+  sq8_prep_queries_kernel<<<blocks_of((int64_t)nq * 32), 256, 0, s>>>(
+      d_q, nq, d, metric, idx->sq_bounds.as<unsigned>(), qcodes.as<int8_t>(),
+      qparams.as<SQParams>(), qf.as<float>(), qinfo.as<float4>(), qeps.as<float>(),
+      qstatus.as<int>());
+  XVEC_LAUNCHED();
+  XVEC_CUDA(cudaGetLastError());
+  // Stage outputs: the final outputs, or scratch when a refine stage follows.
+  Scratch skeys, sscores, scounts, spos;
+  uint64_t* o_keys = d_keys;
+  float* o_scores = d_scores;
+  int* o_counts = d_counts;
+  if ((st = spos.alloc((size_t)nq * stage_k * 4, s))) return st;
+  if (refine) {
+    if ((st = skeys.alloc((size_t)nq * stage_k * 8, s)) ||
+        (st = sscores.alloc((size_t)nq * stage_k * 4, s)) ||
+        (st = scounts.alloc((size_t)nq * 4, s)))
+      return st;
+    o_keys = skeys.as<uint64_t>();
+    o_scores = sscores.as<float>();
+    o_counts = scounts.as<int>();
+  }
+  XVEC_CUDA(cudaMemsetAsync(o_counts, 0, (size_t)nq * 4, s));
+  SQ8Scorer sc{metric, idx->sq_codes.as<int8_t>(), idx->sq_params.as<SQParams>(),
+               qcodes.as<int8_t>(), qparams.as<SQParams>(), qeps.as<float>(), d};
+  const bool fast = n > 0 && (metric == XVEC_METRIC_IP || metric == XVEC_METRIC_L2) &&
+                    simt_cap_for(kp) <= 512;
+  if (fast) {
+    const int qtiles = (nq + 31) / 32;
+    int parts = (int)std::max<int64_t>(
+        1, std::min<int64_t>((592 + qtiles - 1) / qtiles, (n + 1023) / 1024));
+    parts = std::min(parts, std::max(1, flat_merge_capacity() / kp));
+    Scratch pkeys, pcounts, psat;
+    if ((st = pkeys.alloc((size_t)nq * parts * kp * 8, s)) ||
+        (st = pcounts.alloc((size_t)nq * parts * 4, s)) ||
+        (st = psat.alloc((size_t)nq * parts * 8, s)))
+      return st;
+    const SQ8Ranker rk{metric, idx->sq_fast.as<float4>(), qinfo.as<float4>()};
+    XVEC_CUDA(launch_scan_simt(idx->sq_codes.as<int8_t>(), n, d, idx->keyrank.as<uint32_t>(),
+                               qf.as<float>(), nq, d_bitmap, rk, parts, kp, pkeys.as<uint64_t>(),
+                               pcounts.as<int>(), psat.as<uint64_t>(), qflags.as<int>(), s));
+    XVEC_CUDA(launch_merge_rescore(sc, idx->pos_of_kr.as<uint32_t>(), idx->keys.as<uint64_t>(),
+                                   nullptr, nq, stage_k, stage_radius, 0, pkeys.as<uint64_t>(),
+                                   pcounts.as<int>(), psat.as<uint64_t>(), parts, kp, o_keys,
+                                   o_scores, o_counts, spos.as<uint32_t>(), qflags.as<int>(), s));
+    count_launches(2);
+  }
+  std::vector<int> h_status(nq), h_flags(nq);
+  XVEC_CUDA(cudaMemcpyAsync(h_status.data(), qstatus.ptr, (size_t)nq * 4, cudaMemcpyDeviceToHost,
+                            s));
+  XVEC_CUDA(cudaMemcpyAsync(h_flags.data(), qflags.ptr, (size_t)nq * 4, cudaMemcpyDeviceToHost, s));
+  XVEC_CUDA(cudaStreamSynchronize(s));
+  std::vector<int> exact_list;
+  if (n > 0)
+    for (int q = 0; q < nq; ++q)
+      if (h_status[q] == 0 && (!fast || (h_flags[q] & 3))) exact_list.push_back(q);
+  if (!exact_list.empty()) {
+    const int nl = (int)exact_list.size();
+    int parts = (int)std::max<int64_t>(1, std::min<int64_t>((592 + nl - 1) / nl, (n + 1023) / 1024));
+    parts = std::min(parts, std::max(1, flat_merge_capacity() / kp));
+    Scratch ids, pkeys, pcounts, psat;
+    if ((st = ids.alloc((size_t)nl * 4, s)) || (st = pkeys.alloc((size_t)nl * parts * kp * 8, s)) ||
+        (st = pcounts.alloc((size_t)nl * parts * 4, s)) ||
+        (st = psat.alloc((size_t)nl * parts * 8, s)))
+      return st;
+    XVEC_CUDA(cudaMemcpyAsync(ids.ptr, exact_list.data(), (size_t)nl * 4, cudaMemcpyHostToDevice, s));
+    sq8_clear_flags<<<blocks_of(nl), 256, 0, s>>>(ids.as<int>(), nl, qflags.as<int>());
+    XVEC_CUDA(launch_scan_exact(sc, n, idx->keyrank.as<uint32_t>(), ids.as<int>(), nl, d_bitmap,
+                                parts, kp, pkeys.as<uint64_t>(), pcounts.as<int>(),
+                                psat.as<uint64_t>(), qflags.as<int>(), s));
+    XVEC_CUDA(launch_merge_rescore(sc, idx->pos_of_kr.as<uint32_t>(), idx->keys.as<uint64_t>(),
+                                   ids.as<int>(), nl, stage_k, stage_radius, 1,
+                                   pkeys.as<uint64_t>(), pcounts.as<int>(), psat.as<uint64_t>(),
+                                   parts, kp, o_keys, o_scores, o_counts, spos.as<uint32_t>(),
+                                   qflags.as<int>(), s));
+    count_launches(3);
+    XVEC_CUDA(cudaMemcpyAsync(h_flags.data(), qflags.ptr, (size_t)nq * 4, cudaMemcpyDeviceToHost, s));
+    XVEC_CUDA(cudaStreamSynchronize(s));
+    for (int q : exact_list)
+      if (h_flags[q] & 2) return set_error("exact scan could not complete query %d", q), XVEC_GPU_CUDA_ERROR;
+  }
+  if (refine && n > 0) {
+    // The approximate stage's failures are final; the refine stage sees
+    // counts >= 0 only for healthy queries.
+    sq8_status_kernel<<<blocks_of(nq), 256, 0, s>>>(qstatus.as<int>(), qflags.as<int>(), nq,
+                                                    o_counts);
+    XVEC_CUDA(cudaMemsetAsync(d_counts, 0, (size_t)nq * 4, s));
+    refine_kernel<<<nq, 256, 0, s>>>(idx->rows.as<float>(), d, metric, d_q, spos.as<uint32_t>(),
+                                     o_counts, stage_k, idx->keyrank.as<uint32_t>(),
+                                     idx->pos_of_kr.as<uint32_t>(), idx->keys.as<uint64_t>(),
+                                     o.top_k, o.radius, d_keys, d_scores, d_counts,
+                                     qflags.as<int>());
+    count_launches(2);
+    XVEC_CUDA(cudaGetLastError());
+  } else if (refine) {
+    XVEC_CUDA(cudaMemsetAsync(d_counts, 0, (size_t)nq * 4, s));
+  }
+  sq8_status_kernel<<<blocks_of(nq), 256, 0, s>>>(qstatus.as<int>(), qflags.as<int>(), nq,
+                                                  d_counts);
+  XVEC_LAUNCHED();
+  XVEC_CUDA(cudaGetLastError());
+  XVEC_CUDA(cudaMemcpyAsync(h_flags.data(), qflags.ptr, (size_t)nq * 4, cudaMemcpyDeviceToHost, s));
+  XVEC_CUDA(cudaStreamSynchronize(s));
+  count_search(nq, (int64_t)exact_list.size(), 0, 0);
+  if (statuses) {
+    statuses->resize(nq);
+    for (int q = 0; q < nq; ++q) {
+      int sq = h_status[q];
+      if (sq == 0 && (h_flags[q] & 4)) sq = XVEC_GPU_NON_FINITE;
+      (*statuses)[q] = sq;
+    }
+  }
+  return XVEC_GPU_OK;
+}
+
+}  // namespace xvec
