@@ -94,6 +94,7 @@ struct xvec_gpu_index {
 
   // IVF-PQ.
   int32_t nlist = 0, chunks = 0;
+  xvec_gpu_index* probe_index = nullptr;  // Flat index over the IVF centroids
   bool has_model = false;
   xvec::DeviceBuffer centroids;     // float [nlist][d]
   xvec::DeviceBuffer centroid_n2;   // float [nlist]
@@ -112,4 +113,8 @@ struct xvec_gpu_index {
   xvec::DeviceBuffer rq_signs;              // uint8 [4*padded/8]
   xvec::DeviceBuffer rq_codes;              // uint8 [n][padded/8]
   xvec::DeviceBuffer rq_factors;            // double [n][3] + int cluster -> struct
+
+  ~xvec_gpu_index() {
+    if (probe_index) xvec_gpu_index_destroy(probe_index);
+  }
 };

@@ -210,6 +210,72 @@ __device__ __forceinline__ void warp_reference_sums(const RowT* x, const float* 
   *s2 = r2;
 }
 
+// The same reference order evaluated by a single thread (short vectors: PQ
+// chunk scores).  MODE 0: sum (x-q)^2, MODE 1: sum x*q.
+template <int MODE>
+__device__ __forceinline__ float thread_reference_sum(const float* x, const float* q, int d) {
+  float r = 0.f;
+  if (d >= 16) {
+    float lanes[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) lanes[j] = 0.f;
+    const int blocks = d >> 4;
+    for (int v = 0; v < blocks; ++v) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const float xv = x[v * 16 + j], qv = q[v * 16 + j];
+        if (MODE == 0) {
+          const float df = __fsub_rn(xv, qv);
+          lanes[j] = __fmaf_rn(df, df, lanes[j]);
+        } else {
+          lanes[j] = __fmaf_rn(xv, qv, lanes[j]);
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) r = __fadd_rn(r, lanes[j]);
+    for (int i = blocks * 16; i < d; ++i) {
+      if (MODE == 0) {
+        const float df = __fsub_rn(x[i], q[i]);
+        r = __fmaf_rn(df, df, r);
+      } else {
+        r = __fmaf_rn(x[i], q[i], r);
+      }
+    }
+  } else if (d >= 8) {
+    float lanes[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (MODE == 0) {
+        const float df = __fsub_rn(x[j], q[j]);
+        lanes[j] = __fadd_rn(0.f, __fmul_rn(df, df));
+      } else {
+        lanes[j] = __fadd_rn(0.f, __fmul_rn(x[j], q[j]));
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) r = __fadd_rn(r, lanes[j]);
+    for (int i = 8; i < d; ++i) {
+      if (MODE == 0) {
+        const float df = __fsub_rn(x[i], q[i]);
+        r = __fadd_rn(r, __fmul_rn(df, df));
+      } else {
+        r = __fadd_rn(r, __fmul_rn(x[i], q[i]));
+      }
+    }
+  } else {
+    for (int i = 0; i < d; ++i) {
+      if (MODE == 0) {
+        const float df = __fsub_rn(x[i], q[i]);
+        r = __fadd_rn(r, __fmul_rn(df, df));
+      } else {
+        r = __fadd_rn(r, __fmul_rn(x[i], q[i]));
+      }
+    }
+  }
+  return r;
+}
+
 // cosineDistance (distance.go:65-81) from DotNorms output.
 __device__ __forceinline__ float reference_cosine(float inner, float ln, float rn) {
   if (ln == 0.f && rn == 0.f) return 0.f;

@@ -1,0 +1,564 @@
+// ivfpq.cu — IVF list scan over 8-bit PQ codes, and k-means assignment.
+//
+// The reference has no IVF-PQ type; the path is composed from its parts
+// (the same composition the oracle restates in xo_ivfpq_search):
+//   probe   probedListsLocked (internal/core/ivf.go:524-561): the nprobe best
+//           centroids under the index metric, ties to the lower index.  Done
+//           by an internal Flat index over the centroids keyed by centroid
+//           index, so the probe is the Flat path (exact, reference order).
+//   table   PQModel.DistanceTable (internal/core/pq.go:549-571): per query,
+//           chunk-major [chunks][256] of metric.Compute(query chunk, pivot
+//           chunk) in the reference's float32 order (thread_reference_sum).
+//   scan    PQDistanceTable.Lookup (pq.go:574-595) of every code of every
+//           probed list: a float64 sum in chunk order, rounded to float32
+//           with the overflow check; filter before scoring, ties by key.
+//   insert  KMeansModel.Nearest (kmeans.go:169-175) for the list and
+//           PQModel.Encode (pq.go:274-301) for the code: per chunk the best
+//           of the 256 pivots, ties to the lower id.
+// The scan's scores are the reference scores, so its per-list selections are
+// merged in exact mode.
+#include <cub/device/device_radix_sort.cuh>
+#include <cub/device/device_scan.cuh>
+
+#include <algorithm>
+#include <cmath>
+#include <vector>
+
+#include "capi_internal.h"
+#include "common.cuh"
+#include "flat_kernels.cuh"
+#include "index_kernels.cuh"
+#include "pipeline.cuh"
+
+namespace xvec {
+
+xvec_gpu_status search_device_locked(xvec_gpu_index* idx, const void* d_q, int nq,
+                                     const xvec_gpu_search_opts& o, const uint32_t* d_bitmap,
+                                     uint64_t* d_keys, float* d_scores, int* d_counts,
+                                     cudaStream_t s, std::vector<int>* statuses);
+xvec_gpu_status add_device_locked(xvec_gpu_index* idx, const uint64_t* d_keys, const void* d_rows,
+                                  int64_t m, cudaStream_t s);
+
+namespace {
+
+inline unsigned blocks_of(int64_t n, int t = 256) { return (unsigned)((n + t - 1) / t); }
+constexpr int kAssignBatch = 65536;
+
+__global__ void keys_to_labels_kernel(const uint64_t* keys, const int* counts, int64_t n,
+                                      int32_t* labels, int* err) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  if (counts[i] != 1) {
+    atomicExch(err, counts[i] < 0 ? -counts[i] : XVEC_GPU_INVALID_ARGUMENT);
+    labels[i] = 0;
+    return;
+  }
+  labels[i] = (int32_t)keys[i];
+}
+
+// PQModel.Encode: block per row, thread per pivot.
+__global__ void __launch_bounds__(256) pq_encode_kernel(const float* __restrict__ rows, int64_t n,
+                                                        int d, int metric,
+                                                        const float* __restrict__ pivots,
+                                                        const int* __restrict__ offsets,
+                                                        int chunks, uint8_t* __restrict__ codes,
+                                                        int* __restrict__ err) {
+  const int64_t r = blockIdx.x;
+  if (r >= n) return;
+  __shared__ float s_score[8];
+  __shared__ int s_id[8];
+  const int c = threadIdx.x, warp = c >> 5, lane = c & 31;
+  const float* x = rows + r * d;
+  for (int ch = 0; ch < chunks; ++ch) {
+    const int start = offsets[ch], w = offsets[ch + 1] - start;
+    float s = metric == kMetricL2 ? thread_reference_sum<0>(x + start, pivots + (int64_t)c * d + start, w)
+                                  : thread_reference_sum<1>(x + start, pivots + (int64_t)c * d + start, w);
+    if (!finite_f(s)) atomicExch(err, XVEC_GPU_NON_FINITE);
+    // Best (metric Better), ties to the lower pivot id.
+    int id = c;
+    for (int o = 16; o > 0; o >>= 1) {
+      const float os = __shfl_xor_sync(kFullMask, s, o);
+      const int oid = __shfl_xor_sync(kFullMask, id, o);
+      const bool take = metric == kMetricIP ? (os > s || (os == s && oid < id))
+                                            : (os < s || (os == s && oid < id));
+      if (take) {
+        s = os;
+        id = oid;
+      }
+    }
+    if (lane == 0) {
+      s_score[warp] = s;
+      s_id[warp] = id;
+    }
+    __syncthreads();
+    if (c == 0) {
+      float bs = s_score[0];
+      int bi = s_id[0];
+      for (int i = 1; i < 8; ++i) {
+        const bool take = metric == kMetricIP ? (s_score[i] > bs || (s_score[i] == bs && s_id[i] < bi))
+                                              : (s_score[i] < bs || (s_score[i] == bs && s_id[i] < bi));
+        if (take) {
+          bs = s_score[i];
+          bi = s_id[i];
+        }
+      }
+      codes[r * chunks + ch] = (uint8_t)bi;
+    }
+    __syncthreads();
+  }
+}
+
+// PQModel.DistanceTable: block per query, thread per pivot.
+__global__ void __launch_bounds__(256) pq_table_kernel(const float* __restrict__ queries, int nq,
+                                                       int d, int metric,
+                                                       const float* __restrict__ pivots,
+                                                       const int* __restrict__ offsets,
+                                                       int chunks, float* __restrict__ table,
+                                                       int* __restrict__ q_flags) {
+  const int q = blockIdx.x;
+  const int c = threadIdx.x;
+  const float* x = queries + (int64_t)q * d;
+  for (int ch = 0; ch < chunks; ++ch) {
+    const int start = offsets[ch], w = offsets[ch + 1] - start;
+    const float s = metric == kMetricL2
+                        ? thread_reference_sum<0>(x + start, pivots + (int64_t)c * d + start, w)
+                        : thread_reference_sum<1>(x + start, pivots + (int64_t)c * d + start, w);
+    if (!finite_f(s)) atomicOr(&q_flags[q], 4);
+    table[((int64_t)q * chunks + ch) * 256 + c] = s;
+  }
+}
+
+// PQDistanceTable.Lookup: float64 sum in chunk order, float32 result, or
+// false on overflow (ErrPQScoreOverflow).
+__device__ __forceinline__ bool pq_lookup(const float* table, const uint8_t* code, int chunks,
+                                          float* out) {
+  double s = 0.0;
+  for (int c = 0; c < chunks; ++c) s = __dadd_rn(s, (double)table[c * 256 + code[c]]);
+  if (isnan(s) || isinf(s) || s > 3.4028234663852886e38 || s < -3.4028234663852886e38) return false;
+  *out = __double2float_rn(s);
+  return true;
+}
+
+// One block per (query, probed list): the list's codes scored against the
+// query's table in shared memory; the KP best keys are kept per list.
+template <int CAP>
+__global__ void __launch_bounds__(256) ivfpq_scan_kernel(
+    const float* __restrict__ table, int chunks, const uint8_t* __restrict__ codes,
+    const uint64_t* __restrict__ probe_lists, const int* __restrict__ probe_counts, int nprobe,
+    const int64_t* __restrict__ list_offsets, const uint32_t* __restrict__ list_rows,
+    const uint32_t* __restrict__ keyrank, const uint32_t* __restrict__ bitmap, int metric, int kp,
+    uint64_t* __restrict__ part_keys, int* __restrict__ part_counts,
+    uint64_t* __restrict__ part_sat, int* __restrict__ q_flags) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  float* slut = reinterpret_cast<float*>(smem_raw);                     // [chunks][256]
+  uint64_t* buf = reinterpret_cast<uint64_t*>(slut + chunks * 256);     // [CAP]
+  __shared__ AccumState st;
+  const int q = blockIdx.x, j = blockIdx.y;
+  const int64_t slot = (int64_t)q * nprobe + j;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (j >= probe_counts[q]) {
+    if (threadIdx.x == 0) {
+      part_counts[slot] = 0;
+      part_sat[slot] = kEmptyKey;
+    }
+    return;
+  }
+  const uint64_t list = probe_lists[slot];
+  const int64_t begin = list_offsets[list], end = list_offsets[list + 1];
+  for (int i = threadIdx.x; i < chunks * 256; i += blockDim.x)
+    slut[i] = table[(int64_t)q * chunks * 256 + i];
+  if (threadIdx.x == 0) {
+    st.count = 0;
+    st.saturated = 0;
+    st.thr = kEmptyKey;
+  }
+  __syncthreads();
+  for (int64_t base = begin; base < end; base += blockDim.x) {
+    const int64_t i = base + threadIdx.x;
+    if (i < end) {
+      const uint32_t pos = list_rows[i];
+      if (bitmap_pass(bitmap, pos)) {
+        float s;
+        if (!pq_lookup(slut, codes + (int64_t)pos * chunks, chunks, &s)) {
+          atomicOr(&q_flags[q], 8);
+        } else {
+          const uint64_t key = pack_rank(rank_from_score(metric, s), keyrank[pos]);
+          if (key < st.thr) {
+            const int at = atomicAdd(&st.count, 1);
+            buf[at] = key;
+          }
+        }
+      }
+    }
+    __syncthreads();
+    if (warp == 0 && st.count > CAP - (int)blockDim.x) warp_compact<CAP>(buf, &st, kp);
+    __syncthreads();
+  }
+  if (warp == 0) {
+    warp_compact<CAP>(buf, &st, kp);
+    const int cnt = min(st.count, kp);
+    for (int i = lane; i < cnt; i += 32) part_keys[slot * kp + i] = buf[i];
+    if (lane == 0) {
+      part_counts[slot] = cnt;
+      part_sat[slot] = st.thr;
+    }
+  }
+}
+
+struct PQScorer {
+  int metric;
+  const float* table;
+  const uint8_t* codes;
+  int chunks;
+  __device__ float score(int qi, int64_t row) const {
+    float s;
+    if (!pq_lookup(table + (int64_t)qi * chunks * 256, codes + row * chunks, chunks, &s))
+      return __int_as_float(0x7fc00000);
+    return s;
+  }
+  __device__ float eps(int) const { return 0.f; }
+  __device__ int error_flag(float) const { return 8; }
+};
+
+__global__ void ivfpq_status_kernel(const int* q_status, const int* q_flags, int nq,
+                                    int* out_counts) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= nq) return;
+  int st = q_status[i];
+  if (st == 0 && (q_flags[i] & 4)) st = XVEC_GPU_NON_FINITE;
+  if (st == 0 && (q_flags[i] & 8)) st = XVEC_GPU_OVERFLOW;
+  if (st != 0) out_counts[i] = -st;
+}
+
+__global__ void count_lists_kernel(const int32_t* row_list, int64_t n, int64_t* counts) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) atomicAdd((unsigned long long*)&counts[row_list[i]], 1ull);
+}
+__global__ void iota32_kernel(uint32_t* out, int64_t n) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = (uint32_t)i;
+}
+
+// Nearest centroid of each row through a Flat index over the centroids
+// (keys = centroid index): top-1 under the metric, ties to the lower index.
+xvec_gpu_status assign_rows(xvec_gpu_index* probe, const float* d_rows, int64_t n, int d,
+                            int32_t* d_labels, float* d_scores, cudaStream_t s) {
+  xvec_gpu_search_opts o{};
+  o.top_k = 1;
+  xvec_gpu_status st;
+  Scratch keys, scores, counts, err;
+  const int64_t batch = std::min<int64_t>(n, kAssignBatch);
+  if ((st = keys.alloc((size_t)batch * 8, s)) || (st = scores.alloc((size_t)batch * 4, s)) ||
+      (st = counts.alloc((size_t)batch * 4, s)) || (st = err.alloc(4, s)))
+    return st;
+  XVEC_CUDA(cudaMemsetAsync(err.ptr, 0, 4, s));
+  for (int64_t b = 0; b < n; b += kAssignBatch) {
+    const int m = (int)std::min<int64_t>(kAssignBatch, n - b);
+    std::vector<int> statuses;
+    st = search_device_locked(probe, d_rows + b * d, m, o, nullptr, keys.as<uint64_t>(),
+                              d_scores ? d_scores + b : scores.as<float>(), counts.as<int>(), s,
+                              &statuses);
+    if (st) return st;
+    for (int i = 0; i < m; ++i)
+      if (statuses[i]) return set_error("assign row %lld: status %d", (long long)(b + i), statuses[i]),
+                              (xvec_gpu_status)statuses[i];
+    keys_to_labels_kernel<<<blocks_of(m), 256, 0, s>>>(keys.as<uint64_t>(), counts.as<int>(), m,
+                                                        d_labels + b, err.as<int>());
+    XVEC_LAUNCHED();
+  }
+  int h = 0;
+  XVEC_CUDA(cudaMemcpyAsync(&h, err.ptr, 4, cudaMemcpyDeviceToHost, s));
+  XVEC_CUDA(cudaStreamSynchronize(s));
+  if (h) return set_error("k-means assignment failed (status %d)", h), (xvec_gpu_status)h;
+  return XVEC_GPU_OK;
+}
+
+xvec_gpu_status make_probe_index(int device, int metric, int d, const float* d_centroids,
+                                 int nlist, cudaStream_t s, xvec_gpu_index** out) {
+  xvec_gpu_index_desc desc{};
+  desc.kind = XVEC_INDEX_FLAT;
+  desc.dimension = d;
+  desc.metric = metric;
+  desc.storage = XVEC_STORAGE_FP32;
+  desc.device = device;
+  xvec_gpu_index* p = nullptr;
+  xvec_gpu_status st = xvec_gpu_index_create(&desc, &p);
+  if (st) return st;
+  std::vector<uint64_t> ids(nlist);
+  for (int i = 0; i < nlist; ++i) ids[i] = (uint64_t)i;
+  Scratch dk;
+  if ((st = dk.alloc((size_t)nlist * 8, s))) {
+    xvec_gpu_index_destroy(p);
+    return st;
+  }
+  cudaMemcpyAsync(dk.ptr, ids.data(), (size_t)nlist * 8, cudaMemcpyHostToDevice, s);
+  st = add_device_locked(p, dk.as<uint64_t>(), d_centroids, nlist, s);
+  if (st) {
+    xvec_gpu_index_destroy(p);
+    return st;
+  }
+  *out = p;
+  return XVEC_GPU_OK;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// Index hooks.
+// ---------------------------------------------------------------------------
+xvec_gpu_status ivfpq_reserve(xvec_gpu_index* idx, int64_t cap, cudaStream_t s) {
+  xvec_gpu_status st;
+  const int64_t n = idx->n;
+  const int chunks = std::max(1, idx->chunks);
+  if ((st = idx->pq_codes.reserve((size_t)cap * chunks, (size_t)n * chunks, s)) ||
+      (st = idx->row_list.reserve((size_t)cap * 4, (size_t)n * 4, s)))
+    return st;
+  return XVEC_GPU_OK;
+}
+
+xvec_gpu_status ivfpq_commit(xvec_gpu_index* idx, int64_t old_n, int64_t m, cudaStream_t s) {
+  const int d = idx->desc.dimension;
+  xvec_gpu_status st =
+      assign_rows(idx->probe_index, idx->rows.as<float>() + old_n * d, m, d,
+                  idx->row_list.as<int32_t>() + old_n, nullptr, s);
+  if (st) return st;
+  Scratch err;
+  if ((st = err.alloc(4, s))) return st;
+  XVEC_CUDA(cudaMemsetAsync(err.ptr, 0, 4, s));
+  pq_encode_kernel<<<(unsigned)m, 256, 0, s>>>(idx->rows.as<float>() + old_n * d, m, d,
+                                                idx->desc.metric, idx->pivots.as<float>(),
+                                                idx->chunk_offsets.as<int>(), idx->chunks,
+                                                idx->pq_codes.as<uint8_t>() + old_n * idx->chunks,
+                                                err.as<int>());
+  XVEC_LAUNCHED();
+  XVEC_CUDA(cudaGetLastError());
+  int h = 0;
+  XVEC_CUDA(cudaMemcpyAsync(&h, err.ptr, 4, cudaMemcpyDeviceToHost, s));
+  XVEC_CUDA(cudaStreamSynchronize(s));
+  if (h) return set_error("PQ encoding produced a non-finite score"), (xvec_gpu_status)h;
+  idx->lists_dirty = true;
+  return XVEC_GPU_OK;
+}
+
+// CSR of positions per list; positions keep insertion order within a list
+// (ivf.go:193-201 appends in position order; the radix sort is stable).
+static xvec_gpu_status rebuild_lists(xvec_gpu_index* idx, cudaStream_t s) {
+  const int64_t n = idx->n;
+  const int nlist = idx->nlist;
+  xvec_gpu_status st;
+  if ((st = idx->list_offsets.reserve((size_t)(nlist + 1) * 8, 0, s)) ||
+      (st = idx->list_rows.reserve((size_t)std::max<int64_t>(n, 1) * 4, 0, s)))
+    return st;
+  Scratch counts, iota, sorted_lists, temp;
+  if ((st = counts.alloc((size_t)(nlist + 1) * 8, s)) || (st = iota.alloc((size_t)n * 4, s)) ||
+      (st = sorted_lists.alloc((size_t)n * 4, s)))
+    return st;
+  XVEC_CUDA(cudaMemsetAsync(counts.ptr, 0, (size_t)(nlist + 1) * 8, s));
+  count_lists_kernel<<<blocks_of(n), 256, 0, s>>>(idx->row_list.as<int32_t>(), n,
+                                                  counts.as<int64_t>());
+  iota32_kernel<<<blocks_of(n), 256, 0, s>>>(iota.as<uint32_t>(), n);
+  size_t tb = 0, tb2 = 0;
+  XVEC_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, tb, idx->row_list.as<uint32_t>(),
+                                            sorted_lists.as<uint32_t>(), iota.as<uint32_t>(),
+                                            idx->list_rows.as<uint32_t>(), n, 0, 32, s));
+  XVEC_CUDA(cub::DeviceScan::ExclusiveSum(nullptr, tb2, counts.as<int64_t>(),
+                                          idx->list_offsets.as<int64_t>(), nlist + 1, s));
+  if ((st = temp.alloc(std::max(tb, tb2), s))) return st;
+  XVEC_CUDA(cub::DeviceRadixSort::SortPairs(temp.ptr, tb, idx->row_list.as<uint32_t>(),
+                                            sorted_lists.as<uint32_t>(), iota.as<uint32_t>(),
+                                            idx->list_rows.as<uint32_t>(), n, 0, 32, s));
+  XVEC_CUDA(cub::DeviceScan::ExclusiveSum(temp.ptr, tb2, counts.as<int64_t>(),
+                                          idx->list_offsets.as<int64_t>(), nlist + 1, s));
+  XVEC_CUDA(cudaStreamSynchronize(s));
+  idx->lists_dirty = false;
+  return XVEC_GPU_OK;
+}
+
+xvec_gpu_status ivfpq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
+                                  const xvec_gpu_search_opts& o, const uint32_t* d_bitmap,
+                                  uint64_t* d_keys, float* d_scores, int* d_counts,
+                                  cudaStream_t s, std::vector<int>* statuses) {
+  if (!idx->has_model) return set_error("IVF-PQ index has no model"), XVEC_GPU_INVALID_ARGUMENT;
+  if (o.nprobe <= 0) return set_error("core: IVF NProbe must be positive"), XVEC_GPU_INVALID_ARGUMENT;
+  const int d = idx->desc.dimension, metric = idx->desc.metric, k = o.top_k;
+  const int64_t n = idx->n;
+  const int chunks = idx->chunks;
+  xvec_gpu_status st;
+  // The lists are rebuilt under the shared lock: only one searcher may do it.
+  {
+    static std::mutex rebuild_mu;
+    std::lock_guard<std::mutex> g(rebuild_mu);
+    if (idx->lists_dirty && n > 0 && (st = rebuild_lists(idx, s))) return st;
+  }
+  const int nprobe = std::min(o.nprobe, idx->nlist);
+  int kp = 32;
+  while (kp < k + std::max(8, k / 4)) kp <<= 1;
+  if ((int64_t)nprobe * kp > flat_merge_capacity())
+    return set_error("nprobe %d x top_k %d exceeds the merge capacity", nprobe, k),
+           XVEC_GPU_INVALID_ARGUMENT;
+  // Probe: the Flat path over the centroids (validates the queries too).
+  Scratch pkeys_probe, pscores_probe, pcounts_probe, table, qflags, qstatus;
+  if ((st = pkeys_probe.alloc((size_t)nq * nprobe * 8, s)) ||
+      (st = pscores_probe.alloc((size_t)nq * nprobe * 4, s)) ||
+      (st = pcounts_probe.alloc((size_t)nq * 4, s)) ||
+      (st = table.alloc((size_t)nq * chunks * 256 * 4, s)) ||
+      (st = qflags.alloc((size_t)nq * 4, s)) || (st = qstatus.alloc((size_t)nq * 4, s)))
+    return st;
+  xvec_gpu_search_opts po{};
+  po.top_k = nprobe;
+  std::vector<int> probe_status;
+  st = search_device_locked(idx->probe_index, d_q, nq, po, nullptr, pkeys_probe.as<uint64_t>(),
+                            pscores_probe.as<float>(), pcounts_probe.as<int>(), s, &probe_status);
+  if (st) return st;
+  XVEC_CUDA(cudaMemcpyAsync(qstatus.ptr, probe_status.data(), (size_t)nq * 4,
+                            cudaMemcpyHostToDevice, s));
+  XVEC_CUDA(cudaMemsetAsync(qflags.ptr, 0, (size_t)nq * 4, s));
+  XVEC_CUDA(cudaMemsetAsync(d_counts, 0, (size_t)nq * 4, s));
+  pq_table_kernel<<<nq, 256, 0, s>>>(d_q, nq, d, metric, idx->pivots.as<float>(),
+                                     idx->chunk_offsets.as<int>(), chunks, table.as<float>(),
+                                     qflags.as<int>());
+  XVEC_LAUNCHED();
+  if (n > 0) {
+    int cap = 512;
+    while (cap < kp + 2 * 256) cap <<= 1;
+    Scratch lkeys, lcounts, lsat;
+    const size_t lists = (size_t)nq * nprobe;
+    if ((st = lkeys.alloc(lists * kp * 8, s)) || (st = lcounts.alloc(lists * 4, s)) ||
+        (st = lsat.alloc(lists * 8, s)))
+      return st;
+    const size_t smem = (size_t)chunks * 256 * 4 + (size_t)cap * 8;
+    dim3 grid(nq, nprobe);
+#define XVEC_PQ_CASE(C)                                                                        \
+  if (cap == C) {                                                                              \
+    auto kern = ivfpq_scan_kernel<C>;                                                          \
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);        \
+    kern<<<grid, 256, smem, s>>>(table.as<float>(), chunks, idx->pq_codes.as<uint8_t>(),       \
+                                 pkeys_probe.as<uint64_t>(), pcounts_probe.as<int>(), nprobe,  \
+                                 idx->list_offsets.as<int64_t>(), idx->list_rows.as<uint32_t>(), \
+                                 idx->keyrank.as<uint32_t>(), d_bitmap, metric, kp,            \
+                                 lkeys.as<uint64_t>(), lcounts.as<int>(), lsat.as<uint64_t>(), \
+                                 qflags.as<int>());                                            \
+  }
+    XVEC_PQ_CASE(1024)
+    XVEC_PQ_CASE(2048)
+#undef XVEC_PQ_CASE
+    if (cap > 2048) return set_error("top_k %d too large for the IVF-PQ scan", k), XVEC_GPU_INVALID_ARGUMENT;
+    XVEC_LAUNCHED();
+    XVEC_CUDA(cudaGetLastError());
+    PQScorer sc{metric, table.as<float>(), idx->pq_codes.as<uint8_t>(), chunks};
+    XVEC_CUDA(launch_merge_rescore(sc, idx->pos_of_kr.as<uint32_t>(), idx->keys.as<uint64_t>(),
+                                   nullptr, nq, k, o.radius, 1, lkeys.as<uint64_t>(),
+                                   lcounts.as<int>(), lsat.as<uint64_t>(), nprobe, kp, d_keys,
+                                   d_scores, d_counts, nullptr, qflags.as<int>(), s));
+    XVEC_LAUNCHED();
+  }
+  ivfpq_status_kernel<<<blocks_of(nq), 256, 0, s>>>(qstatus.as<int>(), qflags.as<int>(), nq,
+                                                    d_counts);
+  XVEC_LAUNCHED();
+  XVEC_CUDA(cudaGetLastError());
+  std::vector<int> h_flags(nq);
+  XVEC_CUDA(cudaMemcpyAsync(h_flags.data(), qflags.ptr, (size_t)nq * 4, cudaMemcpyDeviceToHost, s));
+  XVEC_CUDA(cudaStreamSynchronize(s));
+  count_search(nq, 0, 0, 0);
+  if (statuses) {
+    statuses->resize(nq);
+    for (int q = 0; q < nq; ++q) {
+      int sq = probe_status[q];
+      if (sq == 0 && (h_flags[q] & 4)) sq = XVEC_GPU_NON_FINITE;
+      if (sq == 0 && (h_flags[q] & 8)) sq = XVEC_GPU_OVERFLOW;
+      (*statuses)[q] = sq;
+    }
+  }
+  return XVEC_GPU_OK;
+}
+
+}  // namespace xvec
+
+using namespace xvec;
+
+extern "C" xvec_gpu_status xvec_gpu_ivfpq_set_model(xvec_gpu_index* idx, const float* centroids,
+                                                    int32_t nlist, const float* pivots,
+                                                    int32_t chunks) {
+  if (!idx || !centroids || !pivots) return set_error("nil argument"), XVEC_GPU_INVALID_ARGUMENT;
+  if (idx->desc.kind != XVEC_INDEX_IVF_PQ)
+    return set_error("not an IVF-PQ index"), XVEC_GPU_INVALID_ARGUMENT;
+  const int d = idx->desc.dimension;
+  if (nlist <= 0 || chunks <= 0 || chunks > d)
+    return set_error("core: invalid PQ options: resolved Chunks must be in [1,%d]", d),
+           XVEC_GPU_INVALID_ARGUMENT;
+  std::unique_lock<std::shared_mutex> lock(idx->mu);
+  if (idx->n > 0) return set_error("set the model before adding rows"), XVEC_GPU_INVALID_ARGUMENT;
+  for (int64_t i = 0; i < (int64_t)nlist * d; ++i)
+    if (!std::isfinite(centroids[i])) return set_error("non-finite centroid"), XVEC_GPU_NON_FINITE;
+  for (int64_t i = 0; i < (int64_t)256 * d; ++i)
+    if (!std::isfinite(pivots[i])) return set_error("non-finite PQ pivot"), XVEC_GPU_NON_FINITE;
+  cudaSetDevice(idx->device);
+  cudaStream_t s = nullptr;
+  // pqChunkOffsets (pq.go:395-406): contiguous chunks, wider chunks first.
+  std::vector<int> offsets(chunks + 1, 0);
+  const int base = d / chunks, larger = d % chunks;
+  for (int c = 0; c < chunks; ++c) offsets[c + 1] = offsets[c] + base + (c < larger ? 1 : 0);
+  xvec_gpu_status st;
+  if ((st = idx->centroids.reserve((size_t)nlist * d * 4, 0, s)) ||
+      (st = idx->pivots.reserve((size_t)256 * d * 4, 0, s)) ||
+      (st = idx->chunk_offsets.reserve((size_t)(chunks + 1) * 4, 0, s)))
+    return st;
+  XVEC_CUDA(cudaMemcpy(idx->centroids.ptr, centroids, (size_t)nlist * d * 4, cudaMemcpyHostToDevice));
+  XVEC_CUDA(cudaMemcpy(idx->pivots.ptr, pivots, (size_t)256 * d * 4, cudaMemcpyHostToDevice));
+  XVEC_CUDA(cudaMemcpy(idx->chunk_offsets.ptr, offsets.data(), (size_t)(chunks + 1) * 4,
+                       cudaMemcpyHostToDevice));
+  if (idx->probe_index) {
+    xvec_gpu_index_destroy(idx->probe_index);
+    idx->probe_index = nullptr;
+  }
+  if ((st = make_probe_index(idx->device, idx->desc.metric, d, idx->centroids.as<float>(), nlist,
+                             s, &idx->probe_index)))
+    return st;
+  idx->nlist = nlist;
+  idx->chunks = chunks;
+  idx->has_model = true;
+  idx->lists_dirty = true;
+  return XVEC_GPU_OK;
+}
+
+extern "C" xvec_gpu_status xvec_gpu_kmeans_assign_device(int32_t device, int32_t metric,
+                                                         const float* d_vectors, int64_t n,
+                                                         const float* d_centroids, int32_t nc,
+                                                         int32_t dim, int32_t* d_labels,
+                                                         float* d_scores, void* stream) {
+  if (nc <= 0 || dim <= 0 || n < 0) return set_error("invalid k-means arguments"), XVEC_GPU_INVALID_ARGUMENT;
+  if (n == 0) return XVEC_GPU_OK;
+  cudaSetDevice(device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  xvec_gpu_index* probe = nullptr;
+  xvec_gpu_status st = make_probe_index(device, metric, dim, d_centroids, nc, s, &probe);
+  if (st) return st;
+  st = assign_rows(probe, d_vectors, n, dim, d_labels, d_scores, s);
+  xvec_gpu_index_destroy(probe);
+  return st;
+}
+
+extern "C" xvec_gpu_status xvec_gpu_kmeans_assign(int32_t device, int32_t metric,
+                                                  const float* vectors, int64_t n,
+                                                  const float* centroids, int32_t nc, int32_t dim,
+                                                  int32_t* labels, float* scores) {
+  if (nc <= 0 || dim <= 0 || n < 0 || !vectors || !centroids || !labels)
+    return set_error("invalid k-means arguments"), XVEC_GPU_INVALID_ARGUMENT;
+  if (n == 0) return XVEC_GPU_OK;
+  cudaSetDevice(device);
+  cudaStream_t s = nullptr;
+  Scratch dv, dc, dl, ds;
+  xvec_gpu_status st;
+  if ((st = dv.alloc((size_t)n * dim * 4, s)) || (st = dc.alloc((size_t)nc * dim * 4, s)) ||
+      (st = dl.alloc((size_t)n * 4, s)) || (st = ds.alloc((size_t)n * 4, s)))
+    return st;
+  XVEC_CUDA(cudaMemcpyAsync(dv.ptr, vectors, (size_t)n * dim * 4, cudaMemcpyHostToDevice, s));
+  XVEC_CUDA(cudaMemcpyAsync(dc.ptr, centroids, (size_t)nc * dim * 4, cudaMemcpyHostToDevice, s));
+  st = xvec_gpu_kmeans_assign_device(device, metric, dv.as<float>(), n, dc.as<float>(), nc, dim,
+                                     dl.as<int32_t>(), ds.as<float>(), s);
+  if (st) return st;
+  XVEC_CUDA(cudaMemcpyAsync(labels, dl.ptr, (size_t)n * 4, cudaMemcpyDeviceToHost, s));
+  if (scores) XVEC_CUDA(cudaMemcpyAsync(scores, ds.ptr, (size_t)n * 4, cudaMemcpyDeviceToHost, s));
+  XVEC_CUDA(cudaStreamSynchronize(s));
+  return XVEC_GPU_OK;
+}
