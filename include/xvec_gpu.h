@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define XVEC_GPU_ABI_VERSION 1
+#define XVEC_GPU_ABI_VERSION 2
 
 typedef enum {
   XVEC_GPU_OK = 0,
@@ -96,9 +96,16 @@ typedef struct {
   int32_t nprobe;           /* IVFSearchOptions.NProbe (ivf.go:387-400); IVF_PQ only */
   float refine_scale;       /* > 0: UseRefiner with QueryParams.ScaleFactor
                                (collection.go:1606-1631, refiner.go:112-129).
-                               SQ8_FLAT: exact fp32 rerank of floor(top_k*scale) codes.
-                               RABITQ: number of estimates refined = floor(top_k*scale)
-                               (>= top_k). */
+                               SQ8_FLAT only: exact fp32 rerank of floor(top_k*scale)
+                               codes. */
+  int32_t ef;               /* HNSWRaBitQSearchOptions.EF (hnsw_rabitq.go:548-550),
+                               RABITQ only: in [1, 2048] (ErrInvalidHNSWEF); with
+                               refine, min(len, max(top_k, ef)) estimates are refined
+                               (hnsw_rabitq.go:579) */
+  int32_t refine;           /* HNSWRaBitQSearchOptions.Refine, RABITQ only: non-zero =
+                               exact fp32 rerank of the best estimates; zero = the
+                               estimates themselves with the public score (IP:
+                               1 - estimate) */
   const uint32_t* filter_bitmap; /* NULL = no filter.  Bit p (word p/32, bit p%32) set =
                                     the row at insertion position p passes
                                     CandidateFilter (query.go:35); evaluated before

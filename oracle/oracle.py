@@ -148,12 +148,13 @@ class Oracle:
                                                 ctypes.c_int32, _u8p, _f32p, _f32p, _f64p, _f64p,
                                                 _f64p]
         lib.xo_rabitq_estimate_coarse.argtypes = [_f32p, ctypes.c_int32, ctypes.c_double, _f64p,
-                                                  _u8p, ctypes.POINTER(RaBitQFactors), _f32p]
+                                                  _f64p, _u8p, ctypes.POINTER(RaBitQFactors),
+                                                  _f32p]
         lib.xo_rabitq_search.argtypes = [ctypes.c_int, ctypes.c_int32, _f32p, ctypes.c_int32,
                                          _u8p, _u8p, ctypes.c_void_p, _f32p, _u64p,
                                          ctypes.c_int64, _f32p, ctypes.c_int32, ctypes.c_int32,
-                                         ctypes.c_int32, ctypes.c_float, _u32p, ctypes.c_int32,
-                                         _u64p, _f32p, _i32p, _i32p]
+                                         ctypes.c_int32, ctypes.c_int32, ctypes.c_float, _u32p,
+                                         ctypes.c_int32, _u64p, _f32p, _i32p, _i32p]
         del search_tail
         lib.xo_use_reference_kernels.argtypes = [ctypes.c_void_p] * 6
         self.kernels = "restated"
@@ -472,21 +473,24 @@ class Oracle:
                                               _ptr(gadd, _f64p), _ptr(gerr, _f64p))
         return st, rot, float(s[0]), gadd, gerr
 
-    def rabitq_estimate_coarse(self, rotated, qsum, gadd, code, factors_row):
+    def rabitq_estimate_coarse(self, rotated, qsum, gadd, code, factors_row, gerr=None):
         rotated = _c(rotated, np.float32)
         gadd = _c(gadd, np.float64)
+        gerr = None if gerr is None else _c(gerr, np.float64)
         code = _c(code, np.uint8)
         f = RaBitQFactors(int(factors_row["cluster"]), 0, float(factors_row["coarse_add"]),
                           float(factors_row["coarse_rescale"]), float(factors_row["coarse_error"]),
                           float(factors_row["full_add"]), float(factors_row["full_rescale"]))
         out = np.zeros(1, np.float32)
         st = self.lib.xo_rabitq_estimate_coarse(_ptr(rotated, _f32p), rotated.size, qsum,
-                                                _ptr(gadd, _f64p), _ptr(code, _u8p),
+                                                _ptr(gadd, _f64p), _ptr(gerr, _f64p),
+                                                _ptr(code, _u8p),
                                                 ctypes.byref(f), _ptr(out, _f32p))
         return st, np.float32(out[0])
 
     def rabitq_search(self, metric, centroids, signs, codes, factors, originals, keys, queries,
-                      k, candidate_count, radius=0.0, bitmap=None, threads=0):
+                      k, candidate_count, radius=0.0, bitmap=None, threads=0, refine=True):
+        """Linear RaBitQ search; candidate_count plays HNSWRaBitQSearchOptions.EF."""
         centroids = _c(centroids, np.float32)
         signs = _c(signs, np.uint8)
         codes = _c(codes, np.uint8)
@@ -501,7 +505,8 @@ class Oracle:
         st = self.lib.xo_rabitq_search(metric, d, _ptr(centroids, _f32p), centroids.shape[0],
                                        _ptr(signs, _u8p), _ptr(codes, _u8p), factors.ctypes.data,
                                        _ptr(originals, _f32p), _ptr(keys, _u64p), n,
-                                       _ptr(queries, _f32p), nq, k, candidate_count, radius,
+                                       _ptr(queries, _f32p), nq, k, candidate_count,
+                                       1 if refine else 0, radius,
                                        _ptr(bm, _u32p), threads or os.cpu_count(),
                                        _ptr(ok, _u64p), _ptr(os_, _f32p), _ptr(oc, _i32p),
                                        _ptr(ost, _i32p))

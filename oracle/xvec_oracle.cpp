@@ -1459,34 +1459,40 @@ extern "C" int xo_rabitq_prepare_query(int metric, int32_t d, const float* centr
 }
 
 // EstimateCoarse (rabitq.go:421-430), raBitQBinaryDot (rabitq_quantize.go:
-// 302-310) and the distance part of makeRaBitQEstimate (rabitq.go:464-476).
+// 302-310) and makeRaBitQEstimate (rabitq.go:464-476); g_error may be null
+// (then the error bound is taken as 0).
 extern "C" int xo_rabitq_estimate_coarse(const float* rotated, int32_t padded, double sum,
-                                         const double* g_add, const uint8_t* bits,
-                                         const xo_rabitq_factors* f, float* distance) {
+                                         const double* g_add, const double* g_error,
+                                         const uint8_t* bits, const xo_rabitq_factors* f,
+                                         float* distance) {
   double dot = 0;
   for (int32_t i = 0; i < padded; ++i)
     if (bits[i / 8] & (1u << (i % 8))) dot += (double)rotated[i];
   double centered = dot - .5 * sum;
   double dist = f->coarse_add + g_add[f->cluster] + f->coarse_rescale * centered;
-  double err = f->coarse_error;  // bound magnitude checked by the caller's gError
-  if (std::isnan(dist) || std::isinf(dist) || std::isnan(err) || std::isinf(err))
+  double eb = g_error ? f->coarse_error * g_error[f->cluster] : 0.0;
+  const double maxf = 3.40282346638528859811704183484516925440e+38;
+  if (std::isnan(dist) || std::isinf(dist) || std::isnan(eb) || std::isinf(eb) || eb < 0)
     return XO_INVALID_ARGUMENT;
-  if (std::fabs(dist) > 3.4028234663852886e38) return XO_OVERFLOW;
+  if (std::fabs(dist) > maxf || eb > maxf) return XO_OVERFLOW;
+  if (dist - eb < -maxf || dist + eb > maxf) return XO_OVERFLOW;
   *distance = (float)dist;
   return XO_OK;
 }
 
-// Composed RaBitQ linear search with exact refinement (hnsw_rabitq.go):
-//   search (:539-586) with Refine and Linear=false but an explicit
-//   candidate_count, scanRaBitQCodes (:615-642) over every code with
-//   raBitQNodeBetter (:739-744: lower estimate, ties → lower key) and
-//   acceptRaBitQNode (:753-757: filter, radius on the public score), then
-//   refinePrepared (:780-801): exact fp32 metric on originals, top-k.
+// Composed RaBitQ linear search (hnsw_rabitq.go:539-586) over every code
+// (scanRaBitQCodes, :615-642: first failing estimate fails the query, then
+// acceptRaBitQNode :753-757, filter and radius on the public score, and a
+// heap with raBitQNodeBetter :739-744, lower estimate, ties to the lower key).
+//   refine != 0: the scan keeps min(n, candidate_count) estimates without the
+//     radius (:579-584) and refinePrepared (:780-801) returns the exact fp32
+//     top-k of those (metric.Compute on the originals, query validated first).
+//   refine == 0: the k best estimates with publicRaBitQScore (:746-751).
 extern "C" int xo_rabitq_search(int metric, int32_t d, const float* centroids, int32_t nc,
                                 const uint8_t* signs, const uint8_t* binary_codes,
                                 const xo_rabitq_factors* factors, const float* originals,
                                 const uint64_t* keys, int64_t n, const float* queries, int32_t nq,
-                                int32_t k, int32_t candidate_count, float radius,
+                                int32_t k, int32_t candidate_count, int32_t refine, float radius,
                                 const uint32_t* bitmap, int32_t threads, uint64_t* out_keys,
                                 float* out_scores, int32_t* out_counts, int32_t* out_status) {
   int st0 = validate_options(k, radius);
@@ -1494,6 +1500,7 @@ extern "C" int xo_rabitq_search(int metric, int32_t d, const float* centroids, i
   int32_t padded = xo_rabitq_padded_dimension(d);
   int32_t bytes = padded / 8;
   std::vector<int32_t> status(nq, XO_OK);
+  auto public_score = [&](float dist) { return metric == XO_IP ? 1.0f - dist : dist; };
   parallel_for(nq, threads, [&](int64_t q) {
     const float* query = queries + q * d;
     std::vector<float> rot(padded);
@@ -1503,39 +1510,42 @@ extern "C" int xo_rabitq_search(int metric, int32_t d, const float* centroids, i
                                      gadd.data(), gerr.data());
     std::vector<Result> res;
     if (st == XO_OK && n > 0) {
-      int32_t cc = (int32_t)std::min<int64_t>(n, std::max(k, candidate_count));
-      // The approximate stage ranks by estimated distance (lower better for
-      // every metric); reuse the heap with the L2 ordering.
+      int32_t cc = refine ? (int32_t)std::min<int64_t>(n, std::max(k, candidate_count)) : k;
+      // Estimates rank lower-is-better for every metric: the L2 heap order.
       WorstFirstHeap heap{XO_L2, {}};
       for (int64_t p = 0; p < n && st == XO_OK; ++p) {
         float est;
-        st = xo_rabitq_estimate_coarse(rot.data(), padded, sum, gadd.data(),
+        st = xo_rabitq_estimate_coarse(rot.data(), padded, sum, gadd.data(), gerr.data(),
                                        binary_codes + p * bytes, &factors[p], &est);
         if (st != XO_OK) break;
         if (!filter_pass(bitmap, p)) continue;
-        // The approximate stage of a refined search carries no radius
-        // (hnsw_rabitq.go:584: SearchOptions{TopK, Filter}).
+        if (!refine && !within_radius(metric, public_score(est), radius)) continue;
         heap.offer(Result{keys[p], est}, (size_t)cc);
       }
       if (st == XO_OK) {
         std::vector<Result> cands = heap.sorted();
-        std::vector<int64_t> cpos(cands.size());
-        for (size_t i = 0; i < cands.size(); ++i) {
-          int64_t pos = -1;
-          for (int64_t pp = 0; pp < n; ++pp)
-            if (keys[pp] == cands[i].key) {
-              pos = pp;
-              break;
-            }
-          cpos[i] = pos;
+        if (!refine) {
+          for (auto& r : cands) r.score = public_score(r.score);
+          res = cands;
+        } else {
+          std::vector<int64_t> cpos(cands.size());
+          for (size_t i = 0; i < cands.size(); ++i) {
+            int64_t pos = -1;
+            for (int64_t pp = 0; pp < n; ++pp)
+              if (keys[pp] == cands[i].key) {
+                pos = pp;
+                break;
+              }
+            cpos[i] = pos;
+          }
+          st = validate_query(metric, query, d);
+          if (st == XO_OK)
+            st = topk_scan(metric, (int64_t)cpos.size(), k, radius, nullptr, keys, cpos.data(),
+                           [&](int64_t pos, float* s) {
+                             return prevalidated(metric, originals + pos * d, query, d, s);
+                           },
+                           &res);
         }
-        if (st == XO_OK) st = validate_query(metric, query, d);
-        if (st == XO_OK)
-          st = topk_scan(metric, (int64_t)cpos.size(), k, radius, nullptr, keys, cpos.data(),
-                         [&](int64_t pos, float* s) {
-                           return prevalidated(metric, originals + pos * d, query, d, s);
-                         },
-                         &res);
       }
     }
     status[q] = st;

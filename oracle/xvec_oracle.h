@@ -166,15 +166,17 @@ int xo_rabitq_prepare_query(int metric, int32_t d, const float* centroids, int32
                             double* sum, double* g_add, double* g_error);
 /* EstimateCoarse (rabitq.go:421-430), distance part. */
 int xo_rabitq_estimate_coarse(const float* rotated, int32_t padded, double sum,
-                              const double* g_add, const uint8_t* binary_code,
-                              const xo_rabitq_factors* factors, float* distance);
-/* Composed linear RaBitQ scan + exact refine (hnsw_rabitq.go:539-642,
- * 739-801) with candidate_count estimates refined to top-k. */
+                              const double* g_add, const double* g_error,
+                              const uint8_t* binary_code, const xo_rabitq_factors* factors,
+                              float* distance);
+/* Composed linear RaBitQ scan (hnsw_rabitq.go:539-642, 739-801): with refine,
+ * min(n, max(k, candidate_count)) estimates refined to the exact top-k;
+ * without, the k best estimates with the public score. */
 int xo_rabitq_search(int metric, int32_t d, const float* centroids, int32_t nc,
                      const uint8_t* signs, const uint8_t* binary_codes,
                      const xo_rabitq_factors* factors, const float* originals,
                      const uint64_t* keys, int64_t n, const float* queries, int32_t nq,
-                     int32_t k, int32_t candidate_count, float radius,
+                     int32_t k, int32_t candidate_count, int32_t refine, float radius,
                      const uint32_t* filter_bitmap, int32_t threads, uint64_t* out_keys,
                      float* out_scores, int32_t* out_counts, int32_t* out_status);
 

@@ -69,6 +69,7 @@ class IndexDesc(ctypes.Structure):
 class SearchOpts(ctypes.Structure):
     _fields_ = [("top_k", ctypes.c_int32), ("radius", ctypes.c_float),
                 ("nprobe", ctypes.c_int32), ("refine_scale", ctypes.c_float),
+                ("ef", ctypes.c_int32), ("refine", ctypes.c_int32),
                 ("filter_bitmap", ctypes.c_void_p), ("filter_words", ctypes.c_int64),
                 ("stream", ctypes.c_void_p), ("cancel_flag", ctypes.c_void_p)]
 
@@ -163,7 +164,9 @@ class SearchOptions:
     radius: float = 0.0
     filter: Optional[np.ndarray] = None  # uint32 bitmap over insertion positions
     nprobe: int = 10                     # DefaultIVFNProbe (ivf.go:380)
-    refine_scale: float = 0.0            # > 0: UseRefiner with this ScaleFactor
+    refine_scale: float = 0.0            # > 0: UseRefiner with this ScaleFactor (SQ8)
+    ef: int = 300                        # HNSWRaBitQSearchOptions.EF (DefaultHNSWEFSearch)
+    refine: bool = True                  # HNSWRaBitQSearchOptions.Refine
 
 
 def bitmap_from_predicate(n: int, keys: Sequence[int], predicate: Callable[[int], bool]) -> np.ndarray:
@@ -234,6 +237,8 @@ class _Index:
         o.radius = options.radius
         o.nprobe = options.nprobe
         o.refine_scale = options.refine_scale
+        o.ef = options.ef
+        o.refine = 1 if options.refine else 0
         if device_filter_ptr is not None:
             o.filter_bitmap = device_filter_ptr
             o.filter_words = (len(self) + 31) // 32

@@ -112,7 +112,9 @@ struct xvec_gpu_index {
   xvec::DeviceBuffer rq_rot_centroids;      // float [c][padded]
   xvec::DeviceBuffer rq_signs;              // uint8 [4*padded/8]
   xvec::DeviceBuffer rq_codes;              // uint8 [n][padded/8]
-  xvec::DeviceBuffer rq_factors;            // double [n][3] + int cluster -> struct
+  xvec::DeviceBuffer rq_factors;            // {double add, rescale, error; int cluster} [n]
+  xvec::DeviceBuffer rq_fast;               // float4 {add, rescale, cluster bits, 0} [n]
+  xvec::DeviceBuffer rq_bounds;             // ordered floats: max |add|, |rescale|, error
 
   ~xvec_gpu_index() {
     if (probe_index) xvec_gpu_index_destroy(probe_index);

@@ -180,6 +180,8 @@ struct FlatScorer {
     return fast_eps(metric, d, q_n2[qi], ordered_to_float(*max_n2_ordered));
   }
   __device__ int error_flag(float) const { return 4; }
+  __device__ float output(float r) const { return score_from_rank(metric, r); }
+  __device__ bool keep(float out, float radius) const { return within_radius(metric, out, radius); }
 };
 
 // ---------------------------------------------------------------------------

@@ -218,6 +218,8 @@ struct PQScorer {
   }
   __device__ float eps(int) const { return 0.f; }
   __device__ int error_flag(float) const { return 8; }
+  __device__ float output(float r) const { return score_from_rank(metric, r); }
+  __device__ bool keep(float out, float radius) const { return within_radius(metric, out, radius); }
 };
 
 __global__ void ivfpq_status_kernel(const int* q_status, const int* q_flags, int nq,

@@ -16,7 +16,9 @@
 // Scorer:  int metric (ordering and radius rule);
 //          float score(int qi, int64_t row)  -- called by a whole warp;
 //          float eps(int qi)                  -- bound on |fast - reference|;
-//          int error_flag(float s)            -- flag bit for a non-finite score.
+//          int error_flag(float s)            -- flag bit for a non-finite score;
+//          float output(float rank)           -- the reported score of a rank;
+//          bool keep(float out, float radius) -- the radius rule on that score.
 #pragma once
 
 #include "common.cuh"
@@ -211,7 +213,8 @@ __global__ void __launch_bounds__(256) scan_exact_kernel(
 // exact_mode: the part keys already hold reference ranks; the candidates are
 // exactly the k best keys.
 // ---------------------------------------------------------------------------
-constexpr int kMaxCandidates = 1024;
+constexpr int kMaxCandidates = 1024;      // rescored candidates per query (k <= 1024)
+constexpr int kMaxCandidatesWide = 2048;  // the same for 1024 < k <= 2048
 constexpr int kMergeSmemEntries = 12288;  // union entries gathered in shared memory
 
 // Radix select over keys[0, m) in shared memory: the kth smallest (1-based)
@@ -250,7 +253,7 @@ static __device__ uint64_t smem_radix_select(const uint64_t* keys, int m, int kt
   return s_prefix;
 }
 
-template <typename Scorer>
+template <typename Scorer, int MAXC>
 __global__ void __launch_bounds__(256) merge_rescore_kernel(
     Scorer sc, const uint32_t* __restrict__ pos_of_keyrank, const uint64_t* __restrict__ keys,
     const int* __restrict__ query_ids, int k, float radius, int exact_mode,
@@ -262,7 +265,7 @@ __global__ void __launch_bounds__(256) merge_rescore_kernel(
   extern __shared__ __align__(16) unsigned char merge_smem[];
   uint64_t* ukeys = reinterpret_cast<uint64_t*>(merge_smem);  // [kMergeSmemEntries]
   __shared__ int hist[256];
-  __shared__ uint64_t cand[kMaxCandidates];
+  __shared__ uint64_t cand[MAXC];
   __shared__ int s_offsets[1025];
   __shared__ int s_ncand, s_fail;
   const int slot_q = blockIdx.x;
@@ -324,11 +327,11 @@ __global__ void __launch_bounds__(256) merge_rescore_kernel(
     const uint64_t key = ukeys[i];
     if (key <= limit) {
       const int slot = atomicAdd(&s_ncand, 1);
-      if (slot < kMaxCandidates) cand[slot] = key;
+      if (slot < MAXC) cand[slot] = key;
     }
   }
   __syncthreads();
-  if (s_fail || s_ncand > kMaxCandidates) {
+  if (s_fail || s_ncand > MAXC) {
     if (threadIdx.x == 0) {
       atomicOr(&q_flags[qi], 2);
       out_counts[qi] = 0;
@@ -348,7 +351,7 @@ __global__ void __launch_bounds__(256) merge_rescore_kernel(
     }
   }
   __syncthreads();
-  block_sort_u64<kMaxCandidates>(cand, ncand);
+  block_sort_u64_fit<MAXC>(cand, ncand);
   // Final top-k (radius is monotone in the sorted order).
   if (threadIdx.x < 32) {
     // Count the prefix within radius with a warp scan over chunks.
@@ -358,8 +361,8 @@ __global__ void __launch_bounds__(256) merge_rescore_kernel(
       bool in = i < ncand;
       float s = 0.f;
       if (in) {
-        s = score_from_rank(metric, rank_of(cand[i]));
-        in = within_radius(metric, s, radius);
+        s = sc.output(rank_of(cand[i]));
+        in = sc.keep(s, radius);
       }
       const unsigned m = __ballot_sync(kFullMask, in);
       const int run = (m == kFullMask) ? 32 : __ffs(~m) - 1;  // leading in-radius run
@@ -444,11 +447,13 @@ cudaError_t launch_merge_rescore(const Scorer& sc, const uint32_t* pos_of_keyran
   if (nlist <= 0) return cudaSuccess;
   if (num_parts > 1024) return cudaErrorInvalidValue;
   const int smem = kMergeSmemEntries * 8;
-  cudaFuncSetAttribute(merge_rescore_kernel<Scorer>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       smem);
-  merge_rescore_kernel<Scorer><<<nlist, 256, smem, stream>>>(
-      sc, pos_of_keyrank, keys, query_ids, k, radius, exact_mode, part_keys, part_counts,
-      part_sat, num_parts, stride, out_keys, out_scores, out_counts, out_pos, q_flags);
+  if (k > kMaxCandidatesWide) return cudaErrorInvalidValue;
+  auto kern = k > kMaxCandidates ? merge_rescore_kernel<Scorer, kMaxCandidatesWide>
+                                 : merge_rescore_kernel<Scorer, kMaxCandidates>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  kern<<<nlist, 256, smem, stream>>>(sc, pos_of_keyrank, keys, query_ids, k, radius, exact_mode,
+                                     part_keys, part_counts, part_sat, num_parts, stride,
+                                     out_keys, out_scores, out_counts, out_pos, q_flags);
   return cudaGetLastError();
 }
 

@@ -1,0 +1,794 @@
+// rabitq.cu — one-bit RaBitQ linear scan with exact float32 refinement.
+//
+// Reference: the HNSW-RaBitQ index's linear scan and refine
+// (internal/core/hnsw_rabitq.go:539-642, 739-801) over RaBitQModel codes with
+// TotalBits = 1 (internal/core/rabitq.go:297-327, 372-430;
+// rabitq_quantize.go:99-262, 302-310; rotation.go:123-153; fht.go:28-101).
+//
+//   model    centroids, rotation signs; the centroids are rotated once.
+//   insert   prepare (cosine: normalise, float64 norm in index order), the
+//            nearest centroid (L2, or IP for IP/cosine; ties to the lower
+//            index, through a Flat index over the centroids), the FHT-Kac
+//            rotation of the zero-padded vector (shared memory, each butterfly
+//            elementwise so the float32 results are the reference's), the
+//            sign bits of the residual and the float64 factors (sums in index
+//            order, explicit round-to-nearest operations).
+//   query    PrepareQuery: rotated query, float64 sum, per-centroid gAdd and
+//            gError (sequential float64 sums).
+//   scan     fast estimate: the bit-plane x query dot in float32 on the
+//            shared FFMA tile kernel (bits read as 0/1), the estimate formula
+//            in float32 within a bound eps of the reference; candidates are
+//            rescored with EstimateCoarse's float64 masked sum in index order.
+//   refine   the k best by metric.Compute on the original rows among the
+//            candidate_count best estimates (refine.cuh).
+#include <algorithm>
+#include <cmath>
+#include <vector>
+
+#include "capi_internal.h"
+#include "common.cuh"
+#include "flat_kernels.cuh"
+#include "index_kernels.cuh"
+#include "pipeline.cuh"
+#include "refine.cuh"
+
+namespace xvec {
+
+xvec_gpu_status search_device_locked(xvec_gpu_index* idx, const void* d_q, int nq,
+                                     const xvec_gpu_search_opts& o, const uint32_t* d_bitmap,
+                                     uint64_t* d_keys, float* d_scores, int* d_counts,
+                                     cudaStream_t s, std::vector<int>* statuses);
+xvec_gpu_status add_device_locked(xvec_gpu_index* idx, const uint64_t* d_keys, const void* d_rows,
+                                  int64_t m, cudaStream_t s);
+
+struct RaBitQFactors {
+  double add;
+  double rescale;
+  double error;
+  int32_t cluster;
+  int32_t pad_;
+};
+
+// A row of packed sign bits seen by the FFMA tile kernel as 0/1 elements.
+struct BitElem {
+  uint8_t raw;
+};
+__device__ __forceinline__ float load_elem(const BitElem* p, int64_t i) {
+  const uint8_t* b = reinterpret_cast<const uint8_t*>(p);
+  return (float)((b[i >> 3] >> (i & 7)) & 1u);
+}
+
+namespace {
+
+constexpr double kU = 5.9604644775390625e-8;  // 2^-24
+// q_flags bits of this file (bits 1 and 2 belong to the pipeline, 4 to refine).
+constexpr int kRaBitQInvalid = 8;      // ErrInvalidRaBitQCode
+constexpr int kRaBitQOverflow = 16;    // ErrQuantizationOverflow
+constexpr int kRaBitQFullCheck = 32;   // estimates may fail: check every row
+inline unsigned blocks_of(int64_t n, int t = 256) { return (unsigned)((n + t - 1) / t); }
+
+// normalizeRaBitQVector (rabitq.go:514-526) of v[0, d) in shared memory.
+__device__ void block_normalize(float* v, int d) {
+  __shared__ float s_inv;
+  __shared__ int s_skip;
+  if (threadIdx.x == 0) {
+    double ns = 0.0;
+    for (int i = 0; i < d; ++i) ns = __dadd_rn(ns, __dmul_rn((double)v[i], (double)v[i]));
+    s_skip = ns == 0.0;
+    s_inv = s_skip ? 0.f : __double2float_rn(__ddiv_rn(1.0, __dsqrt_rn(ns)));
+  }
+  __syncthreads();
+  if (!s_skip)
+    for (int i = threadIdx.x; i < d; i += blockDim.x) v[i] = __fmul_rn(v[i], s_inv);
+  __syncthreads();
+}
+
+// FHTInPlace (fht.go:41-57) on data[0, n), n a power of two.
+__device__ void block_fht(float* data, int n) {
+  for (int w = 1; w < n; w <<= 1) {
+    for (int t = threadIdx.x; t < n / 2; t += blockDim.x) {
+      const int idx = (t / w) * 2 * w + (t % w);
+      const float l = data[idx], r = data[idx + w];
+      data[idx] = __fadd_rn(l, r);
+      data[idx + w] = __fsub_rn(l, r);
+    }
+    __syncthreads();
+  }
+}
+
+// FHTRotator.Rotate (rotation.go:123-153) of a padded vector in shared memory.
+__device__ void block_rotate(float* v, int padded, int truncated, const uint8_t* signs, float inv) {
+  const int bpr = padded / 8;
+  auto flip = [&](const uint8_t* sg) {
+    for (int i = threadIdx.x; i < padded; i += blockDim.x)
+      if (sg[i >> 3] & (1u << (i & 7))) v[i] = -v[i];
+    __syncthreads();
+  };
+  auto scale = [&](float* w, int n, float f) {
+    for (int i = threadIdx.x; i < n; i += blockDim.x) w[i] = __fmul_rn(w[i], f);
+    __syncthreads();
+  };
+  if (truncated == padded) {
+    for (int r = 0; r < 4; ++r) {
+      flip(signs + r * bpr);
+      block_fht(v, padded);
+      scale(v, padded, inv);
+    }
+    return;
+  }
+  const int start = padded - truncated;
+  for (int r = 0; r < 4; ++r) {
+    flip(signs + r * bpr);
+    float* window = (r % 2 != 0) ? v + start : v;
+    block_fht(window, truncated);
+    scale(window, truncated, inv);
+    // FHTKacWalk (fht.go:59-76); padded is even, so there is no middle term.
+    const int half = padded / 2;
+    for (int t = threadIdx.x; t < half; t += blockDim.x) {
+      const float l = v[t], rr = v[t + half];
+      v[t] = __fadd_rn(l, rr);
+      v[t + half] = __fsub_rn(l, rr);
+    }
+    __syncthreads();
+  }
+  scale(v, padded, 0.25f);
+}
+
+// Loads v (d floats) zero-padded to `padded`, optionally normalises, rotates.
+__device__ bool block_prepare_rotate(const float* src, int d, int padded, int truncated,
+                                     const uint8_t* signs, float inv, bool normalize, float* v) {
+  for (int i = threadIdx.x; i < padded; i += blockDim.x) v[i] = i < d ? src[i] : 0.f;
+  __syncthreads();
+  if (normalize) block_normalize(v, d);
+  block_rotate(v, padded, truncated, signs, inv);
+  __shared__ int s_bad;
+  if (threadIdx.x == 0) s_bad = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < padded; i += blockDim.x)
+    if (!finite_f(v[i])) s_bad = 1;
+  __syncthreads();
+  return !s_bad;
+}
+
+// Rotated model centroids (RestoreRaBitQModel, rabitq.go:224-230).
+__global__ void rabitq_rotate_centroids_kernel(const float* centroids, int d, int padded,
+                                               int truncated, const uint8_t* signs, float inv,
+                                               float* out, int* err) {
+  extern __shared__ float v[];
+  if (!block_prepare_rotate(centroids + (int64_t)blockIdx.x * d, d, padded, truncated, signs, inv,
+                            false, v) &&
+      threadIdx.x == 0)
+    atomicExch(err, XVEC_GPU_NON_FINITE);
+  for (int i = threadIdx.x; i < padded; i += blockDim.x) out[(int64_t)blockIdx.x * padded + i] = v[i];
+}
+
+// prepareRaBitQVector for rows that are assigned before rotation.
+__global__ void rabitq_prepare_kernel(const float* rows, int64_t n, int d, bool normalize,
+                                      float* out) {
+  extern __shared__ float v[];
+  const float* src = rows + (int64_t)blockIdx.x * d;
+  for (int i = threadIdx.x; i < d; i += blockDim.x) v[i] = src[i];
+  __syncthreads();
+  if (normalize) block_normalize(v, d);
+  for (int i = threadIdx.x; i < d; i += blockDim.x) out[(int64_t)blockIdx.x * d + i] = v[i];
+}
+
+// quantizeRaBitQVector (rabitq_quantize.go:99-200) with TotalBits = 1 and
+// raBitQFactors (rabitq_quantize.go:210-262), one block per row.
+__global__ void rabitq_encode_kernel(const float* prepared, int64_t n, int d, int padded,
+                                     int truncated, const uint8_t* signs, float inv,
+                                     const float* rot_centroids, const int32_t* labels,
+                                     int inner_product, uint8_t* codes, RaBitQFactors* factors,
+                                     float4* fast, unsigned* bounds, int* err) {
+  extern __shared__ float smem[];
+  float* v = smem;                 // [padded] rotated row
+  __shared__ double s_sum[4];
+  const int64_t r = blockIdx.x;
+  if (!block_prepare_rotate(prepared + r * d, d, padded, truncated, signs, inv, false, v)) {
+    if (threadIdx.x == 0) atomicExch(err, XVEC_GPU_NON_FINITE);
+    return;
+  }
+  const int c = labels[r];
+  const float* cen = rot_centroids + (int64_t)c * padded;
+  // Sign bits of the residual, LSB first (setRaBitQBit).
+  for (int byte = threadIdx.x; byte < padded / 8; byte += blockDim.x) {
+    uint8_t b = 0;
+    for (int j = 0; j < 8; ++j) {
+      const int i = byte * 8 + j;
+      const double res = __dsub_rn((double)v[i], (double)cen[i]);
+      if (res > 0) b |= (uint8_t)(1u << j);
+    }
+    codes[r * (padded / 8) + byte] = b;
+  }
+  // The four float64 sums of raBitQFactors, each in index order.
+  if (threadIdx.x < 4) {
+    double acc = 0.0;
+    for (int i = 0; i < padded; ++i) {
+      const double res = __dsub_rn((double)v[i], (double)cen[i]);
+      const double cc = res > 0 ? 0.5 : -0.5;  // value + center, center = -(2^1 - 1)/2
+      const double ce = (double)cen[i];
+      double t;
+      if (threadIdx.x == 0) t = __dmul_rn(res, res);        // normSquared
+      else if (threadIdx.x == 1) t = __dmul_rn(res, cc);    // residualCodeDot
+      else if (threadIdx.x == 2) t = __dmul_rn(ce, cc);     // centroidCodeDot
+      else t = __dmul_rn(res, ce);                          // residualCentroidDot
+      acc = __dadd_rn(acc, t);
+    }
+    s_sum[threadIdx.x] = acc;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const double ns = s_sum[0], rcd = s_sum[1], ccd = s_sum[2], rcent = s_sum[3];
+    const double cns = 0.25 * (double)padded;  // sum of 0.25 over padded terms, exact
+    double add, rescale, errf;
+    bool ok = true;
+    if (ns == 0) {
+      add = inner_product ? 1.0 : 0.0;
+      rescale = 0.0;
+      errf = 0.0;
+    } else if (!(rcd > 0) || isinf(rcd)) {
+      ok = false;
+    } else {
+      double ratio = __dsub_rn(__ddiv_rn(__dmul_rn(ns, cns), __dmul_rn(rcd, rcd)), 1.0);
+      if (ratio < 0 && ratio > -1e-12) ratio = 0;
+      if (ratio < 0 || isnan(ratio) || isinf(ratio)) ok = false;
+      if (ok) {
+        const double norm = __dsqrt_rn(ns);
+        const double te = __dmul_rn(__dmul_rn(norm, 1.9),
+                                    __dsqrt_rn(__ddiv_rn(ratio, (double)(padded - 1))));
+        if (inner_product) {
+          add = __dadd_rn(__dsub_rn(1.0, rcent), __ddiv_rn(__dmul_rn(ns, ccd), rcd));
+          rescale = __ddiv_rn(-ns, rcd);
+          errf = te;
+        } else {
+          add = __dadd_rn(ns, __ddiv_rn(__dmul_rn(__dmul_rn(2.0, ns), ccd), rcd));
+          rescale = __ddiv_rn(__dmul_rn(-2.0, ns), rcd);
+          errf = __dmul_rn(2.0, te);
+        }
+        if (!isfinite(add) || !isfinite(rescale) || !isfinite(errf)) ok = false;
+      }
+    }
+    if (!ok) {
+      atomicExch(err, XVEC_GPU_OVERFLOW);
+      return;
+    }
+    factors[r] = RaBitQFactors{add, rescale, errf, c, 0};
+    fast[r] = make_float4(__double2float_rn(add), __double2float_rn(rescale), __int_as_float(c),
+                          0.f);
+    atomicMax(&bounds[0], float_to_ordered(fabsf(__double2float_rn(add))));
+    atomicMax(&bounds[1], float_to_ordered(fabsf(__double2float_rn(rescale))));
+    atomicMax(&bounds[2], float_to_ordered(__double2float_ru(errf)));
+  }
+}
+
+// PrepareQuery (rabitq.go:372-408) + the fast-estimate constants and eps.
+__global__ void rabitq_prep_query_kernel(const float* queries, int nq, int d, int padded,
+                                         int truncated, const uint8_t* signs, float inv,
+                                         int normalize, int metric, const float* rot_centroids,
+                                         int nc, const unsigned* bounds, float* q_rot,
+                                         double* q_sum, double* g_add, double* g_error,
+                                         float* q_fast_sum, float* q_fast_gadd, float* q_eps,
+                                         int* q_exact, int* q_status, int* q_flags) {
+  extern __shared__ float v[];
+  __shared__ double s_sum;
+  __shared__ float s_abs;
+  const int q = blockIdx.x;
+  const float* src = queries + (int64_t)q * d;
+  __shared__ int s_bad;
+  if (threadIdx.x == 0) s_bad = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < d; i += blockDim.x)
+    if (!finite_f(src[i])) s_bad = 1;
+  __syncthreads();
+  // A query PrepareQuery rejects gets neutral values (it is never scored).
+  auto reject = [&]() {
+    for (int i = threadIdx.x; i < padded; i += blockDim.x) q_rot[(int64_t)q * padded + i] = 0.f;
+    for (int c = threadIdx.x; c < nc; c += blockDim.x) {
+      g_add[(int64_t)q * nc + c] = 0.0;
+      g_error[(int64_t)q * nc + c] = 0.0;
+      q_fast_gadd[(int64_t)q * nc + c] = 0.f;
+    }
+    if (threadIdx.x == 0) {
+      q_sum[q] = 0.0;
+      q_fast_sum[q] = 0.f;
+      q_eps[q] = 0.f;
+      q_exact[q] = 1;
+      q_status[q] = XVEC_GPU_NON_FINITE;
+    }
+  };
+  if (s_bad) {
+    reject();
+    return;
+  }
+  if (!block_prepare_rotate(src, d, padded, truncated, signs, inv, normalize != 0, v)) {
+    reject();
+    return;
+  }
+  for (int i = threadIdx.x; i < padded; i += blockDim.x) q_rot[(int64_t)q * padded + i] = v[i];
+  if (threadIdx.x == 0) {
+    double s = 0.0, a = 0.0;
+    int g = 1 << 20;  // least exponent of an ulp among the non-zero values
+    for (int i = 0; i < padded; ++i) {
+      s = __dadd_rn(s, (double)v[i]);
+      a = __dadd_rn(a, fabs((double)v[i]));
+      if (v[i] != 0.f) {
+        const int e = (int)((float_bits(v[i]) >> 23) & 0xffu);
+        g = min(g, e == 0 ? -149 : e - 150);
+      }
+    }
+    s_sum = s;
+    s_abs = (float)a;
+    q_sum[q] = s;
+    q_fast_sum[q] = __double2float_rn(s);
+    // Every value is a multiple of 2^g and every partial sum of a subset is
+    // at most a in magnitude; below 2^(52+g) all of them are exact in float64,
+    // so the masked sums may be taken in any order.
+    q_exact[q] = (g == (1 << 20)) || a <= ldexp(1.0, min(1000, 52 + g));
+  }
+  for (int c = threadIdx.x; c < nc; c += blockDim.x) {
+    const float* cen = rot_centroids + (int64_t)c * padded;
+    double sq = 0.0, dot = 0.0;
+    for (int i = 0; i < padded; ++i) {
+      const double diff = __dsub_rn((double)v[i], (double)cen[i]);
+      sq = __dadd_rn(sq, __dmul_rn(diff, diff));
+      dot = __dadd_rn(dot, __dmul_rn((double)v[i], (double)cen[i]));
+    }
+    g_error[(int64_t)q * nc + c] = __dsqrt_rn(sq);
+    const double ga = metric == kMetricL2 ? sq : -dot;
+    g_add[(int64_t)q * nc + c] = ga;
+    q_fast_gadd[(int64_t)q * nc + c] = __double2float_rn(ga);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double maxg = 0.0, maxge = 0.0;
+    for (int c = 0; c < nc; ++c) {
+      maxg = fmax(maxg, fabs(g_add[(int64_t)q * nc + c]));
+      maxge = fmax(maxge, g_error[(int64_t)q * nc + c]);
+    }
+    const double maxA = ordered_to_float(bounds[0]), maxR = ordered_to_float(bounds[1]);
+    const double maxE = ordered_to_float(bounds[2]);
+    const double S1 = (double)s_abs * 1.001;
+    const double sumd = fabs(s_sum);
+    // |estimate| and its error bound over every row; far below MaxFloat32 no
+    // row can fail makeRaBitQEstimate and the float32 fast rank is finite.
+    const double reach = maxA + maxg + maxR * (S1 + 0.5 * sumd) + maxE * maxge;
+    if (!(reach < 1e37)) q_flags[q] |= 1 | kRaBitQFullCheck;
+    // Bound on |fast rank - float32(estimate)| (accumulation of up to padded
+    // terms, the float32 roundings of the inputs and of each operation).
+    const double e = maxR * (double)(padded + 2) * kU * S1 +
+                     6.0 * kU * (maxA + maxg + maxR * (S1 + 0.5 * sumd));
+    q_eps[q] = (float)(2.5 * e) + 1e-30f;
+    q_status[q] = 0;
+  }
+}
+
+__host__ __device__ inline int rabitq_query_status(int prep, int flags, int refine_status) {
+  if (prep) return prep;
+  if (flags & kRaBitQInvalid) return XVEC_GPU_INVALID_ARGUMENT;
+  if (flags & kRaBitQOverflow) return XVEC_GPU_OVERFLOW;
+  if (refine_status) return refine_status;
+  if (flags & 4) return XVEC_GPU_NON_FINITE;
+  return 0;
+}
+
+struct RaBitQRanker {
+  const float4* fast;
+  const float* q_fast_sum;
+  const float* q_fast_gadd;
+  int nc;
+  struct RowInfo {
+    float add, rescale;
+    int cluster;
+  };
+  struct QueryInfo {
+    int qi;
+    float half_sum;
+  };
+  __device__ QueryInfo query(int qi) const { return {qi, 0.5f * q_fast_sum[qi]}; }
+  __device__ RowInfo row(int64_t r) const {
+    const float4 f = fast[r];
+    return {f.x, f.y, __float_as_int(f.z)};
+  }
+  __device__ float rank(float dot, const RowInfo& r, const QueryInfo& q) const {
+    return fmaf(r.rescale, dot - q.half_sum, r.add + q_fast_gadd[(int64_t)q.qi * nc + r.cluster]);
+  }
+};
+
+// EstimateCoarse (rabitq.go:421-430) + makeRaBitQEstimate (rabitq.go:464-476).
+// The masked sum is the reference's float64 sum in index order: taken by the
+// whole warp when every partial sum is exact for this query (q_exact), else
+// sequentially by lane 0.  An invalid estimate scores NaN, an overflowing one
+// +inf (error_flag tells them apart).
+struct RaBitQScorer {
+  int metric;         // ordering: estimates rank ascending for every metric
+  int public_metric;  // the index metric, for the reported score without refine
+  const uint8_t* codes;
+  const RaBitQFactors* factors;
+  const float* q_rot;
+  const double* q_sum;
+  const double* g_add;
+  const double* g_error;
+  const float* q_eps;
+  const int* q_exact;
+  int padded, nc;
+  __device__ float score(int qi, int64_t row) const {
+    const int lane = threadIdx.x & 31;
+    const uint8_t* b = codes + row * (padded / 8);
+    const float* q = q_rot + (int64_t)qi * padded;
+    double dot = 0.0;
+    if (q_exact[qi]) {
+      for (int i = lane; i < padded; i += 32)
+        if (b[i >> 3] & (1u << (i & 7))) dot = __dadd_rn(dot, (double)q[i]);
+      for (int o = 16; o > 0; o >>= 1) dot = __dadd_rn(dot, __shfl_xor_sync(kFullMask, dot, o));
+    } else {
+      if (lane == 0)
+        for (int i = 0; i < padded; ++i)
+          if (b[i >> 3] & (1u << (i & 7))) dot = __dadd_rn(dot, (double)q[i]);
+      dot = __shfl_sync(kFullMask, dot, 0);
+    }
+    const RaBitQFactors f = factors[row];
+    const double centered = __dsub_rn(dot, __dmul_rn(0.5, q_sum[qi]));
+    const double dist = __dadd_rn(__dadd_rn(f.add, g_add[(int64_t)qi * nc + f.cluster]),
+                                  __dmul_rn(f.rescale, centered));
+    const double eb = __dmul_rn(f.error, g_error[(int64_t)qi * nc + f.cluster]);
+    constexpr double kMaxF = 3.40282346638528859811704183484516925440e+38;
+    if (isnan(dist) || isinf(dist) || isnan(eb) || isinf(eb) || eb < 0)
+      return __int_as_float(0x7fc00000);
+    if (fabs(dist) > kMaxF || eb > kMaxF) return __int_as_float(0x7f800000);
+    if (__dsub_rn(dist, eb) < -kMaxF || __dadd_rn(dist, eb) > kMaxF)
+      return __int_as_float(0x7f800000);
+    return __double2float_rn(dist);
+  }
+  __device__ float eps(int qi) const { return q_eps[qi]; }
+  __device__ int error_flag(float s) const { return isnan(s) ? kRaBitQInvalid : kRaBitQOverflow; }
+  // Without refinement the reported score is the public one
+  // (publicRaBitQScore, hnsw_rabitq.go:746-751) and the radius applies to it
+  // (acceptRaBitQNode, hnsw_rabitq.go:753-757).
+  __device__ float output(float r) const {
+    return public_metric == kMetricIP ? __fsub_rn(1.f, r) : r;
+  }
+  __device__ bool keep(float out, float radius) const {
+    return within_radius(public_metric, out, radius);
+  }
+};
+
+// Per-query status: PrepareQuery's, then the scan's, then the refine's.
+__global__ void rabitq_status_kernel(const int* q_status, const int* q_flags,
+                                     const int* refine_status, int nq, int* out_counts) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= nq) return;
+  const int st = rabitq_query_status(q_status[i], q_flags[i], refine_status ? refine_status[i] : 0);
+  if (st != 0) out_counts[i] = -st;
+}
+__global__ void rabitq_clear_flags(const int* ids, int n, int* q_flags) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) q_flags[ids[i]] &= ~3;
+}
+
+int floor_pow2(int v) {
+  int r = 1;
+  while (r <= v / 2) r *= 2;
+  return r;
+}
+float inv_sqrt_size(int truncated) {
+  return 1.0f / (float)std::sqrt((double)(float)truncated);
+}
+
+// Entries kept per (query, part): the candidate count plus a margin for the
+// eps band, a multiple of 32 (the accumulators take any such size).
+int rabitq_kp(int cc) { return (cc + std::max(8, cc / 4) + 31) / 32 * 32; }
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// Index hooks.
+// ---------------------------------------------------------------------------
+xvec_gpu_status rabitq_reserve(xvec_gpu_index* idx, int64_t cap, cudaStream_t s) {
+  const int64_t n = idx->n;
+  const int bytes = idx->padded / 8;
+  xvec_gpu_status st;
+  if ((st = idx->rq_codes.reserve((size_t)cap * bytes, (size_t)n * bytes, s)) ||
+      (st = idx->rq_factors.reserve((size_t)cap * sizeof(RaBitQFactors),
+                                    (size_t)n * sizeof(RaBitQFactors), s)) ||
+      (st = idx->rq_fast.reserve((size_t)cap * 16, (size_t)n * 16, s)))
+    return st;
+  if (!idx->rq_bounds.ptr) {
+    if ((st = idx->rq_bounds.reserve(16, 0, s))) return st;
+    XVEC_CUDA(cudaMemsetAsync(idx->rq_bounds.ptr, 0, 16, s));
+  }
+  return XVEC_GPU_OK;
+}
+
+xvec_gpu_status rabitq_commit(xvec_gpu_index* idx, int64_t old_n, int64_t m, cudaStream_t s) {
+  const int d = idx->desc.dimension, padded = idx->padded, metric = idx->desc.metric;
+  const int truncated = floor_pow2(d);
+  const float inv = inv_sqrt_size(truncated);
+  xvec_gpu_status st;
+  Scratch prepared, labels, err, bounds;
+  if ((st = prepared.alloc((size_t)m * d * 4, s)) || (st = labels.alloc((size_t)m * 4, s)) ||
+      (st = err.alloc(4, s)) || (st = bounds.alloc(16, s)))
+    return st;
+  XVEC_CUDA(cudaMemsetAsync(err.ptr, 0, 4, s));
+  XVEC_CUDA(cudaMemcpyAsync(bounds.ptr, idx->rq_bounds.ptr, 16, cudaMemcpyDeviceToDevice, s));
+  rabitq_prepare_kernel<<<(unsigned)m, 256, d * 4, s>>>(idx->rows.as<float>() + old_n * d, m, d,
+                                                       metric == XVEC_METRIC_COSINE,
+                                                       prepared.as<float>());
+  XVEC_LAUNCHED();
+  // Nearest centroid (L2, or IP for IP and cosine), ties to the lower index.
+  extern xvec_gpu_status rabitq_assign(xvec_gpu_index*, const float*, int64_t, int32_t*,
+                                       cudaStream_t);
+  if ((st = rabitq_assign(idx, prepared.as<float>(), m, labels.as<int32_t>(), s))) return st;
+  rabitq_encode_kernel<<<(unsigned)m, 256, padded * 4, s>>>(
+      prepared.as<float>(), m, d, padded, truncated, idx->rq_signs.as<uint8_t>(), inv,
+      idx->rq_rot_centroids.as<float>(), labels.as<int32_t>(), metric != XVEC_METRIC_L2,
+      idx->rq_codes.as<uint8_t>() + old_n * (padded / 8),
+      idx->rq_factors.as<RaBitQFactors>() + old_n, idx->rq_fast.as<float4>() + old_n,
+      bounds.as<unsigned>(), err.as<int>());
+  XVEC_LAUNCHED();
+  XVEC_CUDA(cudaGetLastError());
+  int h = 0;
+  XVEC_CUDA(cudaMemcpyAsync(&h, err.ptr, 4, cudaMemcpyDeviceToHost, s));
+  XVEC_CUDA(cudaStreamSynchronize(s));
+  if (h) return set_error("core: invalid RaBitQ code (status %d)", h), (xvec_gpu_status)h;
+  XVEC_CUDA(cudaMemcpyAsync(idx->rq_bounds.ptr, bounds.ptr, 16, cudaMemcpyDeviceToDevice, s));
+  return XVEC_GPU_OK;
+}
+
+xvec_gpu_status rabitq_assign(xvec_gpu_index* idx, const float* prepared, int64_t m,
+                              int32_t* labels, cudaStream_t s) {
+  xvec_gpu_search_opts o{};
+  o.top_k = 1;
+  Scratch keys, scores, counts;
+  xvec_gpu_status st;
+  const int64_t batch = std::min<int64_t>(m, 65536);
+  if ((st = keys.alloc((size_t)batch * 8, s)) || (st = scores.alloc((size_t)batch * 4, s)) ||
+      (st = counts.alloc((size_t)batch * 4, s)))
+    return st;
+  const int d = idx->desc.dimension;
+  for (int64_t b = 0; b < m; b += batch) {
+    const int cnt = (int)std::min<int64_t>(batch, m - b);
+    std::vector<int> statuses;
+    st = search_device_locked(idx->probe_index, prepared + b * d, cnt, o, nullptr,
+                              keys.as<uint64_t>(), scores.as<float>(), counts.as<int>(), s,
+                              &statuses);
+    if (st) return st;
+    std::vector<uint64_t> hk(cnt);
+    XVEC_CUDA(cudaMemcpyAsync(hk.data(), keys.ptr, (size_t)cnt * 8, cudaMemcpyDeviceToHost, s));
+    XVEC_CUDA(cudaStreamSynchronize(s));
+    std::vector<int32_t> hl(cnt);
+    for (int i = 0; i < cnt; ++i) {
+      if (statuses[i]) return set_error("assign row: status %d", statuses[i]), (xvec_gpu_status)statuses[i];
+      hl[i] = (int32_t)hk[i];
+    }
+    XVEC_CUDA(cudaMemcpyAsync(labels + b, hl.data(), (size_t)cnt * 4, cudaMemcpyHostToDevice, s));
+    XVEC_CUDA(cudaStreamSynchronize(s));
+  }
+  return XVEC_GPU_OK;
+}
+
+xvec_gpu_status rabitq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
+                                   const xvec_gpu_search_opts& o, const uint32_t* d_bitmap,
+                                   uint64_t* d_keys, float* d_scores, int* d_counts,
+                                   cudaStream_t s, std::vector<int>* statuses) {
+  // hnsw_rabitq.go:548-550, 573-579.
+  if (o.ef <= 0 || o.ef > 2048)
+    return set_error("core: invalid HNSW ef %d (want 1..2048)", o.ef), XVEC_GPU_INVALID_ARGUMENT;
+  if (!idx->has_model) return set_error("RaBitQ index has no model"), XVEC_GPU_INVALID_ARGUMENT;
+  const int d = idx->desc.dimension, padded = idx->padded, metric = idx->desc.metric;
+  const int nc = idx->rq_clusters;
+  const int64_t n = idx->n;
+  const int k = o.top_k;
+  const bool refine = o.refine != 0;
+  const int cc = refine ? (int)std::min<int64_t>(std::max<int64_t>(n, 1), std::max(k, o.ef)) : k;
+  const int kp = rabitq_kp(cc);
+  if (exact_cap_for(kp) > 8192)
+    return set_error("top_k %d exceeds the supported maximum for RaBitQ", k),
+           XVEC_GPU_INVALID_ARGUMENT;
+  const int truncated = floor_pow2(d);
+  const float inv = inv_sqrt_size(truncated);
+  xvec_gpu_status st;
+  Scratch qrot, qsum, gadd, gerr, qfs, qfg, qeps, qexact, qstatus, qflags;
+  if ((st = qrot.alloc((size_t)nq * padded * 4, s)) || (st = qsum.alloc((size_t)nq * 8, s)) ||
+      (st = gadd.alloc((size_t)nq * nc * 8, s)) || (st = gerr.alloc((size_t)nq * nc * 8, s)) ||
+      (st = qfs.alloc((size_t)nq * 4, s)) || (st = qfg.alloc((size_t)nq * nc * 4, s)) ||
+      (st = qeps.alloc((size_t)nq * 4, s)) || (st = qexact.alloc((size_t)nq * 4, s)) ||
+      (st = qstatus.alloc((size_t)nq * 4, s)) || (st = qflags.alloc((size_t)nq * 4, s)))
+    return st;
+  XVEC_CUDA(cudaMemsetAsync(qflags.ptr, 0, (size_t)nq * 4, s));
+  rabitq_prep_query_kernel<<<nq, 256, padded * 4, s>>>(
+      d_q, nq, d, padded, truncated, idx->rq_signs.as<uint8_t>(), inv,
+      metric == XVEC_METRIC_COSINE, metric, idx->rq_rot_centroids.as<float>(), nc,
+      idx->rq_bounds.as<unsigned>(), qrot.as<float>(), qsum.as<double>(), gadd.as<double>(),
+      gerr.as<double>(), qfs.as<float>(), qfg.as<float>(), qeps.as<float>(), qexact.as<int>(),
+      qstatus.as<int>(), qflags.as<int>());
+  XVEC_LAUNCHED();
+  // The approximate stage writes the final results, or the candidates of the
+  // refine stage (no radius there: hnsw_rabitq.go:584).
+  Scratch skeys, sscores, scounts, spos;
+  if ((st = skeys.alloc((size_t)nq * cc * 8, s)) || (st = sscores.alloc((size_t)nq * cc * 4, s)) ||
+      (st = scounts.alloc((size_t)nq * 4, s)) || (st = spos.alloc((size_t)nq * cc * 4, s)))
+    return st;
+  uint64_t* o_keys = refine ? skeys.as<uint64_t>() : d_keys;
+  float* o_scores = refine ? sscores.as<float>() : d_scores;
+  int* o_counts = refine ? scounts.as<int>() : d_counts;
+  XVEC_CUDA(cudaMemsetAsync(o_counts, 0, (size_t)nq * 4, s));
+  const RaBitQScorer sc{kMetricL2,        metric,           idx->rq_codes.as<uint8_t>(),
+                        idx->rq_factors.as<RaBitQFactors>(), qrot.as<float>(),
+                        qsum.as<double>(), gadd.as<double>(), gerr.as<double>(),
+                        qeps.as<float>(), qexact.as<int>(), padded, nc};
+  const float stage_radius = refine ? 0.f : o.radius;
+  const bool fast = n > 0 && simt_cap_for(kp) <= 512;
+  if (fast) {
+    const int qtiles = (nq + 31) / 32;
+    int parts = (int)std::max<int64_t>(
+        1, std::min<int64_t>((592 + qtiles - 1) / qtiles, (n + 1023) / 1024));
+    parts = std::min(parts, std::max(1, flat_merge_capacity() / kp));
+    Scratch pkeys, pcounts, psat;
+    if ((st = pkeys.alloc((size_t)nq * parts * kp * 8, s)) ||
+        (st = pcounts.alloc((size_t)nq * parts * 4, s)) ||
+        (st = psat.alloc((size_t)nq * parts * 8, s)))
+      return st;
+    const RaBitQRanker rk{idx->rq_fast.as<float4>(), qfs.as<float>(), qfg.as<float>(), nc};
+    XVEC_CUDA(launch_scan_simt(reinterpret_cast<const BitElem*>(idx->rq_codes.ptr), n, padded,
+                               idx->keyrank.as<uint32_t>(), qrot.as<float>(), nq, d_bitmap, rk,
+                               parts, kp, pkeys.as<uint64_t>(), pcounts.as<int>(),
+                               psat.as<uint64_t>(), qflags.as<int>(), s));
+    XVEC_CUDA(launch_merge_rescore(sc, idx->pos_of_kr.as<uint32_t>(), idx->keys.as<uint64_t>(),
+                                   nullptr, nq, cc, stage_radius, 0, pkeys.as<uint64_t>(),
+                                   pcounts.as<int>(), psat.as<uint64_t>(), parts, kp, o_keys,
+                                   o_scores, o_counts, spos.as<uint32_t>(), qflags.as<int>(), s));
+    count_launches(2);
+  }
+  std::vector<int> h_status(nq), h_flags(nq);
+  XVEC_CUDA(cudaMemcpyAsync(h_status.data(), qstatus.ptr, (size_t)nq * 4, cudaMemcpyDeviceToHost, s));
+  XVEC_CUDA(cudaMemcpyAsync(h_flags.data(), qflags.ptr, (size_t)nq * 4, cudaMemcpyDeviceToHost, s));
+  XVEC_CUDA(cudaStreamSynchronize(s));
+  // Exact pass: queries the fast pass could not settle, every query when the
+  // candidate count is beyond the fast accumulators, and queries whose
+  // estimates may fail (scanRaBitQCodes stops at the first failing row,
+  // filtered or not, so those are first scored over every row).
+  std::vector<int> exact_list, check_list;
+  if (n > 0)
+    for (int q = 0; q < nq; ++q) {
+      if (h_status[q] != 0) continue;
+      if (!fast || (h_flags[q] & 3)) exact_list.push_back(q);
+      if ((h_flags[q] & kRaBitQFullCheck) && d_bitmap) check_list.push_back(q);
+    }
+  auto exact_pass = [&](const std::vector<int>& list, const uint32_t* bitmap,
+                        bool write) -> xvec_gpu_status {
+    const int nl = (int)list.size();
+    int parts = (int)std::max<int64_t>(1, std::min<int64_t>((592 + nl - 1) / nl, (n + 1023) / 1024));
+    parts = std::min(parts, std::max(1, flat_merge_capacity() / kp));
+    Scratch ids, pkeys, pcounts, psat, dk, ds, dc, dp;
+    xvec_gpu_status e;
+    if ((e = ids.alloc((size_t)nl * 4, s)) || (e = pkeys.alloc((size_t)nl * parts * kp * 8, s)) ||
+        (e = pcounts.alloc((size_t)nl * parts * 4, s)) ||
+        (e = psat.alloc((size_t)nl * parts * 8, s)))
+      return e;
+    XVEC_CUDA(cudaMemcpyAsync(ids.ptr, list.data(), (size_t)nl * 4, cudaMemcpyHostToDevice, s));
+    rabitq_clear_flags<<<blocks_of(nl), 256, 0, s>>>(ids.as<int>(), nl, qflags.as<int>());
+    XVEC_CUDA(launch_scan_exact(sc, n, idx->keyrank.as<uint32_t>(), ids.as<int>(), nl, bitmap,
+                                parts, kp, pkeys.as<uint64_t>(), pcounts.as<int>(),
+                                psat.as<uint64_t>(), qflags.as<int>(), s));
+    count_launches(2);
+    if (!write) return XVEC_GPU_OK;
+    XVEC_CUDA(launch_merge_rescore(sc, idx->pos_of_kr.as<uint32_t>(), idx->keys.as<uint64_t>(),
+                                   ids.as<int>(), nl, cc, stage_radius, 1, pkeys.as<uint64_t>(),
+                                   pcounts.as<int>(), psat.as<uint64_t>(), parts, kp, o_keys,
+                                   o_scores, o_counts, spos.as<uint32_t>(), qflags.as<int>(), s));
+    XVEC_LAUNCHED();
+    XVEC_CUDA(cudaMemcpyAsync(h_flags.data(), qflags.ptr, (size_t)nq * 4, cudaMemcpyDeviceToHost, s));
+    XVEC_CUDA(cudaStreamSynchronize(s));
+    for (int q : list)
+      if (h_flags[q] & 2)
+        return set_error("exact scan could not complete query %d", q), XVEC_GPU_CUDA_ERROR;
+    return XVEC_GPU_OK;
+  };
+  if (!check_list.empty() && (st = exact_pass(check_list, nullptr, false))) return st;
+  if (!exact_list.empty() && (st = exact_pass(exact_list, d_bitmap, true))) return st;
+
+  Scratch rstatus;
+  if (refine) {
+    // refinePrepared (hnsw_rabitq.go:780-801) -> topKCandidatesWithOptions:
+    // metric.Compute(q, q) on the raw query first (topk.go:92-94).
+    Scratch qf, qn2, qaux;
+    if ((st = rstatus.alloc((size_t)nq * 4, s)) || (st = qf.alloc((size_t)nq * d * 4, s)) ||
+        (st = qn2.alloc((size_t)nq * 4, s)) || (st = qaux.alloc((size_t)nq * 4, s)))
+      return st;
+    launch_prep_queries<float>(d_q, nq, d, metric, qf.as<float>(), qn2.as<float>(),
+                               qaux.as<float>(), rstatus.as<int>(), s);
+    XVEC_LAUNCHED();
+    rabitq_status_kernel<<<blocks_of(nq), 256, 0, s>>>(qstatus.as<int>(), qflags.as<int>(),
+                                                       rstatus.as<int>(), nq, o_counts);
+    XVEC_CUDA(cudaMemsetAsync(d_counts, 0, (size_t)nq * 4, s));
+    if (n > 0) {
+      XVEC_CUDA(launch_refine(idx->rows.as<float>(), d, metric, d_q, nq, spos.as<uint32_t>(),
+                              o_counts, cc, idx->keyrank.as<uint32_t>(),
+                              idx->pos_of_kr.as<uint32_t>(), idx->keys.as<uint64_t>(), k,
+                              o.radius, d_keys, d_scores, d_counts, qflags.as<int>(), s));
+      count_launches(2);
+    }
+  }
+  const int* rs = (refine && n > 0) ? rstatus.as<int>() : nullptr;
+  rabitq_status_kernel<<<blocks_of(nq), 256, 0, s>>>(qstatus.as<int>(), qflags.as<int>(), rs, nq,
+                                                     d_counts);
+  XVEC_LAUNCHED();
+  XVEC_CUDA(cudaGetLastError());
+  std::vector<int> h_rs(nq, 0);
+  XVEC_CUDA(cudaMemcpyAsync(h_flags.data(), qflags.ptr, (size_t)nq * 4, cudaMemcpyDeviceToHost, s));
+  if (rs) XVEC_CUDA(cudaMemcpyAsync(h_rs.data(), rs, (size_t)nq * 4, cudaMemcpyDeviceToHost, s));
+  XVEC_CUDA(cudaStreamSynchronize(s));
+  count_search(nq, (int64_t)exact_list.size(), 0, 0);
+  if (statuses) {
+    statuses->resize(nq);
+    for (int q = 0; q < nq; ++q) (*statuses)[q] = rabitq_query_status(h_status[q], h_flags[q], h_rs[q]);
+  }
+  return XVEC_GPU_OK;
+}
+
+}  // namespace xvec
+
+using namespace xvec;
+
+extern "C" xvec_gpu_status xvec_gpu_rabitq_set_model(xvec_gpu_index* idx, const float* centroids,
+                                                     int32_t nclusters,
+                                                     const uint8_t* rotation_signs) {
+  if (!idx || !centroids || !rotation_signs) return set_error("nil argument"), XVEC_GPU_INVALID_ARGUMENT;
+  if (idx->desc.kind != XVEC_INDEX_RABITQ) return set_error("not a RaBitQ index"), XVEC_GPU_INVALID_ARGUMENT;
+  if (nclusters <= 0) return set_error("core: invalid RaBitQ model: no centroids"), XVEC_GPU_INVALID_ARGUMENT;
+  const int d = idx->desc.dimension, padded = idx->padded;
+  std::unique_lock<std::shared_mutex> lock(idx->mu);
+  if (idx->n > 0) return set_error("set the model before adding rows"), XVEC_GPU_INVALID_ARGUMENT;
+  for (int64_t i = 0; i < (int64_t)nclusters * d; ++i)
+    if (!std::isfinite(centroids[i])) return set_error("non-finite centroid"), XVEC_GPU_NON_FINITE;
+  cudaSetDevice(idx->device);
+  cudaStream_t s = nullptr;
+  xvec_gpu_status st;
+  const size_t sign_bytes = (size_t)4 * padded / 8;
+  if ((st = idx->rq_centroids.reserve((size_t)nclusters * d * 4, 0, s)) ||
+      (st = idx->rq_rot_centroids.reserve((size_t)nclusters * padded * 4, 0, s)) ||
+      (st = idx->rq_signs.reserve(sign_bytes, 0, s)))
+    return st;
+  // The bound maxima start at zero: a search of an empty index reads them.
+  if (!idx->rq_bounds.ptr) {
+    if ((st = idx->rq_bounds.reserve(16, 0, s))) return st;
+    XVEC_CUDA(cudaMemset(idx->rq_bounds.ptr, 0, 16));
+  }
+  XVEC_CUDA(cudaMemcpy(idx->rq_centroids.ptr, centroids, (size_t)nclusters * d * 4,
+                       cudaMemcpyHostToDevice));
+  XVEC_CUDA(cudaMemcpy(idx->rq_signs.ptr, rotation_signs, sign_bytes, cudaMemcpyHostToDevice));
+  Scratch err;
+  if ((st = err.alloc(4, s))) return st;
+  XVEC_CUDA(cudaMemsetAsync(err.ptr, 0, 4, s));
+  const int truncated = floor_pow2(d);
+  rabitq_rotate_centroids_kernel<<<nclusters, 256, padded * 4, s>>>(
+      idx->rq_centroids.as<float>(), d, padded, truncated, idx->rq_signs.as<uint8_t>(),
+      inv_sqrt_size(truncated), idx->rq_rot_centroids.as<float>(), err.as<int>());
+  XVEC_CUDA(cudaGetLastError());
+  int h = 0;
+  XVEC_CUDA(cudaMemcpy(&h, err.ptr, 4, cudaMemcpyDeviceToHost));
+  if (h) return set_error("core: invalid RaBitQ model: rotated centroid is not finite"), XVEC_GPU_NON_FINITE;
+  // Nearest-centroid index: L2 for L2, IP for IP and cosine (rabitq.go:309-313).
+  if (idx->probe_index) {
+    xvec_gpu_index_destroy(idx->probe_index);
+    idx->probe_index = nullptr;
+  }
+  xvec_gpu_index_desc desc{};
+  desc.kind = XVEC_INDEX_FLAT;
+  desc.dimension = d;
+  desc.metric = idx->desc.metric == XVEC_METRIC_L2 ? XVEC_METRIC_L2 : XVEC_METRIC_IP;
+  desc.storage = XVEC_STORAGE_FP32;
+  desc.device = idx->device;
+  if ((st = xvec_gpu_index_create(&desc, &idx->probe_index))) return st;
+  std::vector<uint64_t> ids(nclusters);
+  for (int i = 0; i < nclusters; ++i) ids[i] = (uint64_t)i;
+  Scratch dk;
+  if ((st = dk.alloc((size_t)nclusters * 8, s))) return st;
+  XVEC_CUDA(cudaMemcpy(dk.ptr, ids.data(), (size_t)nclusters * 8, cudaMemcpyHostToDevice));
+  if ((st = add_device_locked(idx->probe_index, dk.as<uint64_t>(), idx->rq_centroids.ptr,
+                              nclusters, s)))
+    return st;
+  idx->rq_clusters = nclusters;
+  idx->has_model = true;
+  return XVEC_GPU_OK;
+}

@@ -12,10 +12,12 @@
 
 namespace xvec {
 
-constexpr int kRefineMax = 1024;  // candidates per query
+constexpr int kRefineMax = 2048;  // candidates per query (MaxHNSWEFSearch)
 
-// One block (256 threads) per query.  stage_pos/stage_counts: per query the
-// positions of the approximate stage's results (stride `stage_k`).
+// One block (256 threads) per query; N >= the candidate count, a power of two.
+// stage_pos/stage_counts: per query the positions of the approximate stage's
+// results (stride `stage_k`).
+template <int N>
 __global__ void __launch_bounds__(256) refine_kernel(
     const float* __restrict__ rows, int d, int metric, const float* __restrict__ queries,
     const uint32_t* __restrict__ stage_pos, const int* __restrict__ stage_counts, int stage_k,
@@ -23,14 +25,14 @@ __global__ void __launch_bounds__(256) refine_kernel(
     const uint64_t* __restrict__ keys, int k, float radius,
     uint64_t* __restrict__ out_keys, float* __restrict__ out_scores, int* __restrict__ out_counts,
     int* __restrict__ q_flags) {
-  __shared__ uint64_t cand[kRefineMax];
+  __shared__ uint64_t cand[N];
   const int qi = blockIdx.x;
   const int c = stage_counts[qi];
   if (c <= 0) {
     if (threadIdx.x == 0 && c == 0) out_counts[qi] = 0;
     return;
   }
-  const int n = min(c, kRefineMax);
+  const int n = min(c, N);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float* q = queries + (int64_t)qi * d;
   for (int i = warp; i < n; i += blockDim.x >> 5) {
@@ -43,7 +45,7 @@ __global__ void __launch_bounds__(256) refine_kernel(
   }
   __syncthreads();
   // (rank, key rank) ascending is the reference order.
-  block_sort_u64<kRefineMax>(cand, n);
+  block_sort_u64<N>(cand, n);
   if (threadIdx.x < 32) {
     int count = 0;
     for (int base = 0; base < n && count < k; base += 32) {
@@ -66,6 +68,30 @@ __global__ void __launch_bounds__(256) refine_kernel(
     }
     if (lane == 0) out_counts[qi] = count;
   }
+}
+
+// Launches refine_kernel with the smallest shared buffer that holds
+// `stage_k` (<= kRefineMax) candidates.
+inline cudaError_t launch_refine(const float* rows, int d, int metric, const float* queries,
+                                 int nq, const uint32_t* stage_pos, const int* stage_counts,
+                                 int stage_k, const uint32_t* keyrank,
+                                 const uint32_t* pos_of_keyrank, const uint64_t* keys, int k,
+                                 float radius, uint64_t* out_keys, float* out_scores,
+                                 int* out_counts, int* q_flags, cudaStream_t s) {
+  if (nq <= 0) return cudaSuccess;
+#define XVEC_REFINE_CASE(NN)                                                                  \
+  if (stage_k <= NN) {                                                                        \
+    refine_kernel<NN><<<nq, 256, 0, s>>>(rows, d, metric, queries, stage_pos, stage_counts,   \
+                                         stage_k, keyrank, pos_of_keyrank, keys, k, radius,   \
+                                         out_keys, out_scores, out_counts, q_flags);          \
+    return cudaGetLastError();                                                                \
+  }
+  XVEC_REFINE_CASE(128)
+  XVEC_REFINE_CASE(512)
+  XVEC_REFINE_CASE(1024)
+  XVEC_REFINE_CASE(2048)
+#undef XVEC_REFINE_CASE
+  return cudaErrorInvalidValue;
 }
 
 }  // namespace xvec

@@ -90,6 +90,15 @@ __device__ __forceinline__ void warp_compact(uint64_t* buf, AccumState* st, int 
   __syncwarp();
 }
 
+// block_sort_u64 over the smallest power of two >= n (at least 64, at most N).
+template <int N>
+__device__ __forceinline__ void block_sort_u64_fit(uint64_t* a, int n) {
+  if (N >= 64 && n <= 64) return block_sort_u64<(N < 64 ? N : 64)>(a, n);
+  if (N >= 256 && n <= 256) return block_sort_u64<(N < 256 ? N : 256)>(a, n);
+  if (N >= 1024 && n <= 1024) return block_sort_u64<(N < 1024 ? N : 1024)>(a, n);
+  block_sort_u64<N>(a, n);
+}
+
 // Block-wide radix select: the kth smallest (1-based) of the keys produced by
 // `get(i)` for i in [0, m).  Requires 1 <= kth <= m.  Uses 256 ints of shared
 // scratch `hist` and two shared ints.

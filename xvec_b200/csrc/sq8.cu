@@ -250,6 +250,8 @@ struct SQ8Scorer {
   }
   __device__ float eps(int qi) const { return q_eps[qi]; }
   __device__ int error_flag(float) const { return 4; }
+  __device__ float output(float r) const { return score_from_rank(metric, r); }
+  __device__ bool keep(float out, float radius) const { return within_radius(metric, out, radius); }
 };
 
 __global__ void sq8_status_kernel(const int* q_status, const int* q_flags, int nq,
@@ -447,13 +449,11 @@ xvec_gpu_status sq8_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
     sq8_status_kernel<<<blocks_of(nq), 256, 0, s>>>(qstatus.as<int>(), qflags.as<int>(), nq,
                                                     o_counts);
     XVEC_CUDA(cudaMemsetAsync(d_counts, 0, (size_t)nq * 4, s));
-    refine_kernel<<<nq, 256, 0, s>>>(idx->rows.as<float>(), d, metric, d_q, spos.as<uint32_t>(),
-                                     o_counts, stage_k, idx->keyrank.as<uint32_t>(),
-                                     idx->pos_of_kr.as<uint32_t>(), idx->keys.as<uint64_t>(),
-                                     o.top_k, o.radius, d_keys, d_scores, d_counts,
-                                     qflags.as<int>());
+    XVEC_CUDA(launch_refine(idx->rows.as<float>(), d, metric, d_q, nq, spos.as<uint32_t>(),
+                            o_counts, stage_k, idx->keyrank.as<uint32_t>(),
+                            idx->pos_of_kr.as<uint32_t>(), idx->keys.as<uint64_t>(), o.top_k,
+                            o.radius, d_keys, d_scores, d_counts, qflags.as<int>(), s));
     count_launches(2);
-    XVEC_CUDA(cudaGetLastError());
   } else if (refine) {
     XVEC_CUDA(cudaMemsetAsync(d_counts, 0, (size_t)nq * 4, s));
   }
