@@ -63,6 +63,26 @@ def test_tc_dims_and_ragged_rows(oracle, xb, d):
     run(oracle, xb, COSINE, rows, queries, keys, 10)
 
 
+@pytest.mark.parametrize("metric", [COSINE, L2])
+def test_tc_seeded_threshold(oracle, xb, metric):
+    """Bases of 64k rows and more are scanned in two launches: a prefix whose
+    lists seed every query's shared threshold, then the rest.  A filter whose
+    words straddle the split and duplicate rows on both sides of it."""
+    rng = np.random.default_rng(70 + metric)
+    n = 70_000
+    rows = mixture(rng, n, 128, normalise=metric == COSINE)
+    rows[4300:4400] = rows[100:200]           # duplicates across the prefix boundary
+    keys = rng.permutation(1 << 22)[:n].astype(np.uint64)
+    queries = mixture(rng, 260, 128, normalise=metric == COSINE)
+    queries[:5] = rows[[3, 4200, 4400, 50000, 69999]]
+    run(oracle, xb, metric, rows, queries, keys, 100)
+    bitmap = np.zeros((n + 31) // 32, np.uint32)
+    for p in range(n):
+        if (p * 13) % 7 != 0:
+            bitmap[p >> 5] |= np.uint32(1 << (p & 31))
+    run(oracle, xb, metric, rows, queries, keys, 20, bitmap=bitmap)
+
+
 def test_tc_filter_radius_duplicates(oracle, xb):
     rng = np.random.default_rng(9)
     base = mixture(rng, 1500, 128)

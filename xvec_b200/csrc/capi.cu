@@ -227,23 +227,39 @@ xvec_gpu_status flat_search_impl(xvec_gpu_index* idx, const void* d_q, int nq,
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, idx->device);
     const int qblocks = (nq + 127) / 128;
-    // The merge gathers every list of a query in shared memory.
-    const int64_t merge_cap = flat_merge_capacity() / (kp * flat_tc_lists_per_part());
-    const int64_t max_parts =
-        std::max<int64_t>(1, std::min<int64_t>(std::min<int64_t>(64, merge_cap), n / (256 * 16)));
-    int parts = 1;
-    double best = -1;
-    for (int p = 1; p <= max_parts; ++p) {
-      const int64_t ctas = (int64_t)qblocks * p;
-      const int64_t waves = (ctas + sms - 1) / sms;
-      const double eff = (double)ctas / (double)(waves * sms);
-      if (eff > best + 1e-9) {
-        best = eff;
-        parts = p;
+    auto best_parts = [&](int64_t max_parts) {
+      int parts = 1;
+      double best = -1;
+      for (int p = 1; p <= max_parts; ++p) {
+        const int64_t ctas = (int64_t)qblocks * p;
+        const int64_t waves = (ctas + sms - 1) / sms;
+        const double eff = (double)ctas / (double)(waves * sms);
+        if (eff > best + 1e-9) {
+          best = eff;
+          parts = p;
+        }
       }
+      return parts;
+    };
+    const int lpp = flat_tc_lists_per_part();
+    // The merge gathers every list of a query in shared memory.
+    const int64_t merge_lists = flat_merge_capacity() / kp;
+    // Seeding: a first launch scans a prefix of the rows; the kp-th best key
+    // of each query over all lists of that launch then becomes the shared
+    // threshold of the second launch's lists, which therefore start filtering
+    // at once instead of each filling kp entries on its own.
+    int64_t seed_rows = 0;
+    int seed_parts = 0;
+    if (n >= (int64_t)1 << 16) {
+      seed_rows = n / 16 / 256 * 256;
+      seed_parts = best_parts(std::max<int64_t>(
+          1, std::min<int64_t>(std::min<int64_t>(16, merge_lists / (2 * lpp)), seed_rows / 4096)));
     }
+    const int64_t rest = n - seed_rows;
+    const int parts = best_parts(std::max<int64_t>(
+        1, std::min<int64_t>(std::min<int64_t>(64, merge_lists / lpp - seed_parts), rest / 4096)));
     const int cap = flat_tc_cap();
-    const int lists = parts * flat_tc_lists_per_part();
+    const int lists = (seed_parts + parts) * lpp;
     Scratch pkeys, pcounts, psat, gthr;
     if ((st = pkeys.alloc((size_t)nq * lists * cap * 8, s)) ||
         (st = pcounts.alloc((size_t)nq * lists * 4, s)) ||
@@ -252,12 +268,26 @@ xvec_gpu_status flat_search_impl(xvec_gpu_index* idx, const void* d_q, int nq,
     XVEC_CUDA(cudaMemsetAsync(gthr.ptr, 0xff, (size_t)nq * 8, s));
     const float* row_aux =
         metric == XVEC_METRIC_COSINE ? idx->row_inv.as<float>() : idx->row_n2.as<float>();
+    const __half* hrows = reinterpret_cast<const __half*>(rows);
     timer.mark(1);
+    if (seed_parts > 0) {
+      XVEC_CUDA(launch_flat_scan_tc(metric, static_cast<const __half*>(d_q), nq, hrows, seed_rows,
+                                    d, d, row_aux, idx->keyrank.as<uint32_t>(), qaux.as<float>(),
+                                    qn2.as<float>(), gthr.as<unsigned long long>(), d_bitmap,
+                                    seed_parts, kp, 0, lists, pkeys.as<uint64_t>(),
+                                    pcounts.as<int>(), psat.as<uint64_t>(), qflags.as<int>(),
+                                    kstatus.as<int>(), s));
+      XVEC_CUDA(launch_seed_thresholds(pkeys.as<uint64_t>(), pcounts.as<int>(), nq, lists,
+                                       seed_parts * lpp, cap, kp, gthr.as<unsigned long long>(),
+                                       s));
+      count_launches(2);
+    }
     XVEC_CUDA(launch_flat_scan_tc(metric, static_cast<const __half*>(d_q), nq,
-                                  reinterpret_cast<const __half*>(rows), n, d, d, row_aux,
-                                  idx->keyrank.as<uint32_t>(), qaux.as<float>(), qn2.as<float>(),
-                                  gthr.as<unsigned long long>(), d_bitmap, parts, kp,
-                                  pkeys.as<uint64_t>(),
+                                  hrows + seed_rows * d, rest, d, d, row_aux + seed_rows,
+                                  idx->keyrank.as<uint32_t>() + seed_rows, qaux.as<float>(),
+                                  qn2.as<float>(), gthr.as<unsigned long long>(),
+                                  d_bitmap ? d_bitmap + seed_rows / 32 : nullptr, parts, kp,
+                                  seed_parts * lpp, lists, pkeys.as<uint64_t>(),
                                   pcounts.as<int>(), psat.as<uint64_t>(), qflags.as<int>(),
                                   kstatus.as<int>(), s));
     timer.mark(2);

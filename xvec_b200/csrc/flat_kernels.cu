@@ -216,6 +216,49 @@ template void launch_row_norms<__half>(const __half*, int64_t, int, float*, floa
 
 int flat_merge_capacity() { return kMergeSmemEntries; }
 
+// One block per query: gather the seed lists, radix-select the kp-th key.
+__global__ void __launch_bounds__(256) seed_thresholds_kernel(
+    const uint64_t* __restrict__ cand, const int* __restrict__ counts, int num_lists,
+    int seed_lists, int cap, int kp, unsigned long long* __restrict__ gthr) {
+  extern __shared__ __align__(16) unsigned char seed_smem[];
+  uint64_t* keys = reinterpret_cast<uint64_t*>(seed_smem);
+  __shared__ int hist[256];
+  __shared__ int offs[65];
+  const int q = blockIdx.x;
+  if (threadIdx.x == 0) {
+    int total = 0;
+    for (int l = 0; l < seed_lists; ++l) {
+      offs[l] = total;
+      total += min(counts[(int64_t)q * num_lists + l], kp);
+    }
+    offs[seed_lists] = total;
+  }
+  __syncthreads();
+  const int total = offs[seed_lists];
+  if (total < kp) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int l = warp; l < seed_lists; l += blockDim.x >> 5) {
+    const uint64_t* src = cand + ((int64_t)q * num_lists + l) * cap;
+    const int c = offs[l + 1] - offs[l];
+    for (int j = lane; j < c; j += 32) keys[offs[l] + j] = src[j];
+  }
+  __syncthreads();
+  const uint64_t kth = smem_radix_select(keys, total, kp, 0, hist);
+  if (threadIdx.x == 0) atomicMin(&gthr[q], (unsigned long long)kth);
+}
+
+cudaError_t launch_seed_thresholds(const uint64_t* cand, const int* counts, int nq, int num_lists,
+                                   int seed_lists, int cap, int kp, unsigned long long* gthr,
+                                   cudaStream_t stream) {
+  if (nq <= 0 || seed_lists <= 0) return cudaSuccess;
+  if (seed_lists > 64 || seed_lists * kp > kMergeSmemEntries) return cudaErrorInvalidValue;
+  const int smem = seed_lists * kp * 8;
+  cudaFuncSetAttribute(seed_thresholds_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  seed_thresholds_kernel<<<nq, 256, smem, stream>>>(cand, counts, num_lists, seed_lists, cap, kp,
+                                                    gthr);
+  return cudaGetLastError();
+}
+
 int simt_cap_for(int kp) {
   // CAP must hold KP retained entries plus two tiles of appends.
   int need = kp + 2 * kSimtRT;

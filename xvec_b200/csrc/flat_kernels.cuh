@@ -19,6 +19,15 @@ void launch_row_norms(const RowT* rows, int64_t n, int d, float* n2, float* inv_
 int simt_cap_for(int kp);
 // Union entries per query the merge kernel can hold (parts x kp must fit).
 int flat_merge_capacity();
+
+// Per query, lowers gthr[q] to the kp-th smallest key over lists
+// [0, seed_lists) (cand: [nq][num_lists][cap], counts: [nq][num_lists]) when
+// those lists hold at least kp keys together.  Any kp keys of the query bound
+// its final kp-th best from above, so the result is a valid shared threshold
+// for the lists filled afterwards.  seed_lists * kp <= flat_merge_capacity().
+cudaError_t launch_seed_thresholds(const uint64_t* cand, const int* counts, int nq, int num_lists,
+                                   int seed_lists, int cap, int kp, unsigned long long* gthr,
+                                   cudaStream_t stream);
 int exact_cap_for(int kp);
 
 template <typename RowT>

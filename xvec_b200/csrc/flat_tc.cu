@@ -267,8 +267,9 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
     int64_t n, int d, const float* __restrict__ row_aux, const uint32_t* __restrict__ keyrank,
     const float* __restrict__ q_aux, const float* __restrict__ q_n2,
     unsigned long long* __restrict__ gthr, const uint32_t* __restrict__ bitmap,
-    int64_t rows_per_part, int kp, uint64_t* __restrict__ cand, int* __restrict__ part_counts,
-    uint64_t* __restrict__ part_sat, int* __restrict__ q_flags, int* __restrict__ status) {
+    int64_t rows_per_part, int kp, int list_base, int num_lists, uint64_t* __restrict__ cand,
+    int* __restrict__ part_counts, uint64_t* __restrict__ part_sat, int* __restrict__ q_flags,
+    int* __restrict__ status) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   unsigned char* tiles = smem;  // kStages x (A | B)
@@ -410,8 +411,7 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
     float tq = score_bound<METRIC>(thr_f, qa, qn2);
     int cnt = 0;
     int nonfinite = 0;
-    const int list = part * 2 + half;
-    const int num_lists = num_parts * 2;
+    const int list = list_base + part * 2 + half;
     uint64_t* gbuf = cand + ((int64_t)(qvalid ? qi : 0) * num_lists + list) * kCap;
     int* hist = hist_all + ew * 256;
     float* meta_aux = reinterpret_cast<float*>(meta_all + ew * 256);  // [128]
@@ -611,8 +611,9 @@ cudaError_t launch_flat_scan_tc(int metric, const __half* queries, int nq, const
                                 int64_t n, int d, int64_t row_stride_elems, const float* row_aux,
                                 const uint32_t* keyrank, const float* q_aux, const float* q_n2,
                                 unsigned long long* gthr, const uint32_t* bitmap, int num_parts,
-                                int kp, uint64_t* cand, int* part_counts, uint64_t* part_sat,
-                                int* q_flags, int* status, cudaStream_t stream) {
+                                int kp, int list_base, int num_lists, uint64_t* cand,
+                                int* part_counts, uint64_t* part_sat, int* q_flags, int* status,
+                                cudaStream_t stream) {
   CUtensorMap qmap, rmap;
   if (!make_map(&qmap, queries, nq, d, d, tc::kBM) ||
       !make_map(&rmap, rows, n, d, row_stride_elems, tc::kBN))
@@ -625,8 +626,9 @@ cudaError_t launch_flat_scan_tc(int metric, const __half* queries, int nq, const
     auto kern = tc::flat_scan_tc_kernel<M>;                                                 \
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);         \
     kern<<<grid, tc::kThreads, smem, stream>>>(qmap, rmap, nq, n, d, row_aux, keyrank, q_aux, \
-                                               q_n2, gthr, bitmap, rows_per_part, kp, cand,   \
-                                               part_counts, part_sat, q_flags, status);      \
+                                               q_n2, gthr, bitmap, rows_per_part, kp,         \
+                                               list_base, num_lists, cand, part_counts,       \
+                                               part_sat, q_flags, status);                    \
     break;                                                                                  \
   }
   switch (metric) {

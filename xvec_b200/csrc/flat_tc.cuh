@@ -18,14 +18,17 @@ int flat_tc_lists_per_part();
 // Scans rows [0, n) (row i at rows + i * row_stride_elems) against nq queries.
 // row_aux: 1/||x|| for cosine, ||x||^2 for L2 / MIPS (unused for IP);
 // q_aux: 1/||q|| for cosine, ||q||^2 otherwise.  gthr: per-query key
-// thresholds shared by all lists of a query (initialise to all ones).
-// status != 0 after the launch = a bounded wait expired (the results are
-// then invalid).
+// thresholds shared by all lists of a query (initialise to all ones, or to
+// a bound already known).  The launch fills lists [list_base, list_base +
+// 2 * num_parts) of the num_lists lists each query has (cand: [nq][num_lists]
+// [cap] keys, part_counts / part_sat: [nq][num_lists]).  status != 0 after
+// the launch = a bounded wait expired (the results are then invalid).
 cudaError_t launch_flat_scan_tc(int metric, const __half* queries, int nq, const __half* rows,
                                 int64_t n, int d, int64_t row_stride_elems, const float* row_aux,
                                 const uint32_t* keyrank, const float* q_aux, const float* q_n2,
                                 unsigned long long* gthr, const uint32_t* bitmap, int num_parts,
-                                int kp, uint64_t* cand, int* part_counts, uint64_t* part_sat,
-                                int* q_flags, int* status, cudaStream_t stream);
+                                int kp, int list_base, int num_lists, uint64_t* cand,
+                                int* part_counts, uint64_t* part_sat, int* q_flags, int* status,
+                                cudaStream_t stream);
 
 }  // namespace xvec
