@@ -226,7 +226,8 @@ xvec_gpu_status flat_search_impl(xvec_gpu_index* idx, const void* d_q, int nq,
     // one CTA per SM, keeping at least 16 tiles of 256 rows per part.
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, idx->device);
-    const int qblocks = (nq + 127) / 128;
+    // Query blocks of 128; CTA pairs take them two at a time.
+    const int qblocks = flat_tc_pairs(nq) ? ((nq + 127) / 128 + 1) / 2 * 2 : (nq + 127) / 128;
     auto best_parts = [&](int64_t max_parts) {
       int parts = 1;
       double best = -1;
@@ -244,22 +245,33 @@ xvec_gpu_status flat_search_impl(xvec_gpu_index* idx, const void* d_q, int nq,
     const int lpp = flat_tc_lists_per_part();
     // The merge gathers every list of a query in shared memory.
     const int64_t merge_lists = flat_merge_capacity() / kp;
-    // Seeding: a first launch scans a prefix of the rows; the kp-th best key
-    // of each query over all lists of that launch then becomes the shared
-    // threshold of the second launch's lists, which therefore start filtering
-    // at once instead of each filling kp entries on its own.
-    int64_t seed_rows = 0;
-    int seed_parts = 0;
+    // Seeding: launches over growing prefixes of the rows (1/256, then up to
+    // 1/16); after each, the kp-th best key of every query over all lists
+    // so far lowers its shared threshold, so the lists of the next launch
+    // filter from their first tile instead of each collecting kp entries.
+    std::vector<int64_t> ends;  // row ends of the seeding launches
     if (n >= (int64_t)1 << 16) {
-      seed_rows = n / 16 / 256 * 256;
-      seed_parts = best_parts(std::max<int64_t>(
-          1, std::min<int64_t>(std::min<int64_t>(16, merge_lists / (2 * lpp)), seed_rows / 4096)));
+      const int64_t e0 = n / 256 / 256 * 256, e1 = n / 16 / 256 * 256;
+      if (e0 >= 4096) ends.push_back(e0);
+      ends.push_back(e1);
     }
+    std::vector<int> seed_parts;
+    int64_t prev = 0;
+    int used = 0;
+    for (int64_t e : ends) {
+      const int64_t lim = std::min<int64_t>(
+          std::min<int64_t>(16, (merge_lists / 2 - used * lpp) / lpp), (e - prev) / 4096);
+      const int p = best_parts(std::max<int64_t>(1, lim));
+      seed_parts.push_back(p);
+      used += p;
+      prev = e;
+    }
+    const int64_t seed_rows = ends.empty() ? 0 : ends.back();
     const int64_t rest = n - seed_rows;
     const int parts = best_parts(std::max<int64_t>(
-        1, std::min<int64_t>(std::min<int64_t>(64, merge_lists / lpp - seed_parts), rest / 4096)));
+        1, std::min<int64_t>(std::min<int64_t>(64, merge_lists / lpp - used), rest / 4096)));
     const int cap = flat_tc_cap();
-    const int lists = (seed_parts + parts) * lpp;
+    const int lists = (used + parts) * lpp;
     Scratch pkeys, pcounts, psat, gthr;
     if ((st = pkeys.alloc((size_t)nq * lists * cap * 8, s)) ||
         (st = pcounts.alloc((size_t)nq * lists * 4, s)) ||
@@ -269,27 +281,28 @@ xvec_gpu_status flat_search_impl(xvec_gpu_index* idx, const void* d_q, int nq,
     const float* row_aux =
         metric == XVEC_METRIC_COSINE ? idx->row_inv.as<float>() : idx->row_n2.as<float>();
     const __half* hrows = reinterpret_cast<const __half*>(rows);
+    // One launch over rows [b, e) into lists [list0, list0 + 2 * p).
+    auto scan = [&](int64_t b, int64_t e, int p, int list0) {
+      return launch_flat_scan_tc(metric, static_cast<const __half*>(d_q), nq, hrows + b * d,
+                                 e - b, d, d, row_aux + b, idx->keyrank.as<uint32_t>() + b,
+                                 qaux.as<float>(), qn2.as<float>(),
+                                 gthr.as<unsigned long long>(),
+                                 d_bitmap ? d_bitmap + b / 32 : nullptr, p, kp, list0, lists,
+                                 pkeys.as<uint64_t>(), pcounts.as<int>(), psat.as<uint64_t>(),
+                                 qflags.as<int>(), kstatus.as<int>(), s);
+    };
     timer.mark(1);
-    if (seed_parts > 0) {
-      XVEC_CUDA(launch_flat_scan_tc(metric, static_cast<const __half*>(d_q), nq, hrows, seed_rows,
-                                    d, d, row_aux, idx->keyrank.as<uint32_t>(), qaux.as<float>(),
-                                    qn2.as<float>(), gthr.as<unsigned long long>(), d_bitmap,
-                                    seed_parts, kp, 0, lists, pkeys.as<uint64_t>(),
-                                    pcounts.as<int>(), psat.as<uint64_t>(), qflags.as<int>(),
-                                    kstatus.as<int>(), s));
-      XVEC_CUDA(launch_seed_thresholds(pkeys.as<uint64_t>(), pcounts.as<int>(), nq, lists,
-                                       seed_parts * lpp, cap, kp, gthr.as<unsigned long long>(),
-                                       s));
+    prev = 0;
+    int list0 = 0;
+    for (size_t i = 0; i < ends.size(); ++i) {
+      XVEC_CUDA(scan(prev, ends[i], seed_parts[i], list0));
+      list0 += seed_parts[i] * lpp;
+      XVEC_CUDA(launch_seed_thresholds(pkeys.as<uint64_t>(), pcounts.as<int>(), nq, lists, list0,
+                                       cap, kp, gthr.as<unsigned long long>(), s));
       count_launches(2);
+      prev = ends[i];
     }
-    XVEC_CUDA(launch_flat_scan_tc(metric, static_cast<const __half*>(d_q), nq,
-                                  hrows + seed_rows * d, rest, d, d, row_aux + seed_rows,
-                                  idx->keyrank.as<uint32_t>() + seed_rows, qaux.as<float>(),
-                                  qn2.as<float>(), gthr.as<unsigned long long>(),
-                                  d_bitmap ? d_bitmap + seed_rows / 32 : nullptr, parts, kp,
-                                  seed_parts * lpp, lists, pkeys.as<uint64_t>(),
-                                  pcounts.as<int>(), psat.as<uint64_t>(), qflags.as<int>(),
-                                  kstatus.as<int>(), s));
+    XVEC_CUDA(scan(seed_rows, n, parts, list0));
     timer.mark(2);
     XVEC_LAUNCHED();
     count_tensor_scan();

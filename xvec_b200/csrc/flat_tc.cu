@@ -6,22 +6,33 @@
 // with the per-query candidate selection fused into the epilogue, so the
 // score matrix is never written to memory.
 //
-//   CTA = 6 warps, one CTA per SM (tensor memory and shared memory sized so):
-//     warp 0    TMA producer: query tile A[128 x 64] + row tile B[256 x 64]
-//               per k-step into a 4-stage ring (128-byte swizzle).
+//   CTA = 10 warps, one CTA per SM (tensor memory and shared memory sized so):
+//     warp 0    TMA producer: this CTA's query tile A[128 x 64] and row tile
+//               B[RB x 64] per k-step into a ring of stages (128-byte swizzle).
 //     warp 1    allocates 512 TMEM columns, issues the MMAs (one thread):
-//               D[128 queries x 256 rows] fp32, two accumulators in TMEM so
-//               the epilogue of tile t overlaps the MMAs of tile t+1.
-//     warps 2-5 epilogue: each thread owns one query (one TMEM lane), loads
-//               its 256 dot products with tcgen05.ld, turns them into fast
-//               ranks and appends the ones below its threshold to the
-//               query's candidate buffer (global memory); a full buffer is
-//               compacted to its KP best keys by the warp (select.cuh).
+//               D[queries x 256 rows] fp32, two accumulators in TMEM so the
+//               epilogue of tile t overlaps the MMAs of tile t+1.
+//     warps 2-9 epilogue: each thread owns one query (one TMEM lane) and one
+//               column half, loads 128 dot products per tile with tcgen05.ld,
+//               turns them into fast ranks and appends the ones below its
+//               threshold to the query's candidate list (global memory); a
+//               full list is compacted to its KP best keys by the warp.
+//   Single CTA (PAIR = false): M = 128 queries, RB = 256 rows per CTA.
+//   CTA pair   (PAIR = true, cluster of 2, tcgen05 cta_group::2): M = 256
+//               queries (128 per CTA), N = 256 rows of which each CTA loads
+//               128, so a CTA moves 32 KB instead of 48 KB of operands per
+//               k-step.  Both CTAs' copies of a stage complete on the first
+//               CTA's barrier, armed there for both halves; its single
+//               thread issues the pair's MMAs and signals both CTAs' stage
+//               and accumulator barriers.  At the end the second CTA
+//               publishes how many copies it issued per stage, and the first
+//               waits for every one of them before either CTA leaves.
 //   Grid = (query blocks of 128, row chunks); blockIdx.x varies fastest so
 //   the CTAs resident at any time share row chunks and the rows come from L2.
 //
 // Every mbarrier wait is bounded: on expiry the kernel records an error in
-// `status`, stops issuing work and still releases its tensor memory.
+// `status`, stops issuing work, drains its own copies and still releases its
+// tensor memory.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -37,16 +48,22 @@ namespace tc {
 constexpr int kBM = 128;   // queries per CTA (TMEM lanes)
 constexpr int kBN = 256;   // rows per tile (TMEM columns per accumulator)
 constexpr int kBK = 64;    // k-step: 64 fp16 = 128 bytes (one swizzle row)
-constexpr int kStages = 4;
 constexpr int kCap = 512;  // candidate list entries per (query, part, column half)
 constexpr int kEpiWarps = 8;  // two warps per TMEM lane quarter, one per column half
 constexpr int kThreads = 64 + kEpiWarps * 32;
 constexpr uint32_t kTileABytes = kBM * kBK * 2;  // 16 KB
-constexpr uint32_t kTileBBytes = kBN * kBK * 2;  // 32 KB
-constexpr uint32_t kStageBytes = kTileABytes + kTileBBytes;
 // Per epilogue warp: radix histogram (1 KB) + the current tile's row
 // metadata for its 128 columns (aux floats + key ranks, 1 KB).
-constexpr uint32_t kSmemBytes = kStages * kStageBytes + kEpiWarps * 256 * 4 * 2 + 1024 + 256;
+constexpr uint32_t kEpiSmemBytes = kEpiWarps * 256 * 4 * 2;
+
+template <bool PAIR>
+struct Shape {
+  static constexpr int kRowsPerCta = PAIR ? kBN / 2 : kBN;       // B rows loaded per CTA
+  static constexpr uint32_t kTileBBytes = kRowsPerCta * kBK * 2;  // 16 or 32 KB
+  static constexpr uint32_t kStageBytes = kTileABytes + kTileBBytes;
+  static constexpr int kStages = PAIR ? 6 : 4;
+  static constexpr uint32_t kSmemBytes = kStages * kStageBytes + kEpiSmemBytes + 1024 + 512;
+};
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // a wait gives up after 2 s
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -64,6 +81,32 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
+// Address of the same shared variable in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Arrive with cluster-scope release (orders this thread's earlier
+// observations for the other CTA).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar)
+               : "memory");
+}
+// Plain arrive (release at CTA scope) on a barrier of another CTA: orders
+// this thread's tensor-memory reads, not its global stores.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n"
+               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
 __device__ __forceinline__ uint64_t global_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -80,7 +123,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
     uint32_t done;
     asm volatile(
         "{\n.reg .pred p;\n"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
         "selp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(done)
         : "r"(addr), "r"(parity)
@@ -104,6 +147,22 @@ __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* ba
       : "memory");
 }
 
+// Pair form: the copy lands in this CTA's shared memory and completes on the
+// barrier at `cluster_bar`, which may belong to the other CTA of the pair.
+__device__ __forceinline__ void tma_load_2d_pair(const CUtensorMap* map, uint32_t cluster_bar,
+                                                 void* dst, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"((uint64_t)map), "r"(x), "r"(y), "r"(cluster_bar)
+      : "memory");
+}
+__device__ __forceinline__ uint32_t ld_cluster_u32(uint32_t cluster_addr) {
+  uint32_t v;
+  asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(cluster_addr) : "memory");
+  return v;
+}
+
 // UMMA shared-memory descriptor: K-major, 128-byte swizzle, 8-row groups
 // 1024 bytes apart (SBO), descriptor version 1 (sm_100).
 __device__ __forceinline__ uint64_t smem_desc_sw128(const void* tile) {
@@ -112,19 +171,38 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(const void* tile) {
          (2ull << 61);
 }
 
-// Instruction descriptor: kind::f16, A/B = F16, D = F32, both K-major.
-constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(kBN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
-
-__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t acc) {
-  asm volatile(
-      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
-      "l"(a), "l"(b), "r"(kIdesc), "r"(acc));
+// Instruction descriptor: kind::f16, A/B = F16, D = F32, both K-major, N = 256.
+template <int M>
+constexpr uint32_t idesc_f16() {
+  return (1u << 4) | ((uint32_t)(kBN >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   smem_u32(bar))
-               : "memory");
+
+template <bool PAIR>
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t acc) {
+  if constexpr (PAIR) {
+    asm volatile(
+        "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(idesc_f16<2 * kBM>()), "r"(acc));
+  } else {
+    asm volatile(
+        "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(idesc_f16<kBM>()), "r"(acc));
+  }
+}
+// Arrives on the barrier at a shared::cluster address once every MMA this
+// thread issued so far has completed.
+template <bool PAIR>
+__device__ __forceinline__ void mma_commit(uint32_t cluster_bar) {
+  if constexpr (PAIR)
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     cluster_bar)
+                 : "memory");
+  else
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     cluster_bar)
+                 : "memory");
 }
 __device__ __forceinline__ void tmem_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -146,6 +224,28 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
 }
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Packed float32 pairs (sm_100): one instruction for two columns, rounded
+// like the scalar operation on each element.
+__device__ __forceinline__ void mul2(float a0, float a1, float b0, float b1, float& r0, float& r1) {
+  uint64_t x, y, z;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(x) : "f"(a0), "f"(a1));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(y) : "f"(b0), "f"(b1));
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(z) : "l"(x), "l"(y));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r0), "=f"(r1) : "l"(z));
+}
+__device__ __forceinline__ void add2(float a0, float a1, float b0, float b1, float& r0, float& r1) {
+  uint64_t x, y, z;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(x) : "f"(a0), "f"(a1));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(y) : "f"(b0), "f"(b1));
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(z) : "l"(x), "l"(y));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r0), "=f"(r1) : "l"(z));
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
 }
 
 // Fast rank from the tensor-core dot product.  aux: 1/||x|| (cosine) or
@@ -261,7 +361,7 @@ __device__ __forceinline__ uint64_t warp_select_compact(uint64_t* gbuf, int cnt,
   return prefix;
 }
 
-template <int METRIC>
+template <int METRIC, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
     const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap rmap, int nq,
     int64_t n, int d, const float* __restrict__ row_aux, const uint32_t* __restrict__ keyrank,
@@ -270,62 +370,79 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
     int64_t rows_per_part, int kp, int list_base, int num_lists, uint64_t* __restrict__ cand,
     int* __restrict__ part_counts, uint64_t* __restrict__ part_sat, int* __restrict__ q_flags,
     int* __restrict__ status) {
+  using S = Shape<PAIR>;
+  constexpr int kStages = S::kStages;
+  constexpr uint32_t kStageBytes = S::kStageBytes;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   unsigned char* tiles = smem;  // kStages x (A | B)
   int* hist_all = reinterpret_cast<int*>(smem + kStages * kStageBytes);  // kEpiWarps x 256
   uint32_t* meta_all = reinterpret_cast<uint32_t*>(hist_all + kEpiWarps * 256);  // x 256
   uint64_t* bars = reinterpret_cast<uint64_t*>(meta_all + kEpiWarps * 256);
-  uint64_t* full = bars;               // [kStages]
-  uint64_t* empty = bars + kStages;    // [kStages]
-  uint64_t* tfull = bars + 2 * kStages;   // [2]
-  uint64_t* tempty = bars + 2 * kStages + 2;  // [2]
-  uint64_t* mdone = bars + 2 * kStages + 4;   // all issued MMAs retired
-  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 5);
+  uint64_t* full = bars;                      // [kStages] the stage's copies landed (pair:
+                                              // both CTAs' copies, on the first CTA)
+  uint32_t* issued = reinterpret_cast<uint32_t*>(bars + kStages);  // [kStages] copies per stage
+  uint64_t* empty = bars + 2 * kStages;       // [kStages] the MMAs have read the stage
+  uint64_t* tfull = bars + 3 * kStages;       // [2] accumulator ready
+  uint64_t* tempty = bars + 3 * kStages + 2;  // [2] accumulator drained (issuing CTA's count)
+  uint64_t* mdone = bars + 3 * kStages + 4;   // all issued MMAs retired
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(bars + 3 * kStages + 5);
   __shared__ int s_abort_storage;
   volatile int* s_abort = &s_abort_storage;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qblock = blockIdx.x;
-  const int part = blockIdx.y, num_parts = gridDim.y;
+  const int part = blockIdx.y;
   const int64_t row_begin = (int64_t)part * rows_per_part;
   const int64_t row_end = min(n, row_begin + rows_per_part);
   const int num_tiles = row_end > row_begin ? (int)((row_end - row_begin + kBN - 1) / kBN) : 0;
   const int ksteps = (d + kBK - 1) / kBK;
+  const uint32_t rank = PAIR ? cluster_rank() : 0u;
+  const bool issuer = rank == 0;  // the CTA whose thread issues the MMAs
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
+      issued[s] = 0;
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], kEpiWarps * 32);
+      mbar_init(&tempty[a], (PAIR ? 2 : 1) * kEpiWarps);
     }
     mbar_init(mdone, 1);
     *s_abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(
-                     smem_u32(tmem_base_slot)));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    if constexpr (PAIR) {
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(
+                       smem_u32(tmem_base_slot)));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(
+                       smem_u32(tmem_base_slot)));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
     tmem_fence_before();
   }
   __syncthreads();
+  // Both CTAs' barriers exist before either signals the other.
+  if constexpr (PAIR) cluster_sync_all();
   tmem_fence_after();
   const uint32_t tmem_base = *tmem_base_slot;
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
+      const uint32_t full0 = PAIR ? cluster_addr(&full[0], 0) : smem_u32(&full[0]);
       int stage = 0;
       uint32_t phase = 0;
-      int armed[kStages];
+      uint32_t count[kStages];
 #pragma unroll
-      for (int s2 = 0; s2 < kStages; ++s2) armed[s2] = -1;
+      for (int s2 = 0; s2 < kStages; ++s2) count[s2] = 0;
       for (int t = 0; t < num_tiles && !*s_abort; ++t) {
-        const int row0 = (int)(row_begin + (int64_t)t * kBN);
+        const int row0 = (int)(row_begin + (int64_t)t * kBN) + (int)rank * S::kRowsPerCta;
         for (int ks = 0; ks < ksteps; ++ks) {
           if (!mbar_wait(&empty[stage], phase ^ 1, s_abort)) {
             atomicExch(status, 1);
@@ -334,26 +451,32 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
           }
           unsigned char* a_dst = tiles + stage * kStageBytes;
           unsigned char* b_dst = a_dst + kTileABytes;
-          mbar_expect_tx(&full[stage], kStageBytes);
-          tma_load_2d(&qmap, &full[stage], a_dst, ks * kBK, qblock * kBM);
-          tma_load_2d(&rmap, &full[stage], b_dst, ks * kBK, row0);
-          armed[stage] = (int)phase;
+          if (issuer) mbar_expect_tx(&full[stage], (PAIR ? 2 : 1) * kStageBytes);
+          if constexpr (PAIR) {
+            tma_load_2d_pair(&qmap, full0 + stage * 8, a_dst, ks * kBK, qblock * kBM);
+            tma_load_2d_pair(&rmap, full0 + stage * 8, b_dst, ks * kBK, row0);
+          } else {
+            tma_load_2d(&qmap, &full[stage], a_dst, ks * kBK, qblock * kBM);
+            tma_load_2d(&rmap, &full[stage], b_dst, ks * kBK, row0);
+          }
+          ++count[stage];
           if (++stage == kStages) {
             stage = 0;
             phase ^= 1;
           }
         }
       }
-      // Drain: every armed stage's copies have landed before the CTA can
-      // exit (already true unless another role aborted).
 #pragma unroll
-      for (int s2 = 0; s2 < kStages; ++s2)
-        if (armed[s2] >= 0 && !mbar_wait(&full[s2], (uint32_t)armed[s2], nullptr))
-          atomicExch(status, 5);
+      for (int s2 = 0; s2 < kStages; ++s2) issued[s2] = count[s2];
     }
+  } else if (warp == 1 && !issuer) {
+    // Second CTA of a pair: its tensor memory is written by the first CTA.
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
+      const uint32_t own_empty0 = smem_u32(&empty[0]), own_tfull0 = smem_u32(&tfull[0]);
+      const uint32_t peer_empty0 = PAIR ? cluster_addr(&empty[0], 1) : 0u;
+      const uint32_t peer_tfull0 = PAIR ? cluster_addr(&tfull[0], 1) : 0u;
       int stage = 0;
       uint32_t phase = 0;
       for (int t = 0; t < num_tiles && !*s_abort; ++t) {
@@ -378,18 +501,20 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
           const uint64_t bdesc = smem_desc_sw128(a_src + kTileABytes);
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k)  // 16 fp16 = 32 bytes per MMA
-            mma_f16(d_tmem, adesc + (uint64_t)(k * 2), bdesc + (uint64_t)(k * 2),
-                    (ks > 0 || k > 0) ? 1u : 0u);
-          mma_commit(&empty[stage]);
+            mma_f16<PAIR>(d_tmem, adesc + (uint64_t)(k * 2), bdesc + (uint64_t)(k * 2),
+                          (ks > 0 || k > 0) ? 1u : 0u);
+          mma_commit<PAIR>(own_empty0 + stage * 8);
+          if (PAIR) mma_commit<PAIR>(peer_empty0 + stage * 8);
           if (++stage == kStages) {
             stage = 0;
             phase ^= 1;
           }
         }
-        mma_commit(&tfull[acc]);
+        mma_commit<PAIR>(own_tfull0 + acc * 8);
+        if (PAIR) mma_commit<PAIR>(peer_tfull0 + acc * 8);
       }
       // Retire every issued MMA before tensor memory is released.
-      mma_commit(mdone);
+      mma_commit<PAIR>(smem_u32(mdone));
       if (!mbar_wait(mdone, 0, nullptr)) atomicExch(status, 6);
     }
   } else {
@@ -427,13 +552,15 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
       for (int c = 0; c < 4; ++c) {
         const int64_t row = base + c * 32 + lane;
         const bool ok = t < num_tiles && row < row_end && bitmap_pass(bitmap, row);
-        const float ra = (ok && METRIC != kMetricIP) ? row_aux[row] : 0.f;
-        pf_aux[c] = METRIC == kMetricL2 ? -0.5f * ra : ra;
+        // Raw value; the L2 transform happens at the shared-memory store so
+        // nothing waits on this load before the next tile.
+        pf_aux[c] = (ok && METRIC != kMetricIP) ? row_aux[row] : 0.f;
         pf_kr[c] = ok ? keyrank[row] : 0u;
         pf_vm[c] = __ballot_sync(kFullMask, ok);
       }
     };
     prefetch(0);
+    uint64_t g_next = thr;
     for (int t = 0; t < num_tiles; ++t) {
       const int acc = t & 1;
       const uint32_t acc_phase = (t >> 1) & 1;
@@ -441,21 +568,21 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
       __syncwarp();
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        meta_aux[c * 32 + lane] = pf_aux[c];
+        meta_aux[c * 32 + lane] = METRIC == kMetricL2 ? -0.5f * pf_aux[c] : pf_aux[c];
         meta_kr[c * 32 + lane] = pf_kr[c];
         vm[c] = pf_vm[c];
       }
       __syncwarp();
       prefetch(t + 1);
-      if (qvalid) {
-        const uint64_t g = *(volatile unsigned long long*)&gthr[qi];
-        if (g < thr) {
-          thr = g;
-          thr_f = rank_of(thr);
-          tq = score_bound<METRIC>(thr_f, qa, qn2);
-        }
+      // The shared threshold read during the previous tile.
+      if (g_next < thr) {
+        thr = g_next;
+        thr_f = rank_of(thr);
+        tq = score_bound<METRIC>(thr_f, qa, qn2);
       }
-      if (!mbar_wait(&tfull[acc], acc_phase, s_abort)) {
+      if (qvalid) g_next = *(volatile unsigned long long*)&gthr[qi];
+      // Warp-uniform outcome: the tcgen05.ld below needs every lane.
+      if (!__all_sync(kFullMask, mbar_wait(&tfull[acc], acc_phase, s_abort))) {
         atomicExch(status, 4);
         *s_abort = 1;
         break;
@@ -491,31 +618,60 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
           return -tc_rank<METRIC>(dot, a, qa, qn2);
         };
         const float4* a4 = reinterpret_cast<const float4*>(meta_aux + c * 32);
-        if (vmask == kFullMask) {
+        if (vmask != 0u) {
+          bool any;
+          if constexpr (METRIC == kMetricMIPS) {
+            any = true;
+          } else {
+            // Common path: the chunk's largest score, two columns per packed
+            // operation and two per three-input max (bit-identical to the
+            // scores of the rare path, so it never misses a column).
+            float m0 = -INFINITY, m1 = -INFINITY;
 #pragma unroll
-          for (int g = 0; g < 8; ++g) {
-            const float4 av = a4[g];
-            const float aa[4] = {av.x, av.y, av.z, av.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-              if (score(g * 4 + e, aa[e]) >= tq) rare(g * 4 + e, aa[e]);
+            for (int g = 0; g < 8; ++g) {
+              const float d0 = __uint_as_float(cur[g * 4 + 0]);
+              const float d1 = __uint_as_float(cur[g * 4 + 1]);
+              const float d2 = __uint_as_float(cur[g * 4 + 2]);
+              const float d3 = __uint_as_float(cur[g * 4 + 3]);
+              float s0 = d0, s1 = d1, s2 = d2, s3 = d3;
+              if constexpr (METRIC == kMetricCosine) {
+                const float4 av = a4[g];
+                mul2(d0, d1, av.x, av.y, s0, s1);
+                mul2(d2, d3, av.z, av.w, s2, s3);
+              } else if constexpr (METRIC == kMetricL2) {
+                const float4 av = a4[g];
+                add2(d0, d1, av.x, av.y, s0, s1);
+                add2(d2, d3, av.z, av.w, s2, s3);
+              }
+              m0 = max3(m0, s0, s1);
+              m1 = max3(m1, s2, s3);
+            }
+            any = fmaxf(m0, m1) >= tq;
           }
-        } else if (vmask != 0u) {
+          if (any) {
+            // Rare path, column by column; fully unrolled so the accumulator
+            // registers are indexed at compile time.
 #pragma unroll
-          for (int g = 0; g < 8; ++g) {
-            const float4 av = a4[g];
-            const float aa[4] = {av.x, av.y, av.z, av.w};
+            for (int g = 0; g < 8; ++g) {
+              const float4 av = a4[g];
+              const float aa[4] = {av.x, av.y, av.z, av.w};
 #pragma unroll
-            for (int e = 0; e < 4; ++e)
-              if (((vmask >> (g * 4 + e)) & 1u) && score(g * 4 + e, aa[e]) >= tq)
-                rare(g * 4 + e, aa[e]);
+              for (int e = 0; e < 4; ++e)
+                if (((vmask >> (g * 4 + e)) & 1u) && score(g * 4 + e, aa[e]) >= tq)
+                  rare(g * 4 + e, aa[e]);
+            }
           }
         }
         if (c + 1 < 4) tmem_wait_ld();
       }
-      // Release the accumulator to the MMA warp before any compaction.
+      // Release the accumulator to the MMA warp before any compaction (one
+      // arrival per warp, on the issuing CTA's barrier).
       tmem_fence_before();
-      mbar_arrive(&tempty[acc]);
+      __syncwarp();
+      if (lane == 0) {
+        if constexpr (PAIR) mbar_arrive_remote(cluster_addr(&tempty[acc], 0));
+        else mbar_arrive(&tempty[acc]);
+      }
       // Keep room for the next tile's appends (at most 128 per list).
       uint32_t need = __ballot_sync(kFullMask, cnt > kCap - 128);
       while (need) {
@@ -556,9 +712,31 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
   }
 
   __syncthreads();
+  // Drain: every copy either CTA issued has landed before either leaves
+  // (already true unless a role aborted).  The first CTA's barriers count
+  // both CTAs' copies; a stage phase the second CTA issued but the first
+  // never armed (the first stopped early) is armed here for its half.
+  if constexpr (PAIR) cluster_sync_all();
+  if (threadIdx.x == 0 && issuer) {
+    for (int s2 = 0; s2 < kStages; ++s2) {
+      const uint32_t mine = issued[s2];
+      const uint32_t other = PAIR ? ld_cluster_u32(cluster_addr(&issued[s2], 1)) : mine;
+      if (mine > 0 && !mbar_wait(&full[s2], (mine - 1) & 1, nullptr)) atomicExch(status, 5);
+      if (PAIR && other > mine) {  // at most one phase ahead
+        mbar_expect_tx(&full[s2], kStageBytes);
+        if (!mbar_wait(&full[s2], mine & 1, nullptr)) atomicExch(status, 5);
+      }
+    }
+  }
+  // Neither CTA of a pair leaves while the other may still read its shared
+  // memory, signal its barriers or write its tensor memory.
+  if constexpr (PAIR) cluster_sync_all();
   if (warp == 1) {
     tmem_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem_base));
+    if constexpr (PAIR)
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, 512;" ::"r"(tmem_base));
+    else
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem_base));
   }
 }
 
@@ -607,6 +785,9 @@ bool flat_tc_supported(int d, const void* rows, const void* queries) {
 int flat_tc_cap() { return tc::kCap; }
 int flat_tc_lists_per_part() { return 2; }
 
+// CTA pairs whenever there are two query blocks to pair up.
+bool flat_tc_pairs(int nq) { return nq > tc::kBM; }
+
 cudaError_t launch_flat_scan_tc(int metric, const __half* queries, int nq, const __half* rows,
                                 int64_t n, int d, int64_t row_stride_elems, const float* row_aux,
                                 const uint32_t* keyrank, const float* q_aux, const float* q_n2,
@@ -614,31 +795,51 @@ cudaError_t launch_flat_scan_tc(int metric, const __half* queries, int nq, const
                                 int kp, int list_base, int num_lists, uint64_t* cand,
                                 int* part_counts, uint64_t* part_sat, int* q_flags, int* status,
                                 cudaStream_t stream) {
+  const int qblocks = (nq + tc::kBM - 1) / tc::kBM;
+  const bool pair = flat_tc_pairs(nq);
   CUtensorMap qmap, rmap;
   if (!make_map(&qmap, queries, nq, d, d, tc::kBM) ||
-      !make_map(&rmap, rows, n, d, row_stride_elems, tc::kBN))
+      !make_map(&rmap, rows, n, d, row_stride_elems,
+                pair ? tc::Shape<true>::kRowsPerCta : tc::Shape<false>::kRowsPerCta))
     return cudaErrorInvalidValue;
   const int64_t rows_per_part = ((n + num_parts - 1) / num_parts + tc::kBN - 1) / tc::kBN * tc::kBN;
-  dim3 grid((nq + tc::kBM - 1) / tc::kBM, num_parts);
-  const int smem = (int)tc::kSmemBytes;
-#define XVEC_TC_CASE(M)                                                                     \
-  case M: {                                                                                 \
-    auto kern = tc::flat_scan_tc_kernel<M>;                                                 \
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);         \
-    kern<<<grid, tc::kThreads, smem, stream>>>(qmap, rmap, nq, n, d, row_aux, keyrank, q_aux, \
-                                               q_n2, gthr, bitmap, rows_per_part, kp,         \
-                                               list_base, num_lists, cand, part_counts,       \
-                                               part_sat, q_flags, status);                    \
-    break;                                                                                  \
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(pair ? (qblocks + 1) / 2 * 2 : qblocks, num_parts);
+  cfg.blockDim = dim3(tc::kThreads);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = pair ? 2 : 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t err = cudaErrorInvalidValue;
+#define XVEC_TC_CASE(M, P)                                                                      \
+  {                                                                                             \
+    auto kern = tc::flat_scan_tc_kernel<M, P>;                                                  \
+    cfg.dynamicSmemBytes = tc::Shape<P>::kSmemBytes;                                            \
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,                    \
+                         (int)tc::Shape<P>::kSmemBytes);                                        \
+    err = cudaLaunchKernelEx(&cfg, kern, qmap, rmap, nq, n, d, row_aux, keyrank, q_aux, q_n2,  \
+                             gthr, bitmap, rows_per_part, kp, list_base, num_lists, cand,      \
+                             part_counts, part_sat, q_flags, status);                           \
   }
+#define XVEC_TC_METRIC(M)           \
+  case M:                           \
+    if (pair) XVEC_TC_CASE(M, true) \
+    else XVEC_TC_CASE(M, false)     \
+    break;
   switch (metric) {
-    XVEC_TC_CASE(kMetricL2)
-    XVEC_TC_CASE(kMetricIP)
-    XVEC_TC_CASE(kMetricCosine)
-    XVEC_TC_CASE(kMetricMIPS)
+    XVEC_TC_METRIC(kMetricL2)
+    XVEC_TC_METRIC(kMetricIP)
+    XVEC_TC_METRIC(kMetricCosine)
+    XVEC_TC_METRIC(kMetricMIPS)
     default: return cudaErrorInvalidValue;
   }
+#undef XVEC_TC_METRIC
 #undef XVEC_TC_CASE
+  if (err != cudaSuccess) return err;
   return cudaGetLastError();
 }
 

@@ -14,6 +14,9 @@ bool flat_tc_supported(int d, const void* rows, const void* queries);
 int flat_tc_cap();
 // Candidate lists per row part (one per column half of the tile).
 int flat_tc_lists_per_part();
+// True when a batch of nq queries runs on CTA pairs (256 queries per pair);
+// the grid then has an even number of 128-query blocks.
+bool flat_tc_pairs(int nq);
 
 // Scans rows [0, n) (row i at rows + i * row_stride_elems) against nq queries.
 // row_aux: 1/||x|| for cosine, ||x||^2 for L2 / MIPS (unused for IP);

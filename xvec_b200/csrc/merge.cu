@@ -43,10 +43,21 @@ __global__ void merge_results_kernel(int metric, int k, int nq, int parts, int n
   uint64_t* skey = reinterpret_cast<uint64_t*>(smem);
   uint32_t* srank = reinterpret_cast<uint32_t*>(skey + n_pow2);
   float* sscore = reinterpret_cast<float*>(srank + n_pow2);
-  __shared__ int s_n;
+  __shared__ int s_n, s_err;
   const int q = blockIdx.x;
-  if (threadIdx.x == 0) s_n = 0;
+  if (threadIdx.x == 0) {
+    s_n = 0;
+    // A query that failed on a shard (count = -status) fails as a whole; the
+    // shards validate a query the same way, so the first one's status stands.
+    s_err = 0;
+    for (int p = 0; p < parts && s_err == 0; ++p) {
+      const int c = counts[(int64_t)p * nq + q];
+      if (c < 0) s_err = c;
+    }
+    if (s_err) out_counts[q] = s_err;
+  }
   __syncthreads();
+  if (s_err) return;
   for (int i = threadIdx.x; i < parts * k; i += blockDim.x) {
     const int p = i / k, j = i - p * k;
     const int c = counts[(int64_t)p * nq + q];
@@ -55,7 +66,8 @@ __global__ void merge_results_kernel(int metric, int k, int nq, int parts, int n
       const int slot = atomicAdd(&s_n, 1);
       skey[slot] = keys[src];
       sscore[slot] = scores[src];
-      srank[slot] = float_to_ordered(rank_from_score(metric, scores[src]));
+      // + 0.f: -0 and +0 rank equal (the reference compares scores with ==).
+      srank[slot] = float_to_ordered(rank_from_score(metric, scores[src]) + 0.f);
     }
   }
   __syncthreads();

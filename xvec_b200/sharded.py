@@ -17,6 +17,34 @@ import torch.distributed as dist
 from . import SearchOptions, SearchResults, _Index, merge_results_device
 
 
+def shard_range(n_total: int, rank: int, world: int, align: int = 1):
+    """Contiguous row range [begin, end) of `rank`'s shard: the rows are split
+    into `world` nearly equal parts, each a multiple of `align` rows except
+    the last."""
+    units = (n_total + align - 1) // align
+    per = (units + world - 1) // world
+    begin = min(n_total, rank * per * align)
+    end = min(n_total, (rank + 1) * per * align)
+    return begin, end
+
+
+def exchange(keys: torch.Tensor, scores: torch.Tensor, counts: torch.Tensor, group=None):
+    """All-gather of every rank's per-shard results: [nq, k] keys / scores and
+    [nq] counts in, [world, nq, k] / [world, nq] out, on the tensors' device
+    (NCCL on GPUs; gloo on the CPU)."""
+    world = dist.get_world_size(group)
+    nq, k = keys.shape
+    # Outputs concatenated along dim 0 (the layout every backend accepts).
+    all_keys = torch.empty((world * nq, k), dtype=keys.dtype, device=keys.device)
+    all_scores = torch.empty((world * nq, k), dtype=scores.dtype, device=scores.device)
+    all_counts = torch.empty((world * nq,), dtype=counts.dtype, device=counts.device)
+    dist.all_gather_into_tensor(all_keys, keys.contiguous(), group=group)
+    dist.all_gather_into_tensor(all_scores, scores.contiguous(), group=group)
+    dist.all_gather_into_tensor(all_counts, counts.contiguous(), group=group)
+    return (all_keys.view(world, nq, k), all_scores.view(world, nq, k),
+            all_counts.view(world, nq))
+
+
 class ShardedSearch:
     def __init__(self, index: _Index, group=None):
         self.index = index
@@ -36,12 +64,7 @@ class ShardedSearch:
                                  scores.data_ptr(), counts.data_ptr(), stream=stream)
         if self.world == 1:
             return keys, scores, counts
-        all_keys = torch.empty((self.world, nq, k), dtype=torch.int64, device=self.device)
-        all_scores = torch.empty((self.world, nq, k), dtype=torch.float32, device=self.device)
-        all_counts = torch.empty((self.world, nq), dtype=torch.int32, device=self.device)
-        dist.all_gather_into_tensor(all_keys, keys, group=self.group)
-        dist.all_gather_into_tensor(all_scores, scores, group=self.group)
-        dist.all_gather_into_tensor(all_counts, counts, group=self.group)
+        all_keys, all_scores, all_counts = exchange(keys, scores, counts, self.group)
         out_keys = torch.empty_like(keys)
         out_scores = torch.empty_like(scores)
         out_counts = torch.empty_like(counts)
