@@ -226,28 +226,6 @@ __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// Packed float32 pairs (sm_100): one instruction for two columns, rounded
-// like the scalar operation on each element.
-__device__ __forceinline__ void mul2(float a0, float a1, float b0, float b1, float& r0, float& r1) {
-  uint64_t x, y, z;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(x) : "f"(a0), "f"(a1));
-  asm("mov.b64 %0, {%1, %2};" : "=l"(y) : "f"(b0), "f"(b1));
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(z) : "l"(x), "l"(y));
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(r0), "=f"(r1) : "l"(z));
-}
-__device__ __forceinline__ void add2(float a0, float a1, float b0, float b1, float& r0, float& r1) {
-  uint64_t x, y, z;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(x) : "f"(a0), "f"(a1));
-  asm("mov.b64 %0, {%1, %2};" : "=l"(y) : "f"(b0), "f"(b1));
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(z) : "l"(x), "l"(y));
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(r0), "=f"(r1) : "l"(z));
-}
-__device__ __forceinline__ float max3(float a, float b, float c) {
-  float r;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
-  return r;
-}
-
 // Fast rank from the tensor-core dot product.  aux: 1/||x|| (cosine) or
 // ||x||^2 (L2, MIPS); qa: 1/||q|| (cosine) or ||q||^2.
 template <int METRIC>
@@ -552,15 +530,13 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
       for (int c = 0; c < 4; ++c) {
         const int64_t row = base + c * 32 + lane;
         const bool ok = t < num_tiles && row < row_end && bitmap_pass(bitmap, row);
-        // Raw value; the L2 transform happens at the shared-memory store so
-        // nothing waits on this load before the next tile.
-        pf_aux[c] = (ok && METRIC != kMetricIP) ? row_aux[row] : 0.f;
+        const float ra = (ok && METRIC != kMetricIP) ? row_aux[row] : 0.f;
+        pf_aux[c] = METRIC == kMetricL2 ? -0.5f * ra : ra;
         pf_kr[c] = ok ? keyrank[row] : 0u;
         pf_vm[c] = __ballot_sync(kFullMask, ok);
       }
     };
     prefetch(0);
-    uint64_t g_next = thr;
     for (int t = 0; t < num_tiles; ++t) {
       const int acc = t & 1;
       const uint32_t acc_phase = (t >> 1) & 1;
@@ -568,19 +544,20 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
       __syncwarp();
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        meta_aux[c * 32 + lane] = METRIC == kMetricL2 ? -0.5f * pf_aux[c] : pf_aux[c];
+        meta_aux[c * 32 + lane] = pf_aux[c];
         meta_kr[c * 32 + lane] = pf_kr[c];
         vm[c] = pf_vm[c];
       }
       __syncwarp();
       prefetch(t + 1);
-      // The shared threshold read during the previous tile.
-      if (g_next < thr) {
-        thr = g_next;
-        thr_f = rank_of(thr);
-        tq = score_bound<METRIC>(thr_f, qa, qn2);
+      if (qvalid) {
+        const uint64_t g = *(volatile unsigned long long*)&gthr[qi];
+        if (g < thr) {
+          thr = g;
+          thr_f = rank_of(thr);
+          tq = score_bound<METRIC>(thr_f, qa, qn2);
+        }
       }
-      if (qvalid) g_next = *(volatile unsigned long long*)&gthr[qi];
       // Warp-uniform outcome: the tcgen05.ld below needs every lane.
       if (!__all_sync(kFullMask, mbar_wait(&tfull[acc], acc_phase, s_abort))) {
         atomicExch(status, 4);
@@ -618,48 +595,24 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
           return -tc_rank<METRIC>(dot, a, qa, qn2);
         };
         const float4* a4 = reinterpret_cast<const float4*>(meta_aux + c * 32);
-        if (vmask != 0u) {
-          bool any;
-          if constexpr (METRIC == kMetricMIPS) {
-            any = true;
-          } else {
-            // Common path: the chunk's largest score, two columns per packed
-            // operation and two per three-input max (bit-identical to the
-            // scores of the rare path, so it never misses a column).
-            float m0 = -INFINITY, m1 = -INFINITY;
+        if (vmask == kFullMask) {
 #pragma unroll
-            for (int g = 0; g < 8; ++g) {
-              const float d0 = __uint_as_float(cur[g * 4 + 0]);
-              const float d1 = __uint_as_float(cur[g * 4 + 1]);
-              const float d2 = __uint_as_float(cur[g * 4 + 2]);
-              const float d3 = __uint_as_float(cur[g * 4 + 3]);
-              float s0 = d0, s1 = d1, s2 = d2, s3 = d3;
-              if constexpr (METRIC == kMetricCosine) {
-                const float4 av = a4[g];
-                mul2(d0, d1, av.x, av.y, s0, s1);
-                mul2(d2, d3, av.z, av.w, s2, s3);
-              } else if constexpr (METRIC == kMetricL2) {
-                const float4 av = a4[g];
-                add2(d0, d1, av.x, av.y, s0, s1);
-                add2(d2, d3, av.z, av.w, s2, s3);
-              }
-              m0 = max3(m0, s0, s1);
-              m1 = max3(m1, s2, s3);
-            }
-            any = fmaxf(m0, m1) >= tq;
+          for (int g = 0; g < 8; ++g) {
+            const float4 av = a4[g];
+            const float aa[4] = {av.x, av.y, av.z, av.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              if (score(g * 4 + e, aa[e]) >= tq) rare(g * 4 + e, aa[e]);
           }
-          if (any) {
-            // Rare path, column by column; fully unrolled so the accumulator
-            // registers are indexed at compile time.
+        } else if (vmask != 0u) {
 #pragma unroll
-            for (int g = 0; g < 8; ++g) {
-              const float4 av = a4[g];
-              const float aa[4] = {av.x, av.y, av.z, av.w};
+          for (int g = 0; g < 8; ++g) {
+            const float4 av = a4[g];
+            const float aa[4] = {av.x, av.y, av.z, av.w};
 #pragma unroll
-              for (int e = 0; e < 4; ++e)
-                if (((vmask >> (g * 4 + e)) & 1u) && score(g * 4 + e, aa[e]) >= tq)
-                  rare(g * 4 + e, aa[e]);
-            }
+            for (int e = 0; e < 4; ++e)
+              if (((vmask >> (g * 4 + e)) & 1u) && score(g * 4 + e, aa[e]) >= tq)
+                rare(g * 4 + e, aa[e]);
           }
         }
         if (c + 1 < 4) tmem_wait_ld();
