@@ -341,6 +341,17 @@ def kmeans_assign(metric: int, vectors, centroids, device: int = 0):
     return labels, scores
 
 
+def kmeans_assign_device(device: int, metric: int, vectors_ptr: int, n: int, centroids_ptr: int,
+                         nc: int, dim: int, labels_ptr: int, scores_ptr: int = 0,
+                         stream: int = 0) -> None:
+    """assignKMeans on device memory (xvec_gpu_kmeans_assign_device): float32
+    vectors [n, dim] and centroids [nc, dim] in, int32 labels [n] (and float32
+    scores [n] when scores_ptr is non-zero) out."""
+    _check(_lib.xvec_gpu_kmeans_assign_device(device, metric, vectors_ptr, n, centroids_ptr, nc,
+                                              dim, labels_ptr, scores_ptr or None,
+                                              stream or None))
+
+
 def merge_results_device(device: int, metric: int, top_k: int, nq: int, parts: int, keys_ptr: int,
                          scores_ptr: int, counts_ptr: int, out_keys_ptr: int,
                          out_scores_ptr: int, out_counts_ptr: int, stream: int = 0) -> None:

@@ -147,37 +147,6 @@ bool is_cancelled(const xvec_gpu_search_opts& o) {
   return o.cancel_flag && *o.cancel_flag != 0;
 }
 
-// Optional device timing of search phases (xvec_gpu_stats_enable_timing).
-struct EventTimer {
-  cudaStream_t stream;
-  bool on;
-  cudaEvent_t ev[4] = {};
-  explicit EventTimer(cudaStream_t s) : stream(s), on(timing_enabled()) {
-    if (on)
-      for (auto& e : ev) cudaEventCreate(&e);
-  }
-  ~EventTimer() {
-    if (on)
-      for (auto& e : ev) cudaEventDestroy(e);
-  }
-  void mark(int i) {
-    if (on) cudaEventRecord(ev[i], stream);
-  }
-  // Elapsed ms between two recorded marks (0 if either was not recorded).
-  double ms(int a, int b) {
-    if (!on) return 0;
-    float t = 0;
-    if (cudaEventQuery(ev[a]) != cudaSuccess || cudaEventQuery(ev[b]) != cudaSuccess) {
-      cudaGetLastError();
-      return 0;
-    }
-    if (cudaEventElapsedTime(&t, ev[a], ev[b]) != cudaSuccess) {
-      cudaGetLastError();
-      return 0;
-    }
-    return t;
-  }
-};
 
 int choose_kp(int k) {
   int want = k + std::max(8, k / 4);

@@ -25,6 +25,50 @@ void count_search(int64_t queries, int64_t exact_queries, double scan_ms, double
 bool timing_enabled();
 #define XVEC_LAUNCHED() ::xvec::count_launches(1)
 
+// Searches a search makes internally (the IVF probe over the centroids, the
+// nearest-centroid assignment of inserted rows) are not counted as searches.
+void nested_search_enter();
+void nested_search_leave();
+struct NestedSearch {
+  NestedSearch() { nested_search_enter(); }
+  ~NestedSearch() { nested_search_leave(); }
+};
+
+// Events on the search stream, recorded only while timing is enabled:
+// mark(0) search start, mark(1) / mark(2) around the candidate scan,
+// mark(3) search end.
+struct EventTimer {
+  cudaStream_t stream;
+  bool on;
+  cudaEvent_t ev[4] = {};
+  explicit EventTimer(cudaStream_t s) : stream(s), on(timing_enabled()) {
+    if (on)
+      for (auto& e : ev) cudaEventCreate(&e);
+  }
+  ~EventTimer() {
+    if (on)
+      for (auto& e : ev) cudaEventDestroy(e);
+  }
+  void mark(int i) {
+    if (on) cudaEventRecord(ev[i], stream);
+  }
+  // Elapsed ms between two recorded marks (0 if either was not recorded).
+  double ms(int a, int b) {
+    if (!on) return 0;
+    float t = 0;
+    if (cudaEventQuery(ev[a]) != cudaSuccess || cudaEventQuery(ev[b]) != cudaSuccess) {
+      cudaGetLastError();
+      return 0;
+    }
+    if (cudaEventElapsedTime(&t, ev[a], ev[b]) != cudaSuccess) {
+      cudaGetLastError();
+      return 0;
+    }
+    return t;
+  }
+};
+
+
 #define XVEC_CUDA(expr)                                                                       \
   do {                                                                                        \
     cudaError_t err__ = (expr);                                                               \
@@ -104,6 +148,8 @@ struct xvec_gpu_index {
   xvec::DeviceBuffer row_list;      // int32 [n] list of each row
   xvec::DeviceBuffer list_offsets;  // int64 [nlist+1] CSR over positions
   xvec::DeviceBuffer list_rows;     // uint32 [n] positions grouped by list (insertion order)
+  xvec::DeviceBuffer list_codes;    // uint8 [n][chunks] the PQ codes in list_rows order
+  xvec::DeviceBuffer list_keyrank;  // uint32 [n] key ranks in list_rows order
   bool lists_dirty = true;
 
   // RaBitQ (one-bit).

@@ -139,69 +139,140 @@ __device__ __forceinline__ bool pq_lookup(const float* table, const uint8_t* cod
   return true;
 }
 
-// One block per (query, probed list): the list's codes scored against the
-// query's table in shared memory; the KP best keys are kept per list.
-template <int CAP>
-__global__ void __launch_bounds__(256) ivfpq_scan_kernel(
-    const float* __restrict__ table, int chunks, const uint8_t* __restrict__ codes,
+// Byte c (compile-time) of a 32-byte code held as two 16-byte vectors.
+__device__ __forceinline__ uint32_t code_byte(const uint4& lo, const uint4& hi, int c) {
+  const uint4& v = c < 16 ? lo : hi;
+  const int w = (c >> 2) & 3;
+  const uint32_t word = w == 0 ? v.x : w == 1 ? v.y : w == 2 ? v.z : v.w;
+  return (word >> (8 * (c & 3))) & 0xffu;
+}
+
+// One block (16 warps) per query: the query's table is staged once in shared
+// memory as LutT (float64 when it fits, so the float64 sums need no
+// conversions) and the block walks every probed list; the warps split each
+// list in 64-code steps and work without block barriers.  Each warp keeps its
+// own candidate list (ballot appends, warp compaction to the KP best keys)
+// and the warps share the lowest list threshold through shared memory; the
+// 16 lists of a query are merged in exact mode.  Codes and key ranks are read
+// in list-major order (contiguous per list; positions only for the filter).
+// Each lane scores kPer codes per step with their float64 sums interleaved,
+// each still in chunk order, so every score is the reference's, and loads a
+// row's key rank only when its score can enter the list.
+constexpr int kScanWarps = 16;
+
+template <int CAPW, typename LutT>
+__global__ void __launch_bounds__(kScanWarps * 32, 2) ivfpq_scan_kernel(
+    const float* __restrict__ table, int chunks, const uint8_t* __restrict__ list_codes,
     const uint64_t* __restrict__ probe_lists, const int* __restrict__ probe_counts, int nprobe,
     const int64_t* __restrict__ list_offsets, const uint32_t* __restrict__ list_rows,
-    const uint32_t* __restrict__ keyrank, const uint32_t* __restrict__ bitmap, int metric, int kp,
-    uint64_t* __restrict__ part_keys, int* __restrict__ part_counts,
+    const uint32_t* __restrict__ list_keyrank, const uint32_t* __restrict__ bitmap, int metric,
+    int kp, uint64_t* __restrict__ part_keys, int* __restrict__ part_counts,
     uint64_t* __restrict__ part_sat, int* __restrict__ q_flags) {
+  constexpr int kPer = 2;
+  constexpr int kStep = 32 * kPer;  // codes per warp step
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  float* slut = reinterpret_cast<float*>(smem_raw);                     // [chunks][256]
-  uint64_t* buf = reinterpret_cast<uint64_t*>(slut + chunks * 256);     // [CAP]
-  __shared__ AccumState st;
-  const int q = blockIdx.x, j = blockIdx.y;
-  const int64_t slot = (int64_t)q * nprobe + j;
+  LutT* slut = reinterpret_cast<LutT*>(smem_raw);                       // [chunks][256]
+  uint64_t* wbuf = reinterpret_cast<uint64_t*>(slut + chunks * 256);    // [warps][CAPW]
+  __shared__ AccumState wst[kScanWarps];
+  __shared__ unsigned long long s_thr;
+  const int q = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (j >= probe_counts[q]) {
-    if (threadIdx.x == 0) {
-      part_counts[slot] = 0;
-      part_sat[slot] = kEmptyKey;
-    }
-    return;
-  }
-  const uint64_t list = probe_lists[slot];
-  const int64_t begin = list_offsets[list], end = list_offsets[list + 1];
   for (int i = threadIdx.x; i < chunks * 256; i += blockDim.x)
-    slut[i] = table[(int64_t)q * chunks * 256 + i];
-  if (threadIdx.x == 0) {
-    st.count = 0;
-    st.saturated = 0;
-    st.thr = kEmptyKey;
+    slut[i] = (LutT)table[(int64_t)q * chunks * 256 + i];
+  if (lane == 0) {
+    wst[warp].count = 0;
+    wst[warp].saturated = 0;
+    wst[warp].thr = kEmptyKey;
   }
+  if (threadIdx.x == 0) s_thr = kEmptyKey;
   __syncthreads();
-  for (int64_t base = begin; base < end; base += blockDim.x) {
-    const int64_t i = base + threadIdx.x;
-    if (i < end) {
-      const uint32_t pos = list_rows[i];
-      if (bitmap_pass(bitmap, pos)) {
-        float s;
-        if (!pq_lookup(slut, codes + (int64_t)pos * chunks, chunks, &s)) {
-          atomicOr(&q_flags[q], 8);
-        } else {
-          const uint64_t key = pack_rank(rank_from_score(metric, s), keyrank[pos]);
-          if (key < st.thr) {
-            const int at = atomicAdd(&st.count, 1);
-            buf[at] = key;
-          }
+  uint64_t* buf = wbuf + warp * CAPW;
+  AccumState* st = &wst[warp];
+  int cnt = 0;               // warp-uniform copies of st
+  uint64_t wthr = kEmptyKey;
+  const bool wide = chunks == 32;  // two 16-byte loads per code
+  const int nl = probe_counts[q];
+  for (int j = 0; j < nl; ++j) {
+    const uint64_t list = probe_lists[(int64_t)q * nprobe + j];
+    const int64_t begin = list_offsets[list], end = list_offsets[list + 1];
+    for (int64_t base = begin + (int64_t)warp * kStep; base < end;
+         base += (int64_t)kScanWarps * kStep) {
+      int64_t idx[kPer];
+      bool valid[kPer];
+      double sum[kPer];
+#pragma unroll
+      for (int u = 0; u < kPer; ++u) {
+        idx[u] = base + u * 32 + lane;
+        valid[u] = idx[u] < end;
+        if (bitmap && valid[u]) valid[u] = bitmap_pass(bitmap, list_rows[idx[u]]);
+        if (!valid[u]) idx[u] = begin;
+        sum[u] = 0.0;
+      }
+      if (wide) {
+        uint4 lo[kPer], hi[kPer];
+#pragma unroll
+        for (int u = 0; u < kPer; ++u) {
+          const uint4* cp = reinterpret_cast<const uint4*>(list_codes + idx[u] * 32);
+          lo[u] = __ldg(cp);
+          hi[u] = __ldg(cp + 1);
+        }
+#pragma unroll
+        for (int c = 0; c < 32; ++c)
+#pragma unroll
+          for (int u = 0; u < kPer; ++u)
+            sum[u] = __dadd_rn(sum[u], (double)slut[c * 256 + code_byte(lo[u], hi[u], c)]);
+      } else {
+#pragma unroll
+        for (int u = 0; u < kPer; ++u) {
+          const uint8_t* code = list_codes + idx[u] * chunks;
+          for (int c = 0; c < chunks; ++c)
+            sum[u] = __dadd_rn(sum[u], (double)slut[c * 256 + code[c]]);
         }
       }
+      const uint64_t shared_thr = *(volatile unsigned long long*)&s_thr;
+      const uint64_t thr = shared_thr < wthr ? shared_thr : wthr;
+#pragma unroll
+      for (int u = 0; u < kPer; ++u) {
+        bool take = false;
+        uint64_t key = 0;
+        if (valid[u]) {
+          const double sv = sum[u];
+          if (isnan(sv) || isinf(sv) || sv > 3.4028234663852886e38 ||
+              sv < -3.4028234663852886e38) {
+            atomicOr(&q_flags[q], 8);  // ErrPQScoreOverflow
+          } else {
+            const uint32_t ord = float_to_ordered(rank_from_score(metric, __double2float_rn(sv)));
+            if (ord <= (uint32_t)(thr >> 32)) {
+              key = ((uint64_t)ord << 32) | list_keyrank[idx[u]];
+              take = key < thr;
+            }
+          }
+        }
+        const unsigned m = __ballot_sync(kFullMask, take);
+        if (take) buf[cnt + __popc(m & ((1u << lane) - 1))] = key;
+        cnt += __popc(m);
+      }
+      if (cnt > CAPW - kStep) {
+        __syncwarp();
+        if (lane == 0) st->count = cnt;
+        __syncwarp();
+        warp_compact<CAPW>(buf, st, kp);
+        cnt = st->count;
+        wthr = st->thr;
+        if (lane == 0 && wthr != kEmptyKey) atomicMin(&s_thr, (unsigned long long)wthr);
+      }
     }
-    __syncthreads();
-    if (warp == 0 && st.count > CAP - (int)blockDim.x) warp_compact<CAP>(buf, &st, kp);
-    __syncthreads();
   }
-  if (warp == 0) {
-    warp_compact<CAP>(buf, &st, kp);
-    const int cnt = min(st.count, kp);
-    for (int i = lane; i < cnt; i += 32) part_keys[slot * kp + i] = buf[i];
-    if (lane == 0) {
-      part_counts[slot] = cnt;
-      part_sat[slot] = st.thr;
-    }
+  __syncwarp();
+  if (lane == 0) st->count = cnt;
+  __syncwarp();
+  warp_compact<CAPW>(buf, st, kp);
+  const int out = min(st->count, kp);
+  const int64_t slot = (int64_t)q * kScanWarps + warp;
+  for (int i = lane; i < out; i += 32) part_keys[slot * kp + i] = buf[i];
+  if (lane == 0) {
+    part_counts[slot] = out;
+    part_sat[slot] = st->thr;
   }
 }
 
@@ -257,6 +328,7 @@ xvec_gpu_status assign_rows(xvec_gpu_index* probe, const float* d_rows, int64_t 
   for (int64_t b = 0; b < n; b += kAssignBatch) {
     const int m = (int)std::min<int64_t>(kAssignBatch, n - b);
     std::vector<int> statuses;
+    NestedSearch nested;
     st = search_device_locked(probe, d_rows + b * d, m, o, nullptr, keys.as<uint64_t>(),
                               d_scores ? d_scores + b : scores.as<float>(), counts.as<int>(), s,
                               &statuses);
@@ -344,6 +416,26 @@ xvec_gpu_status ivfpq_commit(xvec_gpu_index* idx, int64_t old_n, int64_t m, cuda
 
 // CSR of positions per list; positions keep insertion order within a list
 // (ivf.go:193-201 appends in position order; the radix sort is stable).
+// List-major copies of the codes and key ranks, so a list scan streams
+// contiguous memory instead of gathering rows scattered in insertion order.
+__global__ void gather_list_major_kernel(const uint32_t* __restrict__ list_rows, int64_t n,
+                                         int chunks, const uint8_t* __restrict__ codes,
+                                         const uint32_t* __restrict__ keyrank,
+                                         uint8_t* __restrict__ list_codes,
+                                         uint32_t* __restrict__ list_keyrank) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const uint32_t pos = list_rows[i];
+  list_keyrank[i] = keyrank[pos];
+  if (chunks % 16 == 0) {
+    const uint4* src = reinterpret_cast<const uint4*>(codes + (int64_t)pos * chunks);
+    uint4* dst = reinterpret_cast<uint4*>(list_codes + i * chunks);
+    for (int c = 0; c < chunks / 16; ++c) dst[c] = src[c];
+  } else {
+    for (int c = 0; c < chunks; ++c) list_codes[i * chunks + c] = codes[(int64_t)pos * chunks + c];
+  }
+}
+
 static xvec_gpu_status rebuild_lists(xvec_gpu_index* idx, cudaStream_t s) {
   const int64_t n = idx->n;
   const int nlist = idx->nlist;
@@ -371,6 +463,16 @@ static xvec_gpu_status rebuild_lists(xvec_gpu_index* idx, cudaStream_t s) {
                                             idx->list_rows.as<uint32_t>(), n, 0, 32, s));
   XVEC_CUDA(cub::DeviceScan::ExclusiveSum(temp.ptr, tb2, counts.as<int64_t>(),
                                           idx->list_offsets.as<int64_t>(), nlist + 1, s));
+  const int chunks = idx->chunks;
+  if ((st = idx->list_codes.reserve((size_t)std::max<int64_t>(n, 1) * chunks, 0, s)) ||
+      (st = idx->list_keyrank.reserve((size_t)std::max<int64_t>(n, 1) * 4, 0, s)))
+    return st;
+  gather_list_major_kernel<<<blocks_of(n), 256, 0, s>>>(
+      idx->list_rows.as<uint32_t>(), n, chunks, idx->pq_codes.as<uint8_t>(),
+      idx->keyrank.as<uint32_t>(), idx->list_codes.as<uint8_t>(),
+      idx->list_keyrank.as<uint32_t>());
+  XVEC_LAUNCHED();
+  XVEC_CUDA(cudaGetLastError());
   XVEC_CUDA(cudaStreamSynchronize(s));
   idx->lists_dirty = false;
   return XVEC_GPU_OK;
@@ -386,6 +488,8 @@ xvec_gpu_status ivfpq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
   const int64_t n = idx->n;
   const int chunks = idx->chunks;
   xvec_gpu_status st;
+  EventTimer timer(s);
+  timer.mark(0);
   // The lists are rebuilt under the shared lock: only one searcher may do it.
   {
     static std::mutex rebuild_mu;
@@ -395,9 +499,8 @@ xvec_gpu_status ivfpq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
   const int nprobe = std::min(o.nprobe, idx->nlist);
   int kp = 32;
   while (kp < k + std::max(8, k / 4)) kp <<= 1;
-  if ((int64_t)nprobe * kp > flat_merge_capacity())
-    return set_error("nprobe %d x top_k %d exceeds the merge capacity", nprobe, k),
-           XVEC_GPU_INVALID_ARGUMENT;
+  if ((int64_t)kScanWarps * kp > flat_merge_capacity())
+    return set_error("top_k %d exceeds the merge capacity", k), XVEC_GPU_INVALID_ARGUMENT;
   // Probe: the Flat path over the centroids (validates the queries too).
   Scratch pkeys_probe, pscores_probe, pcounts_probe, table, qflags, qstatus;
   if ((st = pkeys_probe.alloc((size_t)nq * nprobe * 8, s)) ||
@@ -409,8 +512,12 @@ xvec_gpu_status ivfpq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
   xvec_gpu_search_opts po{};
   po.top_k = nprobe;
   std::vector<int> probe_status;
-  st = search_device_locked(idx->probe_index, d_q, nq, po, nullptr, pkeys_probe.as<uint64_t>(),
-                            pscores_probe.as<float>(), pcounts_probe.as<int>(), s, &probe_status);
+  {
+    NestedSearch nested;
+    st = search_device_locked(idx->probe_index, d_q, nq, po, nullptr, pkeys_probe.as<uint64_t>(),
+                              pscores_probe.as<float>(), pcounts_probe.as<int>(), s,
+                              &probe_status);
+  }
   if (st) return st;
   XVEC_CUDA(cudaMemcpyAsync(qstatus.ptr, probe_status.data(), (size_t)nq * 4,
                             cudaMemcpyHostToDevice, s));
@@ -421,36 +528,46 @@ xvec_gpu_status ivfpq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
                                      qflags.as<int>());
   XVEC_LAUNCHED();
   if (n > 0) {
-    int cap = 512;
-    while (cap < kp + 2 * 256) cap <<= 1;
+    int capw = 128;
+    while (capw < kp + 64) capw <<= 1;
+    if (capw > 1024) return set_error("top_k %d too large for the IVF-PQ scan", k), XVEC_GPU_INVALID_ARGUMENT;
     Scratch lkeys, lcounts, lsat;
-    const size_t lists = (size_t)nq * nprobe;
+    const size_t lists = (size_t)nq * kScanWarps;
     if ((st = lkeys.alloc(lists * kp * 8, s)) || (st = lcounts.alloc(lists * 4, s)) ||
         (st = lsat.alloc(lists * 8, s)))
       return st;
-    const size_t smem = (size_t)chunks * 256 * 4 + (size_t)cap * 8;
-    dim3 grid(nq, nprobe);
-#define XVEC_PQ_CASE(C)                                                                        \
-  if (cap == C) {                                                                              \
-    auto kern = ivfpq_scan_kernel<C>;                                                          \
+    // The table as float64 in shared memory when it fits next to the buffers.
+    const size_t bufs = (size_t)kScanWarps * capw * 8;
+    const bool lut64 = (size_t)chunks * 256 * 8 + bufs <= 200 * 1024;
+    const size_t smem = (size_t)chunks * 256 * (lut64 ? 8 : 4) + bufs;
+    if (smem > 220 * 1024) return set_error("too many PQ chunks for the scan"), XVEC_GPU_UNSUPPORTED;
+    timer.mark(1);
+#define XVEC_PQ_CASE(C, T)                                                                     \
+  if (capw == C && lut64 == (sizeof(T) == 8)) {                                                \
+    auto kern = ivfpq_scan_kernel<C, T>;                                                       \
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);        \
-    kern<<<grid, 256, smem, s>>>(table.as<float>(), chunks, idx->pq_codes.as<uint8_t>(),       \
-                                 pkeys_probe.as<uint64_t>(), pcounts_probe.as<int>(), nprobe,  \
-                                 idx->list_offsets.as<int64_t>(), idx->list_rows.as<uint32_t>(), \
-                                 idx->keyrank.as<uint32_t>(), d_bitmap, metric, kp,            \
-                                 lkeys.as<uint64_t>(), lcounts.as<int>(), lsat.as<uint64_t>(), \
-                                 qflags.as<int>());                                            \
+    kern<<<nq, kScanWarps * 32, smem, s>>>(                                                    \
+        table.as<float>(), chunks, idx->list_codes.as<uint8_t>(), pkeys_probe.as<uint64_t>(),  \
+        pcounts_probe.as<int>(), nprobe, idx->list_offsets.as<int64_t>(),                      \
+        idx->list_rows.as<uint32_t>(), idx->list_keyrank.as<uint32_t>(), d_bitmap, metric, kp, \
+        lkeys.as<uint64_t>(), lcounts.as<int>(), lsat.as<uint64_t>(), qflags.as<int>());       \
   }
-    XVEC_PQ_CASE(1024)
-    XVEC_PQ_CASE(2048)
+    XVEC_PQ_CASE(128, double)
+    XVEC_PQ_CASE(256, double)
+    XVEC_PQ_CASE(512, double)
+    XVEC_PQ_CASE(1024, double)
+    XVEC_PQ_CASE(128, float)
+    XVEC_PQ_CASE(256, float)
+    XVEC_PQ_CASE(512, float)
+    XVEC_PQ_CASE(1024, float)
 #undef XVEC_PQ_CASE
-    if (cap > 2048) return set_error("top_k %d too large for the IVF-PQ scan", k), XVEC_GPU_INVALID_ARGUMENT;
+    timer.mark(2);
     XVEC_LAUNCHED();
     XVEC_CUDA(cudaGetLastError());
     PQScorer sc{metric, table.as<float>(), idx->pq_codes.as<uint8_t>(), chunks};
     XVEC_CUDA(launch_merge_rescore(sc, idx->pos_of_kr.as<uint32_t>(), idx->keys.as<uint64_t>(),
                                    nullptr, nq, k, o.radius, 1, lkeys.as<uint64_t>(),
-                                   lcounts.as<int>(), lsat.as<uint64_t>(), nprobe, kp, d_keys,
+                                   lcounts.as<int>(), lsat.as<uint64_t>(), kScanWarps, kp, d_keys,
                                    d_scores, d_counts, nullptr, qflags.as<int>(), s));
     XVEC_LAUNCHED();
   }
@@ -460,8 +577,9 @@ xvec_gpu_status ivfpq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
   XVEC_CUDA(cudaGetLastError());
   std::vector<int> h_flags(nq);
   XVEC_CUDA(cudaMemcpyAsync(h_flags.data(), qflags.ptr, (size_t)nq * 4, cudaMemcpyDeviceToHost, s));
+  timer.mark(3);
   XVEC_CUDA(cudaStreamSynchronize(s));
-  count_search(nq, 0, 0, 0);
+  count_search(nq, 0, timer.ms(1, 2), timer.ms(0, 3));
   if (statuses) {
     statuses->resize(nq);
     for (int q = 0; q < nq; ++q) {

@@ -20,7 +20,12 @@ std::atomic<int> g_timing{0};
 
 void count_launches(int64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 void count_tensor_scan() { g_tensor.fetch_add(1); }
+thread_local int g_nested = 0;
+void nested_search_enter() { ++g_nested; }
+void nested_search_leave() { --g_nested; }
+
 void count_search(int64_t queries, int64_t exact_queries, double scan_ms, double search_ms) {
+  if (g_nested > 0) return;
   g_searches.fetch_add(1);
   g_queries.fetch_add(queries);
   g_exact.fetch_add(exact_queries);

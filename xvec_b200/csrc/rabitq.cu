@@ -548,6 +548,7 @@ xvec_gpu_status rabitq_assign(xvec_gpu_index* idx, const float* prepared, int64_
   for (int64_t b = 0; b < m; b += batch) {
     const int cnt = (int)std::min<int64_t>(batch, m - b);
     std::vector<int> statuses;
+    NestedSearch nested;
     st = search_device_locked(idx->probe_index, prepared + b * d, cnt, o, nullptr,
                               keys.as<uint64_t>(), scores.as<float>(), counts.as<int>(), s,
                               &statuses);
@@ -570,6 +571,8 @@ xvec_gpu_status rabitq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq
                                    const xvec_gpu_search_opts& o, const uint32_t* d_bitmap,
                                    uint64_t* d_keys, float* d_scores, int* d_counts,
                                    cudaStream_t s, std::vector<int>* statuses) {
+  EventTimer timer(s);
+  timer.mark(0);
   // hnsw_rabitq.go:548-550, 573-579.
   if (o.ef <= 0 || o.ef > 2048)
     return set_error("core: invalid HNSW ef %d (want 1..2048)", o.ef), XVEC_GPU_INVALID_ARGUMENT;
@@ -629,10 +632,12 @@ xvec_gpu_status rabitq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq
         (st = psat.alloc((size_t)nq * parts * 8, s)))
       return st;
     const RaBitQRanker rk{idx->rq_fast.as<float4>(), qfs.as<float>(), qfg.as<float>(), nc};
+    timer.mark(1);
     XVEC_CUDA(launch_scan_simt(reinterpret_cast<const BitElem*>(idx->rq_codes.ptr), n, padded,
                                idx->keyrank.as<uint32_t>(), qrot.as<float>(), nq, d_bitmap, rk,
                                parts, kp, pkeys.as<uint64_t>(), pcounts.as<int>(),
                                psat.as<uint64_t>(), qflags.as<int>(), s));
+    timer.mark(2);
     XVEC_CUDA(launch_merge_rescore(sc, idx->pos_of_kr.as<uint32_t>(), idx->keys.as<uint64_t>(),
                                    nullptr, nq, cc, stage_radius, 0, pkeys.as<uint64_t>(),
                                    pcounts.as<int>(), psat.as<uint64_t>(), parts, kp, o_keys,
@@ -717,8 +722,9 @@ xvec_gpu_status rabitq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq
   std::vector<int> h_rs(nq, 0);
   XVEC_CUDA(cudaMemcpyAsync(h_flags.data(), qflags.ptr, (size_t)nq * 4, cudaMemcpyDeviceToHost, s));
   if (rs) XVEC_CUDA(cudaMemcpyAsync(h_rs.data(), rs, (size_t)nq * 4, cudaMemcpyDeviceToHost, s));
+  timer.mark(3);
   XVEC_CUDA(cudaStreamSynchronize(s));
-  count_search(nq, (int64_t)exact_list.size(), 0, 0);
+  count_search(nq, (int64_t)exact_list.size(), timer.ms(1, 2), timer.ms(0, 3));
   if (statuses) {
     statuses->resize(nq);
     for (int q = 0; q < nq; ++q) (*statuses)[q] = rabitq_query_status(h_status[q], h_flags[q], h_rs[q]);

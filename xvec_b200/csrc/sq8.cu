@@ -337,6 +337,8 @@ xvec_gpu_status sq8_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
                                 const xvec_gpu_search_opts& o, const uint32_t* d_bitmap,
                                 uint64_t* d_keys, float* d_scores, int* d_counts, cudaStream_t s,
                                 std::vector<int>* statuses) {
+  EventTimer timer(s);
+  timer.mark(0);
   const int d = idx->desc.dimension, metric = idx->desc.metric;
   const int64_t n = idx->n;
   const bool refine = o.refine_scale > 0;
@@ -400,9 +402,11 @@ xvec_gpu_status sq8_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
         (st = psat.alloc((size_t)nq * parts * 8, s)))
       return st;
     const SQ8Ranker rk{metric, idx->sq_fast.as<float4>(), qinfo.as<float4>()};
+    timer.mark(1);
     XVEC_CUDA(launch_scan_simt(idx->sq_codes.as<int8_t>(), n, d, idx->keyrank.as<uint32_t>(),
                                qf.as<float>(), nq, d_bitmap, rk, parts, kp, pkeys.as<uint64_t>(),
                                pcounts.as<int>(), psat.as<uint64_t>(), qflags.as<int>(), s));
+    timer.mark(2);
     XVEC_CUDA(launch_merge_rescore(sc, idx->pos_of_kr.as<uint32_t>(), idx->keys.as<uint64_t>(),
                                    nullptr, nq, stage_k, stage_radius, 0, pkeys.as<uint64_t>(),
                                    pcounts.as<int>(), psat.as<uint64_t>(), parts, kp, o_keys,
@@ -462,8 +466,9 @@ xvec_gpu_status sq8_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
   XVEC_LAUNCHED();
   XVEC_CUDA(cudaGetLastError());
   XVEC_CUDA(cudaMemcpyAsync(h_flags.data(), qflags.ptr, (size_t)nq * 4, cudaMemcpyDeviceToHost, s));
+  timer.mark(3);
   XVEC_CUDA(cudaStreamSynchronize(s));
-  count_search(nq, (int64_t)exact_list.size(), 0, 0);
+  count_search(nq, (int64_t)exact_list.size(), timer.ms(1, 2), timer.ms(0, 3));
   if (statuses) {
     statuses->resize(nq);
     for (int q = 0; q < nq; ++q) {
