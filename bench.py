@@ -44,12 +44,15 @@ def parse():
     p.add_argument("--n", type=int, default=N_BASE)
     p.add_argument("--nq", type=int, default=N_QUERIES)
     p.add_argument("--cpu-sample-rows", type=int, default=1_000_000)
-    p.add_argument("--cpu-sample-queries", type=int, default=32)
+    p.add_argument("--cpu-sample-queries", type=int, default=480)
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--workload", choices=["flat_cosine_fp16", "ivfpq_l2"],
+    p.add_argument("--workload",
+                   choices=["flat_cosine_fp16", "ivfpq_l2", "sq8_ip_refine", "rabitq_l2_refine"],
                    default="flat_cosine_fp16",
                    help="flat_cosine_fp16: the Flat configuration above (default); ivfpq_l2: "
-                        "IVF-PQ L2, 1e8 x 128, nlist 16384, 32 x 256 PQ, nprobe 64, k=10")
+                        "IVF-PQ L2, 1e8 x 128, nlist 16384, 32 x 256 PQ, nprobe 64, k=10; "
+                        "sq8_ip_refine: INT8 SQ Flat IP, 2e7 x 1024, k=10, ScaleFactor 4; "
+                        "rabitq_l2_refine: one-bit RaBitQ L2, 1e7 x 960, k=10, EF 100")
     return p.parse_args()
 
 
@@ -258,6 +261,7 @@ def run_ivfpq(args):
     index = xb.IVFPQIndex(PQ_DIM, xb.METRIC_L2, device=local)
     index.set_model(cents.cpu().numpy(), pivots.cpu().numpy(), PQ_CHUNKS)
     b, e = shard_range(n, rank, world, align=PQ_CHUNK_ROWS)
+    index.reserve(e - b)
     sizes = torch.zeros(PQ_NLIST, dtype=torch.int64, device=dev)
     labels = torch.empty(PQ_CHUNK_ROWS, dtype=torch.int32, device=dev)
     stream = torch.cuda.current_stream().cuda_stream
@@ -280,8 +284,58 @@ def run_ivfpq(args):
     h_sizes = sizes.cpu().numpy()
     scanned = int(h_sizes[pr.keys.astype(np.int64)].sum())
     probe.close()
-    search = ShardedSearch(index)
     opts = xb.SearchOptions(top_k=PQ_K, nprobe=PQ_NPROBE)
+    ms, scan_ms, e2e_ms, st, clocks = time_search(ShardedSearch(index), queries, opts, args, dev,
+                                                  world, local)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_ivfpq_qps(cents.cpu().numpy(), pivots.cpu().numpy(), h_sizes,
+                            queries[:args.cpu_sample_queries].cpu().numpy())
+    if rank == 0:
+        _, hbm_peak, peak_kind = peaks()
+        nbytes = scanned * PQ_CHUNKS
+        achieved = nbytes / (scan_ms / 1000.0) / 1e9 if scan_ms > 0 else None
+        line = {
+            "metric": METRIC, "value": nq / (ms / 1000.0), "unit": "queries/sec",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "u8 codes, f32 tables, f64 sums", "data": "synthetic",
+            "config": {"workload": PQ_WORKLOAD, "global_batch": nq, "top_k": PQ_K,
+                       "base_vectors": n, "dim": PQ_DIM, "metric": "l2", "nlist": PQ_NLIST,
+                       "pq_chunks": PQ_CHUNKS, "nprobe": PQ_NPROBE,
+                       "model": "seeded mixture draws stand in for the k-means centroids and "
+                                "PQ codebook",
+                       "parallelism": f"rows sharded over {world} GPU(s), NCCL all-gather + merge",
+                       "l2": "inputs larger than L2 (3.2 GB codes, 51 GB originals)"},
+            "e2e": {"value": nq / (e2e_ms / 1000.0), "unit": "queries/sec",
+                    "h2d_bytes_per_step": nq * PQ_DIM * 4,
+                    "d2h_bytes_per_step": nq * PQ_K * 12 + nq * 4},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": (achieved / hbm_peak) if achieved else None, "traffic": None,
+                         "peak_source": f"{peak_kind} HBM copy bandwidth",
+                         "kernel": "IVF-PQ list scan", "kernel_ms": scan_ms,
+                         "algorithmic_bytes_per_launch": nbytes,
+                         "scanned_codes_per_launch": scanned},
+            "cpu_baseline": cpu,
+            "clocks": clocks,
+            "gpu_launches": int(st["kernel_launches"]),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def time_search(search, queries, opts, args, dev, world, local):
+    """W warm-up searches, then K timed ones between barriers (CUDA events on
+    the stream, max over ranks, clocks sampled meanwhile), then K end-to-end
+    searches from pinned host queries.  Returns (ms, scan_ms, e2e_ms, stats,
+    clocks); scan_ms is the library's device time of the candidate scan."""
+    import torch
+    import torch.distributed as dist
+
+    import xvec_b200 as xb
 
     def barrier():
         if world > 1:
@@ -321,44 +375,210 @@ def run_ivfpq(args):
         t = torch.tensor([e2e_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
+    return ms, scan_ms, e2e_ms, st, clocks.summary()
 
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_ivfpq_qps(cents.cpu().numpy(), pivots.cpu().numpy(), h_sizes,
-                            queries[:args.cpu_sample_queries].cpu().numpy())
-    if rank == 0:
-        _, hbm_peak, peak_kind = peaks()
-        nbytes = scanned * PQ_CHUNKS
-        achieved = nbytes / (scan_ms / 1000.0) / 1e9 if scan_ms > 0 else None
-        line = {
-            "metric": METRIC, "value": nq / (ms / 1000.0), "unit": "queries/sec",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "u8 codes, f32 tables, f64 sums", "data": "synthetic",
-            "config": {"workload": PQ_WORKLOAD, "global_batch": nq, "top_k": PQ_K,
-                       "base_vectors": n, "dim": PQ_DIM, "metric": "l2", "nlist": PQ_NLIST,
-                       "pq_chunks": PQ_CHUNKS, "nprobe": PQ_NPROBE,
-                       "model": "seeded mixture draws stand in for the k-means centroids and "
-                                "PQ codebook",
-                       "parallelism": f"rows sharded over {world} GPU(s), NCCL all-gather + merge",
-                       "l2": "inputs larger than L2 (3.2 GB codes, 51 GB originals)"},
-            "e2e": {"value": nq / (e2e_ms / 1000.0), "unit": "queries/sec",
-                    "h2d_bytes_per_step": nq * PQ_DIM * 4,
-                    "d2h_bytes_per_step": nq * PQ_K * 12 + nq * 4},
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                         "frac": (achieved / hbm_peak) if achieved else None, "traffic": None,
-                         "peak_source": f"{peak_kind} HBM copy bandwidth",
-                         "kernel": "IVF-PQ list scan", "kernel_ms": scan_ms,
-                         "algorithmic_bytes_per_launch": nbytes,
-                         "scanned_codes_per_launch": scanned},
-            "cpu_baseline": cpu,
-            "clocks": clocks.summary(),
-            "gpu_launches": int(st["kernel_launches"]),
-        }
-        print(json.dumps(line), flush=True)
+
+def init_ranks(args):
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
+    return world, rank, local, dev
+
+
+def finish_ranks(world):
+    import torch.distributed as dist
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def common_line(nq, ms, e2e_ms, args, world, dtype, config, roofline, cpu, clocks, st, k, d,
+                q_bytes):
+    return {
+        "metric": METRIC, "value": nq / (ms / 1000.0), "unit": "queries/sec", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": dtype,
+        "data": "synthetic", "config": config,
+        "e2e": {"value": nq / (e2e_ms / 1000.0), "unit": "queries/sec",
+                "h2d_bytes_per_step": nq * d * q_bytes, "d2h_bytes_per_step": nq * k * 12 + nq * 4},
+        "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks,
+        "gpu_launches": int(st["kernel_launches"]),
+    }
+
+
+# ---------------------------------------------------------------------------
+# INT8 scalar-quantized Flat, inner product, FP32 refinement: 20,000,000 x
+# 1024, N(0,1) scaled per dimension by U(0.5, 2) (seeded), per-vector INT8
+# codes; 10,000 queries; top-k 10 with ScaleFactor 4 (40 codes refined).
+# ---------------------------------------------------------------------------
+SQ_N, SQ_DIM, SQ_K, SQ_SCALE, SQ_CHUNK_ROWS = 20_000_000, 1024, 10, 4.0, 500_000
+SQ_WORKLOAD = ("INT8 scalar-quantized Flat IP search with FP32 refinement, 20,000,000 x 1024 "
+               "(N(0,1) x per-dimension U(0.5,2)), 10,000 queries, top-k=10, ScaleFactor 4")
+
+
+def sq_rows(torch, scale, tag, rows, device):
+    g = torch.Generator(device=device).manual_seed(9_000_011 + tag)
+    return torch.randn(rows, scale.shape[0], generator=g, device=device) * scale
+
+
+def run_sq8(args):
+    import numpy as np
+    import torch
+
+    import xvec_b200 as xb
+    from xvec_b200.sharded import ShardedSearch, shard_range
+    world, rank, local, dev = init_ranks(args)
+    n = args.n if args.n != N_BASE else SQ_N
+    nq = args.nq
+    g = torch.Generator(device=dev).manual_seed(77)
+    scale = torch.rand(SQ_DIM, generator=g, device=dev) * 1.5 + 0.5
+    index = xb.ScalarQuantizedFlatIndex(SQ_DIM, xb.METRIC_IP, device=local)
+    b, e = shard_range(n, rank, world, align=SQ_CHUNK_ROWS)
+    index.reserve(e - b)
+    stream = torch.cuda.current_stream().cuda_stream
+    for c0 in range(b, e, SQ_CHUNK_ROWS):
+        m = min(SQ_CHUNK_ROWS, e - c0)
+        rows = sq_rows(torch, scale, c0 // SQ_CHUNK_ROWS, m, dev).contiguous()
+        keys = torch.arange(c0, c0 + m, dtype=torch.int64, device=dev)
+        index.add_device(keys.data_ptr(), rows.data_ptr(), m, stream)
+        del rows, keys
+    queries = sq_rows(torch, scale, 10**6, nq, dev).contiguous()
+    torch.cuda.synchronize()
+    opts = xb.SearchOptions(top_k=SQ_K, refine_scale=SQ_SCALE)
+    ms, scan_ms, e2e_ms, st, clocks = time_search(ShardedSearch(index), queries, opts, args, dev,
+                                                  world, local)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        m = min(args.cpu_sample_rows // 10, n)
+        sample = sq_rows(torch, scale, 0, m, dev).cpu().numpy()
+        cpu = cpu_sq8_qps(sample, queries[:max(8, args.cpu_sample_queries // 8)].cpu().numpy(), n)
+    if rank == 0:
+        shard = e - b
+        ops = 2.0 * nq * shard * SQ_DIM
+        achieved = ops / (scan_ms / 1000.0) / 1e12 if scan_ms > 0 else None
+        peak = 4500.0
+        roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOP/s",
+                "frac": (achieved / peak) if achieved else None, "traffic": None,
+                "peak_source": "nominal dense INT8 tensor (no measured INT8 figure); the scan "
+                               "runs on FP32 FFMA over the INT8 codes",
+                "kernel": "SQ8 code scan", "kernel_ms": scan_ms,
+                "algorithmic_int_ops_per_launch": ops}
+        config = {"workload": SQ_WORKLOAD, "global_batch": nq, "top_k": SQ_K, "base_vectors": n,
+                  "dim": SQ_DIM, "metric": "ip", "refine_scale": SQ_SCALE,
+                  "parallelism": f"rows sharded over {world} GPU(s), NCCL all-gather + merge",
+                  "l2": "inputs larger than L2 (20 GB codes)"}
+        print(json.dumps(common_line(nq, ms, e2e_ms, args, world, "i8 codes, f32/f64 scores",
+                                     config, roof, cpu, clocks, st, SQ_K, SQ_DIM, 4)), flush=True)
+    finish_ranks(world)
+
+
+def cpu_sq8_qps(sample, queries, n_total):
+    import numpy as np
+
+    from oracle.oracle import IP, Oracle
+    ora = Oracle()
+    codes, params = ora.quantize_int8_batch(sample)
+    keys = np.arange(sample.shape[0], dtype=np.uint64)
+    threads = os.cpu_count() or 1
+    t0 = time.perf_counter()
+    ora.sq8_search(IP, codes, params, sample, keys, queries, SQ_K, 0.0, SQ_SCALE, threads=threads)
+    dt = time.perf_counter() - t0
+    return {"value": queries.shape[0] / dt * sample.shape[0] / n_total, "unit": "queries/sec",
+            "cores": threads, "kind": "port",
+            "sample": f"{queries.shape[0]} queries x {sample.shape[0]}-row sample, {dt:.1f} s on "
+                      f"{threads} threads; QPS scaled by rows/{n_total}"}
+
+
+# ---------------------------------------------------------------------------
+# One-bit RaBitQ, L2, exact FP32 refinement: 10,000,000 x 960 from a
+# 1,000-cluster mixture (not normalised); 16 clusters and seeded rotation
+# signs; 10,000 queries; top-k 10 with EF 100 (10x over-fetch) and Refine.
+# ---------------------------------------------------------------------------
+RQ_N, RQ_DIM, RQ_NC, RQ_K, RQ_EF, RQ_CHUNK_ROWS = 10_000_000, 960, 16, 10, 100, 500_000
+RQ_WORKLOAD = ("RaBitQ 1-bit L2 search with exact FP32 refinement, 10,000,000 x 960 "
+               "(1,000-cluster mixture), 16 clusters, 10,000 queries, top-k=10, EF 100")
+
+
+def run_rabitq(args):
+    import numpy as np
+    import torch
+
+    import xvec_b200 as xb
+    from xvec_b200.sharded import ShardedSearch, shard_range
+    world, rank, local, dev = init_ranks(args)
+    n = args.n if args.n != N_BASE else RQ_N
+    nq = args.nq
+    g = torch.Generator(device=dev).manual_seed(960)
+    centers = torch.randn(CLUSTERS, RQ_DIM, generator=g, device=dev)
+    cents = pq_mixture(torch, centers, 10**6 + 11, RQ_NC, dev).contiguous()
+    padded = (RQ_DIM + 63) // 64 * 64
+    signs = np.random.default_rng(961).integers(0, 256, 4 * padded // 8, dtype=np.uint8)
+    index = xb.RaBitQIndex(RQ_DIM, xb.METRIC_L2, device=local)
+    index.set_model(cents.cpu().numpy(), signs)
+    b, e = shard_range(n, rank, world, align=RQ_CHUNK_ROWS)
+    index.reserve(e - b)
+    stream = torch.cuda.current_stream().cuda_stream
+    for c0 in range(b, e, RQ_CHUNK_ROWS):
+        m = min(RQ_CHUNK_ROWS, e - c0)
+        rows = pq_mixture(torch, centers, 2 * 10**6 + c0 // RQ_CHUNK_ROWS, m, dev).contiguous()
+        keys = torch.arange(c0, c0 + m, dtype=torch.int64, device=dev)
+        index.add_device(keys.data_ptr(), rows.data_ptr(), m, stream)
+        del rows, keys
+    queries = pq_mixture(torch, centers, 3 * 10**6, nq, dev).contiguous()
+    torch.cuda.synchronize()
+    opts = xb.SearchOptions(top_k=RQ_K, ef=RQ_EF, refine=True)
+    ms, scan_ms, e2e_ms, st, clocks = time_search(ShardedSearch(index), queries, opts, args, dev,
+                                                  world, local)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        m = min(args.cpu_sample_rows // 50, n)
+        sample = pq_mixture(torch, centers, 2 * 10**6, m, dev).cpu().numpy()
+        cpu = cpu_rabitq_qps(cents.cpu().numpy(), signs, sample,
+                             queries[:max(8, args.cpu_sample_queries // 4)].cpu().numpy(), n)
+    if rank == 0:
+        bf16_peak, _, peak_kind = peaks()
+        flops = 2.0 * nq * (e - b) * padded
+        achieved = flops / (scan_ms / 1000.0) / 1e12 if scan_ms > 0 else None
+        roof = {"bound": "tensor", "achieved": achieved, "peak": bf16_peak, "unit": "TFLOP/s",
+                "frac": (achieved / bf16_peak) if achieved else None, "traffic": None,
+                "peak_source": f"{peak_kind} sustained bf16 dense GEMM; the bit scan runs on "
+                               "FP32 FFMA",
+                "kernel": "RaBitQ bit scan", "kernel_ms": scan_ms,
+                "algorithmic_flops_per_launch": flops}
+        config = {"workload": RQ_WORKLOAD, "global_batch": nq, "top_k": RQ_K, "base_vectors": n,
+                  "dim": RQ_DIM, "metric": "l2", "clusters": RQ_NC, "ef": RQ_EF,
+                  "parallelism": f"rows sharded over {world} GPU(s), NCCL all-gather + merge",
+                  "l2": "inputs larger than L2 (1.2 GB codes, 38 GB originals)"}
+        print(json.dumps(common_line(nq, ms, e2e_ms, args, world, "1-bit codes, f32/f64 estimates",
+                                     config, roof, cpu, clocks, st, RQ_K, RQ_DIM, 4)), flush=True)
+    finish_ranks(world)
+
+
+def cpu_rabitq_qps(cents, signs, sample, queries, n_total):
+    import numpy as np
+
+    from oracle.oracle import L2, Oracle
+    ora = Oracle()
+    codes, factors = ora.rabitq_encode1_batch(L2, cents, signs, sample)
+    keys = np.arange(sample.shape[0], dtype=np.uint64)
+    threads = os.cpu_count() or 1
+    t0 = time.perf_counter()
+    ora.rabitq_search(L2, cents, signs, codes, factors, sample, keys, queries, RQ_K, RQ_EF,
+                      threads=threads)
+    dt = time.perf_counter() - t0
+    return {"value": queries.shape[0] / dt * sample.shape[0] / n_total, "unit": "queries/sec",
+            "cores": threads, "kind": "port",
+            "sample": f"{queries.shape[0]} queries x {sample.shape[0]}-row sample, {dt:.1f} s on "
+                      f"{threads} threads; QPS scaled by rows/{n_total}"}
 
 
 def cpu_ivfpq_qps(cents, pivots, list_sizes, queries):
@@ -395,6 +615,10 @@ def main():
         return run_reference(args)
     if args.workload == "ivfpq_l2":
         return run_ivfpq(args)
+    if args.workload == "sq8_ip_refine":
+        return run_sq8(args)
+    if args.workload == "rabitq_l2_refine":
+        return run_rabitq(args)
 
     import numpy as np
     import torch
@@ -420,6 +644,7 @@ def main():
     my_chunks = range(rank * per_rank, min(chunks, (rank + 1) * per_rank))
     centers = mixture_centers(torch, dev)
     index = xb.DenseFlatIndex(DIM, xb.METRIC_COSINE, xb.STORAGE_FP16, device=local)
+    index.reserve(sum(min(CHUNK, n - c * CHUNK) for c in my_chunks))
     for c in my_chunks:
         rows = mixture_chunk(torch, centers, c, min(CHUNK, n - c * CHUNK), dev)
         keys = torch.arange(c * CHUNK, c * CHUNK + rows.shape[0], dtype=torch.int64, device=dev)

@@ -133,6 +133,12 @@ int32_t xvec_gpu_device_count(void);
 xvec_gpu_status xvec_gpu_index_create(const xvec_gpu_index_desc* desc, xvec_gpu_index** out);
 xvec_gpu_status xvec_gpu_index_destroy(xvec_gpu_index* index);
 int64_t xvec_gpu_index_len(const xvec_gpu_index* index);
+/* Pre-sizes the index for `capacity` rows, like make([]T, 0, capacity) for
+ * the slices the reference grows by append (flat.go:148-152); no reference
+ * call corresponds.  Growing happens anyway on add, but growing a buffer
+ * needs its old and new copies at once, so a caller that knows the final
+ * size of a large index reserves it first. */
+xvec_gpu_status xvec_gpu_index_reserve(xvec_gpu_index* index, int64_t capacity);
 
 /* Appends n rows at positions len..len+n-1 (DenseFlatIndex.Add, flat.go:122-153;
  * batch form).  rows: n*dimension float32, or uint16 for FP16 storage.  Keys

@@ -50,7 +50,7 @@ EXPORTED_SYMBOLS = (
     "xvec_gpu_rabitq_set_model", "xvec_gpu_index_search", "xvec_gpu_index_search_device",
     "xvec_gpu_kmeans_assign", "xvec_gpu_kmeans_assign_device", "xvec_gpu_merge_results_device",
     "xvec_gpu_stats_enable_timing", "xvec_gpu_get_stats", "xvec_gpu_reset_stats",
-    "xvec_gpu_index_search_noalloc",
+    "xvec_gpu_index_search_noalloc", "xvec_gpu_index_reserve",
 )
 
 
@@ -83,7 +83,7 @@ class Stats(ctypes.Structure):
 
 def _load() -> ctypes.CDLL:
     if not os.path.exists(LIB_PATH):
-        raise ImportError(f"{LIB_PATH} is missing: run `python -m xvec_b200.build` "
+        raise ImportError(f"{LIB_PATH} is missing: run `python xvec_b200/build.py` "
                           "(or __graft_entry__.build()) first")
     lib = ctypes.CDLL(LIB_PATH)
     vp, i32, i64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64
@@ -104,6 +104,7 @@ def _load() -> ctypes.CDLL:
                                                  vp, vp]
     lib.xvec_gpu_kmeans_assign.argtypes = [i32, i32, vp, i64, vp, i32, i32, vp, vp]
     lib.xvec_gpu_kmeans_assign_device.argtypes = [i32, i32, vp, i64, vp, i32, i32, vp, vp, vp]
+    lib.xvec_gpu_index_reserve.argtypes = [vp, i64]
     lib.xvec_gpu_merge_results_device.argtypes = [i32, i32, i32, i32, i32, vp, vp, vp, vp, vp,
                                                   vp, vp]
     lib.xvec_gpu_index_search_noalloc.argtypes = [vp, vp, i32, ctypes.POINTER(SearchOpts), vp,
@@ -218,6 +219,10 @@ class _Index:
 
     def _row_dtype(self):
         return np.uint16 if self.storage == STORAGE_FP16 else np.float32
+
+    def reserve(self, capacity: int) -> None:
+        """Pre-sizes the index for `capacity` rows (xvec_gpu_index_reserve)."""
+        _check(_lib.xvec_gpu_index_reserve(self._h, capacity))
 
     def add(self, keys, vectors) -> None:
         """Batch form of DenseFlatIndex.Add (flat.go:122-153)."""

@@ -431,6 +431,24 @@ size_t query_elem_bytes(const xvec_gpu_index* idx) {
 // ---------------------------------------------------------------------------
 // Insertion.
 // ---------------------------------------------------------------------------
+// Grows every per-row buffer to `cap` rows, keeping the rows already stored
+// (each buffer briefly exists twice while it is copied).
+static xvec_gpu_status grow_locked(xvec_gpu_index* idx, int64_t cap, cudaStream_t s) {
+  const int64_t old_n = idx->n;
+  const size_t in_row_bytes = (size_t)idx->desc.dimension * query_elem_bytes(idx);
+  xvec_gpu_status st;
+  if ((st = idx->rows.reserve((size_t)cap * in_row_bytes, (size_t)old_n * in_row_bytes, s)) ||
+      (st = idx->keys.reserve((size_t)cap * 8, (size_t)old_n * 8, s)) ||
+      (st = idx->row_n2.reserve((size_t)cap * 4, (size_t)old_n * 4, s)) ||
+      (st = idx->row_inv.reserve((size_t)cap * 4, (size_t)old_n * 4, s)) ||
+      (st = idx->keyrank.reserve((size_t)cap * 4, (size_t)old_n * 4, s)) ||
+      (st = idx->pos_of_kr.reserve((size_t)cap * 4, (size_t)old_n * 4, s)))
+    return st;
+  if ((st = extra_reserve(idx, cap, s))) return st;
+  idx->capacity = cap;
+  return XVEC_GPU_OK;
+}
+
 xvec_gpu_status add_device_locked(xvec_gpu_index* idx, const uint64_t* d_keys, const void* d_rows,
                                   int64_t m, cudaStream_t s) {
   const int d = idx->desc.dimension;
@@ -439,17 +457,9 @@ xvec_gpu_status add_device_locked(xvec_gpu_index* idx, const uint64_t* d_keys, c
   if (new_n > 0xffffffffll) return set_error("index capacity exceeded"), XVEC_GPU_INVALID_ARGUMENT;
   const size_t in_row_bytes = (size_t)d * query_elem_bytes(idx);
   if (new_n > idx->capacity) {
-    int64_t cap = std::max<int64_t>(new_n, idx->capacity + idx->capacity / 2);
-    xvec_gpu_status st;
-    if ((st = idx->rows.reserve((size_t)cap * in_row_bytes, (size_t)old_n * in_row_bytes, s)) ||
-        (st = idx->keys.reserve((size_t)cap * 8, (size_t)old_n * 8, s)) ||
-        (st = idx->row_n2.reserve((size_t)cap * 4, (size_t)old_n * 4, s)) ||
-        (st = idx->row_inv.reserve((size_t)cap * 4, (size_t)old_n * 4, s)) ||
-        (st = idx->keyrank.reserve((size_t)cap * 4, (size_t)old_n * 4, s)) ||
-        (st = idx->pos_of_kr.reserve((size_t)cap * 4, (size_t)old_n * 4, s)))
-      return st;
-    if ((st = extra_reserve(idx, cap, s))) return st;
-    idx->capacity = cap;
+    xvec_gpu_status st =
+        grow_locked(idx, std::max<int64_t>(new_n, idx->capacity + idx->capacity / 2), s);
+    if (st) return st;
   }
   if (!idx->max_n2.ptr) {
     xvec_gpu_status st = idx->max_n2.reserve(4, 0, s);
@@ -599,6 +609,17 @@ extern "C" xvec_gpu_status xvec_gpu_index_destroy(xvec_gpu_index* idx) {
 }
 
 extern "C" int64_t xvec_gpu_index_len(const xvec_gpu_index* idx) { return idx ? idx->n : 0; }
+
+extern "C" xvec_gpu_status xvec_gpu_index_reserve(xvec_gpu_index* idx, int64_t capacity) {
+  if (!idx || capacity < 0 || capacity > 0xffffffffll)
+    return set_error("invalid reserve arguments"), XVEC_GPU_INVALID_ARGUMENT;
+  std::unique_lock<std::shared_mutex> lock(idx->mu);
+  if (capacity <= idx->capacity) return XVEC_GPU_OK;
+  cudaSetDevice(idx->device);
+  xvec_gpu_status st = grow_locked(idx, capacity, nullptr);
+  cudaStreamSynchronize(nullptr);
+  return st;
+}
 
 extern "C" xvec_gpu_status xvec_gpu_index_add_device(xvec_gpu_index* idx, const uint64_t* d_keys,
                                                      const void* d_rows, int64_t n,
