@@ -469,7 +469,7 @@ def run_sq8(args):
         roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOP/s",
                 "frac": (achieved / peak) if achieved else None, "traffic": None,
                 "peak_source": "nominal dense INT8 tensor (no measured INT8 figure); the scan "
-                               "runs on FP32 FFMA over the INT8 codes",
+                               "runs on tcgen05 kind::i8",
                 "kernel": "SQ8 code scan", "kernel_ms": scan_ms,
                 "algorithmic_int_ops_per_launch": ops}
         config = {"workload": SQ_WORKLOAD, "global_batch": nq, "top_k": SQ_K, "base_vectors": n,

@@ -80,3 +80,17 @@ def test_sq8_filter_radius_edge_vectors(oracle, xb):
     run(oracle, xb, L2, rows, keys, queries, 40, radius=50.0)
     run(oracle, xb, L2, rows, keys, queries, 10, radius=50.0, refine=3.0)
     run(oracle, xb, IP, rows, keys, queries, 40, radius=2.0)
+
+
+@pytest.mark.parametrize("metric", [IP, L2])
+def test_sq8_tensor_core_seeded(oracle, xb, metric):
+    """70,000 rows: the INT8 tensor-core scan in seeding launches plus the rest."""
+    rng = np.random.default_rng(70 + metric)
+    rows = scaled_gaussian(rng, 70_000, 128)
+    rows[4300:4400] = rows[100:200]          # duplicates across the first launches
+    keys = rng.permutation(1 << 22)[:70_000].astype(np.uint64)
+    queries = scaled_gaussian(rng, 200, 128)
+    before = xb.stats()["tensor_scans"]
+    run(oracle, xb, metric, rows, keys, queries, 10)
+    assert xb.stats()["tensor_scans"] > before, "tensor-core path not taken"
+    run(oracle, xb, metric, rows, keys, queries, 10, refine=4.0)

@@ -156,6 +156,86 @@ int choose_kp(int k) {
 }
 
 // ---------------------------------------------------------------------------
+// Tensor-core candidate scan in launches over growing row prefixes.
+// ---------------------------------------------------------------------------
+xvec_gpu_status tc_seeded_scan(int device, int nq, int64_t n, int kp, cudaStream_t s,
+                               const TcScanLaunch& scan, Scratch& pkeys, Scratch& pcounts,
+                               Scratch& psat, int* lists_out) {
+  // Parts: pick the row split whose CTA count best fills whole waves of
+  // one CTA per SM, keeping at least 16 tiles of 256 rows per part.
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  // Query blocks of 128; CTA pairs take them two at a time.
+  const int qblocks = flat_tc_pairs(nq) ? ((nq + 127) / 128 + 1) / 2 * 2 : (nq + 127) / 128;
+  auto best_parts = [&](int64_t max_parts) {
+    int parts = 1;
+    double best = -1;
+    for (int p = 1; p <= max_parts; ++p) {
+      const int64_t ctas = (int64_t)qblocks * p;
+      const int64_t waves = (ctas + sms - 1) / sms;
+      const double eff = (double)ctas / (double)(waves * sms);
+      if (eff > best + 1e-9) {
+        best = eff;
+        parts = p;
+      }
+    }
+    return parts;
+  };
+  const int lpp = flat_tc_lists_per_part();
+  // The merge gathers every list of a query in shared memory.
+  const int64_t merge_lists = flat_merge_capacity() / kp;
+  // Seeding: launches over growing prefixes of the rows (1/256, then up to
+  // 1/16); after each, the kp-th best key of every query over all lists
+  // so far lowers its shared threshold, so the lists of the next launch
+  // filter from their first tile instead of each collecting kp entries.
+  std::vector<int64_t> ends;  // row ends of the seeding launches
+  if (n >= (int64_t)1 << 16) {
+    const int64_t e0 = n / 256 / 256 * 256, e1 = n / 16 / 256 * 256;
+    if (e0 >= 4096) ends.push_back(e0);
+    ends.push_back(e1);
+  }
+  std::vector<int> seed_parts;
+  int64_t prev = 0;
+  int used = 0;
+  for (int64_t e : ends) {
+    const int64_t lim = std::min<int64_t>(
+        std::min<int64_t>(16, (merge_lists / 2 - used * lpp) / lpp), (e - prev) / 4096);
+    const int p = best_parts(std::max<int64_t>(1, lim));
+    seed_parts.push_back(p);
+    used += p;
+    prev = e;
+  }
+  const int64_t seed_rows = ends.empty() ? 0 : ends.back();
+  const int64_t rest = n - seed_rows;
+  const int parts = best_parts(std::max<int64_t>(
+      1, std::min<int64_t>(std::min<int64_t>(64, merge_lists / lpp - used), rest / 4096)));
+  const int cap = flat_tc_cap();
+  const int lists = (used + parts) * lpp;
+  Scratch gthr;
+  xvec_gpu_status st;
+  if ((st = pkeys.alloc((size_t)nq * lists * cap * 8, s)) ||
+      (st = pcounts.alloc((size_t)nq * lists * 4, s)) ||
+      (st = psat.alloc((size_t)nq * lists * 8, s)) || (st = gthr.alloc((size_t)nq * 8, s)))
+    return st;
+  XVEC_CUDA(cudaMemsetAsync(gthr.ptr, 0xff, (size_t)nq * 8, s));
+  prev = 0;
+  int list0 = 0;
+  for (size_t i = 0; i < ends.size(); ++i) {
+    XVEC_CUDA(scan(prev, ends[i], seed_parts[i], list0, lists, gthr.as<unsigned long long>(),
+                   pkeys.as<uint64_t>(), pcounts.as<int>(), psat.as<uint64_t>()));
+    list0 += seed_parts[i] * lpp;
+    XVEC_CUDA(launch_seed_thresholds(pkeys.as<uint64_t>(), pcounts.as<int>(), nq, lists, list0,
+                                     cap, kp, gthr.as<unsigned long long>(), s));
+    count_launches(2);
+    prev = ends[i];
+  }
+  XVEC_CUDA(scan(seed_rows, n, parts, list0, lists, gthr.as<unsigned long long>(),
+                 pkeys.as<uint64_t>(), pcounts.as<int>(), psat.as<uint64_t>()));
+  *lists_out = lists;
+  return XVEC_GPU_OK;
+}
+
+// ---------------------------------------------------------------------------
 // Flat search (device memory in and out).
 // ---------------------------------------------------------------------------
 template <typename RowT>
@@ -191,87 +271,26 @@ xvec_gpu_status flat_search_impl(xvec_gpu_index* idx, const void* d_q, int nq,
   const bool fast = use_tc || (simt_cap_for(kp) <= 512 && n > 0);
   if (use_tc) {
     if (is_cancelled(o)) return set_error("cancelled"), XVEC_GPU_CANCELLED;
-    // Parts: pick the row split whose CTA count best fills whole waves of
-    // one CTA per SM, keeping at least 16 tiles of 256 rows per part.
-    int sms = 148;
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, idx->device);
-    // Query blocks of 128; CTA pairs take them two at a time.
-    const int qblocks = flat_tc_pairs(nq) ? ((nq + 127) / 128 + 1) / 2 * 2 : (nq + 127) / 128;
-    auto best_parts = [&](int64_t max_parts) {
-      int parts = 1;
-      double best = -1;
-      for (int p = 1; p <= max_parts; ++p) {
-        const int64_t ctas = (int64_t)qblocks * p;
-        const int64_t waves = (ctas + sms - 1) / sms;
-        const double eff = (double)ctas / (double)(waves * sms);
-        if (eff > best + 1e-9) {
-          best = eff;
-          parts = p;
-        }
-      }
-      return parts;
-    };
-    const int lpp = flat_tc_lists_per_part();
-    // The merge gathers every list of a query in shared memory.
-    const int64_t merge_lists = flat_merge_capacity() / kp;
-    // Seeding: launches over growing prefixes of the rows (1/256, then up to
-    // 1/16); after each, the kp-th best key of every query over all lists
-    // so far lowers its shared threshold, so the lists of the next launch
-    // filter from their first tile instead of each collecting kp entries.
-    std::vector<int64_t> ends;  // row ends of the seeding launches
-    if (n >= (int64_t)1 << 16) {
-      const int64_t e0 = n / 256 / 256 * 256, e1 = n / 16 / 256 * 256;
-      if (e0 >= 4096) ends.push_back(e0);
-      ends.push_back(e1);
-    }
-    std::vector<int> seed_parts;
-    int64_t prev = 0;
-    int used = 0;
-    for (int64_t e : ends) {
-      const int64_t lim = std::min<int64_t>(
-          std::min<int64_t>(16, (merge_lists / 2 - used * lpp) / lpp), (e - prev) / 4096);
-      const int p = best_parts(std::max<int64_t>(1, lim));
-      seed_parts.push_back(p);
-      used += p;
-      prev = e;
-    }
-    const int64_t seed_rows = ends.empty() ? 0 : ends.back();
-    const int64_t rest = n - seed_rows;
-    const int parts = best_parts(std::max<int64_t>(
-        1, std::min<int64_t>(std::min<int64_t>(64, merge_lists / lpp - used), rest / 4096)));
     const int cap = flat_tc_cap();
-    const int lists = (used + parts) * lpp;
-    Scratch pkeys, pcounts, psat, gthr;
-    if ((st = pkeys.alloc((size_t)nq * lists * cap * 8, s)) ||
-        (st = pcounts.alloc((size_t)nq * lists * 4, s)) ||
-        (st = psat.alloc((size_t)nq * lists * 8, s)) || (st = gthr.alloc((size_t)nq * 8, s)))
-      return st;
-    XVEC_CUDA(cudaMemsetAsync(gthr.ptr, 0xff, (size_t)nq * 8, s));
     const float* row_aux =
         metric == XVEC_METRIC_COSINE ? idx->row_inv.as<float>() : idx->row_n2.as<float>();
     const __half* hrows = reinterpret_cast<const __half*>(rows);
-    // One launch over rows [b, e) into lists [list0, list0 + 2 * p).
-    auto scan = [&](int64_t b, int64_t e, int p, int list0) {
-      return launch_flat_scan_tc(metric, static_cast<const __half*>(d_q), nq, hrows + b * d,
-                                 e - b, d, d, row_aux + b, idx->keyrank.as<uint32_t>() + b,
-                                 qaux.as<float>(), qn2.as<float>(),
-                                 gthr.as<unsigned long long>(),
-                                 d_bitmap ? d_bitmap + b / 32 : nullptr, p, kp, list0, lists,
-                                 pkeys.as<uint64_t>(), pcounts.as<int>(), psat.as<uint64_t>(),
-                                 qflags.as<int>(), kstatus.as<int>(), s);
-    };
+    Scratch pkeys, pcounts, psat;
+    int lists = 0;
     timer.mark(1);
-    prev = 0;
-    int list0 = 0;
-    for (size_t i = 0; i < ends.size(); ++i) {
-      XVEC_CUDA(scan(prev, ends[i], seed_parts[i], list0));
-      list0 += seed_parts[i] * lpp;
-      XVEC_CUDA(launch_seed_thresholds(pkeys.as<uint64_t>(), pcounts.as<int>(), nq, lists, list0,
-                                       cap, kp, gthr.as<unsigned long long>(), s));
-      count_launches(2);
-      prev = ends[i];
-    }
-    XVEC_CUDA(scan(seed_rows, n, parts, list0));
+    st = tc_seeded_scan(idx->device, nq, n, kp, s,
+                        [&](int64_t b, int64_t e, int p, int list0, int nlists,
+                            unsigned long long* gthr, uint64_t* cand, int* counts,
+                            uint64_t* sat) {
+                          return launch_flat_scan_tc(
+                              metric, static_cast<const __half*>(d_q), nq, hrows + b * d, e - b,
+                              d, d, row_aux + b, idx->keyrank.as<uint32_t>() + b,
+                              qaux.as<float>(), qn2.as<float>(), gthr,
+                              d_bitmap ? d_bitmap + b / 32 : nullptr, p, kp, list0, nlists, cand,
+                              counts, sat, qflags.as<int>(), kstatus.as<int>(), s);
+                        },
+                        pkeys, pcounts, psat, &lists);
+    if (st) return st;
     timer.mark(2);
     XVEC_LAUNCHED();
     count_tensor_scan();

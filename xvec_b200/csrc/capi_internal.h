@@ -6,6 +6,7 @@
 #include <cstdarg>
 #include <cstdint>
 #include <cstdio>
+#include <functional>
 #include <mutex>
 #include <shared_mutex>
 #include <string>
@@ -110,6 +111,18 @@ struct Scratch {
     return static_cast<T*>(ptr);
   }
 };
+
+// One launch of a tensor-core candidate scan over rows [b, e) into lists
+// [list0, list0 + 2 * parts) of `lists` per query (flat_tc.cuh).
+using TcScanLaunch = std::function<cudaError_t(int64_t b, int64_t e, int parts, int list0,
+                                               int lists, unsigned long long* gthr,
+                                               uint64_t* cand, int* counts, uint64_t* sat)>;
+// Runs the scan over all n rows as seeding launches over growing prefixes
+// (each followed by a threshold seeding) and one launch over the rest;
+// allocates the lists and reports their number per query.
+xvec_gpu_status tc_seeded_scan(int device, int nq, int64_t n, int kp, cudaStream_t s,
+                               const TcScanLaunch& scan, Scratch& pkeys, Scratch& pcounts,
+                               Scratch& psat, int* lists_out);
 
 }  // namespace xvec
 

@@ -53,8 +53,12 @@ constexpr int kEpiWarps = 8;  // two warps per TMEM lane quarter, one per column
 constexpr int kThreads = 64 + kEpiWarps * 32;
 constexpr uint32_t kTileABytes = kBM * kBK * 2;  // 16 KB
 // Per epilogue warp: radix histogram (1 KB) + the current tile's row
-// metadata for its 128 columns (aux floats + key ranks, 1 KB).
-constexpr uint32_t kEpiSmemBytes = kEpiWarps * 256 * 4 * 2;
+// metadata for its 128 columns (aux floats + key ranks, 1 KB; SQ8: the rows'
+// float4 rank terms, 2 KB).
+constexpr uint32_t kEpiSmemBytes = kEpiWarps * (256 * 4 * 2 + 128 * 16);
+// Kernel modes: a Flat metric (FP16 operands, fp32 accumulators) or
+// kModeSq8 + metric (INT8 codes, kind::i8, exact int32 accumulators).
+constexpr int kModeSq8 = 16;
 
 template <bool PAIR>
 struct Shape {
@@ -175,6 +179,27 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(const void* tile) {
 template <int M>
 constexpr uint32_t idesc_f16() {
   return (1u << 4) | ((uint32_t)(kBN >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// kind::i8: A/B signed 8-bit, D = S32.
+template <int M>
+constexpr uint32_t idesc_s8() {
+  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kBN >> 3) << 17) |
+         ((uint32_t)(M >> 4) << 24);
+}
+template <bool PAIR>
+__device__ __forceinline__ void mma_s8(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t acc) {
+  if constexpr (PAIR) {
+    asm volatile(
+        "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+        "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(idesc_s8<2 * kBM>()), "r"(acc));
+  } else {
+    asm volatile(
+        "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(idesc_s8<kBM>()), "r"(acc));
+  }
 }
 
 template <bool PAIR>
@@ -339,7 +364,7 @@ __device__ __forceinline__ uint64_t warp_select_compact(uint64_t* gbuf, int cnt,
   return prefix;
 }
 
-template <int METRIC, bool PAIR>
+template <int MODE, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
     const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap rmap, int nq,
     int64_t n, int d, const float* __restrict__ row_aux, const uint32_t* __restrict__ keyrank,
@@ -348,6 +373,9 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
     int64_t rows_per_part, int kp, int list_base, int num_lists, uint64_t* __restrict__ cand,
     int* __restrict__ part_counts, uint64_t* __restrict__ part_sat, int* __restrict__ q_flags,
     int* __restrict__ status) {
+  constexpr bool SQ = MODE >= kModeSq8;      // INT8 codes (SQ8) instead of FP16 rows
+  constexpr int METRIC = MODE & 15;
+  constexpr int kElemBytes = SQ ? 1 : 2;
   using S = Shape<PAIR>;
   constexpr int kStages = S::kStages;
   constexpr uint32_t kStageBytes = S::kStageBytes;
@@ -356,7 +384,8 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
   unsigned char* tiles = smem;  // kStages x (A | B)
   int* hist_all = reinterpret_cast<int*>(smem + kStages * kStageBytes);  // kEpiWarps x 256
   uint32_t* meta_all = reinterpret_cast<uint32_t*>(hist_all + kEpiWarps * 256);  // x 256
-  uint64_t* bars = reinterpret_cast<uint64_t*>(meta_all + kEpiWarps * 256);
+  float4* meta4_all = reinterpret_cast<float4*>(meta_all + kEpiWarps * 256);  // x 128
+  uint64_t* bars = reinterpret_cast<uint64_t*>(meta4_all + kEpiWarps * 128);
   uint64_t* full = bars;                      // [kStages] the stage's copies landed (pair:
                                               // both CTAs' copies, on the first CTA)
   uint32_t* issued = reinterpret_cast<uint32_t*>(bars + kStages);  // [kStages] copies per stage
@@ -374,7 +403,9 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
   const int64_t row_begin = (int64_t)part * rows_per_part;
   const int64_t row_end = min(n, row_begin + rows_per_part);
   const int num_tiles = row_end > row_begin ? (int)((row_end - row_begin + kBN - 1) / kBN) : 0;
-  const int ksteps = (d + kBK - 1) / kBK;
+  // k-steps of 128 bytes (kBK FP16 or 2 kBK INT8 elements).
+  const int ksteps = (d * kElemBytes + 127) / 128;
+  constexpr int kStepElems = 128 / kElemBytes;
   const uint32_t rank = PAIR ? cluster_rank() : 0u;
   const bool issuer = rank == 0;  // the CTA whose thread issues the MMAs
 
@@ -431,11 +462,11 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
           unsigned char* b_dst = a_dst + kTileABytes;
           if (issuer) mbar_expect_tx(&full[stage], (PAIR ? 2 : 1) * kStageBytes);
           if constexpr (PAIR) {
-            tma_load_2d_pair(&qmap, full0 + stage * 8, a_dst, ks * kBK, qblock * kBM);
-            tma_load_2d_pair(&rmap, full0 + stage * 8, b_dst, ks * kBK, row0);
+            tma_load_2d_pair(&qmap, full0 + stage * 8, a_dst, ks * kStepElems, qblock * kBM);
+            tma_load_2d_pair(&rmap, full0 + stage * 8, b_dst, ks * kStepElems, row0);
           } else {
-            tma_load_2d(&qmap, &full[stage], a_dst, ks * kBK, qblock * kBM);
-            tma_load_2d(&rmap, &full[stage], b_dst, ks * kBK, row0);
+            tma_load_2d(&qmap, &full[stage], a_dst, ks * kStepElems, qblock * kBM);
+            tma_load_2d(&rmap, &full[stage], b_dst, ks * kStepElems, row0);
           }
           ++count[stage];
           if (++stage == kStages) {
@@ -478,9 +509,14 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
           const uint64_t adesc = smem_desc_sw128(a_src);
           const uint64_t bdesc = smem_desc_sw128(a_src + kTileABytes);
 #pragma unroll
-          for (int k = 0; k < kBK / 16; ++k)  // 16 fp16 = 32 bytes per MMA
-            mma_f16<PAIR>(d_tmem, adesc + (uint64_t)(k * 2), bdesc + (uint64_t)(k * 2),
-                          (ks > 0 || k > 0) ? 1u : 0u);
+          for (int k = 0; k < 4; ++k) {  // 32 bytes of K per MMA (16 FP16 or 32 INT8)
+            if constexpr (SQ)
+              mma_s8<PAIR>(d_tmem, adesc + (uint64_t)(k * 2), bdesc + (uint64_t)(k * 2),
+                           (ks > 0 || k > 0) ? 1u : 0u);
+            else
+              mma_f16<PAIR>(d_tmem, adesc + (uint64_t)(k * 2), bdesc + (uint64_t)(k * 2),
+                            (ks > 0 || k > 0) ? 1u : 0u);
+          }
           mma_commit<PAIR>(own_empty0 + stage * 8);
           if (PAIR) mma_commit<PAIR>(peer_empty0 + stage * 8);
           if (++stage == kStages) {
@@ -503,8 +539,11 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
     const int qlocal = quarter * 32 + lane;
     const int qi = qblock * kBM + qlocal;
     const bool qvalid = qi < nq;
-    const float qa = qvalid ? q_aux[qi] : 0.f;
-    const float qn2 = qvalid ? q_n2[qi] : 0.f;
+    const float qa = (!SQ && qvalid) ? q_aux[qi] : 0.f;
+    const float qn2 = (!SQ && qvalid) ? q_n2[qi] : 0.f;
+    // SQ8: the query's rank terms {A, B, C, ||q||^2} (sq8.cu); q_aux holds them.
+    const float4 qinfo = (SQ && qvalid) ? reinterpret_cast<const float4*>(q_aux)[qi]
+                                        : make_float4(0.f, 0.f, 0.f, 0.f);
     // Per-query thresholds are shared by every list of the query (gthr,
     // lowered with atomicMin after each compaction): a list may drop any key
     // above another list's kp-th key, so only the first lists of a query pay
@@ -519,10 +558,12 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
     int* hist = hist_all + ew * 256;
     float* meta_aux = reinterpret_cast<float*>(meta_all + ew * 256);  // [128]
     uint32_t* meta_kr = meta_all + ew * 256 + 128;                     // [128]
+    float4* meta4 = meta4_all + ew * 128;                              // [128] (SQ8)
     // Row metadata (aux, key rank, filter) of this warp's 128 columns is
     // loaded one tile ahead into registers and staged in shared memory, so
     // neither the scoring loop nor the append path waits on global memory.
     float pf_aux[4];
+    float4 pf4[SQ ? 4 : 1];
     uint32_t pf_kr[4], pf_vm[4];
     auto prefetch = [&](int t) {
       const int64_t base = row_begin + (int64_t)t * kBN + half * 128;
@@ -530,8 +571,14 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
       for (int c = 0; c < 4; ++c) {
         const int64_t row = base + c * 32 + lane;
         const bool ok = t < num_tiles && row < row_end && bitmap_pass(bitmap, row);
-        const float ra = (ok && METRIC != kMetricIP) ? row_aux[row] : 0.f;
-        pf_aux[c] = METRIC == kMetricL2 ? -0.5f * ra : ra;
+        if constexpr (SQ) {
+          pf4[c] = ok ? reinterpret_cast<const float4*>(row_aux)[row]
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+          pf_aux[c] = 0.f;
+        } else {
+          const float ra = (ok && METRIC != kMetricIP) ? row_aux[row] : 0.f;
+          pf_aux[c] = METRIC == kMetricL2 ? -0.5f * ra : ra;
+        }
         pf_kr[c] = ok ? keyrank[row] : 0u;
         pf_vm[c] = __ballot_sync(kFullMask, ok);
       }
@@ -545,6 +592,7 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         meta_aux[c * 32 + lane] = pf_aux[c];
+        if constexpr (SQ) meta4[c * 32 + lane] = pf4[c];
         meta_kr[c * 32 + lane] = pf_kr[c];
         vm[c] = pf_vm[c];
       }
@@ -595,7 +643,28 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
           return -tc_rank<METRIC>(dot, a, qa, qn2);
         };
         const float4* a4 = reinterpret_cast<const float4*>(meta_aux + c * 32);
-        if (vmask == kFullMask) {
+        if constexpr (SQ) {
+          // SQ8Ranker (sq8.cu) on the exact integer dot product.
+          if (vmask != 0u) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float4 r = meta4[c * 32 + j];
+              const float dot = (float)(int)cur[j];
+              const float tt = fmaf(qinfo.x, dot, qinfo.y * r.z);
+              const float inner = fmaf(r.x, tt, r.y * qinfo.z);
+              const float rank =
+                  METRIC == kMetricIP ? -inner : (r.w + qinfo.w) - 2.f * inner;
+              if (((vmask >> j) & 1u) && !(rank > thr_f)) {
+                if (!isfinite(rank)) {
+                  nonfinite = 1;
+                } else {
+                  const uint64_t key = pack_rank(rank, meta_kr[c * 32 + j]);
+                  if (key < thr) gbuf[cnt++] = key;
+                }
+              }
+            }
+          }
+        } else if (vmask == kFullMask) {
 #pragma unroll
           for (int g = 0; g < 8; ++g) {
             const float4 av = a4[g];
@@ -714,16 +783,19 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 // Row-major [rows][d] binary16 matrix viewed with a row stride of
 // `row_stride_elems`, box [box_rows][64], 128-byte swizzle.
+// Row-major [rows][d] matrix of 1- or 2-byte elements viewed with a row
+// stride of `row_stride_elems`, box [box_rows][128 bytes], 128-byte swizzle.
 bool make_map(CUtensorMap* map, const void* base, int64_t rows, int d, int64_t row_stride_elems,
-              int box_rows) {
+              int box_rows, int elem_bytes = 2) {
   auto fn = encode_fn();
   if (!fn) return false;
   cuuint64_t dims[2] = {(cuuint64_t)d, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)row_stride_elems * 2};
-  cuuint32_t box[2] = {(cuuint32_t)tc::kBK, (cuuint32_t)box_rows};
+  cuuint64_t strides[1] = {(cuuint64_t)row_stride_elems * elem_bytes};
+  cuuint32_t box[2] = {(cuuint32_t)(128 / elem_bytes), (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides,
-                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+  CUresult r = fn(map, elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8,
+                  2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
@@ -741,19 +813,22 @@ int flat_tc_lists_per_part() { return 2; }
 // CTA pairs whenever there are two query blocks to pair up.
 bool flat_tc_pairs(int nq) { return nq > tc::kBM; }
 
-cudaError_t launch_flat_scan_tc(int metric, const __half* queries, int nq, const __half* rows,
-                                int64_t n, int d, int64_t row_stride_elems, const float* row_aux,
-                                const uint32_t* keyrank, const float* q_aux, const float* q_n2,
-                                unsigned long long* gthr, const uint32_t* bitmap, int num_parts,
-                                int kp, int list_base, int num_lists, uint64_t* cand,
-                                int* part_counts, uint64_t* part_sat, int* q_flags, int* status,
-                                cudaStream_t stream) {
+namespace {
+// Launches mode MODE (a Flat metric, or kModeSq8 + metric) on CTA pairs when
+// there are two query blocks, else on single CTAs.
+template <int MODE>
+cudaError_t launch_tc(int nq, const void* queries, const void* rows, int64_t n, int d,
+                      int64_t row_stride_elems, int elem_bytes, const float* row_aux,
+                      const uint32_t* keyrank, const float* q_aux, const float* q_n2,
+                      unsigned long long* gthr, const uint32_t* bitmap, int num_parts, int kp,
+                      int list_base, int num_lists, uint64_t* cand, int* part_counts,
+                      uint64_t* part_sat, int* q_flags, int* status, cudaStream_t stream) {
   const int qblocks = (nq + tc::kBM - 1) / tc::kBM;
   const bool pair = flat_tc_pairs(nq);
   CUtensorMap qmap, rmap;
-  if (!make_map(&qmap, queries, nq, d, d, tc::kBM) ||
+  if (!make_map(&qmap, queries, nq, d, d, tc::kBM, elem_bytes) ||
       !make_map(&rmap, rows, n, d, row_stride_elems,
-                pair ? tc::Shape<true>::kRowsPerCta : tc::Shape<false>::kRowsPerCta))
+                pair ? tc::Shape<true>::kRowsPerCta : tc::Shape<false>::kRowsPerCta, elem_bytes))
     return cudaErrorInvalidValue;
   const int64_t rows_per_part = ((n + num_parts - 1) / num_parts + tc::kBN - 1) / tc::kBN * tc::kBN;
   cudaLaunchConfig_t cfg = {};
@@ -767,33 +842,72 @@ cudaError_t launch_flat_scan_tc(int metric, const __half* queries, int nq, const
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t err = cudaErrorInvalidValue;
-#define XVEC_TC_CASE(M, P)                                                                      \
-  {                                                                                             \
-    auto kern = tc::flat_scan_tc_kernel<M, P>;                                                  \
-    cfg.dynamicSmemBytes = tc::Shape<P>::kSmemBytes;                                            \
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,                    \
-                         (int)tc::Shape<P>::kSmemBytes);                                        \
-    err = cudaLaunchKernelEx(&cfg, kern, qmap, rmap, nq, n, d, row_aux, keyrank, q_aux, q_n2,  \
-                             gthr, bitmap, rows_per_part, kp, list_base, num_lists, cand,      \
-                             part_counts, part_sat, q_flags, status);                           \
+  cudaError_t err;
+  if (pair) {
+    auto kern = tc::flat_scan_tc_kernel<MODE, true>;
+    cfg.dynamicSmemBytes = tc::Shape<true>::kSmemBytes;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)tc::Shape<true>::kSmemBytes);
+    err = cudaLaunchKernelEx(&cfg, kern, qmap, rmap, nq, n, d, row_aux, keyrank, q_aux, q_n2,
+                             gthr, bitmap, rows_per_part, kp, list_base, num_lists, cand,
+                             part_counts, part_sat, q_flags, status);
+  } else {
+    auto kern = tc::flat_scan_tc_kernel<MODE, false>;
+    cfg.dynamicSmemBytes = tc::Shape<false>::kSmemBytes;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)tc::Shape<false>::kSmemBytes);
+    err = cudaLaunchKernelEx(&cfg, kern, qmap, rmap, nq, n, d, row_aux, keyrank, q_aux, q_n2,
+                             gthr, bitmap, rows_per_part, kp, list_base, num_lists, cand,
+                             part_counts, part_sat, q_flags, status);
   }
-#define XVEC_TC_METRIC(M)           \
-  case M:                           \
-    if (pair) XVEC_TC_CASE(M, true) \
-    else XVEC_TC_CASE(M, false)     \
-    break;
-  switch (metric) {
-    XVEC_TC_METRIC(kMetricL2)
-    XVEC_TC_METRIC(kMetricIP)
-    XVEC_TC_METRIC(kMetricCosine)
-    XVEC_TC_METRIC(kMetricMIPS)
-    default: return cudaErrorInvalidValue;
-  }
-#undef XVEC_TC_METRIC
-#undef XVEC_TC_CASE
   if (err != cudaSuccess) return err;
   return cudaGetLastError();
+}
+}  // namespace
+
+cudaError_t launch_flat_scan_tc(int metric, const __half* queries, int nq, const __half* rows,
+                                int64_t n, int d, int64_t row_stride_elems, const float* row_aux,
+                                const uint32_t* keyrank, const float* q_aux, const float* q_n2,
+                                unsigned long long* gthr, const uint32_t* bitmap, int num_parts,
+                                int kp, int list_base, int num_lists, uint64_t* cand,
+                                int* part_counts, uint64_t* part_sat, int* q_flags, int* status,
+                                cudaStream_t stream) {
+#define XVEC_TC_ARGS                                                                           \
+  nq, queries, rows, n, d, row_stride_elems, 2, row_aux, keyrank, q_aux, q_n2, gthr, bitmap, \
+      num_parts, kp, list_base, num_lists, cand, part_counts, part_sat, q_flags, status, stream
+  switch (metric) {
+    case kMetricL2: return launch_tc<kMetricL2>(XVEC_TC_ARGS);
+    case kMetricIP: return launch_tc<kMetricIP>(XVEC_TC_ARGS);
+    case kMetricCosine: return launch_tc<kMetricCosine>(XVEC_TC_ARGS);
+    case kMetricMIPS: return launch_tc<kMetricMIPS>(XVEC_TC_ARGS);
+    default: return cudaErrorInvalidValue;
+  }
+#undef XVEC_TC_ARGS
+}
+
+cudaError_t launch_sq8_scan_tc(int metric, const int8_t* qcodes, int nq, const int8_t* codes,
+                               int64_t n, int d, const float4* row_info, const uint32_t* keyrank,
+                               const float4* q_info, unsigned long long* gthr,
+                               const uint32_t* bitmap, int num_parts, int kp, int list_base,
+                               int num_lists, uint64_t* cand, int* part_counts,
+                               uint64_t* part_sat, int* q_flags, int* status,
+                               cudaStream_t stream) {
+#define XVEC_TC_ARGS                                                                           \
+  nq, qcodes, codes, n, d, (int64_t)d, 1, reinterpret_cast<const float*>(row_info), keyrank,  \
+      reinterpret_cast<const float*>(q_info), nullptr, gthr, bitmap, num_parts, kp, list_base, \
+      num_lists, cand, part_counts, part_sat, q_flags, status, stream
+  switch (metric) {
+    case kMetricL2: return launch_tc<tc::kModeSq8 + kMetricL2>(XVEC_TC_ARGS);
+    case kMetricIP: return launch_tc<tc::kModeSq8 + kMetricIP>(XVEC_TC_ARGS);
+    default: return cudaErrorInvalidValue;
+  }
+#undef XVEC_TC_ARGS
+}
+
+bool sq8_tc_supported(int d, const void* codes, const void* qcodes) {
+  // 16-byte row strides for TMA; |dot| <= 127^2 d stays exact in float32.
+  return d % 16 == 0 && d >= 128 && d <= 1040 && ((uintptr_t)codes % 16 == 0) &&
+         ((uintptr_t)qcodes % 16 == 0) && encode_fn() != nullptr;
 }
 
 }  // namespace xvec

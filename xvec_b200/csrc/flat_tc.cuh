@@ -34,4 +34,18 @@ cudaError_t launch_flat_scan_tc(int metric, const __half* queries, int nq, const
                                 int* part_counts, uint64_t* part_sat, int* q_flags, int* status,
                                 cudaStream_t stream);
 
+// The same scan over INT8 codes (SQ8 index, L2 or IP): tcgen05 kind::i8 on
+// the row codes [n][d] and the query codes [nq][d], exact int32 dot products
+// ranked with the SQ8 fast rank (row_info / q_info: the float4 rank terms of
+// sq8.cu).  Lists, thresholds and status as for launch_flat_scan_tc.
+cudaError_t launch_sq8_scan_tc(int metric, const int8_t* qcodes, int nq, const int8_t* codes,
+                               int64_t n, int d, const float4* row_info, const uint32_t* keyrank,
+                               const float4* q_info, unsigned long long* gthr,
+                               const uint32_t* bitmap, int num_parts, int kp, int list_base,
+                               int num_lists, uint64_t* cand, int* part_counts,
+                               uint64_t* part_sat, int* q_flags, int* status,
+                               cudaStream_t stream);
+// True when the INT8 tensor-core scan can take this layout.
+bool sq8_tc_supported(int d, const void* codes, const void* qcodes);
+
 }  // namespace xvec

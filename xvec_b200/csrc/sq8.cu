@@ -20,6 +20,7 @@
 #include "capi_internal.h"
 #include "common.cuh"
 #include "flat_kernels.cuh"
+#include "flat_tc.cuh"
 #include "index_kernels.cuh"
 #include "pipeline.cuh"
 #include "refine.cuh"
@@ -389,9 +390,46 @@ xvec_gpu_status sq8_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
   XVEC_CUDA(cudaMemsetAsync(o_counts, 0, (size_t)nq * 4, s));
   SQ8Scorer sc{metric, idx->sq_codes.as<int8_t>(), idx->sq_params.as<SQParams>(),
                qcodes.as<int8_t>(), qparams.as<SQParams>(), qeps.as<float>(), d};
-  const bool fast = n > 0 && (metric == XVEC_METRIC_IP || metric == XVEC_METRIC_L2) &&
-                    simt_cap_for(kp) <= 512;
-  if (fast) {
+  const bool ranked = n > 0 && (metric == XVEC_METRIC_IP || metric == XVEC_METRIC_L2);
+  // INT8 tensor cores (tcgen05 kind::i8) when the layout allows, else FFMA.
+  const bool use_tc = ranked && kp + 128 <= flat_tc_cap() && n < (1ll << 31) - 256 &&
+                      sq8_tc_supported(d, idx->sq_codes.ptr, qcodes.ptr);
+  const bool fast = use_tc || (ranked && simt_cap_for(kp) <= 512);
+  if (use_tc) {
+    Scratch pkeys, pcounts, psat, kstatus;
+    int lists = 0;
+    if ((st = kstatus.alloc(4, s))) return st;
+    XVEC_CUDA(cudaMemsetAsync(kstatus.ptr, 0, 4, s));
+    timer.mark(1);
+    st = tc_seeded_scan(
+        idx->device, nq, n, kp, s,
+        [&](int64_t b, int64_t e, int p, int list0, int nlists, unsigned long long* gthr,
+            uint64_t* cand, int* counts, uint64_t* sat) {
+          return launch_sq8_scan_tc(metric, qcodes.as<int8_t>(), nq,
+                                    idx->sq_codes.as<int8_t>() + b * d, e - b, d,
+                                    idx->sq_fast.as<float4>() + b,
+                                    idx->keyrank.as<uint32_t>() + b, qinfo.as<float4>(), gthr,
+                                    d_bitmap ? d_bitmap + b / 32 : nullptr, p, kp, list0, nlists,
+                                    cand, counts, sat, qflags.as<int>(), kstatus.as<int>(), s);
+        },
+        pkeys, pcounts, psat, &lists);
+    if (st) return st;
+    timer.mark(2);
+    XVEC_LAUNCHED();
+    count_tensor_scan();
+    XVEC_CUDA(launch_merge_rescore(sc, idx->pos_of_kr.as<uint32_t>(), idx->keys.as<uint64_t>(),
+                                   nullptr, nq, stage_k, stage_radius, 0, pkeys.as<uint64_t>(),
+                                   pcounts.as<int>(), psat.as<uint64_t>(), lists, flat_tc_cap(),
+                                   o_keys, o_scores, o_counts, spos.as<uint32_t>(),
+                                   qflags.as<int>(), s));
+    XVEC_LAUNCHED();
+    int h_kstatus = 0;
+    XVEC_CUDA(cudaMemcpyAsync(&h_kstatus, kstatus.ptr, 4, cudaMemcpyDeviceToHost, s));
+    XVEC_CUDA(cudaStreamSynchronize(s));
+    if (h_kstatus != 0)
+      return set_error("tensor-core scan: a bounded device wait expired (code %d)", h_kstatus),
+             XVEC_GPU_TIMEOUT;
+  } else if (fast) {
     const int qtiles = (nq + 31) / 32;
     int parts = (int)std::max<int64_t>(
         1, std::min<int64_t>((592 + qtiles - 1) / qtiles, (n + 1023) / 1024));
