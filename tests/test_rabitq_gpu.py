@@ -187,3 +187,23 @@ def test_rabitq_invalid_options(xb):
     with pytest.raises(xb.XvecGPUError):          # dimension outside [64, 4095]
         xb.RaBitQIndex(63, L2)
     idx.close()
+
+
+@pytest.mark.parametrize("metric", [L2, IP])
+def test_rabitq_tensor_core_seeded(oracle, xb, metric):
+    """70,000 rows and 200 queries: the FP16 tensor-core scan on CTA pairs in
+    seeding launches plus the rest, refined and not."""
+    rng = np.random.default_rng(770 + metric)
+    d = 128
+    centers = rng.standard_normal((40, d)).astype(np.float32)
+    rows = mixture(rng, 70_000, d, centers)
+    rows[4300:4400] = rows[100:200]          # duplicates across the first launches
+    keys = rng.permutation(1 << 22)[:70_000].astype(np.uint64)
+    cents, signs = model(rng, d, 16, centers)
+    queries = mixture(rng, 200, d, centers)
+    case = Case(oracle, xb, metric, rows, keys, cents, signs)
+    before = xb.stats()["tensor_scans"]
+    case.check(xb, queries, 10, 100, refine=True)
+    assert xb.stats()["tensor_scans"] > before, "tensor-core path not taken"
+    case.check(xb, queries, 10, 100, refine=False)
+    case.close()

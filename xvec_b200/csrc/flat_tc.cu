@@ -52,21 +52,33 @@ constexpr int kCap = 512;  // candidate list entries per (query, part, column ha
 constexpr int kEpiWarps = 8;  // two warps per TMEM lane quarter, one per column half
 constexpr int kThreads = 64 + kEpiWarps * 32;
 constexpr uint32_t kTileABytes = kBM * kBK * 2;  // 16 KB
-// Per epilogue warp: radix histogram (1 KB) + the current tile's row
-// metadata for its 128 columns (aux floats + key ranks, 1 KB; SQ8: the rows'
-// float4 rank terms, 2 KB).
-constexpr uint32_t kEpiSmemBytes = kEpiWarps * (256 * 4 * 2 + 128 * 16);
-// Kernel modes: a Flat metric (FP16 operands, fp32 accumulators) or
-// kModeSq8 + metric (INT8 codes, kind::i8, exact int32 accumulators).
+// Kernel modes: a Flat metric (FP16 operands, fp32 accumulators);
+// kModeSq8 + metric (INT8 codes, kind::i8, exact int32 accumulators);
+// kModeRaBitQ (FP16 0/1 code planes against a query split into FP16 high and
+// low parts: two MMAs per k-step into one fp32 accumulator).
 constexpr int kModeSq8 = 16;
+constexpr int kModeRaBitQ = 32;
+constexpr int kRaBitQMaxClusters = 16;
+// Per epilogue warp: radix histogram (1 KB) + the current tile's row
+// metadata for its 128 columns (aux floats + key ranks, 1 KB; SQ8/RaBitQ: the
+// rows' float4 rank terms, 2 KB; RaBitQ: the 32 queries' per-cluster terms,
+// 2 KB).
+constexpr uint32_t epi_smem_bytes(bool rq) {
+  return kEpiWarps * (256 * 4 * 2 + 128 * 16 + (rq ? kRaBitQMaxClusters * 32 * 4 : 0));
+}
+constexpr uint32_t kSmemBudget = 232448 - 1024 - 1024 - 512;  // dynamic bytes for stages
 
-template <bool PAIR>
+template <bool PAIR, bool RQ = false>
 struct Shape {
   static constexpr int kRowsPerCta = PAIR ? kBN / 2 : kBN;       // B rows loaded per CTA
   static constexpr uint32_t kTileBBytes = kRowsPerCta * kBK * 2;  // 16 or 32 KB
-  static constexpr uint32_t kStageBytes = kTileABytes + kTileBBytes;
-  static constexpr int kStages = PAIR ? 6 : 4;
-  static constexpr uint32_t kSmemBytes = kStages * kStageBytes + kEpiSmemBytes + 1024 + 512;
+  static constexpr uint32_t kTileABytesM = RQ ? 2 * kTileABytes : kTileABytes;  // (hi | lo)
+  static constexpr uint32_t kStageBytes = kTileABytesM + kTileBBytes;
+  static constexpr uint32_t kEpiBytes = epi_smem_bytes(RQ);
+  static constexpr int kFit = (int)((kSmemBudget - kEpiBytes) / kStageBytes);
+  static constexpr int kStages = kFit < 6 ? kFit : 6;
+  static constexpr uint32_t kSmemBytes = kStages * kStageBytes + kEpiBytes + 1024 + 512;
+  static_assert(kStages >= 2, "shared memory too small for the stage ring");
 };
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // a wait gives up after 2 s
 
@@ -366,17 +378,19 @@ __device__ __forceinline__ uint64_t warp_select_compact(uint64_t* gbuf, int cnt,
 
 template <int MODE, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
-    const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap rmap, int nq,
+    const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap qmap2,
+    const __grid_constant__ CUtensorMap rmap, int nc, int nq,
     int64_t n, int d, const float* __restrict__ row_aux, const uint32_t* __restrict__ keyrank,
     const float* __restrict__ q_aux, const float* __restrict__ q_n2,
     unsigned long long* __restrict__ gthr, const uint32_t* __restrict__ bitmap,
     int64_t rows_per_part, int kp, int list_base, int num_lists, uint64_t* __restrict__ cand,
     int* __restrict__ part_counts, uint64_t* __restrict__ part_sat, int* __restrict__ q_flags,
     int* __restrict__ status) {
-  constexpr bool SQ = MODE >= kModeSq8;      // INT8 codes (SQ8) instead of FP16 rows
+  constexpr bool RQ = MODE == kModeRaBitQ;   // RaBitQ code planes, hi/lo queries
+  constexpr bool SQ = MODE >= kModeSq8 && !RQ;  // INT8 codes (SQ8) instead of FP16 rows
   constexpr int METRIC = MODE & 15;
   constexpr int kElemBytes = SQ ? 1 : 2;
-  using S = Shape<PAIR>;
+  using S = Shape<PAIR, RQ>;
   constexpr int kStages = S::kStages;
   constexpr uint32_t kStageBytes = S::kStageBytes;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -385,7 +399,10 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
   int* hist_all = reinterpret_cast<int*>(smem + kStages * kStageBytes);  // kEpiWarps x 256
   uint32_t* meta_all = reinterpret_cast<uint32_t*>(hist_all + kEpiWarps * 256);  // x 256
   float4* meta4_all = reinterpret_cast<float4*>(meta_all + kEpiWarps * 256);  // x 128
-  uint64_t* bars = reinterpret_cast<uint64_t*>(meta4_all + kEpiWarps * 128);
+  float* gadd_all = reinterpret_cast<float*>(meta4_all + kEpiWarps * 128);    // RaBitQ
+  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<unsigned char*>(meta4_all) +
+                                               kEpiWarps * 128 * 16 +
+                                               (RQ ? kEpiWarps * kRaBitQMaxClusters * 32 * 4 : 0));
   uint64_t* full = bars;                      // [kStages] the stage's copies landed (pair:
                                               // both CTAs' copies, on the first CTA)
   uint32_t* issued = reinterpret_cast<uint32_t*>(bars + kStages);  // [kStages] copies per stage
@@ -459,13 +476,19 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
             break;
           }
           unsigned char* a_dst = tiles + stage * kStageBytes;
-          unsigned char* b_dst = a_dst + kTileABytes;
+          unsigned char* b_dst = a_dst + S::kTileABytesM;
           if (issuer) mbar_expect_tx(&full[stage], (PAIR ? 2 : 1) * kStageBytes);
           if constexpr (PAIR) {
             tma_load_2d_pair(&qmap, full0 + stage * 8, a_dst, ks * kStepElems, qblock * kBM);
+            if constexpr (RQ)
+              tma_load_2d_pair(&qmap2, full0 + stage * 8, a_dst + kTileABytes, ks * kStepElems,
+                               qblock * kBM);
             tma_load_2d_pair(&rmap, full0 + stage * 8, b_dst, ks * kStepElems, row0);
           } else {
             tma_load_2d(&qmap, &full[stage], a_dst, ks * kStepElems, qblock * kBM);
+            if constexpr (RQ)
+              tma_load_2d(&qmap2, &full[stage], a_dst + kTileABytes, ks * kStepElems,
+                          qblock * kBM);
             tma_load_2d(&rmap, &full[stage], b_dst, ks * kStepElems, row0);
           }
           ++count[stage];
@@ -507,7 +530,7 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
           tmem_fence_after();
           const unsigned char* a_src = tiles + stage * kStageBytes;
           const uint64_t adesc = smem_desc_sw128(a_src);
-          const uint64_t bdesc = smem_desc_sw128(a_src + kTileABytes);
+          const uint64_t bdesc = smem_desc_sw128(a_src + S::kTileABytesM);
 #pragma unroll
           for (int k = 0; k < 4; ++k) {  // 32 bytes of K per MMA (16 FP16 or 32 INT8)
             if constexpr (SQ)
@@ -516,6 +539,13 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
             else
               mma_f16<PAIR>(d_tmem, adesc + (uint64_t)(k * 2), bdesc + (uint64_t)(k * 2),
                             (ks > 0 || k > 0) ? 1u : 0u);
+          }
+          if constexpr (RQ) {
+            // The low parts of the queries against the same code planes.
+            const uint64_t adesc_lo = smem_desc_sw128(a_src + kTileABytes);
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              mma_f16<PAIR>(d_tmem, adesc_lo + (uint64_t)(k * 2), bdesc + (uint64_t)(k * 2), 1u);
           }
           mma_commit<PAIR>(own_empty0 + stage * 8);
           if (PAIR) mma_commit<PAIR>(peer_empty0 + stage * 8);
@@ -544,6 +574,15 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
     // SQ8: the query's rank terms {A, B, C, ||q||^2} (sq8.cu); q_aux holds them.
     const float4 qinfo = (SQ && qvalid) ? reinterpret_cast<const float4*>(q_aux)[qi]
                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+    // RaBitQ: half the query's coordinate sum (q_aux) and its per-cluster
+    // terms gAdd (q_n2, [nq][nc]) in a per-warp table [cluster][lane].
+    const float rq_hs = (RQ && qvalid) ? q_aux[qi] : 0.f;
+    float* gadd_tab = gadd_all + ew * kRaBitQMaxClusters * 32;
+    if constexpr (RQ) {
+      for (int c = 0; c < nc; ++c)
+        gadd_tab[c * 32 + lane] = qvalid ? q_n2[(int64_t)qi * nc + c] : 0.f;
+      __syncwarp();
+    }
     // Per-query thresholds are shared by every list of the query (gthr,
     // lowered with atomicMin after each compaction): a list may drop any key
     // above another list's kp-th key, so only the first lists of a query pay
@@ -563,7 +602,7 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
     // loaded one tile ahead into registers and staged in shared memory, so
     // neither the scoring loop nor the append path waits on global memory.
     float pf_aux[4];
-    float4 pf4[SQ ? 4 : 1];
+    float4 pf4[(SQ || RQ) ? 4 : 1];
     uint32_t pf_kr[4], pf_vm[4];
     auto prefetch = [&](int t) {
       const int64_t base = row_begin + (int64_t)t * kBN + half * 128;
@@ -571,7 +610,7 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
       for (int c = 0; c < 4; ++c) {
         const int64_t row = base + c * 32 + lane;
         const bool ok = t < num_tiles && row < row_end && bitmap_pass(bitmap, row);
-        if constexpr (SQ) {
+        if constexpr (SQ || RQ) {
           pf4[c] = ok ? reinterpret_cast<const float4*>(row_aux)[row]
                       : make_float4(0.f, 0.f, 0.f, 0.f);
           pf_aux[c] = 0.f;
@@ -592,7 +631,7 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         meta_aux[c * 32 + lane] = pf_aux[c];
-        if constexpr (SQ) meta4[c * 32 + lane] = pf4[c];
+        if constexpr (SQ || RQ) meta4[c * 32 + lane] = pf4[c];
         meta_kr[c * 32 + lane] = pf_kr[c];
         vm[c] = pf_vm[c];
       }
@@ -643,7 +682,25 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
           return -tc_rank<METRIC>(dot, a, qa, qn2);
         };
         const float4* a4 = reinterpret_cast<const float4*>(meta_aux + c * 32);
-        if constexpr (SQ) {
+        if constexpr (RQ) {
+          // RaBitQRanker (rabitq.cu): add + gAdd[cluster] + rescale (dot - sum/2).
+          if (vmask != 0u) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float4 r = meta4[c * 32 + j];
+              const float g = gadd_tab[__float_as_int(r.z) * 32 + lane];
+              const float rank = fmaf(r.y, __uint_as_float(cur[j]) - rq_hs, r.x + g);
+              if (((vmask >> j) & 1u) && !(rank > thr_f)) {
+                if (!isfinite(rank)) {
+                  nonfinite = 1;
+                } else {
+                  const uint64_t key = pack_rank(rank, meta_kr[c * 32 + j]);
+                  if (key < thr) gbuf[cnt++] = key;
+                }
+              }
+            }
+          }
+        } else if constexpr (SQ) {
           // SQ8Ranker (sq8.cu) on the exact integer dot product.
           if (vmask != 0u) {
 #pragma unroll
@@ -817,16 +874,19 @@ namespace {
 // Launches mode MODE (a Flat metric, or kModeSq8 + metric) on CTA pairs when
 // there are two query blocks, else on single CTAs.
 template <int MODE>
-cudaError_t launch_tc(int nq, const void* queries, const void* rows, int64_t n, int d,
-                      int64_t row_stride_elems, int elem_bytes, const float* row_aux,
+cudaError_t launch_tc(int nq, const void* queries, const void* queries2, int nc, const void* rows,
+                      int64_t n, int d, int64_t row_stride_elems, int elem_bytes,
+                      const float* row_aux,
                       const uint32_t* keyrank, const float* q_aux, const float* q_n2,
                       unsigned long long* gthr, const uint32_t* bitmap, int num_parts, int kp,
                       int list_base, int num_lists, uint64_t* cand, int* part_counts,
                       uint64_t* part_sat, int* q_flags, int* status, cudaStream_t stream) {
   const int qblocks = (nq + tc::kBM - 1) / tc::kBM;
   const bool pair = flat_tc_pairs(nq);
-  CUtensorMap qmap, rmap;
+  constexpr bool RQ = MODE == tc::kModeRaBitQ;
+  CUtensorMap qmap, qmap2, rmap;
   if (!make_map(&qmap, queries, nq, d, d, tc::kBM, elem_bytes) ||
+      !make_map(&qmap2, queries2 ? queries2 : queries, nq, d, d, tc::kBM, elem_bytes) ||
       !make_map(&rmap, rows, n, d, row_stride_elems,
                 pair ? tc::Shape<true>::kRowsPerCta : tc::Shape<false>::kRowsPerCta, elem_bytes))
     return cudaErrorInvalidValue;
@@ -845,19 +905,19 @@ cudaError_t launch_tc(int nq, const void* queries, const void* rows, int64_t n, 
   cudaError_t err;
   if (pair) {
     auto kern = tc::flat_scan_tc_kernel<MODE, true>;
-    cfg.dynamicSmemBytes = tc::Shape<true>::kSmemBytes;
+    cfg.dynamicSmemBytes = tc::Shape<true, RQ>::kSmemBytes;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)tc::Shape<true>::kSmemBytes);
-    err = cudaLaunchKernelEx(&cfg, kern, qmap, rmap, nq, n, d, row_aux, keyrank, q_aux, q_n2,
-                             gthr, bitmap, rows_per_part, kp, list_base, num_lists, cand,
+                         (int)tc::Shape<true, RQ>::kSmemBytes);
+    err = cudaLaunchKernelEx(&cfg, kern, qmap, qmap2, rmap, nc, nq, n, d, row_aux, keyrank, q_aux,
+                             q_n2, gthr, bitmap, rows_per_part, kp, list_base, num_lists, cand,
                              part_counts, part_sat, q_flags, status);
   } else {
     auto kern = tc::flat_scan_tc_kernel<MODE, false>;
-    cfg.dynamicSmemBytes = tc::Shape<false>::kSmemBytes;
+    cfg.dynamicSmemBytes = tc::Shape<false, RQ>::kSmemBytes;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)tc::Shape<false>::kSmemBytes);
-    err = cudaLaunchKernelEx(&cfg, kern, qmap, rmap, nq, n, d, row_aux, keyrank, q_aux, q_n2,
-                             gthr, bitmap, rows_per_part, kp, list_base, num_lists, cand,
+                         (int)tc::Shape<false, RQ>::kSmemBytes);
+    err = cudaLaunchKernelEx(&cfg, kern, qmap, qmap2, rmap, nc, nq, n, d, row_aux, keyrank, q_aux,
+                             q_n2, gthr, bitmap, rows_per_part, kp, list_base, num_lists, cand,
                              part_counts, part_sat, q_flags, status);
   }
   if (err != cudaSuccess) return err;
@@ -873,7 +933,8 @@ cudaError_t launch_flat_scan_tc(int metric, const __half* queries, int nq, const
                                 int* part_counts, uint64_t* part_sat, int* q_flags, int* status,
                                 cudaStream_t stream) {
 #define XVEC_TC_ARGS                                                                           \
-  nq, queries, rows, n, d, row_stride_elems, 2, row_aux, keyrank, q_aux, q_n2, gthr, bitmap, \
+  nq, queries, nullptr, 0, rows, n, d, row_stride_elems, 2, row_aux, keyrank, q_aux, q_n2,     \
+      gthr, bitmap,                                                                            \
       num_parts, kp, list_base, num_lists, cand, part_counts, part_sat, q_flags, status, stream
   switch (metric) {
     case kMetricL2: return launch_tc<kMetricL2>(XVEC_TC_ARGS);
@@ -893,7 +954,8 @@ cudaError_t launch_sq8_scan_tc(int metric, const int8_t* qcodes, int nq, const i
                                uint64_t* part_sat, int* q_flags, int* status,
                                cudaStream_t stream) {
 #define XVEC_TC_ARGS                                                                           \
-  nq, qcodes, codes, n, d, (int64_t)d, 1, reinterpret_cast<const float*>(row_info), keyrank,  \
+  nq, qcodes, nullptr, 0, codes, n, d, (int64_t)d, 1,                                         \
+      reinterpret_cast<const float*>(row_info), keyrank,                                       \
       reinterpret_cast<const float*>(q_info), nullptr, gthr, bitmap, num_parts, kp, list_base, \
       num_lists, cand, part_counts, part_sat, q_flags, status, stream
   switch (metric) {
@@ -903,6 +965,24 @@ cudaError_t launch_sq8_scan_tc(int metric, const int8_t* qcodes, int nq, const i
   }
 #undef XVEC_TC_ARGS
 }
+
+cudaError_t launch_rabitq_scan_tc(const __half* q_hi, const __half* q_lo, int nq,
+                                  const __half* planes, int64_t n, int padded,
+                                  const float4* row_info, const uint32_t* keyrank,
+                                  const float* q_half_sum, const float* q_gadd, int nc,
+                                  unsigned long long* gthr, const uint32_t* bitmap,
+                                  int num_parts, int kp, int list_base, int num_lists,
+                                  uint64_t* cand, int* part_counts, uint64_t* part_sat,
+                                  int* q_flags, int* status, cudaStream_t stream) {
+  if (nc > tc::kRaBitQMaxClusters) return cudaErrorInvalidValue;
+  return launch_tc<tc::kModeRaBitQ>(nq, q_hi, q_lo, nc, planes, n, padded, (int64_t)padded, 2,
+                                    reinterpret_cast<const float*>(row_info), keyrank,
+                                    q_half_sum, q_gadd, gthr, bitmap, num_parts, kp, list_base,
+                                    num_lists, cand, part_counts, part_sat, q_flags, status,
+                                    stream);
+}
+
+int rabitq_tc_max_clusters() { return tc::kRaBitQMaxClusters; }
 
 bool sq8_tc_supported(int d, const void* codes, const void* qcodes) {
   // 16-byte row strides for TMA; |dot| <= 127^2 d stays exact in float32.

@@ -25,9 +25,12 @@
 #include <cmath>
 #include <vector>
 
+#include <cuda_fp16.h>
+
 #include "capi_internal.h"
 #include "common.cuh"
 #include "flat_kernels.cuh"
+#include "flat_tc.cuh"
 #include "index_kernels.cuh"
 #include "pipeline.cuh"
 #include "refine.cuh"
@@ -261,6 +264,19 @@ __global__ void rabitq_encode_kernel(const float* prepared, int64_t n, int d, in
   }
 }
 
+// The sign bits as binary16 0/1 planes (the tensor-core scan's operand), one
+// thread per code byte.
+__global__ void rabitq_planes_kernel(const uint8_t* __restrict__ codes, int64_t bytes_total,
+                                     __half* __restrict__ planes) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= bytes_total) return;
+  const uint32_t b = codes[i];
+  __align__(16) __half h[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) h[j] = __float2half_rn((float)((b >> j) & 1u));
+  *reinterpret_cast<uint4*>(planes + i * 8) = *reinterpret_cast<const uint4*>(h);
+}
+
 // PrepareQuery (rabitq.go:372-408) + the fast-estimate constants and eps.
 __global__ void rabitq_prep_query_kernel(const float* queries, int nq, int d, int padded,
                                          int truncated, const uint8_t* signs, float inv,
@@ -268,7 +284,8 @@ __global__ void rabitq_prep_query_kernel(const float* queries, int nq, int d, in
                                          int nc, const unsigned* bounds, float* q_rot,
                                          double* q_sum, double* g_add, double* g_error,
                                          float* q_fast_sum, float* q_fast_gadd, float* q_eps,
-                                         int* q_exact, int* q_status, int* q_flags) {
+                                         int* q_exact, int* q_status, int* q_flags,
+                                         __half* q_hi, __half* q_lo, float* q_half_sum) {
   extern __shared__ float v[];
   __shared__ double s_sum;
   __shared__ float s_abs;
@@ -282,7 +299,11 @@ __global__ void rabitq_prep_query_kernel(const float* queries, int nq, int d, in
   __syncthreads();
   // A query PrepareQuery rejects gets neutral values (it is never scored).
   auto reject = [&]() {
-    for (int i = threadIdx.x; i < padded; i += blockDim.x) q_rot[(int64_t)q * padded + i] = 0.f;
+    for (int i = threadIdx.x; i < padded; i += blockDim.x) {
+      q_rot[(int64_t)q * padded + i] = 0.f;
+      q_hi[(int64_t)q * padded + i] = __float2half_rn(0.f);
+      q_lo[(int64_t)q * padded + i] = __float2half_rn(0.f);
+    }
     for (int c = threadIdx.x; c < nc; c += blockDim.x) {
       g_add[(int64_t)q * nc + c] = 0.0;
       g_error[(int64_t)q * nc + c] = 0.0;
@@ -291,6 +312,7 @@ __global__ void rabitq_prep_query_kernel(const float* queries, int nq, int d, in
     if (threadIdx.x == 0) {
       q_sum[q] = 0.0;
       q_fast_sum[q] = 0.f;
+      q_half_sum[q] = 0.f;
       q_eps[q] = 0.f;
       q_exact[q] = 1;
       q_status[q] = XVEC_GPU_NON_FINITE;
@@ -304,13 +326,22 @@ __global__ void rabitq_prep_query_kernel(const float* queries, int nq, int d, in
     reject();
     return;
   }
-  for (int i = threadIdx.x; i < padded; i += blockDim.x) q_rot[(int64_t)q * padded + i] = v[i];
+  for (int i = threadIdx.x; i < padded; i += blockDim.x) {
+    q_rot[(int64_t)q * padded + i] = v[i];
+    // The tensor-core scan's operands: hi + lo = v to about 2^-22 |v|.
+    const __half hi = __float2half_rn(v[i]);
+    q_hi[(int64_t)q * padded + i] = hi;
+    q_lo[(int64_t)q * padded + i] = __float2half_rn(v[i] - __half2float(hi));
+  }
+  __shared__ float s_maxabs;
   if (threadIdx.x == 0) {
     double s = 0.0, a = 0.0;
+    float mx = 0.f;
     int g = 1 << 20;  // least exponent of an ulp among the non-zero values
     for (int i = 0; i < padded; ++i) {
       s = __dadd_rn(s, (double)v[i]);
       a = __dadd_rn(a, fabs((double)v[i]));
+      mx = fmaxf(mx, fabsf(v[i]));
       if (v[i] != 0.f) {
         const int e = (int)((float_bits(v[i]) >> 23) & 0xffu);
         g = min(g, e == 0 ? -149 : e - 150);
@@ -318,8 +349,10 @@ __global__ void rabitq_prep_query_kernel(const float* queries, int nq, int d, in
     }
     s_sum = s;
     s_abs = (float)a;
+    s_maxabs = mx;
     q_sum[q] = s;
     q_fast_sum[q] = __double2float_rn(s);
+    q_half_sum[q] = 0.5f * __double2float_rn(s);
     // Every value is a multiple of 2^g and every partial sum of a subset is
     // at most a in magnitude; below 2^(52+g) all of them are exact in float64,
     // so the masked sums may be taken in any order.
@@ -353,11 +386,17 @@ __global__ void rabitq_prep_query_kernel(const float* queries, int nq, int d, in
     // row can fail makeRaBitQEstimate and the float32 fast rank is finite.
     const double reach = maxA + maxg + maxR * (S1 + 0.5 * sumd) + maxE * maxge;
     if (!(reach < 1e37)) q_flags[q] |= 1 | kRaBitQFullCheck;
-    // Bound on |fast rank - float32(estimate)| (accumulation of up to padded
-    // terms, the float32 roundings of the inputs and of each operation).
-    const double e = maxR * (double)(padded + 2) * kU * S1 +
-                     6.0 * kU * (maxA + maxg + maxR * (S1 + 0.5 * sumd));
+    // Bound on |fast rank - float32(estimate)|: the float32 sum of up to
+    // padded terms (FFMA scan) or of 2 padded products with accumulators
+    // that may truncate plus the hi/lo split (tensor-core scan), the float32
+    // roundings of the inputs and of each operation.
+    const double dot_err = fmax((double)(padded + 2) * kU * S1,
+                                (double)(2 * padded + 8) * 2.0 * kU * S1 + 4.0 * kU * S1 +
+                                    (double)padded * 2.98e-8);
+    const double e = maxR * dot_err + 6.0 * kU * (maxA + maxg + maxR * (S1 + 0.5 * sumd));
     q_eps[q] = (float)(2.5 * e) + 1e-30f;
+    // Values beyond the FP16 range go to the exact scan.
+    if (!(s_maxabs < 6.0e4f)) q_flags[q] |= 1;
     q_status[q] = 0;
   }
 }
@@ -490,7 +529,8 @@ xvec_gpu_status rabitq_reserve(xvec_gpu_index* idx, int64_t cap, cudaStream_t s)
   if ((st = idx->rq_codes.reserve((size_t)cap * bytes, (size_t)n * bytes, s)) ||
       (st = idx->rq_factors.reserve((size_t)cap * sizeof(RaBitQFactors),
                                     (size_t)n * sizeof(RaBitQFactors), s)) ||
-      (st = idx->rq_fast.reserve((size_t)cap * 16, (size_t)n * 16, s)))
+      (st = idx->rq_fast.reserve((size_t)cap * 16, (size_t)n * 16, s)) ||
+      (st = idx->rq_planes.reserve((size_t)cap * idx->padded * 2, (size_t)n * idx->padded * 2, s)))
     return st;
   if (!idx->rq_bounds.ptr) {
     if ((st = idx->rq_bounds.reserve(16, 0, s))) return st;
@@ -530,6 +570,12 @@ xvec_gpu_status rabitq_commit(xvec_gpu_index* idx, int64_t old_n, int64_t m, cud
   XVEC_CUDA(cudaMemcpyAsync(&h, err.ptr, 4, cudaMemcpyDeviceToHost, s));
   XVEC_CUDA(cudaStreamSynchronize(s));
   if (h) return set_error("core: invalid RaBitQ code (status %d)", h), (xvec_gpu_status)h;
+  const int64_t code_bytes = m * (padded / 8);
+  rabitq_planes_kernel<<<blocks_of(code_bytes), 256, 0, s>>>(
+      idx->rq_codes.as<uint8_t>() + old_n * (padded / 8), code_bytes,
+      idx->rq_planes.as<__half>() + old_n * padded);
+  XVEC_LAUNCHED();
+  XVEC_CUDA(cudaGetLastError());
   XVEC_CUDA(cudaMemcpyAsync(idx->rq_bounds.ptr, bounds.ptr, 16, cudaMemcpyDeviceToDevice, s));
   return XVEC_GPU_OK;
 }
@@ -590,7 +636,10 @@ xvec_gpu_status rabitq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq
   const int truncated = floor_pow2(d);
   const float inv = inv_sqrt_size(truncated);
   xvec_gpu_status st;
-  Scratch qrot, qsum, gadd, gerr, qfs, qfg, qeps, qexact, qstatus, qflags;
+  Scratch qrot, qsum, gadd, gerr, qfs, qfg, qeps, qexact, qstatus, qflags, qhi, qlo, qhs;
+  if ((st = qhi.alloc((size_t)nq * padded * 2, s)) || (st = qlo.alloc((size_t)nq * padded * 2, s)) ||
+      (st = qhs.alloc((size_t)nq * 4, s)))
+    return st;
   if ((st = qrot.alloc((size_t)nq * padded * 4, s)) || (st = qsum.alloc((size_t)nq * 8, s)) ||
       (st = gadd.alloc((size_t)nq * nc * 8, s)) || (st = gerr.alloc((size_t)nq * nc * 8, s)) ||
       (st = qfs.alloc((size_t)nq * 4, s)) || (st = qfg.alloc((size_t)nq * nc * 4, s)) ||
@@ -603,7 +652,7 @@ xvec_gpu_status rabitq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq
       metric == XVEC_METRIC_COSINE, metric, idx->rq_rot_centroids.as<float>(), nc,
       idx->rq_bounds.as<unsigned>(), qrot.as<float>(), qsum.as<double>(), gadd.as<double>(),
       gerr.as<double>(), qfs.as<float>(), qfg.as<float>(), qeps.as<float>(), qexact.as<int>(),
-      qstatus.as<int>(), qflags.as<int>());
+      qstatus.as<int>(), qflags.as<int>(), qhi.as<__half>(), qlo.as<__half>(), qhs.as<float>());
   XVEC_LAUNCHED();
   // The approximate stage writes the final results, or the candidates of the
   // refine stage (no radius there: hnsw_rabitq.go:584).
@@ -620,8 +669,46 @@ xvec_gpu_status rabitq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq
                         qsum.as<double>(), gadd.as<double>(), gerr.as<double>(),
                         qeps.as<float>(), qexact.as<int>(), padded, nc};
   const float stage_radius = refine ? 0.f : o.radius;
-  const bool fast = n > 0 && simt_cap_for(kp) <= 512;
-  if (fast) {
+  // FP16 tensor cores on the code planes when the layout allows, else FFMA.
+  const bool use_tc = n > 0 && nc <= rabitq_tc_max_clusters() && kp + 128 <= flat_tc_cap() &&
+                      n < (1ll << 31) - 256 &&
+                      flat_tc_supported(padded, idx->rq_planes.ptr, qhi.ptr) &&
+                      flat_tc_supported(padded, idx->rq_planes.ptr, qlo.ptr);
+  const bool fast = use_tc || (n > 0 && simt_cap_for(kp) <= 512);
+  if (use_tc) {
+    Scratch pkeys, pcounts, psat, kstatus;
+    int lists = 0;
+    if ((st = kstatus.alloc(4, s))) return st;
+    XVEC_CUDA(cudaMemsetAsync(kstatus.ptr, 0, 4, s));
+    timer.mark(1);
+    st = tc_seeded_scan(
+        idx->device, nq, n, kp, s,
+        [&](int64_t b, int64_t e, int p, int list0, int nlists, unsigned long long* gthr,
+            uint64_t* cand, int* counts, uint64_t* sat) {
+          return launch_rabitq_scan_tc(
+              qhi.as<__half>(), qlo.as<__half>(), nq, idx->rq_planes.as<__half>() + b * padded,
+              e - b, padded, idx->rq_fast.as<float4>() + b, idx->keyrank.as<uint32_t>() + b,
+              qhs.as<float>(), qfg.as<float>(), nc, gthr, d_bitmap ? d_bitmap + b / 32 : nullptr,
+              p, kp, list0, nlists, cand, counts, sat, qflags.as<int>(), kstatus.as<int>(), s);
+        },
+        pkeys, pcounts, psat, &lists);
+    if (st) return st;
+    timer.mark(2);
+    XVEC_LAUNCHED();
+    count_tensor_scan();
+    XVEC_CUDA(launch_merge_rescore(sc, idx->pos_of_kr.as<uint32_t>(), idx->keys.as<uint64_t>(),
+                                   nullptr, nq, cc, stage_radius, 0, pkeys.as<uint64_t>(),
+                                   pcounts.as<int>(), psat.as<uint64_t>(), lists, flat_tc_cap(),
+                                   o_keys, o_scores, o_counts, spos.as<uint32_t>(),
+                                   qflags.as<int>(), s));
+    XVEC_LAUNCHED();
+    int h_kstatus = 0;
+    XVEC_CUDA(cudaMemcpyAsync(&h_kstatus, kstatus.ptr, 4, cudaMemcpyDeviceToHost, s));
+    XVEC_CUDA(cudaStreamSynchronize(s));
+    if (h_kstatus != 0)
+      return set_error("tensor-core scan: a bounded device wait expired (code %d)", h_kstatus),
+             XVEC_GPU_TIMEOUT;
+  } else if (fast) {
     const int qtiles = (nq + 31) / 32;
     int parts = (int)std::max<int64_t>(
         1, std::min<int64_t>((592 + qtiles - 1) / qtiles, (n + 1023) / 1024));
