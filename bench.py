@@ -545,22 +545,22 @@ def run_rabitq(args):
         cpu = cpu_rabitq_qps(cents.cpu().numpy(), signs, sample,
                              queries[:max(8, args.cpu_sample_queries // 4)].cpu().numpy(), n)
     if rank == 0:
-        bf16_peak, _, peak_kind = peaks()
-        # Two FP16 passes (the query's high and low parts) over the 0/1 code
-        # planes: 2 x 2 x nq x n x padded flop.
-        flops = 4.0 * nq * (e - b) * padded
-        achieved = flops / (scan_ms / 1000.0) / 1e12 if scan_ms > 0 else None
-        roof = {"bound": "tensor", "achieved": achieved, "peak": bf16_peak, "unit": "TFLOP/s",
-                "frac": (achieved / bf16_peak) if achieved else None, "traffic": None,
-                "peak_source": f"{peak_kind} sustained bf16 dense GEMM; the scan runs on "
-                               "tcgen05 kind::f16 (code planes x query hi/lo)",
+        # INT8 MMAs over the code planes [127 b | b] against the integer query
+        # [h | l]: 2 x nq x n x (2 padded) integer ops.
+        ops = 2.0 * nq * (e - b) * (2 * padded)
+        achieved = ops / (scan_ms / 1000.0) / 1e12 if scan_ms > 0 else None
+        peak = 4500.0
+        roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOP/s",
+                "frac": (achieved / peak) if achieved else None, "traffic": None,
+                "peak_source": "nominal dense INT8 tensor (no measured INT8 figure); the scan "
+                               "runs on tcgen05 kind::i8",
                 "kernel": "RaBitQ code-plane scan", "kernel_ms": scan_ms,
-                "algorithmic_flops_per_launch": flops}
+                "algorithmic_int_ops_per_launch": ops}
         config = {"workload": RQ_WORKLOAD, "global_batch": nq, "top_k": RQ_K, "base_vectors": n,
                   "dim": RQ_DIM, "metric": "l2", "clusters": RQ_NC, "ef": RQ_EF,
                   "parallelism": f"rows sharded over {world} GPU(s), NCCL all-gather + merge",
-                  "l2": "inputs larger than L2 (1.2 GB codes, 38 GB originals)"}
-        print(json.dumps(common_line(nq, ms, e2e_ms, args, world, "1-bit codes, f32/f64 estimates",
+                  "l2": "inputs larger than L2 (19.2 GB code planes, 38 GB originals)"}
+        print(json.dumps(common_line(nq, ms, e2e_ms, args, world, "1-bit codes as i8 planes, i32 dots, f32/f64 estimates",
                                      config, roof, cpu, clocks, st, RQ_K, RQ_DIM, 4)), flush=True)
     finish_ranks(world)
 

@@ -191,8 +191,9 @@ def test_rabitq_invalid_options(xb):
 
 @pytest.mark.parametrize("metric", [L2, IP])
 def test_rabitq_tensor_core_seeded(oracle, xb, metric):
-    """70,000 rows and 200 queries: the FP16 tensor-core scan on CTA pairs in
-    seeding launches plus the rest, refined and not."""
+    """70,000 rows and 200 queries: the INT8 tensor-core scan on CTA pairs in
+    seeding launches plus the rest, refined and not; query magnitudes from
+    1e-8 to 1e6 (each query has its own integer scale)."""
     rng = np.random.default_rng(770 + metric)
     d = 128
     centers = rng.standard_normal((40, d)).astype(np.float32)
@@ -206,4 +207,8 @@ def test_rabitq_tensor_core_seeded(oracle, xb, metric):
     case.check(xb, queries, 10, 100, refine=True)
     assert xb.stats()["tensor_scans"] > before, "tensor-core path not taken"
     case.check(xb, queries, 10, 100, refine=False)
+    scales = np.repeat(np.array([1e-8, 1e-3, 1.0, 1e3, 1e6], np.float32), 40)
+    before = xb.stats()["tensor_scans"]
+    case.check(xb, queries * scales[:, None], 10, 100, refine=False)
+    assert xb.stats()["tensor_scans"] > before
     case.close()

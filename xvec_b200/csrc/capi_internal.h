@@ -173,7 +173,7 @@ struct xvec_gpu_index {
   xvec::DeviceBuffer rq_codes;              // uint8 [n][padded/8]
   xvec::DeviceBuffer rq_factors;            // {double add, rescale, error; int cluster} [n]
   xvec::DeviceBuffer rq_fast;               // float4 {add, rescale, cluster bits, 0} [n]
-  xvec::DeviceBuffer rq_planes;             // binary16 0/1 [n][padded]: the tensor-core operand
+  xvec::DeviceBuffer rq_planes;             // int8 [n][2 padded] (127 b | b): the tensor-core operand
   xvec::DeviceBuffer rq_bounds;             // ordered floats: max |add|, |rescale|, error
 
   ~xvec_gpu_index() {

@@ -54,8 +54,9 @@ constexpr int kThreads = 64 + kEpiWarps * 32;
 constexpr uint32_t kTileABytes = kBM * kBK * 2;  // 16 KB
 // Kernel modes: a Flat metric (FP16 operands, fp32 accumulators);
 // kModeSq8 + metric (INT8 codes, kind::i8, exact int32 accumulators);
-// kModeRaBitQ (FP16 0/1 code planes against a query split into FP16 high and
-// low parts: two MMAs per k-step into one fp32 accumulator).
+// kModeRaBitQ (kind::i8 on the code planes [127 b | b] against each query as
+// integers [h | l], 127 h + l = the query / its scale: one exact int32
+// accumulator).
 constexpr int kModeSq8 = 16;
 constexpr int kModeRaBitQ = 32;
 constexpr int kRaBitQMaxClusters = 16;
@@ -72,8 +73,7 @@ template <bool PAIR, bool RQ = false>
 struct Shape {
   static constexpr int kRowsPerCta = PAIR ? kBN / 2 : kBN;       // B rows loaded per CTA
   static constexpr uint32_t kTileBBytes = kRowsPerCta * kBK * 2;  // 16 or 32 KB
-  static constexpr uint32_t kTileABytesM = RQ ? 2 * kTileABytes : kTileABytes;  // (hi | lo)
-  static constexpr uint32_t kStageBytes = kTileABytesM + kTileBBytes;
+  static constexpr uint32_t kStageBytes = kTileABytes + kTileBBytes;
   static constexpr uint32_t kEpiBytes = epi_smem_bytes(RQ);
   static constexpr int kFit = (int)((kSmemBudget - kEpiBytes) / kStageBytes);
   static constexpr int kStages = kFit < 6 ? kFit : 6;
@@ -378,18 +378,19 @@ __device__ __forceinline__ uint64_t warp_select_compact(uint64_t* gbuf, int cnt,
 
 template <int MODE, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
-    const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap qmap2,
-    const __grid_constant__ CUtensorMap rmap, int nc, int nq,
+    const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap rmap, int nc,
+    int nq,
     int64_t n, int d, const float* __restrict__ row_aux, const uint32_t* __restrict__ keyrank,
     const float* __restrict__ q_aux, const float* __restrict__ q_n2,
     unsigned long long* __restrict__ gthr, const uint32_t* __restrict__ bitmap,
     int64_t rows_per_part, int kp, int list_base, int num_lists, uint64_t* __restrict__ cand,
     int* __restrict__ part_counts, uint64_t* __restrict__ part_sat, int* __restrict__ q_flags,
     int* __restrict__ status) {
-  constexpr bool RQ = MODE == kModeRaBitQ;   // RaBitQ code planes, hi/lo queries
+  constexpr bool RQ = MODE == kModeRaBitQ;   // RaBitQ code planes, integer queries
   constexpr bool SQ = MODE >= kModeSq8 && !RQ;  // INT8 codes (SQ8) instead of FP16 rows
+  constexpr bool I8 = SQ || RQ;                 // kind::i8 operands
   constexpr int METRIC = MODE & 15;
-  constexpr int kElemBytes = SQ ? 1 : 2;
+  constexpr int kElemBytes = I8 ? 1 : 2;
   using S = Shape<PAIR, RQ>;
   constexpr int kStages = S::kStages;
   constexpr uint32_t kStageBytes = S::kStageBytes;
@@ -476,19 +477,13 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
             break;
           }
           unsigned char* a_dst = tiles + stage * kStageBytes;
-          unsigned char* b_dst = a_dst + S::kTileABytesM;
+          unsigned char* b_dst = a_dst + kTileABytes;
           if (issuer) mbar_expect_tx(&full[stage], (PAIR ? 2 : 1) * kStageBytes);
           if constexpr (PAIR) {
             tma_load_2d_pair(&qmap, full0 + stage * 8, a_dst, ks * kStepElems, qblock * kBM);
-            if constexpr (RQ)
-              tma_load_2d_pair(&qmap2, full0 + stage * 8, a_dst + kTileABytes, ks * kStepElems,
-                               qblock * kBM);
             tma_load_2d_pair(&rmap, full0 + stage * 8, b_dst, ks * kStepElems, row0);
           } else {
             tma_load_2d(&qmap, &full[stage], a_dst, ks * kStepElems, qblock * kBM);
-            if constexpr (RQ)
-              tma_load_2d(&qmap2, &full[stage], a_dst + kTileABytes, ks * kStepElems,
-                          qblock * kBM);
             tma_load_2d(&rmap, &full[stage], b_dst, ks * kStepElems, row0);
           }
           ++count[stage];
@@ -530,22 +525,15 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
           tmem_fence_after();
           const unsigned char* a_src = tiles + stage * kStageBytes;
           const uint64_t adesc = smem_desc_sw128(a_src);
-          const uint64_t bdesc = smem_desc_sw128(a_src + S::kTileABytesM);
+          const uint64_t bdesc = smem_desc_sw128(a_src + kTileABytes);
 #pragma unroll
           for (int k = 0; k < 4; ++k) {  // 32 bytes of K per MMA (16 FP16 or 32 INT8)
-            if constexpr (SQ)
+            if constexpr (I8)
               mma_s8<PAIR>(d_tmem, adesc + (uint64_t)(k * 2), bdesc + (uint64_t)(k * 2),
                            (ks > 0 || k > 0) ? 1u : 0u);
             else
               mma_f16<PAIR>(d_tmem, adesc + (uint64_t)(k * 2), bdesc + (uint64_t)(k * 2),
                             (ks > 0 || k > 0) ? 1u : 0u);
-          }
-          if constexpr (RQ) {
-            // The low parts of the queries against the same code planes.
-            const uint64_t adesc_lo = smem_desc_sw128(a_src + kTileABytes);
-#pragma unroll
-            for (int k = 0; k < 4; ++k)
-              mma_f16<PAIR>(d_tmem, adesc_lo + (uint64_t)(k * 2), bdesc + (uint64_t)(k * 2), 1u);
           }
           mma_commit<PAIR>(own_empty0 + stage * 8);
           if (PAIR) mma_commit<PAIR>(peer_empty0 + stage * 8);
@@ -574,9 +562,11 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
     // SQ8: the query's rank terms {A, B, C, ||q||^2} (sq8.cu); q_aux holds them.
     const float4 qinfo = (SQ && qvalid) ? reinterpret_cast<const float4*>(q_aux)[qi]
                                         : make_float4(0.f, 0.f, 0.f, 0.f);
-    // RaBitQ: half the query's coordinate sum (q_aux) and its per-cluster
-    // terms gAdd (q_n2, [nq][nc]) in a per-warp table [cluster][lane].
-    const float rq_hs = (RQ && qvalid) ? q_aux[qi] : 0.f;
+    // RaBitQ: half the query's coordinate sum and its integer scale (q_aux,
+    // float2 per query) and its per-cluster terms gAdd (q_n2, [nq][nc]) in a
+    // per-warp table [cluster][lane].
+    const float2 rq_q = (RQ && qvalid) ? reinterpret_cast<const float2*>(q_aux)[qi]
+                                       : make_float2(0.f, 0.f);
     float* gadd_tab = gadd_all + ew * kRaBitQMaxClusters * 32;
     if constexpr (RQ) {
       for (int c = 0; c < nc; ++c)
@@ -689,7 +679,8 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
             for (int j = 0; j < 32; ++j) {
               const float4 r = meta4[c * 32 + j];
               const float g = gadd_tab[__float_as_int(r.z) * 32 + lane];
-              const float rank = fmaf(r.y, __uint_as_float(cur[j]) - rq_hs, r.x + g);
+              const float dot = (float)(int)cur[j] * rq_q.y;
+              const float rank = fmaf(r.y, dot - rq_q.x, r.x + g);
               if (((vmask >> j) & 1u) && !(rank > thr_f)) {
                 if (!isfinite(rank)) {
                   nonfinite = 1;
@@ -874,7 +865,7 @@ namespace {
 // Launches mode MODE (a Flat metric, or kModeSq8 + metric) on CTA pairs when
 // there are two query blocks, else on single CTAs.
 template <int MODE>
-cudaError_t launch_tc(int nq, const void* queries, const void* queries2, int nc, const void* rows,
+cudaError_t launch_tc(int nq, const void* queries, int nc, const void* rows,
                       int64_t n, int d, int64_t row_stride_elems, int elem_bytes,
                       const float* row_aux,
                       const uint32_t* keyrank, const float* q_aux, const float* q_n2,
@@ -884,9 +875,8 @@ cudaError_t launch_tc(int nq, const void* queries, const void* queries2, int nc,
   const int qblocks = (nq + tc::kBM - 1) / tc::kBM;
   const bool pair = flat_tc_pairs(nq);
   constexpr bool RQ = MODE == tc::kModeRaBitQ;
-  CUtensorMap qmap, qmap2, rmap;
+  CUtensorMap qmap, rmap;
   if (!make_map(&qmap, queries, nq, d, d, tc::kBM, elem_bytes) ||
-      !make_map(&qmap2, queries2 ? queries2 : queries, nq, d, d, tc::kBM, elem_bytes) ||
       !make_map(&rmap, rows, n, d, row_stride_elems,
                 pair ? tc::Shape<true>::kRowsPerCta : tc::Shape<false>::kRowsPerCta, elem_bytes))
     return cudaErrorInvalidValue;
@@ -908,7 +898,7 @@ cudaError_t launch_tc(int nq, const void* queries, const void* queries2, int nc,
     cfg.dynamicSmemBytes = tc::Shape<true, RQ>::kSmemBytes;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)tc::Shape<true, RQ>::kSmemBytes);
-    err = cudaLaunchKernelEx(&cfg, kern, qmap, qmap2, rmap, nc, nq, n, d, row_aux, keyrank, q_aux,
+    err = cudaLaunchKernelEx(&cfg, kern, qmap, rmap, nc, nq, n, d, row_aux, keyrank, q_aux,
                              q_n2, gthr, bitmap, rows_per_part, kp, list_base, num_lists, cand,
                              part_counts, part_sat, q_flags, status);
   } else {
@@ -916,7 +906,7 @@ cudaError_t launch_tc(int nq, const void* queries, const void* queries2, int nc,
     cfg.dynamicSmemBytes = tc::Shape<false, RQ>::kSmemBytes;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)tc::Shape<false, RQ>::kSmemBytes);
-    err = cudaLaunchKernelEx(&cfg, kern, qmap, qmap2, rmap, nc, nq, n, d, row_aux, keyrank, q_aux,
+    err = cudaLaunchKernelEx(&cfg, kern, qmap, rmap, nc, nq, n, d, row_aux, keyrank, q_aux,
                              q_n2, gthr, bitmap, rows_per_part, kp, list_base, num_lists, cand,
                              part_counts, part_sat, q_flags, status);
   }
@@ -933,7 +923,7 @@ cudaError_t launch_flat_scan_tc(int metric, const __half* queries, int nq, const
                                 int* part_counts, uint64_t* part_sat, int* q_flags, int* status,
                                 cudaStream_t stream) {
 #define XVEC_TC_ARGS                                                                           \
-  nq, queries, nullptr, 0, rows, n, d, row_stride_elems, 2, row_aux, keyrank, q_aux, q_n2,     \
+  nq, queries, 0, rows, n, d, row_stride_elems, 2, row_aux, keyrank, q_aux, q_n2,     \
       gthr, bitmap,                                                                            \
       num_parts, kp, list_base, num_lists, cand, part_counts, part_sat, q_flags, status, stream
   switch (metric) {
@@ -954,7 +944,7 @@ cudaError_t launch_sq8_scan_tc(int metric, const int8_t* qcodes, int nq, const i
                                uint64_t* part_sat, int* q_flags, int* status,
                                cudaStream_t stream) {
 #define XVEC_TC_ARGS                                                                           \
-  nq, qcodes, nullptr, 0, codes, n, d, (int64_t)d, 1,                                         \
+  nq, qcodes, 0, codes, n, d, (int64_t)d, 1,                                         \
       reinterpret_cast<const float*>(row_info), keyrank,                                       \
       reinterpret_cast<const float*>(q_info), nullptr, gthr, bitmap, num_parts, kp, list_base, \
       num_lists, cand, part_counts, part_sat, q_flags, status, stream
@@ -966,23 +956,30 @@ cudaError_t launch_sq8_scan_tc(int metric, const int8_t* qcodes, int nq, const i
 #undef XVEC_TC_ARGS
 }
 
-cudaError_t launch_rabitq_scan_tc(const __half* q_hi, const __half* q_lo, int nq,
-                                  const __half* planes, int64_t n, int padded,
-                                  const float4* row_info, const uint32_t* keyrank,
-                                  const float* q_half_sum, const float* q_gadd, int nc,
+cudaError_t launch_rabitq_scan_tc(const int8_t* q_int, int nq, const int8_t* planes, int64_t n,
+                                  int padded, const float4* row_info, const uint32_t* keyrank,
+                                  const float2* q_terms, const float* q_gadd, int nc,
                                   unsigned long long* gthr, const uint32_t* bitmap,
                                   int num_parts, int kp, int list_base, int num_lists,
                                   uint64_t* cand, int* part_counts, uint64_t* part_sat,
                                   int* q_flags, int* status, cudaStream_t stream) {
-  if (nc > tc::kRaBitQMaxClusters) return cudaErrorInvalidValue;
-  return launch_tc<tc::kModeRaBitQ>(nq, q_hi, q_lo, nc, planes, n, padded, (int64_t)padded, 2,
+  if (nc > tc::kRaBitQMaxClusters || !rabitq_tc_supported(padded, planes, q_int))
+    return cudaErrorInvalidValue;
+  return launch_tc<tc::kModeRaBitQ>(nq, q_int, nc, planes, n, 2 * padded, (int64_t)2 * padded, 1,
                                     reinterpret_cast<const float*>(row_info), keyrank,
-                                    q_half_sum, q_gadd, gthr, bitmap, num_parts, kp, list_base,
+                                    reinterpret_cast<const float*>(q_terms), q_gadd, gthr, bitmap, num_parts, kp, list_base,
                                     num_lists, cand, part_counts, part_sat, q_flags, status,
                                     stream);
 }
 
 int rabitq_tc_max_clusters() { return tc::kRaBitQMaxClusters; }
+
+bool rabitq_tc_supported(int padded, const void* planes, const void* q_int) {
+  // Rows of 2 padded bytes in 128-byte k-steps; |dot| <= 16192 padded < 2^31.
+  return padded % 64 == 0 && padded >= 64 && padded <= 65536 &&
+         ((uintptr_t)planes % 16 == 0) && ((uintptr_t)q_int % 16 == 0) &&
+         encode_fn() != nullptr;
+}
 
 bool sq8_tc_supported(int d, const void* codes, const void* qcodes) {
   // 16-byte row strides for TMA; |dot| <= 127^2 d stays exact in float32.

@@ -48,20 +48,22 @@ cudaError_t launch_sq8_scan_tc(int metric, const int8_t* qcodes, int nq, const i
 // True when the INT8 tensor-core scan can take this layout.
 bool sq8_tc_supported(int d, const void* codes, const void* qcodes);
 
-// The same scan for the RaBitQ index: rows = the codes as FP16 0/1 planes
-// [n][padded]; each query = an FP16 high part and an FP16 low part
-// ([nq][padded] each; hi + lo = the rotated query to ~2^-22), multiplied into
-// one fp32 accumulator; ranked with the RaBitQ fast estimate (row_info:
-// {add, rescale, cluster bits, 0}; q_half_sum: sum/2; q_gadd: [nq][nc]).
-cudaError_t launch_rabitq_scan_tc(const __half* q_hi, const __half* q_lo, int nq,
-                                  const __half* planes, int64_t n, int padded,
-                                  const float4* row_info, const uint32_t* keyrank,
-                                  const float* q_half_sum, const float* q_gadd, int nc,
+// The same scan for the RaBitQ index on INT8 tensor cores: rows = the codes
+// as int8 planes [n][2 padded] (127 b | b); each query = integers [nq][2 padded]
+// (h | l) with 127 h + l = round(rotated query / scale), so the int32
+// accumulator is the exact integer dot product of the bits with the scaled
+// query; ranked with the RaBitQ fast estimate (row_info: {add, rescale,
+// cluster bits, 0}; q_terms: {sum/2, scale}; q_gadd: [nq][nc]).
+cudaError_t launch_rabitq_scan_tc(const int8_t* q_int, int nq, const int8_t* planes, int64_t n,
+                                  int padded, const float4* row_info, const uint32_t* keyrank,
+                                  const float2* q_terms, const float* q_gadd, int nc,
                                   unsigned long long* gthr, const uint32_t* bitmap,
                                   int num_parts, int kp, int list_base, int num_lists,
                                   uint64_t* cand, int* part_counts, uint64_t* part_sat,
                                   int* q_flags, int* status, cudaStream_t stream);
 // Most clusters the RaBitQ tensor-core epilogue takes.
 int rabitq_tc_max_clusters();
+// True when the RaBitQ tensor-core scan can take this layout.
+bool rabitq_tc_supported(int padded, const void* planes, const void* q_int);
 
 }  // namespace xvec

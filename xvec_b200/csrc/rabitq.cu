@@ -15,10 +15,13 @@
 //            order, explicit round-to-nearest operations).
 //   query    PrepareQuery: rotated query, float64 sum, per-centroid gAdd and
 //            gError (sequential float64 sums).
-//   scan     fast estimate: the bit-plane x query dot in float32 on the
-//            shared FFMA tile kernel (bits read as 0/1), the estimate formula
-//            in float32 within a bound eps of the reference; candidates are
-//            rescored with EstimateCoarse's float64 masked sum in index order.
+//   scan     fast estimate: the bit-plane x query dot as an exact integer
+//            dot product on INT8 tensor cores (flat_tc.cu; the query rounded
+//            to integers with a per-query scale and an exact bound on that
+//            rounding), or in float32 on the shared FFMA tile kernel; the
+//            estimate formula in float32 within a bound eps of the reference;
+//            candidates are rescored with EstimateCoarse's float64 masked sum
+//            in index order.
 //   refine   the k best by metric.Compute on the original rows among the
 //            candidate_count best estimates (refine.cuh).
 #include <algorithm>
@@ -264,17 +267,34 @@ __global__ void rabitq_encode_kernel(const float* prepared, int64_t n, int d, in
   }
 }
 
-// The sign bits as binary16 0/1 planes (the tensor-core scan's operand), one
-// thread per code byte.
+// The sign bits as the tensor-core scan's int8 planes: row r holds
+// [127 b_0 .. 127 b_{padded-1} | b_0 .. b_{padded-1}], one thread per code byte.
 __global__ void rabitq_planes_kernel(const uint8_t* __restrict__ codes, int64_t bytes_total,
-                                     __half* __restrict__ planes) {
+                                     int padded, int8_t* __restrict__ planes) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= bytes_total) return;
+  const int bpr = padded / 8;
+  const int64_t r = i / bpr;
+  const int col = (int)(i - r * bpr) * 8;
   const uint32_t b = codes[i];
-  __align__(16) __half h[8];
+  uint32_t lo = 0, hi = 0;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) h[j] = __float2half_rn((float)((b >> j) & 1u));
-  *reinterpret_cast<uint4*>(planes + i * 8) = *reinterpret_cast<const uint4*>(h);
+  for (int j = 0; j < 4; ++j) {
+    lo |= ((b >> j) & 1u) << (8 * j);
+    hi |= ((b >> (j + 4)) & 1u) << (8 * j);
+  }
+  int8_t* row = planes + r * 2 * padded;
+  *reinterpret_cast<uint2*>(row + col) = make_uint2(lo * 127u, hi * 127u);
+  *reinterpret_cast<uint2*>(row + padded + col) = make_uint2(lo, hi);
+}
+
+// The query as the integers of the tensor-core scan: w = round(v / scale)
+// with |w| <= kRaBitQIntMax, written as w = 127 h + l (|h| <= 127, |l| <= 63).
+constexpr int kRaBitQIntMax = 127 * 127 + 63;
+__device__ __forceinline__ int rabitq_query_int(float v, float scale) {
+  if (!(scale > 0.f)) return 0;
+  const double w = rint((double)v / (double)scale);
+  return (int)fmin(fmax(w, -(double)kRaBitQIntMax), (double)kRaBitQIntMax);
 }
 
 // PrepareQuery (rabitq.go:372-408) + the fast-estimate constants and eps.
@@ -285,7 +305,7 @@ __global__ void rabitq_prep_query_kernel(const float* queries, int nq, int d, in
                                          double* q_sum, double* g_add, double* g_error,
                                          float* q_fast_sum, float* q_fast_gadd, float* q_eps,
                                          int* q_exact, int* q_status, int* q_flags,
-                                         __half* q_hi, __half* q_lo, float* q_half_sum) {
+                                         int8_t* q_int, float2* q_terms) {
   extern __shared__ float v[];
   __shared__ double s_sum;
   __shared__ float s_abs;
@@ -301,8 +321,8 @@ __global__ void rabitq_prep_query_kernel(const float* queries, int nq, int d, in
   auto reject = [&]() {
     for (int i = threadIdx.x; i < padded; i += blockDim.x) {
       q_rot[(int64_t)q * padded + i] = 0.f;
-      q_hi[(int64_t)q * padded + i] = __float2half_rn(0.f);
-      q_lo[(int64_t)q * padded + i] = __float2half_rn(0.f);
+      q_int[(int64_t)q * 2 * padded + i] = 0;
+      q_int[(int64_t)q * 2 * padded + padded + i] = 0;
     }
     for (int c = threadIdx.x; c < nc; c += blockDim.x) {
       g_add[(int64_t)q * nc + c] = 0.0;
@@ -312,7 +332,7 @@ __global__ void rabitq_prep_query_kernel(const float* queries, int nq, int d, in
     if (threadIdx.x == 0) {
       q_sum[q] = 0.0;
       q_fast_sum[q] = 0.f;
-      q_half_sum[q] = 0.f;
+      q_terms[q] = make_float2(0.f, 0.f);
       q_eps[q] = 0.f;
       q_exact[q] = 1;
       q_status[q] = XVEC_GPU_NON_FINITE;
@@ -326,14 +346,9 @@ __global__ void rabitq_prep_query_kernel(const float* queries, int nq, int d, in
     reject();
     return;
   }
-  for (int i = threadIdx.x; i < padded; i += blockDim.x) {
-    q_rot[(int64_t)q * padded + i] = v[i];
-    // The tensor-core scan's operands: hi + lo = v to about 2^-22 |v|.
-    const __half hi = __float2half_rn(v[i]);
-    q_hi[(int64_t)q * padded + i] = hi;
-    q_lo[(int64_t)q * padded + i] = __float2half_rn(v[i] - __half2float(hi));
-  }
-  __shared__ float s_maxabs;
+  for (int i = threadIdx.x; i < padded; i += blockDim.x) q_rot[(int64_t)q * padded + i] = v[i];
+  __shared__ float s_maxabs, s_scale;
+  __shared__ double s_resid;
   if (threadIdx.x == 0) {
     double s = 0.0, a = 0.0;
     float mx = 0.f;
@@ -352,7 +367,11 @@ __global__ void rabitq_prep_query_kernel(const float* queries, int nq, int d, in
     s_maxabs = mx;
     q_sum[q] = s;
     q_fast_sum[q] = __double2float_rn(s);
-    q_half_sum[q] = 0.5f * __double2float_rn(s);
+    // The scale of the tensor-core scan's integer query.
+    const float scale = mx > 0.f ? mx / (float)kRaBitQIntMax : 0.f;
+    s_scale = scale;
+    s_resid = 0.0;
+    q_terms[q] = make_float2(0.5f * __double2float_rn(s), scale);
     // Every value is a multiple of 2^g and every partial sum of a subset is
     // at most a in magnitude; below 2^(52+g) all of them are exact in float64,
     // so the masked sums may be taken in any order.
@@ -372,6 +391,23 @@ __global__ void rabitq_prep_query_kernel(const float* queries, int nq, int d, in
     q_fast_gadd[(int64_t)q * nc + c] = __double2float_rn(ga);
   }
   __syncthreads();
+  {
+    // The integer query and the bound on its rounding, sum |v_i - scale w_i|
+    // (each term exact in float64; the sum is only a bound).
+    const float scale = s_scale;
+    int8_t* qi = q_int + (int64_t)q * 2 * padded;
+    double resid = 0.0;
+    for (int i = threadIdx.x; i < padded; i += blockDim.x) {
+      const int w = rabitq_query_int(v[i], scale);
+      const int h = (int)rintf((float)w / 127.f);
+      qi[i] = (int8_t)h;
+      qi[padded + i] = (int8_t)(w - 127 * h);
+      resid += fabs((double)v[i] - (double)scale * (double)w);
+    }
+    for (int o = 16; o > 0; o >>= 1) resid += __shfl_xor_sync(0xffffffffu, resid, o);
+    if ((threadIdx.x & 31) == 0) atomicAdd(&s_resid, resid);
+  }
+  __syncthreads();
   if (threadIdx.x == 0) {
     double maxg = 0.0, maxge = 0.0;
     for (int c = 0; c < nc; ++c) {
@@ -387,16 +423,17 @@ __global__ void rabitq_prep_query_kernel(const float* queries, int nq, int d, in
     const double reach = maxA + maxg + maxR * (S1 + 0.5 * sumd) + maxE * maxge;
     if (!(reach < 1e37)) q_flags[q] |= 1 | kRaBitQFullCheck;
     // Bound on |fast rank - float32(estimate)|: the float32 sum of up to
-    // padded terms (FFMA scan) or of 2 padded products with accumulators
-    // that may truncate plus the hi/lo split (tensor-core scan), the float32
-    // roundings of the inputs and of each operation.
+    // padded terms (FFMA scan) or the integer query's rounding plus the
+    // float32 conversion and scaling of the exact integer dot product
+    // (tensor-core scan), the float32 roundings of the inputs and of each
+    // operation.
+    const double resid = s_resid * 1.0001;
     const double dot_err = fmax((double)(padded + 2) * kU * S1,
-                                (double)(2 * padded + 8) * 2.0 * kU * S1 + 4.0 * kU * S1 +
-                                    (double)padded * 2.98e-8);
+                                resid + 3.0 * kU * (S1 + resid));
     const double e = maxR * dot_err + 6.0 * kU * (maxA + maxg + maxR * (S1 + 0.5 * sumd));
     q_eps[q] = (float)(2.5 * e) + 1e-30f;
-    // Values beyond the FP16 range go to the exact scan.
-    if (!(s_maxabs < 6.0e4f)) q_flags[q] |= 1;
+    // Magnitudes whose scale would lose precision go to the exact scan.
+    if (!(s_maxabs < 1e30f) || (s_maxabs > 0.f && s_maxabs < 1e-30f)) q_flags[q] |= 1;
     q_status[q] = 0;
   }
 }
@@ -530,7 +567,8 @@ xvec_gpu_status rabitq_reserve(xvec_gpu_index* idx, int64_t cap, cudaStream_t s)
       (st = idx->rq_factors.reserve((size_t)cap * sizeof(RaBitQFactors),
                                     (size_t)n * sizeof(RaBitQFactors), s)) ||
       (st = idx->rq_fast.reserve((size_t)cap * 16, (size_t)n * 16, s)) ||
-      (st = idx->rq_planes.reserve((size_t)cap * idx->padded * 2, (size_t)n * idx->padded * 2, s)))
+      (st = idx->rq_planes.reserve((size_t)cap * idx->padded * 2, (size_t)n * idx->padded * 2,
+                                     s)))
     return st;
   if (!idx->rq_bounds.ptr) {
     if ((st = idx->rq_bounds.reserve(16, 0, s))) return st;
@@ -572,8 +610,8 @@ xvec_gpu_status rabitq_commit(xvec_gpu_index* idx, int64_t old_n, int64_t m, cud
   if (h) return set_error("core: invalid RaBitQ code (status %d)", h), (xvec_gpu_status)h;
   const int64_t code_bytes = m * (padded / 8);
   rabitq_planes_kernel<<<blocks_of(code_bytes), 256, 0, s>>>(
-      idx->rq_codes.as<uint8_t>() + old_n * (padded / 8), code_bytes,
-      idx->rq_planes.as<__half>() + old_n * padded);
+      idx->rq_codes.as<uint8_t>() + old_n * (padded / 8), code_bytes, padded,
+      idx->rq_planes.as<int8_t>() + old_n * 2 * padded);
   XVEC_LAUNCHED();
   XVEC_CUDA(cudaGetLastError());
   XVEC_CUDA(cudaMemcpyAsync(idx->rq_bounds.ptr, bounds.ptr, 16, cudaMemcpyDeviceToDevice, s));
@@ -636,9 +674,8 @@ xvec_gpu_status rabitq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq
   const int truncated = floor_pow2(d);
   const float inv = inv_sqrt_size(truncated);
   xvec_gpu_status st;
-  Scratch qrot, qsum, gadd, gerr, qfs, qfg, qeps, qexact, qstatus, qflags, qhi, qlo, qhs;
-  if ((st = qhi.alloc((size_t)nq * padded * 2, s)) || (st = qlo.alloc((size_t)nq * padded * 2, s)) ||
-      (st = qhs.alloc((size_t)nq * 4, s)))
+  Scratch qrot, qsum, gadd, gerr, qfs, qfg, qeps, qexact, qstatus, qflags, qint, qterms;
+  if ((st = qint.alloc((size_t)nq * padded * 2, s)) || (st = qterms.alloc((size_t)nq * 8, s)))
     return st;
   if ((st = qrot.alloc((size_t)nq * padded * 4, s)) || (st = qsum.alloc((size_t)nq * 8, s)) ||
       (st = gadd.alloc((size_t)nq * nc * 8, s)) || (st = gerr.alloc((size_t)nq * nc * 8, s)) ||
@@ -652,7 +689,7 @@ xvec_gpu_status rabitq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq
       metric == XVEC_METRIC_COSINE, metric, idx->rq_rot_centroids.as<float>(), nc,
       idx->rq_bounds.as<unsigned>(), qrot.as<float>(), qsum.as<double>(), gadd.as<double>(),
       gerr.as<double>(), qfs.as<float>(), qfg.as<float>(), qeps.as<float>(), qexact.as<int>(),
-      qstatus.as<int>(), qflags.as<int>(), qhi.as<__half>(), qlo.as<__half>(), qhs.as<float>());
+      qstatus.as<int>(), qflags.as<int>(), qint.as<int8_t>(), qterms.as<float2>());
   XVEC_LAUNCHED();
   // The approximate stage writes the final results, or the candidates of the
   // refine stage (no radius there: hnsw_rabitq.go:584).
@@ -669,11 +706,10 @@ xvec_gpu_status rabitq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq
                         qsum.as<double>(), gadd.as<double>(), gerr.as<double>(),
                         qeps.as<float>(), qexact.as<int>(), padded, nc};
   const float stage_radius = refine ? 0.f : o.radius;
-  // FP16 tensor cores on the code planes when the layout allows, else FFMA.
+  // INT8 tensor cores on the code planes when the layout allows, else FFMA.
   const bool use_tc = n > 0 && nc <= rabitq_tc_max_clusters() && kp + 128 <= flat_tc_cap() &&
                       n < (1ll << 31) - 256 &&
-                      flat_tc_supported(padded, idx->rq_planes.ptr, qhi.ptr) &&
-                      flat_tc_supported(padded, idx->rq_planes.ptr, qlo.ptr);
+                      rabitq_tc_supported(padded, idx->rq_planes.ptr, qint.ptr);
   const bool fast = use_tc || (n > 0 && simt_cap_for(kp) <= 512);
   if (use_tc) {
     Scratch pkeys, pcounts, psat, kstatus;
@@ -686,9 +722,9 @@ xvec_gpu_status rabitq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq
         [&](int64_t b, int64_t e, int p, int list0, int nlists, unsigned long long* gthr,
             uint64_t* cand, int* counts, uint64_t* sat) {
           return launch_rabitq_scan_tc(
-              qhi.as<__half>(), qlo.as<__half>(), nq, idx->rq_planes.as<__half>() + b * padded,
-              e - b, padded, idx->rq_fast.as<float4>() + b, idx->keyrank.as<uint32_t>() + b,
-              qhs.as<float>(), qfg.as<float>(), nc, gthr, d_bitmap ? d_bitmap + b / 32 : nullptr,
+              qint.as<int8_t>(), nq, idx->rq_planes.as<int8_t>() + b * 2 * padded, e - b,
+              padded, idx->rq_fast.as<float4>() + b, idx->keyrank.as<uint32_t>() + b,
+              qterms.as<float2>(), qfg.as<float>(), nc, gthr, d_bitmap ? d_bitmap + b / 32 : nullptr,
               p, kp, list0, nlists, cand, counts, sat, qflags.as<int>(), kstatus.as<int>(), s);
         },
         pkeys, pcounts, psat, &lists);
