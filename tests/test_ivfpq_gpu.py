@@ -1,7 +1,8 @@
 """IVF-PQ list scan and k-means assignment: CUDA path against the oracle.
 
-The PQ scan's scores are the reference's float64 look-up sums, so keys and
-float32 scores must be identical."""
+The scan ranks codes by a float32 look-up sum and rescores its candidates
+with the reference's float64 sums, so keys and float32 scores must be
+identical."""
 import numpy as np
 import pytest
 
@@ -81,6 +82,39 @@ def test_ivfpq_filter_radius_and_more_probes_than_lists(oracle, xb):
             bitmap[p >> 5] |= np.uint32(1 << (p & 31))
     run(oracle, xb, L2, rows, keys, queries, centroids, pivots, 16, 20, 4, bitmap=bitmap)
     run(oracle, xb, L2, rows, keys, queries, centroids, pivots, 16, 20, 99, radius=9.0)
+
+
+@pytest.mark.parametrize("metric", [L2, IP])
+@pytest.mark.parametrize("chunks", [64, 128])
+def test_ivfpq_wide_chunks(oracle, xb, metric, chunks):
+    """64 chunks: the fast scan with two chunk groups per lane; 128 chunks:
+    the exact scan alone."""
+    rng = np.random.default_rng(70 + chunks + metric)
+    rows = mixture(rng, 3000, 128)
+    keys = rng.permutation(1 << 20)[:3000].astype(np.uint64)
+    queries = mixture(rng, 21, 128)
+    centroids = rows[rng.choice(3000, 12, replace=False)].copy()
+    pivots = rows[rng.choice(3000, 256, replace=False)].copy()
+    xb.reset_stats()
+    run(oracle, xb, metric, rows, keys, queries, centroids, pivots, chunks, 10, 4)
+    exact = xb.stats()["exact_queries"]
+    assert exact == (0 if chunks == 64 else 21), exact
+
+
+def test_ivfpq_fast_scan_falls_back_on_ties(oracle, xb):
+    """700 copies of one row: more equal fast ranks than a warp's list
+    keeps, so the fast pass cannot prove its candidates complete and those
+    queries take the exact scan; results stay the reference's."""
+    rng = np.random.default_rng(5)
+    rows = mixture(rng, 4000, 32)
+    rows[1000:1700] = rows[17]
+    keys = rng.permutation(1 << 20)[:4000].astype(np.uint64)
+    queries = np.concatenate([rows[17:18] + 0.01, mixture(rng, 9, 32)]).astype(np.float32)
+    centroids = rows[rng.choice(4000, 8, replace=False)].copy()
+    pivots = rows[rng.choice(4000, 256, replace=False)].copy()
+    xb.reset_stats()
+    run(oracle, xb, L2, rows, keys, queries, centroids, pivots, 8, 10, 8)
+    assert xb.stats()["exact_queries"] >= 1
 
 
 @pytest.mark.parametrize("metric", [L2, IP, COSINE, MIPSL2])

@@ -163,6 +163,10 @@ struct xvec_gpu_index {
   xvec::DeviceBuffer list_rows;     // uint32 [n] positions grouped by list (insertion order)
   xvec::DeviceBuffer list_codes;    // uint8 [n][chunks] the PQ codes in list_rows order
   xvec::DeviceBuffer list_keyrank;  // uint32 [n] key ranks in list_rows order
+  // The codes again for the fast scan, 32 G chunk slots per code: code i of
+  // a list holds at byte t its chunk (i mod 32 + t) mod 32 G (zero past the
+  // last chunk).
+  xvec::DeviceBuffer list_codes_t;  // uint8 [n][32 G] in list_rows order
   bool lists_dirty = true;
 
   // RaBitQ (one-bit).

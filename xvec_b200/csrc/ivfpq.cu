@@ -12,11 +12,17 @@
 //   scan    PQDistanceTable.Lookup (pq.go:574-595) of every code of every
 //           probed list: a float64 sum in chunk order, rounded to float32
 //           with the overflow check; filter before scoring, ties by key.
+//           The fast scan ranks the codes by a float32 sum (one code per
+//           lane, each code's bytes rotated so that the 32 look-ups of a warp
+//           hit 32 different shared-memory banks) and the merge rescores
+//           the candidates within its error bound with that float64 sum; the
+//           exact scan (float64 sums throughout) takes the queries the fast
+//           pass cannot settle, and layouts it does not cover.
 //   insert  KMeansModel.Nearest (kmeans.go:169-175) for the list and
 //           PQModel.Encode (pq.go:274-301) for the code: per chunk the best
 //           of the 256 pivots, ties to the lower id.
-// The scan's scores are the reference scores, so its per-list selections are
-// merged in exact mode.
+// The exact scan's scores are the reference scores, so its per-list
+// selections are merged in exact mode.
 #include <cub/device/device_radix_sort.cuh>
 #include <cub/device/device_scan.cuh>
 
@@ -166,8 +172,8 @@ __global__ void __launch_bounds__(kScanWarps * 32, 2) ivfpq_scan_kernel(
     const uint64_t* __restrict__ probe_lists, const int* __restrict__ probe_counts, int nprobe,
     const int64_t* __restrict__ list_offsets, const uint32_t* __restrict__ list_rows,
     const uint32_t* __restrict__ list_keyrank, const uint32_t* __restrict__ bitmap, int metric,
-    int kp, uint64_t* __restrict__ part_keys, int* __restrict__ part_counts,
-    uint64_t* __restrict__ part_sat, int* __restrict__ q_flags) {
+    int kp, const int* __restrict__ query_ids, uint64_t* __restrict__ part_keys,
+    int* __restrict__ part_counts, uint64_t* __restrict__ part_sat, int* __restrict__ q_flags) {
   constexpr int kPer = 2;
   constexpr int kStep = 32 * kPer;  // codes per warp step
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -175,7 +181,7 @@ __global__ void __launch_bounds__(kScanWarps * 32, 2) ivfpq_scan_kernel(
   uint64_t* wbuf = reinterpret_cast<uint64_t*>(slut + chunks * 256);    // [warps][CAPW]
   __shared__ AccumState wst[kScanWarps];
   __shared__ unsigned long long s_thr;
-  const int q = blockIdx.x;
+  const int q = query_ids ? query_ids[blockIdx.x] : blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int i = threadIdx.x; i < chunks * 256; i += blockDim.x)
     slut[i] = (LutT)table[(int64_t)q * chunks * 256 + i];
@@ -268,6 +274,167 @@ __global__ void __launch_bounds__(kScanWarps * 32, 2) ivfpq_scan_kernel(
   __syncwarp();
   warp_compact<CAPW>(buf, st, kp);
   const int out = min(st->count, kp);
+  const int64_t slot = (int64_t)blockIdx.x * kScanWarps + warp;
+  for (int i = lane; i < out; i += 32) part_keys[slot * kp + i] = buf[i];
+  if (lane == 0) {
+    part_counts[slot] = out;
+    part_sat[slot] = st->thr;
+  }
+}
+
+// Fast scan: the same block-per-query structure on a float32 rank, one
+// code per lane and no cross-lane reduction.  The table is staged as rows
+// of W = 32 G + 32 entries, T2[e][s] = T[e][s mod 32 G] (zero past
+// `chunks`), and each code of a list is stored with its 32 G chunk bytes
+// rotated by its position in the list mod 32, so lane l reads byte t of its
+// code and looks up chunk (l + t) mod 32 G at T2[e][l + t]: the 32 lanes of
+// a look-up always hit 32 different banks.  Four float32 accumulators per
+// lane (terms t mod 4); the rank is within q_eps of the reference's float64
+// sum rounded to float32 (8 G - 1 sequential additions per accumulator, two
+// combining levels, one rounding of the reference's result, over terms
+// bounded by the per-chunk maxima).  A warp walks its 32-code blocks of all
+// probed lists in order with the next block's codes loaded ahead into
+// registers.  A non-finite or near-overflow rank sends the query to the
+// exact scan (q_flags bit 2); the merge rescores the candidates in reference
+// order.
+template <int G>
+__device__ __forceinline__ void load_code(const uint8_t* codes_t, int64_t idx, bool ok,
+                                          uint4 (&c)[2 * G]) {
+  const uint4* p = reinterpret_cast<const uint4*>(codes_t + idx * (32 * G));
+#pragma unroll
+  for (int i = 0; i < 2 * G; ++i) c[i] = ok ? __ldg(p + i) : make_uint4(0u, 0u, 0u, 0u);
+}
+template <int G>
+__device__ __forceinline__ uint32_t rot_byte(const uint4 (&c)[2 * G], int t) {
+  const uint4& v = c[t >> 4];
+  const int w = (t >> 2) & 3;
+  const uint32_t word = w == 0 ? v.x : w == 1 ? v.y : w == 2 ? v.z : v.w;
+  return (word >> (8 * (t & 3))) & 0xffu;
+}
+
+template <int CAPW, int G>
+__global__ void __launch_bounds__(kScanWarps * 32, 1) ivfpq_fast_kernel(
+    const float* __restrict__ table, int chunks, const uint8_t* __restrict__ codes_t,
+    const uint64_t* __restrict__ probe_lists, const int* __restrict__ probe_counts, int nprobe,
+    const int64_t* __restrict__ list_offsets, const uint32_t* __restrict__ list_rows,
+    const uint32_t* __restrict__ list_keyrank, const uint32_t* __restrict__ bitmap, int metric,
+    int kp, uint64_t* __restrict__ part_keys, int* __restrict__ part_counts,
+    uint64_t* __restrict__ part_sat, float* __restrict__ q_eps, int* __restrict__ q_flags) {
+  constexpr int kSlots = 32 * G;
+  constexpr int W = kSlots + 32;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  float* lut = reinterpret_cast<float*>(smem_raw);                            // [256][W]
+  uint64_t* wbuf = reinterpret_cast<uint64_t*>(lut + 256 * W);              // [warps][CAPW]
+  __shared__ AccumState wst[kScanWarps];
+  __shared__ unsigned long long s_thr;
+  __shared__ float s_cmax[kSlots];
+  const int q = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float* tq = table + (int64_t)q * chunks * 256;
+  for (int i = threadIdx.x; i < 256 * W; i += blockDim.x) {
+    const int e = i / W, c = (i % W) % kSlots;
+    lut[i] = c < chunks ? __ldg(tq + c * 256 + e) : 0.f;
+  }
+  // Per-chunk maxima |T[.][c]| for the error bound.
+  for (int c = warp; c < kSlots; c += kScanWarps) {
+    float m = 0.f;
+    if (c < chunks)
+      for (int e = lane; e < 256; e += 32) m = fmaxf(m, fabsf(__ldg(tq + c * 256 + e)));
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(kFullMask, m, o));
+    if (lane == 0) s_cmax[c] = m;
+  }
+  if (lane == 0) {
+    wst[warp].count = 0;
+    wst[warp].saturated = 0;
+    wst[warp].thr = kEmptyKey;
+  }
+  if (threadIdx.x == 0) s_thr = kEmptyKey;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double sum = 0.0;
+    for (int c = 0; c < kSlots; ++c) sum += (double)s_cmax[c];
+    q_eps[q] = __double2float_ru((double)(8 * G + 3) * 5.9604644775390625e-8 * 1.001 * sum);
+  }
+  uint64_t* buf = wbuf + warp * CAPW;
+  AccumState* st = &wst[warp];
+  int cnt = 0;
+  uint64_t wthr = kEmptyKey;
+  const float* lb = lut + lane;
+  const int nl = probe_counts[q];
+
+  // Cursor over this warp's blocks: list cj, block cbb of the list; it
+  // starts before list 0, so the first next_block() enters it.
+  int cj = -1, cbb = 0, cnb = 0;
+  int64_t cbegin = 0, cend = 0;
+  auto next_block = [&]() {
+    cbb += kScanWarps;
+    while (cbb >= cnb) {
+      if (++cj >= nl) return;
+      const uint64_t list = probe_lists[(int64_t)q * nprobe + cj];
+      cbegin = list_offsets[list];
+      cend = list_offsets[list + 1];
+      cnb = (int)((cend - cbegin + 31) >> 5);
+      cbb = warp;
+    }
+  };
+  next_block();
+  bool have = cj < nl;
+  int64_t idx = have ? cbegin + (int64_t)cbb * 32 + lane : 0;
+  int64_t lend = cend;
+  uint4 code[2 * G];
+  load_code<G>(codes_t, idx, have && idx < lend, code);
+  while (have) {
+    // The next block's codes, in flight while this one is scored.
+    next_block();
+    const bool have_next = cj < nl;
+    const int64_t nidx = have_next ? cbegin + (int64_t)cbb * 32 + lane : 0;
+    const int64_t nend = cend;
+    uint4 ncode[2 * G];
+    load_code<G>(codes_t, nidx, have_next && nidx < nend, ncode);
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int t = 0; t < kSlots; ++t) acc[t & 3] += lb[rot_byte<G>(code, t) * W + t];
+    const float fast = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+    bool valid = idx < lend;
+    if (bitmap && valid) valid = bitmap_pass(bitmap, list_rows[idx]);
+    const uint64_t shared_thr = *(volatile unsigned long long*)&s_thr;
+    const uint64_t thr = shared_thr < wthr ? shared_thr : wthr;
+    bool take = false;
+    uint64_t key = 0;
+    if (valid) {
+      if (!(fabsf(fast) < 3.0e38f)) {
+        atomicOr(&q_flags[q], 2);
+      } else {
+        const uint32_t ord = float_to_ordered(rank_from_score(metric, fast));
+        if (ord <= (uint32_t)(thr >> 32)) {
+          key = ((uint64_t)ord << 32) | list_keyrank[idx];
+          take = key < thr;
+        }
+      }
+    }
+    const unsigned m = __ballot_sync(kFullMask, take);
+    if (take) buf[cnt + __popc(m & ((1u << lane) - 1))] = key;
+    cnt += __popc(m);
+    if (cnt > CAPW - 32) {
+      __syncwarp();
+      if (lane == 0) st->count = cnt;
+      __syncwarp();
+      warp_compact<CAPW>(buf, st, kp);
+      cnt = st->count;
+      wthr = st->thr;
+      if (lane == 0 && wthr != kEmptyKey) atomicMin(&s_thr, (unsigned long long)wthr);
+    }
+    have = have_next;
+    idx = nidx;
+    lend = nend;
+#pragma unroll
+    for (int i = 0; i < 2 * G; ++i) code[i] = ncode[i];
+  }
+  __syncwarp();
+  if (lane == 0) st->count = cnt;
+  __syncwarp();
+  warp_compact<CAPW>(buf, st, kp);
+  const int out = min(st->count, kp);
   const int64_t slot = (int64_t)q * kScanWarps + warp;
   for (int i = lane; i < out; i += 32) part_keys[slot * kp + i] = buf[i];
   if (lane == 0) {
@@ -281,13 +448,14 @@ struct PQScorer {
   const float* table;
   const uint8_t* codes;
   int chunks;
+  const float* q_eps;  // fast-rank error bound per query (null: exact lists)
   __device__ float score(int qi, int64_t row) const {
     float s;
     if (!pq_lookup(table + (int64_t)qi * chunks * 256, codes + row * chunks, chunks, &s))
       return __int_as_float(0x7fc00000);
     return s;
   }
-  __device__ float eps(int) const { return 0.f; }
+  __device__ float eps(int qi) const { return q_eps ? q_eps[qi] : 0.f; }
   __device__ int error_flag(float) const { return 8; }
   __device__ float output(float r) const { return score_from_rank(metric, r); }
   __device__ bool keep(float out, float radius) const { return within_radius(metric, out, radius); }
@@ -301,6 +469,11 @@ __global__ void ivfpq_status_kernel(const int* q_status, const int* q_flags, int
   if (st == 0 && (q_flags[i] & 4)) st = XVEC_GPU_NON_FINITE;
   if (st == 0 && (q_flags[i] & 8)) st = XVEC_GPU_OVERFLOW;
   if (st != 0) out_counts[i] = -st;
+}
+
+__global__ void clear_flag_kernel(const int* ids, int n, int bit, int* q_flags) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) q_flags[ids[i]] &= ~bit;
 }
 
 __global__ void count_lists_kernel(const int32_t* row_list, int64_t n, int64_t* counts) {
@@ -436,6 +609,25 @@ __global__ void gather_list_major_kernel(const uint32_t* __restrict__ list_rows,
   }
 }
 
+// The fast scan's code layout (list_codes_t), one CTA per list: code i of
+// the list holds at byte t its chunk (i mod 32 + t) mod slots (zero past
+// `chunks`).
+__global__ void rotate_list_codes_kernel(const int64_t* __restrict__ list_offsets, int chunks,
+                                         int slots, const uint8_t* __restrict__ list_codes,
+                                         uint8_t* __restrict__ codes_t) {
+  const int l = blockIdx.x;
+  const int64_t begin = list_offsets[l], len = list_offsets[l + 1] - begin;
+  for (int64_t x = threadIdx.x; x < len * slots; x += blockDim.x) {
+    const int64_t i = x / slots;
+    const int t = (int)(x - i * slots);
+    const int c = ((int)(i & 31) + t) % slots;
+    codes_t[(begin + i) * slots + t] = c < chunks ? list_codes[(begin + i) * chunks + c] : (uint8_t)0;
+  }
+}
+
+// Chunk slots of the fast scan (0: the layout does not apply).
+int fast_slots(int chunks) { return chunks <= 32 ? 32 : chunks <= 64 ? 64 : 0; }
+
 static xvec_gpu_status rebuild_lists(xvec_gpu_index* idx, cudaStream_t s) {
   const int64_t n = idx->n;
   const int nlist = idx->nlist;
@@ -473,6 +665,16 @@ static xvec_gpu_status rebuild_lists(xvec_gpu_index* idx, cudaStream_t s) {
       idx->list_keyrank.as<uint32_t>());
   XVEC_LAUNCHED();
   XVEC_CUDA(cudaGetLastError());
+  const int slots = fast_slots(chunks);
+  if (slots > 0) {
+    const size_t bytes = (size_t)std::max<int64_t>(n, 1) * slots;
+    if ((st = idx->list_codes_t.reserve(bytes, 0, s))) return st;
+    rotate_list_codes_kernel<<<nlist, 256, 0, s>>>(idx->list_offsets.as<int64_t>(), chunks, slots,
+                                                   idx->list_codes.as<uint8_t>(),
+                                                   idx->list_codes_t.as<uint8_t>());
+    XVEC_LAUNCHED();
+    XVEC_CUDA(cudaGetLastError());
+  }
   XVEC_CUDA(cudaStreamSynchronize(s));
   idx->lists_dirty = false;
   return XVEC_GPU_OK;
@@ -527,49 +729,111 @@ xvec_gpu_status ivfpq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
                                      idx->chunk_offsets.as<int>(), chunks, table.as<float>(),
                                      qflags.as<int>());
   XVEC_LAUNCHED();
+  int exact_count = 0;
   if (n > 0) {
     int capw = 128;
     while (capw < kp + 64) capw <<= 1;
     if (capw > 1024) return set_error("top_k %d too large for the IVF-PQ scan", k), XVEC_GPU_INVALID_ARGUMENT;
-    Scratch lkeys, lcounts, lsat;
+    Scratch lkeys, lcounts, lsat, qeps;
     const size_t lists = (size_t)nq * kScanWarps;
     if ((st = lkeys.alloc(lists * kp * 8, s)) || (st = lcounts.alloc(lists * 4, s)) ||
-        (st = lsat.alloc(lists * 8, s)))
+        (st = lsat.alloc(lists * 8, s)) || (st = qeps.alloc((size_t)nq * 4, s)))
       return st;
-    // The table as float64 in shared memory when it fits next to the buffers.
     const size_t bufs = (size_t)kScanWarps * capw * 8;
-    const bool lut64 = (size_t)chunks * 256 * 8 + bufs <= 200 * 1024;
-    const size_t smem = (size_t)chunks * 256 * (lut64 ? 8 : 4) + bufs;
-    if (smem > 220 * 1024) return set_error("too many PQ chunks for the scan"), XVEC_GPU_UNSUPPORTED;
-    timer.mark(1);
+    // Exact scan: the table as float64 in shared memory when it fits next
+    // to the buffers.
+    auto exact_scan = [&](const int* ids, int count) -> xvec_gpu_status {
+      const bool lut64 = (size_t)chunks * 256 * 8 + bufs <= 200 * 1024;
+      const size_t smem = (size_t)chunks * 256 * (lut64 ? 8 : 4) + bufs;
+      if (smem > 220 * 1024) return set_error("too many PQ chunks for the scan"), XVEC_GPU_UNSUPPORTED;
 #define XVEC_PQ_CASE(C, T)                                                                     \
   if (capw == C && lut64 == (sizeof(T) == 8)) {                                                \
     auto kern = ivfpq_scan_kernel<C, T>;                                                       \
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);        \
-    kern<<<nq, kScanWarps * 32, smem, s>>>(                                                    \
+    kern<<<count, kScanWarps * 32, smem, s>>>(                                                 \
         table.as<float>(), chunks, idx->list_codes.as<uint8_t>(), pkeys_probe.as<uint64_t>(),  \
         pcounts_probe.as<int>(), nprobe, idx->list_offsets.as<int64_t>(),                      \
         idx->list_rows.as<uint32_t>(), idx->list_keyrank.as<uint32_t>(), d_bitmap, metric, kp, \
-        lkeys.as<uint64_t>(), lcounts.as<int>(), lsat.as<uint64_t>(), qflags.as<int>());       \
+        ids, lkeys.as<uint64_t>(), lcounts.as<int>(), lsat.as<uint64_t>(), qflags.as<int>());  \
   }
-    XVEC_PQ_CASE(128, double)
-    XVEC_PQ_CASE(256, double)
-    XVEC_PQ_CASE(512, double)
-    XVEC_PQ_CASE(1024, double)
-    XVEC_PQ_CASE(128, float)
-    XVEC_PQ_CASE(256, float)
-    XVEC_PQ_CASE(512, float)
-    XVEC_PQ_CASE(1024, float)
+      XVEC_PQ_CASE(128, double)
+      XVEC_PQ_CASE(256, double)
+      XVEC_PQ_CASE(512, double)
+      XVEC_PQ_CASE(1024, double)
+      XVEC_PQ_CASE(128, float)
+      XVEC_PQ_CASE(256, float)
+      XVEC_PQ_CASE(512, float)
+      XVEC_PQ_CASE(1024, float)
 #undef XVEC_PQ_CASE
-    timer.mark(2);
-    XVEC_LAUNCHED();
-    XVEC_CUDA(cudaGetLastError());
-    PQScorer sc{metric, table.as<float>(), idx->pq_codes.as<uint8_t>(), chunks};
-    XVEC_CUDA(launch_merge_rescore(sc, idx->pos_of_kr.as<uint32_t>(), idx->keys.as<uint64_t>(),
-                                   nullptr, nq, k, o.radius, 1, lkeys.as<uint64_t>(),
-                                   lcounts.as<int>(), lsat.as<uint64_t>(), kScanWarps, kp, d_keys,
-                                   d_scores, d_counts, nullptr, qflags.as<int>(), s));
-    XVEC_LAUNCHED();
+      XVEC_LAUNCHED();
+      XVEC_CUDA(cudaGetLastError());
+      PQScorer sc{metric, table.as<float>(), idx->pq_codes.as<uint8_t>(), chunks, nullptr};
+      XVEC_CUDA(launch_merge_rescore(sc, idx->pos_of_kr.as<uint32_t>(), idx->keys.as<uint64_t>(),
+                                     ids, count, k, o.radius, 1, lkeys.as<uint64_t>(),
+                                     lcounts.as<int>(), lsat.as<uint64_t>(), kScanWarps, kp,
+                                     d_keys, d_scores, d_counts, nullptr, qflags.as<int>(), s));
+      XVEC_LAUNCHED();
+      return XVEC_GPU_OK;
+    };
+    // Fast scan: the widened table and the warps' lists.
+    const int slots = fast_slots(chunks);
+    const size_t fast_smem = (size_t)256 * (slots + 32) * 4 + bufs;
+    const bool fast = slots > 0 && fast_smem <= 220 * 1024;
+    timer.mark(1);
+    if (fast) {
+      bool launched = false;
+#define XVEC_PQ_FAST(C, G)                                                                     \
+  if (capw == C && slots == 32 * G) {                                                          \
+    auto kern = ivfpq_fast_kernel<C, G>;                                                       \
+    launched = true;                                                                           \
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fast_smem);   \
+    kern<<<nq, kScanWarps * 32, fast_smem, s>>>(                                               \
+        table.as<float>(), chunks, idx->list_codes_t.as<uint8_t>(), pkeys_probe.as<uint64_t>(), \
+        pcounts_probe.as<int>(), nprobe, idx->list_offsets.as<int64_t>(), idx->list_rows.as<uint32_t>(),                \
+        idx->list_keyrank.as<uint32_t>(), d_bitmap, metric, kp, lkeys.as<uint64_t>(),          \
+        lcounts.as<int>(), lsat.as<uint64_t>(), qeps.as<float>(), qflags.as<int>());           \
+  }
+      XVEC_PQ_FAST(128, 1)
+      XVEC_PQ_FAST(256, 1)
+      XVEC_PQ_FAST(512, 1)
+      XVEC_PQ_FAST(1024, 1)
+      XVEC_PQ_FAST(128, 2)
+      XVEC_PQ_FAST(256, 2)
+      XVEC_PQ_FAST(512, 2)
+#undef XVEC_PQ_FAST
+      if (!launched) return set_error("no fast IVF-PQ scan for this layout"), XVEC_GPU_UNSUPPORTED;
+      timer.mark(2);
+      XVEC_LAUNCHED();
+      XVEC_CUDA(cudaGetLastError());
+      PQScorer sc{metric, table.as<float>(), idx->pq_codes.as<uint8_t>(), chunks, qeps.as<float>()};
+      XVEC_CUDA(launch_merge_rescore(sc, idx->pos_of_kr.as<uint32_t>(), idx->keys.as<uint64_t>(),
+                                     nullptr, nq, k, o.radius, 0, lkeys.as<uint64_t>(),
+                                     lcounts.as<int>(), lsat.as<uint64_t>(), kScanWarps, kp,
+                                     d_keys, d_scores, d_counts, nullptr, qflags.as<int>(), s));
+      XVEC_LAUNCHED();
+      // Queries the fast pass could not settle go through the exact scan.
+      std::vector<int> h_fl(nq), exact_list;
+      XVEC_CUDA(cudaMemcpyAsync(h_fl.data(), qflags.ptr, (size_t)nq * 4, cudaMemcpyDeviceToHost, s));
+      XVEC_CUDA(cudaStreamSynchronize(s));
+      for (int q = 0; q < nq; ++q)
+        if (probe_status[q] == 0 && (h_fl[q] & 2)) exact_list.push_back(q);
+      if (!exact_list.empty()) {
+        const int nl = (int)exact_list.size();
+        Scratch ids;
+        if ((st = ids.alloc((size_t)nl * 4, s))) return st;
+        XVEC_CUDA(cudaMemcpyAsync(ids.ptr, exact_list.data(), (size_t)nl * 4,
+                                  cudaMemcpyHostToDevice, s));
+        clear_flag_kernel<<<blocks_of(nl), 256, 0, s>>>(ids.as<int>(), nl, 2, qflags.as<int>());
+        XVEC_LAUNCHED();
+        if ((st = exact_scan(ids.as<int>(), nl))) return st;
+        XVEC_CUDA(cudaStreamSynchronize(s));
+        exact_count = nl;
+      }
+    } else {
+      if ((st = exact_scan(nullptr, nq))) return st;
+      timer.mark(2);
+      exact_count = nq;
+    }
   }
   ivfpq_status_kernel<<<blocks_of(nq), 256, 0, s>>>(qstatus.as<int>(), qflags.as<int>(), nq,
                                                     d_counts);
@@ -579,7 +843,7 @@ xvec_gpu_status ivfpq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
   XVEC_CUDA(cudaMemcpyAsync(h_flags.data(), qflags.ptr, (size_t)nq * 4, cudaMemcpyDeviceToHost, s));
   timer.mark(3);
   XVEC_CUDA(cudaStreamSynchronize(s));
-  count_search(nq, 0, timer.ms(1, 2), timer.ms(0, 3));
+  count_search(nq, exact_count, timer.ms(1, 2), timer.ms(0, 3));
   if (statuses) {
     statuses->resize(nq);
     for (int q = 0; q < nq; ++q) {
