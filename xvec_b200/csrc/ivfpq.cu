@@ -312,8 +312,13 @@ __device__ __forceinline__ uint32_t rot_byte(const uint4 (&c)[2 * G], int t) {
   return (word >> (8 * (t & 3))) & 0xffu;
 }
 
+// Two CTAs per SM where the shared memory allows (32 G + 32 table columns
+// plus the lists: G = 1 with lists of <= 256 keys).
 template <int CAPW, int G>
-__global__ void __launch_bounds__(kScanWarps * 32, 1) ivfpq_fast_kernel(
+constexpr int fast_min_blocks() { return (G == 1 && CAPW <= 256) ? 2 : 1; }
+
+template <int CAPW, int G>
+__global__ void __launch_bounds__(kScanWarps * 32, (fast_min_blocks<CAPW, G>())) ivfpq_fast_kernel(
     const float* __restrict__ table, int chunks, const uint8_t* __restrict__ codes_t,
     const uint64_t* __restrict__ probe_lists, const int* __restrict__ probe_counts, int nprobe,
     const int64_t* __restrict__ list_offsets, const uint32_t* __restrict__ list_rows,
