@@ -28,6 +28,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <utility>
 #include <vector>
 
 #include "capi_internal.h"
@@ -304,12 +305,27 @@ __device__ __forceinline__ void load_code(const uint8_t* codes_t, int64_t idx, b
 #pragma unroll
   for (int i = 0; i < 2 * G; ++i) c[i] = ok ? __ldg(p + i) : make_uint4(0u, 0u, 0u, 0u);
 }
+// Byte t of the code as an integer (one PRMT).
 template <int G>
 __device__ __forceinline__ uint32_t rot_byte(const uint4 (&c)[2 * G], int t) {
   const uint4& v = c[t >> 4];
   const int w = (t >> 2) & 3;
   const uint32_t word = w == 0 ? v.x : w == 1 ? v.y : w == 2 ? v.z : v.w;
-  return (word >> (8 * (t & 3))) & 0xffu;
+  return __byte_perm(word, 0u, 0x4440u | (uint32_t)(t & 3));
+}
+// ld.shared.f32 at addr + OFF (OFF an immediate of the instruction).
+template <int OFF>
+__device__ __forceinline__ float lds_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1+%2];" : "=f"(v) : "r"(addr), "n"(OFF));
+  return v;
+}
+// The 32 G look-ups of one code: term t = T2[byte t][lane + t], summed into
+// accumulator t mod 4.
+template <int G, int W, int... T>
+__device__ __forceinline__ void pq_lookups(const uint4 (&code)[2 * G], uint32_t lbase,
+                                           float (&acc)[4], std::integer_sequence<int, T...>) {
+  ((acc[T & 3] += lds_f32<T * 4>(rot_byte<G>(code, T) * (uint32_t)(W * 4) + lbase)), ...);
 }
 
 // Two CTAs per SM where the shared memory allows (32 G + 32 table columns
@@ -364,7 +380,8 @@ __global__ void __launch_bounds__(kScanWarps * 32, (fast_min_blocks<CAPW, G>()))
   AccumState* st = &wst[warp];
   int cnt = 0;
   uint64_t wthr = kEmptyKey;
-  const float* lb = lut + lane;
+  // Shared-memory address of this lane's column of the table.
+  const uint32_t lbase = (uint32_t)__cvta_generic_to_shared(lut + lane);
   const int nl = probe_counts[q];
 
   // Cursor over this warp's blocks: list cj, block cbb of the list; it
@@ -397,37 +414,43 @@ __global__ void __launch_bounds__(kScanWarps * 32, (fast_min_blocks<CAPW, G>()))
     uint4 ncode[2 * G];
     load_code<G>(codes_t, nidx, have_next && nidx < nend, ncode);
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int t = 0; t < kSlots; ++t) acc[t & 3] += lb[rot_byte<G>(code, t) * W + t];
+    pq_lookups<G, W>(code, lbase, acc, std::make_integer_sequence<int, kSlots>{});
     const float fast = (acc[0] + acc[1]) + (acc[2] + acc[3]);
-    bool valid = idx < lend;
-    if (bitmap && valid) valid = bitmap_pass(bitmap, list_rows[idx]);
     const uint64_t shared_thr = *(volatile unsigned long long*)&s_thr;
     const uint64_t thr = shared_thr < wthr ? shared_thr : wthr;
-    bool take = false;
-    uint64_t key = 0;
-    if (valid) {
-      if (!(fabsf(fast) < 3.0e38f)) {
-        atomicOr(&q_flags[q], 2);
-      } else {
-        const uint32_t ord = float_to_ordered(rank_from_score(metric, fast));
-        if (ord <= (uint32_t)(thr >> 32)) {
-          key = ((uint64_t)ord << 32) | list_keyrank[idx];
-          take = key < thr;
+    // Common case first: no lane's rank can enter the list (the float bound
+    // is NaN, accepting everything, until a list is full).
+    const float rank = rank_from_score(metric, fast);
+    const bool in_list = idx < lend;
+    const bool maybe = in_list && (!(rank > rank_of(thr)) || !(fabsf(fast) < 3.0e38f));
+    if (__any_sync(kFullMask, maybe)) {
+      bool valid = in_list;
+      if (bitmap && valid) valid = bitmap_pass(bitmap, list_rows[idx]);
+      bool take = false;
+      uint64_t key = 0;
+      if (valid) {
+        if (!(fabsf(fast) < 3.0e38f)) {
+          atomicOr(&q_flags[q], 2);
+        } else {
+          const uint32_t ord = float_to_ordered(rank);
+          if (ord <= (uint32_t)(thr >> 32)) {
+            key = ((uint64_t)ord << 32) | list_keyrank[idx];
+            take = key < thr;
+          }
         }
       }
-    }
-    const unsigned m = __ballot_sync(kFullMask, take);
-    if (take) buf[cnt + __popc(m & ((1u << lane) - 1))] = key;
-    cnt += __popc(m);
-    if (cnt > CAPW - 32) {
-      __syncwarp();
-      if (lane == 0) st->count = cnt;
-      __syncwarp();
-      warp_compact<CAPW>(buf, st, kp);
-      cnt = st->count;
-      wthr = st->thr;
-      if (lane == 0 && wthr != kEmptyKey) atomicMin(&s_thr, (unsigned long long)wthr);
+      const unsigned m = __ballot_sync(kFullMask, take);
+      if (take) buf[cnt + __popc(m & ((1u << lane) - 1))] = key;
+      cnt += __popc(m);
+      if (cnt > CAPW - 32) {
+        __syncwarp();
+        if (lane == 0) st->count = cnt;
+        __syncwarp();
+        warp_compact<CAPW>(buf, st, kp);
+        cnt = st->count;
+        wthr = st->thr;
+        if (lane == 0 && wthr != kEmptyKey) atomicMin(&s_thr, (unsigned long long)wthr);
+      }
     }
     have = have_next;
     idx = nidx;
