@@ -1,7 +1,8 @@
-"""Tensor-core (tcgen05) scan for FP16 Flat search: parity with the oracle.
+"""Tensor-core (tcgen05) scan for Flat search: parity with the oracle.
 
-The FP16 path ranks candidates with tcgen05.mma and rescores them in the
-reference order, so scores must be bit-identical and key lists identical."""
+FP16 storage and FP32 storage (bfloat16 high/low parts, three MMAs per
+k-step) rank candidates with tcgen05.mma and rescore them in the reference
+order, so scores must be bit-identical and key lists identical."""
 import numpy as np
 import pytest
 
@@ -125,3 +126,56 @@ def test_tc_large_scale_property(xb):
     assert torch.equal(ok[:, 0], pick * 3)
     assert (os_[:, 0] <= 1e-6).all()
     assert (os_[:, 1:] >= os_[:, :-1]).all()
+
+
+def run32(oracle, xb, metric, rows, queries, keys, k, bitmap=None, radius=0.0, exact_ok=False):
+    """FP32 storage: the tensor-core scan on bfloat16 high/low parts."""
+    idx = xb.DenseFlatIndex(rows.shape[1], metric, xb.STORAGE_FP32)
+    idx.add(keys, rows)
+    st0 = xb.stats()
+    res = idx.search_with_options(queries, xb.SearchOptions(top_k=k, filter=bitmap, radius=radius))
+    st1 = xb.stats()
+    assert st1["tensor_scans"] == st0["tensor_scans"] + 1, "tensor-core path not taken"
+    if not exact_ok:
+        assert st1["exact_queries"] == st0["exact_queries"], "fast pass did not settle"
+    st, ok, os_, oc, _ = oracle.flat_search(metric, rows, keys, queries, k, radius, bitmap)
+    assert st == 0
+    assert np.array_equal(res.counts, oc)
+    for q in range(queries.shape[0]):
+        c = int(oc[q])
+        assert np.array_equal(res.keys[q, :c], ok[q, :c]), q
+        assert np.array_equal(res.scores[q, :c].view(np.uint32), os_[q, :c].view(np.uint32)), q
+    idx.close()
+
+
+@pytest.mark.parametrize("metric", [L2, IP, COSINE, MIPSL2])
+def test_tc_fp32_split(oracle, xb, metric):
+    """FP32 rows: 70,000 x 128 (a seeding launch plus the rest, CTA pairs),
+    k = 1 (nearest-centroid assignment) and k = 64 (an IVF probe), and a
+    filter."""
+    rng = np.random.default_rng(300 + metric)
+    n = 70_000
+    rows = mixture(rng, n, 128, normalise=False)
+    rows[5000:5050] = rows[10:60]            # duplicates across the prefix boundary
+    keys = rng.permutation(1 << 22)[:n].astype(np.uint64)
+    queries = mixture(rng, 300, 128, normalise=False)
+    queries[:3] = rows[[10, 5000, 69999]]
+    run32(oracle, xb, metric, rows, queries, keys, 1)
+    run32(oracle, xb, metric, rows, queries, keys, 64)
+    bitmap = np.zeros((n + 31) // 32, np.uint32)
+    for p in range(n):
+        if (p * 11) % 5 != 0:
+            bitmap[p >> 5] |= np.uint32(1 << (p & 31))
+    run32(oracle, xb, metric, rows, queries[:100], keys, 10, bitmap=bitmap)
+
+
+@pytest.mark.parametrize("scale", [1e-18, 1e15])
+def test_tc_fp32_split_magnitudes(oracle, xb, scale):
+    """bfloat16 keeps float32's exponent range: tiny and huge rows need no
+    scaling; the bound is relative to the norms."""
+    rng = np.random.default_rng(int(-np.log10(scale)) + 40)
+    rows = (mixture(rng, 5000, 64, normalise=False) * scale).astype(np.float32)
+    keys = np.arange(5000, dtype=np.uint64)
+    queries = (mixture(rng, 150, 64, normalise=False) * scale).astype(np.float32)
+    for metric in (L2, IP, COSINE):
+        run32(oracle, xb, metric, rows, queries, keys, 10, exact_ok=True)

@@ -266,8 +266,23 @@ xvec_gpu_status flat_search_impl(xvec_gpu_index* idx, const void* d_q, int nq,
 
   std::vector<int> h_status(nq), h_flags(nq);
   const int kp = choose_kp(k);
-  const bool use_tc = std::is_same<RowT, __half>::value && n > 0 && n < (1ll << 31) - 256 &&
-                      kp + 128 <= flat_tc_cap() && flat_tc_supported(d, rows, d_q);
+  // FP32 rows: the tensor-core scan on bfloat16 high/low parts of the rows
+  // (kept beside them) and of the queries.
+  constexpr bool kSplit = std::is_same<RowT, float>::value;
+  Scratch qhi, qlo;
+  const bool tc_layout = n > 0 && n < (1ll << 31) - 256 && kp + 128 <= flat_tc_cap() &&
+                         d % 8 == 0 && d >= 64;
+  if (kSplit && tc_layout) {
+    if ((st = qhi.alloc((size_t)nq * d * 2, s)) || (st = qlo.alloc((size_t)nq * d * 2, s)))
+      return st;
+    XVEC_CUDA(launch_split_bf16(static_cast<const float*>(d_q), (int64_t)nq * d,
+                                qhi.as<__nv_bfloat16>(), qlo.as<__nv_bfloat16>(), s));
+    XVEC_LAUNCHED();
+  }
+  const bool use_tc =
+      tc_layout && (kSplit ? flat_tc_supported(d, idx->rows_bhi.ptr, qhi.ptr) &&
+                                 flat_tc_supported(d, idx->rows_blo.ptr, qlo.ptr)
+                           : flat_tc_supported(d, rows, d_q));
   const bool fast = use_tc || (simt_cap_for(kp) <= 512 && n > 0);
   if (use_tc) {
     if (is_cancelled(o)) return set_error("cancelled"), XVEC_GPU_CANCELLED;
@@ -282,6 +297,15 @@ xvec_gpu_status flat_search_impl(xvec_gpu_index* idx, const void* d_q, int nq,
                         [&](int64_t b, int64_t e, int p, int list0, int nlists,
                             unsigned long long* gthr, uint64_t* cand, int* counts,
                             uint64_t* sat) {
+                          if (kSplit)
+                            return launch_flat_scan_tc_split(
+                                metric, qhi.as<__nv_bfloat16>(), qlo.as<__nv_bfloat16>(), nq,
+                                idx->rows_bhi.as<__nv_bfloat16>() + b * d,
+                                idx->rows_blo.as<__nv_bfloat16>() + b * d, e - b, d, row_aux + b,
+                                idx->keyrank.as<uint32_t>() + b, qaux.as<float>(),
+                                qn2.as<float>(), gthr, d_bitmap ? d_bitmap + b / 32 : nullptr, p,
+                                kp, list0, nlists, cand, counts, sat, qflags.as<int>(),
+                                kstatus.as<int>(), s);
                           return launch_flat_scan_tc(
                               metric, static_cast<const __half*>(d_q), nq, hrows + b * d, e - b,
                               d, d, row_aux + b, idx->keyrank.as<uint32_t>() + b,
@@ -299,7 +323,7 @@ xvec_gpu_status flat_search_impl(xvec_gpu_index* idx, const void* d_q, int nq,
         rows, d, idx->pos_of_kr.as<uint32_t>(), idx->keys.as<uint64_t>(), qf.as<float>(),
         qn2.as<float>(), idx->max_n2.as<unsigned>(), nullptr, nq, metric, k, o.radius, 0,
         pkeys.as<uint64_t>(), pcounts.as<int>(), psat.as<uint64_t>(), lists, cap, d_keys_out,
-        d_scores_out, d_counts_out, qflags.as<int>(), s));
+        d_scores_out, d_counts_out, qflags.as<int>(), s, kSplit ? 1 : 0));
     XVEC_LAUNCHED();
   } else if (fast) {
     if (is_cancelled(o)) return set_error("cancelled"), XVEC_GPU_CANCELLED;

@@ -177,6 +177,10 @@ struct xvec_gpu_index {
   xvec::DeviceBuffer rq_codes;              // uint8 [n][padded/8]
   xvec::DeviceBuffer rq_factors;            // {double add, rescale, error; int cluster} [n]
   xvec::DeviceBuffer rq_fast;               // float4 {add, rescale, cluster bits, 0} [n]
+  // Flat FP32: the rows as bfloat16 high and low parts (the tensor-core
+  // scan's operands; the float32 rows stay the reference data).
+  xvec::DeviceBuffer rows_bhi;              // bf16 [n][d]
+  xvec::DeviceBuffer rows_blo;              // bf16 [n][d]
   xvec::DeviceBuffer rq_planes;             // int8 [n][2 padded] (127 b | b): the tensor-core operand
   xvec::DeviceBuffer rq_bounds;             // ordered floats: max |add|, |rescale|, error
 

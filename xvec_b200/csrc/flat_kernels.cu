@@ -133,9 +133,15 @@ __device__ __forceinline__ float fast_rank(int metric, float dot, float xn2, flo
 // Bound on |fast rank - reference rank| for a query (both accumulate d
 // exact-or-rounded products in float32; factor 4 covers both sides and a
 // non round-to-nearest accumulator).
-__device__ __forceinline__ float fast_eps(int metric, int d, float qn2, float max_xn2) {
+// split: the fast dot came from bfloat16 high/low parts (three products per
+// element, x = hi + lo to 2^-18 |x|, the lo·lo product dropped) accumulated
+// in fp32 by the tensor cores, whose additions may truncate: a relative
+// bound of 3.2·2^-18 + (3d + 8)·2u on top.
+__device__ __forceinline__ float fast_eps(int metric, int d, float qn2, float max_xn2,
+                                          int split = 0) {
   const float u = 5.9604645e-8f;  // 2^-24
-  const float g = 4.f * (float)(d + 8) * u;
+  const float g = 4.f * (float)(d + 8) * u +
+                  (split ? 2.f * (3.2f * 3.8146973e-6f + (float)(3 * d + 8) * 2.f * u) : 0.f);
   const float qn = sqrtf(qn2), xn = sqrtf(max_xn2);
   switch (metric) {
     case kMetricL2: return g * (xn + qn) * (xn + qn) * 1.0001f;
@@ -173,11 +179,12 @@ struct FlatScorer {
   int d;
   const float* q_n2;
   const unsigned* max_n2_ordered;
+  int split;  // fast ranks from the bfloat16-split tensor-core scan
   __device__ float score(int qi, int64_t row) const {
     return warp_reference_score(metric, rows + row * d, qf + (int64_t)qi * d, d);
   }
   __device__ float eps(int qi) const {
-    return fast_eps(metric, d, q_n2[qi], ordered_to_float(*max_n2_ordered));
+    return fast_eps(metric, d, q_n2[qi], ordered_to_float(*max_n2_ordered), split);
   }
   __device__ int error_flag(float) const { return 4; }
   __device__ float output(float r) const { return score_from_rank(metric, r); }
@@ -320,8 +327,8 @@ cudaError_t launch_flat_merge_rescore(const RowT* rows, int d, const uint32_t* p
                                       const uint64_t* part_keys, const int* part_counts,
                                       const uint64_t* part_sat, int num_parts, int stride,
                                       uint64_t* out_keys, float* out_scores, int* out_counts,
-                                      int* q_flags, cudaStream_t stream) {
-  FlatScorer<RowT> sc{metric, rows, qf, d, q_n2, max_n2};
+                                      int* q_flags, cudaStream_t stream, int split_eps) {
+  FlatScorer<RowT> sc{metric, rows, qf, d, q_n2, max_n2, split_eps};
   return launch_merge_rescore(sc, pos_of_keyrank, keys, query_ids, nlist, k, radius, exact_mode,
                               part_keys, part_counts, part_sat, num_parts, stride, out_keys,
                               out_scores, out_counts, nullptr, q_flags, stream);
@@ -331,13 +338,13 @@ template cudaError_t launch_flat_merge_rescore<float>(const float*, int, const u
                                                       const unsigned*, const int*, int, int, int,
                                                       float, int, const uint64_t*, const int*,
                                                       const uint64_t*, int, int, uint64_t*, float*,
-                                                      int*, int*, cudaStream_t);
+                                                      int*, int*, cudaStream_t, int);
 template cudaError_t launch_flat_merge_rescore<__half>(const __half*, int, const uint32_t*,
                                                        const uint64_t*, const float*,
                                                        const float*, const unsigned*, const int*,
                                                        int, int, int, float, int, const uint64_t*,
                                                        const int*, const uint64_t*, int, int,
                                                        uint64_t*, float*, int*, int*,
-                                                       cudaStream_t);
+                                                       cudaStream_t, int);
 
 }  // namespace xvec

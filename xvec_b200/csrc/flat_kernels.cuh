@@ -52,6 +52,6 @@ cudaError_t launch_flat_merge_rescore(const RowT* rows, int d, const uint32_t* p
                                       const uint64_t* part_keys, const int* part_counts,
                                       const uint64_t* part_sat, int num_parts, int stride,
                                       uint64_t* out_keys, float* out_scores, int* out_counts,
-                                      int* q_flags, cudaStream_t stream);
+                                      int* q_flags, cudaStream_t stream, int split_eps = 0);
 
 }  // namespace xvec

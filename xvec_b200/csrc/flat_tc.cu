@@ -57,8 +57,12 @@ constexpr uint32_t kTileABytes = kBM * kBK * 2;  // 16 KB
 // kModeRaBitQ (kind::i8 on the code planes [127 b | b] against each query as
 // integers [h | l], 127 h + l = the query / its scale: one exact int32
 // accumulator).
+// kModeSplit + metric (float32 rows and queries as bfloat16 high + low
+// parts: hi·hi + hi·lo + lo·hi, three MMAs per k-step into one fp32
+// accumulator).
 constexpr int kModeSq8 = 16;
 constexpr int kModeRaBitQ = 32;
+constexpr int kModeSplit = 64;
 constexpr int kRaBitQMaxClusters = 16;
 // Per epilogue warp: radix histogram (1 KB) + the current tile's row
 // metadata for its 128 columns (aux floats + key ranks, 1 KB; SQ8/RaBitQ: the
@@ -69,11 +73,12 @@ constexpr uint32_t epi_smem_bytes(bool rq) {
 }
 constexpr uint32_t kSmemBudget = 232448 - 1024 - 1024 - 512;  // dynamic bytes for stages
 
-template <bool PAIR, bool RQ = false>
+template <bool PAIR, bool RQ = false, bool SPLIT = false>
 struct Shape {
   static constexpr int kRowsPerCta = PAIR ? kBN / 2 : kBN;       // B rows loaded per CTA
   static constexpr uint32_t kTileBBytes = kRowsPerCta * kBK * 2;  // 16 or 32 KB
-  static constexpr uint32_t kStageBytes = kTileABytes + kTileBBytes;
+  static constexpr int kParts = SPLIT ? 2 : 1;                    // high (+ low) tiles
+  static constexpr uint32_t kStageBytes = kParts * (kTileABytes + kTileBBytes);
   static constexpr uint32_t kEpiBytes = epi_smem_bytes(RQ);
   static constexpr int kFit = (int)((kSmemBudget - kEpiBytes) / kStageBytes);
   static constexpr int kStages = kFit < 6 ? kFit : 6;
@@ -191,6 +196,27 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(const void* tile) {
 template <int M>
 constexpr uint32_t idesc_f16() {
   return (1u << 4) | ((uint32_t)(kBN >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// kind::f16 with A/B = BF16, D = F32.
+template <int M>
+constexpr uint32_t idesc_bf16() {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kBN >> 3) << 17) |
+         ((uint32_t)(M >> 4) << 24);
+}
+template <bool PAIR>
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t acc) {
+  if constexpr (PAIR) {
+    asm volatile(
+        "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(idesc_bf16<2 * kBM>()), "r"(acc));
+  } else {
+    asm volatile(
+        "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(idesc_bf16<kBM>()), "r"(acc));
+  }
 }
 
 // kind::i8: A/B signed 8-bit, D = S32.
@@ -378,7 +404,8 @@ __device__ __forceinline__ uint64_t warp_select_compact(uint64_t* gbuf, int cnt,
 
 template <int MODE, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
-    const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap rmap, int nc,
+    const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap rmap,
+    const __grid_constant__ CUtensorMap qmap2, const __grid_constant__ CUtensorMap rmap2, int nc,
     int nq,
     int64_t n, int d, const float* __restrict__ row_aux, const uint32_t* __restrict__ keyrank,
     const float* __restrict__ q_aux, const float* __restrict__ q_n2,
@@ -387,11 +414,12 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
     int* __restrict__ part_counts, uint64_t* __restrict__ part_sat, int* __restrict__ q_flags,
     int* __restrict__ status) {
   constexpr bool RQ = MODE == kModeRaBitQ;   // RaBitQ code planes, integer queries
-  constexpr bool SQ = MODE >= kModeSq8 && !RQ;  // INT8 codes (SQ8) instead of FP16 rows
+  constexpr bool SQ = (MODE & kModeSq8) != 0;   // INT8 codes (SQ8) instead of FP16 rows
+  constexpr bool SPLIT = (MODE & kModeSplit) != 0;  // bfloat16 high/low parts of float32
   constexpr bool I8 = SQ || RQ;                 // kind::i8 operands
   constexpr int METRIC = MODE & 15;
   constexpr int kElemBytes = I8 ? 1 : 2;
-  using S = Shape<PAIR, RQ>;
+  using S = Shape<PAIR, RQ, SPLIT>;
   constexpr int kStages = S::kStages;
   constexpr uint32_t kStageBytes = S::kStageBytes;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -476,15 +504,26 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
             *s_abort = 1;
             break;
           }
+          // Stage layout: A (high), B (high)[, A (low), B (low)].
           unsigned char* a_dst = tiles + stage * kStageBytes;
           unsigned char* b_dst = a_dst + kTileABytes;
+          unsigned char* a2_dst = b_dst + S::kTileBBytes;
+          unsigned char* b2_dst = a2_dst + kTileABytes;
           if (issuer) mbar_expect_tx(&full[stage], (PAIR ? 2 : 1) * kStageBytes);
           if constexpr (PAIR) {
             tma_load_2d_pair(&qmap, full0 + stage * 8, a_dst, ks * kStepElems, qblock * kBM);
             tma_load_2d_pair(&rmap, full0 + stage * 8, b_dst, ks * kStepElems, row0);
+            if constexpr (SPLIT) {
+              tma_load_2d_pair(&qmap2, full0 + stage * 8, a2_dst, ks * kStepElems, qblock * kBM);
+              tma_load_2d_pair(&rmap2, full0 + stage * 8, b2_dst, ks * kStepElems, row0);
+            }
           } else {
             tma_load_2d(&qmap, &full[stage], a_dst, ks * kStepElems, qblock * kBM);
             tma_load_2d(&rmap, &full[stage], b_dst, ks * kStepElems, row0);
+            if constexpr (SPLIT) {
+              tma_load_2d(&qmap2, &full[stage], a2_dst, ks * kStepElems, qblock * kBM);
+              tma_load_2d(&rmap2, &full[stage], b2_dst, ks * kStepElems, row0);
+            }
           }
           ++count[stage];
           if (++stage == kStages) {
@@ -531,9 +570,25 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
             if constexpr (I8)
               mma_s8<PAIR>(d_tmem, adesc + (uint64_t)(k * 2), bdesc + (uint64_t)(k * 2),
                            (ks > 0 || k > 0) ? 1u : 0u);
+            else if constexpr (SPLIT)
+              mma_bf16<PAIR>(d_tmem, adesc + (uint64_t)(k * 2), bdesc + (uint64_t)(k * 2),
+                             (ks > 0 || k > 0) ? 1u : 0u);
             else
               mma_f16<PAIR>(d_tmem, adesc + (uint64_t)(k * 2), bdesc + (uint64_t)(k * 2),
                             (ks > 0 || k > 0) ? 1u : 0u);
+          }
+          if constexpr (SPLIT) {
+            // The high query part against the low row part, and the low
+            // query part against the high row part.
+            const uint64_t a2desc = smem_desc_sw128(a_src + kTileABytes + S::kTileBBytes);
+            const uint64_t b2desc =
+                smem_desc_sw128(a_src + 2 * kTileABytes + S::kTileBBytes);
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              mma_bf16<PAIR>(d_tmem, adesc + (uint64_t)(k * 2), b2desc + (uint64_t)(k * 2), 1u);
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              mma_bf16<PAIR>(d_tmem, a2desc + (uint64_t)(k * 2), bdesc + (uint64_t)(k * 2), 1u);
           }
           mma_commit<PAIR>(own_empty0 + stage * 8);
           if (PAIR) mma_commit<PAIR>(peer_empty0 + stage * 8);
@@ -865,7 +920,8 @@ namespace {
 // Launches mode MODE (a Flat metric, or kModeSq8 + metric) on CTA pairs when
 // there are two query blocks, else on single CTAs.
 template <int MODE>
-cudaError_t launch_tc(int nq, const void* queries, int nc, const void* rows,
+cudaError_t launch_tc(int nq, const void* queries, const void* queries2, int nc, const void* rows,
+                      const void* rows2,
                       int64_t n, int d, int64_t row_stride_elems, int elem_bytes,
                       const float* row_aux,
                       const uint32_t* keyrank, const float* q_aux, const float* q_n2,
@@ -875,10 +931,14 @@ cudaError_t launch_tc(int nq, const void* queries, int nc, const void* rows,
   const int qblocks = (nq + tc::kBM - 1) / tc::kBM;
   const bool pair = flat_tc_pairs(nq);
   constexpr bool RQ = MODE == tc::kModeRaBitQ;
-  CUtensorMap qmap, rmap;
+  constexpr bool SPLIT = (MODE & tc::kModeSplit) != 0;
+  const int box_rows = pair ? tc::Shape<true>::kRowsPerCta : tc::Shape<false>::kRowsPerCta;
+  // The low parts' maps (unused unless SPLIT) repeat the high parts'.
+  CUtensorMap qmap, rmap, qmap2, rmap2;
   if (!make_map(&qmap, queries, nq, d, d, tc::kBM, elem_bytes) ||
-      !make_map(&rmap, rows, n, d, row_stride_elems,
-                pair ? tc::Shape<true>::kRowsPerCta : tc::Shape<false>::kRowsPerCta, elem_bytes))
+      !make_map(&rmap, rows, n, d, row_stride_elems, box_rows, elem_bytes) ||
+      !make_map(&qmap2, queries2 ? queries2 : queries, nq, d, d, tc::kBM, elem_bytes) ||
+      !make_map(&rmap2, rows2 ? rows2 : rows, n, d, row_stride_elems, box_rows, elem_bytes))
     return cudaErrorInvalidValue;
   const int64_t rows_per_part = ((n + num_parts - 1) / num_parts + tc::kBN - 1) / tc::kBN * tc::kBN;
   cudaLaunchConfig_t cfg = {};
@@ -895,18 +955,18 @@ cudaError_t launch_tc(int nq, const void* queries, int nc, const void* rows,
   cudaError_t err;
   if (pair) {
     auto kern = tc::flat_scan_tc_kernel<MODE, true>;
-    cfg.dynamicSmemBytes = tc::Shape<true, RQ>::kSmemBytes;
+    cfg.dynamicSmemBytes = tc::Shape<true, RQ, SPLIT>::kSmemBytes;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)tc::Shape<true, RQ>::kSmemBytes);
-    err = cudaLaunchKernelEx(&cfg, kern, qmap, rmap, nc, nq, n, d, row_aux, keyrank, q_aux,
+                         (int)tc::Shape<true, RQ, SPLIT>::kSmemBytes);
+    err = cudaLaunchKernelEx(&cfg, kern, qmap, rmap, qmap2, rmap2, nc, nq, n, d, row_aux, keyrank, q_aux,
                              q_n2, gthr, bitmap, rows_per_part, kp, list_base, num_lists, cand,
                              part_counts, part_sat, q_flags, status);
   } else {
     auto kern = tc::flat_scan_tc_kernel<MODE, false>;
-    cfg.dynamicSmemBytes = tc::Shape<false, RQ>::kSmemBytes;
+    cfg.dynamicSmemBytes = tc::Shape<false, RQ, SPLIT>::kSmemBytes;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)tc::Shape<false, RQ>::kSmemBytes);
-    err = cudaLaunchKernelEx(&cfg, kern, qmap, rmap, nc, nq, n, d, row_aux, keyrank, q_aux,
+                         (int)tc::Shape<false, RQ, SPLIT>::kSmemBytes);
+    err = cudaLaunchKernelEx(&cfg, kern, qmap, rmap, qmap2, rmap2, nc, nq, n, d, row_aux, keyrank, q_aux,
                              q_n2, gthr, bitmap, rows_per_part, kp, list_base, num_lists, cand,
                              part_counts, part_sat, q_flags, status);
   }
@@ -923,7 +983,7 @@ cudaError_t launch_flat_scan_tc(int metric, const __half* queries, int nq, const
                                 int* part_counts, uint64_t* part_sat, int* q_flags, int* status,
                                 cudaStream_t stream) {
 #define XVEC_TC_ARGS                                                                           \
-  nq, queries, 0, rows, n, d, row_stride_elems, 2, row_aux, keyrank, q_aux, q_n2,     \
+  nq, queries, nullptr, 0, rows, nullptr, n, d, row_stride_elems, 2, row_aux, keyrank, q_aux, q_n2,     \
       gthr, bitmap,                                                                            \
       num_parts, kp, list_base, num_lists, cand, part_counts, part_sat, q_flags, status, stream
   switch (metric) {
@@ -936,6 +996,48 @@ cudaError_t launch_flat_scan_tc(int metric, const __half* queries, int nq, const
 #undef XVEC_TC_ARGS
 }
 
+cudaError_t launch_flat_scan_tc_split(int metric, const __nv_bfloat16* q_hi,
+                                      const __nv_bfloat16* q_lo, int nq, const __nv_bfloat16* r_hi,
+                                      const __nv_bfloat16* r_lo, int64_t n, int d,
+                                      const float* row_aux, const uint32_t* keyrank,
+                                      const float* q_aux, const float* q_n2,
+                                      unsigned long long* gthr, const uint32_t* bitmap,
+                                      int num_parts, int kp, int list_base, int num_lists,
+                                      uint64_t* cand, int* part_counts, uint64_t* part_sat,
+                                      int* q_flags, int* status, cudaStream_t stream) {
+#define XVEC_TC_ARGS                                                                           \
+  nq, q_hi, q_lo, 0, r_hi, r_lo, n, d, (int64_t)d, 2, row_aux, keyrank, q_aux, q_n2, gthr,     \
+      bitmap, num_parts, kp, list_base, num_lists, cand, part_counts, part_sat, q_flags,       \
+      status, stream
+  switch (metric) {
+    case kMetricL2: return launch_tc<tc::kModeSplit + kMetricL2>(XVEC_TC_ARGS);
+    case kMetricIP: return launch_tc<tc::kModeSplit + kMetricIP>(XVEC_TC_ARGS);
+    case kMetricCosine: return launch_tc<tc::kModeSplit + kMetricCosine>(XVEC_TC_ARGS);
+    case kMetricMIPS: return launch_tc<tc::kModeSplit + kMetricMIPS>(XVEC_TC_ARGS);
+    default: return cudaErrorInvalidValue;
+  }
+#undef XVEC_TC_ARGS
+}
+
+// bfloat16 high and low parts of float32 values: hi = bf16(x), lo =
+// bf16(x - hi) (x - hi is exact in float32).
+__global__ void split_bf16_kernel(const float* __restrict__ x, int64_t count,
+                                  __nv_bfloat16* __restrict__ hi, __nv_bfloat16* __restrict__ lo) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= count) return;
+  const float v = x[i];
+  const __nv_bfloat16 h = __float2bfloat16_rn(v);
+  hi[i] = h;
+  lo[i] = __float2bfloat16_rn(v - __bfloat162float(h));
+}
+
+cudaError_t launch_split_bf16(const float* x, int64_t count, __nv_bfloat16* hi, __nv_bfloat16* lo,
+                              cudaStream_t stream) {
+  if (count <= 0) return cudaSuccess;
+  split_bf16_kernel<<<(unsigned)((count + 255) / 256), 256, 0, stream>>>(x, count, hi, lo);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_sq8_scan_tc(int metric, const int8_t* qcodes, int nq, const int8_t* codes,
                                int64_t n, int d, const float4* row_info, const uint32_t* keyrank,
                                const float4* q_info, unsigned long long* gthr,
@@ -944,7 +1046,7 @@ cudaError_t launch_sq8_scan_tc(int metric, const int8_t* qcodes, int nq, const i
                                uint64_t* part_sat, int* q_flags, int* status,
                                cudaStream_t stream) {
 #define XVEC_TC_ARGS                                                                           \
-  nq, qcodes, 0, codes, n, d, (int64_t)d, 1,                                         \
+  nq, qcodes, nullptr, 0, codes, nullptr, n, d, (int64_t)d, 1,                                         \
       reinterpret_cast<const float*>(row_info), keyrank,                                       \
       reinterpret_cast<const float*>(q_info), nullptr, gthr, bitmap, num_parts, kp, list_base, \
       num_lists, cand, part_counts, part_sat, q_flags, status, stream
@@ -965,7 +1067,8 @@ cudaError_t launch_rabitq_scan_tc(const int8_t* q_int, int nq, const int8_t* pla
                                   int* q_flags, int* status, cudaStream_t stream) {
   if (nc > tc::kRaBitQMaxClusters || !rabitq_tc_supported(padded, planes, q_int))
     return cudaErrorInvalidValue;
-  return launch_tc<tc::kModeRaBitQ>(nq, q_int, nc, planes, n, 2 * padded, (int64_t)2 * padded, 1,
+  return launch_tc<tc::kModeRaBitQ>(nq, q_int, nullptr, nc, planes, nullptr, n, 2 * padded,
+                                    (int64_t)2 * padded, 1,
                                     reinterpret_cast<const float*>(row_info), keyrank,
                                     reinterpret_cast<const float*>(q_terms), q_gadd, gthr, bitmap, num_parts, kp, list_base,
                                     num_lists, cand, part_counts, part_sat, q_flags, status,

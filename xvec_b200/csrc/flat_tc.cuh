@@ -1,6 +1,7 @@
 // flat_tc.cuh — tensor-core (tcgen05) candidate scan for FP16 Flat search.
 #pragma once
 
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -45,6 +46,21 @@ cudaError_t launch_sq8_scan_tc(int metric, const int8_t* qcodes, int nq, const i
                                int num_lists, uint64_t* cand, int* part_counts,
                                uint64_t* part_sat, int* q_flags, int* status,
                                cudaStream_t stream);
+// The same scan for float32 rows and queries held as bfloat16 high and low
+// parts (x = hi + lo to 2^-18 |x|): three MMAs per k-step (hi·hi, hi·lo,
+// lo·hi) into one fp32 accumulator; ranks as launch_flat_scan_tc.
+cudaError_t launch_flat_scan_tc_split(int metric, const __nv_bfloat16* q_hi,
+                                      const __nv_bfloat16* q_lo, int nq, const __nv_bfloat16* r_hi,
+                                      const __nv_bfloat16* r_lo, int64_t n, int d,
+                                      const float* row_aux, const uint32_t* keyrank,
+                                      const float* q_aux, const float* q_n2,
+                                      unsigned long long* gthr, const uint32_t* bitmap,
+                                      int num_parts, int kp, int list_base, int num_lists,
+                                      uint64_t* cand, int* part_counts, uint64_t* part_sat,
+                                      int* q_flags, int* status, cudaStream_t stream);
+// hi = bf16(x), lo = bf16(x - hi) for `count` float32 values.
+cudaError_t launch_split_bf16(const float* x, int64_t count, __nv_bfloat16* hi, __nv_bfloat16* lo,
+                              cudaStream_t stream);
 // True when the INT8 tensor-core scan can take this layout.
 bool sq8_tc_supported(int d, const void* codes, const void* qcodes);
 
