@@ -203,6 +203,42 @@ xvec_gpu_status xvec_gpu_merge_results_device(int32_t device, int32_t metric, in
                                               uint64_t* d_out_keys, float* d_out_scores,
                                               int32_t* d_out_counts, void* stream);
 
+/* The two halves of a refined search, for a search whose rows are split
+ * over several indexes (shards).  RefinedSearch (refiner.go:133-166) refines
+ * the RefinementCandidateCount best approximate results of the whole index,
+ * and the HNSW-RaBitQ search its max(TopK, EF) best estimates
+ * (hnsw_rabitq.go:584, 780-801); over shards that candidate list is the
+ * merge of the shards' lists.  Order: candidates on every shard; merge them
+ * with xvec_gpu_merge_results_device under XVEC_METRIC_L2 (ranks: lower is
+ * better, ties by key); refine the merged list on every shard; merge those
+ * results under the index metric.
+ *
+ * candidate_count: candidates per query for these options (SQ8_FLAT:
+ * max(1, floor(top_k * refine_scale)); RABITQ with refine: max(top_k, ef));
+ * 0 when the options ask for no refinement.
+ * candidates_device: the approximate stage alone (no radius): per query up
+ * to candidate_count keys with their ranks (the approximate distance, or the
+ * negated inner product; for RaBitQ the estimate), best first, at stride
+ * candidate_count.  Per-query failures are negative counts (-status); the
+ * call itself returns OK for them.
+ * refine_device: DenseRefiner.Refine (refiner.go:30-33, 66-108) of the given
+ * candidate keys: those this index holds are scored by metric.Compute on
+ * the float32 original rows, and the top_k best within `radius` (ties by key)
+ * are written at stride top_k.  Keys the index does not hold are skipped;
+ * negative candidate counts pass through.  Indexes with float32 rows only. */
+int32_t xvec_gpu_index_candidate_count(const xvec_gpu_index* index,
+                                       const xvec_gpu_search_opts* opts);
+xvec_gpu_status xvec_gpu_index_candidates_device(xvec_gpu_index* index, const void* d_queries,
+                                                 int32_t nq, const xvec_gpu_search_opts* opts,
+                                                 uint64_t* d_keys, float* d_ranks,
+                                                 int32_t* d_counts);
+xvec_gpu_status xvec_gpu_index_refine_device(xvec_gpu_index* index, const float* d_queries,
+                                             int32_t nq, const uint64_t* d_cand_keys,
+                                             int32_t cand_stride, const int32_t* d_cand_counts,
+                                             int32_t top_k, float radius, void* stream,
+                                             uint64_t* d_keys, float* d_scores,
+                                             int32_t* d_counts);
+
 /* Flat search that allocates no device memory during the call (no
  * counterpart in the reference).  For callers that cannot allocate while they
  * search: a process that plans a fixed device-memory budget up front, or a

@@ -51,6 +51,8 @@ EXPORTED_SYMBOLS = (
     "xvec_gpu_kmeans_assign", "xvec_gpu_kmeans_assign_device", "xvec_gpu_merge_results_device",
     "xvec_gpu_stats_enable_timing", "xvec_gpu_get_stats", "xvec_gpu_reset_stats",
     "xvec_gpu_index_search_noalloc", "xvec_gpu_index_reserve",
+    "xvec_gpu_index_candidate_count", "xvec_gpu_index_candidates_device",
+    "xvec_gpu_index_refine_device",
 )
 
 
@@ -109,6 +111,12 @@ def _load() -> ctypes.CDLL:
                                                   vp, vp]
     lib.xvec_gpu_index_search_noalloc.argtypes = [vp, vp, i32, ctypes.POINTER(SearchOpts), vp,
                                                   vp, vp]
+    lib.xvec_gpu_index_candidate_count.restype = i32
+    lib.xvec_gpu_index_candidate_count.argtypes = [vp, ctypes.POINTER(SearchOpts)]
+    lib.xvec_gpu_index_candidates_device.argtypes = [vp, vp, i32, ctypes.POINTER(SearchOpts), vp,
+                                                     vp, vp]
+    lib.xvec_gpu_index_refine_device.argtypes = [vp, vp, i32, vp, i32, vp, i32, ctypes.c_float,
+                                                 vp, vp, vp, vp]
     lib.xvec_gpu_stats_enable_timing.argtypes = [i32]
     lib.xvec_gpu_get_stats.argtypes = [ctypes.POINTER(Stats)]
     for name in EXPORTED_SYMBOLS:
@@ -285,6 +293,33 @@ class _Index:
         o = self._opts(options, stream=stream or None, device_filter_ptr=filter_ptr)
         _check(_lib.xvec_gpu_index_search_device(self._h, queries_ptr, nq, ctypes.byref(o),
                                                  out_keys_ptr, out_scores_ptr, out_counts_ptr))
+
+    def candidate_count(self, options: SearchOptions) -> int:
+        """Candidates per query of a refined search's approximate stage
+        (xvec_gpu_index_candidate_count); 0 without refinement."""
+        o = self._opts(options)
+        return int(_lib.xvec_gpu_index_candidate_count(self._h, ctypes.byref(o)))
+
+    def candidates_device(self, queries_ptr: int, nq: int, options: SearchOptions,
+                          out_keys_ptr: int, out_ranks_ptr: int, out_counts_ptr: int,
+                          stream: int = 0, filter_ptr: Optional[int] = None) -> None:
+        """The approximate stage of a refined search (xvec_gpu_index_candidates_device):
+        keys and ranks at stride candidate_count(options); failed queries have
+        negative counts."""
+        o = self._opts(options, stream=stream or None, device_filter_ptr=filter_ptr)
+        _check(_lib.xvec_gpu_index_candidates_device(self._h, queries_ptr, nq, ctypes.byref(o),
+                                                     out_keys_ptr, out_ranks_ptr,
+                                                     out_counts_ptr))
+
+    def refine_device(self, queries_ptr: int, nq: int, cand_keys_ptr: int, cand_stride: int,
+                      cand_counts_ptr: int, top_k: int, radius: float, out_keys_ptr: int,
+                      out_scores_ptr: int, out_counts_ptr: int, stream: int = 0) -> None:
+        """DenseRefiner.Refine of given candidate keys (xvec_gpu_index_refine_device):
+        exact scores of the keys this index holds, top_k within radius."""
+        _check(_lib.xvec_gpu_index_refine_device(self._h, queries_ptr, nq, cand_keys_ptr,
+                                                 cand_stride, cand_counts_ptr, top_k, radius,
+                                                 stream or None, out_keys_ptr, out_scores_ptr,
+                                                 out_counts_ptr))
 
 
 class _NoAllocMixin:

@@ -23,10 +23,13 @@ xvec_gpu_status ivfpq_commit(xvec_gpu_index* idx, int64_t old_n, int64_t m, cuda
 xvec_gpu_status rabitq_reserve(xvec_gpu_index* idx, int64_t capacity, cudaStream_t s);
 xvec_gpu_status rabitq_commit(xvec_gpu_index* idx, int64_t old_n, int64_t m, cudaStream_t s);
 
+// candidates_only (refined searches): stop after the approximate stage and
+// write its candidates (up to the refine candidate count per query) with
+// their ranks (lower is better) in place of scores.
 xvec_gpu_status sq8_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
                                 const xvec_gpu_search_opts& o, const uint32_t* d_bitmap,
                                 uint64_t* d_keys, float* d_scores, int* d_counts, cudaStream_t s,
-                                std::vector<int>* statuses);
+                                std::vector<int>* statuses, bool candidates_only = false);
 xvec_gpu_status ivfpq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
                                   const xvec_gpu_search_opts& o, const uint32_t* d_bitmap,
                                   uint64_t* d_keys, float* d_scores, int* d_counts,
@@ -34,6 +37,11 @@ xvec_gpu_status ivfpq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
 xvec_gpu_status rabitq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
                                    const xvec_gpu_search_opts& o, const uint32_t* d_bitmap,
                                    uint64_t* d_keys, float* d_scores, int* d_counts,
-                                   cudaStream_t s, std::vector<int>* statuses);
+                                   cudaStream_t s, std::vector<int>* statuses,
+                                   bool candidates_only = false);
+// Candidates per query of the approximate stage of a refined search (0 when
+// the options ask for no refinement).
+int sq8_candidate_count(const xvec_gpu_search_opts& o);
+int rabitq_candidate_count(const xvec_gpu_search_opts& o);
 
 }  // namespace xvec

@@ -651,10 +651,15 @@ xvec_gpu_status rabitq_assign(xvec_gpu_index* idx, const float* prepared, int64_
   return XVEC_GPU_OK;
 }
 
+int rabitq_candidate_count(const xvec_gpu_search_opts& o) {
+  return o.refine ? std::max(o.top_k, o.ef) : 0;
+}
+
 xvec_gpu_status rabitq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
                                    const xvec_gpu_search_opts& o, const uint32_t* d_bitmap,
                                    uint64_t* d_keys, float* d_scores, int* d_counts,
-                                   cudaStream_t s, std::vector<int>* statuses) {
+                                   cudaStream_t s, std::vector<int>* statuses,
+                                   bool candidates_only) {
   EventTimer timer(s);
   timer.mark(0);
   // hnsw_rabitq.go:548-550, 573-579.
@@ -666,6 +671,8 @@ xvec_gpu_status rabitq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq
   const int64_t n = idx->n;
   const int k = o.top_k;
   const bool refine = o.refine != 0;
+  if (candidates_only && !refine)
+    return set_error("candidates of a search without refinement"), XVEC_GPU_INVALID_ARGUMENT;
   const int cc = refine ? (int)std::min<int64_t>(std::max<int64_t>(n, 1), std::max(k, o.ef)) : k;
   const int kp = rabitq_kp(cc);
   if (exact_cap_for(kp) > 8192)
@@ -701,7 +708,9 @@ xvec_gpu_status rabitq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq
   float* o_scores = refine ? sscores.as<float>() : d_scores;
   int* o_counts = refine ? scounts.as<int>() : d_counts;
   XVEC_CUDA(cudaMemsetAsync(o_counts, 0, (size_t)nq * 4, s));
-  const RaBitQScorer sc{kMetricL2,        metric,           idx->rq_codes.as<uint8_t>(),
+  // The candidates-only form reports the estimates themselves (ranks).
+  const RaBitQScorer sc{kMetricL2, candidates_only ? kMetricL2 : metric,
+                        idx->rq_codes.as<uint8_t>(),
                         idx->rq_factors.as<RaBitQFactors>(), qrot.as<float>(),
                         qsum.as<double>(), gadd.as<double>(), gerr.as<double>(),
                         qeps.as<float>(), qexact.as<int>(), padded, nc};
@@ -816,7 +825,18 @@ xvec_gpu_status rabitq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq
   if (!exact_list.empty() && (st = exact_pass(exact_list, d_bitmap, true))) return st;
 
   Scratch rstatus;
-  if (refine) {
+  if (candidates_only) {
+    // The approximate stage's candidates, at stride max(top_k, ef).
+    const int stride = rabitq_candidate_count(o);
+    rabitq_status_kernel<<<blocks_of(nq), 256, 0, s>>>(qstatus.as<int>(), qflags.as<int>(),
+                                                       nullptr, nq, o_counts);
+    XVEC_LAUNCHED();
+    XVEC_CUDA(cudaMemcpy2DAsync(d_keys, (size_t)stride * 8, o_keys, (size_t)cc * 8,
+                                (size_t)cc * 8, nq, cudaMemcpyDeviceToDevice, s));
+    XVEC_CUDA(cudaMemcpy2DAsync(d_scores, (size_t)stride * 4, o_scores, (size_t)cc * 4,
+                                (size_t)cc * 4, nq, cudaMemcpyDeviceToDevice, s));
+    XVEC_CUDA(cudaMemcpyAsync(d_counts, o_counts, (size_t)nq * 4, cudaMemcpyDeviceToDevice, s));
+  } else if (refine) {
     // refinePrepared (hnsw_rabitq.go:780-801) -> topKCandidatesWithOptions:
     // metric.Compute(q, q) on the raw query first (topk.go:92-94).
     Scratch qf, qn2, qaux;
@@ -837,7 +857,7 @@ xvec_gpu_status rabitq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq
       count_launches(2);
     }
   }
-  const int* rs = (refine && n > 0) ? rstatus.as<int>() : nullptr;
+  const int* rs = (refine && !candidates_only && n > 0) ? rstatus.as<int>() : nullptr;
   rabitq_status_kernel<<<blocks_of(nq), 256, 0, s>>>(qstatus.as<int>(), qflags.as<int>(), rs, nq,
                                                      d_counts);
   XVEC_LAUNCHED();

@@ -14,6 +14,16 @@ namespace xvec {
 
 constexpr int kRefineMax = 2048;  // candidates per query (MaxHNSWEFSearch)
 
+// Scores of a stage's output rows turned into ranks (lower is better) in
+// place: -score for inner product, unchanged otherwise.
+static __global__ void scores_to_ranks_kernel(float* scores, const int* counts, int nq,
+                                              int stride, int metric) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)nq * stride) return;
+  const int q = (int)(i / stride), j = (int)(i - (int64_t)q * stride);
+  if (j < counts[q]) scores[i] = rank_from_score(metric, scores[i]);
+}
+
 // One block (256 threads) per query; N >= the candidate count, a power of two.
 // stage_pos/stage_counts: per query the positions of the approximate stage's
 // results (stride `stage_k`).

@@ -334,15 +334,22 @@ xvec_gpu_status sq8_commit(xvec_gpu_index* idx, int64_t old_n, int64_t m, cudaSt
 // ---------------------------------------------------------------------------
 // Search.
 // ---------------------------------------------------------------------------
+int sq8_candidate_count(const xvec_gpu_search_opts& o) {
+  if (!(o.refine_scale > 0) || std::isinf(o.refine_scale)) return 0;
+  return std::max(1, (int)std::floor((double)o.top_k * (double)o.refine_scale));
+}
+
 xvec_gpu_status sq8_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
                                 const xvec_gpu_search_opts& o, const uint32_t* d_bitmap,
                                 uint64_t* d_keys, float* d_scores, int* d_counts, cudaStream_t s,
-                                std::vector<int>* statuses) {
+                                std::vector<int>* statuses, bool candidates_only) {
   EventTimer timer(s);
   timer.mark(0);
   const int d = idx->desc.dimension, metric = idx->desc.metric;
   const int64_t n = idx->n;
   const bool refine = o.refine_scale > 0;
+  if (candidates_only && !refine)
+    return set_error("candidates of a search without refinement"), XVEC_GPU_INVALID_ARGUMENT;
   int stage_k = o.top_k;
   if (refine) {
     if (!(o.refine_scale > 0) || std::isinf(o.refine_scale))
@@ -378,7 +385,7 @@ xvec_gpu_status sq8_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
   float* o_scores = d_scores;
   int* o_counts = d_counts;
   if ((st = spos.alloc((size_t)nq * stage_k * 4, s))) return st;
-  if (refine) {
+  if (refine && !candidates_only) {
     if ((st = skeys.alloc((size_t)nq * stage_k * 8, s)) ||
         (st = sscores.alloc((size_t)nq * stage_k * 4, s)) ||
         (st = scounts.alloc((size_t)nq * 4, s)))
@@ -485,7 +492,9 @@ xvec_gpu_status sq8_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
     for (int q : exact_list)
       if (h_flags[q] & 2) return set_error("exact scan could not complete query %d", q), XVEC_GPU_CUDA_ERROR;
   }
-  if (refine && n > 0) {
+  if (candidates_only) {
+    // The approximate stage's candidates are the output.
+  } else if (refine && n > 0) {
     // The approximate stage's failures are final; the refine stage sees
     // counts >= 0 only for healthy queries.
     sq8_status_kernel<<<blocks_of(nq), 256, 0, s>>>(qstatus.as<int>(), qflags.as<int>(), nq,
@@ -502,6 +511,11 @@ xvec_gpu_status sq8_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
   sq8_status_kernel<<<blocks_of(nq), 256, 0, s>>>(qstatus.as<int>(), qflags.as<int>(), nq,
                                                   d_counts);
   XVEC_LAUNCHED();
+  if (candidates_only && metric == XVEC_METRIC_IP) {
+    scores_to_ranks_kernel<<<blocks_of((int64_t)nq * stage_k), 256, 0, s>>>(
+        d_scores, d_counts, nq, stage_k, metric);
+    XVEC_LAUNCHED();
+  }
   XVEC_CUDA(cudaGetLastError());
   XVEC_CUDA(cudaMemcpyAsync(h_flags.data(), qflags.ptr, (size_t)nq * 4, cudaMemcpyDeviceToHost, s));
   timer.mark(3);

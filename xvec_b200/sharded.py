@@ -7,6 +7,15 @@ keys globally unique), searches it, the per-shard lists are exchanged with
 one NCCL all-gather, and every rank merges them on its GPU with the same
 ordering rule.  torch.distributed is the plumbing; the search and the merge
 are this library's kernels.
+
+Refined searches (SQ8 with a refine scale, RaBitQ with Refine) take two
+exchanges, so that the refined candidates are the reference's: the
+RefinementCandidateCount (or max(TopK, EF)) best approximate results of the
+whole index (refiner.go:133-166, hnsw_rabitq.go:584, 780-801), not of each
+shard.  Every rank computes its shard's candidates with their ranks, the
+lists are exchanged and merged by rank (ties by key), every rank refines the
+merged candidates it holds, and those results are exchanged and merged under
+the index metric.
 """
 from __future__ import annotations
 
@@ -14,7 +23,7 @@ import numpy as np
 import torch
 import torch.distributed as dist
 
-from . import SearchOptions, SearchResults, _Index, merge_results_device
+from . import METRIC_L2, SearchOptions, SearchResults, _Index, merge_results_device
 
 
 def shard_range(n_total: int, rank: int, world: int, align: int = 1):
@@ -45,6 +54,24 @@ def exchange(keys: torch.Tensor, scores: torch.Tensor, counts: torch.Tensor, gro
             all_counts.view(world, nq))
 
 
+def refined_search(candidates_fn, refine_fn, merge_fn, metric: int, k: int, c: int, group=None):
+    """The two-exchange refined search over the ranks of `group`.
+
+    candidates_fn() -> (keys [nq, c] int64, ranks [nq, c] float32, counts [nq] int32):
+        this rank's candidates (failed queries: negative counts);
+    refine_fn(cand_keys [nq, c], cand_counts [nq]) -> (keys [nq, k], scores, counts):
+        the exact top-k among the candidates this rank holds;
+    merge_fn(metric, k, keys [world, nq, kk], scores, counts) -> ([nq, kk], [nq, kk], [nq]):
+        MergeSearchResults of the gathered lists.
+    Returns the merged final (keys, scores, counts), identical on every rank."""
+    keys, ranks, counts = candidates_fn()
+    all_keys, all_ranks, all_counts = exchange(keys, ranks, counts, group)
+    cand_keys, _, cand_counts = merge_fn(METRIC_L2, c, all_keys, all_ranks, all_counts)
+    rkeys, rscores, rcounts = refine_fn(cand_keys, cand_counts)
+    all_keys, all_scores, all_counts = exchange(rkeys, rscores, rcounts, group)
+    return merge_fn(metric, k, all_keys, all_scores, all_counts)
+
+
 class ShardedSearch:
     def __init__(self, index: _Index, group=None):
         self.index = index
@@ -57,6 +84,9 @@ class ShardedSearch:
         Returns merged (keys int64 [nq,k], scores float32 [nq,k], counts int32 [nq])."""
         nq, k = queries.shape[0], options.top_k
         stream = torch.cuda.current_stream(self.device).cuda_stream
+        c = self.index.candidate_count(options) if self.world > 1 else 0
+        if c > 0:
+            return self._refined(queries, options, c, stream)
         keys = torch.empty((nq, k), dtype=torch.int64, device=self.device)
         scores = torch.empty((nq, k), dtype=torch.float32, device=self.device)
         counts = torch.empty((nq,), dtype=torch.int32, device=self.device)
@@ -73,6 +103,42 @@ class ShardedSearch:
                              out_keys.data_ptr(), out_scores.data_ptr(), out_counts.data_ptr(),
                              stream=stream)
         return out_keys, out_scores, out_counts
+
+    def _merge(self, metric, kk, all_keys, all_scores, all_counts):
+        world, nq = all_counts.shape
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        out_keys = torch.empty((nq, kk), dtype=torch.int64, device=self.device)
+        out_scores = torch.empty((nq, kk), dtype=torch.float32, device=self.device)
+        out_counts = torch.empty((nq,), dtype=torch.int32, device=self.device)
+        merge_results_device(self.index.device, metric, kk, nq, world,
+                             all_keys.data_ptr(), all_scores.data_ptr(), all_counts.data_ptr(),
+                             out_keys.data_ptr(), out_scores.data_ptr(), out_counts.data_ptr(),
+                             stream=stream)
+        return out_keys, out_scores, out_counts
+
+    def _refined(self, queries: torch.Tensor, options: SearchOptions, c: int, stream: int):
+        nq, k = queries.shape[0], options.top_k
+        dev = self.device
+
+        def candidates():
+            keys = torch.empty((nq, c), dtype=torch.int64, device=dev)
+            ranks = torch.empty((nq, c), dtype=torch.float32, device=dev)
+            counts = torch.empty((nq,), dtype=torch.int32, device=dev)
+            self.index.candidates_device(queries.data_ptr(), nq, options, keys.data_ptr(),
+                                         ranks.data_ptr(), counts.data_ptr(), stream=stream)
+            return keys, ranks, counts
+
+        def refine(cand_keys, cand_counts):
+            keys = torch.empty((nq, k), dtype=torch.int64, device=dev)
+            scores = torch.empty((nq, k), dtype=torch.float32, device=dev)
+            counts = torch.empty((nq,), dtype=torch.int32, device=dev)
+            self.index.refine_device(queries.data_ptr(), nq, cand_keys.data_ptr(), c,
+                                     cand_counts.data_ptr(), k, options.radius, keys.data_ptr(),
+                                     scores.data_ptr(), counts.data_ptr(), stream=stream)
+            return keys, scores, counts
+
+        return refined_search(candidates, refine, self._merge, self.index.metric, k, c,
+                              self.group)
 
     def search(self, queries_host: torch.Tensor, options: SearchOptions) -> SearchResults:
         """End-to-end form: host (pinned) queries in, host results out on every rank."""
