@@ -46,6 +46,10 @@ def parse():
     p.add_argument("--cpu-sample-rows", type=int, default=1_000_000)
     p.add_argument("--cpu-sample-queries", type=int, default=480)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--batch-sweep", default="",
+                   help="comma-separated batch sizes (e.g. 1,8,64): after the main timing, "
+                        "the median device latency of one search of each size is added to "
+                        "the JSON line as batch_sweep (rabitq_l2_refine, ivfpq_l2, sq8_ip_refine)")
     p.add_argument("--workload",
                    choices=["flat_cosine_fp16", "ivfpq_l2", "sq8_ip_refine", "rabitq_l2_refine",
                             "flat_l2_fp32"],
@@ -391,6 +395,46 @@ def time_search(search, queries, opts, args, dev, world, local):
     return ms, scan_ms, e2e_ms, st, clocks.summary()
 
 
+def batch_sweep(search, queries, opts, sizes, reps=15):
+    """Median device latency (CUDA events) of one search of each batch size,
+    queries resident on the device; which scan served it (tensor cores or
+    not) from the library's counters."""
+    import torch
+
+    import xvec_b200 as xb
+    out = []
+    for b in sizes:
+        q = queries[:b].contiguous()
+        for _ in range(3):
+            search.search_device(q, opts)
+        torch.cuda.synchronize()
+        xb.reset_stats()
+        times = []
+        for _ in range(reps):
+            a, z = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            search.search_device(q, opts)
+            z.record()
+            torch.cuda.synchronize()
+            times.append(a.elapsed_time(z))
+        times.sort()
+        st = xb.stats()
+        # One more pass with the library's device timers (scan vs whole search).
+        xb.enable_timing(True)
+        xb.reset_stats()
+        for _ in range(reps):
+            search.search_device(q, opts)
+        torch.cuda.synchronize()
+        xb.enable_timing(False)
+        tst = xb.stats()
+        med = times[len(times) // 2]
+        out.append({"nq": b, "ms": med, "queries_per_sec": b / (med / 1000.0),
+                    "tensor_scans_per_search": st["tensor_scans"] / reps,
+                    "scan_ms": tst["scan_ms"] / reps, "search_device_ms": tst["search_ms"] / reps,
+                    "exact_queries": st["exact_queries"]})
+    return out
+
+
 def init_ranks(args):
     import torch
     import torch.distributed as dist
@@ -630,6 +674,10 @@ def run_rabitq(args):
     opts = xb.SearchOptions(top_k=RQ_K, ef=RQ_EF, refine=True)
     ms, scan_ms, e2e_ms, st, clocks = time_search(ShardedSearch(index), queries, opts, args, dev,
                                                   world, local)
+    sweep = None
+    if args.batch_sweep and world == 1:
+        sweep = batch_sweep(ShardedSearch(index), queries, opts,
+                            [int(x) for x in args.batch_sweep.split(",")])
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         m = min(args.cpu_sample_rows // 50, n)
@@ -652,8 +700,12 @@ def run_rabitq(args):
                   "dim": RQ_DIM, "metric": "l2", "clusters": RQ_NC, "ef": RQ_EF,
                   "parallelism": f"rows sharded over {world} GPU(s), NCCL all-gather + merge",
                   "l2": "inputs larger than L2 (19.2 GB code planes, 38 GB originals)"}
-        print(json.dumps(common_line(nq, ms, e2e_ms, args, world, "1-bit codes as i8 planes, i32 dots, f32/f64 estimates",
-                                     config, roof, cpu, clocks, st, RQ_K, RQ_DIM, 4)), flush=True)
+        line = common_line(nq, ms, e2e_ms, args, world,
+                           "1-bit codes as i8 planes, i32 dots, f32/f64 estimates", config, roof,
+                           cpu, clocks, st, RQ_K, RQ_DIM, 4)
+        if sweep is not None:
+            line["batch_sweep"] = sweep
+        print(json.dumps(line), flush=True)
     finish_ranks(world)
 
 

@@ -192,6 +192,29 @@ xvec_gpu_status xvec_gpu_kmeans_assign_device(int32_t device, int32_t metric,
                                               const float* d_centroids, int32_t nc, int32_t dim,
                                               int32_t* d_labels, float* d_scores, void* stream);
 
+/* k-means training: trainKMeansWithAssignments (kmeans.go:208-298) with the
+ * IVF builder's options (DefaultKMeansOptions, kmeans.go:83-92): reservoir
+ * initialisation from splitMix64(seed), Lloyd updates (float64 sums in input
+ * order, algorithm/lloyd_cluster.go:53-137), empty clusters reseeded with
+ * the worst-assigned vectors, stop after max_iterations or when
+ * |cost - previous| < tolerance.  vectors [n*dim] (n < 2^31); centroids
+ * [min(clusters, n)*dim]; labels [n] (the final assignment).  Outputs the
+ * cluster count, iterations, whether it converged and the final cost.
+ * Bit-identical to TrainKMeans on the same inputs. */
+xvec_gpu_status xvec_gpu_kmeans_train(int32_t device, int32_t metric, const float* vectors,
+                                      int64_t n, int32_t dim, int32_t clusters,
+                                      int32_t max_iterations, double tolerance, uint64_t seed,
+                                      float* centroids, int32_t* labels, int32_t* out_clusters,
+                                      int32_t* out_iterations, int32_t* out_converged,
+                                      double* out_cost);
+xvec_gpu_status xvec_gpu_kmeans_train_device(int32_t device, int32_t metric,
+                                             const float* d_vectors, int64_t n, int32_t dim,
+                                             int32_t clusters, int32_t max_iterations,
+                                             double tolerance, uint64_t seed, float* d_centroids,
+                                             int32_t* d_labels, int32_t* out_clusters,
+                                             int32_t* out_iterations, int32_t* out_converged,
+                                             double* out_cost, void* stream);
+
 /* Cross-shard merge: MergeSearchResults (query.go:154-191) of `parts` result
  * lists per query, as produced by xvec_gpu_index_search_device on each shard
  * (layout [parts][nq][top_k] keys/scores and [parts][nq] counts, all device

@@ -212,3 +212,31 @@ def test_rabitq_tensor_core_seeded(oracle, xb, metric):
     case.check(xb, queries * scales[:, None], 10, 100, refine=False)
     assert xb.stats()["tensor_scans"] > before
     case.close()
+
+
+@pytest.mark.parametrize("nq", [1, 3, 8])
+def test_rabitq_small_batches(oracle, xb, nq):
+    """Batches of at most 8 queries scan the sign bits through a per-query
+    byte table (no tensor-core scan): 70,000 rows, refined and not, a filter,
+    and 600 copies of one row (more equal ranks than a part's list keeps)."""
+    rng = np.random.default_rng(880 + nq)
+    d = 256
+    centers = rng.standard_normal((40, d)).astype(np.float32)
+    rows = mixture(rng, 70_000, d, centers)
+    rows[20_000:20_600] = rows[5]
+    keys = rng.permutation(1 << 22)[:70_000].astype(np.uint64)
+    cents, signs = model(rng, d, 16, centers)
+    queries = mixture(rng, nq, d, centers)
+    queries[0] = rows[5] + 0.01
+    case = Case(oracle, xb, L2, rows, keys, cents, signs)
+    st0 = xb.stats()
+    case.check(xb, queries, 10, 100, refine=True)
+    st1 = xb.stats()
+    assert st1["tensor_scans"] == st0["tensor_scans"], "small batches skip the tensor cores"
+    case.check(xb, queries, 10, 100, refine=False)
+    bitmap = np.zeros((70_000 + 31) // 32, np.uint32)
+    for p in range(70_000):
+        if p % 3:
+            bitmap[p >> 5] |= np.uint32(1 << (p & 31))
+    case.check(xb, queries, 5, 40, refine=True, bitmap=bitmap)
+    case.close()

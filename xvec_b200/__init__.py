@@ -52,7 +52,7 @@ EXPORTED_SYMBOLS = (
     "xvec_gpu_stats_enable_timing", "xvec_gpu_get_stats", "xvec_gpu_reset_stats",
     "xvec_gpu_index_search_noalloc", "xvec_gpu_index_reserve",
     "xvec_gpu_index_candidate_count", "xvec_gpu_index_candidates_device",
-    "xvec_gpu_index_refine_device",
+    "xvec_gpu_index_refine_device", "xvec_gpu_kmeans_train", "xvec_gpu_kmeans_train_device",
 )
 
 
@@ -111,6 +111,11 @@ def _load() -> ctypes.CDLL:
                                                   vp, vp]
     lib.xvec_gpu_index_search_noalloc.argtypes = [vp, vp, i32, ctypes.POINTER(SearchOpts), vp,
                                                   vp, vp]
+    lib.xvec_gpu_kmeans_train.argtypes = [i32, i32, vp, i64, i32, i32, i32, ctypes.c_double,
+                                          ctypes.c_uint64, vp, vp, vp, vp, vp, vp]
+    lib.xvec_gpu_kmeans_train_device.argtypes = [i32, i32, vp, i64, i32, i32, i32,
+                                                 ctypes.c_double, ctypes.c_uint64, vp, vp, vp,
+                                                 vp, vp, vp, vp]
     lib.xvec_gpu_index_candidate_count.restype = i32
     lib.xvec_gpu_index_candidate_count.argtypes = [vp, ctypes.POINTER(SearchOpts)]
     lib.xvec_gpu_index_candidates_device.argtypes = [vp, vp, i32, ctypes.POINTER(SearchOpts), vp,
@@ -390,6 +395,42 @@ def kmeans_assign_device(device: int, metric: int, vectors_ptr: int, n: int, cen
     _check(_lib.xvec_gpu_kmeans_assign_device(device, metric, vectors_ptr, n, centroids_ptr, nc,
                                               dim, labels_ptr, scores_ptr or None,
                                               stream or None))
+
+
+def kmeans_train(metric: int, vectors, clusters: int, iterations: int = 10,
+                 tolerance: float = 1.1920928955078125e-7, seed: int = 0, device: int = 0):
+    """TrainKMeans with the IVF builder's options (kmeans.go:83-92, 208-298)
+    on the GPU: returns (centroids [min(clusters, n), d], labels [n],
+    iterations run, converged, final cost)."""
+    vectors = np.ascontiguousarray(vectors, np.float32)
+    n, d = vectors.shape
+    kc = min(clusters, n)
+    cents = np.zeros((max(kc, 1), d), np.float32)
+    labels = np.zeros(n, np.int32)
+    out = (ctypes.c_int32 * 3)()
+    cost = ctypes.c_double()
+    _check(_lib.xvec_gpu_kmeans_train(device, metric, _ptr(vectors), n, d, clusters, iterations,
+                                      tolerance, seed, _ptr(cents), _ptr(labels),
+                                      ctypes.byref(out, 0), ctypes.byref(out, 4),
+                                      ctypes.byref(out, 8), ctypes.byref(cost)))
+    return cents[:out[0]], labels, int(out[1]), bool(out[2]), float(cost.value)
+
+
+def kmeans_train_device(device: int, metric: int, vectors_ptr: int, n: int, dim: int,
+                        clusters: int, centroids_ptr: int, labels_ptr: int, iterations: int = 10,
+                        tolerance: float = 1.1920928955078125e-7, seed: int = 0,
+                        stream: int = 0):
+    """xvec_gpu_kmeans_train_device: device vectors in, device centroids
+    [min(clusters, n), dim] and labels [n] out; returns (clusters,
+    iterations, converged, cost)."""
+    out = (ctypes.c_int32 * 3)()
+    cost = ctypes.c_double()
+    _check(_lib.xvec_gpu_kmeans_train_device(device, metric, vectors_ptr, n, dim, clusters,
+                                             iterations, tolerance, seed, centroids_ptr,
+                                             labels_ptr, ctypes.byref(out, 0),
+                                             ctypes.byref(out, 4), ctypes.byref(out, 8),
+                                             ctypes.byref(cost), stream or None))
+    return int(out[0]), int(out[1]), bool(out[2]), float(cost.value)
 
 
 def merge_results_device(device: int, metric: int, top_k: int, nq: int, parts: int, keys_ptr: int,

@@ -541,6 +541,157 @@ __global__ void rabitq_clear_flags(const int* ids, int n, int* q_flags) {
   if (i < n) q_flags[ids[i]] &= ~3;
 }
 
+// Small batches: a scan of the sign bits (n x padded/8 bytes) instead of
+// the tensor-core operand planes (16 x larger).  One block per (row part,
+// query).  The block's query is a byte table in shared memory: entry (b,
+// pos) = the float32 sum of q[8 pos + i] over the set bits i of b, stored at
+// column (pos mod 4) * 32 + pos / 4 of row b (128 columns, zero past
+// padded/8).  Steps of 256 rows are staged in shared memory (coalesced
+// 8-byte loads, double-buffered, rows padded with zeros to 128 bytes); lane
+// l of a warp scores row l, reading its 32 code words in the rotated order
+// w = (g + l) mod 32, so the code reads (bank w) and the four table reads of
+// a word (column j * 32 + w, bank w) of the 32 lanes all hit different
+// banks.  A row's dot is a float32 sum of at most `padded` terms (within the
+// FFMA term of q_eps); ranks use the RaBitQRanker formula; keys below the
+// block's threshold go to one block list, compacted to the KP best by a
+// block sort when full.
+constexpr int kLutThreads = 256;
+constexpr int kLutCap = 1024;       // block list entries
+constexpr int kLutMaxBytes = 128;   // padded / 8 (padded <= 1024)
+
+__global__ void __launch_bounds__(kLutThreads, 1) rabitq_lut_scan_kernel(
+    const uint8_t* __restrict__ codes, int64_t n, int padded, const float4* __restrict__ fast,
+    const uint32_t* __restrict__ keyrank, const uint32_t* __restrict__ bitmap,
+    const float* __restrict__ q_rot, const float* __restrict__ q_fast_sum,
+    const float* __restrict__ q_fast_gadd, int nc, int64_t rows_per_part, int kp,
+    uint64_t* __restrict__ part_keys, int* __restrict__ part_counts,
+    uint64_t* __restrict__ part_sat, int* __restrict__ q_flags) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  float* lut = reinterpret_cast<float*>(smem_raw);                          // [256][128]
+  uint32_t* stage = reinterpret_cast<uint32_t*>(lut + 256 * kLutMaxBytes);  // [2][256][32]
+  uint64_t* list = reinterpret_cast<uint64_t*>(stage + 2 * kLutThreads * 32);  // [kLutCap]
+  float* gadd = reinterpret_cast<float*>(list + kLutCap);                   // [nc]
+  __shared__ int s_count, s_bad;
+  __shared__ unsigned long long s_thr;
+  const int part = blockIdx.x, q = blockIdx.y, parts = gridDim.x;
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int bytes = padded / 8, words8 = bytes / 8;  // 8-byte words per row
+  const float* qr = q_rot + (int64_t)q * padded;
+  // Table: thread pos < 128 fills column col(pos) for every byte value b,
+  // entry b = entry (b with its lowest set bit cleared) + that bit's value.
+  if (tid < kLutMaxBytes) {
+    const int pos = tid, col = (pos & 3) * 32 + (pos >> 2);
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = pos < bytes ? qr[pos * 8 + i] : 0.f;
+    lut[col] = 0.f;
+    for (int b = 1; b < 256; ++b)
+      lut[b * kLutMaxBytes + col] = lut[(b & (b - 1)) * kLutMaxBytes + col] + v[__ffs(b) - 1];
+  }
+  // Zero padding of the staged rows (bytes past padded/8, never overwritten).
+  for (int i = tid; i < 2 * kLutThreads * 32; i += kLutThreads)
+    if ((i & 31) >= bytes / 4) stage[i] = 0u;
+  for (int c = tid; c < nc; c += kLutThreads) gadd[c] = q_fast_gadd[(int64_t)q * nc + c];
+  if (tid == 0) {
+    s_count = 0;
+    s_bad = 0;
+    s_thr = kEmptyKey;
+  }
+  const float half_sum = 0.5f * q_fast_sum[q];
+  const int64_t begin = (int64_t)part * rows_per_part;
+  const int64_t end = min(n, begin + rows_per_part);
+  const int steps = (int)((end - begin + kLutThreads - 1) / kLutThreads);
+  // Step i's rows [begin + 256 i, ...) as 8-byte words: thread t takes words
+  // t, t + 256, ... of the step's contiguous bytes.
+  const int per_step = kLutThreads * words8;
+  constexpr int kMaxLoads = kLutMaxBytes / 8;  // words per thread per step
+  uint2 pre[kMaxLoads];
+  auto load_step = [&](int i) {
+    const int64_t r0 = begin + (int64_t)i * kLutThreads;
+    const int64_t words_avail = (min(end, r0 + kLutThreads) - r0) * words8;
+    const uint2* src = reinterpret_cast<const uint2*>(codes + r0 * bytes);
+#pragma unroll
+    for (int k = 0; k < kMaxLoads; ++k) {
+      const int u = tid + k * kLutThreads;
+      pre[k] = (u < per_step && u < words_avail) ? __ldg(src + u) : make_uint2(0u, 0u);
+    }
+  };
+  auto store_step = [&](int buf) {
+    uint32_t* dst = stage + buf * kLutThreads * 32;
+#pragma unroll
+    for (int k = 0; k < kMaxLoads; ++k) {
+      const int u = tid + k * kLutThreads;
+      if (u < per_step) {
+        const int r = u / words8, w = u - r * words8;
+        *reinterpret_cast<uint2*>(dst + r * 32 + w * 2) = pre[k];
+      }
+    }
+  };
+  if (steps > 0) {
+    load_step(0);
+    store_step(0);
+  }
+  __syncthreads();
+  bool saturated = false;
+  for (int i = 0; i < steps; ++i) {
+    if (i + 1 < steps) load_step(i + 1);
+    const int64_t row = begin + (int64_t)i * kLutThreads + tid;
+    const bool ok = row < end && bitmap_pass(bitmap, row);
+    const uint32_t* mine = stage + (i & 1) * kLutThreads * 32 + tid * 32;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+    for (int g = 0; g < 32; ++g) {
+      const int w = (g + lane) & 31;
+      const uint32_t word = mine[w];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        acc[j] += lut[((word >> (8 * j)) & 0xffu) * kLutMaxBytes + j * 32 + w];
+    }
+    const float dot = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+    if (ok) {
+      const float4 f = fast[row];
+      const float rank = fmaf(f.y, dot - half_sum, f.x + gadd[__float_as_int(f.z)]);
+      if (!finite_f(rank)) {
+        s_bad = 1;
+      } else {
+        const uint64_t key = pack_rank(rank, keyrank[row]);
+        if (key < *(volatile unsigned long long*)&s_thr) {
+          const int slot = atomicAdd(&s_count, 1);
+          list[slot] = key;
+        }
+      }
+    }
+    if (i + 1 < steps) store_step((i + 1) & 1);
+    __syncthreads();
+    // Room for the next step's appends: compact to the KP best.
+    if (s_count > kLutCap - kLutThreads) {
+      const int cnt = s_count;
+      block_sort_u64<kLutCap>(list, cnt);
+      __syncthreads();
+      if (tid == 0) {
+        if (cnt > kp) saturated = true;
+        s_thr = list[kp - 1];
+        s_count = kp;
+      }
+      __syncthreads();
+    }
+  }
+  __syncthreads();
+  const int cnt = s_count;
+  block_sort_u64<kLutCap>(list, cnt);
+  __syncthreads();
+  const int out = min(cnt, kp);
+  const int64_t slot = (int64_t)q * parts + part;
+  for (int i = tid; i < out; i += kLutThreads) part_keys[slot * kp + i] = list[i];
+  if (tid == 0) {
+    part_counts[slot] = out;
+    // Every dropped key is at or above the KP-th kept one.
+    part_sat[slot] = (saturated || cnt > kp || s_thr != kEmptyKey) && cnt >= kp ? list[kp - 1]
+                                                                               : kEmptyKey;
+    if (s_bad) atomicOr(&q_flags[q], 1);
+  }
+}
+
 int floor_pow2(int v) {
   int r = 1;
   while (r <= v / 2) r *= 2;
@@ -715,12 +866,44 @@ xvec_gpu_status rabitq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq
                         qsum.as<double>(), gadd.as<double>(), gerr.as<double>(),
                         qeps.as<float>(), qexact.as<int>(), padded, nc};
   const float stage_radius = refine ? 0.f : o.radius;
+  // Small batches: the sign bits through a byte table (the tensor-core scan
+  // streams 16x more bytes and fills few SMs at this size).
+  const bool small = n > 0 && nq <= 8 && padded <= 8 * kLutMaxBytes && kp <= 256;
   // INT8 tensor cores on the code planes when the layout allows, else FFMA.
-  const bool use_tc = n > 0 && nc <= rabitq_tc_max_clusters() && kp + 128 <= flat_tc_cap() &&
+  const bool use_tc = !small && n > 0 && nc <= rabitq_tc_max_clusters() &&
+                      kp + 128 <= flat_tc_cap() &&
                       n < (1ll << 31) - 256 &&
                       rabitq_tc_supported(padded, idx->rq_planes.ptr, qint.ptr);
-  const bool fast = use_tc || (n > 0 && simt_cap_for(kp) <= 512);
-  if (use_tc) {
+  const bool fast = small || use_tc || (n > 0 && simt_cap_for(kp) <= 512);
+  if (small) {
+    int parts = (int)std::max<int64_t>(
+        1, std::min<int64_t>(flat_merge_capacity() / kp, (n + 4095) / 4096));
+    const int64_t rows_per_part = ((n + parts - 1) / parts + kLutThreads - 1) / kLutThreads *
+                                  kLutThreads;
+    parts = (int)((n + rows_per_part - 1) / rows_per_part);
+    Scratch pkeys, pcounts, psat;
+    if ((st = pkeys.alloc((size_t)nq * parts * kp * 8, s)) ||
+        (st = pcounts.alloc((size_t)nq * parts * 4, s)) ||
+        (st = psat.alloc((size_t)nq * parts * 8, s)))
+      return st;
+    const int smem = kLutMaxBytes * 256 * 4 + 2 * kLutThreads * 128 + kLutCap * 8 + nc * 4;
+    cudaFuncSetAttribute(rabitq_lut_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         smem);
+    timer.mark(1);
+    rabitq_lut_scan_kernel<<<dim3(parts, nq), kLutThreads, smem, s>>>(
+        idx->rq_codes.as<uint8_t>(), n, padded, idx->rq_fast.as<float4>(),
+        idx->keyrank.as<uint32_t>(), d_bitmap, qrot.as<float>(), qfs.as<float>(),
+        qfg.as<float>(), nc, rows_per_part, kp, pkeys.as<uint64_t>(), pcounts.as<int>(),
+        psat.as<uint64_t>(), qflags.as<int>());
+    XVEC_LAUNCHED();
+    XVEC_CUDA(cudaGetLastError());
+    timer.mark(2);
+    XVEC_CUDA(launch_merge_rescore(sc, idx->pos_of_kr.as<uint32_t>(), idx->keys.as<uint64_t>(),
+                                   nullptr, nq, cc, stage_radius, 0, pkeys.as<uint64_t>(),
+                                   pcounts.as<int>(), psat.as<uint64_t>(), parts, kp, o_keys,
+                                   o_scores, o_counts, spos.as<uint32_t>(), qflags.as<int>(), s));
+    XVEC_LAUNCHED();
+  } else if (use_tc) {
     Scratch pkeys, pcounts, psat, kstatus;
     int lists = 0;
     if ((st = kstatus.alloc(4, s))) return st;
