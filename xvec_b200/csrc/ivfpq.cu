@@ -49,7 +49,7 @@ xvec_gpu_status add_device_locked(xvec_gpu_index* idx, const uint64_t* d_keys, c
 namespace {
 
 inline unsigned blocks_of(int64_t n, int t = 256) { return (unsigned)((n + t - 1) / t); }
-constexpr int kAssignBatch = 65536;
+constexpr int kAssignBatch = 131072;  // rows per nearest-centroid search
 
 __global__ void keys_to_labels_kernel(const uint64_t* keys, const int* counts, int64_t n,
                                       int32_t* labels, int* err) {
