@@ -68,7 +68,11 @@ typedef enum {
   XVEC_INDEX_IVF_PQ = 3,
   /* One-bit RaBitQ linear scan + exact refine (internal/core/hnsw_rabitq.go:539-642,
    * 780-801; internal/core/rabitq.go:372-430). */
-  XVEC_INDEX_RABITQ = 4
+  XVEC_INDEX_RABITQ = 4,
+  /* IVF with exact scoring of the probed lists' original rows: core.IVFIndex
+   * (internal/core/ivf.go:214-230, searchIVF :427-493, probedListsLocked
+   * :524-561; cosine with cached magnitudes, :469-478). */
+  XVEC_INDEX_IVF_FLAT = 5
 } xvec_gpu_index_kind;
 
 typedef enum {
@@ -180,6 +184,13 @@ xvec_gpu_status xvec_gpu_index_search_device(xvec_gpu_index* index, const void* 
                                              int32_t nq, const xvec_gpu_search_opts* opts,
                                              uint64_t* d_out_keys, float* d_out_scores,
                                              int32_t* d_out_counts);
+
+/* IVF model: the nlist centroids [nlist*dim] of an IVF_FLAT index (the
+ * trained KMeansModel of IVFBuilder.Build, ivf.go:144-212); set before any
+ * row is added.  Rows go to their nearest centroid (KMeansModel.Nearest,
+ * kmeans.go:169-175). */
+xvec_gpu_status xvec_gpu_ivf_set_model(xvec_gpu_index* index, const float* centroids,
+                                       int32_t nlist);
 
 /* k-means assignment: assignKMeans / assignKMeansCosine (kmeans.go:382-479):
  * for each vector the metric-best centroid (lower index wins ties) and its

@@ -32,7 +32,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libxvec_gpu.so")
 
 METRIC_L2, METRIC_IP, METRIC_COSINE, METRIC_MIPSL2 = 1, 2, 3, 4
-INDEX_FLAT, INDEX_SQ8_FLAT, INDEX_IVF_PQ, INDEX_RABITQ = 1, 2, 3, 4
+INDEX_FLAT, INDEX_SQ8_FLAT, INDEX_IVF_PQ, INDEX_RABITQ, INDEX_IVF_FLAT = 1, 2, 3, 4, 5
 STORAGE_FP32, STORAGE_FP16 = 1, 2
 
 STATUS_NAMES = {
@@ -53,6 +53,7 @@ EXPORTED_SYMBOLS = (
     "xvec_gpu_index_search_noalloc", "xvec_gpu_index_reserve",
     "xvec_gpu_index_candidate_count", "xvec_gpu_index_candidates_device",
     "xvec_gpu_index_refine_device", "xvec_gpu_kmeans_train", "xvec_gpu_kmeans_train_device",
+    "xvec_gpu_ivf_set_model",
 )
 
 
@@ -101,6 +102,7 @@ def _load() -> ctypes.CDLL:
     lib.xvec_gpu_index_add_device.argtypes = [vp, vp, vp, i64, vp]
     lib.xvec_gpu_ivfpq_set_model.argtypes = [vp, vp, i32, vp, i32]
     lib.xvec_gpu_rabitq_set_model.argtypes = [vp, vp, i32, vp]
+    lib.xvec_gpu_ivf_set_model.argtypes = [vp, vp, i32]
     lib.xvec_gpu_index_search.argtypes = [vp, vp, i32, ctypes.POINTER(SearchOpts), vp, vp, vp]
     lib.xvec_gpu_index_search_device.argtypes = [vp, vp, i32, ctypes.POINTER(SearchOpts), vp,
                                                  vp, vp]
@@ -361,6 +363,16 @@ class IVFPQIndex(_Index):
         pivots = np.ascontiguousarray(pivots, np.float32)
         _check(_lib.xvec_gpu_ivfpq_set_model(self._h, _ptr(centroids), centroids.shape[0],
                                              _ptr(pivots), chunks))
+
+
+class IVFIndex(_Index):
+    """core.IVFIndex (internal/core/ivf.go:214-597): probe the nprobe best
+    centroids, exact-score the original rows of those lists."""
+    kind = INDEX_IVF_FLAT
+
+    def set_model(self, centroids) -> None:
+        centroids = np.ascontiguousarray(centroids, np.float32)
+        _check(_lib.xvec_gpu_ivf_set_model(self._h, _ptr(centroids), centroids.shape[0]))
 
 
 class RaBitQIndex(_Index):

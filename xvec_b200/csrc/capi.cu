@@ -463,6 +463,9 @@ xvec_gpu_status search_device_locked(xvec_gpu_index* idx, const void* d_q, int n
     case XVEC_INDEX_RABITQ:
       return rabitq_search_impl(idx, static_cast<const float*>(d_q), nq, o, d_bitmap, d_keys,
                                 d_scores, d_counts, s, statuses);
+    case XVEC_INDEX_IVF_FLAT:
+      return ivf_flat_search_impl(idx, static_cast<const float*>(d_q), nq, o, d_bitmap, d_keys,
+                                  d_scores, d_counts, s, statuses);
     default: return set_error("invalid index kind"), XVEC_GPU_INVALID_ARGUMENT;
   }
 }
@@ -615,6 +618,8 @@ extern "C" xvec_gpu_status xvec_gpu_index_create(const xvec_gpu_index_desc* desc
       if (desc->dimension < 64 || desc->dimension > 4095)
         return set_error("core: invalid RaBitQ options: dimension must be in [64,4095]"),
                XVEC_GPU_INVALID_ARGUMENT;
+      break;
+    case XVEC_INDEX_IVF_FLAT:
       break;
     default: return set_error("invalid index kind %d", desc->kind), XVEC_GPU_INVALID_ARGUMENT;
   }

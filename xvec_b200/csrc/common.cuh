@@ -312,6 +312,24 @@ __device__ __forceinline__ float warp_reference_score(int metric, const RowT* x,
   return metric == kMetricCosine ? reference_cosine(s0, s1, s2) : reference_mips(s0, s1, s2);
 }
 
+// Fast rank of a (row, query) pair from its dot product and the exact
+// squared norms (see fast_eps for the bound on |fast - reference|).
+__device__ __forceinline__ float fast_rank(int metric, float dot, float xn2, float qn2) {
+  switch (metric) {
+    case kMetricL2: return (xn2 + qn2) - 2.f * dot;
+    case kMetricIP: return -dot;
+    case kMetricCosine:
+      if (xn2 == 0.f && qn2 == 0.f) return 0.f;
+      if (xn2 == 0.f || qn2 == 0.f) return 1.f;
+      return 1.f - dot * rsqrtf(xn2) * rsqrtf(qn2);
+    default: {
+      const float den = fmaxf(xn2, qn2);
+      if (den == 0.f) return 0.f;
+      return 2.f - 2.f * dot / den;
+    }
+  }
+}
+
 // Rank (lower = better) from a metric score: IP ranks by -score.
 __device__ __forceinline__ float rank_from_score(int metric, float s) {
   return metric == kMetricIP ? -s : s;

@@ -112,24 +112,6 @@ __global__ void row_norms_kernel(const RowT* __restrict__ rows, int64_t n, int d
   }
 }
 
-// Fast rank of a (row, query) pair from its dot product and the exact
-// squared norms (see fast_eps for the bound on |fast - reference|).
-__device__ __forceinline__ float fast_rank(int metric, float dot, float xn2, float qn2) {
-  switch (metric) {
-    case kMetricL2: return (xn2 + qn2) - 2.f * dot;
-    case kMetricIP: return -dot;
-    case kMetricCosine:
-      if (xn2 == 0.f && qn2 == 0.f) return 0.f;
-      if (xn2 == 0.f || qn2 == 0.f) return 1.f;
-      return 1.f - dot * rsqrtf(xn2) * rsqrtf(qn2);
-    default: {
-      const float den = fmaxf(xn2, qn2);
-      if (den == 0.f) return 0.f;
-      return 2.f - 2.f * dot / den;
-    }
-  }
-}
-
 // Bound on |fast rank - reference rank| for a query (both accumulate d
 // exact-or-rounded products in float32; factor 4 covers both sides and a
 // non round-to-nearest accumulator).

@@ -20,6 +20,22 @@ xvec_gpu_status sq8_commit(xvec_gpu_index* idx, int64_t old_n, int64_t m, cudaSt
 xvec_gpu_status ivfpq_reserve(xvec_gpu_index* idx, int64_t capacity, cudaStream_t s);
 xvec_gpu_status ivfpq_commit(xvec_gpu_index* idx, int64_t old_n, int64_t m, cudaStream_t s);
 
+// IVF helpers shared by the IVF kinds (ivfpq.cu): the nearest centroid of
+// each row through a Flat index over the centroids (keys = centroid index),
+// that index, and the CSR lists of positions (+ key ranks in list order).
+xvec_gpu_status assign_rows(xvec_gpu_index* probe, const float* d_rows, int64_t n, int d,
+                            int32_t* d_labels, float* d_scores, cudaStream_t s);
+xvec_gpu_status make_probe_index(int device, int metric, int d, const float* d_centroids,
+                                 int nlist, cudaStream_t s, xvec_gpu_index** out);
+xvec_gpu_status rebuild_lists(xvec_gpu_index* idx, cudaStream_t s);
+
+xvec_gpu_status ivf_flat_reserve(xvec_gpu_index* idx, int64_t capacity, cudaStream_t s);
+xvec_gpu_status ivf_flat_commit(xvec_gpu_index* idx, int64_t old_n, int64_t m, cudaStream_t s);
+xvec_gpu_status ivf_flat_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
+                                     const xvec_gpu_search_opts& o, const uint32_t* d_bitmap,
+                                     uint64_t* d_keys, float* d_scores, int* d_counts,
+                                     cudaStream_t s, std::vector<int>* statuses);
+
 xvec_gpu_status rabitq_reserve(xvec_gpu_index* idx, int64_t capacity, cudaStream_t s);
 xvec_gpu_status rabitq_commit(xvec_gpu_index* idx, int64_t old_n, int64_t m, cudaStream_t s);
 

@@ -22,6 +22,7 @@ xvec_gpu_status extra_reserve(xvec_gpu_index* idx, int64_t cap, cudaStream_t s) 
   if (idx->desc.kind == XVEC_INDEX_SQ8_FLAT) return sq8_reserve(idx, cap, s);
   if (idx->desc.kind == XVEC_INDEX_IVF_PQ) return ivfpq_reserve(idx, cap, s);
   if (idx->desc.kind == XVEC_INDEX_RABITQ) return rabitq_reserve(idx, cap, s);
+  if (idx->desc.kind == XVEC_INDEX_IVF_FLAT) return ivf_flat_reserve(idx, cap, s);
   return XVEC_GPU_OK;
 }
 xvec_gpu_status extra_validate(xvec_gpu_index* idx, int64_t, int64_t, cudaStream_t) {
@@ -29,6 +30,8 @@ xvec_gpu_status extra_validate(xvec_gpu_index* idx, int64_t, int64_t, cudaStream
     return set_error("set the IVF-PQ model before adding rows"), XVEC_GPU_INVALID_ARGUMENT;
   if (idx->desc.kind == XVEC_INDEX_RABITQ && !idx->has_model)
     return set_error("set the RaBitQ model before adding rows"), XVEC_GPU_INVALID_ARGUMENT;
+  if (idx->desc.kind == XVEC_INDEX_IVF_FLAT && !idx->has_model)
+    return set_error("set the IVF model before adding rows"), XVEC_GPU_INVALID_ARGUMENT;
   return XVEC_GPU_OK;
 }
 xvec_gpu_status extra_commit(xvec_gpu_index* idx, int64_t old_n, int64_t m, cudaStream_t s) {
@@ -43,6 +46,7 @@ xvec_gpu_status extra_commit(xvec_gpu_index* idx, int64_t old_n, int64_t m, cuda
   if (idx->desc.kind == XVEC_INDEX_SQ8_FLAT) return sq8_commit(idx, old_n, m, s);
   if (idx->desc.kind == XVEC_INDEX_IVF_PQ) return ivfpq_commit(idx, old_n, m, s);
   if (idx->desc.kind == XVEC_INDEX_RABITQ) return rabitq_commit(idx, old_n, m, s);
+  if (idx->desc.kind == XVEC_INDEX_IVF_FLAT) return ivf_flat_commit(idx, old_n, m, s);
   return XVEC_GPU_OK;
 }
 

@@ -513,6 +513,8 @@ __global__ void iota32_kernel(uint32_t* out, int64_t n) {
   if (i < n) out[i] = (uint32_t)i;
 }
 
+}  // namespace
+
 // Nearest centroid of each row through a Flat index over the centroids
 // (keys = centroid index): top-1 under the metric, ties to the lower index.
 xvec_gpu_status assign_rows(xvec_gpu_index* probe, const float* d_rows, int64_t n, int d,
@@ -576,7 +578,6 @@ xvec_gpu_status make_probe_index(int device, int metric, int d, const float* d_c
   return XVEC_GPU_OK;
 }
 
-}  // namespace
 
 // ---------------------------------------------------------------------------
 // Index hooks.
@@ -656,7 +657,7 @@ __global__ void rotate_list_codes_kernel(const int64_t* __restrict__ list_offset
 // Chunk slots of the fast scan (0: the layout does not apply).
 int fast_slots(int chunks) { return chunks <= 32 ? 32 : chunks <= 64 ? 64 : 0; }
 
-static xvec_gpu_status rebuild_lists(xvec_gpu_index* idx, cudaStream_t s) {
+xvec_gpu_status rebuild_lists(xvec_gpu_index* idx, cudaStream_t s) {
   const int64_t n = idx->n;
   const int nlist = idx->nlist;
   xvec_gpu_status st;
@@ -683,8 +684,10 @@ static xvec_gpu_status rebuild_lists(xvec_gpu_index* idx, cudaStream_t s) {
                                             idx->list_rows.as<uint32_t>(), n, 0, 32, s));
   XVEC_CUDA(cub::DeviceScan::ExclusiveSum(temp.ptr, tb2, counts.as<int64_t>(),
                                           idx->list_offsets.as<int64_t>(), nlist + 1, s));
-  const int chunks = idx->chunks;
-  if ((st = idx->list_codes.reserve((size_t)std::max<int64_t>(n, 1) * chunks, 0, s)) ||
+  // IVF-PQ: list-major codes (and their rotated copy); every IVF kind: the
+  // key ranks in list order.
+  const int chunks = idx->desc.kind == XVEC_INDEX_IVF_PQ ? idx->chunks : 0;
+  if ((st = idx->list_codes.reserve((size_t)std::max<int64_t>(n, 1) * std::max(chunks, 1), 0, s)) ||
       (st = idx->list_keyrank.reserve((size_t)std::max<int64_t>(n, 1) * 4, 0, s)))
     return st;
   gather_list_major_kernel<<<blocks_of(n), 256, 0, s>>>(
@@ -694,7 +697,7 @@ static xvec_gpu_status rebuild_lists(xvec_gpu_index* idx, cudaStream_t s) {
   XVEC_LAUNCHED();
   XVEC_CUDA(cudaGetLastError());
   const int slots = fast_slots(chunks);
-  if (slots > 0) {
+  if (chunks > 0 && slots > 0) {
     const size_t bytes = (size_t)std::max<int64_t>(n, 1) * slots;
     if ((st = idx->list_codes_t.reserve(bytes, 0, s))) return st;
     rotate_list_codes_kernel<<<nlist, 256, 0, s>>>(idx->list_offsets.as<int64_t>(), chunks, slots,

@@ -163,7 +163,7 @@ __global__ void __launch_bounds__(256) scan_exact_kernel(
   uint64_t* buf = reinterpret_cast<uint64_t*>(smem_raw);
   __shared__ AccumState st;
   constexpr int kRowsPerRound = 8 * 16;
-  const int qi = query_ids[blockIdx.x];
+  const int qi = query_ids ? query_ids[blockIdx.x] : blockIdx.x;
   const int slot_q = blockIdx.x;  // part buffers are indexed by list slot
   const int part = blockIdx.y, num_parts = gridDim.y;
   const int64_t row_begin = (int64_t)part * rows_per_part;
