@@ -52,14 +52,15 @@ def parse():
                         "the JSON line as batch_sweep (rabitq_l2_refine, ivfpq_l2, sq8_ip_refine)")
     p.add_argument("--workload",
                    choices=["flat_cosine_fp16", "ivfpq_l2", "sq8_ip_refine", "rabitq_l2_refine",
-                            "flat_l2_fp32"],
+                            "flat_l2_fp32", "ivf_flat_l2"],
                    default="flat_cosine_fp16",
                    help="flat_cosine_fp16: the Flat configuration above (default); ivfpq_l2: "
                         "IVF-PQ L2, 1e8 x 128, nlist 16384, 32 x 256 PQ, nprobe 64, k=10; "
                         "sq8_ip_refine: INT8 SQ Flat IP, 2e7 x 1024, k=10, ScaleFactor 4; "
                         "rabitq_l2_refine: one-bit RaBitQ L2, 1e7 x 960, k=10, EF 100; "
                         "flat_l2_fp32: Flat L2 over FP32 storage, 1e6 x 128 N(0,1), 1,000 "
-                        "queries, k=10")
+                        "queries, k=10; ivf_flat_l2: IVF with exact scoring, 1e7 x 128, "
+                        "nlist 4096, nprobe 32, k=10")
     return p.parse_args()
 
 
@@ -494,6 +495,108 @@ def common_line(nq, ms, e2e_ms, args, world, dtype, config, roofline, cpu, clock
 
 
 # ---------------------------------------------------------------------------
+# IVF with exact scoring of the probed lists (IVFIndex.SearchIVF): 10,000,000
+# x 128 float32 from the 10,000-cluster mixture, nlist 4,096 centroids trained
+# with the GPU k-means on the first 1,000,000 rows, nprobe 32, 10,000
+# queries, top-k 10.
+# ---------------------------------------------------------------------------
+IVF_N, IVF_NLIST, IVF_NPROBE, IVF_K, IVF_TRAIN = 10_000_000, 4096, 32, 10, 1_000_000
+IVF_WORKLOAD = ("IVF exact L2 search, 10,000,000 x 128 float32 (10,000-cluster mixture), nlist "
+                "4,096 (GPU k-means on the first 1,000,000 rows), nprobe 32, 10,000 queries, "
+                "top-k=10")
+
+
+def run_ivf_flat(args):
+    import numpy as np
+    import torch
+
+    import xvec_b200 as xb
+    from xvec_b200.sharded import ShardedSearch, shard_range
+    world, rank, local, dev = init_ranks(args)
+    n = args.n if args.n != N_BASE else IVF_N
+    nq = args.nq
+    g = torch.Generator(device=dev).manual_seed(4321)
+    centers = torch.randn(PQ_CLUSTERS, PQ_DIM, generator=g, device=dev)
+    train_n = min(n, IVF_TRAIN)
+    train = pq_mixture(torch, centers, 0, train_n, dev).contiguous()
+    cents = torch.empty(IVF_NLIST, PQ_DIM, device=dev)
+    labels = torch.empty(train_n, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream().cuda_stream
+    kc, iters, _, _ = xb.kmeans_train_device(local, xb.METRIC_L2, train.data_ptr(), train_n,
+                                             PQ_DIM, IVF_NLIST, cents.data_ptr(),
+                                             labels.data_ptr(), iterations=10, seed=4096,
+                                             stream=stream)
+    cents = cents[:kc].contiguous()
+    del train, labels
+    index = xb.IVFIndex(PQ_DIM, xb.METRIC_L2, device=local)
+    index.set_model(cents.cpu().numpy())
+    b, e = shard_range(n, rank, world, align=PQ_CHUNK_ROWS)
+    index.reserve(e - b)
+    sizes = torch.zeros(kc, dtype=torch.int64, device=dev)
+    lab = torch.empty(PQ_CHUNK_ROWS, dtype=torch.int32, device=dev)
+    host_rows = [] if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
+    host_labels = []
+    for c0 in range(b, e, PQ_CHUNK_ROWS):
+        m = min(PQ_CHUNK_ROWS, e - c0)
+        rows = pq_mixture(torch, centers, c0 // PQ_CHUNK_ROWS, m, dev).contiguous()
+        keys = torch.arange(c0, c0 + m, dtype=torch.int64, device=dev)
+        index.add_device(keys.data_ptr(), rows.data_ptr(), m, stream)
+        xb.kmeans_assign_device(local, xb.METRIC_L2, rows.data_ptr(), m, cents.data_ptr(), kc,
+                                PQ_DIM, lab.data_ptr(), 0, stream)
+        sizes += torch.bincount(lab[:m].long(), minlength=kc)
+        if host_rows is not None:
+            host_rows.append(rows.cpu().numpy())
+            host_labels.append(lab[:m].cpu().numpy())
+        del rows, keys
+    queries = pq_mixture(torch, centers, 10**6 + 3, nq, dev).contiguous()
+    torch.cuda.synchronize()
+    probe = xb.DenseFlatIndex(PQ_DIM, xb.METRIC_L2, device=local)
+    probe.add(np.arange(kc, dtype=np.uint64), cents.cpu().numpy())
+    pr = probe.search(queries.cpu().numpy(), IVF_NPROBE)
+    h_sizes = sizes.cpu().numpy()
+    scanned = int(h_sizes[pr.keys.astype(np.int64)].sum())
+    probe.close()
+    opts = xb.SearchOptions(top_k=IVF_K, nprobe=IVF_NPROBE)
+    ms, scan_ms, e2e_ms, st, clocks = time_search(ShardedSearch(index), queries, opts, args, dev,
+                                                  world, local)
+    cpu = None
+    if host_rows is not None:
+        from oracle.oracle import L2 as OL2, Oracle
+        allrows = np.concatenate(host_rows)
+        labels_h = np.concatenate(host_labels)  # the GPU's nearest-centroid labels
+        offsets = np.zeros(kc + 1, np.int64)
+        np.add.at(offsets, labels_h + 1, 1)
+        offsets = np.cumsum(offsets)
+        positions = np.argsort(labels_h, kind="stable").astype(np.int64)
+        qs = queries[:max(8, args.cpu_sample_queries // 4)].cpu().numpy()
+        threads = os.cpu_count() or 1
+        t0 = time.perf_counter()
+        Oracle().ivf_flat_search(OL2, allrows, np.arange(n, dtype=np.uint64), cents.cpu().numpy(),
+                                 offsets, positions, qs, IVF_K, IVF_NPROBE, threads=threads)
+        dt = time.perf_counter() - t0
+        cpu = {"value": qs.shape[0] / dt, "unit": "queries/sec", "cores": threads, "kind": "port",
+               "sample": f"{qs.shape[0]} queries over the full index, {dt:.1f} s on {threads} "
+                         "threads (lists from the GPU assignment, not timed)"}
+    if rank == 0:
+        _, hbm_peak, peak_kind = peaks()
+        nbytes = scanned * PQ_DIM * 4
+        achieved = nbytes / (scan_ms / 1000.0) / 1e9 if scan_ms > 0 else None
+        roof = {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                "frac": (achieved / hbm_peak) if achieved else None, "traffic": None,
+                "peak_source": f"{peak_kind} HBM copy bandwidth",
+                "kernel": "IVF exact list scan", "kernel_ms": scan_ms,
+                "algorithmic_bytes_per_launch": nbytes, "scanned_rows_per_launch": scanned}
+        config = {"workload": IVF_WORKLOAD, "global_batch": nq, "top_k": IVF_K, "base_vectors": n,
+                  "dim": PQ_DIM, "metric": "l2", "nlist": kc, "nprobe": IVF_NPROBE,
+                  "kmeans_iterations": iters,
+                  "parallelism": f"rows sharded over {world} GPU(s), NCCL all-gather + merge",
+                  "l2": "inputs larger than L2 (5.1 GB rows)"}
+        print(json.dumps(common_line(nq, ms, e2e_ms, args, world, "f32", config, roof, cpu, clocks,
+                                     st, IVF_K, PQ_DIM, 4)), flush=True)
+    finish_ranks(world)
+
+
+# ---------------------------------------------------------------------------
 # Flat L2 over FP32 storage: 1,000,000 x 128 i.i.d. N(0,1), 1,000 queries from
 # the same distribution, top-k 10 (the configuration the reference runs on
 # its CPU path).
@@ -786,6 +889,8 @@ def main():
         return run_sq8(args)
     if args.workload == "flat_l2_fp32":
         return run_flat_fp32(args)
+    if args.workload == "ivf_flat_l2":
+        return run_ivf_flat(args)
     if args.workload == "rabitq_l2_refine":
         return run_rabitq(args)
 
