@@ -72,7 +72,12 @@ typedef enum {
   /* IVF with exact scoring of the probed lists' original rows: core.IVFIndex
    * (internal/core/ivf.go:214-230, searchIVF :427-493, probedListsLocked
    * :524-561; cosine with cached magnitudes, :469-478). */
-  XVEC_INDEX_IVF_FLAT = 5
+  XVEC_INDEX_IVF_FLAT = 5,
+  /* IVF with INT8 scalar-quantized scoring of the probed lists' rows:
+   * core.ScalarQuantizedIVFIndex (internal/core/ivf_quantized.go:23-192): the
+   * IVF probe with the original metric, the SQ8_FLAT scoring of the probed
+   * positions (quantized_index.go:313-335) and the optional refine stage. */
+  XVEC_INDEX_IVF_SQ8 = 6
 } xvec_gpu_index_kind;
 
 typedef enum {
@@ -185,7 +190,7 @@ xvec_gpu_status xvec_gpu_index_search_device(xvec_gpu_index* index, const void* 
                                              uint64_t* d_out_keys, float* d_out_scores,
                                              int32_t* d_out_counts);
 
-/* IVF model: the nlist centroids [nlist*dim] of an IVF_FLAT index (the
+/* IVF model: the nlist centroids [nlist*dim] of an IVF_FLAT or IVF_SQ8 index (the
  * trained KMeansModel of IVFBuilder.Build, ivf.go:144-212); set before any
  * row is added.  Rows go to their nearest centroid (KMeansModel.Nearest,
  * kmeans.go:169-175). */

@@ -124,6 +124,11 @@ class Oracle:
                                            _f32p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                            ctypes.c_float, _u32p, ctypes.c_int32, _u64p, _f32p,
                                            _i32p, _i32p]
+        lib.xo_ivf_sq8_search.argtypes = [ctypes.c_int, _i8p, ctypes.c_void_p, _f32p, _u64p,
+                                          ctypes.c_int64, ctypes.c_int32, _f32p, ctypes.c_int32,
+                                          _i64p, _i64p, _f32p, ctypes.c_int32, ctypes.c_int32,
+                                          ctypes.c_int32, ctypes.c_float, ctypes.c_float, _u32p,
+                                          ctypes.c_int32, _u64p, _f32p, _i32p, _i32p]
         lib.xo_pq_chunk_offsets.argtypes = [ctypes.c_int32, ctypes.c_int32, _i32p]
         lib.xo_pq_encode.argtypes = [ctypes.c_int, _f32p, _i32p, ctypes.c_int32, ctypes.c_int32,
                                      _f32p, _u8p]
@@ -351,6 +356,30 @@ class Oracle:
                                          nq, k, nprobe, radius, _ptr(bm, _u32p),
                                          threads or os.cpu_count(), _ptr(ok, _u64p),
                                          _ptr(os_, _f32p), _ptr(oc, _i32p), _ptr(ost, _i32p))
+        return st, ok.reshape(nq, k), os_.reshape(nq, k), oc, ost
+
+    def ivf_sq8_search(self, metric, codes, params, originals, keys, centroids, list_offsets,
+                       list_positions, queries, k, nprobe, radius=0.0, refine_scale=0.0,
+                       bitmap=None, threads=0):
+        codes = _c(codes, np.int8)
+        params = np.ascontiguousarray(params, SQ_PARAMS_DTYPE)
+        originals = _c(originals, np.float32)
+        keys = _c(keys, np.uint64)
+        centroids = _c(centroids, np.float32)
+        lo = _c(list_offsets, np.int64)
+        lp = _c(list_positions, np.int64)
+        queries = _c(queries, np.float32)
+        n, d = codes.shape
+        nq = queries.shape[0]
+        ok, os_, oc, ost = self._outs(nq, k)
+        bm = None if bitmap is None else _c(bitmap, np.uint32)
+        st = self.lib.xo_ivf_sq8_search(metric, _ptr(codes, _i8p), params.ctypes.data,
+                                        _ptr(originals, _f32p), _ptr(keys, _u64p), n, d,
+                                        _ptr(centroids, _f32p), centroids.shape[0],
+                                        _ptr(lo, _i64p), _ptr(lp, _i64p), _ptr(queries, _f32p),
+                                        nq, k, nprobe, radius, refine_scale, _ptr(bm, _u32p),
+                                        threads or os.cpu_count(), _ptr(ok, _u64p),
+                                        _ptr(os_, _f32p), _ptr(oc, _i32p), _ptr(ost, _i32p))
         return st, ok.reshape(nq, k), os_.reshape(nq, k), oc, ost
 
     def pq_chunk_offsets(self, d, chunks):

@@ -1075,6 +1075,84 @@ extern "C" int xo_ivf_flat_search(int metric, const float* rows, const uint64_t*
   return first;
 }
 
+// ScalarQuantizedIVFIndex.search (ivf_quantized.go:135-192): quantizedQuery
+// first (validation, then the INT8 code), then the probe with the original
+// metric, then searchWithCode (quantized_index.go:313-335) over the probed
+// lists' positions; with refine_scale > 0 the refine stage of xo_sq8_search.
+extern "C" int xo_ivf_sq8_search(int metric, const int8_t* codes, const xo_sq_params* params,
+                                 const float* originals, const uint64_t* keys, int64_t n,
+                                 int32_t d, const float* centroids, int32_t nlist,
+                                 const int64_t* list_offsets, const int64_t* list_positions,
+                                 const float* queries, int32_t nq, int32_t k, int32_t nprobe,
+                                 float radius, float refine_scale, const uint32_t* bitmap,
+                                 int32_t threads, uint64_t* out_keys, float* out_scores,
+                                 int32_t* out_counts, int32_t* out_status) {
+  int st0 = validate_options(k, radius);
+  if (st0 != XO_OK) return st0;
+  if (nprobe <= 0) return XO_INVALID_ARGUMENT;
+  int32_t stage_k = k;
+  float stage_radius = radius;
+  const bool refine = refine_scale > 0;
+  if (refine) {
+    st0 = xo_refinement_candidate_count(k, refine_scale, &stage_k);
+    if (st0 != XO_OK) return st0;
+    stage_radius = 0;
+  }
+  std::vector<int32_t> status(nq, XO_OK);
+  parallel_for(nq, threads, [&](int64_t q) {
+    const float* query = queries + q * d;
+    std::vector<Result> res;
+    int st = validate_query(metric, query, d);
+    std::vector<int8_t> qcode(d);
+    xo_sq_params qp;
+    if (st == XO_OK) st = xo_quantize_int8(query, d, qcode.data(), &qp);
+    std::vector<Result> stage;
+    std::vector<int64_t> pos;
+    if (st == XO_OK && n > 0) {
+      std::vector<int32_t> lists(std::min(nprobe, nlist));
+      int32_t np = xo_ivf_probe(metric, centroids, nlist, d, query, nprobe, lists.data());
+      if (np < 0) st = -np;
+      for (int32_t i = 0; i < np; ++i)
+        for (int64_t j = list_offsets[lists[i]]; j < list_offsets[lists[i] + 1]; ++j)
+          pos.push_back(list_positions[j]);
+      WorstFirstHeap heap{metric, {}};
+      for (size_t i = 0; i < pos.size() && st == XO_OK; ++i) {
+        const int64_t p = pos[i];
+        if (!filter_pass(bitmap, p)) continue;
+        float sc;
+        st = xo_quantized_distance_int8(metric, codes + p * d, &params[p], qcode.data(), &qp, d,
+                                        &sc);
+        if (st != XO_OK) break;
+        if (!within_radius(metric, sc, stage_radius)) continue;
+        heap.offer(Result{keys[p], sc}, (size_t)stage_k);
+      }
+      if (st == XO_OK) stage = heap.sorted();
+    }
+    if (st == XO_OK && refine) {
+      std::vector<int64_t> stage_pos(stage.size(), -1);
+      for (size_t i = 0; i < stage.size(); ++i)
+        for (int64_t p : pos)
+          if (keys[p] == stage[i].key) {
+            stage_pos[i] = p;
+            break;
+          }
+      st = refine_exact(metric, query, d, stage, stage_pos, originals, keys, k, radius, bitmap,
+                        &res);
+    } else if (st == XO_OK) {
+      res = stage;
+    }
+    status[q] = st;
+    if (st != XO_OK) res.clear();
+    write_results(res, k, (int32_t)q, out_keys, out_scores, out_counts);
+  });
+  int first = XO_OK;
+  for (int32_t q = 0; q < nq; ++q) {
+    if (out_status) out_status[q] = status[q];
+    if (first == XO_OK) first = status[q];
+  }
+  return first;
+}
+
 // ---------------------------------------------------------------------------
 // Product quantization (internal/core/pq.go).
 // ---------------------------------------------------------------------------

@@ -119,6 +119,15 @@ int xo_ivf_flat_search(int metric, const float* rows, const uint64_t* keys, int6
                        float radius, const uint32_t* filter_bitmap, int32_t threads,
                        uint64_t* out_keys, float* out_scores, int32_t* out_counts,
                        int32_t* out_status);
+/* ScalarQuantizedIVFIndex search (ivf_quantized.go:135-192): the IVF probe,
+ * INT8 scoring of the probed positions, optional refine (refine_scale > 0). */
+int xo_ivf_sq8_search(int metric, const int8_t* codes, const xo_sq_params* params,
+                      const float* originals, const uint64_t* keys, int64_t n, int32_t d,
+                      const float* centroids, int32_t nlist, const int64_t* list_offsets,
+                      const int64_t* list_positions, const float* queries, int32_t nq, int32_t k,
+                      int32_t nprobe, float radius, float refine_scale,
+                      const uint32_t* filter_bitmap, int32_t threads, uint64_t* out_keys,
+                      float* out_scores, int32_t* out_counts, int32_t* out_status);
 
 /* ---- Product quantization (internal/core/pq.go) ------------------------ */
 void xo_pq_chunk_offsets(int32_t d, int32_t chunks, int32_t* offsets);

@@ -255,3 +255,39 @@ def test_flat_search_same_with_reference_kernels():
     finally:
         ora.use_reference_kernels(None)
     assert np.array_equal(a[1], b[1]) and np.array_equal(a[2], b[2])
+
+
+@pytest.mark.parametrize("metric", [L2, IP, COSINE, MIPSL2])
+def test_ivf_sq8_is_sq8_over_the_probed_lists(oracle, metric):
+    """ScalarQuantizedIVFIndex.search (ivf_quantized.go:135-192) is the SQ8
+    search (quantized_index.go:313-335) restricted to the positions of the
+    probed lists: per query, the SQ8 search with a filter holding exactly
+    those positions gives the same keys and scores (refine included)."""
+    rng = np.random.default_rng(40 + metric)
+    n, d, nlist = 700, 20, 9
+    rows = rng.standard_normal((n, d)).astype(np.float32)
+    keys = rng.permutation(50_000)[:n].astype(np.uint64)
+    queries = rng.standard_normal((6, d)).astype(np.float32)
+    centroids = rows[:nlist].copy()
+    st, labels, _ = oracle.kmeans_assign(metric, rows, centroids)
+    assert st == OK
+    offsets = np.cumsum(np.concatenate([[0], np.bincount(labels, minlength=nlist)])).astype(np.int64)
+    positions = np.argsort(labels, kind="stable").astype(np.int64)
+    codes, params = oracle.quantize_int8_batch(rows)
+    for nprobe, scale in ((3, 0.0), (3, 2.5), (nlist, 0.0)):
+        st, ok, os_, oc, ost = oracle.ivf_sq8_search(metric, codes, params, rows, keys, centroids,
+                                                     offsets, positions, queries, 12, nprobe,
+                                                     refine_scale=scale)
+        assert st == OK and (ost == 0).all()
+        for q in range(queries.shape[0]):
+            lists = oracle.ivf_probe(metric, centroids, queries[q], nprobe)
+            bitmap = np.zeros((n + 31) // 32, np.uint32)
+            for li in lists:
+                for p in positions[offsets[li]:offsets[li + 1]]:
+                    bitmap[p >> 5] |= np.uint32(1 << int(p & 31))
+            _, fk, fs, fc, _ = oracle.sq8_search(metric, codes, params, rows, keys,
+                                                 queries[q:q + 1], 12, refine_scale=scale,
+                                                 bitmap=bitmap)
+            assert oc[q] == fc[0]
+            assert np.array_equal(ok[q, :oc[q]], fk[0, :fc[0]])
+            assert np.array_equal(os_[q, :oc[q]].view(np.uint32), fs[0, :fc[0]].view(np.uint32))

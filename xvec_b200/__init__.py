@@ -32,7 +32,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libxvec_gpu.so")
 
 METRIC_L2, METRIC_IP, METRIC_COSINE, METRIC_MIPSL2 = 1, 2, 3, 4
-INDEX_FLAT, INDEX_SQ8_FLAT, INDEX_IVF_PQ, INDEX_RABITQ, INDEX_IVF_FLAT = 1, 2, 3, 4, 5
+INDEX_FLAT, INDEX_SQ8_FLAT, INDEX_IVF_PQ, INDEX_RABITQ, INDEX_IVF_FLAT, INDEX_IVF_SQ8 = (
+    1, 2, 3, 4, 5, 6)
 STORAGE_FP32, STORAGE_FP16 = 1, 2
 
 STATUS_NAMES = {
@@ -373,6 +374,14 @@ class IVFIndex(_Index):
     def set_model(self, centroids) -> None:
         centroids = np.ascontiguousarray(centroids, np.float32)
         _check(_lib.xvec_gpu_ivf_set_model(self._h, _ptr(centroids), centroids.shape[0]))
+
+
+class ScalarQuantizedIVFIndex(IVFIndex):
+    """core.ScalarQuantizedIVFIndex (internal/core/ivf_quantized.go:23-192):
+    probe the nprobe best centroids with the original metric, score the
+    probed lists' rows with INT8 codes (refine_scale > 0: exact rerank of the
+    floor(top_k * scale) best codes)."""
+    kind = INDEX_IVF_SQ8
 
 
 class RaBitQIndex(_Index):

@@ -466,6 +466,9 @@ xvec_gpu_status search_device_locked(xvec_gpu_index* idx, const void* d_q, int n
     case XVEC_INDEX_IVF_FLAT:
       return ivf_flat_search_impl(idx, static_cast<const float*>(d_q), nq, o, d_bitmap, d_keys,
                                   d_scores, d_counts, s, statuses);
+    case XVEC_INDEX_IVF_SQ8:
+      return ivf_sq8_search_impl(idx, static_cast<const float*>(d_q), nq, o, d_bitmap, d_keys,
+                                 d_scores, d_counts, s, statuses);
     default: return set_error("invalid index kind"), XVEC_GPU_INVALID_ARGUMENT;
   }
 }
@@ -602,6 +605,7 @@ extern "C" xvec_gpu_status xvec_gpu_index_create(const xvec_gpu_index_desc* desc
         return set_error("invalid storage"), XVEC_GPU_INVALID_ARGUMENT;
       break;
     case XVEC_INDEX_SQ8_FLAT:
+    case XVEC_INDEX_IVF_SQ8:
       if (desc->dimension > 65535)
         return set_error("core: invalid vector dimension: got %d", desc->dimension),
                XVEC_GPU_INVALID_ARGUMENT;

@@ -29,12 +29,21 @@ xvec_gpu_status make_probe_index(int device, int metric, int d, const float* d_c
                                  int nlist, cudaStream_t s, xvec_gpu_index** out);
 xvec_gpu_status rebuild_lists(xvec_gpu_index* idx, cudaStream_t s);
 
+xvec_gpu_status ivf_probe(xvec_gpu_index* idx, const float* d_q, int nq, int nprobe,
+                          const float* qf, const float* qn2, const int* q_status,
+                          uint64_t* pkeys, float* pscores, int* pcounts, int* q_flags,
+                          std::vector<int>* h_status, cudaStream_t s);
 xvec_gpu_status ivf_flat_reserve(xvec_gpu_index* idx, int64_t capacity, cudaStream_t s);
 xvec_gpu_status ivf_flat_commit(xvec_gpu_index* idx, int64_t old_n, int64_t m, cudaStream_t s);
 xvec_gpu_status ivf_flat_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
                                      const xvec_gpu_search_opts& o, const uint32_t* d_bitmap,
                                      uint64_t* d_keys, float* d_scores, int* d_counts,
                                      cudaStream_t s, std::vector<int>* statuses);
+
+xvec_gpu_status ivf_sq8_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
+                                    const xvec_gpu_search_opts& o, const uint32_t* d_bitmap,
+                                    uint64_t* d_keys, float* d_scores, int* d_counts,
+                                    cudaStream_t s, std::vector<int>* statuses);
 
 xvec_gpu_status rabitq_reserve(xvec_gpu_index* idx, int64_t capacity, cudaStream_t s);
 xvec_gpu_status rabitq_commit(xvec_gpu_index* idx, int64_t old_n, int64_t m, cudaStream_t s);

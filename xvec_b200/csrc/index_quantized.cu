@@ -1,5 +1,6 @@
 // index_quantized.cu — dispatch of the per-kind insertion hooks: the
-// quantized kinds (SQ8: sq8.cu, IVF-PQ: ivfpq.cu, RaBitQ: rabitq.cu) and the
+// quantized kinds (SQ8: sq8.cu, IVF-PQ: ivfpq.cu, RaBitQ: rabitq.cu), the IVF
+// list assignment (IVF-Flat and IVF-SQ8: ivf_flat.cu) and the
 // bfloat16 split of Flat FP32 rows (the tensor-core scan's operands).
 #include "flat_tc.cuh"
 #include "index_kernels.cuh"
@@ -23,6 +24,10 @@ xvec_gpu_status extra_reserve(xvec_gpu_index* idx, int64_t cap, cudaStream_t s) 
   if (idx->desc.kind == XVEC_INDEX_IVF_PQ) return ivfpq_reserve(idx, cap, s);
   if (idx->desc.kind == XVEC_INDEX_RABITQ) return rabitq_reserve(idx, cap, s);
   if (idx->desc.kind == XVEC_INDEX_IVF_FLAT) return ivf_flat_reserve(idx, cap, s);
+  if (idx->desc.kind == XVEC_INDEX_IVF_SQ8) {
+    const xvec_gpu_status st = sq8_reserve(idx, cap, s);
+    return st ? st : ivf_flat_reserve(idx, cap, s);
+  }
   return XVEC_GPU_OK;
 }
 xvec_gpu_status extra_validate(xvec_gpu_index* idx, int64_t, int64_t, cudaStream_t) {
@@ -30,7 +35,8 @@ xvec_gpu_status extra_validate(xvec_gpu_index* idx, int64_t, int64_t, cudaStream
     return set_error("set the IVF-PQ model before adding rows"), XVEC_GPU_INVALID_ARGUMENT;
   if (idx->desc.kind == XVEC_INDEX_RABITQ && !idx->has_model)
     return set_error("set the RaBitQ model before adding rows"), XVEC_GPU_INVALID_ARGUMENT;
-  if (idx->desc.kind == XVEC_INDEX_IVF_FLAT && !idx->has_model)
+  if ((idx->desc.kind == XVEC_INDEX_IVF_FLAT || idx->desc.kind == XVEC_INDEX_IVF_SQ8) &&
+      !idx->has_model)
     return set_error("set the IVF model before adding rows"), XVEC_GPU_INVALID_ARGUMENT;
   return XVEC_GPU_OK;
 }
@@ -47,6 +53,10 @@ xvec_gpu_status extra_commit(xvec_gpu_index* idx, int64_t old_n, int64_t m, cuda
   if (idx->desc.kind == XVEC_INDEX_IVF_PQ) return ivfpq_commit(idx, old_n, m, s);
   if (idx->desc.kind == XVEC_INDEX_RABITQ) return rabitq_commit(idx, old_n, m, s);
   if (idx->desc.kind == XVEC_INDEX_IVF_FLAT) return ivf_flat_commit(idx, old_n, m, s);
+  if (idx->desc.kind == XVEC_INDEX_IVF_SQ8) {
+    const xvec_gpu_status st = sq8_commit(idx, old_n, m, s);
+    return st ? st : ivf_flat_commit(idx, old_n, m, s);
+  }
   return XVEC_GPU_OK;
 }
 

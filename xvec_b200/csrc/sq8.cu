@@ -16,12 +16,15 @@
 // round-to-nearest intrinsics) and selects the k (or refine-count) best.
 #include <algorithm>
 #include <cmath>
+#include <mutex>
+#include <vector>
 
 #include "capi_internal.h"
 #include "common.cuh"
 #include "flat_kernels.cuh"
 #include "flat_tc.cuh"
 #include "index_kernels.cuh"
+#include "ivf_scan.cuh"
 #include "pipeline.cuh"
 #include "refine.cuh"
 
@@ -278,6 +281,48 @@ int sq8_kp(int k) {
   return kp;
 }
 
+// The IVF list scan over INT8 codes (ivf_scan.cuh): the exact integer dot of
+// the row's codes with the query's codes (staged in shared memory, dp4a on
+// 4-byte groups), ranked with SQ8Ranker; the reference score as SQ8Scorer.
+struct Sq8IvfPolicy {
+  int metric;
+  const int8_t* codes;
+  const SQParams* params;
+  const float4* row_fast;
+  const int8_t* qcodes;
+  const SQParams* qparams;
+  const float4* q_info;
+  int d;
+  __host__ __device__ int smem_bytes(int dim) const { return (dim + 15) / 16 * 16; }
+  __device__ void stage(int q, unsigned char* smem) const {
+    int8_t* sq = reinterpret_cast<int8_t*>(smem);
+    for (int i = threadIdx.x; i < d; i += blockDim.x) sq[i] = qcodes[(int64_t)q * d + i];
+  }
+  __device__ float fast_rank(int q, uint32_t pos, const unsigned char* smem) const {
+    const int8_t* a = codes + (int64_t)pos * d;
+    int dot = 0;
+    if ((d & 3) == 0) {
+      const int* a4 = reinterpret_cast<const int*>(a);
+      const int* b4 = reinterpret_cast<const int*>(smem);
+      for (int i = 0; i < d / 4; ++i) dot = __dp4a(__ldg(a4 + i), b4[i], dot);
+    } else {
+      const int8_t* b = reinterpret_cast<const int8_t*>(smem);
+      for (int i = 0; i < d; ++i) dot += (int)__ldg(a + i) * (int)b[i];
+    }
+    const SQ8Ranker rk{metric, row_fast, q_info};
+    return rk.rank((float)dot, row_fast[pos], q_info[q]);
+  }
+  __device__ float exact_score(int q, uint32_t pos, const unsigned char* smem) const {
+    const int lane = threadIdx.x & 31;
+    const int8_t* a = codes + (int64_t)pos * d;
+    const int8_t* b = reinterpret_cast<const int8_t*>(smem);
+    int dot = 0;
+    for (int i = lane; i < d; i += 32) dot += (int)a[i] * (int)b[i];
+    for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(kFullMask, dot, o);
+    return sq_reference_score(metric, (double)dot, params[pos], qparams[q], d);
+  }
+};
+
 }  // namespace
 
 // ---------------------------------------------------------------------------
@@ -521,6 +566,215 @@ xvec_gpu_status sq8_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
   timer.mark(3);
   XVEC_CUDA(cudaStreamSynchronize(s));
   count_search(nq, (int64_t)exact_list.size(), timer.ms(1, 2), timer.ms(0, 3));
+  if (statuses) {
+    statuses->resize(nq);
+    for (int q = 0; q < nq; ++q) {
+      int sq = h_status[q];
+      if (sq == 0 && (h_flags[q] & 4)) sq = XVEC_GPU_NON_FINITE;
+      (*statuses)[q] = sq;
+    }
+  }
+  return XVEC_GPU_OK;
+}
+
+// ---------------------------------------------------------------------------
+// IVF over INT8 codes: ScalarQuantizedIVFIndex.search (ivf_quantized.go:
+// 135-192): the query's INT8 code first (quantizedQuery: validation, then
+// quantization), the IVF probe with the original metric (ivf_probe, shared
+// with the exact IVF), then the scalar-quantized scoring of the probed
+// lists' positions (searchWithCode, quantized_index.go:313-335), and the
+// refine stage when a refine scale is given (refiner.go:66-129).
+// ---------------------------------------------------------------------------
+xvec_gpu_status ivf_sq8_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
+                                    const xvec_gpu_search_opts& o, const uint32_t* d_bitmap,
+                                    uint64_t* d_keys, float* d_scores, int* d_counts,
+                                    cudaStream_t s, std::vector<int>* statuses) {
+  if (!idx->has_model) return set_error("IVF index has no model"), XVEC_GPU_INVALID_ARGUMENT;
+  if (o.nprobe <= 0) return set_error("core: IVF NProbe must be positive"), XVEC_GPU_INVALID_ARGUMENT;
+  EventTimer timer(s);
+  timer.mark(0);
+  const int d = idx->desc.dimension, metric = idx->desc.metric;
+  const int64_t n = idx->n;
+  const bool refine = o.refine_scale > 0;
+  int stage_k = o.top_k;
+  if (refine) {
+    if (std::isinf(o.refine_scale))
+      return set_error("core: refiner scale factor must be finite and positive"),
+             XVEC_GPU_INVALID_ARGUMENT;
+    const double product = (double)o.top_k * (double)o.refine_scale;
+    if (product >= 1024.0 + 1.0)
+      return set_error("refinement candidate count %.0f exceeds 1024", std::floor(product)),
+             XVEC_GPU_INVALID_ARGUMENT;
+    stage_k = std::max(1, (int)std::floor(product));  // RefinementCandidateCount
+  }
+  const float stage_radius = refine ? 0.f : o.radius;  // collection.go:1623
+  xvec_gpu_status st;
+  {
+    static std::mutex rebuild_mu;
+    std::lock_guard<std::mutex> g(rebuild_mu);
+    if (idx->lists_dirty && n > 0 && (st = rebuild_lists(idx, s))) return st;
+  }
+  const int nprobe = std::min(o.nprobe, idx->nlist);
+  const int kp = sq8_kp(stage_k);
+  if ((int64_t)kIvfWarps * kp > flat_merge_capacity())
+    return set_error("top_k %d exceeds the merge capacity", stage_k), XVEC_GPU_INVALID_ARGUMENT;
+  // The probe's query terms (metric.Compute validation, cosine magnitudes).
+  Scratch pf, pn2, paux, pstatus, pkeys, pscores, pcounts;
+  if ((st = pf.alloc((size_t)nq * d * 4, s)) || (st = pn2.alloc((size_t)nq * 4, s)) ||
+      (st = paux.alloc((size_t)nq * 4, s)) || (st = pstatus.alloc((size_t)nq * 4, s)) ||
+      (st = pkeys.alloc((size_t)nq * nprobe * 8, s)) ||
+      (st = pscores.alloc((size_t)nq * nprobe * 4, s)) || (st = pcounts.alloc((size_t)nq * 4, s)))
+    return st;
+  // The scalar-quantized query.
+  Scratch qcodes, qparams, qf, qinfo, qeps, qstatus, qflags;
+  if ((st = qcodes.alloc((size_t)nq * d, s)) ||
+      (st = qparams.alloc((size_t)nq * sizeof(SQParams), s)) ||
+      (st = qf.alloc((size_t)nq * d * 4, s)) || (st = qinfo.alloc((size_t)nq * 16, s)) ||
+      (st = qeps.alloc((size_t)nq * 4, s)) || (st = qstatus.alloc((size_t)nq * 4, s)) ||
+      (st = qflags.alloc((size_t)nq * 4, s)))
+    return st;
+  XVEC_CUDA(cudaMemsetAsync(qflags.ptr, 0, (size_t)nq * 4, s));
+  XVEC_CUDA(cudaMemsetAsync(qstatus.ptr, 0, (size_t)nq * 4, s));
+  sq8_prep_queries_kernel<<<blocks_of((int64_t)nq * 32), 256, 0, s>>>(
+      d_q, nq, d, metric, idx->sq_bounds.as<unsigned>(), qcodes.as<int8_t>(),
+      qparams.as<SQParams>(), qf.as<float>(), qinfo.as<float4>(), qeps.as<float>(),
+      qstatus.as<int>());
+  XVEC_LAUNCHED();
+  launch_prep_queries<float>(d_q, nq, d, metric, pf.as<float>(), pn2.as<float>(),
+                             paux.as<float>(), pstatus.as<int>(), s);
+  XVEC_LAUNCHED();
+  std::vector<int> h_probe(nq), h_sq(nq);
+  if ((st = ivf_probe(idx, d_q, nq, nprobe, pf.as<float>(), pn2.as<float>(), pstatus.as<int>(),
+                      pkeys.as<uint64_t>(), pscores.as<float>(), pcounts.as<int>(),
+                      qflags.as<int>(), &h_probe, s)))
+    return st;
+  XVEC_CUDA(cudaMemcpyAsync(h_sq.data(), qstatus.ptr, (size_t)nq * 4, cudaMemcpyDeviceToHost, s));
+  XVEC_CUDA(cudaStreamSynchronize(s));
+  // Per-query status before the scan: the quantization's, then the probe's.
+  std::vector<int> h_status(nq);
+  for (int q = 0; q < nq; ++q) h_status[q] = h_sq[q] ? h_sq[q] : h_probe[q];
+  XVEC_CUDA(cudaMemcpyAsync(qstatus.ptr, h_status.data(), (size_t)nq * 4, cudaMemcpyHostToDevice,
+                            s));
+  // Stage outputs: the final outputs, or scratch when a refine stage follows.
+  Scratch skeys, sscores, scounts, spos;
+  uint64_t* o_keys = d_keys;
+  float* o_scores = d_scores;
+  int* o_counts = d_counts;
+  if ((st = spos.alloc((size_t)nq * stage_k * 4, s))) return st;
+  if (refine) {
+    if ((st = skeys.alloc((size_t)nq * stage_k * 8, s)) ||
+        (st = sscores.alloc((size_t)nq * stage_k * 4, s)) ||
+        (st = scounts.alloc((size_t)nq * 4, s)))
+      return st;
+    o_keys = skeys.as<uint64_t>();
+    o_scores = sscores.as<float>();
+    o_counts = scounts.as<int>();
+  }
+  XVEC_CUDA(cudaMemsetAsync(o_counts, 0, (size_t)nq * 4, s));
+  int exact_count = 0;
+  if (n > 0) {
+    Scratch lkeys, lcounts, lsat;
+    const size_t lists = (size_t)nq * kIvfWarps;
+    if ((st = lkeys.alloc(lists * kp * 8, s)) || (st = lcounts.alloc(lists * 4, s)) ||
+        (st = lsat.alloc(lists * 8, s)))
+      return st;
+    const SQ8Scorer sc{metric, idx->sq_codes.as<int8_t>(), idx->sq_params.as<SQParams>(),
+                       qcodes.as<int8_t>(), qparams.as<SQParams>(), qeps.as<float>(), d};
+    const Sq8IvfPolicy pol{metric,
+                           idx->sq_codes.as<int8_t>(),
+                           idx->sq_params.as<SQParams>(),
+                           idx->sq_fast.as<float4>(),
+                           qcodes.as<int8_t>(),
+                           qparams.as<SQParams>(),
+                           qinfo.as<float4>(),
+                           d};
+    auto scan = [&](bool exact, const int* ids, int count) -> xvec_gpu_status {
+      cudaError_t e =
+          exact ? launch_ivf_list_scan<true>(pol, d, pkeys.as<uint64_t>(), pcounts.as<int>(),
+                                             nprobe, idx->list_offsets.as<int64_t>(),
+                                             idx->list_rows.as<uint32_t>(),
+                                             idx->list_keyrank.as<uint32_t>(), d_bitmap, ids,
+                                             count, kp, lkeys.as<uint64_t>(), lcounts.as<int>(),
+                                             lsat.as<uint64_t>(), qflags.as<int>(), s)
+                : launch_ivf_list_scan<false>(pol, d, pkeys.as<uint64_t>(), pcounts.as<int>(),
+                                              nprobe, idx->list_offsets.as<int64_t>(),
+                                              idx->list_rows.as<uint32_t>(),
+                                              idx->list_keyrank.as<uint32_t>(), d_bitmap, ids,
+                                              count, kp, lkeys.as<uint64_t>(), lcounts.as<int>(),
+                                              lsat.as<uint64_t>(), qflags.as<int>(), s);
+      if (e == cudaErrorInvalidValue)
+        return set_error("top_k %d or dimension %d too large for the IVF scan", stage_k, d),
+               XVEC_GPU_UNSUPPORTED;
+      XVEC_CUDA(e);
+      XVEC_LAUNCHED();
+      XVEC_CUDA(launch_merge_rescore(sc, idx->pos_of_kr.as<uint32_t>(), idx->keys.as<uint64_t>(),
+                                     ids, count, stage_k, stage_radius, exact ? 1 : 0,
+                                     lkeys.as<uint64_t>(), lcounts.as<int>(), lsat.as<uint64_t>(),
+                                     kIvfWarps, kp, o_keys, o_scores, o_counts,
+                                     spos.as<uint32_t>(), qflags.as<int>(), s));
+      XVEC_LAUNCHED();
+      return XVEC_GPU_OK;
+    };
+    // Inner product and L2 have a fast rank; cosine and MIPS are scored in
+    // reference order from the start.
+    const bool ranked = metric == XVEC_METRIC_IP || metric == XVEC_METRIC_L2;
+    timer.mark(1);
+    std::vector<int> exact_list;
+    if (ranked) {
+      if ((st = scan(false, nullptr, nq))) return st;
+      std::vector<int> h_fl(nq);
+      XVEC_CUDA(cudaMemcpyAsync(h_fl.data(), qflags.ptr, (size_t)nq * 4, cudaMemcpyDeviceToHost,
+                                s));
+      XVEC_CUDA(cudaStreamSynchronize(s));
+      for (int q = 0; q < nq; ++q)
+        if (h_status[q] == 0 && (h_fl[q] & 3)) exact_list.push_back(q);
+    } else {
+      for (int q = 0; q < nq; ++q)
+        if (h_status[q] == 0) exact_list.push_back(q);
+    }
+    timer.mark(2);
+    if (!exact_list.empty()) {
+      const int nl = (int)exact_list.size();
+      Scratch ids;
+      if ((st = ids.alloc((size_t)nl * 4, s))) return st;
+      XVEC_CUDA(cudaMemcpyAsync(ids.ptr, exact_list.data(), (size_t)nl * 4,
+                                cudaMemcpyHostToDevice, s));
+      sq8_clear_flags<<<blocks_of(nl), 256, 0, s>>>(ids.as<int>(), nl, qflags.as<int>());
+      XVEC_LAUNCHED();
+      if ((st = scan(true, ids.as<int>(), nl))) return st;
+      exact_count = nl;
+      std::vector<int> h_fl(nq);
+      XVEC_CUDA(cudaMemcpyAsync(h_fl.data(), qflags.ptr, (size_t)nq * 4, cudaMemcpyDeviceToHost,
+                                s));
+      XVEC_CUDA(cudaStreamSynchronize(s));
+      for (int q : exact_list)
+        if (h_fl[q] & 2)
+          return set_error("exact scan could not complete query %d", q), XVEC_GPU_CUDA_ERROR;
+    }
+  }
+  if (refine && n > 0) {
+    // The approximate stage's failures are final; the refine stage sees
+    // counts >= 0 only for healthy queries.
+    sq8_status_kernel<<<blocks_of(nq), 256, 0, s>>>(qstatus.as<int>(), qflags.as<int>(), nq,
+                                                    o_counts);
+    XVEC_CUDA(cudaMemsetAsync(d_counts, 0, (size_t)nq * 4, s));
+    XVEC_CUDA(launch_refine(idx->rows.as<float>(), d, metric, d_q, nq, spos.as<uint32_t>(),
+                            o_counts, stage_k, idx->keyrank.as<uint32_t>(),
+                            idx->pos_of_kr.as<uint32_t>(), idx->keys.as<uint64_t>(), o.top_k,
+                            o.radius, d_keys, d_scores, d_counts, qflags.as<int>(), s));
+    count_launches(2);
+  } else if (refine) {
+    XVEC_CUDA(cudaMemsetAsync(d_counts, 0, (size_t)nq * 4, s));
+  }
+  sq8_status_kernel<<<blocks_of(nq), 256, 0, s>>>(qstatus.as<int>(), qflags.as<int>(), nq,
+                                                  d_counts);
+  XVEC_LAUNCHED();
+  XVEC_CUDA(cudaGetLastError());
+  std::vector<int> h_flags(nq);
+  XVEC_CUDA(cudaMemcpyAsync(h_flags.data(), qflags.ptr, (size_t)nq * 4, cudaMemcpyDeviceToHost, s));
+  timer.mark(3);
+  XVEC_CUDA(cudaStreamSynchronize(s));
+  count_search(nq, exact_count, timer.ms(1, 2), timer.ms(0, 3));
   if (statuses) {
     statuses->resize(nq);
     for (int q = 0; q < nq; ++q) {
