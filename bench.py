@@ -52,7 +52,7 @@ def parse():
                         "the JSON line as batch_sweep (rabitq_l2_refine, ivfpq_l2, sq8_ip_refine)")
     p.add_argument("--workload",
                    choices=["flat_cosine_fp16", "ivfpq_l2", "sq8_ip_refine", "rabitq_l2_refine",
-                            "flat_l2_fp32", "ivf_flat_l2"],
+                            "flat_l2_fp32", "ivf_flat_l2", "ivf_sq8_l2_refine"],
                    default="flat_cosine_fp16",
                    help="flat_cosine_fp16: the Flat configuration above (default); ivfpq_l2: "
                         "IVF-PQ L2, 1e8 x 128, nlist 16384, 32 x 256 PQ, nprobe 64, k=10; "
@@ -60,7 +60,8 @@ def parse():
                         "rabitq_l2_refine: one-bit RaBitQ L2, 1e7 x 960, k=10, EF 100; "
                         "flat_l2_fp32: Flat L2 over FP32 storage, 1e6 x 128 N(0,1), 1,000 "
                         "queries, k=10; ivf_flat_l2: IVF with exact scoring, 1e7 x 128, "
-                        "nlist 4096, nprobe 32, k=10")
+                        "nlist 4096, nprobe 32, k=10; ivf_sq8_l2_refine: the same IVF with "
+                        "INT8 list scoring and ScaleFactor 4")
     return p.parse_args()
 
 
@@ -504,9 +505,15 @@ IVF_N, IVF_NLIST, IVF_NPROBE, IVF_K, IVF_TRAIN = 10_000_000, 4096, 32, 10, 1_000
 IVF_WORKLOAD = ("IVF exact L2 search, 10,000,000 x 128 float32 (10,000-cluster mixture), nlist "
                 "4,096 (GPU k-means on the first 1,000,000 rows), nprobe 32, 10,000 queries, "
                 "top-k=10")
+# The same index with INT8 scalar-quantized list scoring
+# (ScalarQuantizedIVFIndex.SearchIVF) and the FP32 refine of the 40 best codes.
+IVF_SQ_SCALE = 4.0
+IVF_SQ_WORKLOAD = ("IVF INT8 scalar-quantized L2 search with FP32 refinement, 10,000,000 x 128 "
+                   "(10,000-cluster mixture), nlist 4,096 (GPU k-means on the first 1,000,000 "
+                   "rows), nprobe 32, 10,000 queries, top-k=10, ScaleFactor 4")
 
 
-def run_ivf_flat(args):
+def run_ivf_flat(args, sq8=False):
     import numpy as np
     import torch
 
@@ -528,7 +535,8 @@ def run_ivf_flat(args):
                                              stream=stream)
     cents = cents[:kc].contiguous()
     del train, labels
-    index = xb.IVFIndex(PQ_DIM, xb.METRIC_L2, device=local)
+    cls = xb.ScalarQuantizedIVFIndex if sq8 else xb.IVFIndex
+    index = cls(PQ_DIM, xb.METRIC_L2, device=local)
     index.set_model(cents.cpu().numpy())
     b, e = shard_range(n, rank, world, align=PQ_CHUNK_ROWS)
     index.reserve(e - b)
@@ -556,7 +564,8 @@ def run_ivf_flat(args):
     h_sizes = sizes.cpu().numpy()
     scanned = int(h_sizes[pr.keys.astype(np.int64)].sum())
     probe.close()
-    opts = xb.SearchOptions(top_k=IVF_K, nprobe=IVF_NPROBE)
+    opts = xb.SearchOptions(top_k=IVF_K, nprobe=IVF_NPROBE,
+                            refine_scale=IVF_SQ_SCALE if sq8 else 0.0)
     ms, scan_ms, e2e_ms, st, clocks = time_search(ShardedSearch(index), queries, opts, args, dev,
                                                   world, local)
     cpu = None
@@ -568,30 +577,50 @@ def run_ivf_flat(args):
         np.add.at(offsets, labels_h + 1, 1)
         offsets = np.cumsum(offsets)
         positions = np.argsort(labels_h, kind="stable").astype(np.int64)
-        qs = queries[:max(8, args.cpu_sample_queries // 4)].cpu().numpy()
+        # About 10-20 s of CPU work on the box's host cores.
+        qs = queries[:max(8, args.cpu_sample_queries * 4)].cpu().numpy()
         threads = os.cpu_count() or 1
-        t0 = time.perf_counter()
-        Oracle().ivf_flat_search(OL2, allrows, np.arange(n, dtype=np.uint64), cents.cpu().numpy(),
-                                 offsets, positions, qs, IVF_K, IVF_NPROBE, threads=threads)
+        ora = Oracle()
+        all_keys = np.arange(n, dtype=np.uint64)
+        if sq8:
+            codes, params = ora.quantize_int8_batch(allrows)
+            t0 = time.perf_counter()
+            ora.ivf_sq8_search(OL2, codes, params, allrows, all_keys, cents.cpu().numpy(),
+                               offsets, positions, qs, IVF_K, IVF_NPROBE,
+                               refine_scale=IVF_SQ_SCALE, threads=threads)
+        else:
+            t0 = time.perf_counter()
+            ora.ivf_flat_search(OL2, allrows, all_keys, cents.cpu().numpy(), offsets, positions,
+                                qs, IVF_K, IVF_NPROBE, threads=threads)
         dt = time.perf_counter() - t0
         cpu = {"value": qs.shape[0] / dt, "unit": "queries/sec", "cores": threads, "kind": "port",
                "sample": f"{qs.shape[0]} queries over the full index, {dt:.1f} s on {threads} "
-                         "threads (lists from the GPU assignment, not timed)"}
+                         "threads (lists from the GPU assignment"
+                         + (", codes from the oracle's quantizer" if sq8 else "")
+                         + ", not timed)"}
     if rank == 0:
         _, hbm_peak, peak_kind = peaks()
-        nbytes = scanned * PQ_DIM * 4
+        # Per scanned row: the float32 row, or the INT8 codes and the row's
+        # 16-byte scoring terms.
+        row_bytes = PQ_DIM + 16 if sq8 else PQ_DIM * 4
+        nbytes = scanned * row_bytes
         achieved = nbytes / (scan_ms / 1000.0) / 1e9 if scan_ms > 0 else None
         roof = {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                 "frac": (achieved / hbm_peak) if achieved else None, "traffic": None,
                 "peak_source": f"{peak_kind} HBM copy bandwidth",
-                "kernel": "IVF exact list scan", "kernel_ms": scan_ms,
-                "algorithmic_bytes_per_launch": nbytes, "scanned_rows_per_launch": scanned}
-        config = {"workload": IVF_WORKLOAD, "global_batch": nq, "top_k": IVF_K, "base_vectors": n,
-                  "dim": PQ_DIM, "metric": "l2", "nlist": kc, "nprobe": IVF_NPROBE,
-                  "kmeans_iterations": iters,
+                "kernel": "IVF INT8 list scan" if sq8 else "IVF exact list scan",
+                "kernel_ms": scan_ms, "algorithmic_bytes_per_launch": nbytes,
+                "scanned_rows_per_launch": scanned}
+        config = {"workload": IVF_SQ_WORKLOAD if sq8 else IVF_WORKLOAD, "global_batch": nq,
+                  "top_k": IVF_K, "base_vectors": n, "dim": PQ_DIM, "metric": "l2", "nlist": kc,
+                  "nprobe": IVF_NPROBE, "kmeans_iterations": iters,
                   "parallelism": f"rows sharded over {world} GPU(s), NCCL all-gather + merge",
-                  "l2": "inputs larger than L2 (5.1 GB rows)"}
-        print(json.dumps(common_line(nq, ms, e2e_ms, args, world, "f32", config, roof, cpu, clocks,
+                  "l2": ("inputs larger than L2 (1.3 GB codes, 5.1 GB rows)" if sq8
+                         else "inputs larger than L2 (5.1 GB rows)")}
+        if sq8:
+            config["refine_scale"] = IVF_SQ_SCALE
+        dtype = "i8 codes, f32/f64 scores" if sq8 else "f32"
+        print(json.dumps(common_line(nq, ms, e2e_ms, args, world, dtype, config, roof, cpu, clocks,
                                      st, IVF_K, PQ_DIM, 4)), flush=True)
     finish_ranks(world)
 
@@ -891,6 +920,8 @@ def main():
         return run_flat_fp32(args)
     if args.workload == "ivf_flat_l2":
         return run_ivf_flat(args)
+    if args.workload == "ivf_sq8_l2_refine":
+        return run_ivf_flat(args, sq8=True)
     if args.workload == "rabitq_l2_refine":
         return run_rabitq(args)
 

@@ -102,6 +102,8 @@ class Oracle:
         lib.xo_quantized_distance_int8.argtypes = [ctypes.c_int, _i8p, ctypes.POINTER(SQParams),
                                                    _i8p, ctypes.POINTER(SQParams),
                                                    ctypes.c_int32, _f32p]
+        lib.xo_quantize_int8_batch.argtypes = [_f32p, ctypes.c_int64, ctypes.c_int32,
+                                               ctypes.c_int32, _i8p, ctypes.c_void_p]
         lib.xo_refinement_candidate_count.argtypes = [ctypes.c_int32, ctypes.c_float, _i32p]
         lib.xo_sq8_search.argtypes = [ctypes.c_int, _i8p, ctypes.c_void_p, _f32p, _u64p,
                                       ctypes.c_int64, ctypes.c_int32, _f32p, ctypes.c_int32,
@@ -244,18 +246,15 @@ class Oracle:
         st = self.lib.xo_quantize_int8(_ptr(v, _f32p), v.size, _ptr(codes, _i8p), ctypes.byref(p))
         return st, codes, p
 
-    def quantize_int8_batch(self, rows):
+    def quantize_int8_batch(self, rows, threads=0):
         rows = _c(rows, np.float32)
         n, d = rows.shape
         codes = np.zeros((n, d), np.int8)
         params = np.zeros(n, SQ_PARAMS_DTYPE)
-        for i in range(n):
-            p = SQParams()
-            st = self.lib.xo_quantize_int8(_ptr(rows[i], _f32p), d, _ptr(codes[i], _i8p),
-                                           ctypes.byref(p))
-            if st != OK:
-                raise ValueError(f"quantize row {i}: status {st}")
-            params[i] = (p.inverse_scale, p.offset, p.code_sum, p.code_square)
+        st = self.lib.xo_quantize_int8_batch(_ptr(rows, _f32p), n, d, threads or os.cpu_count(),
+                                             _ptr(codes, _i8p), params.ctypes.data)
+        if st != OK:
+            raise ValueError(f"quantize rows: status {st}")
         return codes, params
 
     def quantize_int4(self, v):

@@ -637,6 +637,20 @@ extern "C" int xo_quantize_int8(const float* v, int32_t d, int8_t* codes, xo_sq_
   return quantize_integer(v, d, -127, 127, p, [&](int32_t i, int c) { codes[i] = (int8_t)c; });
 }
 
+// QuantizeVector(QuantizationInt8, row) for each of n rows (threads > 1:
+// rows split across threads; the per-row result does not depend on it).
+// Returns the first failing row's status.
+extern "C" int xo_quantize_int8_batch(const float* rows, int64_t n, int32_t d, int32_t threads,
+                                      int8_t* codes, xo_sq_params* params) {
+  std::vector<int> status(n > 0 ? (size_t)n : 1, XO_OK);
+  parallel_for(n, threads, [&](int64_t i) {
+    status[i] = xo_quantize_int8(rows + i * d, d, codes + i * d, &params[i]);
+  });
+  for (int64_t i = 0; i < n; ++i)
+    if (status[i] != XO_OK) return status[i];
+  return XO_OK;
+}
+
 extern "C" int xo_quantize_int4(const float* v, int32_t d, uint8_t* packed, xo_sq_params* p) {
   if (d % 2 != 0) return XO_INVALID_ARGUMENT;  // ErrOddInt4Dimension
   std::memset(packed, 0, (size_t)d / 2);

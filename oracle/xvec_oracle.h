@@ -80,6 +80,9 @@ typedef struct {
 } xo_sq_params;
 
 int xo_quantize_int8(const float* v, int32_t d, int8_t* codes, xo_sq_params* params);
+/* xo_quantize_int8 over n rows [n*d] (threads > 1: rows split across threads). */
+int xo_quantize_int8_batch(const float* rows, int64_t n, int32_t d, int32_t threads,
+                           int8_t* codes, xo_sq_params* params);
 int xo_quantize_int4(const float* v, int32_t d, uint8_t* packed, xo_sq_params* params);
 int xo_quantized_distance_int8(int metric, const int8_t* left, const xo_sq_params* lp,
                                const int8_t* right, const xo_sq_params* rp, int32_t d,

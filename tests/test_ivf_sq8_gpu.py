@@ -132,3 +132,31 @@ def test_ivf_sq8_requires_model_and_nprobe(xb):
                                   xb.SearchOptions(top_k=2, nprobe=1))
     assert res.keys[0, 0] == 0 and res.keys[1, 0] == 1
     idx.close()
+
+
+@pytest.mark.parametrize("metric,d", [(L2, 4), (L2, 64), (IP, 32), (COSINE, 24)])
+def test_ivf_sq8_full_probe_matches_sq8_flat(xb, metric, d):
+    """TestScalarQuantizedIVFFullProbeMatchesQuantizedFlat
+    (quantized_index_test.go:173-201), with INT8 codes: probing every list
+    with a key filter gives exactly the SQ8 Flat index's result."""
+    rng = np.random.default_rng(173 + d)
+    n = 320
+    rows = rng.standard_normal((n, d)).astype(np.float32)
+    keys = np.arange(1, n + 1, dtype=np.uint64) * 3
+    centroids = rows[rng.choice(n, 16, replace=False)].copy()
+    ivf = xb.ScalarQuantizedIVFIndex(d, metric)
+    ivf.set_model(centroids)
+    ivf.add(keys, rows)
+    flat = xb.ScalarQuantizedFlatIndex(d, metric)
+    flat.add(keys, rows)
+    bitmap = xb.bitmap_from_predicate(n, keys, lambda k: k % 5 != 0)
+    queries = np.concatenate([rows[217:218], rng.standard_normal((7, d)).astype(np.float32)])
+    got = ivf.search_with_options(queries, xb.SearchOptions(top_k=31, nprobe=16, filter=bitmap))
+    want = flat.search_with_options(queries, xb.SearchOptions(top_k=31, filter=bitmap))
+    assert np.array_equal(got.counts, want.counts)
+    for q in range(queries.shape[0]):
+        c = int(want.counts[q])
+        assert np.array_equal(got.keys[q, :c], want.keys[q, :c]), q
+        assert np.array_equal(got.scores[q, :c].view(np.uint32), want.scores[q, :c].view(np.uint32))
+    ivf.close()
+    flat.close()

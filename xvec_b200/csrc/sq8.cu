@@ -301,7 +301,18 @@ struct Sq8IvfPolicy {
   __device__ float fast_rank(int q, uint32_t pos, const unsigned char* smem) const {
     const int8_t* a = codes + (int64_t)pos * d;
     int dot = 0;
-    if ((d & 3) == 0) {
+    if ((d & 15) == 0) {
+      // 16-byte loads: the lane's code row in d/16 requests.
+      const int4* a16 = reinterpret_cast<const int4*>(a);
+      const int4* b16 = reinterpret_cast<const int4*>(smem);
+      for (int i = 0; i < d / 16; ++i) {
+        const int4 x = __ldg(a16 + i), y = b16[i];
+        dot = __dp4a(x.x, y.x, dot);
+        dot = __dp4a(x.y, y.y, dot);
+        dot = __dp4a(x.z, y.z, dot);
+        dot = __dp4a(x.w, y.w, dot);
+      }
+    } else if ((d & 3) == 0) {
       const int* a4 = reinterpret_cast<const int*>(a);
       const int* b4 = reinterpret_cast<const int*>(smem);
       for (int i = 0; i < d / 4; ++i) dot = __dp4a(__ldg(a4 + i), b4[i], dot);
