@@ -55,7 +55,7 @@ def test_tc_768_many_query_blocks(oracle, xb, metric):
     run(oracle, xb, metric, rows, queries, keys, 100)
 
 
-@pytest.mark.parametrize("d", [64, 72, 128, 200, 960])
+@pytest.mark.parametrize("d", [64, 72, 128, 200, 512, 520, 960])
 def test_tc_dims_and_ragged_rows(oracle, xb, d):
     rng = np.random.default_rng(d)
     rows = mixture(rng, 4097, d)

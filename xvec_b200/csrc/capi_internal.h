@@ -167,6 +167,11 @@ struct xvec_gpu_index {
   // a list holds at byte t its chunk (i mod 32 + t) mod 32 G (zero past the
   // last chunk).
   xvec::DeviceBuffer list_codes_t;  // uint8 [n][32 G] in list_rows order
+  // IVF-SQ8 (d % 16 == 0): the INT8 codes in list_rows order, interleaved by
+  // 32-row groups: 16-byte chunk c of list entry i at chunk index
+  // ((i / 32) (d / 16) + c) 32 + i mod 32; the float4 rank terms in list order.
+  xvec::DeviceBuffer list_sq_codes;
+  xvec::DeviceBuffer list_sq_fast;
   bool lists_dirty = true;
 
   // RaBitQ (one-bit).

@@ -133,7 +133,7 @@ struct IvfFlatPolicy {
     const float* qv = qf + (int64_t)q * d;
     for (int i = threadIdx.x; i < d; i += blockDim.x) sq[i] = qv[i];
   }
-  __device__ float fast_rank(int q, uint32_t pos, const unsigned char* smem) const {
+  __device__ float fast_rank(int q, int64_t, uint32_t pos, const unsigned char* smem) const {
     const float* x = rows + (int64_t)pos * d;
     const float* sq = reinterpret_cast<const float*>(smem);
     float dot = 0.f;

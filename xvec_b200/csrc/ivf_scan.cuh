@@ -13,8 +13,9 @@
 //
 // Policy:  int smem_bytes(int d)                     -- per-query staging
 //          void stage(int q, unsigned char* smem)   -- called by the block
-//          float fast_rank(int q, uint32_t pos, const unsigned char* smem)
-//                                                    -- one lane, one row
+//          float fast_rank(int q, int64_t idx, uint32_t pos,
+//                          const unsigned char* smem)  -- one lane, one row
+//                                                       (idx: list order)
 //          float exact_score(int q, uint32_t pos, const unsigned char* smem)
 //                                                    -- the whole warp
 //          int metric                               (ranking order)
@@ -76,7 +77,7 @@ __global__ void __launch_bounds__(kIvfWarps * 32, 1) ivf_list_scan_kernel(
           if (lane == r) rank = rank_from_score(pol.metric, sc);
         }
       } else if (valid) {
-        rank = pol.fast_rank(q, pos, qsmem);
+        rank = pol.fast_rank(q, idx, pos, qsmem);
       }
       const uint64_t shared_thr = *(volatile unsigned long long*)&s_thr;
       const uint64_t thr = shared_thr < wthr ? shared_thr : wthr;

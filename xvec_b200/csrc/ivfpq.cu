@@ -638,6 +638,25 @@ __global__ void gather_list_major_kernel(const uint32_t* __restrict__ list_rows,
   }
 }
 
+// IVF-SQ8's list-major codes, one thread per (list entry, 16-byte chunk):
+// chunk c of entry i goes to ((i / 32) C + c) 32 + i mod 32 (C = d / 16), so a
+// warp reading chunk c of 32 consecutive entries reads 512 contiguous bytes;
+// the entry's float4 rank terms follow in list order.
+__global__ void gather_sq8_list_kernel(const uint32_t* __restrict__ list_rows, int64_t n, int d,
+                                       const uint4* __restrict__ codes,
+                                       const float4* __restrict__ fast,
+                                       uint4* __restrict__ list_codes,
+                                       float4* __restrict__ list_fast) {
+  const int C = d / 16;
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= n * C) return;
+  const int64_t i = t / C;
+  const int c = (int)(t - i * C);
+  const uint32_t pos = list_rows[i];
+  list_codes[((i >> 5) * C + c) * 32 + (i & 31)] = codes[(int64_t)pos * C + c];
+  if (c == 0) list_fast[i] = fast[pos];
+}
+
 // The fast scan's code layout (list_codes_t), one CTA per list: code i of
 // the list holds at byte t its chunk (i mod 32 + t) mod slots (zero past
 // `chunks`).
@@ -703,6 +722,19 @@ xvec_gpu_status rebuild_lists(xvec_gpu_index* idx, cudaStream_t s) {
     rotate_list_codes_kernel<<<nlist, 256, 0, s>>>(idx->list_offsets.as<int64_t>(), chunks, slots,
                                                    idx->list_codes.as<uint8_t>(),
                                                    idx->list_codes_t.as<uint8_t>());
+    XVEC_LAUNCHED();
+    XVEC_CUDA(cudaGetLastError());
+  }
+  if (idx->desc.kind == XVEC_INDEX_IVF_SQ8 && idx->desc.dimension % 16 == 0) {
+    const int d = idx->desc.dimension;
+    const int64_t padded = (n + 31) / 32 * 32;
+    if ((st = idx->list_sq_codes.reserve((size_t)padded * d, 0, s)) ||
+        (st = idx->list_sq_fast.reserve((size_t)padded * 16, 0, s)))
+      return st;
+    gather_sq8_list_kernel<<<blocks_of(n * (d / 16)), 256, 0, s>>>(
+        idx->list_rows.as<uint32_t>(), n, d, idx->sq_codes.as<uint4>(),
+        idx->sq_fast.as<float4>(), idx->list_sq_codes.as<uint4>(),
+        idx->list_sq_fast.as<float4>());
     XVEC_LAUNCHED();
     XVEC_CUDA(cudaGetLastError());
   }

@@ -289,6 +289,8 @@ struct Sq8IvfPolicy {
   const int8_t* codes;
   const SQParams* params;
   const float4* row_fast;
+  const int4* list_codes;    // list-major interleaved codes (d % 16 == 0), or null
+  const float4* list_fast;   // rank terms in list order (with list_codes)
   const int8_t* qcodes;
   const SQParams* qparams;
   const float4* q_info;
@@ -298,9 +300,24 @@ struct Sq8IvfPolicy {
     int8_t* sq = reinterpret_cast<int8_t*>(smem);
     for (int i = threadIdx.x; i < d; i += blockDim.x) sq[i] = qcodes[(int64_t)q * d + i];
   }
-  __device__ float fast_rank(int q, uint32_t pos, const unsigned char* smem) const {
+  __device__ float fast_rank(int q, int64_t idx, uint32_t pos, const unsigned char* smem) const {
     const int8_t* a = codes + (int64_t)pos * d;
     int dot = 0;
+    if (list_codes) {
+      // Chunk c of list entry idx: coalesced across the warp's 32 entries.
+      const int C = d / 16;
+      const int4* src = list_codes + (idx >> 5) * C * 32 + (idx & 31);
+      const int4* b16 = reinterpret_cast<const int4*>(smem);
+      for (int c = 0; c < C; ++c) {
+        const int4 x = __ldg(src + c * 32), y = b16[c];
+        dot = __dp4a(x.x, y.x, dot);
+        dot = __dp4a(x.y, y.y, dot);
+        dot = __dp4a(x.z, y.z, dot);
+        dot = __dp4a(x.w, y.w, dot);
+      }
+      const SQ8Ranker rk{metric, row_fast, q_info};
+      return rk.rank((float)dot, __ldg(list_fast + idx), q_info[q]);
+    }
     if ((d & 15) == 0) {
       // 16-byte loads: the lane's code row in d/16 requests.
       const int4* a16 = reinterpret_cast<const int4*>(a);
@@ -695,6 +712,8 @@ xvec_gpu_status ivf_sq8_search_impl(xvec_gpu_index* idx, const float* d_q, int n
                            idx->sq_codes.as<int8_t>(),
                            idx->sq_params.as<SQParams>(),
                            idx->sq_fast.as<float4>(),
+                           idx->list_sq_codes.ptr ? idx->list_sq_codes.as<int4>() : nullptr,
+                           idx->list_sq_codes.ptr ? idx->list_sq_fast.as<float4>() : nullptr,
                            qcodes.as<int8_t>(),
                            qparams.as<SQParams>(),
                            qinfo.as<float4>(),
