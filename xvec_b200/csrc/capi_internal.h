@@ -172,6 +172,11 @@ struct xvec_gpu_index {
   // ((i / 32) (d / 16) + c) 32 + i mod 32; the float4 rank terms in list order.
   xvec::DeviceBuffer list_sq_codes;
   xvec::DeviceBuffer list_sq_fast;
+  // IVF-Flat (d % 4 == 0): the float32 rows in list_rows order, interleaved
+  // the same way by float4 chunks (chunk c of entry i at ((i / 32) (d / 4) +
+  // c) 32 + i mod 32), and their reference-order ||x||^2 in list order.
+  xvec::DeviceBuffer list_rows_f;
+  xvec::DeviceBuffer list_n2;
   bool lists_dirty = true;
 
   // RaBitQ (one-bit).

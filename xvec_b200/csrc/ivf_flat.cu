@@ -124,6 +124,8 @@ struct IvfFlatPolicy {
   int metric;
   const float* rows;
   const float* row_n2;
+  const float4* list_rows;  // list-major interleaved rows (d % 4 == 0), or null
+  const float* list_n2;     // ||x||^2 in list order (with list_rows)
   const float* qf;
   const float* q_n2;
   int d;
@@ -133,10 +135,26 @@ struct IvfFlatPolicy {
     const float* qv = qf + (int64_t)q * d;
     for (int i = threadIdx.x; i < d; i += blockDim.x) sq[i] = qv[i];
   }
-  __device__ float fast_rank(int q, int64_t, uint32_t pos, const unsigned char* smem) const {
+  __device__ float fast_rank(int q, int64_t idx, uint32_t pos, const unsigned char* smem) const {
     const float* x = rows + (int64_t)pos * d;
     const float* sq = reinterpret_cast<const float*>(smem);
     float dot = 0.f;
+    if (list_rows) {
+      // Chunk c of list entry idx: coalesced across the warp's 32 entries.
+      const int C = d / 4;
+      const float4* src = list_rows + (idx >> 5) * C * 32 + (idx & 31);
+      const float4* q4 = reinterpret_cast<const float4*>(sq);
+      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+      for (int c = 0; c < C; ++c) {
+        const float4 xv = __ldg(src + c * 32), qq = q4[c];
+        a0 = fmaf(xv.x, qq.x, a0);
+        a1 = fmaf(xv.y, qq.y, a1);
+        a2 = fmaf(xv.z, qq.z, a2);
+        a3 = fmaf(xv.w, qq.w, a3);
+      }
+      dot = (a0 + a1) + (a2 + a3);
+      return ::xvec::fast_rank(metric, dot, __ldg(list_n2 + idx), q_n2[q]);
+    }
     if ((d & 3) == 0) {
       const float4* x4 = reinterpret_cast<const float4*>(x);
       const float4* q4 = reinterpret_cast<const float4*>(sq);
@@ -298,8 +316,15 @@ xvec_gpu_status ivf_flat_search_impl(xvec_gpu_index* idx, const float* d_q, int 
     const IvfFlatScorer sc{metric,           idx->rows.as<float>(), idx->row_n2.as<float>(),
                            qf.as<float>(),   qn2.as<float>(),       idx->max_n2.as<unsigned>(),
                            d};
-    const IvfFlatPolicy pol{metric,         idx->rows.as<float>(), idx->row_n2.as<float>(),
-                            qf.as<float>(), qn2.as<float>(),       d};
+    const bool lm = idx->list_rows_f.ptr != nullptr;
+    const IvfFlatPolicy pol{metric,
+                            idx->rows.as<float>(),
+                            idx->row_n2.as<float>(),
+                            lm ? idx->list_rows_f.as<float4>() : nullptr,
+                            lm ? idx->list_n2.as<float>() : nullptr,
+                            qf.as<float>(),
+                            qn2.as<float>(),
+                            d};
     auto scan = [&](bool exact, const int* ids, int count) -> xvec_gpu_status {
       cudaError_t e =
           exact ? launch_ivf_list_scan<true>(pol, d, pkeys.as<uint64_t>(), pcounts.as<int>(),

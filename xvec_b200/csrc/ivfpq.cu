@@ -657,6 +657,23 @@ __global__ void gather_sq8_list_kernel(const uint32_t* __restrict__ list_rows, i
   if (c == 0) list_fast[i] = fast[pos];
 }
 
+// IVF-Flat's list-major rows, one thread per (list entry, float4 chunk), in
+// the same interleaved order; the entry's ||x||^2 follows in list order.
+__global__ void gather_flat_list_kernel(const uint32_t* __restrict__ list_rows, int64_t n, int d,
+                                        const float4* __restrict__ rows,
+                                        const float* __restrict__ row_n2,
+                                        float4* __restrict__ list_rows_f,
+                                        float* __restrict__ list_n2) {
+  const int C = d / 4;
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= n * C) return;
+  const int64_t i = t / C;
+  const int c = (int)(t - i * C);
+  const uint32_t pos = list_rows[i];
+  list_rows_f[((i >> 5) * C + c) * 32 + (i & 31)] = rows[(int64_t)pos * C + c];
+  if (c == 0) list_n2[i] = row_n2[pos];
+}
+
 // The fast scan's code layout (list_codes_t), one CTA per list: code i of
 // the list holds at byte t its chunk (i mod 32 + t) mod slots (zero past
 // `chunks`).
@@ -735,6 +752,18 @@ xvec_gpu_status rebuild_lists(xvec_gpu_index* idx, cudaStream_t s) {
         idx->list_rows.as<uint32_t>(), n, d, idx->sq_codes.as<uint4>(),
         idx->sq_fast.as<float4>(), idx->list_sq_codes.as<uint4>(),
         idx->list_sq_fast.as<float4>());
+    XVEC_LAUNCHED();
+    XVEC_CUDA(cudaGetLastError());
+  }
+  if (idx->desc.kind == XVEC_INDEX_IVF_FLAT && idx->desc.dimension % 4 == 0) {
+    const int d = idx->desc.dimension;
+    const int64_t padded = (n + 31) / 32 * 32;
+    if ((st = idx->list_rows_f.reserve((size_t)padded * d * 4, 0, s)) ||
+        (st = idx->list_n2.reserve((size_t)padded * 4, 0, s)))
+      return st;
+    gather_flat_list_kernel<<<blocks_of(n * (d / 4)), 256, 0, s>>>(
+        idx->list_rows.as<uint32_t>(), n, d, idx->rows.as<float4>(), idx->row_n2.as<float>(),
+        idx->list_rows_f.as<float4>(), idx->list_n2.as<float>());
     XVEC_LAUNCHED();
     XVEC_CUDA(cudaGetLastError());
   }
