@@ -668,6 +668,10 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
       }
     };
     prefetch(0);
+    // The shared threshold is read one tile ahead: a stale value is still a
+    // valid bound (it only decreases), and the read's latency overlaps the
+    // tile instead of stalling before it.
+    uint64_t g_next = qvalid ? (uint64_t)*(volatile unsigned long long*)&gthr[qi] : kEmptyKey;
     for (int t = 0; t < num_tiles; ++t) {
       const int acc = t & 1;
       const uint32_t acc_phase = (t >> 1) & 1;
@@ -682,14 +686,12 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
       }
       __syncwarp();
       prefetch(t + 1);
-      if (qvalid) {
-        const uint64_t g = *(volatile unsigned long long*)&gthr[qi];
-        if (g < thr) {
-          thr = g;
-          thr_f = rank_of(thr);
-          tq = score_bound<METRIC>(thr_f, qa, qn2);
-        }
+      if (g_next < thr) {
+        thr = g_next;
+        thr_f = rank_of(thr);
+        tq = score_bound<METRIC>(thr_f, qa, qn2);
       }
+      if (qvalid) g_next = (uint64_t)*(volatile unsigned long long*)&gthr[qi];
       // Warp-uniform outcome: the tcgen05.ld below needs every lane.
       if (!__all_sync(kFullMask, mbar_wait(&tfull[acc], acc_phase, s_abort))) {
         atomicExch(status, 4);
