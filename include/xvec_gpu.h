@@ -174,6 +174,16 @@ xvec_gpu_status xvec_gpu_ivfpq_set_model(xvec_gpu_index* index, const float* cen
 xvec_gpu_status xvec_gpu_rabitq_set_model(xvec_gpu_index* index, const float* centroids,
                                           int32_t nclusters, const uint8_t* rotation_signs);
 
+/* RaBitQ model with RaBitQModelState.TotalBits in [1, 9] and ExtraScale
+ * (RestoreRaBitQModel, rabitq.go:189-241: zero for one bit, finite and
+ * positive otherwise).  TotalBits > 1: rows get their extra-bit codes and full
+ * factors (quantizeRaBitQVector, rabitq_quantize.go:99-200) and searches rank
+ * by Estimate (rabitq.go:434-446) on the full codes before the refine stage;
+ * TotalBits = 1 is xvec_gpu_rabitq_set_model. */
+xvec_gpu_status xvec_gpu_rabitq_set_model_bits(xvec_gpu_index* index, const float* centroids,
+                                               int32_t nclusters, const uint8_t* rotation_signs,
+                                               int32_t total_bits, double extra_scale);
+
 /* Batched search: queries [nq*dimension] (float32, or uint16 for FP16 storage).
  * out_keys / out_scores: nq*top_k (slots past out_counts[q] are unspecified).
  * Replaces DenseQuerySearcher.SearchWithOptions (query.go:58-61) per query,

@@ -151,6 +151,18 @@ class Oracle:
                                            _u8p, _u8p, ctypes.POINTER(RaBitQFactors)]
         lib.xo_rabitq_encode1.argtypes = [ctypes.c_int, ctypes.c_int32, _f32p, ctypes.c_int32,
                                           _u8p, _f32p, _u8p, ctypes.POINTER(RaBitQFactors)]
+        lib.xo_rabitq_encode.argtypes = [ctypes.c_int, ctypes.c_int32, _f32p, ctypes.c_int32,
+                                         _u8p, ctypes.c_int32, ctypes.c_double, _f32p, _u8p,
+                                         _u8p, ctypes.POINTER(RaBitQFactors)]
+        lib.xo_rabitq_estimate.argtypes = [_f32p, ctypes.c_int32, ctypes.c_double, _f64p, _f64p,
+                                           ctypes.c_int32, _u8p, _u8p,
+                                           ctypes.POINTER(RaBitQFactors), _f32p]
+        lib.xo_rabitq_search_bits.argtypes = [ctypes.c_int, ctypes.c_int32, _f32p,
+                                              ctypes.c_int32, _u8p, ctypes.c_int32, _u8p, _u8p,
+                                              ctypes.c_void_p, _f32p, _u64p, ctypes.c_int64,
+                                              _f32p, ctypes.c_int32, ctypes.c_int32,
+                                              ctypes.c_int32, ctypes.c_int32, ctypes.c_float,
+                                              _u32p, ctypes.c_int32, _u64p, _f32p, _i32p, _i32p]
         lib.xo_rabitq_prepare_query.argtypes = [ctypes.c_int, ctypes.c_int32, _f32p,
                                                 ctypes.c_int32, _u8p, _f32p, _f32p, _f64p, _f64p,
                                                 _f64p]
@@ -485,6 +497,50 @@ class Oracle:
                           f.full_add, f.full_rescale)
         return codes, factors
 
+    def rabitq_extra_bytes(self, d, total_bits):
+        padded = self.rabitq_padded_dimension(d)
+        return (padded * (total_bits - 1) + 7) // 8
+
+    def rabitq_encode_batch(self, metric, centroids, signs, rows, total_bits, extra_scale):
+        """RaBitQModel.Encode of every row with TotalBits / ExtraScale: (sign
+        bits [n][padded/8], extra codes [n][extra bytes], factors)."""
+        centroids = _c(centroids, np.float32)
+        signs = _c(signs, np.uint8)
+        rows = _c(rows, np.float32)
+        n, d = rows.shape
+        padded = self.rabitq_padded_dimension(d)
+        xb = max(1, self.rabitq_extra_bytes(d, total_bits))
+        codes = np.zeros((n, padded // 8), np.uint8)
+        extra = np.zeros((n, xb), np.uint8)
+        factors = np.zeros(n, RABITQ_FACTORS_DTYPE)
+        for i in range(n):
+            f = RaBitQFactors()
+            st = self.lib.xo_rabitq_encode(metric, d, _ptr(centroids, _f32p), centroids.shape[0],
+                                           _ptr(signs, _u8p), total_bits, extra_scale,
+                                           _ptr(rows[i], _f32p), _ptr(codes[i], _u8p),
+                                           _ptr(extra[i], _u8p), ctypes.byref(f))
+            if st != OK:
+                raise ValueError(f"encode row {i}: status {st}")
+            factors[i] = (f.cluster, 0, f.coarse_add, f.coarse_rescale, f.coarse_error,
+                          f.full_add, f.full_rescale)
+        return codes, extra[:, :self.rabitq_extra_bytes(d, total_bits)].copy(), factors
+
+    def rabitq_estimate(self, rotated, qsum, gadd, gerr, total_bits, code, extra, factors_row):
+        rotated = _c(rotated, np.float32)
+        gadd = _c(gadd, np.float64)
+        gerr = None if gerr is None else _c(gerr, np.float64)
+        code = _c(code, np.uint8)
+        extra = None if extra is None else _c(extra, np.uint8)
+        f = RaBitQFactors(int(factors_row["cluster"]), 0, float(factors_row["coarse_add"]),
+                          float(factors_row["coarse_rescale"]), float(factors_row["coarse_error"]),
+                          float(factors_row["full_add"]), float(factors_row["full_rescale"]))
+        out = np.zeros(1, np.float32)
+        st = self.lib.xo_rabitq_estimate(_ptr(rotated, _f32p), rotated.size, qsum,
+                                         _ptr(gadd, _f64p), _ptr(gerr, _f64p), total_bits,
+                                         _ptr(code, _u8p), _ptr(extra, _u8p), ctypes.byref(f),
+                                         _ptr(out, _f32p))
+        return st, np.float32(out[0])
+
     def rabitq_prepare_query(self, metric, centroids, signs, query):
         centroids = _c(centroids, np.float32)
         signs = _c(signs, np.uint8)
@@ -517,8 +573,13 @@ class Oracle:
         return st, np.float32(out[0])
 
     def rabitq_search(self, metric, centroids, signs, codes, factors, originals, keys, queries,
-                      k, candidate_count, radius=0.0, bitmap=None, threads=0, refine=True):
+                      k, candidate_count, radius=0.0, bitmap=None, threads=0, refine=True,
+                      total_bits=1, extra=None):
         """Linear RaBitQ search; candidate_count plays HNSWRaBitQSearchOptions.EF."""
+        if total_bits > 1:
+            return self._rabitq_search_bits(metric, centroids, signs, codes, extra, factors,
+                                            originals, keys, queries, k, candidate_count,
+                                            radius, bitmap, threads, refine, total_bits)
         centroids = _c(centroids, np.float32)
         signs = _c(signs, np.uint8)
         codes = _c(codes, np.uint8)
@@ -538,6 +599,33 @@ class Oracle:
                                        _ptr(bm, _u32p), threads or os.cpu_count(),
                                        _ptr(ok, _u64p), _ptr(os_, _f32p), _ptr(oc, _i32p),
                                        _ptr(ost, _i32p))
+        return st, ok.reshape(nq, k), os_.reshape(nq, k), oc, ost
+
+
+    def _rabitq_search_bits(self, metric, centroids, signs, codes, extra, factors, originals,
+                            keys, queries, k, candidate_count, radius, bitmap, threads, refine,
+                            total_bits):
+        centroids = _c(centroids, np.float32)
+        signs = _c(signs, np.uint8)
+        codes = _c(codes, np.uint8)
+        extra = _c(extra, np.uint8)
+        factors = np.ascontiguousarray(factors, RABITQ_FACTORS_DTYPE)
+        originals = _c(originals, np.float32)
+        keys = _c(keys, np.uint64)
+        queries = _c(queries, np.float32)
+        n, d = originals.shape
+        assert extra.shape == (n, self.rabitq_extra_bytes(d, total_bits))
+        nq = queries.shape[0]
+        ok, os_, oc, ost = self._outs(nq, k)
+        bm = None if bitmap is None else _c(bitmap, np.uint32)
+        st = self.lib.xo_rabitq_search_bits(metric, d, _ptr(centroids, _f32p), centroids.shape[0],
+                                            _ptr(signs, _u8p), total_bits, _ptr(codes, _u8p),
+                                            _ptr(extra, _u8p), factors.ctypes.data,
+                                            _ptr(originals, _f32p), _ptr(keys, _u64p), n,
+                                            _ptr(queries, _f32p), nq, k, candidate_count,
+                                            1 if refine else 0, radius, _ptr(bm, _u32p),
+                                            threads or os.cpu_count(), _ptr(ok, _u64p),
+                                            _ptr(os_, _f32p), _ptr(oc, _i32p), _ptr(ost, _i32p))
         return st, ok.reshape(nq, k), os_.reshape(nq, k), oc, ost
 
 

@@ -1497,12 +1497,14 @@ std::vector<float> prepare_vector(const float* v, int32_t d, int metric) {
 }
 }  // namespace
 
-// RaBitQModel.Encode (rabitq.go:297-327) with TotalBits = 1: nearest
-// centroid under L2 (IP for IP/cosine), rotate, quantize against the rotated
-// centroid (RestoreRaBitQModel rotates centroids, rabitq.go:224-230).
-extern "C" int xo_rabitq_encode1(int metric, int32_t d, const float* centroids, int32_t nc,
-                                 const uint8_t* signs, const float* v, uint8_t* binary_code,
-                                 xo_rabitq_factors* f) {
+// RaBitQModel.Encode (rabitq.go:297-327): nearest centroid under L2 (IP for
+// IP/cosine), rotate, quantize against the rotated centroid with the model's
+// TotalBits and ExtraScale (RestoreRaBitQModel rotates centroids,
+// rabitq.go:224-230).  extra_code: (padded (total_bits - 1) + 7) / 8 bytes.
+extern "C" int xo_rabitq_encode(int metric, int32_t d, const float* centroids, int32_t nc,
+                                const uint8_t* signs, int32_t total_bits, double extra_scale,
+                                const float* v, uint8_t* binary_code, uint8_t* extra_code,
+                                xo_rabitq_factors* f) {
   for (int32_t i = 0; i < d; ++i)
     if (!finite32(v[i])) return XO_NON_FINITE;
   std::vector<float> prepared = prepare_vector(v, d, metric);
@@ -1517,8 +1519,15 @@ extern "C" int xo_rabitq_encode1(int metric, int32_t d, const float* centroids, 
   if (st != XO_OK) return st;
   st = xo_rabitq_rotate(d, signs, centroids + (int64_t)cluster * d, rcen.data());
   if (st != XO_OK) return st;
-  return xo_rabitq_quantize(rot.data(), rcen.data(), padded, cluster, 1, 0, metric != XO_L2,
-                            binary_code, nullptr, f);
+  return xo_rabitq_quantize(rot.data(), rcen.data(), padded, cluster, total_bits, extra_scale,
+                            metric != XO_L2, binary_code, extra_code, f);
+}
+
+// The TotalBits = 1 encoding.
+extern "C" int xo_rabitq_encode1(int metric, int32_t d, const float* centroids, int32_t nc,
+                                 const uint8_t* signs, const float* v, uint8_t* binary_code,
+                                 xo_rabitq_factors* f) {
+  return xo_rabitq_encode(metric, d, centroids, nc, signs, 1, 0, v, binary_code, nullptr, f);
 }
 
 // PrepareQuery (rabitq.go:372-408).
@@ -1572,6 +1581,40 @@ extern "C" int xo_rabitq_estimate_coarse(const float* rotated, int32_t padded, d
   return XO_OK;
 }
 
+// Estimate (rabitq.go:434-446): EstimateCoarse for one bit, else the full
+// code dot raBitQFullCodeDot (rabitq_quantize.go:312-323: value = extra |
+// sign bit << extra bits, float64 products summed in index order) with
+// center -(2^extra - 1/2), and the coarse error over 2^extra.
+extern "C" int xo_rabitq_estimate(const float* rotated, int32_t padded, double sum,
+                                  const double* g_add, const double* g_error, int32_t total_bits,
+                                  const uint8_t* bits, const uint8_t* extra,
+                                  const xo_rabitq_factors* f, float* distance) {
+  if (total_bits <= 1)
+    return xo_rabitq_estimate_coarse(rotated, padded, sum, g_add, g_error, bits, f, distance);
+  const int eb = total_bits - 1;
+  double dot = 0;
+  for (int32_t i = 0; i < padded; ++i) {
+    uint32_t q = 0;
+    for (int b = 0; b < eb; ++b) {
+      const size_t p = (size_t)i * eb + b;
+      if (extra[p / 8] & (1u << (p % 8))) q |= 1u << b;
+    }
+    if (bits[i / 8] & (1u << (i % 8))) q |= 1u << eb;
+    dot += (double)q * (double)rotated[i];
+  }
+  const double center = -((double)(1ull << eb) - .5);
+  double dist = f->full_add + g_add[f->cluster] + f->full_rescale * (dot + center * sum);
+  double eb_err = g_error ? f->coarse_error * g_error[f->cluster] / (double)(1ull << eb) : 0.0;
+  const double maxf = 3.40282346638528859811704183484516925440e+38;
+  if (std::isnan(dist) || std::isinf(dist) || std::isnan(eb_err) || std::isinf(eb_err) ||
+      eb_err < 0)
+    return XO_INVALID_ARGUMENT;
+  if (std::fabs(dist) > maxf || eb_err > maxf) return XO_OVERFLOW;
+  if (dist - eb_err < -maxf || dist + eb_err > maxf) return XO_OVERFLOW;
+  *distance = (float)dist;
+  return XO_OK;
+}
+
 // Composed RaBitQ linear search (hnsw_rabitq.go:539-586) over every code
 // (scanRaBitQCodes, :615-642: first failing estimate fails the query, then
 // acceptRaBitQNode :753-757, filter and radius on the public score, and a
@@ -1580,17 +1623,23 @@ extern "C" int xo_rabitq_estimate_coarse(const float* rotated, int32_t padded, d
 //     radius (:579-584) and refinePrepared (:780-801) returns the exact fp32
 //     top-k of those (metric.Compute on the originals, query validated first).
 //   refine == 0: the k best estimates with publicRaBitQScore (:746-751).
-extern "C" int xo_rabitq_search(int metric, int32_t d, const float* centroids, int32_t nc,
-                                const uint8_t* signs, const uint8_t* binary_codes,
-                                const xo_rabitq_factors* factors, const float* originals,
-                                const uint64_t* keys, int64_t n, const float* queries, int32_t nq,
-                                int32_t k, int32_t candidate_count, int32_t refine, float radius,
-                                const uint32_t* bitmap, int32_t threads, uint64_t* out_keys,
-                                float* out_scores, int32_t* out_counts, int32_t* out_status) {
+// total_bits > 1: Estimate on the full codes (extra_codes: per row
+// (padded (total_bits - 1) + 7) / 8 bytes).
+extern "C" int xo_rabitq_search_bits(int metric, int32_t d, const float* centroids, int32_t nc,
+                                     const uint8_t* signs, int32_t total_bits,
+                                     const uint8_t* binary_codes, const uint8_t* extra_codes,
+                                     const xo_rabitq_factors* factors, const float* originals,
+                                     const uint64_t* keys, int64_t n, const float* queries,
+                                     int32_t nq, int32_t k, int32_t candidate_count,
+                                     int32_t refine, float radius, const uint32_t* bitmap,
+                                     int32_t threads, uint64_t* out_keys, float* out_scores,
+                                     int32_t* out_counts, int32_t* out_status) {
   int st0 = validate_options(k, radius);
   if (st0 != XO_OK) return st0;
+  if (total_bits < 1 || total_bits > 9) return XO_INVALID_ARGUMENT;
   int32_t padded = xo_rabitq_padded_dimension(d);
   int32_t bytes = padded / 8;
+  const int64_t xbytes = ((int64_t)padded * (total_bits - 1) + 7) / 8;
   std::vector<int32_t> status(nq, XO_OK);
   auto public_score = [&](float dist) { return metric == XO_IP ? 1.0f - dist : dist; };
   parallel_for(nq, threads, [&](int64_t q) {
@@ -1607,8 +1656,10 @@ extern "C" int xo_rabitq_search(int metric, int32_t d, const float* centroids, i
       WorstFirstHeap heap{XO_L2, {}};
       for (int64_t p = 0; p < n && st == XO_OK; ++p) {
         float est;
-        st = xo_rabitq_estimate_coarse(rot.data(), padded, sum, gadd.data(), gerr.data(),
-                                       binary_codes + p * bytes, &factors[p], &est);
+        st = xo_rabitq_estimate(rot.data(), padded, sum, gadd.data(), gerr.data(), total_bits,
+                                binary_codes + p * bytes,
+                                total_bits > 1 ? extra_codes + p * xbytes : nullptr, &factors[p],
+                                &est);
         if (st != XO_OK) break;
         if (!filter_pass(bitmap, p)) continue;
         if (!refine && !within_radius(metric, public_score(est), radius)) continue;
@@ -1650,4 +1701,17 @@ extern "C" int xo_rabitq_search(int metric, int32_t d, const float* centroids, i
     if (first == XO_OK) first = status[q];
   }
   return first;
+}
+
+extern "C" int xo_rabitq_search(int metric, int32_t d, const float* centroids, int32_t nc,
+                                const uint8_t* signs, const uint8_t* binary_codes,
+                                const xo_rabitq_factors* factors, const float* originals,
+                                const uint64_t* keys, int64_t n, const float* queries, int32_t nq,
+                                int32_t k, int32_t candidate_count, int32_t refine, float radius,
+                                const uint32_t* bitmap, int32_t threads, uint64_t* out_keys,
+                                float* out_scores, int32_t* out_counts, int32_t* out_status) {
+  return xo_rabitq_search_bits(metric, d, centroids, nc, signs, 1, binary_codes, nullptr, factors,
+                               originals, keys, n, queries, nq, k, candidate_count, refine,
+                               radius, bitmap, threads, out_keys, out_scores, out_counts,
+                               out_status);
 }

@@ -172,6 +172,11 @@ int xo_rabitq_quantize(const float* rotated, const float* rotated_centroid, int3
 int xo_rabitq_encode1(int metric, int32_t d, const float* centroids, int32_t nc,
                       const uint8_t* signs, const float* v, uint8_t* binary_code,
                       xo_rabitq_factors* factors);
+/* RaBitQModel.Encode with TotalBits and ExtraScale; extra_code holds
+ * (padded (total_bits - 1) + 7) / 8 bytes (unused for one bit). */
+int xo_rabitq_encode(int metric, int32_t d, const float* centroids, int32_t nc,
+                     const uint8_t* signs, int32_t total_bits, double extra_scale, const float* v,
+                     uint8_t* binary_code, uint8_t* extra_code, xo_rabitq_factors* factors);
 /* PrepareQuery (rabitq.go:372-408): rotated query (padded), sum, gAdd, gError. */
 int xo_rabitq_prepare_query(int metric, int32_t d, const float* centroids, int32_t nc,
                             const uint8_t* signs, const float* query, float* rotated,
@@ -181,6 +186,22 @@ int xo_rabitq_estimate_coarse(const float* rotated, int32_t padded, double sum,
                               const double* g_add, const double* g_error,
                               const uint8_t* binary_code, const xo_rabitq_factors* factors,
                               float* distance);
+/* Estimate (rabitq.go:434-446): the coarse estimate for one bit, else the
+ * full-code estimate. */
+int xo_rabitq_estimate(const float* rotated, int32_t padded, double sum, const double* g_add,
+                       const double* g_error, int32_t total_bits, const uint8_t* binary_code,
+                       const uint8_t* extra_code, const xo_rabitq_factors* factors,
+                       float* distance);
+/* xo_rabitq_search with TotalBits (extra_codes: per row
+ * (padded (total_bits - 1) + 7) / 8 bytes). */
+int xo_rabitq_search_bits(int metric, int32_t d, const float* centroids, int32_t nc,
+                          const uint8_t* signs, int32_t total_bits, const uint8_t* binary_codes,
+                          const uint8_t* extra_codes, const xo_rabitq_factors* factors,
+                          const float* originals, const uint64_t* keys, int64_t n,
+                          const float* queries, int32_t nq, int32_t k, int32_t candidate_count,
+                          int32_t refine, float radius, const uint32_t* filter_bitmap,
+                          int32_t threads, uint64_t* out_keys, float* out_scores,
+                          int32_t* out_counts, int32_t* out_status);
 /* Composed linear RaBitQ scan (hnsw_rabitq.go:539-642, 739-801): with refine,
  * min(n, max(k, candidate_count)) estimates refined to the exact top-k;
  * without, the k best estimates with the public score. */

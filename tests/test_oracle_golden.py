@@ -291,3 +291,44 @@ def test_ivf_sq8_is_sq8_over_the_probed_lists(oracle, metric):
             assert oc[q] == fc[0]
             assert np.array_equal(ok[q, :oc[q]], fk[0, :fc[0]])
             assert np.array_equal(os_[q, :oc[q]].view(np.uint32), fs[0, :fc[0]].view(np.uint32))
+
+
+@pytest.mark.parametrize("metric", [L2, IP])
+def test_rabitq_full_estimate(oracle, metric):
+    """Estimate (rabitq.go:434-446) on multi-bit codes: the oracle against a
+    direct numpy evaluation of raBitQFullCodeDot and the estimate formula, and
+    the estimate tracking the true distance more closely as TotalBits grows."""
+    rng = np.random.default_rng(11 + metric)
+    d, n = 96, 200
+    cents = rng.standard_normal((4, d)).astype(np.float32)
+    rows = (cents[rng.integers(0, 4, n)] + 0.4 * rng.standard_normal((n, d))).astype(np.float32)
+    q = (cents[1] + 0.4 * rng.standard_normal(d)).astype(np.float32)
+    padded = oracle.rabitq_padded_dimension(d)
+    signs = rng.integers(0, 256, 4 * padded // 8, dtype=np.uint8)
+    st, rot, qsum, gadd, gerr = oracle.rabitq_prepare_query(metric, cents, signs, q)
+    assert st == OK
+    errs = {}
+    for tb, scale in ((1, 0.0), (4, 5.2), (7, 15.75)):
+        codes, extra, fac = oracle.rabitq_encode_batch(metric, cents, signs, rows, tb, scale)
+        eb = tb - 1
+        est = np.zeros(n)
+        for i in range(n):
+            st, e = oracle.rabitq_estimate(rot, qsum, gadd, gerr, tb, codes[i],
+                                           extra[i] if eb else None, fac[i])
+            assert st == OK
+            est[i] = e
+            if eb:
+                bits = np.unpackbits(codes[i], bitorder="little")[:padded]
+                xb = np.unpackbits(extra[i], bitorder="little")
+                vals = [int(sum(int(xb[j * eb + b]) << b for b in range(eb))) | (int(bits[j]) << eb)
+                        for j in range(padded)]
+                dot = 0.0
+                for j in range(padded):
+                    dot += float(vals[j]) * float(rot[j])
+                center = -((1 << eb) - 0.5)
+                c = int(fac[i]["cluster"])
+                want = fac[i]["full_add"] + gadd[c] + fac[i]["full_rescale"] * (dot + center * qsum)
+                assert e == np.float32(want), (tb, i)
+        truth = ((rows - q) ** 2).sum(1) if metric == L2 else 1.0 - rows @ q
+        errs[tb] = np.abs(est - truth).mean()
+    assert errs[7] < errs[4] < errs[1], errs

@@ -54,7 +54,7 @@ EXPORTED_SYMBOLS = (
     "xvec_gpu_index_search_noalloc", "xvec_gpu_index_reserve",
     "xvec_gpu_index_candidate_count", "xvec_gpu_index_candidates_device",
     "xvec_gpu_index_refine_device", "xvec_gpu_kmeans_train", "xvec_gpu_kmeans_train_device",
-    "xvec_gpu_ivf_set_model",
+    "xvec_gpu_ivf_set_model", "xvec_gpu_rabitq_set_model_bits",
 )
 
 
@@ -103,6 +103,7 @@ def _load() -> ctypes.CDLL:
     lib.xvec_gpu_index_add_device.argtypes = [vp, vp, vp, i64, vp]
     lib.xvec_gpu_ivfpq_set_model.argtypes = [vp, vp, i32, vp, i32]
     lib.xvec_gpu_rabitq_set_model.argtypes = [vp, vp, i32, vp]
+    lib.xvec_gpu_rabitq_set_model_bits.argtypes = [vp, vp, i32, vp, i32, ctypes.c_double]
     lib.xvec_gpu_ivf_set_model.argtypes = [vp, vp, i32]
     lib.xvec_gpu_index_search.argtypes = [vp, vp, i32, ctypes.POINTER(SearchOpts), vp, vp, vp]
     lib.xvec_gpu_index_search_device.argtypes = [vp, vp, i32, ctypes.POINTER(SearchOpts), vp,
@@ -385,14 +386,22 @@ class ScalarQuantizedIVFIndex(IVFIndex):
 
 
 class RaBitQIndex(_Index):
-    """One-bit RaBitQ linear scan with exact refinement (hnsw_rabitq.go:539-642, 780-801)."""
+    """RaBitQ linear scan with exact refinement (hnsw_rabitq.go:539-642, 780-801)
+    over codes of RaBitQModelState.TotalBits bits (one bit: EstimateCoarse;
+    more: Estimate on the full codes, rabitq.go:421-446)."""
     kind = INDEX_RABITQ
 
-    def set_model(self, centroids, rotation_signs) -> None:
+    def set_model(self, centroids, rotation_signs, total_bits: int = 1,
+                  extra_scale: float = 0.0) -> None:
         centroids = np.ascontiguousarray(centroids, np.float32)
         signs = np.ascontiguousarray(rotation_signs, np.uint8)
-        _check(_lib.xvec_gpu_rabitq_set_model(self._h, _ptr(centroids), centroids.shape[0],
-                                              _ptr(signs)))
+        if total_bits == 1 and extra_scale == 0.0:
+            _check(_lib.xvec_gpu_rabitq_set_model(self._h, _ptr(centroids), centroids.shape[0],
+                                                  _ptr(signs)))
+        else:
+            _check(_lib.xvec_gpu_rabitq_set_model_bits(self._h, _ptr(centroids),
+                                                       centroids.shape[0], _ptr(signs),
+                                                       total_bits, float(extra_scale)))
 
 
 def kmeans_assign(metric: int, vectors, centroids, device: int = 0):

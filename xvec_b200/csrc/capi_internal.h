@@ -185,8 +185,17 @@ struct xvec_gpu_index {
   xvec::DeviceBuffer rq_rot_centroids;      // float [c][padded]
   xvec::DeviceBuffer rq_signs;              // uint8 [4*padded/8]
   xvec::DeviceBuffer rq_codes;              // uint8 [n][padded/8]
-  xvec::DeviceBuffer rq_factors;            // {double add, rescale, error; int cluster} [n]
+  xvec::DeviceBuffer rq_factors;            // {double add, rescale, error, full add,
+                                            //  full rescale; int cluster} [n]
   xvec::DeviceBuffer rq_fast;               // float4 {add, rescale, cluster bits, 0} [n]
+                                            // (multi-bit: the full add and rescale)
+  // Multi-bit models (RaBitQModelState.TotalBits > 1, ExtraScale): the full
+  // code values v = extra | sign bit << (TotalBits - 1) per padded coordinate
+  // as 16-bit floats [n][padded] (bfloat16 up to 8 bits, binary16 for 9;
+  // exact either way): the tensor-core operand and the exact scorer's input.
+  int32_t rq_total_bits = 1;
+  double rq_extra_scale = 0.0;
+  xvec::DeviceBuffer rq_values;
   // Flat FP32: the rows as bfloat16 high and low parts (the tensor-core
   // scan's operands; the float32 rows stay the reference data).
   xvec::DeviceBuffer rows_bhi;              // bf16 [n][d]

@@ -63,6 +63,10 @@ constexpr uint32_t kTileABytes = kBM * kBK * 2;  // 16 KB
 constexpr int kModeSq8 = 16;
 constexpr int kModeRaBitQ = 32;
 constexpr int kModeSplit = 64;
+// kModeRaBitQFull: multi-bit RaBitQ, the rows' full code values (bfloat16,
+// exact up to 256) against the query's bfloat16 high and low parts, two MMAs
+// per k-step into one fp32 accumulator; the RaBitQ epilogue on the float dot.
+constexpr int kModeRaBitQFull = 128;
 constexpr int kRaBitQMaxClusters = 16;
 // Per epilogue warp: radix histogram (1 KB) + the current tile's row
 // metadata for its 128 columns (aux floats + key ranks, 1 KB; SQ8/RaBitQ: the
@@ -73,12 +77,14 @@ constexpr uint32_t epi_smem_bytes(bool rq) {
 }
 constexpr uint32_t kSmemBudget = 232448 - 1024 - 1024 - 512;  // dynamic bytes for stages
 
-template <bool PAIR, bool RQ = false, bool SPLIT = false>
+template <bool PAIR, bool RQ = false, bool SPLIT = false, bool SPLITA = false>
 struct Shape {
   static constexpr int kRowsPerCta = PAIR ? kBN / 2 : kBN;       // B rows loaded per CTA
   static constexpr uint32_t kTileBBytes = kRowsPerCta * kBK * 2;  // 16 or 32 KB
   static constexpr int kParts = SPLIT ? 2 : 1;                    // high (+ low) tiles
-  static constexpr uint32_t kStageBytes = kParts * (kTileABytes + kTileBBytes);
+  // SPLITA: A high, B, A low.
+  static constexpr uint32_t kStageBytes =
+      SPLITA ? 2 * kTileABytes + kTileBBytes : kParts * (kTileABytes + kTileBBytes);
   static constexpr uint32_t kEpiBytes = epi_smem_bytes(RQ);
   static constexpr int kFit = (int)((kSmemBudget - kEpiBytes) / kStageBytes);
   static constexpr int kStages = kFit < 6 ? kFit : 6;
@@ -413,13 +419,15 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
     int64_t rows_per_part, int kp, int list_base, int num_lists, uint64_t* __restrict__ cand,
     int* __restrict__ part_counts, uint64_t* __restrict__ part_sat, int* __restrict__ q_flags,
     int* __restrict__ status) {
-  constexpr bool RQ = MODE == kModeRaBitQ;   // RaBitQ code planes, integer queries
+  constexpr bool RQ1 = MODE == kModeRaBitQ;   // RaBitQ code planes, integer queries
+  constexpr bool RQF = MODE == kModeRaBitQFull;  // multi-bit values, bfloat16 query parts
+  constexpr bool RQ = RQ1 || RQF;                // the RaBitQ epilogue
   constexpr bool SQ = (MODE & kModeSq8) != 0;   // INT8 codes (SQ8) instead of FP16 rows
   constexpr bool SPLIT = (MODE & kModeSplit) != 0;  // bfloat16 high/low parts of float32
-  constexpr bool I8 = SQ || RQ;                 // kind::i8 operands
+  constexpr bool I8 = SQ || RQ1;                // kind::i8 operands
   constexpr int METRIC = MODE & 15;
   constexpr int kElemBytes = I8 ? 1 : 2;
-  using S = Shape<PAIR, RQ, SPLIT>;
+  using S = Shape<PAIR, RQ, SPLIT, RQF>;
   constexpr int kStages = S::kStages;
   constexpr uint32_t kStageBytes = S::kStageBytes;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -517,6 +525,8 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
               tma_load_2d_pair(&qmap2, full0 + stage * 8, a2_dst, ks * kStepElems, qblock * kBM);
               tma_load_2d_pair(&rmap2, full0 + stage * 8, b2_dst, ks * kStepElems, row0);
             }
+            if constexpr (RQF)
+              tma_load_2d_pair(&qmap2, full0 + stage * 8, a2_dst, ks * kStepElems, qblock * kBM);
           } else {
             tma_load_2d(&qmap, &full[stage], a_dst, ks * kStepElems, qblock * kBM);
             tma_load_2d(&rmap, &full[stage], b_dst, ks * kStepElems, row0);
@@ -524,6 +534,8 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
               tma_load_2d(&qmap2, &full[stage], a2_dst, ks * kStepElems, qblock * kBM);
               tma_load_2d(&rmap2, &full[stage], b2_dst, ks * kStepElems, row0);
             }
+            if constexpr (RQF)
+              tma_load_2d(&qmap2, &full[stage], a2_dst, ks * kStepElems, qblock * kBM);
           }
           ++count[stage];
           if (++stage == kStages) {
@@ -570,12 +582,19 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
             if constexpr (I8)
               mma_s8<PAIR>(d_tmem, adesc + (uint64_t)(k * 2), bdesc + (uint64_t)(k * 2),
                            (ks > 0 || k > 0) ? 1u : 0u);
-            else if constexpr (SPLIT)
+            else if constexpr (SPLIT || RQF)
               mma_bf16<PAIR>(d_tmem, adesc + (uint64_t)(k * 2), bdesc + (uint64_t)(k * 2),
                              (ks > 0 || k > 0) ? 1u : 0u);
             else
               mma_f16<PAIR>(d_tmem, adesc + (uint64_t)(k * 2), bdesc + (uint64_t)(k * 2),
                             (ks > 0 || k > 0) ? 1u : 0u);
+          }
+          if constexpr (RQF) {
+            // The low query part against the same row values.
+            const uint64_t a2desc = smem_desc_sw128(a_src + kTileABytes + S::kTileBBytes);
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              mma_bf16<PAIR>(d_tmem, a2desc + (uint64_t)(k * 2), bdesc + (uint64_t)(k * 2), 1u);
           }
           if constexpr (SPLIT) {
             // The high query part against the low row part, and the low
@@ -730,13 +749,15 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
         };
         const float4* a4 = reinterpret_cast<const float4*>(meta_aux + c * 32);
         if constexpr (RQ) {
-          // RaBitQRanker (rabitq.cu): add + gAdd[cluster] + rescale (dot - sum/2).
+          // RaBitQRanker (rabitq.cu): add + gAdd[cluster] + rescale (dot - sum/2);
+          // multi-bit: full add + gAdd[cluster] + full rescale (dot + center sum)
+          // with rq_q.x = -(center sum).
           if (vmask != 0u) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
               const float4 r = meta4[c * 32 + j];
               const float g = gadd_tab[__float_as_int(r.z) * 32 + lane];
-              const float dot = (float)(int)cur[j] * rq_q.y;
+              const float dot = RQF ? __uint_as_float(cur[j]) : (float)(int)cur[j] * rq_q.y;
               const float rank = fmaf(r.y, dot - rq_q.x, r.x + g);
               if (((vmask >> j) & 1u) && !(rank > thr_f)) {
                 if (!isfinite(rank)) {
@@ -932,7 +953,8 @@ cudaError_t launch_tc(int nq, const void* queries, const void* queries2, int nc,
                       uint64_t* part_sat, int* q_flags, int* status, cudaStream_t stream) {
   const int qblocks = (nq + tc::kBM - 1) / tc::kBM;
   const bool pair = flat_tc_pairs(nq);
-  constexpr bool RQ = MODE == tc::kModeRaBitQ;
+  constexpr bool RQF = MODE == tc::kModeRaBitQFull;
+  constexpr bool RQ = MODE == tc::kModeRaBitQ || RQF;
   constexpr bool SPLIT = (MODE & tc::kModeSplit) != 0;
   const int box_rows = pair ? tc::Shape<true>::kRowsPerCta : tc::Shape<false>::kRowsPerCta;
   // The low parts' maps (unused unless SPLIT) repeat the high parts'.
@@ -957,17 +979,17 @@ cudaError_t launch_tc(int nq, const void* queries, const void* queries2, int nc,
   cudaError_t err;
   if (pair) {
     auto kern = tc::flat_scan_tc_kernel<MODE, true>;
-    cfg.dynamicSmemBytes = tc::Shape<true, RQ, SPLIT>::kSmemBytes;
+    cfg.dynamicSmemBytes = tc::Shape<true, RQ, SPLIT, RQF>::kSmemBytes;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)tc::Shape<true, RQ, SPLIT>::kSmemBytes);
+                         (int)tc::Shape<true, RQ, SPLIT, RQF>::kSmemBytes);
     err = cudaLaunchKernelEx(&cfg, kern, qmap, rmap, qmap2, rmap2, nc, nq, n, d, row_aux, keyrank, q_aux,
                              q_n2, gthr, bitmap, rows_per_part, kp, list_base, num_lists, cand,
                              part_counts, part_sat, q_flags, status);
   } else {
     auto kern = tc::flat_scan_tc_kernel<MODE, false>;
-    cfg.dynamicSmemBytes = tc::Shape<false, RQ, SPLIT>::kSmemBytes;
+    cfg.dynamicSmemBytes = tc::Shape<false, RQ, SPLIT, RQF>::kSmemBytes;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)tc::Shape<false, RQ, SPLIT>::kSmemBytes);
+                         (int)tc::Shape<false, RQ, SPLIT, RQF>::kSmemBytes);
     err = cudaLaunchKernelEx(&cfg, kern, qmap, rmap, qmap2, rmap2, nc, nq, n, d, row_aux, keyrank, q_aux,
                              q_n2, gthr, bitmap, rows_per_part, kp, list_base, num_lists, cand,
                              part_counts, part_sat, q_flags, status);
@@ -1075,6 +1097,26 @@ cudaError_t launch_rabitq_scan_tc(const int8_t* q_int, int nq, const int8_t* pla
                                     reinterpret_cast<const float*>(q_terms), q_gadd, gthr, bitmap, num_parts, kp, list_base,
                                     num_lists, cand, part_counts, part_sat, q_flags, status,
                                     stream);
+}
+
+cudaError_t launch_rabitq_full_scan_tc(const __nv_bfloat16* q_hi, const __nv_bfloat16* q_lo,
+                                       int nq, const __nv_bfloat16* values, int64_t n,
+                                       int padded, const float4* row_info,
+                                       const uint32_t* keyrank, const float2* q_terms,
+                                       const float* q_gadd, int nc, unsigned long long* gthr,
+                                       const uint32_t* bitmap, int num_parts, int kp,
+                                       int list_base, int num_lists, uint64_t* cand,
+                                       int* part_counts, uint64_t* part_sat, int* q_flags,
+                                       int* status, cudaStream_t stream) {
+  if (nc > tc::kRaBitQMaxClusters || !flat_tc_supported(padded, values, q_hi) ||
+      (uintptr_t)q_lo % 16 != 0)
+    return cudaErrorInvalidValue;
+  return launch_tc<tc::kModeRaBitQFull>(nq, q_hi, q_lo, nc, values, nullptr, n, padded,
+                                        (int64_t)padded, 2,
+                                        reinterpret_cast<const float*>(row_info), keyrank,
+                                        reinterpret_cast<const float*>(q_terms), q_gadd, gthr,
+                                        bitmap, num_parts, kp, list_base, num_lists, cand,
+                                        part_counts, part_sat, q_flags, status, stream);
 }
 
 int rabitq_tc_max_clusters() { return tc::kRaBitQMaxClusters; }

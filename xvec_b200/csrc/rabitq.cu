@@ -28,6 +28,7 @@
 #include <cmath>
 #include <vector>
 
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
 #include "capi_internal.h"
@@ -48,9 +49,11 @@ xvec_gpu_status add_device_locked(xvec_gpu_index* idx, const uint64_t* d_keys, c
                                   int64_t m, cudaStream_t s);
 
 struct RaBitQFactors {
-  double add;
+  double add;           // coarse (one-bit) factors
   double rescale;
   double error;
+  double full_add;      // multi-bit factors (equal to the coarse ones for one bit)
+  double full_rescale;
   int32_t cluster;
   int32_t pad_;
 };
@@ -62,6 +65,26 @@ struct BitElem {
 __device__ __forceinline__ float load_elem(const BitElem* p, int64_t i) {
   const uint8_t* b = reinterpret_cast<const uint8_t*>(p);
   return (float)((b[i >> 3] >> (i & 7)) & 1u);
+}
+// Multi-bit code values as 16-bit floats (bfloat16 up to 8 bits, binary16
+// for 9), seen by the FFMA tile kernel and the exact scorer.
+struct Bf16Value {
+  __nv_bfloat16 v;
+};
+struct HalfValue {
+  __half v;
+};
+__device__ __forceinline__ float load_elem(const Bf16Value* p, int64_t i) {
+  return __bfloat162float(p[i].v);
+}
+__device__ __forceinline__ float load_elem(const HalfValue* p, int64_t i) {
+  return __half2float(p[i].v);
+}
+// The value at coordinate i of a row of the 16-bit plane.
+__device__ __forceinline__ double rabitq_value(const uint16_t* row, int i, bool half) {
+  const uint16_t raw = row[i];
+  return half ? (double)__half2float(__ushort_as_half(raw))
+              : (double)__bfloat162float(__ushort_as_bfloat16(raw));
 }
 
 namespace {
@@ -179,16 +202,75 @@ __global__ void rabitq_prepare_kernel(const float* rows, int64_t n, int d, bool 
   for (int i = threadIdx.x; i < d; i += blockDim.x) out[(int64_t)blockIdx.x * d + i] = v[i];
 }
 
-// quantizeRaBitQVector (rabitq_quantize.go:99-200) with TotalBits = 1 and
-// raBitQFactors (rabitq_quantize.go:210-262), one block per row.
+// raBitQFactors (rabitq_quantize.go:210-262) from its five float64 sums
+// (index order); ok = false where the reference returns an error.
+__device__ bool rabitq_factor_formula(double ns, double cns, double rcd, double ccd, double rcent,
+                                      int padded, int inner_product, double* add,
+                                      double* rescale, double* errf) {
+  if (ns == 0) {
+    *add = inner_product ? 1.0 : 0.0;
+    *rescale = 0.0;
+    *errf = 0.0;
+    return true;
+  }
+  if (!(rcd > 0) || isinf(rcd)) return false;
+  double ratio = __dsub_rn(__ddiv_rn(__dmul_rn(ns, cns), __dmul_rn(rcd, rcd)), 1.0);
+  if (ratio < 0 && ratio > -1e-12) ratio = 0;
+  if (ratio < 0 || isnan(ratio) || isinf(ratio)) return false;
+  const double norm = __dsqrt_rn(ns);
+  const double te =
+      __dmul_rn(__dmul_rn(norm, 1.9), __dsqrt_rn(__ddiv_rn(ratio, (double)(padded - 1))));
+  if (inner_product) {
+    *add = __dadd_rn(__dsub_rn(1.0, rcent), __ddiv_rn(__dmul_rn(ns, ccd), rcd));
+    *rescale = __ddiv_rn(-ns, rcd);
+    *errf = te;
+  } else {
+    *add = __dadd_rn(ns, __ddiv_rn(__dmul_rn(__dmul_rn(2.0, ns), ccd), rcd));
+    *rescale = __ddiv_rn(__dmul_rn(-2.0, ns), rcd);
+    *errf = __dmul_rn(2.0, te);
+  }
+  return isfinite(*add) && isfinite(*rescale) && isfinite(*errf);
+}
+
+// The extra-bit quantization of one coordinate (quantizeRaBitQVector,
+// rabitq_quantize.go:140-180): an = |r| / norm, q = int(scale an + 1e-5)
+// clamped to [0, 2^eb - 1], the extra value (mirrored for r < 0), the factor
+// value extra | (r >= 0) << eb and the code value extra | (r > 0) << eb.
+struct RaBitQExtra {
+  double an;
+  int q, factor_value, code_value;
+};
+__device__ __forceinline__ RaBitQExtra rabitq_extra(double res, double norm, double extra_scale,
+                                                    int eb) {
+  RaBitQExtra x{0.0, 0, 0, 0};
+  if (!(norm > 0)) return x;  // the reference leaves every value zero
+  const int max_extra = (1 << eb) - 1;
+  x.an = __ddiv_rn(fabs(res), norm);
+  int q = __double2int_rz(__dadd_rn(__dmul_rn(extra_scale, x.an), 1e-5));
+  q = min(max(q, 0), max_extra);
+  x.q = q;
+  const int e = res < 0 ? max_extra - q : q;
+  x.factor_value = e | ((res >= 0 ? 1 : 0) << eb);
+  x.code_value = e | ((res > 0 ? 1 : 0) << eb);
+  return x;
+}
+
+// quantizeRaBitQVector (rabitq_quantize.go:99-200) and raBitQFactors
+// (rabitq_quantize.go:210-262), one block per row: the sign bits, the coarse
+// factors and, for TotalBits > 1, the full code values (16-bit floats) and the
+// full factors (full rescale = -norm / ip (IP) or -2 norm / ip, ip = sum of
+// (q + 1/2) an in index order).
 __global__ void rabitq_encode_kernel(const float* prepared, int64_t n, int d, int padded,
                                      int truncated, const uint8_t* signs, float inv,
                                      const float* rot_centroids, const int32_t* labels,
-                                     int inner_product, uint8_t* codes, RaBitQFactors* factors,
+                                     int inner_product, int total_bits, double extra_scale,
+                                     uint8_t* codes, uint16_t* values, RaBitQFactors* factors,
                                      float4* fast, unsigned* bounds, int* err) {
   extern __shared__ float smem[];
   float* v = smem;                 // [padded] rotated row
   __shared__ double s_sum[4];
+  __shared__ double s_full[4];
+  const int eb = total_bits - 1;
   const int64_t r = blockIdx.x;
   if (!block_prepare_rotate(prepared + r * d, d, padded, truncated, signs, inv, false, v)) {
     if (threadIdx.x == 0) atomicExch(err, XVEC_GPU_NON_FINITE);
@@ -223,47 +305,68 @@ __global__ void rabitq_encode_kernel(const float* prepared, int64_t n, int d, in
     s_sum[threadIdx.x] = acc;
   }
   __syncthreads();
+  const double norm = __dsqrt_rn(s_sum[0]);
+  if (eb > 0) {
+    // The code values (any order), then the full sums (index order): ip of
+    // the extra quantization, and the code norm, residual and centroid dots
+    // of the factor values (center -(2^TotalBits - 1)/2).
+    const bool half = total_bits > 8;
+    for (int i = threadIdx.x; i < padded; i += blockDim.x) {
+      const double res = __dsub_rn((double)v[i], (double)cen[i]);
+      const float cv = (float)rabitq_extra(res, norm, extra_scale, eb).code_value;
+      values[r * padded + i] = half ? __half_as_ushort(__float2half_rn(cv))
+                                    : __bfloat16_as_ushort(__float2bfloat16_rn(cv));
+    }
+    if (threadIdx.x < 4) {
+      const double center = -((double)(1 << total_bits) - 1.0) / 2.0;
+      double acc = 0.0;
+      for (int i = 0; i < padded; ++i) {
+        const double res = __dsub_rn((double)v[i], (double)cen[i]);
+        const RaBitQExtra x = rabitq_extra(res, norm, extra_scale, eb);
+        const double cc = __dadd_rn((double)x.factor_value, center);
+        double t;
+        if (threadIdx.x == 0) {
+          if (!(norm > 0)) continue;
+          t = __dmul_rn(__dadd_rn((double)x.q, 0.5), x.an);  // ip of the quantization
+        } else if (threadIdx.x == 1) {
+          t = __dmul_rn(cc, cc);                    // codeNormSquared
+        } else if (threadIdx.x == 2) {
+          t = __dmul_rn(res, cc);                   // residualCodeDot
+        } else {
+          t = __dmul_rn((double)cen[i], cc);        // centroidCodeDot
+        }
+        acc = __dadd_rn(acc, t);
+      }
+      s_full[threadIdx.x] = acc;
+    }
+    __syncthreads();
+  }
   if (threadIdx.x == 0) {
     const double ns = s_sum[0], rcd = s_sum[1], ccd = s_sum[2], rcent = s_sum[3];
     const double cns = 0.25 * (double)padded;  // sum of 0.25 over padded terms, exact
     double add, rescale, errf;
-    bool ok = true;
-    if (ns == 0) {
-      add = inner_product ? 1.0 : 0.0;
-      rescale = 0.0;
-      errf = 0.0;
-    } else if (!(rcd > 0) || isinf(rcd)) {
-      ok = false;
-    } else {
-      double ratio = __dsub_rn(__ddiv_rn(__dmul_rn(ns, cns), __dmul_rn(rcd, rcd)), 1.0);
-      if (ratio < 0 && ratio > -1e-12) ratio = 0;
-      if (ratio < 0 || isnan(ratio) || isinf(ratio)) ok = false;
-      if (ok) {
-        const double norm = __dsqrt_rn(ns);
-        const double te = __dmul_rn(__dmul_rn(norm, 1.9),
-                                    __dsqrt_rn(__ddiv_rn(ratio, (double)(padded - 1))));
-        if (inner_product) {
-          add = __dadd_rn(__dsub_rn(1.0, rcent), __ddiv_rn(__dmul_rn(ns, ccd), rcd));
-          rescale = __ddiv_rn(-ns, rcd);
-          errf = te;
-        } else {
-          add = __dadd_rn(ns, __ddiv_rn(__dmul_rn(__dmul_rn(2.0, ns), ccd), rcd));
-          rescale = __ddiv_rn(__dmul_rn(-2.0, ns), rcd);
-          errf = __dmul_rn(2.0, te);
-        }
-        if (!isfinite(add) || !isfinite(rescale) || !isfinite(errf)) ok = false;
-      }
+    bool ok = rabitq_factor_formula(ns, cns, rcd, ccd, rcent, padded, inner_product, &add,
+                                    &rescale, &errf);
+    double fadd = add, frescale = rescale, ferr_scaled = errf;
+    if (ok && eb > 0) {
+      double unused;
+      ok = rabitq_factor_formula(ns, s_full[1], s_full[2], s_full[3], rcent, padded,
+                                 inner_product, &fadd, &frescale, &unused);
+      const double ipn = s_full[0];
+      const double inv_ip = (norm > 0 && ipn > 0 && isfinite(ipn)) ? __ddiv_rn(1.0, ipn) : 1.0;
+      frescale = inner_product ? __dmul_rn(-norm, inv_ip) : __dmul_rn(__dmul_rn(-2.0, norm), inv_ip);
+      ferr_scaled = ldexp(errf, -eb);  // Estimate's error bound over 2^extra bits
     }
     if (!ok) {
       atomicExch(err, XVEC_GPU_OVERFLOW);
       return;
     }
-    factors[r] = RaBitQFactors{add, rescale, errf, c, 0};
-    fast[r] = make_float4(__double2float_rn(add), __double2float_rn(rescale), __int_as_float(c),
+    factors[r] = RaBitQFactors{add, rescale, errf, fadd, frescale, c, 0};
+    fast[r] = make_float4(__double2float_rn(fadd), __double2float_rn(frescale), __int_as_float(c),
                           0.f);
-    atomicMax(&bounds[0], float_to_ordered(fabsf(__double2float_rn(add))));
-    atomicMax(&bounds[1], float_to_ordered(fabsf(__double2float_rn(rescale))));
-    atomicMax(&bounds[2], float_to_ordered(__double2float_ru(errf)));
+    atomicMax(&bounds[0], float_to_ordered(fabsf(__double2float_rn(fadd))));
+    atomicMax(&bounds[1], float_to_ordered(fabsf(__double2float_rn(frescale))));
+    atomicMax(&bounds[2], float_to_ordered(__double2float_ru(ferr_scaled)));
   }
 }
 
@@ -305,7 +408,13 @@ __global__ void rabitq_prep_query_kernel(const float* queries, int nq, int d, in
                                          double* q_sum, double* g_add, double* g_error,
                                          float* q_fast_sum, float* q_fast_gadd, float* q_eps,
                                          int* q_exact, int* q_status, int* q_flags,
-                                         int8_t* q_int, float2* q_terms) {
+                                         int8_t* q_int, float2* q_terms, int total_bits,
+                                         __nv_bfloat16* q_bf) {
+  // total_bits > 1: q_bf holds the rotated queries' bfloat16 high parts
+  // [nq][padded] followed by their low parts [nq][padded] (the multi-bit
+  // tensor-core operands) and q_int is unused.
+  const bool multi = total_bits > 1;
+  const double vmax = (double)((1 << total_bits) - 1);  // largest code value
   extern __shared__ float v[];
   __shared__ double s_sum;
   __shared__ float s_abs;
@@ -321,8 +430,13 @@ __global__ void rabitq_prep_query_kernel(const float* queries, int nq, int d, in
   auto reject = [&]() {
     for (int i = threadIdx.x; i < padded; i += blockDim.x) {
       q_rot[(int64_t)q * padded + i] = 0.f;
-      q_int[(int64_t)q * 2 * padded + i] = 0;
-      q_int[(int64_t)q * 2 * padded + padded + i] = 0;
+      if (multi) {
+        q_bf[(int64_t)q * padded + i] = __float2bfloat16_rn(0.f);
+        q_bf[((int64_t)nq + q) * padded + i] = __float2bfloat16_rn(0.f);
+      } else {
+        q_int[(int64_t)q * 2 * padded + i] = 0;
+        q_int[(int64_t)q * 2 * padded + padded + i] = 0;
+      }
     }
     for (int c = threadIdx.x; c < nc; c += blockDim.x) {
       g_add[(int64_t)q * nc + c] = 0.0;
@@ -371,11 +485,15 @@ __global__ void rabitq_prep_query_kernel(const float* queries, int nq, int d, in
     const float scale = mx > 0.f ? mx / (float)kRaBitQIntMax : 0.f;
     s_scale = scale;
     s_resid = 0.0;
-    q_terms[q] = make_float2(0.5f * __double2float_rn(s), scale);
-    // Every value is a multiple of 2^g and every partial sum of a subset is
-    // at most a in magnitude; below 2^(52+g) all of them are exact in float64,
-    // so the masked sums may be taken in any order.
-    q_exact[q] = (g == (1 << 20)) || a <= ldexp(1.0, min(1000, 52 + g));
+    // Multi-bit: -(center sum), center = -(2^(TotalBits-1) - 1/2) (Estimate).
+    const double center = multi ? -(ldexp(1.0, total_bits - 1) - 0.5) : -0.5;
+    q_terms[q] = multi ? make_float2(-__double2float_rn(__dmul_rn(center, s)), 0.f)
+                       : make_float2(0.5f * __double2float_rn(s), scale);
+    // Every value is a multiple of 2^g, so is every product with a code value
+    // (at most vmax), and every partial sum of such products is at most
+    // vmax a in magnitude; below 2^(52+g) all of them are exact in float64,
+    // so the sums may be taken in any order.
+    q_exact[q] = (g == (1 << 20)) || __dmul_ru(a, vmax) <= ldexp(1.0, min(1000, 52 + g));
   }
   for (int c = threadIdx.x; c < nc; c += blockDim.x) {
     const float* cen = rot_centroids + (int64_t)c * padded;
@@ -391,7 +509,17 @@ __global__ void rabitq_prep_query_kernel(const float* queries, int nq, int d, in
     q_fast_gadd[(int64_t)q * nc + c] = __double2float_rn(ga);
   }
   __syncthreads();
-  {
+  if (multi) {
+    // bfloat16 high and low parts: hi = bf16(v), lo = bf16(v - hi) (v - hi is
+    // exact in float32).
+    __nv_bfloat16* qhi = q_bf + (int64_t)q * padded;
+    __nv_bfloat16* qlo = q_bf + ((int64_t)nq + q) * padded;
+    for (int i = threadIdx.x; i < padded; i += blockDim.x) {
+      const __nv_bfloat16 hi = __float2bfloat16_rn(v[i]);
+      qhi[i] = hi;
+      qlo[i] = __float2bfloat16_rn(v[i] - __bfloat162float(hi));
+    }
+  } else {
     // The integer query and the bound on its rounding, sum |v_i - scale w_i|
     // (each term exact in float64; the sum is only a bound).
     const float scale = s_scale;
@@ -418,19 +546,33 @@ __global__ void rabitq_prep_query_kernel(const float* queries, int nq, int d, in
     const double maxE = ordered_to_float(bounds[2]);
     const double S1 = (double)s_abs * 1.001;
     const double sumd = fabs(s_sum);
+    // Multi-bit: |dot + center sum| <= vmax S1 + |center sum|.
+    const double csum = multi ? (ldexp(1.0, total_bits - 1) - 0.5) * sumd : 0.5 * sumd;
     // |estimate| and its error bound over every row; far below MaxFloat32 no
     // row can fail makeRaBitQEstimate and the float32 fast rank is finite.
-    const double reach = maxA + maxg + maxR * (S1 + 0.5 * sumd) + maxE * maxge;
+    const double reach = maxA + maxg + maxR * (vmax * S1 + csum) + maxE * maxge;
     if (!(reach < 1e37)) q_flags[q] |= 1 | kRaBitQFullCheck;
     // Bound on |fast rank - float32(estimate)|: the float32 sum of up to
     // padded terms (FFMA scan) or the integer query's rounding plus the
     // float32 conversion and scaling of the exact integer dot product
     // (tensor-core scan), the float32 roundings of the inputs and of each
     // operation.
-    const double resid = s_resid * 1.0001;
-    const double dot_err = fmax((double)(padded + 2) * kU * S1,
-                                resid + 3.0 * kU * (S1 + resid));
-    const double e = maxR * dot_err + 6.0 * kU * (maxA + maxg + maxR * (S1 + 0.5 * sumd));
+    double e;
+    if (multi) {
+      // The bfloat16 split (|v - hi - lo| <= 2^-16 |v|, plus underflow) and
+      // an fp32 accumulation of 2 padded exact products on the tensor cores
+      // (the FFMA scan's float32 sum of padded terms is within the same
+      // bound), the float32 roundings of the terms and of the formula.
+      const double dot_err =
+          vmax * (S1 * (ldexp(1.0, -16) + (2.0 * padded + 8.0) * ldexp(1.0, -23) * 1.01) +
+                  (double)padded * ldexp(1.0, -126));
+      e = maxR * (dot_err + kU * csum) + 6.0 * kU * (maxA + maxg + maxR * (vmax * S1 + csum));
+    } else {
+      const double resid = s_resid * 1.0001;
+      const double dot_err = fmax((double)(padded + 2) * kU * S1,
+                                  resid + 3.0 * kU * (S1 + resid));
+      e = maxR * dot_err + 6.0 * kU * (maxA + maxg + maxR * (S1 + 0.5 * sumd));
+    }
     q_eps[q] = (float)(2.5 * e) + 1e-30f;
     // Magnitudes whose scale would lose precision go to the exact scan.
     if (!(s_maxabs < 1e30f) || (s_maxabs > 0.f && s_maxabs < 1e-30f)) q_flags[q] |= 1;
@@ -447,11 +589,14 @@ __host__ __device__ inline int rabitq_query_status(int prep, int flags, int refi
   return 0;
 }
 
+// FULL: the multi-bit estimate, dot - q_terms.x with q_terms.x = -(center sum).
+template <bool FULL>
 struct RaBitQRanker {
   const float4* fast;
   const float* q_fast_sum;
   const float* q_fast_gadd;
   int nc;
+  const float2* q_terms;
   struct RowInfo {
     float add, rescale;
     int cluster;
@@ -460,7 +605,10 @@ struct RaBitQRanker {
     int qi;
     float half_sum;
   };
-  __device__ QueryInfo query(int qi) const { return {qi, 0.5f * q_fast_sum[qi]}; }
+  __device__ QueryInfo query(int qi) const {
+    if constexpr (FULL) return {qi, q_terms[qi].x};
+    return {qi, 0.5f * q_fast_sum[qi]};
+  }
   __device__ RowInfo row(int64_t r) const {
     const float4 f = fast[r];
     return {f.x, f.y, __float_as_int(f.z)};
@@ -487,26 +635,47 @@ struct RaBitQScorer {
   const float* q_eps;
   const int* q_exact;
   int padded, nc;
+  int total_bits;          // > 1: Estimate on the full code values
+  const uint16_t* values;  // [n][padded] 16-bit floats (multi-bit)
   __device__ float score(int qi, int64_t row) const {
     const int lane = threadIdx.x & 31;
     const uint8_t* b = codes + row * (padded / 8);
     const float* q = q_rot + (int64_t)qi * padded;
+    const bool multi = total_bits > 1, half = total_bits > 8;
+    const uint16_t* vrow = multi ? values + row * padded : nullptr;
+    // raBitQBinaryDot / raBitQFullCodeDot: float64 sum in index order (or in
+    // any order when every partial sum is exact for this query).
+    auto term = [&](int i) -> double {
+      if (multi) return __dmul_rn(rabitq_value(vrow, i, half), (double)q[i]);
+      return (b[i >> 3] & (1u << (i & 7))) ? (double)q[i] : 0.0;
+    };
     double dot = 0.0;
     if (q_exact[qi]) {
-      for (int i = lane; i < padded; i += 32)
-        if (b[i >> 3] & (1u << (i & 7))) dot = __dadd_rn(dot, (double)q[i]);
+      for (int i = lane; i < padded; i += 32) dot = __dadd_rn(dot, term(i));
       for (int o = 16; o > 0; o >>= 1) dot = __dadd_rn(dot, __shfl_xor_sync(kFullMask, dot, o));
     } else {
       if (lane == 0)
-        for (int i = 0; i < padded; ++i)
-          if (b[i >> 3] & (1u << (i & 7))) dot = __dadd_rn(dot, (double)q[i]);
+        for (int i = 0; i < padded; ++i) {
+          const double t = term(i);
+          if (multi || t != 0.0 || (b[i >> 3] & (1u << (i & 7)))) dot = __dadd_rn(dot, t);
+        }
       dot = __shfl_sync(kFullMask, dot, 0);
     }
     const RaBitQFactors f = factors[row];
-    const double centered = __dsub_rn(dot, __dmul_rn(0.5, q_sum[qi]));
-    const double dist = __dadd_rn(__dadd_rn(f.add, g_add[(int64_t)qi * nc + f.cluster]),
-                                  __dmul_rn(f.rescale, centered));
-    const double eb = __dmul_rn(f.error, g_error[(int64_t)qi * nc + f.cluster]);
+    double dist, eb;
+    if (multi) {
+      // Estimate (rabitq.go:434-446).
+      const double center = -(ldexp(1.0, total_bits - 1) - 0.5);
+      dist = __dadd_rn(__dadd_rn(f.full_add, g_add[(int64_t)qi * nc + f.cluster]),
+                       __dmul_rn(f.full_rescale, __dadd_rn(dot, __dmul_rn(center, q_sum[qi]))));
+      eb = __ddiv_rn(__dmul_rn(f.error, g_error[(int64_t)qi * nc + f.cluster]),
+                     ldexp(1.0, total_bits - 1));
+    } else {
+      const double centered = __dsub_rn(dot, __dmul_rn(0.5, q_sum[qi]));
+      dist = __dadd_rn(__dadd_rn(f.add, g_add[(int64_t)qi * nc + f.cluster]),
+                       __dmul_rn(f.rescale, centered));
+      eb = __dmul_rn(f.error, g_error[(int64_t)qi * nc + f.cluster]);
+    }
     constexpr double kMaxF = 3.40282346638528859811704183484516925440e+38;
     if (isnan(dist) || isinf(dist) || isnan(eb) || isinf(eb) || eb < 0)
       return __int_as_float(0x7fc00000);
@@ -714,12 +883,14 @@ xvec_gpu_status rabitq_reserve(xvec_gpu_index* idx, int64_t cap, cudaStream_t s)
   const int64_t n = idx->n;
   const int bytes = idx->padded / 8;
   xvec_gpu_status st;
+  // One bit: the int8 code planes [127 b | b]; multi-bit: the 16-bit code
+  // values; both 2 padded bytes per row.
+  DeviceBuffer& plane = idx->rq_total_bits > 1 ? idx->rq_values : idx->rq_planes;
   if ((st = idx->rq_codes.reserve((size_t)cap * bytes, (size_t)n * bytes, s)) ||
       (st = idx->rq_factors.reserve((size_t)cap * sizeof(RaBitQFactors),
                                     (size_t)n * sizeof(RaBitQFactors), s)) ||
       (st = idx->rq_fast.reserve((size_t)cap * 16, (size_t)n * 16, s)) ||
-      (st = idx->rq_planes.reserve((size_t)cap * idx->padded * 2, (size_t)n * idx->padded * 2,
-                                     s)))
+      (st = plane.reserve((size_t)cap * idx->padded * 2, (size_t)n * idx->padded * 2, s)))
     return st;
   if (!idx->rq_bounds.ptr) {
     if ((st = idx->rq_bounds.reserve(16, 0, s))) return st;
@@ -750,7 +921,8 @@ xvec_gpu_status rabitq_commit(xvec_gpu_index* idx, int64_t old_n, int64_t m, cud
   rabitq_encode_kernel<<<(unsigned)m, 256, padded * 4, s>>>(
       prepared.as<float>(), m, d, padded, truncated, idx->rq_signs.as<uint8_t>(), inv,
       idx->rq_rot_centroids.as<float>(), labels.as<int32_t>(), metric != XVEC_METRIC_L2,
-      idx->rq_codes.as<uint8_t>() + old_n * (padded / 8),
+      idx->rq_total_bits, idx->rq_extra_scale, idx->rq_codes.as<uint8_t>() + old_n * (padded / 8),
+      idx->rq_total_bits > 1 ? idx->rq_values.as<uint16_t>() + old_n * padded : nullptr,
       idx->rq_factors.as<RaBitQFactors>() + old_n, idx->rq_fast.as<float4>() + old_n,
       bounds.as<unsigned>(), err.as<int>());
   XVEC_LAUNCHED();
@@ -759,12 +931,14 @@ xvec_gpu_status rabitq_commit(xvec_gpu_index* idx, int64_t old_n, int64_t m, cud
   XVEC_CUDA(cudaMemcpyAsync(&h, err.ptr, 4, cudaMemcpyDeviceToHost, s));
   XVEC_CUDA(cudaStreamSynchronize(s));
   if (h) return set_error("core: invalid RaBitQ code (status %d)", h), (xvec_gpu_status)h;
+  if (idx->rq_total_bits == 1) {
   const int64_t code_bytes = m * (padded / 8);
   rabitq_planes_kernel<<<blocks_of(code_bytes), 256, 0, s>>>(
       idx->rq_codes.as<uint8_t>() + old_n * (padded / 8), code_bytes, padded,
       idx->rq_planes.as<int8_t>() + old_n * 2 * padded);
   XVEC_LAUNCHED();
   XVEC_CUDA(cudaGetLastError());
+  }
   XVEC_CUDA(cudaMemcpyAsync(idx->rq_bounds.ptr, bounds.ptr, 16, cudaMemcpyDeviceToDevice, s));
   return XVEC_GPU_OK;
 }
@@ -832,8 +1006,11 @@ xvec_gpu_status rabitq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq
   const int truncated = floor_pow2(d);
   const float inv = inv_sqrt_size(truncated);
   xvec_gpu_status st;
-  Scratch qrot, qsum, gadd, gerr, qfs, qfg, qeps, qexact, qstatus, qflags, qint, qterms;
-  if ((st = qint.alloc((size_t)nq * padded * 2, s)) || (st = qterms.alloc((size_t)nq * 8, s)))
+  const int total_bits = idx->rq_total_bits;
+  const bool multi = total_bits > 1;
+  Scratch qrot, qsum, gadd, gerr, qfs, qfg, qeps, qexact, qstatus, qflags, qint, qterms, qbf;
+  if ((st = qint.alloc((size_t)nq * padded * 2, s)) || (st = qterms.alloc((size_t)nq * 8, s)) ||
+      (multi && (st = qbf.alloc((size_t)nq * padded * 4, s))))
     return st;
   if ((st = qrot.alloc((size_t)nq * padded * 4, s)) || (st = qsum.alloc((size_t)nq * 8, s)) ||
       (st = gadd.alloc((size_t)nq * nc * 8, s)) || (st = gerr.alloc((size_t)nq * nc * 8, s)) ||
@@ -847,7 +1024,8 @@ xvec_gpu_status rabitq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq
       metric == XVEC_METRIC_COSINE, metric, idx->rq_rot_centroids.as<float>(), nc,
       idx->rq_bounds.as<unsigned>(), qrot.as<float>(), qsum.as<double>(), gadd.as<double>(),
       gerr.as<double>(), qfs.as<float>(), qfg.as<float>(), qeps.as<float>(), qexact.as<int>(),
-      qstatus.as<int>(), qflags.as<int>(), qint.as<int8_t>(), qterms.as<float2>());
+      qstatus.as<int>(), qflags.as<int>(), qint.as<int8_t>(), qterms.as<float2>(), total_bits,
+      multi ? qbf.as<__nv_bfloat16>() : nullptr);
   XVEC_LAUNCHED();
   // The approximate stage writes the final results, or the candidates of the
   // refine stage (no radius there: hnsw_rabitq.go:584).
@@ -864,16 +1042,19 @@ xvec_gpu_status rabitq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq
                         idx->rq_codes.as<uint8_t>(),
                         idx->rq_factors.as<RaBitQFactors>(), qrot.as<float>(),
                         qsum.as<double>(), gadd.as<double>(), gerr.as<double>(),
-                        qeps.as<float>(), qexact.as<int>(), padded, nc};
+                        qeps.as<float>(), qexact.as<int>(), padded, nc, total_bits,
+                        multi ? idx->rq_values.as<uint16_t>() : nullptr};
   const float stage_radius = refine ? 0.f : o.radius;
   // Small batches: the sign bits through a byte table (the tensor-core scan
   // streams 16x more bytes and fills few SMs at this size).
-  const bool small = n > 0 && nq <= 8 && padded <= 8 * kLutMaxBytes && kp <= 256;
-  // INT8 tensor cores on the code planes when the layout allows, else FFMA.
+  const bool small = !multi && n > 0 && nq <= 8 && padded <= 8 * kLutMaxBytes && kp <= 256;
+  // INT8 tensor cores on the code planes (one bit), or BF16 tensor cores on
+  // the full code values (up to 8 bits), when the layout allows, else FFMA.
   const bool use_tc = !small && n > 0 && nc <= rabitq_tc_max_clusters() &&
-                      kp + 128 <= flat_tc_cap() &&
-                      n < (1ll << 31) - 256 &&
-                      rabitq_tc_supported(padded, idx->rq_planes.ptr, qint.ptr);
+                      kp + 128 <= flat_tc_cap() && n < (1ll << 31) - 256 &&
+                      (multi ? total_bits <= 8 && (uintptr_t)idx->rq_values.ptr % 16 == 0 &&
+                                   (uintptr_t)qbf.ptr % 16 == 0
+                             : rabitq_tc_supported(padded, idx->rq_planes.ptr, qint.ptr));
   const bool fast = small || use_tc || (n > 0 && simt_cap_for(kp) <= 512);
   if (small) {
     int parts = (int)std::max<int64_t>(
@@ -913,6 +1094,14 @@ xvec_gpu_status rabitq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq
         idx->device, nq, n, kp, s,
         [&](int64_t b, int64_t e, int p, int list0, int nlists, unsigned long long* gthr,
             uint64_t* cand, int* counts, uint64_t* sat) {
+          if (multi)
+            return launch_rabitq_full_scan_tc(
+                qbf.as<__nv_bfloat16>(), qbf.as<__nv_bfloat16>() + (int64_t)nq * padded, nq,
+                idx->rq_values.as<__nv_bfloat16>() + b * padded, e - b, padded,
+                idx->rq_fast.as<float4>() + b, idx->keyrank.as<uint32_t>() + b,
+                qterms.as<float2>(), qfg.as<float>(), nc, gthr,
+                d_bitmap ? d_bitmap + b / 32 : nullptr, p, kp, list0, nlists, cand, counts, sat,
+                qflags.as<int>(), kstatus.as<int>(), s);
           return launch_rabitq_scan_tc(
               qint.as<int8_t>(), nq, idx->rq_planes.as<int8_t>() + b * 2 * padded, e - b,
               padded, idx->rq_fast.as<float4>() + b, idx->keyrank.as<uint32_t>() + b,
@@ -946,12 +1135,26 @@ xvec_gpu_status rabitq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq
         (st = pcounts.alloc((size_t)nq * parts * 4, s)) ||
         (st = psat.alloc((size_t)nq * parts * 8, s)))
       return st;
-    const RaBitQRanker rk{idx->rq_fast.as<float4>(), qfs.as<float>(), qfg.as<float>(), nc};
+    const RaBitQRanker<false> rk{idx->rq_fast.as<float4>(), qfs.as<float>(), qfg.as<float>(),
+                                 nc, nullptr};
+    const RaBitQRanker<true> rkf{idx->rq_fast.as<float4>(), qfs.as<float>(), qfg.as<float>(),
+                                 nc, qterms.as<float2>()};
     timer.mark(1);
-    XVEC_CUDA(launch_scan_simt(reinterpret_cast<const BitElem*>(idx->rq_codes.ptr), n, padded,
-                               idx->keyrank.as<uint32_t>(), qrot.as<float>(), nq, d_bitmap, rk,
-                               parts, kp, pkeys.as<uint64_t>(), pcounts.as<int>(),
-                               psat.as<uint64_t>(), qflags.as<int>(), s));
+    if (!multi)
+      XVEC_CUDA(launch_scan_simt(reinterpret_cast<const BitElem*>(idx->rq_codes.ptr), n, padded,
+                                 idx->keyrank.as<uint32_t>(), qrot.as<float>(), nq, d_bitmap, rk,
+                                 parts, kp, pkeys.as<uint64_t>(), pcounts.as<int>(),
+                                 psat.as<uint64_t>(), qflags.as<int>(), s));
+    else if (total_bits <= 8)
+      XVEC_CUDA(launch_scan_simt(reinterpret_cast<const Bf16Value*>(idx->rq_values.ptr), n,
+                                 padded, idx->keyrank.as<uint32_t>(), qrot.as<float>(), nq,
+                                 d_bitmap, rkf, parts, kp, pkeys.as<uint64_t>(), pcounts.as<int>(),
+                                 psat.as<uint64_t>(), qflags.as<int>(), s));
+    else
+      XVEC_CUDA(launch_scan_simt(reinterpret_cast<const HalfValue*>(idx->rq_values.ptr), n,
+                                 padded, idx->keyrank.as<uint32_t>(), qrot.as<float>(), nq,
+                                 d_bitmap, rkf, parts, kp, pkeys.as<uint64_t>(), pcounts.as<int>(),
+                                 psat.as<uint64_t>(), qflags.as<int>(), s));
     timer.mark(2);
     XVEC_CUDA(launch_merge_rescore(sc, idx->pos_of_kr.as<uint32_t>(), idx->keys.as<uint64_t>(),
                                    nullptr, nq, cc, stage_radius, 0, pkeys.as<uint64_t>(),
@@ -1065,9 +1268,28 @@ using namespace xvec;
 extern "C" xvec_gpu_status xvec_gpu_rabitq_set_model(xvec_gpu_index* idx, const float* centroids,
                                                      int32_t nclusters,
                                                      const uint8_t* rotation_signs) {
+  return xvec_gpu_rabitq_set_model_bits(idx, centroids, nclusters, rotation_signs, 1, 0.0);
+}
+
+extern "C" xvec_gpu_status xvec_gpu_rabitq_set_model_bits(xvec_gpu_index* idx,
+                                                          const float* centroids,
+                                                          int32_t nclusters,
+                                                          const uint8_t* rotation_signs,
+                                                          int32_t total_bits,
+                                                          double extra_scale) {
   if (!idx || !centroids || !rotation_signs) return set_error("nil argument"), XVEC_GPU_INVALID_ARGUMENT;
   if (idx->desc.kind != XVEC_INDEX_RABITQ) return set_error("not a RaBitQ index"), XVEC_GPU_INVALID_ARGUMENT;
+  // RestoreRaBitQModel (rabitq.go:196-211).
+  if (total_bits < 1 || total_bits > 9)
+    return set_error("core: invalid RaBitQ model: TotalBits must be in [1,9]"),
+           XVEC_GPU_INVALID_ARGUMENT;
   if (nclusters <= 0) return set_error("core: invalid RaBitQ model: no centroids"), XVEC_GPU_INVALID_ARGUMENT;
+  if (total_bits == 1 && extra_scale != 0)
+    return set_error("core: invalid RaBitQ model: one-bit model must have zero ExtraScale"),
+           XVEC_GPU_INVALID_ARGUMENT;
+  if (total_bits > 1 && !(extra_scale > 0 && std::isfinite(extra_scale)))
+    return set_error("core: invalid RaBitQ model: ExtraScale must be finite and positive"),
+           XVEC_GPU_INVALID_ARGUMENT;
   const int d = idx->desc.dimension, padded = idx->padded;
   std::unique_lock<std::shared_mutex> lock(idx->mu);
   if (idx->n > 0) return set_error("set the model before adding rows"), XVEC_GPU_INVALID_ARGUMENT;
@@ -1121,6 +1343,8 @@ extern "C" xvec_gpu_status xvec_gpu_rabitq_set_model(xvec_gpu_index* idx, const 
                               nclusters, s)))
     return st;
   idx->rq_clusters = nclusters;
+  idx->rq_total_bits = total_bits;
+  idx->rq_extra_scale = extra_scale;
   idx->has_model = true;
   return XVEC_GPU_OK;
 }
