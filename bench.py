@@ -52,7 +52,8 @@ def parse():
                         "the JSON line as batch_sweep (rabitq_l2_refine, ivfpq_l2, sq8_ip_refine)")
     p.add_argument("--workload",
                    choices=["flat_cosine_fp16", "ivfpq_l2", "sq8_ip_refine", "rabitq_l2_refine",
-                            "flat_l2_fp32", "ivf_flat_l2", "ivf_sq8_l2_refine"],
+                            "flat_l2_fp32", "ivf_flat_l2", "ivf_sq8_l2_refine",
+                            "rabitq7_l2_refine"],
                    default="flat_cosine_fp16",
                    help="flat_cosine_fp16: the Flat configuration above (default); ivfpq_l2: "
                         "IVF-PQ L2, 1e8 x 128, nlist 16384, 32 x 256 PQ, nprobe 64, k=10; "
@@ -61,7 +62,8 @@ def parse():
                         "flat_l2_fp32: Flat L2 over FP32 storage, 1e6 x 128 N(0,1), 1,000 "
                         "queries, k=10; ivf_flat_l2: IVF with exact scoring, 1e7 x 128, "
                         "nlist 4096, nprobe 32, k=10; ivf_sq8_l2_refine: the same IVF with "
-                        "INT8 list scoring and ScaleFactor 4")
+                        "INT8 list scoring and ScaleFactor 4; rabitq7_l2_refine: the RaBitQ "
+                        "data with TotalBits 7")
     return p.parse_args()
 
 
@@ -795,9 +797,16 @@ def cpu_sq8_qps(sample, queries, n_total):
 RQ_N, RQ_DIM, RQ_NC, RQ_K, RQ_EF, RQ_CHUNK_ROWS = 10_000_000, 960, 16, 10, 100, 500_000
 RQ_WORKLOAD = ("RaBitQ 1-bit L2 search with exact FP32 refinement, 10,000,000 x 960 "
                "(1,000-cluster mixture), 16 clusters, 10,000 queries, top-k=10, EF 100")
+# The same data with the reference's default TotalBits 7 (6 extra bits); the
+# ExtraScale stands in for TrainRaBitQ's trained value (the scale that maps
+# the rotated unit residuals' coordinates, |N(0,1)|/sqrt(960), onto 0..63).
+RQ7_BITS, RQ7_SCALE = 7, 620.0
+RQ7_WORKLOAD = ("RaBitQ 7-bit (TotalBits 7, ExtraScale 620) L2 search with exact FP32 "
+                "refinement, 10,000,000 x 960 (1,000-cluster mixture), 16 clusters, 10,000 "
+                "queries, top-k=10, EF 100")
 
 
-def run_rabitq(args):
+def run_rabitq(args, total_bits=1):
     import numpy as np
     import torch
 
@@ -812,7 +821,8 @@ def run_rabitq(args):
     padded = (RQ_DIM + 63) // 64 * 64
     signs = np.random.default_rng(961).integers(0, 256, 4 * padded // 8, dtype=np.uint8)
     index = xb.RaBitQIndex(RQ_DIM, xb.METRIC_L2, device=local)
-    index.set_model(cents.cpu().numpy(), signs)
+    extra_scale = RQ7_SCALE if total_bits > 1 else 0.0
+    index.set_model(cents.cpu().numpy(), signs, total_bits, extra_scale)
     b, e = shard_range(n, rank, world, align=RQ_CHUNK_ROWS)
     index.reserve(e - b)
     stream = torch.cuda.current_stream().cuda_stream
@@ -836,43 +846,64 @@ def run_rabitq(args):
         m = min(args.cpu_sample_rows // 50, n)
         sample = pq_mixture(torch, centers, 2 * 10**6, m, dev).cpu().numpy()
         cpu = cpu_rabitq_qps(cents.cpu().numpy(), signs, sample,
-                             queries[:max(8, args.cpu_sample_queries // 4)].cpu().numpy(), n)
+                             queries[:max(8, args.cpu_sample_queries // 4)].cpu().numpy(), n,
+                             total_bits, extra_scale)
     if rank == 0:
-        # INT8 MMAs over the code planes [127 b | b] against the integer query
-        # [h | l]: 2 x nq x n x (2 padded) integer ops.
-        ops = 2.0 * nq * (e - b) * (2 * padded)
-        achieved = ops / (scan_ms / 1000.0) / 1e12 if scan_ms > 0 else None
-        peak = 4500.0
-        roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOP/s",
-                "frac": (achieved / peak) if achieved else None, "traffic": None,
-                "peak_source": "nominal dense INT8 tensor (no measured INT8 figure); the scan "
-                               "runs on tcgen05 kind::i8",
-                "kernel": "RaBitQ code-plane scan", "kernel_ms": scan_ms,
-                "algorithmic_int_ops_per_launch": ops}
-        config = {"workload": RQ_WORKLOAD, "global_batch": nq, "top_k": RQ_K, "base_vectors": n,
+        if total_bits > 1:
+            # BF16 MMAs of the code values against the query's high and low
+            # parts: 2 x nq x n x (2 padded) flops on the tensor pipe
+            # (2 x nq x n x padded algorithmic).
+            ops = 2.0 * nq * (e - b) * padded
+            achieved = ops / (scan_ms / 1000.0) / 1e12 if scan_ms > 0 else None
+            bf16, _, peak_kind = peaks()
+            roof = {"bound": "tensor", "achieved": achieved, "peak": bf16, "unit": "TFLOP/s",
+                    "frac": (achieved / bf16) if achieved else None, "traffic": None,
+                    "peak_source": f"{peak_kind} sustained bf16 dense GEMM; the scan runs two "
+                                   "kind::f16 (BF16) MMAs per k-step, so the tensor pipe does "
+                                   "twice the algorithmic flops",
+                    "kernel": "RaBitQ full-code scan", "kernel_ms": scan_ms,
+                    "algorithmic_flops_per_launch": ops}
+            workload, dtype = RQ7_WORKLOAD, "7-bit codes as bf16, f32 dots, f32/f64 estimates"
+            l2note = "inputs larger than L2 (19.2 GB code values, 38 GB originals)"
+        else:
+            # INT8 MMAs over the code planes [127 b | b] against the integer
+            # query [h | l]: 2 x nq x n x (2 padded) integer ops.
+            ops = 2.0 * nq * (e - b) * (2 * padded)
+            achieved = ops / (scan_ms / 1000.0) / 1e12 if scan_ms > 0 else None
+            peak = 4500.0
+            roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOP/s",
+                    "frac": (achieved / peak) if achieved else None, "traffic": None,
+                    "peak_source": "nominal dense INT8 tensor (no measured INT8 figure); the "
+                                   "scan runs on tcgen05 kind::i8",
+                    "kernel": "RaBitQ code-plane scan", "kernel_ms": scan_ms,
+                    "algorithmic_int_ops_per_launch": ops}
+            workload, dtype = RQ_WORKLOAD, "1-bit codes as i8 planes, i32 dots, f32/f64 estimates"
+            l2note = "inputs larger than L2 (19.2 GB code planes, 38 GB originals)"
+        config = {"workload": workload, "global_batch": nq, "top_k": RQ_K, "base_vectors": n,
                   "dim": RQ_DIM, "metric": "l2", "clusters": RQ_NC, "ef": RQ_EF,
+                  "total_bits": total_bits,
                   "parallelism": f"rows sharded over {world} GPU(s), NCCL all-gather + merge",
-                  "l2": "inputs larger than L2 (19.2 GB code planes, 38 GB originals)"}
-        line = common_line(nq, ms, e2e_ms, args, world,
-                           "1-bit codes as i8 planes, i32 dots, f32/f64 estimates", config, roof,
-                           cpu, clocks, st, RQ_K, RQ_DIM, 4)
+                  "l2": l2note}
+        line = common_line(nq, ms, e2e_ms, args, world, dtype, config, roof, cpu, clocks, st,
+                           RQ_K, RQ_DIM, 4)
         if sweep is not None:
             line["batch_sweep"] = sweep
         print(json.dumps(line), flush=True)
     finish_ranks(world)
 
 
-def cpu_rabitq_qps(cents, signs, sample, queries, n_total):
+def cpu_rabitq_qps(cents, signs, sample, queries, n_total, total_bits=1, extra_scale=0.0):
     import numpy as np
 
     from oracle.oracle import L2, Oracle
     ora = Oracle()
-    codes, factors = ora.rabitq_encode1_batch(L2, cents, signs, sample)
+    codes, extra, factors = ora.rabitq_encode_batch(L2, cents, signs, sample, total_bits,
+                                                    extra_scale)
     keys = np.arange(sample.shape[0], dtype=np.uint64)
     threads = os.cpu_count() or 1
     t0 = time.perf_counter()
     ora.rabitq_search(L2, cents, signs, codes, factors, sample, keys, queries, RQ_K, RQ_EF,
-                      threads=threads)
+                      threads=threads, total_bits=total_bits, extra=extra)
     dt = time.perf_counter() - t0
     return {"value": queries.shape[0] / dt * sample.shape[0] / n_total, "unit": "queries/sec",
             "cores": threads, "kind": "port",
@@ -924,6 +955,8 @@ def main():
         return run_ivf_flat(args, sq8=True)
     if args.workload == "rabitq_l2_refine":
         return run_rabitq(args)
+    if args.workload == "rabitq7_l2_refine":
+        return run_rabitq(args, total_bits=RQ7_BITS)
 
     import numpy as np
     import torch
