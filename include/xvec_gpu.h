@@ -47,7 +47,8 @@ typedef enum {
   XVEC_GPU_OVERFLOW = 8,         /* ErrQuantizationOverflow / ErrPQScoreOverflow */
   XVEC_GPU_NOT_FOUND = 9,        /* ErrMissingRefineVector */
   XVEC_GPU_DUPLICATE_KEY = 10,   /* ErrDuplicateKey */
-  XVEC_GPU_UNSUPPORTED = 11      /* no sm_100a device / feature not available */
+  XVEC_GPU_UNSUPPORTED = 11,     /* no sm_100a device / feature not available */
+  XVEC_GPU_CHECKSUM_MISMATCH = 12 /* ErrIVFChecksumMismatch (ivf.go:736-738) */
 } xvec_gpu_status;
 
 typedef enum {
@@ -206,6 +207,47 @@ xvec_gpu_status xvec_gpu_index_search_device(xvec_gpu_index* index, const void* 
  * kmeans.go:169-175). */
 xvec_gpu_status xvec_gpu_ivf_set_model(xvec_gpu_index* index, const float* centroids,
                                        int32_t nlist);
+
+/* Rows with their IVF lists given (0 <= list < nlist) instead of the nearest
+ * centroid, for IVF_FLAT and IVF_SQ8 indexes with a model: the device upload
+ * of an IVF layout built elsewhere (IVFIndex.listForPosition, ivf.go:229,
+ * which streaming adds do not keep nearest-centroid).  Otherwise as
+ * xvec_gpu_index_add. */
+xvec_gpu_status xvec_gpu_ivf_add_with_lists(xvec_gpu_index* index, const uint64_t* keys,
+                                            const float* rows, const int32_t* lists, int64_t n);
+
+/* The header of a verified ZVECIVF version 1 file (IVFIndex.Save,
+ * ivf.go:866-904): rows, dimension, effective lists, metric, the build
+ * options and the training metadata. */
+typedef struct {
+  int64_t count;
+  int32_t dimension;
+  int32_t nlist;               /* effective lists (centroids in the file) */
+  int32_t metric;              /* xvec_gpu_metric: the same values as metric.Metric */
+  int32_t converged;
+  int64_t options_nlist;       /* IVFBuildOptions */
+  int64_t options_iterations;
+  int64_t options_workers;
+  uint64_t options_seed;
+  double options_tolerance;
+  double training_cost;
+  int64_t training_iterations;
+} xvec_gpu_ivf_file_header;
+
+/* Reads and verifies a ZVECIVF file on the host, as decodeIVFIndex
+ * (ivf.go:906-1057) does: magic, version (XVEC_GPU_UNSUPPORTED for another
+ * one), header fields and reserved zeros, the header and payload CRC32C
+ * (XVEC_GPU_CHECKSUM_MISMATCH), lengths, build options, training metadata,
+ * finite centroids and vectors, unique keys, list ranges
+ * (XVEC_GPU_INVALID_ARGUMENT for the rest).  No device work. */
+xvec_gpu_status xvec_gpu_ivf_file_info(const char* path, xvec_gpu_ivf_file_header* out);
+
+/* OpenIVFIndex (ivf.go:815-830) into a device index: an IVF_FLAT index on
+ * `device` with the file's metric and centroids, its rows at their file
+ * positions and each row in the list the file gives.  A file with no rows
+ * gives an index without a model (searching it reports the missing model;
+ * the reference returns no results). */
+xvec_gpu_status xvec_gpu_ivf_open(const char* path, int32_t device, xvec_gpu_index** out);
 
 /* k-means assignment: assignKMeans / assignKMeansCosine (kmeans.go:382-479):
  * for each vector the metric-best centroid (lower index wins ties) and its

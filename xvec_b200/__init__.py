@@ -39,9 +39,10 @@ STORAGE_FP32, STORAGE_FP16 = 1, 2
 STATUS_NAMES = {
     0: "OK", 1: "INVALID_ARGUMENT", 2: "OUT_OF_MEMORY", 3: "CANCELLED", 4: "TIMEOUT",
     5: "CUDA_ERROR", 6: "NCCL_ERROR", 7: "NON_FINITE", 8: "OVERFLOW", 9: "NOT_FOUND",
-    10: "DUPLICATE_KEY", 11: "UNSUPPORTED",
+    10: "DUPLICATE_KEY", 11: "UNSUPPORTED", 12: "CHECKSUM_MISMATCH",
 }
 OK, INVALID_ARGUMENT, NON_FINITE, DUPLICATE_KEY, UNSUPPORTED, CANCELLED = 0, 1, 7, 10, 11, 3
+NOT_FOUND, CHECKSUM_MISMATCH = 9, 12
 
 # Entry points of include/xvec_gpu.h (checked by the CPU test suite).
 EXPORTED_SYMBOLS = (
@@ -54,7 +55,8 @@ EXPORTED_SYMBOLS = (
     "xvec_gpu_index_search_noalloc", "xvec_gpu_index_reserve",
     "xvec_gpu_index_candidate_count", "xvec_gpu_index_candidates_device",
     "xvec_gpu_index_refine_device", "xvec_gpu_kmeans_train", "xvec_gpu_kmeans_train_device",
-    "xvec_gpu_ivf_set_model", "xvec_gpu_rabitq_set_model_bits",
+    "xvec_gpu_ivf_set_model", "xvec_gpu_rabitq_set_model_bits", "xvec_gpu_ivf_add_with_lists",
+    "xvec_gpu_ivf_file_info", "xvec_gpu_ivf_open",
 )
 
 
@@ -104,6 +106,9 @@ def _load() -> ctypes.CDLL:
     lib.xvec_gpu_ivfpq_set_model.argtypes = [vp, vp, i32, vp, i32]
     lib.xvec_gpu_rabitq_set_model.argtypes = [vp, vp, i32, vp]
     lib.xvec_gpu_rabitq_set_model_bits.argtypes = [vp, vp, i32, vp, i32, ctypes.c_double]
+    lib.xvec_gpu_ivf_add_with_lists.argtypes = [vp, vp, vp, vp, i64]
+    lib.xvec_gpu_ivf_file_info.argtypes = [ctypes.c_char_p, vp]
+    lib.xvec_gpu_ivf_open.argtypes = [ctypes.c_char_p, i32, vp]
     lib.xvec_gpu_ivf_set_model.argtypes = [vp, vp, i32]
     lib.xvec_gpu_index_search.argtypes = [vp, vp, i32, ctypes.POINTER(SearchOpts), vp, vp, vp]
     lib.xvec_gpu_index_search_device.argtypes = [vp, vp, i32, ctypes.POINTER(SearchOpts), vp,
@@ -367,6 +372,22 @@ class IVFPQIndex(_Index):
                                              _ptr(pivots), chunks))
 
 
+class IvfFileHeader(ctypes.Structure):
+    _fields_ = [("count", ctypes.c_int64), ("dimension", ctypes.c_int32),
+                ("nlist", ctypes.c_int32), ("metric", ctypes.c_int32),
+                ("converged", ctypes.c_int32), ("options_nlist", ctypes.c_int64),
+                ("options_iterations", ctypes.c_int64), ("options_workers", ctypes.c_int64),
+                ("options_seed", ctypes.c_uint64), ("options_tolerance", ctypes.c_double),
+                ("training_cost", ctypes.c_double), ("training_iterations", ctypes.c_int64)]
+
+
+def ivf_file_info(path: str) -> dict:
+    """The header of a verified ZVECIVF file (xvec_gpu_ivf_file_info)."""
+    h = IvfFileHeader()
+    _check(_lib.xvec_gpu_ivf_file_info(os.fsencode(path), ctypes.byref(h)))
+    return {name: getattr(h, name) for name, _ in IvfFileHeader._fields_}
+
+
 class IVFIndex(_Index):
     """core.IVFIndex (internal/core/ivf.go:214-597): probe the nprobe best
     centroids, exact-score the original rows of those lists."""
@@ -375,6 +396,34 @@ class IVFIndex(_Index):
     def set_model(self, centroids) -> None:
         centroids = np.ascontiguousarray(centroids, np.float32)
         _check(_lib.xvec_gpu_ivf_set_model(self._h, _ptr(centroids), centroids.shape[0]))
+
+    def add_with_lists(self, keys, vectors, lists) -> None:
+        """Rows with their lists given (xvec_gpu_ivf_add_with_lists)."""
+        keys = np.ascontiguousarray(keys, np.uint64)
+        vectors = np.ascontiguousarray(vectors, np.float32)
+        lists = np.ascontiguousarray(lists, np.int32)
+        if vectors.ndim != 2 or vectors.shape[1] != self.dimension or \
+                vectors.shape[0] != keys.size or lists.size != keys.size:
+            raise XvecGPUError(INVALID_ARGUMENT, "core: invalid vector dimension")
+        _check(_lib.xvec_gpu_ivf_add_with_lists(self._h, _ptr(keys), _ptr(vectors), _ptr(lists),
+                                                keys.size))
+
+    @classmethod
+    def open(cls, path: str, device: int = 0) -> "IVFIndex":
+        """OpenIVFIndex (ivf.go:815-830) onto the device (xvec_gpu_ivf_open);
+        the file holds an exact IVF index."""
+        if cls is not IVFIndex:
+            raise TypeError("a ZVECIVF file opens as an IVFIndex")
+        handle = ctypes.c_void_p()
+        _check(_lib.xvec_gpu_ivf_open(os.fsencode(path), device, ctypes.byref(handle)))
+        info = ivf_file_info(path)
+        self = cls.__new__(cls)
+        self._h = handle
+        self.dimension = info["dimension"]
+        self.metric = info["metric"]
+        self.storage = STORAGE_FP32
+        self.device = device
+        return self
 
 
 class ScalarQuantizedIVFIndex(IVFIndex):

@@ -193,6 +193,9 @@ struct xvec_gpu_index {
   // code values v = extra | sign bit << (TotalBits - 1) per padded coordinate
   // as 16-bit floats [n][padded] (bfloat16 up to 8 bits, binary16 for 9;
   // exact either way): the tensor-core operand and the exact scorer's input.
+  // IVF rows added with their lists given (xvec_gpu_ivf_add_with_lists): the
+  // batch's lists on the device while it is committed, else null.
+  const int32_t* given_lists = nullptr;
   int32_t rq_total_bits = 1;
   double rq_extra_scale = 0.0;
   xvec::DeviceBuffer rq_values;

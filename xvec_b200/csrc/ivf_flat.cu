@@ -211,9 +211,15 @@ xvec_gpu_status ivf_flat_reserve(xvec_gpu_index* idx, int64_t cap, cudaStream_t 
 
 xvec_gpu_status ivf_flat_commit(xvec_gpu_index* idx, int64_t old_n, int64_t m, cudaStream_t s) {
   const int d = idx->desc.dimension;
-  xvec_gpu_status st = assign_rows(idx->probe_index, idx->rows.as<float>() + old_n * d, m, d,
-                                   idx->row_list.as<int32_t>() + old_n, nullptr, s);
-  if (st) return st;
+  if (idx->given_lists) {
+    // Lists given by the caller (checked against nlist on the host).
+    XVEC_CUDA(cudaMemcpyAsync(idx->row_list.as<int32_t>() + old_n, idx->given_lists,
+                              (size_t)m * 4, cudaMemcpyDeviceToDevice, s));
+  } else {
+    const xvec_gpu_status st = assign_rows(idx->probe_index, idx->rows.as<float>() + old_n * d,
+                                           m, d, idx->row_list.as<int32_t>() + old_n, nullptr, s);
+    if (st) return st;
+  }
   idx->lists_dirty = true;
   return XVEC_GPU_OK;
 }
