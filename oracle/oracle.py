@@ -132,6 +132,14 @@ class Oracle:
                                           ctypes.c_int32, ctypes.c_float, ctypes.c_float, _u32p,
                                           ctypes.c_int32, _u64p, _f32p, _i32p, _i32p]
         lib.xo_pq_chunk_offsets.argtypes = [ctypes.c_int32, ctypes.c_int32, _i32p]
+        lib.xo_kmeans_train_init.argtypes = [ctypes.c_int, _f32p, ctypes.c_int64, ctypes.c_int32,
+                                             ctypes.c_int32, _f32p, ctypes.c_int32,
+                                             ctypes.c_double, ctypes.c_int32, _f32p, _i32p]
+        lib.xo_pq_kmc2.argtypes = [ctypes.c_int, _f32p, ctypes.c_int64, ctypes.c_int32,
+                                   ctypes.c_int32, ctypes.c_uint64, _f32p]
+        lib.xo_pq_train.argtypes = [ctypes.c_int, _f32p, ctypes.c_int64, ctypes.c_int32,
+                                    ctypes.c_int32, ctypes.c_int64, ctypes.c_int32,
+                                    ctypes.c_uint64, ctypes.c_int32, _f32p]
         lib.xo_pq_encode.argtypes = [ctypes.c_int, _f32p, _i32p, ctypes.c_int32, ctypes.c_int32,
                                      _f32p, _u8p]
         lib.xo_pq_distance_table.argtypes = [ctypes.c_int, _f32p, _i32p, ctypes.c_int32,
@@ -392,6 +400,40 @@ class Oracle:
                                         threads or os.cpu_count(), _ptr(ok, _u64p),
                                         _ptr(os_, _f32p), _ptr(oc, _i32p), _ptr(ost, _i32p))
         return st, ok.reshape(nq, k), os_.reshape(nq, k), oc, ost
+
+    def pq_kmc2(self, metric, vectors, clusters, seed):
+        """initializePQKMC2 (pq.go:410-459)."""
+        vectors = _c(vectors, np.float32)
+        n, d = vectors.shape
+        out = np.zeros((clusters, d), np.float32)
+        st = self.lib.xo_pq_kmc2(metric, _ptr(vectors, _f32p), n, d, clusters, seed,
+                                 _ptr(out, _f32p))
+        return st, out
+
+    def kmeans_train_init(self, metric, vectors, initial, iterations,
+                          tolerance=1.1920928955078125e-7, threads=0):
+        vectors = _c(vectors, np.float32)
+        initial = _c(initial, np.float32)
+        n, d = vectors.shape
+        kc = initial.shape[0]
+        cents = np.zeros((kc, d), np.float32)
+        labels = np.zeros(n, np.int32)
+        st = self.lib.xo_kmeans_train_init(metric, _ptr(vectors, _f32p), n, d, kc,
+                                           _ptr(initial, _f32p), iterations, tolerance,
+                                           threads or os.cpu_count(), _ptr(cents, _f32p),
+                                           _ptr(labels, _i32p))
+        return st, cents, labels
+
+    def pq_train(self, metric, vectors, chunks, max_train_samples=200_000, max_iterations=12,
+                 seed=0, threads=0):
+        """TrainPQ (pq.go:107-179): pivots [256][d]."""
+        vectors = _c(vectors, np.float32)
+        n, d = vectors.shape
+        pivots = np.zeros((256, d), np.float32)
+        st = self.lib.xo_pq_train(metric, _ptr(vectors, _f32p), n, d, chunks, max_train_samples,
+                                  max_iterations, seed, threads or os.cpu_count(),
+                                  _ptr(pivots, _f32p))
+        return st, pivots
 
     def pq_chunk_offsets(self, d, chunks):
         out = np.zeros(chunks + 1, np.int32)

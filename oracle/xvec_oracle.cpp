@@ -935,17 +935,11 @@ extern "C" int xo_kmeans_assign(int metric, const float* vectors, int64_t n,
 // trainKMeansWithAssignments (kmeans.go:208-298) with the default options of
 // DefaultKMeansOptions (kmeans.go:83-92): reservoir initialisation,
 // EmptyReseedFarthest, non-spherical; LloydUpdate (lloyd_cluster.go:53-138).
-extern "C" int xo_kmeans_train(int metric, const float* vectors, int64_t n, int32_t d,
-                               int32_t clusters, int32_t max_iterations, double tolerance,
-                               uint64_t seed, int32_t threads, float* centroids_out,
-                               int32_t* clusters_out, int32_t* labels_out) {
-  if (n <= 0 || d <= 0 || clusters <= 0 || max_iterations <= 0) return XO_INVALID_ARGUMENT;
-  int32_t kc = (int32_t)std::min<int64_t>(clusters, n);
-  std::vector<int64_t> idx(kc);
-  xo_kmeans_reservoir(n, kc, seed, idx.data());
-  std::vector<float> cents((size_t)kc * d);
-  for (int32_t c = 0; c < kc; ++c)
-    std::memcpy(&cents[(size_t)c * d], vectors + idx[c] * d, sizeof(float) * d);
+// Lloyd iterations of TrainKMeans (kmeans.go:240-298) from kc initial
+// centroids (cents, updated in place).
+static int kmeans_lloyd(int metric, const float* vectors, int64_t n, int32_t d, int32_t kc,
+                        std::vector<float>& cents, int32_t max_iterations, double tolerance,
+                        int32_t threads, float* centroids_out, int32_t* labels_out) {
   std::vector<int32_t> labels(n);
   std::vector<float> scores(n);
   double previous = 0;
@@ -997,7 +991,133 @@ extern "C" int xo_kmeans_train(int metric, const float* vectors, int64_t n, int3
                             scores.data());
   if (st != XO_OK) return st;
   std::memcpy(centroids_out, cents.data(), sizeof(float) * cents.size());
+  return XO_OK;
+}
+
+extern "C" int xo_kmeans_train(int metric, const float* vectors, int64_t n, int32_t d,
+                               int32_t clusters, int32_t max_iterations, double tolerance,
+                               uint64_t seed, int32_t threads, float* centroids_out,
+                               int32_t* clusters_out, int32_t* labels_out) {
+  if (n <= 0 || d <= 0 || clusters <= 0 || max_iterations <= 0) return XO_INVALID_ARGUMENT;
+  int32_t kc = (int32_t)std::min<int64_t>(clusters, n);
+  std::vector<int64_t> idx(kc);
+  xo_kmeans_reservoir(n, kc, seed, idx.data());
+  std::vector<float> cents((size_t)kc * d);
+  for (int32_t c = 0; c < kc; ++c)
+    std::memcpy(&cents[(size_t)c * d], vectors + idx[c] * d, sizeof(float) * d);
+  int st = kmeans_lloyd(metric, vectors, n, d, kc, cents, max_iterations, tolerance, threads,
+                        centroids_out, labels_out);
+  if (st != XO_OK) return st;
   *clusters_out = kc;
+  return XO_OK;
+}
+
+// TrainKMeans with KMeansOptions.InitialCentroids (kmeans.go:354-363): kc =
+// min(clusters, n) given centroids, then the Lloyd iterations.
+extern "C" int xo_kmeans_train_init(int metric, const float* vectors, int64_t n, int32_t d,
+                                    int32_t kc, const float* initial, int32_t max_iterations,
+                                    double tolerance, int32_t threads, float* centroids_out,
+                                    int32_t* labels_out) {
+  if (n <= 0 || d <= 0 || kc <= 0 || kc > n || max_iterations <= 0) return XO_INVALID_ARGUMENT;
+  std::vector<float> cents(initial, initial + (size_t)kc * d);
+  for (float v : cents)
+    if (!finite32(v)) return XO_INVALID_ARGUMENT;
+  return kmeans_lloyd(metric, vectors, n, d, kc, cents, max_iterations, tolerance, threads,
+                      centroids_out, labels_out);
+}
+
+// splitMix64.float64 (kmeans.go:630-632).
+static double splitmix_float64(uint64_t* state) {
+  return (double)(xo_splitmix64_next(state) >> 11) * (1.0 / 9007199254740992.0);
+}
+
+// pqUniformSampleIndices (pq.go:461-476): `sample` of `count` indices in
+// increasing order, index i kept with odds remaining / (count - i).
+static std::vector<int64_t> pq_uniform_sample(int64_t count, int64_t sample, uint64_t* state) {
+  std::vector<int64_t> out;
+  int64_t remaining = sample;
+  for (int64_t i = 0; i < count && remaining > 0; ++i)
+    if (splitmix_intn(state, count - i) < remaining) {
+      out.push_back(i);
+      --remaining;
+    }
+  return out;
+}
+
+// initializePQKMC2 (pq.go:410-459): the first centroid uniformly, then each
+// next one by a Markov chain over min(32, n) uniform candidates scored by
+// their nearest centroid (metric.Compute; IP negated), accepting a candidate
+// when the current score is 0 or score * float32(U) < candidate score.
+extern "C" int xo_pq_kmc2(int metric, const float* vectors, int64_t n, int32_t d,
+                          int32_t clusters, uint64_t seed, float* centroids_out) {
+  if (clusters <= 0 || clusters > n) return XO_INVALID_ARGUMENT;
+  uint64_t state = seed;
+  std::vector<int64_t> first = pq_uniform_sample(n, 1, &state);
+  std::vector<const float*> chosen{vectors + first[0] * d};
+  while ((int32_t)chosen.size() < clusters) {
+    std::vector<int64_t> cand = pq_uniform_sample(n, std::min<int64_t>(32, n), &state);
+    std::vector<float> scores(cand.size());
+    for (size_t ci = 0; ci < cand.size(); ++ci) {
+      float best = 3.40282346638528859811704183484516925440e+38f;
+      for (const float* c : chosen) {
+        float sc;
+        int st = xo_metric_compute(metric, c, vectors + cand[ci] * d, d, &sc);
+        if (st != XO_OK) return st;
+        if (metric == XO_IP) sc = -sc;
+        if (sc < best) best = sc;
+      }
+      scores[ci] = best;
+    }
+    float sel_score = scores[0];
+    size_t sel = 0;
+    for (size_t ci = 1; ci < scores.size(); ++ci) {
+      // The draw happens only when the current score is not 0 (|| short-circuits).
+      if (sel_score == 0 || sel_score * (float)splitmix_float64(&state) < scores[ci]) {
+        sel_score = scores[ci];
+        sel = ci;
+      }
+    }
+    chosen.push_back(vectors + cand[sel] * d);
+  }
+  for (int32_t c = 0; c < clusters; ++c)
+    std::memcpy(centroids_out + (int64_t)c * d, chosen[c], sizeof(float) * d);
+  return XO_OK;
+}
+
+// TrainPQ (pq.go:107-179): per contiguous chunk (pqChunkOffsets), the first
+// min(n, max_train_samples) rows' sub-vectors, KMC2 seeding and TrainKMeans
+// with 256 clusters, seed ^ (0x70716b6d00000000 + chunk), max_iterations and
+// the default tolerance; pivots [256][d] centroid-major, rows past the
+// trained centroids repeating centroid 0.
+extern "C" int xo_pq_train(int metric, const float* vectors, int64_t n, int32_t d, int32_t chunks,
+                           int64_t max_train_samples, int32_t max_iterations, uint64_t seed,
+                           int32_t threads, float* pivots_out) {
+  if (n <= 0 || d <= 0 || chunks <= 0 || chunks > d || max_train_samples <= 0 ||
+      max_iterations <= 0 || (metric != XO_L2 && metric != XO_IP))
+    return XO_INVALID_ARGUMENT;
+  std::vector<int32_t> offsets(chunks + 1);
+  xo_pq_chunk_offsets(d, chunks, offsets.data());
+  const int64_t samples = std::min<int64_t>(n, max_train_samples);
+  for (int32_t chunk = 0; chunk < chunks; ++chunk) {
+    const int32_t start = offsets[chunk], width = offsets[chunk + 1] - offsets[chunk];
+    std::vector<float> training((size_t)samples * width);
+    for (int64_t i = 0; i < samples; ++i)
+      std::memcpy(&training[(size_t)i * width], vectors + i * d + start, sizeof(float) * width);
+    const uint64_t cseed = seed ^ (0x70716b6d00000000ULL + (uint64_t)chunk);
+    const int32_t kc = (int32_t)std::min<int64_t>(256, samples);
+    std::vector<float> init((size_t)kc * width), cents((size_t)kc * width);
+    std::vector<int32_t> labels(samples);
+    int st = xo_pq_kmc2(metric, training.data(), samples, width, kc, cseed, init.data());
+    if (st != XO_OK) return st;
+    st = xo_kmeans_train_init(metric, training.data(), samples, width, kc, init.data(),
+                              max_iterations, 1.1920928955078125e-7, threads, cents.data(),
+                              labels.data());
+    if (st != XO_OK) return st;
+    for (int32_t c = 0; c < 256; ++c) {
+      const float* src = &cents[(size_t)(c < kc ? c : 0) * width];
+      std::memcpy(pivots_out + (int64_t)c * d + start, src, sizeof(float) * width);
+    }
+  }
   return XO_OK;
 }
 

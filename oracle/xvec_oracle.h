@@ -132,7 +132,19 @@ int xo_ivf_sq8_search(int metric, const int8_t* codes, const xo_sq_params* param
                       const uint32_t* filter_bitmap, int32_t threads, uint64_t* out_keys,
                       float* out_scores, int32_t* out_counts, int32_t* out_status);
 
+/* TrainKMeans with InitialCentroids (kmeans.go:354-363): kc given centroids. */
+int xo_kmeans_train_init(int metric, const float* vectors, int64_t n, int32_t d, int32_t kc,
+                         const float* initial, int32_t max_iterations, double tolerance,
+                         int32_t threads, float* centroids_out, int32_t* labels_out);
+
 /* ---- Product quantization (internal/core/pq.go) ------------------------ */
+/* initializePQKMC2 (pq.go:410-459). */
+int xo_pq_kmc2(int metric, const float* vectors, int64_t n, int32_t d, int32_t clusters,
+               uint64_t seed, float* centroids_out);
+/* TrainPQ (pq.go:107-179): pivots [256][d]. */
+int xo_pq_train(int metric, const float* vectors, int64_t n, int32_t d, int32_t chunks,
+                int64_t max_train_samples, int32_t max_iterations, uint64_t seed,
+                int32_t threads, float* pivots_out);
 void xo_pq_chunk_offsets(int32_t d, int32_t chunks, int32_t* offsets);
 int xo_pq_encode(int metric, const float* pivots, const int32_t* offsets, int32_t chunks,
                  int32_t d, const float* v, uint8_t* code);

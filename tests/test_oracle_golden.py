@@ -332,3 +332,34 @@ def test_rabitq_full_estimate(oracle, metric):
         truth = ((rows - q) ** 2).sum(1) if metric == L2 else 1.0 - rows @ q
         errs[tb] = np.abs(est - truth).mean()
     assert errs[7] < errs[4] < errs[1], errs
+
+
+def test_pq_kmc2_seed_fixture(oracle):
+    """TestPQKMC2SeedFixture (pq_test.go:59-66)."""
+    st, cents = oracle.pq_kmc2(L2, np.arange(6, dtype=np.float32)[:, None], 3, 0)
+    assert st == OK
+    assert cents[:, 0].tolist() == [1.0, 5.0, 3.0]
+
+
+def test_pq_train_prefix_and_padding(oracle):
+    """TrainPQ (pq.go:107-179): the codebook depends only on the first
+    MaxTrainSamples rows; each chunk is KMC2-seeded k-means with its own seed;
+    with fewer than 256 samples the remaining pivots repeat centroid 0."""
+    rng = np.random.default_rng(2)
+    v = rng.standard_normal((700, 8)).astype(np.float32)
+    st, a = oracle.pq_train(L2, v, 4, max_train_samples=500, max_iterations=5, seed=9)
+    assert st == OK
+    w = v.copy()
+    w[500:] = rng.standard_normal((200, 8))
+    st, b = oracle.pq_train(L2, w, 4, max_train_samples=500, max_iterations=5, seed=9)
+    assert st == OK and np.array_equal(a, b)
+    offsets = oracle.pq_chunk_offsets(8, 4)
+    for c in range(4):
+        lo, hi = offsets[c], offsets[c + 1]
+        seed = 9 ^ (0x70716b6d00000000 + c)
+        st, init = oracle.pq_kmc2(L2, v[:500, lo:hi], 256, seed)
+        st, cents, _ = oracle.kmeans_train_init(L2, v[:500, lo:hi], init, 5)
+        assert np.array_equal(a[:, lo:hi], cents)
+    st, small = oracle.pq_train(IP, v[:100], 4, max_iterations=3, seed=1)
+    assert st == OK
+    assert np.array_equal(small[100:], np.repeat(small[:1], 156, axis=0))
