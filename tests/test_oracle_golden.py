@@ -363,3 +363,23 @@ def test_pq_train_prefix_and_padding(oracle):
     st, small = oracle.pq_train(IP, v[:100], 4, max_iterations=3, seed=1)
     assert st == OK
     assert np.array_equal(small[100:], np.repeat(small[:1], 156, axis=0))
+
+
+@pytest.mark.parametrize("metric", [L2, IP, COSINE, MIPSL2])
+def test_ivf_full_probe_matches_flat(oracle, metric):
+    """TestIVFFullProbeMatchesFlat (ivf_test.go:324-345): probing every list
+    returns exactly the Flat top-k (cosine with cached magnitudes included)."""
+    keys = np.array([9, 2, 7, 4, 1, 8], np.uint64)
+    vecs = np.array([[-2, 1, 0], [1, 0, 2], [0, 3, -1], [2, 2, 2], [-1, -1, 1], [4, 0, -2]],
+                    np.float32)
+    q = np.array([[1, 2, 0.5]], np.float32)
+    cents = vecs[[0, 2, 5]].copy()
+    st, labels, _ = oracle.kmeans_assign(metric, vecs, cents)
+    assert st == OK
+    offsets = np.cumsum(np.concatenate([[0], np.bincount(labels, minlength=3)])).astype(np.int64)
+    positions = np.argsort(labels, kind="stable").astype(np.int64)
+    _, ik, isc, ic, _ = oracle.ivf_flat_search(metric, vecs, keys, cents, offsets, positions, q, 6, 3)
+    _, fk, fs, fc, _ = oracle.flat_search(metric, vecs, keys, q, 6)
+    assert ic[0] == fc[0] == 6
+    assert np.array_equal(ik, fk)
+    assert np.array_equal(isc.view(np.uint32), fs.view(np.uint32))
