@@ -283,6 +283,38 @@ xvec_gpu_status xvec_gpu_kmeans_train_device(int32_t device, int32_t metric,
                                              int32_t* out_iterations, int32_t* out_converged,
                                              double* out_cost, void* stream);
 
+/* k-means training from given initial centroids: TrainKMeans with
+ * KMeansOptions.InitialCentroids (kmeans.go:354-363), the Lloyd iterations
+ * above started from d_initial [kc*dim] (1 <= kc <= n, all finite) instead of
+ * the reservoir sample.  Device memory; d_centroids [kc*dim], d_labels [n]. */
+xvec_gpu_status xvec_gpu_kmeans_train_init_device(
+    int32_t device, int32_t metric, const float* d_vectors, int64_t n, int32_t dim, int32_t kc,
+    const float* d_initial, int32_t max_iterations, double tolerance, float* d_centroids,
+    int32_t* d_labels, int32_t* out_iterations, int32_t* out_converged, double* out_cost,
+    void* stream);
+
+/* Product-quantizer training: TrainPQ (pq.go:107-179) with PQOptions{Metric,
+ * Chunks, MaxTrainSamples, MaxIterations, Seed}.  chunks 0 resolves to
+ * dim / 2; metric L2 or inner product.  Per contiguous chunk of the first
+ * min(n, max_train_samples) rows: KMC2 seeding (initializePQKMC2,
+ * pq.go:410-459), then TrainKMeans with those initial centroids, 256
+ * clusters, seed ^ (0x70716b6d00000000 + chunk) and the default tolerance.
+ * Writes PQModelState: chunk_offsets_out [chunks+1] (host, may be NULL) and
+ * pivots [256*dim] centroid-major, rows past the trained centroids repeating
+ * centroid 0; *out_chunks the resolved chunk count.  Bit-identical pivots.
+ * vectors and pivots are host memory (every row is validated finite, the
+ * training sample alone is copied to the device). */
+xvec_gpu_status xvec_gpu_pq_train(int32_t device, int32_t metric, const float* vectors,
+                                  int64_t n, int32_t dim, int32_t chunks,
+                                  int64_t max_train_samples, int32_t max_iterations,
+                                  uint64_t seed, int32_t* chunk_offsets_out, float* pivots,
+                                  int32_t* out_chunks);
+xvec_gpu_status xvec_gpu_pq_train_device(int32_t device, int32_t metric, const float* d_vectors,
+                                         int64_t n, int32_t dim, int32_t chunks,
+                                         int64_t max_train_samples, int32_t max_iterations,
+                                         uint64_t seed, int32_t* chunk_offsets_out,
+                                         float* d_pivots, int32_t* out_chunks, void* stream);
+
 /* Cross-shard merge: MergeSearchResults (query.go:154-191) of `parts` result
  * lists per query, as produced by xvec_gpu_index_search_device on each shard
  * (layout [parts][nq][top_k] keys/scores and [parts][nq] counts, all device

@@ -56,7 +56,8 @@ EXPORTED_SYMBOLS = (
     "xvec_gpu_index_candidate_count", "xvec_gpu_index_candidates_device",
     "xvec_gpu_index_refine_device", "xvec_gpu_kmeans_train", "xvec_gpu_kmeans_train_device",
     "xvec_gpu_ivf_set_model", "xvec_gpu_rabitq_set_model_bits", "xvec_gpu_ivf_add_with_lists",
-    "xvec_gpu_ivf_file_info", "xvec_gpu_ivf_open",
+    "xvec_gpu_ivf_file_info", "xvec_gpu_ivf_open", "xvec_gpu_kmeans_train_init_device",
+    "xvec_gpu_pq_train", "xvec_gpu_pq_train_device",
 )
 
 
@@ -125,6 +126,12 @@ def _load() -> ctypes.CDLL:
     lib.xvec_gpu_kmeans_train_device.argtypes = [i32, i32, vp, i64, i32, i32, i32,
                                                  ctypes.c_double, ctypes.c_uint64, vp, vp, vp,
                                                  vp, vp, vp, vp]
+    lib.xvec_gpu_kmeans_train_init_device.argtypes = [i32, i32, vp, i64, i32, i32, vp, i32,
+                                                      ctypes.c_double, vp, vp, vp, vp, vp, vp]
+    lib.xvec_gpu_pq_train.argtypes = [i32, i32, vp, i64, i32, i32, i64, i32, ctypes.c_uint64,
+                                      vp, vp, vp]
+    lib.xvec_gpu_pq_train_device.argtypes = [i32, i32, vp, i64, i32, i32, i64, i32,
+                                             ctypes.c_uint64, vp, vp, vp, vp]
     lib.xvec_gpu_index_candidate_count.restype = i32
     lib.xvec_gpu_index_candidate_count.argtypes = [vp, ctypes.POINTER(SearchOpts)]
     lib.xvec_gpu_index_candidates_device.argtypes = [vp, vp, i32, ctypes.POINTER(SearchOpts), vp,
@@ -510,6 +517,45 @@ def kmeans_train_device(device: int, metric: int, vectors_ptr: int, n: int, dim:
                                              ctypes.byref(out, 4), ctypes.byref(out, 8),
                                              ctypes.byref(cost), stream or None))
     return int(out[0]), int(out[1]), bool(out[2]), float(cost.value)
+
+
+def kmeans_train_init_device(device: int, metric: int, vectors_ptr: int, n: int, dim: int,
+                             kc: int, initial_ptr: int, centroids_ptr: int, labels_ptr: int,
+                             iterations: int = 10, tolerance: float = 1.1920928955078125e-7,
+                             stream: int = 0):
+    """xvec_gpu_kmeans_train_init_device: TrainKMeans from kc given initial
+    centroids (kmeans.go:354-363), device memory in and out; returns
+    (iterations, converged, cost)."""
+    out = (ctypes.c_int32 * 2)()
+    cost = ctypes.c_double()
+    _check(_lib.xvec_gpu_kmeans_train_init_device(device, metric, vectors_ptr, n, dim, kc,
+                                                  initial_ptr, iterations, tolerance,
+                                                  centroids_ptr, labels_ptr,
+                                                  ctypes.byref(out, 0), ctypes.byref(out, 4),
+                                                  ctypes.byref(cost), stream or None))
+    return int(out[0]), bool(out[1]), float(cost.value)
+
+
+PQ_CENTROIDS = 256
+
+
+def pq_train(metric: int, vectors, chunks: int = 0, max_train_samples: int = 200_000,
+             max_iterations: int = 12, seed: int = 0, device: int = 0):
+    """TrainPQ (pq.go:107-179) on the GPU: PQOptions{Metric, Chunks,
+    MaxTrainSamples, MaxIterations, Seed}; chunks 0 means dim // 2.  Returns
+    PQModelState's (chunk_offsets [chunks + 1], pivots [256, dim]), ready for
+    IVFPQIndex.set_model."""
+    vectors = np.ascontiguousarray(vectors, np.float32)
+    if vectors.ndim != 2:
+        raise ValueError("vectors must be [n, dim]")
+    n, d = vectors.shape
+    offsets = np.zeros(max(chunks if chunks > 0 else d // 2, 1) + 1, np.int32)
+    pivots = np.zeros((PQ_CENTROIDS, max(d, 1)), np.float32)
+    resolved = ctypes.c_int32()
+    _check(_lib.xvec_gpu_pq_train(device, metric, _ptr(vectors), n, d, chunks, max_train_samples,
+                                  max_iterations, seed, _ptr(offsets), _ptr(pivots),
+                                  ctypes.byref(resolved)))
+    return offsets[:resolved.value + 1].copy(), pivots
 
 
 def merge_results_device(device: int, metric: int, top_k: int, nq: int, parts: int, keys_ptr: int,

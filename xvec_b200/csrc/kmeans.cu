@@ -104,55 +104,17 @@ inline unsigned blocks_of(int64_t n, int t = 256) { return (unsigned)((n + t - 1
 
 using namespace xvec;
 
-extern "C" xvec_gpu_status xvec_gpu_kmeans_train_device(
-    int32_t device, int32_t metric, const float* d_vectors, int64_t n, int32_t dim,
-    int32_t clusters, int32_t max_iterations, double tolerance, uint64_t seed,
-    float* d_centroids, int32_t* d_labels, int32_t* out_clusters, int32_t* out_iterations,
-    int32_t* out_converged, double* out_cost, void* stream) {
-  if (metric < XVEC_METRIC_L2 || metric > XVEC_METRIC_MIPSL2)
-    return set_error("core: invalid k-means options: invalid metric"), XVEC_GPU_INVALID_ARGUMENT;
-  if (clusters <= 0)
-    return set_error("core: invalid k-means options: Clusters must be positive"),
-           XVEC_GPU_INVALID_ARGUMENT;
-  if (max_iterations <= 0)
-    return set_error("core: invalid k-means options: MaxIterations must be positive"),
-           XVEC_GPU_INVALID_ARGUMENT;
-  if (!(tolerance >= 0) || std::isinf(tolerance))
-    return set_error("core: invalid k-means options: Tolerance must be finite and non-negative"),
-           XVEC_GPU_INVALID_ARGUMENT;
-  if (n <= 0) return set_error("core: empty k-means training set"), XVEC_GPU_INVALID_ARGUMENT;
-  if (dim <= 0 || n > 0x7fffffffll || !d_vectors || !d_centroids || !d_labels)
-    return set_error("invalid k-means arguments"), XVEC_GPU_INVALID_ARGUMENT;
-  cudaSetDevice(device);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
+// The Lloyd iterations of trainKMeansWithAssignments (kmeans.go:240-298)
+// from kc initial centroids (device, [kc][d]).
+static xvec_gpu_status lloyd_train(int32_t device, int32_t metric, const float* d_vectors,
+                                   int64_t n, int d, int kc, const float* d_initial,
+                                   int32_t max_iterations, double tolerance, float* d_centroids,
+                                   int32_t* d_labels, int32_t* out_iterations,
+                                   int32_t* out_converged, double* out_cost, cudaStream_t s) {
   xvec_gpu_status st;
-  const int d = dim;
-  {
-    Scratch bad;
-    if ((st = bad.alloc(4, s))) return st;
-    XVEC_CUDA(cudaMemsetAsync(bad.ptr, 0, 4, s));
-    finite_check_kernel<<<blocks_of(n * d), 256, 0, s>>>(d_vectors, n * d, bad.as<int>());
-    XVEC_LAUNCHED();
-    int h = 0;
-    XVEC_CUDA(cudaMemcpyAsync(&h, bad.ptr, 4, cudaMemcpyDeviceToHost, s));
-    XVEC_CUDA(cudaStreamSynchronize(s));
-    if (h) return set_error("ailego: vector contains a non-finite value"), XVEC_GPU_NON_FINITE;
-  }
-  const int kc = (int)std::min<int64_t>(clusters, n);
-  // InitializeReservoir.
-  std::vector<int64_t> init(kc);
-  {
-    uint64_t state = seed;
-    for (int i = 0; i < kc; ++i) init[i] = i;
-    for (int64_t i = kc; i < n; ++i) {
-      const int64_t sel = splitmix_intn(&state, i + 1);
-      if (sel < kc) init[sel] = i;
-    }
-  }
-  Scratch cents_a, cents_b, init_rows, scores, counts, offsets, members, iota, sorted_labels,
-      temp;
+  Scratch cents_a, cents_b, scores, counts, offsets, members, iota, sorted_labels, temp;
   if ((st = cents_a.alloc((size_t)kc * d * 4, s)) || (st = cents_b.alloc((size_t)kc * d * 4, s)) ||
-      (st = init_rows.alloc((size_t)kc * 8, s)) || (st = scores.alloc((size_t)n * 4, s)) ||
+      (st = scores.alloc((size_t)n * 4, s)) ||
       (st = counts.alloc((size_t)(kc + 1) * 8, s)) ||
       (st = offsets.alloc((size_t)(kc + 1) * 8, s)) || (st = members.alloc((size_t)n * 4, s)) ||
       (st = iota.alloc((size_t)n * 4, s)) || (st = sorted_labels.alloc((size_t)n * 4, s)))
@@ -160,9 +122,7 @@ extern "C" xvec_gpu_status xvec_gpu_kmeans_train_device(
   // The current centroids and the next ones (swapped after each update).
   float* cents = cents_a.as<float>();
   float* next = cents_b.as<float>();
-  XVEC_CUDA(cudaMemcpyAsync(init_rows.ptr, init.data(), (size_t)kc * 8, cudaMemcpyHostToDevice, s));
-  gather_rows_kernel<<<kc, 128, 0, s>>>(d_vectors, d, init_rows.as<int64_t>(), kc, cents);
-  XVEC_LAUNCHED();
+  XVEC_CUDA(cudaMemcpyAsync(cents, d_initial, (size_t)kc * d * 4, cudaMemcpyDeviceToDevice, s));
   iota_kernel<<<blocks_of(n), 256, 0, s>>>(iota.as<uint32_t>(), n);
   XVEC_LAUNCHED();
   int bits = 1;
@@ -244,11 +204,109 @@ extern "C" xvec_gpu_status xvec_gpu_kmeans_train_device(
   XVEC_CUDA(cudaMemcpyAsync(h_scores.data(), scores.ptr, (size_t)n * 4, cudaMemcpyDeviceToHost,
                             s));
   XVEC_CUDA(cudaStreamSynchronize(s));
-  if (out_clusters) *out_clusters = kc;
   if (out_iterations) *out_iterations = iterations;
   if (out_converged) *out_converged = converged ? 1 : 0;
   if (out_cost) *out_cost = objective();
   return XVEC_GPU_OK;
+}
+
+extern "C" xvec_gpu_status xvec_gpu_kmeans_train_device(
+    int32_t device, int32_t metric, const float* d_vectors, int64_t n, int32_t dim,
+    int32_t clusters, int32_t max_iterations, double tolerance, uint64_t seed,
+    float* d_centroids, int32_t* d_labels, int32_t* out_clusters, int32_t* out_iterations,
+    int32_t* out_converged, double* out_cost, void* stream) {
+  if (metric < XVEC_METRIC_L2 || metric > XVEC_METRIC_MIPSL2)
+    return set_error("core: invalid k-means options: invalid metric"), XVEC_GPU_INVALID_ARGUMENT;
+  if (clusters <= 0)
+    return set_error("core: invalid k-means options: Clusters must be positive"),
+           XVEC_GPU_INVALID_ARGUMENT;
+  if (max_iterations <= 0)
+    return set_error("core: invalid k-means options: MaxIterations must be positive"),
+           XVEC_GPU_INVALID_ARGUMENT;
+  if (!(tolerance >= 0) || std::isinf(tolerance))
+    return set_error("core: invalid k-means options: Tolerance must be finite and non-negative"),
+           XVEC_GPU_INVALID_ARGUMENT;
+  if (n <= 0) return set_error("core: empty k-means training set"), XVEC_GPU_INVALID_ARGUMENT;
+  if (dim <= 0 || n > 0x7fffffffll || !d_vectors || !d_centroids || !d_labels)
+    return set_error("invalid k-means arguments"), XVEC_GPU_INVALID_ARGUMENT;
+  cudaSetDevice(device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  xvec_gpu_status st;
+  const int d = dim;
+  {
+    Scratch bad;
+    if ((st = bad.alloc(4, s))) return st;
+    XVEC_CUDA(cudaMemsetAsync(bad.ptr, 0, 4, s));
+    finite_check_kernel<<<blocks_of(n * d), 256, 0, s>>>(d_vectors, n * d, bad.as<int>());
+    XVEC_LAUNCHED();
+    int h = 0;
+    XVEC_CUDA(cudaMemcpyAsync(&h, bad.ptr, 4, cudaMemcpyDeviceToHost, s));
+    XVEC_CUDA(cudaStreamSynchronize(s));
+    if (h) return set_error("ailego: vector contains a non-finite value"), XVEC_GPU_NON_FINITE;
+  }
+  const int kc = (int)std::min<int64_t>(clusters, n);
+  // InitializeReservoir.
+  std::vector<int64_t> init(kc);
+  {
+    uint64_t state = seed;
+    for (int i = 0; i < kc; ++i) init[i] = i;
+    for (int64_t i = kc; i < n; ++i) {
+      const int64_t sel = splitmix_intn(&state, i + 1);
+      if (sel < kc) init[sel] = i;
+    }
+  }
+  Scratch init_rows, initial;
+  if ((st = init_rows.alloc((size_t)kc * 8, s)) || (st = initial.alloc((size_t)kc * d * 4, s)))
+    return st;
+  XVEC_CUDA(cudaMemcpyAsync(init_rows.ptr, init.data(), (size_t)kc * 8, cudaMemcpyHostToDevice, s));
+  gather_rows_kernel<<<kc, 128, 0, s>>>(d_vectors, d, init_rows.as<int64_t>(), kc,
+                                        initial.as<float>());
+  XVEC_LAUNCHED();
+  if (out_clusters) *out_clusters = kc;
+  return lloyd_train(device, metric, d_vectors, n, d, kc, initial.as<float>(), max_iterations,
+                     tolerance, d_centroids, d_labels, out_iterations, out_converged, out_cost, s);
+}
+
+extern "C" xvec_gpu_status xvec_gpu_kmeans_train_init_device(
+    int32_t device, int32_t metric, const float* d_vectors, int64_t n, int32_t dim, int32_t kc,
+    const float* d_initial, int32_t max_iterations, double tolerance, float* d_centroids,
+    int32_t* d_labels, int32_t* out_iterations, int32_t* out_converged, double* out_cost,
+    void* stream) {
+  if (metric < XVEC_METRIC_L2 || metric > XVEC_METRIC_MIPSL2)
+    return set_error("core: invalid k-means options: invalid metric"), XVEC_GPU_INVALID_ARGUMENT;
+  if (max_iterations <= 0)
+    return set_error("core: invalid k-means options: MaxIterations must be positive"),
+           XVEC_GPU_INVALID_ARGUMENT;
+  if (!(tolerance >= 0) || std::isinf(tolerance))
+    return set_error("core: invalid k-means options: Tolerance must be finite and non-negative"),
+           XVEC_GPU_INVALID_ARGUMENT;
+  if (n <= 0) return set_error("core: empty k-means training set"), XVEC_GPU_INVALID_ARGUMENT;
+  if (kc <= 0 || kc > n)
+    return set_error("core: invalid centroid: got %d initial centroids, want %lld", kc,
+                     (long long)std::min<int64_t>(kc, n)),
+           XVEC_GPU_INVALID_ARGUMENT;
+  if (dim <= 0 || n > 0x7fffffffll || !d_vectors || !d_initial || !d_centroids || !d_labels)
+    return set_error("invalid k-means arguments"), XVEC_GPU_INVALID_ARGUMENT;
+  cudaSetDevice(device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  xvec_gpu_status st;
+  {
+    Scratch bad;
+    if ((st = bad.alloc(4, s))) return st;
+    XVEC_CUDA(cudaMemsetAsync(bad.ptr, 0, 4, s));
+    finite_check_kernel<<<blocks_of(n * dim), 256, 0, s>>>(d_vectors, n * dim, bad.as<int>());
+    XVEC_LAUNCHED();
+    finite_check_kernel<<<blocks_of((int64_t)kc * dim), 256, 0, s>>>(d_initial,
+                                                                    (int64_t)kc * dim,
+                                                                    bad.as<int>());
+    XVEC_LAUNCHED();
+    int h = 0;
+    XVEC_CUDA(cudaMemcpyAsync(&h, bad.ptr, 4, cudaMemcpyDeviceToHost, s));
+    XVEC_CUDA(cudaStreamSynchronize(s));
+    if (h) return set_error("ailego: vector contains a non-finite value"), XVEC_GPU_NON_FINITE;
+  }
+  return lloyd_train(device, metric, d_vectors, n, dim, kc, d_initial, max_iterations, tolerance,
+                     d_centroids, d_labels, out_iterations, out_converged, out_cost, s);
 }
 
 extern "C" xvec_gpu_status xvec_gpu_kmeans_train(int32_t device, int32_t metric,
