@@ -78,7 +78,13 @@ typedef enum {
    * core.ScalarQuantizedIVFIndex (internal/core/ivf_quantized.go:23-192): the
    * IVF probe with the original metric, the SQ8_FLAT scoring of the probed
    * positions (quantized_index.go:313-335) and the optional refine stage. */
-  XVEC_INDEX_IVF_SQ8 = 6
+  XVEC_INDEX_IVF_SQ8 = 6,
+  /* INT4 scalar-quantized Flat: core.ScalarQuantizedFlatIndex with
+   * QuantizationInt4 (quantization.go:91-103, 267-321): two codes in [-8, 7]
+   * per byte, the INT8 kind's scoring on them (QuantizedDistance,
+   * quantization.go:171-235) and the same optional refine stage.  The
+   * dimension must be even for rows and queries (ErrOddInt4Dimension). */
+  XVEC_INDEX_SQ4_FLAT = 7
 } xvec_gpu_index_kind;
 
 typedef enum {

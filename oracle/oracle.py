@@ -109,6 +109,15 @@ class Oracle:
                                       ctypes.c_int64, ctypes.c_int32, _f32p, ctypes.c_int32,
                                       ctypes.c_int32, ctypes.c_float, ctypes.c_float, _u32p,
                                       ctypes.c_int32, _u64p, _f32p, _i32p, _i32p]
+        lib.xo_quantize_int4_batch.argtypes = [_f32p, ctypes.c_int64, ctypes.c_int32,
+                                               ctypes.c_int32, _u8p, ctypes.c_void_p]
+        lib.xo_quantized_distance_int4.argtypes = [ctypes.c_int, _u8p, ctypes.POINTER(SQParams),
+                                                   _u8p, ctypes.POINTER(SQParams),
+                                                   ctypes.c_int32, _f32p]
+        lib.xo_sq4_search.argtypes = [ctypes.c_int, _u8p, ctypes.c_void_p, _f32p, _u64p,
+                                      ctypes.c_int64, ctypes.c_int32, _f32p, ctypes.c_int32,
+                                      ctypes.c_int32, ctypes.c_float, ctypes.c_float, _u32p,
+                                      ctypes.c_int32, _u64p, _f32p, _i32p, _i32p]
         lib.xo_splitmix64_next.restype = ctypes.c_uint64
         lib.xo_splitmix64_next.argtypes = [_u64p]
         lib.xo_kmeans_reservoir.argtypes = [ctypes.c_int64, ctypes.c_int32, ctypes.c_uint64, _i64p]
@@ -284,6 +293,26 @@ class Oracle:
         st = self.lib.xo_quantize_int4(_ptr(v, _f32p), v.size, _ptr(packed, _u8p), ctypes.byref(p))
         return st, packed, p
 
+    def quantize_int4_batch(self, rows, threads=0):
+        """QuantizeVector(QuantizationInt4, row) per row: packed [n, d / 2]."""
+        rows = _c(rows, np.float32)
+        n, d = rows.shape
+        packed = np.zeros((n, d // 2), np.uint8)
+        params = np.zeros(n, SQ_PARAMS_DTYPE)
+        st = self.lib.xo_quantize_int4_batch(_ptr(rows, _f32p), n, d, threads or os.cpu_count(),
+                                             _ptr(packed, _u8p), params.ctypes.data)
+        if st != OK:
+            raise ValueError(f"quantize rows: status {st}")
+        return packed, params
+
+    def quantized_distance_int4(self, metric, lcodes, lp, rcodes, rp, d):
+        lcodes, rcodes = _c(lcodes, np.uint8), _c(rcodes, np.uint8)
+        out = np.zeros(1, np.float32)
+        st = self.lib.xo_quantized_distance_int4(metric, _ptr(lcodes, _u8p), ctypes.byref(lp),
+                                                 _ptr(rcodes, _u8p), ctypes.byref(rp), d,
+                                                 _ptr(out, _f32p))
+        return st, np.float32(out[0])
+
     def quantized_distance_int8(self, metric, lcodes, lp, rcodes, rp):
         lcodes, rcodes = _c(lcodes, np.int8), _c(rcodes, np.int8)
         out = np.zeros(1, np.float32)
@@ -309,6 +338,25 @@ class Oracle:
         ok, os_, oc, ost = self._outs(nq, k)
         bm = None if bitmap is None else _c(bitmap, np.uint32)
         st = self.lib.xo_sq8_search(metric, _ptr(codes, _i8p), params.ctypes.data,
+                                    _ptr(originals, _f32p), _ptr(keys, _u64p), n, d,
+                                    _ptr(queries, _f32p), nq, k, radius, refine_scale,
+                                    _ptr(bm, _u32p), threads or os.cpu_count(), _ptr(ok, _u64p),
+                                    _ptr(os_, _f32p), _ptr(oc, _i32p), _ptr(ost, _i32p))
+        return st, ok.reshape(nq, k), os_.reshape(nq, k), oc, ost
+
+    def sq4_search(self, metric, packed, params, originals, keys, queries, k, radius=0.0,
+                   refine_scale=0.0, bitmap=None, threads=0):
+        """xo_sq4_search: the SQ-Flat search over INT4 codes (packed [n, d / 2])."""
+        packed = _c(packed, np.uint8)
+        params = np.ascontiguousarray(params, SQ_PARAMS_DTYPE)
+        originals = _c(originals, np.float32)
+        keys = _c(keys, np.uint64)
+        queries = _c(queries, np.float32)
+        n, d = originals.shape[0], queries.shape[1]
+        nq = queries.shape[0]
+        ok, os_, oc, ost = self._outs(nq, k)
+        bm = None if bitmap is None else _c(bitmap, np.uint32)
+        st = self.lib.xo_sq4_search(metric, _ptr(packed, _u8p), params.ctypes.data,
                                     _ptr(originals, _f32p), _ptr(keys, _u64p), n, d,
                                     _ptr(queries, _f32p), nq, k, radius, refine_scale,
                                     _ptr(bm, _u32p), threads or os.cpu_count(), _ptr(ok, _u64p),

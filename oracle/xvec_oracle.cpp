@@ -662,6 +662,19 @@ extern "C" int xo_quantize_int4(const float* v, int32_t d, uint8_t* packed, xo_s
   });
 }
 
+// xo_quantize_int4 over n rows (packed d / 2 bytes each).
+extern "C" int xo_quantize_int4_batch(const float* rows, int64_t n, int32_t d, int32_t threads,
+                                      uint8_t* packed, xo_sq_params* params) {
+  if (d % 2 != 0) return XO_INVALID_ARGUMENT;
+  std::vector<int> status(n > 0 ? (size_t)n : 1, XO_OK);
+  parallel_for(n, threads, [&](int64_t i) {
+    status[i] = xo_quantize_int4(rows + i * d, d, packed + i * (d / 2), &params[i]);
+  });
+  for (int64_t i = 0; i < n; ++i)
+    if (status[i] != XO_OK) return status[i];
+  return XO_OK;
+}
+
 namespace {
 // finiteQuantizedScore (quantization.go:387-393).
 inline int finite_quantized(double value, float* out) { return finite_score(value, out); }
@@ -719,6 +732,24 @@ extern "C" int xo_quantized_distance_int8(int metric, const int8_t* left, const 
   return quantized_formula(metric, int8_code_dot(left, right, d), *lp, *rp, d, score);
 }
 
+namespace {
+// QuantizedVector.integerCode for INT4 (quantization.go:368-383).
+inline int int4_code(const uint8_t* packed, int32_t i) {
+  int v = (i % 2 == 0) ? (packed[i / 2] & 0x0f) : (packed[i / 2] >> 4);
+  if (v & 0x08) v -= 16;
+  return v;
+}
+}  // namespace
+
+// QuantizedDistance on two INT4 codes (packed d / 2 bytes each).
+extern "C" int xo_quantized_distance_int4(int metric, const uint8_t* left, const xo_sq_params* lp,
+                                          const uint8_t* right, const xo_sq_params* rp,
+                                          int32_t d, float* score) {
+  double dot = 0;
+  for (int32_t i = 0; i < d; ++i) dot += (double)(int4_code(left, i) * int4_code(right, i));
+  return quantized_formula(metric, dot, *lp, *rp, d, score);
+}
+
 // RefinementCandidateCount (refiner.go:112-129).
 extern "C" int xo_refinement_candidate_count(int32_t top_k, float scale, int32_t* count) {
   if (top_k <= 0) return XO_INVALID_ARGUMENT;
@@ -758,7 +789,7 @@ int refine_exact(int metric, const float* query, int32_t d, const std::vector<Re
 // SQ-Flat search with optional refinement.  Quantized stage:
 // scalarQuantizedVectors.search → searchWithCode (quantized_index.go:296-335):
 // every accepted (filter, radius) score, then MergeSearchResults.
-extern "C" int xo_sq8_search(int metric, const int8_t* codes, const xo_sq_params* params,
+static int sq_flat_search(int bits, int metric, const uint8_t* codes, const xo_sq_params* params,
                              const float* originals, const uint64_t* keys, int64_t n, int32_t d,
                              const float* queries, int32_t nq, int32_t k, float radius,
                              float refine_scale, const uint32_t* bitmap, int32_t threads,
@@ -779,9 +810,11 @@ extern "C" int xo_sq8_search(int metric, const int8_t* codes, const xo_sq_params
     const float* query = queries + q * d;
     std::vector<Result> res;
     int st = validate_query(metric, query, d);  // validateQuery (quantized_index.go:264-272)
-    std::vector<int8_t> qcode(d);
+    std::vector<uint8_t> qcode(bits == 4 ? d / 2 + 1 : d);
     xo_sq_params qp;
-    if (st == XO_OK) st = xo_quantize_int8(query, d, qcode.data(), &qp);
+    if (st == XO_OK)
+      st = bits == 4 ? xo_quantize_int4(query, d, qcode.data(), &qp)
+                     : xo_quantize_int8(query, d, reinterpret_cast<int8_t*>(qcode.data()), &qp);
     std::vector<Result> stage;
     std::vector<int64_t> stage_pos;
     if (st == XO_OK) {
@@ -791,8 +824,12 @@ extern "C" int xo_sq8_search(int metric, const int8_t* codes, const xo_sq_params
       for (int64_t pos = 0; pos < n && st == XO_OK; ++pos) {
         if (!filter_pass(bitmap, pos)) continue;
         float s;
-        st = xo_quantized_distance_int8(metric, codes + pos * d, &params[pos], qcode.data(), &qp,
-                                        d, &s);
+        st = bits == 4
+                 ? xo_quantized_distance_int4(metric, codes + pos * (d / 2), &params[pos],
+                                              qcode.data(), &qp, d, &s)
+                 : xo_quantized_distance_int8(
+                       metric, reinterpret_cast<const int8_t*>(codes) + pos * d, &params[pos],
+                       reinterpret_cast<const int8_t*>(qcode.data()), &qp, d, &s);
         if (st != XO_OK) break;
         if (!within_radius(metric, s, stage_radius)) continue;
         heap.offer(Result{keys[pos], s}, (size_t)stage_k);
@@ -826,6 +863,30 @@ extern "C" int xo_sq8_search(int metric, const int8_t* codes, const xo_sq_params
     if (first == XO_OK) first = status[q];
   }
   return first;
+}
+
+extern "C" int xo_sq8_search(int metric, const int8_t* codes, const xo_sq_params* params,
+                             const float* originals, const uint64_t* keys, int64_t n, int32_t d,
+                             const float* queries, int32_t nq, int32_t k, float radius,
+                             float refine_scale, const uint32_t* bitmap, int32_t threads,
+                             uint64_t* out_keys, float* out_scores, int32_t* out_counts,
+                             int32_t* out_status) {
+  return sq_flat_search(8, metric, reinterpret_cast<const uint8_t*>(codes), params, originals,
+                        keys, n, d, queries, nq, k, radius, refine_scale, bitmap, threads,
+                        out_keys, out_scores, out_counts, out_status);
+}
+
+// The same search over INT4 codes (QuantizationInt4; packed d / 2 bytes per
+// row).  An odd d fails every query in quantizeVector (ErrOddInt4Dimension).
+extern "C" int xo_sq4_search(int metric, const uint8_t* codes, const xo_sq_params* params,
+                             const float* originals, const uint64_t* keys, int64_t n, int32_t d,
+                             const float* queries, int32_t nq, int32_t k, float radius,
+                             float refine_scale, const uint32_t* bitmap, int32_t threads,
+                             uint64_t* out_keys, float* out_scores, int32_t* out_counts,
+                             int32_t* out_status) {
+  return sq_flat_search(4, metric, codes, params, originals, keys, n, d, queries, nq, k, radius,
+                        refine_scale, bitmap, threads, out_keys, out_scores, out_counts,
+                        out_status);
 }
 
 // ---------------------------------------------------------------------------

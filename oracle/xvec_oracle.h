@@ -84,6 +84,11 @@ int xo_quantize_int8(const float* v, int32_t d, int8_t* codes, xo_sq_params* par
 int xo_quantize_int8_batch(const float* rows, int64_t n, int32_t d, int32_t threads,
                            int8_t* codes, xo_sq_params* params);
 int xo_quantize_int4(const float* v, int32_t d, uint8_t* packed, xo_sq_params* params);
+int xo_quantize_int4_batch(const float* rows, int64_t n, int32_t d, int32_t threads,
+                           uint8_t* packed, xo_sq_params* params);
+int xo_quantized_distance_int4(int metric, const uint8_t* left, const xo_sq_params* lp,
+                               const uint8_t* right, const xo_sq_params* rp, int32_t d,
+                               float* score);
 int xo_quantized_distance_int8(int metric, const int8_t* left, const xo_sq_params* lp,
                                const int8_t* right, const xo_sq_params* rp, int32_t d,
                                float* score);
@@ -94,6 +99,13 @@ int xo_refinement_candidate_count(int32_t top_k, float scale_factor, int32_t* co
  * refine_scale > 0 the quantized stage retrieves RefinementCandidateCount
  * candidates without radius and the exact fp32 refiner produces top-k. */
 int xo_sq8_search(int metric, const int8_t* codes, const xo_sq_params* params,
+                  const float* originals, const uint64_t* keys, int64_t n, int32_t d,
+                  const float* queries, int32_t nq, int32_t k, float radius,
+                  float refine_scale, const uint32_t* filter_bitmap, int32_t threads,
+                  uint64_t* out_keys, float* out_scores, int32_t* out_counts,
+                  int32_t* out_status);
+/* xo_sq8_search over INT4 codes (packed d / 2 bytes per row). */
+int xo_sq4_search(int metric, const uint8_t* codes, const xo_sq_params* params,
                   const float* originals, const uint64_t* keys, int64_t n, int32_t d,
                   const float* queries, int32_t nq, int32_t k, float radius,
                   float refine_scale, const uint32_t* filter_bitmap, int32_t threads,

@@ -34,6 +34,7 @@ LIB_PATH = os.path.join(HERE, "libxvec_gpu.so")
 METRIC_L2, METRIC_IP, METRIC_COSINE, METRIC_MIPSL2 = 1, 2, 3, 4
 INDEX_FLAT, INDEX_SQ8_FLAT, INDEX_IVF_PQ, INDEX_RABITQ, INDEX_IVF_FLAT, INDEX_IVF_SQ8 = (
     1, 2, 3, 4, 5, 6)
+INDEX_SQ4_FLAT = 7
 STORAGE_FP32, STORAGE_FP16 = 1, 2
 
 STATUS_NAMES = {
@@ -42,7 +43,7 @@ STATUS_NAMES = {
     10: "DUPLICATE_KEY", 11: "UNSUPPORTED", 12: "CHECKSUM_MISMATCH",
 }
 OK, INVALID_ARGUMENT, NON_FINITE, DUPLICATE_KEY, UNSUPPORTED, CANCELLED = 0, 1, 7, 10, 11, 3
-NOT_FOUND, CHECKSUM_MISMATCH = 9, 12
+NOT_FOUND, CHECKSUM_MISMATCH, OVERFLOW = 9, 12, 8
 
 # Entry points of include/xvec_gpu.h (checked by the CPU test suite).
 EXPORTED_SYMBOLS = (
@@ -300,7 +301,9 @@ class _Index:
         o = self._opts(options, cancel_flag=None if cancel_flag is None else cancel_flag.ctypes.data)
         st = _lib.xvec_gpu_index_search(self._h, _ptr(queries), nq, ctypes.byref(o), _ptr(keys),
                                         _ptr(scores), _ptr(counts))
-        if st != OK and (raise_on_error or st not in (NON_FINITE,) or not (counts < 0).any()):
+        # Per-query failures come back as negative counts (the call's status
+        # is the first one); anything else failed the whole call.
+        if st != OK and (raise_on_error or not (counts < 0).any()):
             raise XvecGPUError(st, last_error())
         return SearchResults(keys[:, :k], scores[:, :k], counts)
 
@@ -366,6 +369,81 @@ class DenseFlatIndex(_NoAllocMixin, _Index):
 class ScalarQuantizedFlatIndex(_Index):
     """core.ScalarQuantizedFlatIndex with QuantizationInt8 (quantized_index.go:28-120)."""
     kind = INDEX_SQ8_FLAT
+
+
+class Int4QuantizedFlatIndex(_Index):
+    """core.ScalarQuantizedFlatIndex with QuantizationInt4 (quantized_index.go:28-120,
+    quantization.go:91-103, 267-321): nibble-packed codes in [-8, 7], the INT8
+    kind's scoring and refine stage; rows and queries need an even dimension."""
+    kind = INDEX_SQ4_FLAT
+
+
+FP16_MAX = 65504.0
+
+
+def quantize_fp16(metric: int, vectors):
+    """QuantizeVector(QuantizationFP16, v) per row (quantization.go:240-265)
+    after the index's metric.Compute(v, v) validation (quantized_index.go:
+    233-235, 264-272): returns (IEEE binary16 bit patterns [n, d] as uint16,
+    status per row: OK, NON_FINITE or OVERFLOW).  The conversion rounds to
+    nearest even, as utility.Float32ToFloat16Bits does."""
+    v = np.ascontiguousarray(vectors, np.float32)
+    if v.ndim == 1:
+        v = v[None, :]
+    status = np.zeros(v.shape[0], np.int32)
+    finite = np.isfinite(v).all(axis=1)
+    status[~finite] = NON_FINITE
+    if metric != METRIC_L2:
+        with np.errstate(over="ignore", invalid="ignore"):
+            selfdot = np.einsum("ij,ij->i", v.astype(np.float64), v.astype(np.float64))
+        status[(status == 0) & ~(selfdot <= np.finfo(np.float32).max)] = NON_FINITE
+    with np.errstate(over="ignore", invalid="ignore"):
+        half = v.astype(np.float16)
+    overflow = np.isinf(half).any(axis=1) & finite
+    status[(status == 0) & overflow] = OVERFLOW
+    half[status != 0] = 0
+    return half.view(np.uint16), status
+
+
+class FP16QuantizedFlatIndex:
+    """core.ScalarQuantizedFlatIndex with QuantizationFP16: rows and queries
+    become binary16 (quantize_fp16) and QuantizedDistance decodes both and
+    applies metric.Compute (quantization.go:187-191), which is the FLAT kind
+    with FP16 storage.  A row that fails conversion fails the add; a query
+    that fails it fails alone (negative count)."""
+
+    def __init__(self, dimension: int, metric: int, device: int = 0):
+        self._flat = DenseFlatIndex(dimension, metric, STORAGE_FP16, device)
+        self.dimension, self.metric, self.device = dimension, metric, device
+
+    def close(self) -> None:
+        self._flat.close()
+
+    def __len__(self) -> int:
+        return len(self._flat)
+
+    def add(self, keys, vectors) -> None:
+        half, status = quantize_fp16(self.metric, vectors)
+        bad = np.flatnonzero(status)
+        if bad.size:
+            raise XvecGPUError(int(status[bad[0]]), f"core: quantize vector {int(bad[0])}")
+        self._flat.add(keys, half)
+
+    def search_with_options(self, queries, options: SearchOptions,
+                            raise_on_error: bool = True) -> SearchResults:
+        half, status = quantize_fp16(self.metric, queries)
+        res = self._flat.search_with_options(half, options, raise_on_error=raise_on_error)
+        bad = np.flatnonzero(status)
+        if bad.size:
+            if raise_on_error:
+                raise XvecGPUError(int(status[bad[0]]), f"core: quantize query {int(bad[0])}")
+            res.counts[bad] = -status[bad]
+            res.keys[bad] = 0
+            res.scores[bad] = 0
+        return res
+
+    def search(self, queries, k: int) -> SearchResults:
+        return self.search_with_options(queries, SearchOptions(top_k=k))
 
 
 class IVFPQIndex(_Index):

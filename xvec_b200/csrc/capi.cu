@@ -455,6 +455,7 @@ xvec_gpu_status search_device_locked(xvec_gpu_index* idx, const void* d_q, int n
       return flat_search_impl<float>(idx, d_q, nq, o, d_bitmap, d_keys, d_scores, d_counts, s,
                                      statuses);
     case XVEC_INDEX_SQ8_FLAT:
+    case XVEC_INDEX_SQ4_FLAT:
       return sq8_search_impl(idx, static_cast<const float*>(d_q), nq, o, d_bitmap, d_keys,
                              d_scores, d_counts, s, statuses);
     case XVEC_INDEX_IVF_PQ:
@@ -605,6 +606,7 @@ extern "C" xvec_gpu_status xvec_gpu_index_create(const xvec_gpu_index_desc* desc
         return set_error("invalid storage"), XVEC_GPU_INVALID_ARGUMENT;
       break;
     case XVEC_INDEX_SQ8_FLAT:
+    case XVEC_INDEX_SQ4_FLAT:
     case XVEC_INDEX_IVF_SQ8:
       if (desc->dimension > 65535)
         return set_error("core: invalid vector dimension: got %d", desc->dimension),

@@ -20,7 +20,8 @@ xvec_gpu_status extra_reserve(xvec_gpu_index* idx, int64_t cap, cudaStream_t s) 
       return st;
     return XVEC_GPU_OK;
   }
-  if (idx->desc.kind == XVEC_INDEX_SQ8_FLAT) return sq8_reserve(idx, cap, s);
+  if (idx->desc.kind == XVEC_INDEX_SQ8_FLAT || idx->desc.kind == XVEC_INDEX_SQ4_FLAT)
+    return sq8_reserve(idx, cap, s);
   if (idx->desc.kind == XVEC_INDEX_IVF_PQ) return ivfpq_reserve(idx, cap, s);
   if (idx->desc.kind == XVEC_INDEX_RABITQ) return rabitq_reserve(idx, cap, s);
   if (idx->desc.kind == XVEC_INDEX_IVF_FLAT) return ivf_flat_reserve(idx, cap, s);
@@ -49,7 +50,8 @@ xvec_gpu_status extra_commit(xvec_gpu_index* idx, int64_t old_n, int64_t m, cuda
     XVEC_LAUNCHED();
     return XVEC_GPU_OK;
   }
-  if (idx->desc.kind == XVEC_INDEX_SQ8_FLAT) return sq8_commit(idx, old_n, m, s);
+  if (idx->desc.kind == XVEC_INDEX_SQ8_FLAT || idx->desc.kind == XVEC_INDEX_SQ4_FLAT)
+    return sq8_commit(idx, old_n, m, s);
   if (idx->desc.kind == XVEC_INDEX_IVF_PQ) return ivfpq_commit(idx, old_n, m, s);
   if (idx->desc.kind == XVEC_INDEX_RABITQ) return rabitq_commit(idx, old_n, m, s);
   if (idx->desc.kind == XVEC_INDEX_IVF_FLAT) return ivf_flat_commit(idx, old_n, m, s);

@@ -82,7 +82,8 @@ using namespace xvec;
 extern "C" int32_t xvec_gpu_index_candidate_count(const xvec_gpu_index* idx,
                                                   const xvec_gpu_search_opts* opts) {
   if (!idx || !opts) return 0;
-  if (idx->desc.kind == XVEC_INDEX_SQ8_FLAT) return sq8_candidate_count(*opts);
+  if (idx->desc.kind == XVEC_INDEX_SQ8_FLAT || idx->desc.kind == XVEC_INDEX_SQ4_FLAT)
+    return sq8_candidate_count(*opts);
   if (idx->desc.kind == XVEC_INDEX_RABITQ) return rabitq_candidate_count(*opts);
   return 0;
 }
@@ -106,7 +107,7 @@ extern "C" xvec_gpu_status xvec_gpu_index_candidates_device(xvec_gpu_index* idx,
   cudaStream_t s = static_cast<cudaStream_t>(opts->stream);
   std::vector<int> statuses;
   const float* q = static_cast<const float*>(d_queries);
-  if (idx->desc.kind == XVEC_INDEX_SQ8_FLAT)
+  if (idx->desc.kind == XVEC_INDEX_SQ8_FLAT || idx->desc.kind == XVEC_INDEX_SQ4_FLAT)
     return sq8_search_impl(idx, q, nq, *opts, opts->filter_bitmap, d_keys, d_ranks, d_counts, s,
                            &statuses, true);
   return rabitq_search_impl(idx, q, nq, *opts, opts->filter_bitmap, d_keys, d_ranks, d_counts, s,

@@ -83,6 +83,61 @@ __device__ bool warp_quantize_int8(const float* v, int d, int8_t* codes, SQParam
   return true;
 }
 
+// quantizeInteger (quantization.go:267-321) for INT4 ([-8, 7]), one warp per
+// vector of even dimension, a lane per element pair.  `packed` (d / 2 bytes)
+// and `unpacked` (d int8 codes) may each be null.
+__device__ bool warp_quantize_int4(const float* v, int d, uint8_t* packed, int8_t* unpacked,
+                                   SQParams* p) {
+  const int lane = threadIdx.x & 31;
+  float mn = v[0], mx = v[0];
+  for (int i = lane; i < d; i += 32) {
+    mn = go_min_zero(mn, v[i]);
+    mx = go_max_zero(mx, v[i]);
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    mn = go_min_zero(mn, __shfl_xor_sync(kFullMask, mn, o));
+    mx = go_max_zero(mx, __shfl_xor_sync(kFullMask, mx, o));
+  }
+  const int half = d >> 1;
+  if (mn == mx) {
+    for (int j = lane; j < half; j += 32) {
+      if (packed) packed[j] = 0;
+      if (unpacked) unpacked[2 * j] = unpacked[2 * j + 1] = 0;
+    }
+    if (lane == 0) *p = SQParams{0.f, mn, 0.0, 0.0};
+    return true;
+  }
+  const float eps32 = 1.1920928955078125e-7f;
+  const float span = __fsub_rn(mx, mn);
+  const float scale = __fdiv_rn(15.f, go_maxf(span, eps32));
+  const float bias = __fadd_rn(__fmul_rn(-mn, scale), -8.f);
+  const float inv = __fdiv_rn(1.f, scale);
+  const float off = __fdiv_rn(-bias, scale);
+  if (!finite_f(inv) || !finite_f(off)) return false;
+  long long sum = 0, sq = 0;
+  for (int j = lane; j < half; j += 32) {
+    int c[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const float t = __fadd_rn(__fmul_rn(v[2 * j + e], scale), bias);
+      c[e] = min(7, max(-8, (int)round((double)t)));
+      sum += c[e];
+      sq += c[e] * c[e];
+    }
+    if (packed) packed[j] = (uint8_t)((c[0] & 15) | ((c[1] & 15) << 4));
+    if (unpacked) {
+      unpacked[2 * j] = (int8_t)c[0];
+      unpacked[2 * j + 1] = (int8_t)c[1];
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    sum += __shfl_xor_sync(kFullMask, sum, o);
+    sq += __shfl_xor_sync(kFullMask, sq, o);
+  }
+  if (lane == 0) *p = SQParams{inv, off, (double)sum, (double)sq};
+  return true;
+}
+
 // The squared norm of the decoded vector, float64 in the reference order
 // (leftNorm / rightNorm of quantization.go:205-208).
 __device__ __forceinline__ double sq_norm64(const SQParams& p, int d) {
@@ -132,8 +187,10 @@ __device__ float sq_reference_score(int metric, double dot, const SQParams& l, c
 }
 
 // Rows: quantize, fast-rank terms and the index-wide error-bound maxima.
+// BITS 8: d int8 codes per row; BITS 4: d / 2 bytes of nibble pairs.
+template <int BITS>
 __global__ void sq8_encode_rows_kernel(const float* __restrict__ rows, int64_t n, int d,
-                                       int8_t* __restrict__ codes, SQParams* __restrict__ params,
+                                       uint8_t* __restrict__ codes, SQParams* __restrict__ params,
                                        float4* __restrict__ fast, unsigned* __restrict__ bounds,
                                        int* __restrict__ err) {
   const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -142,7 +199,11 @@ __global__ void sq8_encode_rows_kernel(const float* __restrict__ rows, int64_t n
   SQParams p;
   __shared__ SQParams sp[8];
   const int wl = threadIdx.x >> 5;
-  if (!warp_quantize_int8(rows + w * d, d, codes + w * d, &sp[wl])) {
+  const bool ok =
+      BITS == 8 ? warp_quantize_int8(rows + w * d, d, reinterpret_cast<int8_t*>(codes) + w * d,
+                                     &sp[wl])
+                : warp_quantize_int4(rows + w * d, d, codes + w * (d / 2), nullptr, &sp[wl]);
+  if (!ok) {
     if (lane == 0) atomicExch(err, XVEC_GPU_OVERFLOW);
     return;
   }
@@ -164,7 +225,10 @@ __global__ void sq8_encode_rows_kernel(const float* __restrict__ rows, int64_t n
 
 // Queries: validation (metric.Compute(q, q), quantized_index.go:264-272),
 // quantization, the float codes for the scan, the fast-rank constants and
-// eps (bound on |fast rank - reference rank|, see sq8.cu header).
+// eps (bound on |fast rank - reference rank|, see sq8.cu header).  qcodes
+// hold d int8 codes per query for either width (INT4 codes unpacked); an odd
+// dimension fails every INT4 query (ErrOddInt4Dimension, quantization.go:91-93).
+template <int BITS>
 __global__ void sq8_prep_queries_kernel(const float* __restrict__ q, int nq, int d, int metric,
                                         const unsigned* __restrict__ bounds,
                                         int8_t* __restrict__ qcodes, SQParams* __restrict__ qparams,
@@ -183,7 +247,10 @@ __global__ void sq8_prep_queries_kernel(const float* __restrict__ q, int nq, int
   if (!finite || (metric != kMetricL2 && !finite_f(s0))) st = XVEC_GPU_NON_FINITE;
   __shared__ SQParams sp[8];
   const int wl = threadIdx.x >> 5;
-  if (st == 0 && !warp_quantize_int8(v, d, qcodes + (int64_t)w * d, &sp[wl]))
+  if (st == 0 && BITS == 4 && (d & 1)) st = XVEC_GPU_INVALID_ARGUMENT;
+  if (st == 0 &&
+      !(BITS == 8 ? warp_quantize_int8(v, d, qcodes + (int64_t)w * d, &sp[wl])
+                  : warp_quantize_int4(v, d, nullptr, qcodes + (int64_t)w * d, &sp[wl])))
     st = XVEC_GPU_OVERFLOW;
   __syncwarp();
   if (st != 0) {
@@ -237,18 +304,24 @@ struct SQ8Ranker {
 
 struct SQ8Scorer {
   int metric;
-  const int8_t* codes;
+  const uint8_t* codes;
   const SQParams* params;
   const int8_t* qcodes;
   const SQParams* qparams;
   const float* q_eps;
   int d;
+  int int4;  // 1: nibble-packed INT4 rows (d / 2 bytes each)
   __device__ float score(int qi, int64_t row) const {
     const int lane = threadIdx.x & 31;
-    const int8_t* a = codes + row * d;
     const int8_t* b = qcodes + (int64_t)qi * d;
     int dot = 0;
-    for (int i = lane; i < d; i += 32) dot += (int)a[i] * (int)b[i];
+    if (!int4) {
+      const int8_t* a = reinterpret_cast<const int8_t*>(codes) + row * d;
+      for (int i = lane; i < d; i += 32) dot += (int)a[i] * (int)b[i];
+    } else {
+      const uint8_t* a = codes + row * (d / 2);
+      for (int i = lane; i < d; i += 32) dot += int4_at(a, i) * (int)b[i];
+    }
     for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(kFullMask, dot, o);
     return sq_reference_score(metric, (double)dot, params[row], qparams[qi], d);
   }
@@ -356,11 +429,17 @@ struct Sq8IvfPolicy {
 // ---------------------------------------------------------------------------
 // Insertion hooks.
 // ---------------------------------------------------------------------------
-xvec_gpu_status sq8_reserve(xvec_gpu_index* idx, int64_t cap, cudaStream_t s) {
+// Code bytes per row: d (INT8) or d / 2 (INT4 nibble pairs).
+inline size_t sq_row_bytes(const xvec_gpu_index* idx) {
   const int d = idx->desc.dimension;
+  return idx->desc.kind == XVEC_INDEX_SQ4_FLAT ? (size_t)(d / 2) : (size_t)d;
+}
+
+xvec_gpu_status sq8_reserve(xvec_gpu_index* idx, int64_t cap, cudaStream_t s) {
+  const size_t rb = sq_row_bytes(idx);
   const int64_t n = idx->n;
   xvec_gpu_status st;
-  if ((st = idx->sq_codes.reserve((size_t)cap * d, (size_t)n * d, s)) ||
+  if ((st = idx->sq_codes.reserve((size_t)cap * rb, (size_t)n * rb, s)) ||
       (st = idx->sq_params.reserve((size_t)cap * sizeof(SQParams), (size_t)n * sizeof(SQParams), s)) ||
       (st = idx->sq_fast.reserve((size_t)cap * 16, (size_t)n * 16, s)))
     return st;
@@ -385,15 +464,26 @@ xvec_gpu_status sq8_commit(xvec_gpu_index* idx, int64_t old_n, int64_t m, cudaSt
                          (long long)(old_n + i)),
                XVEC_GPU_NON_FINITE;
   }
+  const bool int4 = idx->desc.kind == XVEC_INDEX_SQ4_FLAT;
+  if (int4 && (d & 1))
+    return set_error("core: quantize vector %lld: core: INT4 quantization requires an even "
+                     "dimension: got %d",
+                     (long long)old_n, d),
+           XVEC_GPU_INVALID_ARGUMENT;
   Scratch err, bounds;
   xvec_gpu_status st;
   if ((st = err.alloc(4, s)) || (st = bounds.alloc(16, s))) return st;
   XVEC_CUDA(cudaMemsetAsync(err.ptr, 0, 4, s));
   XVEC_CUDA(cudaMemcpyAsync(bounds.ptr, idx->sq_bounds.ptr, 16, cudaMemcpyDeviceToDevice, s));
-  sq8_encode_rows_kernel<<<blocks_of(m * 32), 256, 0, s>>>(
-      idx->rows.as<float>() + old_n * d, m, d, idx->sq_codes.as<int8_t>() + old_n * d,
-      idx->sq_params.as<SQParams>() + old_n, idx->sq_fast.as<float4>() + old_n,
-      bounds.as<unsigned>(), err.as<int>());
+  uint8_t* codes = idx->sq_codes.as<uint8_t>() + old_n * sq_row_bytes(idx);
+  if (int4)
+    sq8_encode_rows_kernel<4><<<blocks_of(m * 32), 256, 0, s>>>(
+        idx->rows.as<float>() + old_n * d, m, d, codes, idx->sq_params.as<SQParams>() + old_n,
+        idx->sq_fast.as<float4>() + old_n, bounds.as<unsigned>(), err.as<int>());
+  else
+    sq8_encode_rows_kernel<8><<<blocks_of(m * 32), 256, 0, s>>>(
+        idx->rows.as<float>() + old_n * d, m, d, codes, idx->sq_params.as<SQParams>() + old_n,
+        idx->sq_fast.as<float4>() + old_n, bounds.as<unsigned>(), err.as<int>());
   XVEC_LAUNCHED();
   XVEC_CUDA(cudaGetLastError());
   int h_err = 0;
@@ -446,10 +536,17 @@ xvec_gpu_status sq8_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
     return st;
   XVEC_CUDA(cudaMemsetAsync(qflags.ptr, 0, (size_t)nq * 4, s));
   XVEC_CUDA(cudaMemsetAsync(qstatus.ptr, 0, (size_t)nq * 4, s));
-  sq8_prep_queries_kernel<<<blocks_of((int64_t)nq * 32), 256, 0, s>>>(
-      d_q, nq, d, metric, idx->sq_bounds.as<unsigned>(), qcodes.as<int8_t>(),
-      qparams.as<SQParams>(), qf.as<float>(), qinfo.as<float4>(), qeps.as<float>(),
-      qstatus.as<int>());
+  const bool int4 = idx->desc.kind == XVEC_INDEX_SQ4_FLAT;
+  if (int4)
+    sq8_prep_queries_kernel<4><<<blocks_of((int64_t)nq * 32), 256, 0, s>>>(
+        d_q, nq, d, metric, idx->sq_bounds.as<unsigned>(), qcodes.as<int8_t>(),
+        qparams.as<SQParams>(), qf.as<float>(), qinfo.as<float4>(), qeps.as<float>(),
+        qstatus.as<int>());
+  else
+    sq8_prep_queries_kernel<8><<<blocks_of((int64_t)nq * 32), 256, 0, s>>>(
+        d_q, nq, d, metric, idx->sq_bounds.as<unsigned>(), qcodes.as<int8_t>(),
+        qparams.as<SQParams>(), qf.as<float>(), qinfo.as<float4>(), qeps.as<float>(),
+        qstatus.as<int>());
   XVEC_LAUNCHED();
   XVEC_CUDA(cudaGetLastError());
   // Stage outputs: the final outputs, or scratch when a refine stage follows.
@@ -468,11 +565,11 @@ xvec_gpu_status sq8_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
     o_counts = scounts.as<int>();
   }
   XVEC_CUDA(cudaMemsetAsync(o_counts, 0, (size_t)nq * 4, s));
-  SQ8Scorer sc{metric, idx->sq_codes.as<int8_t>(), idx->sq_params.as<SQParams>(),
-               qcodes.as<int8_t>(), qparams.as<SQParams>(), qeps.as<float>(), d};
+  SQ8Scorer sc{metric, idx->sq_codes.as<uint8_t>(), idx->sq_params.as<SQParams>(),
+               qcodes.as<int8_t>(), qparams.as<SQParams>(), qeps.as<float>(), d, int4 ? 1 : 0};
   const bool ranked = n > 0 && (metric == XVEC_METRIC_IP || metric == XVEC_METRIC_L2);
   // INT8 tensor cores (tcgen05 kind::i8) when the layout allows, else FFMA.
-  const bool use_tc = ranked && kp + 128 <= flat_tc_cap() && n < (1ll << 31) - 256 &&
+  const bool use_tc = !int4 && ranked && kp + 128 <= flat_tc_cap() && n < (1ll << 31) - 256 &&
                       sq8_tc_supported(d, idx->sq_codes.ptr, qcodes.ptr);
   const bool fast = use_tc || (ranked && simt_cap_for(kp) <= 512);
   if (use_tc) {
@@ -521,9 +618,16 @@ xvec_gpu_status sq8_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
       return st;
     const SQ8Ranker rk{metric, idx->sq_fast.as<float4>(), qinfo.as<float4>()};
     timer.mark(1);
-    XVEC_CUDA(launch_scan_simt(idx->sq_codes.as<int8_t>(), n, d, idx->keyrank.as<uint32_t>(),
-                               qf.as<float>(), nq, d_bitmap, rk, parts, kp, pkeys.as<uint64_t>(),
-                               pcounts.as<int>(), psat.as<uint64_t>(), qflags.as<int>(), s));
+    if (int4)
+      XVEC_CUDA(launch_scan_simt(idx->sq_codes.as<Int4Pair>(), n, d, idx->keyrank.as<uint32_t>(),
+                                 qf.as<float>(), nq, d_bitmap, rk, parts, kp,
+                                 pkeys.as<uint64_t>(), pcounts.as<int>(), psat.as<uint64_t>(),
+                                 qflags.as<int>(), s));
+    else
+      XVEC_CUDA(launch_scan_simt(idx->sq_codes.as<int8_t>(), n, d, idx->keyrank.as<uint32_t>(),
+                                 qf.as<float>(), nq, d_bitmap, rk, parts, kp,
+                                 pkeys.as<uint64_t>(), pcounts.as<int>(), psat.as<uint64_t>(),
+                                 qflags.as<int>(), s));
     timer.mark(2);
     XVEC_CUDA(launch_merge_rescore(sc, idx->pos_of_kr.as<uint32_t>(), idx->keys.as<uint64_t>(),
                                    nullptr, nq, stage_k, stage_radius, 0, pkeys.as<uint64_t>(),
@@ -663,7 +767,7 @@ xvec_gpu_status ivf_sq8_search_impl(xvec_gpu_index* idx, const float* d_q, int n
     return st;
   XVEC_CUDA(cudaMemsetAsync(qflags.ptr, 0, (size_t)nq * 4, s));
   XVEC_CUDA(cudaMemsetAsync(qstatus.ptr, 0, (size_t)nq * 4, s));
-  sq8_prep_queries_kernel<<<blocks_of((int64_t)nq * 32), 256, 0, s>>>(
+  sq8_prep_queries_kernel<8><<<blocks_of((int64_t)nq * 32), 256, 0, s>>>(
       d_q, nq, d, metric, idx->sq_bounds.as<unsigned>(), qcodes.as<int8_t>(),
       qparams.as<SQParams>(), qf.as<float>(), qinfo.as<float4>(), qeps.as<float>(),
       qstatus.as<int>());
@@ -706,7 +810,7 @@ xvec_gpu_status ivf_sq8_search_impl(xvec_gpu_index* idx, const float* d_q, int n
     if ((st = lkeys.alloc(lists * kp * 8, s)) || (st = lcounts.alloc(lists * 4, s)) ||
         (st = lsat.alloc(lists * 8, s)))
       return st;
-    const SQ8Scorer sc{metric, idx->sq_codes.as<int8_t>(), idx->sq_params.as<SQParams>(),
+    const SQ8Scorer sc{metric, idx->sq_codes.as<uint8_t>(), idx->sq_params.as<SQParams>(),
                        qcodes.as<int8_t>(), qparams.as<SQParams>(), qeps.as<float>(), d};
     const Sq8IvfPolicy pol{metric,
                            idx->sq_codes.as<int8_t>(),
