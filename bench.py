@@ -53,7 +53,7 @@ def parse():
     p.add_argument("--workload",
                    choices=["flat_cosine_fp16", "ivfpq_l2", "sq8_ip_refine", "rabitq_l2_refine",
                             "flat_l2_fp32", "ivf_flat_l2", "ivf_sq8_l2_refine",
-                            "rabitq7_l2_refine"],
+                            "rabitq7_l2_refine", "sq4_l2_refine", "pq_train_l2"],
                    default="flat_cosine_fp16",
                    help="flat_cosine_fp16: the Flat configuration above (default); ivfpq_l2: "
                         "IVF-PQ L2, 1e8 x 128, nlist 16384, 32 x 256 PQ, nprobe 64, k=10; "
@@ -63,7 +63,9 @@ def parse():
                         "queries, k=10; ivf_flat_l2: IVF with exact scoring, 1e7 x 128, "
                         "nlist 4096, nprobe 32, k=10; ivf_sq8_l2_refine: the same IVF with "
                         "INT8 list scoring and ScaleFactor 4; rabitq7_l2_refine: the RaBitQ "
-                        "data with TotalBits 7")
+                        "data with TotalBits 7; sq4_l2_refine: INT4 SQ Flat L2, 4e6 x 128, "
+                        "1,000 queries, k=10, ScaleFactor 4; pq_train_l2: TrainPQ (32 chunks, "
+                        "200,000-row sample, 12 iterations) on 1e6 x 128, one training per step")
     return p.parse_args()
 
 
@@ -772,6 +774,163 @@ def run_sq8(args):
     finish_ranks(world)
 
 
+# ---------------------------------------------------------------------------
+# INT4 scalar-quantized Flat, L2, FP32 refinement: 4,000,000 x 128, N(0,1)
+# scaled per dimension by U(0.5, 2); 1,000 queries; top-k 10, ScaleFactor 4.
+# The codes (256 MB) are larger than L2.
+# ---------------------------------------------------------------------------
+SQ4_N, SQ4_DIM, SQ4_NQ, SQ4_K, SQ4_SCALE = 4_000_000, 128, 1000, 10, 4.0
+SQ4_WORKLOAD = ("INT4 scalar-quantized Flat L2 search with FP32 refinement, 4,000,000 x 128 "
+                "(N(0,1) x per-dimension U(0.5,2)), 1,000 queries, top-k=10, ScaleFactor 4")
+
+
+def run_sq4(args):
+    import numpy as np
+    import torch
+
+    import xvec_b200 as xb
+    from xvec_b200.sharded import ShardedSearch, shard_range
+    world, rank, local, dev = init_ranks(args)
+    n = args.n if args.n != N_BASE else SQ4_N
+    nq = args.nq if args.nq != N_QUERIES else SQ4_NQ
+    g = torch.Generator(device=dev).manual_seed(44)
+    scale = torch.rand(SQ4_DIM, generator=g, device=dev) * 1.5 + 0.5
+    index = xb.Int4QuantizedFlatIndex(SQ4_DIM, xb.METRIC_L2, device=local)
+    b, e = shard_range(n, rank, world, align=SQ_CHUNK_ROWS)
+    index.reserve(e - b)
+    stream = torch.cuda.current_stream().cuda_stream
+    for c0 in range(b, e, SQ_CHUNK_ROWS):
+        m = min(SQ_CHUNK_ROWS, e - c0)
+        rows = sq_rows(torch, scale, c0 // SQ_CHUNK_ROWS, m, dev).contiguous()
+        keys = torch.arange(c0, c0 + m, dtype=torch.int64, device=dev)
+        index.add_device(keys.data_ptr(), rows.data_ptr(), m, stream)
+        del rows, keys
+    queries = sq_rows(torch, scale, 10**6, nq, dev).contiguous()
+    torch.cuda.synchronize()
+    opts = xb.SearchOptions(top_k=SQ4_K, refine_scale=SQ4_SCALE)
+    ms, scan_ms, e2e_ms, st, clocks = time_search(ShardedSearch(index), queries, opts, args, dev,
+                                                  world, local)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle.oracle import L2, Oracle
+        ora = Oracle()
+        m = min(args.cpu_sample_rows // 10, n)
+        sample = sq_rows(torch, scale, 0, m, dev).cpu().numpy()
+        qs = queries[:max(8, args.cpu_sample_queries // 4)].cpu().numpy()
+        packed, params = ora.quantize_int4_batch(sample)
+        threads = os.cpu_count() or 1
+        t0 = time.perf_counter()
+        ora.sq4_search(L2, packed, params, sample, np.arange(m, dtype=np.uint64), qs, SQ4_K, 0.0,
+                       SQ4_SCALE, threads=threads)
+        dt = time.perf_counter() - t0
+        cpu = {"value": qs.shape[0] / dt * m / n, "unit": "queries/sec", "cores": threads,
+               "kind": "port",
+               "sample": f"{qs.shape[0]} queries x {m}-row sample, {dt:.1f} s on {threads} "
+                         f"threads; QPS scaled by rows/{n}"}
+    if rank == 0:
+        shard = e - b
+        flops = 2.0 * nq * shard * SQ4_DIM
+        achieved = flops / (scan_ms / 1000.0) / 1e12 if scan_ms > 0 else None
+        peak = 80.0
+        roof = {"bound": "fp32 ffma", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                "frac": (achieved / peak) if achieved else None, "traffic": None,
+                "peak_source": "nominal FP32 FFMA (148 SMs x 128 lanes x 2 flop x ~2.1 GHz); "
+                               "the INT4 scan runs the FFMA tile kernel",
+                "kernel": "INT4 code scan", "kernel_ms": scan_ms,
+                "algorithmic_flops_per_launch": flops}
+        config = {"workload": SQ4_WORKLOAD, "global_batch": nq, "top_k": SQ4_K,
+                  "base_vectors": n, "dim": SQ4_DIM, "metric": "l2", "refine_scale": SQ4_SCALE,
+                  "parallelism": f"rows sharded over {world} GPU(s), NCCL all-gather + merge",
+                  "l2": "inputs larger than L2 (256 MB codes)"}
+        print(json.dumps(common_line(nq, ms, e2e_ms, args, world, "i4 codes, f32/f64 scores",
+                                     config, roof, cpu, clocks, st, SQ4_K, SQ4_DIM, 4)),
+              flush=True)
+    finish_ranks(world)
+
+
+# ---------------------------------------------------------------------------
+# TrainPQ: 1,000,000 x 128 from the IVF-PQ mixture generator's distribution
+# (i.i.d. N(0,1) here), 32 chunks of 4 dimensions, the default 200,000-row
+# sample and 12 iterations.  One step is one training; the metric is
+# trainings per second.
+# ---------------------------------------------------------------------------
+PQT_N, PQT_DIM, PQT_CHUNKS = 1_000_000, 128, 32
+PQT_WORKLOAD = ("TrainPQ L2, 1,000,000 x 128 N(0,1), 32 chunks x 256 centroids, 200,000-row "
+                "sample, 12 Lloyd iterations, KMC2 seeding")
+
+
+def run_pq_train(args):
+    import numpy as np
+    import torch
+
+    import xvec_b200 as xb
+    world, rank, local, dev = init_ranks(args)
+    if world != 1:
+        raise SystemExit("pq_train_l2 runs on one GPU (the training is not sharded)")
+    n = args.n if args.n != N_BASE else PQT_N
+    g = torch.Generator(device=dev).manual_seed(303)
+    rows = torch.randn(n, PQT_DIM, generator=g, device=dev)
+    offsets = np.zeros(PQT_CHUNKS + 1, np.int32)
+    pivots = torch.empty(256, PQT_DIM, device=dev)
+    stream = torch.cuda.current_stream().cuda_stream
+    lib = xb.library()
+
+    def train():
+        import ctypes
+        out = ctypes.c_int32()
+        st = lib.xvec_gpu_pq_train_device(local, xb.METRIC_L2, rows.data_ptr(), n, PQT_DIM,
+                                          PQT_CHUNKS, 200_000, 12, 7, offsets.ctypes.data,
+                                          pivots.data_ptr(), ctypes.byref(out), stream)
+        if st != 0:
+            raise xb.XvecGPUError(st, xb.last_error())
+
+    for _ in range(args.warmup):
+        train()
+    torch.cuda.synchronize()
+    st0 = xb.stats()
+    with ClockSampler(local) as clocks:
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(args.steps):
+            train()
+        end.record()
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / args.steps
+    launches = xb.stats()["kernel_launches"] - st0["kernel_launches"]
+    # End to end: host rows in, host pivots out (xvec_gpu_pq_train).
+    host = rows[:200_000].cpu().numpy()
+    t0 = time.perf_counter()
+    for _ in range(max(1, args.steps // 2)):
+        xb.pq_train(xb.METRIC_L2, host, PQT_CHUNKS, 200_000, 12, 7, device=local)
+    e2e_ms = (time.perf_counter() - t0) * 1000.0 / max(1, args.steps // 2)
+    cpu = None
+    if not args.no_cpu_baseline:
+        from oracle.oracle import L2, Oracle
+        ora = Oracle()
+        sample_chunks = 4
+        sub = np.ascontiguousarray(host[:, :sample_chunks * PQT_DIM // PQT_CHUNKS])
+        threads = os.cpu_count() or 1
+        t0 = time.perf_counter()
+        ora.pq_train(L2, sub, sample_chunks, 200_000, 12, 7, threads=threads)
+        dt = (time.perf_counter() - t0) * PQT_CHUNKS / sample_chunks
+        cpu = {"value": 1.0 / dt, "unit": "trainings/sec", "cores": threads, "kind": "port",
+               "sample": f"{sample_chunks} of {PQT_CHUNKS} chunks trained, time scaled by "
+                         f"{PQT_CHUNKS // sample_chunks}"}
+    print(json.dumps({
+        "metric": "TrainPQ trainings per second", "value": 1000.0 / ms, "unit": "trainings/sec",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32/f64",
+        "data": "synthetic",
+        "config": {"workload": PQT_WORKLOAD, "base_vectors": n, "dim": PQT_DIM,
+                   "chunks": PQT_CHUNKS, "l2": "200,000 x 128 sample (102 MB) re-read per "
+                                              "iteration; not flushed"},
+        "e2e": {"value": 1000.0 / e2e_ms, "unit": "trainings/sec",
+                "h2d_bytes_per_step": 200_000 * PQT_DIM * 4,
+                "d2h_bytes_per_step": 256 * PQT_DIM * 4},
+        "roofline": None, "cpu_baseline": cpu, "clocks": clocks.summary(),
+        "gpu_launches": int(launches)}), flush=True)
+
+
 def cpu_sq8_qps(sample, queries, n_total):
     import numpy as np
 
@@ -957,6 +1116,10 @@ def main():
         return run_rabitq(args)
     if args.workload == "rabitq7_l2_refine":
         return run_rabitq(args, total_bits=RQ7_BITS)
+    if args.workload == "sq4_l2_refine":
+        return run_sq4(args)
+    if args.workload == "pq_train_l2":
+        return run_pq_train(args)
 
     import numpy as np
     import torch
