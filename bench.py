@@ -64,7 +64,7 @@ def parse():
                         "nlist 4096, nprobe 32, k=10; ivf_sq8_l2_refine: the same IVF with "
                         "INT8 list scoring and ScaleFactor 4; rabitq7_l2_refine: the RaBitQ "
                         "data with TotalBits 7; sq4_l2_refine: INT4 SQ Flat L2, 4e6 x 128, "
-                        "1,000 queries, k=10, ScaleFactor 4; pq_train_l2: TrainPQ (32 chunks, "
+                        "10,000 queries, k=10, ScaleFactor 4; pq_train_l2: TrainPQ (32 chunks, "
                         "200,000-row sample, 12 iterations) on 1e6 x 128, one training per step")
     return p.parse_args()
 
@@ -776,12 +776,12 @@ def run_sq8(args):
 
 # ---------------------------------------------------------------------------
 # INT4 scalar-quantized Flat, L2, FP32 refinement: 4,000,000 x 128, N(0,1)
-# scaled per dimension by U(0.5, 2); 1,000 queries; top-k 10, ScaleFactor 4.
-# The codes (256 MB) are larger than L2.
+# scaled per dimension by U(0.5, 2); 10,000 queries; top-k 10, ScaleFactor 4.
+# The codes (512 MB, one per byte) are larger than L2.
 # ---------------------------------------------------------------------------
-SQ4_N, SQ4_DIM, SQ4_NQ, SQ4_K, SQ4_SCALE = 4_000_000, 128, 1000, 10, 4.0
+SQ4_N, SQ4_DIM, SQ4_NQ, SQ4_K, SQ4_SCALE = 4_000_000, 128, 10_000, 10, 4.0
 SQ4_WORKLOAD = ("INT4 scalar-quantized Flat L2 search with FP32 refinement, 4,000,000 x 128 "
-                "(N(0,1) x per-dimension U(0.5,2)), 1,000 queries, top-k=10, ScaleFactor 4")
+                "(N(0,1) x per-dimension U(0.5,2)), 10,000 queries, top-k=10, ScaleFactor 4")
 
 
 def run_sq4(args):
@@ -831,17 +831,17 @@ def run_sq4(args):
         shard = e - b
         flops = 2.0 * nq * shard * SQ4_DIM
         achieved = flops / (scan_ms / 1000.0) / 1e12 if scan_ms > 0 else None
-        peak = 80.0
-        roof = {"bound": "fp32 ffma", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+        peak = 4500.0
+        roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOP/s",
                 "frac": (achieved / peak) if achieved else None, "traffic": None,
-                "peak_source": "nominal FP32 FFMA (148 SMs x 128 lanes x 2 flop x ~2.1 GHz); "
-                               "the INT4 scan runs the FFMA tile kernel",
+                "peak_source": "nominal dense INT8 tensor (no measured INT8 figure); the INT4 "
+                               "codes are scanned by tcgen05 kind::i8",
                 "kernel": "INT4 code scan", "kernel_ms": scan_ms,
-                "algorithmic_flops_per_launch": flops}
+                "algorithmic_int_ops_per_launch": flops}
         config = {"workload": SQ4_WORKLOAD, "global_batch": nq, "top_k": SQ4_K,
                   "base_vectors": n, "dim": SQ4_DIM, "metric": "l2", "refine_scale": SQ4_SCALE,
                   "parallelism": f"rows sharded over {world} GPU(s), NCCL all-gather + merge",
-                  "l2": "inputs larger than L2 (256 MB codes)"}
+                  "l2": "inputs larger than L2 (512 MB codes)"}
         print(json.dumps(common_line(nq, ms, e2e_ms, args, world, "i4 codes, f32/f64 scores",
                                      config, roof, cpu, clocks, st, SQ4_K, SQ4_DIM, 4)),
               flush=True)

@@ -80,10 +80,11 @@ typedef enum {
    * positions (quantized_index.go:313-335) and the optional refine stage. */
   XVEC_INDEX_IVF_SQ8 = 6,
   /* INT4 scalar-quantized Flat: core.ScalarQuantizedFlatIndex with
-   * QuantizationInt4 (quantization.go:91-103, 267-321): two codes in [-8, 7]
-   * per byte, the INT8 kind's scoring on them (QuantizedDistance,
-   * quantization.go:171-235) and the same optional refine stage.  The
-   * dimension must be even for rows and queries (ErrOddInt4Dimension). */
+   * QuantizationInt4 (quantization.go:91-103, 267-321): codes in [-8, 7],
+   * kept one per byte in device memory so that they share the INT8 kind's
+   * tcgen05 kind::i8 scan, its scoring (QuantizedDistance,
+   * quantization.go:171-235) and its optional refine stage.  The dimension
+   * must be even for rows and queries (ErrOddInt4Dimension). */
   XVEC_INDEX_SQ4_FLAT = 7
 } xvec_gpu_index_kind;
 

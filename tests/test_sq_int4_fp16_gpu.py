@@ -1,7 +1,8 @@
 """INT4 and FP16 scalar-quantized Flat search on the GPU against the oracle.
 
 INT4 (XVEC_INDEX_SQ4_FLAT): the oracle's SQ-Flat search over INT4 codes
-(quantized_index.go:296-335 with QuantizationInt4).  FP16: QuantizedDistance
+(quantized_index.go:296-335 with QuantizationInt4); the library keeps the
+codes one per byte and scans them with the INT8 kind's kernels.  FP16: QuantizedDistance
 decodes both binary16 vectors and applies metric.Compute (quantization.go:
 187-191), so the oracle is its Flat search over the decoded rows and queries.
 Keys identical, float32 scores bit-identical."""
@@ -57,8 +58,11 @@ def test_int4_parity(oracle, xb, metric, d):
     rows = scaled_gaussian(rng, 2500, d)
     keys = rng.permutation(50000)[:2500].astype(np.uint64)
     queries = scaled_gaussian(rng, 37, d)
+    st0 = xb.stats()
     run_int4(oracle, xb, metric, rows, keys, queries, 10)
     run_int4(oracle, xb, metric, rows, keys, queries, 10, refine=4.0)
+    if d == 128 and metric in (L2, IP):     # the tcgen05 kind::i8 scan of the INT8 kind
+        assert xb.stats()["tensor_scans"] > st0["tensor_scans"]
 
 
 def test_int4_filter_radius_ties(oracle, xb):

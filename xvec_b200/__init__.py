@@ -373,8 +373,9 @@ class ScalarQuantizedFlatIndex(_Index):
 
 class Int4QuantizedFlatIndex(_Index):
     """core.ScalarQuantizedFlatIndex with QuantizationInt4 (quantized_index.go:28-120,
-    quantization.go:91-103, 267-321): nibble-packed codes in [-8, 7], the INT8
-    kind's scoring and refine stage; rows and queries need an even dimension."""
+    quantization.go:91-103, 267-321): codes in [-8, 7] held one per byte on the
+    device, scanned, scored and refined by the INT8 kind's paths; rows and
+    queries need an even dimension."""
     kind = INDEX_SQ4_FLAT
 
 

@@ -75,21 +75,6 @@ __device__ __forceinline__ float load_elem(const float* p, int64_t i) { return p
 __device__ __forceinline__ float load_elem(const __half* p, int64_t i) { return __half2float(p[i]); }
 __device__ __forceinline__ float load_elem(const int8_t* p, int64_t i) { return (float)p[i]; }
 
-// INT4 codes, two per byte: element i is the low (even i) or high (odd i)
-// nibble of byte i / 2, two's complement (QuantizedVector.integerCode,
-// quantization.go:368-383).  A row of even dimension d holds d / 2 bytes, so
-// element k of row r is element r·d + k of the array.
-struct Int4Pair {
-  uint8_t b;
-};
-__device__ __forceinline__ int int4_at(const uint8_t* p, int64_t i) {
-  const int v = (i & 1) ? (p[i >> 1] >> 4) : (p[i >> 1] & 15);
-  return v - ((v & 8) << 1);
-}
-__device__ __forceinline__ float load_elem(const Int4Pair* p, int64_t i) {
-  return (float)int4_at(reinterpret_cast<const uint8_t*>(p), i);
-}
-
 // Go's min/max built-ins on floats propagate NaN.
 __device__ __forceinline__ float go_minf(float a, float b) {
   if (a != a || b != b) return __int_as_float(0x7fc00000);

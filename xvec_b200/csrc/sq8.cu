@@ -84,10 +84,10 @@ __device__ bool warp_quantize_int8(const float* v, int d, int8_t* codes, SQParam
 }
 
 // quantizeInteger (quantization.go:267-321) for INT4 ([-8, 7]), one warp per
-// vector of even dimension, a lane per element pair.  `packed` (d / 2 bytes)
-// and `unpacked` (d int8 codes) may each be null.
-__device__ bool warp_quantize_int4(const float* v, int d, uint8_t* packed, int8_t* unpacked,
-                                   SQParams* p) {
+// vector of even dimension, a lane per element pair.  The codes are written
+// one per byte (the reference packs two per byte; the values, code sums and
+// scores are the same).
+__device__ bool warp_quantize_int4(const float* v, int d, int8_t* codes, SQParams* p) {
   const int lane = threadIdx.x & 31;
   float mn = v[0], mx = v[0];
   for (int i = lane; i < d; i += 32) {
@@ -100,10 +100,7 @@ __device__ bool warp_quantize_int4(const float* v, int d, uint8_t* packed, int8_
   }
   const int half = d >> 1;
   if (mn == mx) {
-    for (int j = lane; j < half; j += 32) {
-      if (packed) packed[j] = 0;
-      if (unpacked) unpacked[2 * j] = unpacked[2 * j + 1] = 0;
-    }
+    for (int j = lane; j < half; j += 32) codes[2 * j] = codes[2 * j + 1] = 0;
     if (lane == 0) *p = SQParams{0.f, mn, 0.0, 0.0};
     return true;
   }
@@ -124,11 +121,8 @@ __device__ bool warp_quantize_int4(const float* v, int d, uint8_t* packed, int8_
       sum += c[e];
       sq += c[e] * c[e];
     }
-    if (packed) packed[j] = (uint8_t)((c[0] & 15) | ((c[1] & 15) << 4));
-    if (unpacked) {
-      unpacked[2 * j] = (int8_t)c[0];
-      unpacked[2 * j + 1] = (int8_t)c[1];
-    }
+    codes[2 * j] = (int8_t)c[0];
+    codes[2 * j + 1] = (int8_t)c[1];
   }
   for (int o = 16; o > 0; o >>= 1) {
     sum += __shfl_xor_sync(kFullMask, sum, o);
@@ -187,7 +181,8 @@ __device__ float sq_reference_score(int metric, double dot, const SQParams& l, c
 }
 
 // Rows: quantize, fast-rank terms and the index-wide error-bound maxima.
-// BITS 8: d int8 codes per row; BITS 4: d / 2 bytes of nibble pairs.
+// d int8 codes per row for either width (INT4 codes in [-8, 7], one per
+// byte, so both widths share the tcgen05 kind::i8 scan).
 template <int BITS>
 __global__ void sq8_encode_rows_kernel(const float* __restrict__ rows, int64_t n, int d,
                                        uint8_t* __restrict__ codes, SQParams* __restrict__ params,
@@ -199,10 +194,9 @@ __global__ void sq8_encode_rows_kernel(const float* __restrict__ rows, int64_t n
   SQParams p;
   __shared__ SQParams sp[8];
   const int wl = threadIdx.x >> 5;
-  const bool ok =
-      BITS == 8 ? warp_quantize_int8(rows + w * d, d, reinterpret_cast<int8_t*>(codes) + w * d,
-                                     &sp[wl])
-                : warp_quantize_int4(rows + w * d, d, codes + w * (d / 2), nullptr, &sp[wl]);
+  int8_t* row_codes = reinterpret_cast<int8_t*>(codes) + w * d;
+  const bool ok = BITS == 8 ? warp_quantize_int8(rows + w * d, d, row_codes, &sp[wl])
+                            : warp_quantize_int4(rows + w * d, d, row_codes, &sp[wl]);
   if (!ok) {
     if (lane == 0) atomicExch(err, XVEC_GPU_OVERFLOW);
     return;
@@ -250,7 +244,7 @@ __global__ void sq8_prep_queries_kernel(const float* __restrict__ q, int nq, int
   if (st == 0 && BITS == 4 && (d & 1)) st = XVEC_GPU_INVALID_ARGUMENT;
   if (st == 0 &&
       !(BITS == 8 ? warp_quantize_int8(v, d, qcodes + (int64_t)w * d, &sp[wl])
-                  : warp_quantize_int4(v, d, nullptr, qcodes + (int64_t)w * d, &sp[wl])))
+                  : warp_quantize_int4(v, d, qcodes + (int64_t)w * d, &sp[wl])))
     st = XVEC_GPU_OVERFLOW;
   __syncwarp();
   if (st != 0) {
@@ -310,18 +304,12 @@ struct SQ8Scorer {
   const SQParams* qparams;
   const float* q_eps;
   int d;
-  int int4;  // 1: nibble-packed INT4 rows (d / 2 bytes each)
   __device__ float score(int qi, int64_t row) const {
     const int lane = threadIdx.x & 31;
     const int8_t* b = qcodes + (int64_t)qi * d;
     int dot = 0;
-    if (!int4) {
-      const int8_t* a = reinterpret_cast<const int8_t*>(codes) + row * d;
-      for (int i = lane; i < d; i += 32) dot += (int)a[i] * (int)b[i];
-    } else {
-      const uint8_t* a = codes + row * (d / 2);
-      for (int i = lane; i < d; i += 32) dot += int4_at(a, i) * (int)b[i];
-    }
+    const int8_t* a = reinterpret_cast<const int8_t*>(codes) + row * d;
+    for (int i = lane; i < d; i += 32) dot += (int)a[i] * (int)b[i];
     for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(kFullMask, dot, o);
     return sq_reference_score(metric, (double)dot, params[row], qparams[qi], d);
   }
@@ -429,11 +417,8 @@ struct Sq8IvfPolicy {
 // ---------------------------------------------------------------------------
 // Insertion hooks.
 // ---------------------------------------------------------------------------
-// Code bytes per row: d (INT8) or d / 2 (INT4 nibble pairs).
-inline size_t sq_row_bytes(const xvec_gpu_index* idx) {
-  const int d = idx->desc.dimension;
-  return idx->desc.kind == XVEC_INDEX_SQ4_FLAT ? (size_t)(d / 2) : (size_t)d;
-}
+// Code bytes per row: d for both widths (INT4 codes are kept one per byte).
+inline size_t sq_row_bytes(const xvec_gpu_index* idx) { return (size_t)idx->desc.dimension; }
 
 xvec_gpu_status sq8_reserve(xvec_gpu_index* idx, int64_t cap, cudaStream_t s) {
   const size_t rb = sq_row_bytes(idx);
@@ -566,10 +551,10 @@ xvec_gpu_status sq8_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
   }
   XVEC_CUDA(cudaMemsetAsync(o_counts, 0, (size_t)nq * 4, s));
   SQ8Scorer sc{metric, idx->sq_codes.as<uint8_t>(), idx->sq_params.as<SQParams>(),
-               qcodes.as<int8_t>(), qparams.as<SQParams>(), qeps.as<float>(), d, int4 ? 1 : 0};
+               qcodes.as<int8_t>(), qparams.as<SQParams>(), qeps.as<float>(), d};
   const bool ranked = n > 0 && (metric == XVEC_METRIC_IP || metric == XVEC_METRIC_L2);
   // INT8 tensor cores (tcgen05 kind::i8) when the layout allows, else FFMA.
-  const bool use_tc = !int4 && ranked && kp + 128 <= flat_tc_cap() && n < (1ll << 31) - 256 &&
+  const bool use_tc = ranked && kp + 128 <= flat_tc_cap() && n < (1ll << 31) - 256 &&
                       sq8_tc_supported(d, idx->sq_codes.ptr, qcodes.ptr);
   const bool fast = use_tc || (ranked && simt_cap_for(kp) <= 512);
   if (use_tc) {
@@ -618,16 +603,9 @@ xvec_gpu_status sq8_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
       return st;
     const SQ8Ranker rk{metric, idx->sq_fast.as<float4>(), qinfo.as<float4>()};
     timer.mark(1);
-    if (int4)
-      XVEC_CUDA(launch_scan_simt(idx->sq_codes.as<Int4Pair>(), n, d, idx->keyrank.as<uint32_t>(),
-                                 qf.as<float>(), nq, d_bitmap, rk, parts, kp,
-                                 pkeys.as<uint64_t>(), pcounts.as<int>(), psat.as<uint64_t>(),
-                                 qflags.as<int>(), s));
-    else
-      XVEC_CUDA(launch_scan_simt(idx->sq_codes.as<int8_t>(), n, d, idx->keyrank.as<uint32_t>(),
-                                 qf.as<float>(), nq, d_bitmap, rk, parts, kp,
-                                 pkeys.as<uint64_t>(), pcounts.as<int>(), psat.as<uint64_t>(),
-                                 qflags.as<int>(), s));
+    XVEC_CUDA(launch_scan_simt(idx->sq_codes.as<int8_t>(), n, d, idx->keyrank.as<uint32_t>(),
+                               qf.as<float>(), nq, d_bitmap, rk, parts, kp, pkeys.as<uint64_t>(),
+                               pcounts.as<int>(), psat.as<uint64_t>(), qflags.as<int>(), s));
     timer.mark(2);
     XVEC_CUDA(launch_merge_rescore(sc, idx->pos_of_kr.as<uint32_t>(), idx->keys.as<uint64_t>(),
                                    nullptr, nq, stage_k, stage_radius, 0, pkeys.as<uint64_t>(),
