@@ -85,7 +85,11 @@ typedef enum {
    * tcgen05 kind::i8 scan, its scoring (QuantizedDistance,
    * quantization.go:171-235) and its optional refine stage.  The dimension
    * must be even for rows and queries (ErrOddInt4Dimension). */
-  XVEC_INDEX_SQ4_FLAT = 7
+  XVEC_INDEX_SQ4_FLAT = 7,
+  /* IVF with INT4 scalar-quantized scoring of the probed lists' rows:
+   * ScalarQuantizedIVFIndex with QuantizationInt4 (ivf_quantized.go:31-54),
+   * the IVF_SQ8 kind with INT4 codes (kept one per byte, as SQ4_FLAT). */
+  XVEC_INDEX_IVF_SQ4 = 8
 } xvec_gpu_index_kind;
 
 typedef enum {

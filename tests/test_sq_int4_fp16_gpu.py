@@ -98,6 +98,42 @@ def test_int4_odd_dimension(xb):
     idx.close()
 
 
+@pytest.mark.parametrize("metric", [L2, IP, COSINE])
+def test_int4_ivf_is_int4_over_the_probed_lists(oracle, xb, metric):
+    """ScalarQuantizedIVFIndex with QuantizationInt4 (ivf_quantized.go:135-192)
+    is the INT4 SQ search restricted to the probed lists' positions: per
+    query, the oracle's INT4 search with a filter holding exactly those
+    positions (the same composition the oracle pins for INT8)."""
+    from oracle.zvecivf import csr_of
+    rng = np.random.default_rng(60 + metric)
+    n, d, nlist = 3000, 64, 16
+    rows = scaled_gaussian(rng, n, d)
+    keys = rng.permutation(1 << 20)[:n].astype(np.uint64)
+    cents = rows[rng.choice(n, nlist, replace=False)].copy()
+    lists = rng.integers(0, nlist, n).astype(np.int32)
+    queries = scaled_gaussian(rng, 21, d)
+    idx = xb.Int4QuantizedIVFIndex(d, metric)
+    idx.set_model(cents)
+    idx.add_with_lists(keys, rows, lists)
+    offsets, positions = csr_of(lists, nlist)
+    packed, params = oracle.quantize_int4_batch(rows)
+    for nprobe, scale in ((4, 0.0), (4, 3.0), (nlist, 0.0)):
+        res = idx.search_with_options(queries, xb.SearchOptions(top_k=10, nprobe=nprobe,
+                                                                 refine_scale=scale),
+                                      raise_on_error=False)
+        for q in range(queries.shape[0]):
+            probed = oracle.ivf_probe(metric, cents, queries[q], nprobe)
+            bitmap = np.zeros((n + 31) // 32, np.uint32)
+            for li in probed:
+                for p in positions[offsets[li]:offsets[li + 1]]:
+                    bitmap[p >> 5] |= np.uint32(1 << int(p & 31))
+            st, ok, os_, oc, ost = oracle.sq4_search(metric, packed, params, rows, keys,
+                                                     queries[q:q + 1], 10, 0.0, scale, bitmap)
+            one = type(res)(res.keys[q:q + 1], res.scores[q:q + 1], res.counts[q:q + 1])
+            compare(one, ok, os_, oc, ost, (metric, nprobe, scale, q))
+    idx.close()
+
+
 @pytest.mark.parametrize("metric", [L2, IP, COSINE, MIPSL2])
 def test_fp16_quantized_parity(oracle, xb, metric):
     rng = np.random.default_rng(90 + metric)

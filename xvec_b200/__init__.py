@@ -34,7 +34,7 @@ LIB_PATH = os.path.join(HERE, "libxvec_gpu.so")
 METRIC_L2, METRIC_IP, METRIC_COSINE, METRIC_MIPSL2 = 1, 2, 3, 4
 INDEX_FLAT, INDEX_SQ8_FLAT, INDEX_IVF_PQ, INDEX_RABITQ, INDEX_IVF_FLAT, INDEX_IVF_SQ8 = (
     1, 2, 3, 4, 5, 6)
-INDEX_SQ4_FLAT = 7
+INDEX_SQ4_FLAT, INDEX_IVF_SQ4 = 7, 8
 STORAGE_FP32, STORAGE_FP16 = 1, 2
 
 STATUS_NAMES = {
@@ -518,6 +518,13 @@ class ScalarQuantizedIVFIndex(IVFIndex):
     probed lists' rows with INT8 codes (refine_scale > 0: exact rerank of the
     floor(top_k * scale) best codes)."""
     kind = INDEX_IVF_SQ8
+
+
+class Int4QuantizedIVFIndex(IVFIndex):
+    """ScalarQuantizedIVFIndex with QuantizationInt4 (ivf_quantized.go:31-54):
+    the INT8 kind's probe, list scan and refine stage over INT4 codes (held
+    one per byte on the device)."""
+    kind = INDEX_IVF_SQ4
 
 
 class RaBitQIndex(_Index):

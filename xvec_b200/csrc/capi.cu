@@ -468,6 +468,7 @@ xvec_gpu_status search_device_locked(xvec_gpu_index* idx, const void* d_q, int n
       return ivf_flat_search_impl(idx, static_cast<const float*>(d_q), nq, o, d_bitmap, d_keys,
                                   d_scores, d_counts, s, statuses);
     case XVEC_INDEX_IVF_SQ8:
+    case XVEC_INDEX_IVF_SQ4:
       return ivf_sq8_search_impl(idx, static_cast<const float*>(d_q), nq, o, d_bitmap, d_keys,
                                  d_scores, d_counts, s, statuses);
     default: return set_error("invalid index kind"), XVEC_GPU_INVALID_ARGUMENT;
@@ -608,6 +609,7 @@ extern "C" xvec_gpu_status xvec_gpu_index_create(const xvec_gpu_index_desc* desc
     case XVEC_INDEX_SQ8_FLAT:
     case XVEC_INDEX_SQ4_FLAT:
     case XVEC_INDEX_IVF_SQ8:
+    case XVEC_INDEX_IVF_SQ4:
       if (desc->dimension > 65535)
         return set_error("core: invalid vector dimension: got %d", desc->dimension),
                XVEC_GPU_INVALID_ARGUMENT;

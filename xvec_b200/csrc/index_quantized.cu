@@ -25,7 +25,7 @@ xvec_gpu_status extra_reserve(xvec_gpu_index* idx, int64_t cap, cudaStream_t s) 
   if (idx->desc.kind == XVEC_INDEX_IVF_PQ) return ivfpq_reserve(idx, cap, s);
   if (idx->desc.kind == XVEC_INDEX_RABITQ) return rabitq_reserve(idx, cap, s);
   if (idx->desc.kind == XVEC_INDEX_IVF_FLAT) return ivf_flat_reserve(idx, cap, s);
-  if (idx->desc.kind == XVEC_INDEX_IVF_SQ8) {
+  if (idx->desc.kind == XVEC_INDEX_IVF_SQ8 || idx->desc.kind == XVEC_INDEX_IVF_SQ4) {
     const xvec_gpu_status st = sq8_reserve(idx, cap, s);
     return st ? st : ivf_flat_reserve(idx, cap, s);
   }
@@ -36,7 +36,8 @@ xvec_gpu_status extra_validate(xvec_gpu_index* idx, int64_t, int64_t, cudaStream
     return set_error("set the IVF-PQ model before adding rows"), XVEC_GPU_INVALID_ARGUMENT;
   if (idx->desc.kind == XVEC_INDEX_RABITQ && !idx->has_model)
     return set_error("set the RaBitQ model before adding rows"), XVEC_GPU_INVALID_ARGUMENT;
-  if ((idx->desc.kind == XVEC_INDEX_IVF_FLAT || idx->desc.kind == XVEC_INDEX_IVF_SQ8) &&
+  if ((idx->desc.kind == XVEC_INDEX_IVF_FLAT || idx->desc.kind == XVEC_INDEX_IVF_SQ8 ||
+       idx->desc.kind == XVEC_INDEX_IVF_SQ4) &&
       !idx->has_model)
     return set_error("set the IVF model before adding rows"), XVEC_GPU_INVALID_ARGUMENT;
   return XVEC_GPU_OK;
@@ -55,7 +56,7 @@ xvec_gpu_status extra_commit(xvec_gpu_index* idx, int64_t old_n, int64_t m, cuda
   if (idx->desc.kind == XVEC_INDEX_IVF_PQ) return ivfpq_commit(idx, old_n, m, s);
   if (idx->desc.kind == XVEC_INDEX_RABITQ) return rabitq_commit(idx, old_n, m, s);
   if (idx->desc.kind == XVEC_INDEX_IVF_FLAT) return ivf_flat_commit(idx, old_n, m, s);
-  if (idx->desc.kind == XVEC_INDEX_IVF_SQ8) {
+  if (idx->desc.kind == XVEC_INDEX_IVF_SQ8 || idx->desc.kind == XVEC_INDEX_IVF_SQ4) {
     const xvec_gpu_status st = sq8_commit(idx, old_n, m, s);
     return st ? st : ivf_flat_commit(idx, old_n, m, s);
   }

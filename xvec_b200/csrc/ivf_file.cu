@@ -227,7 +227,8 @@ extern "C" xvec_gpu_status xvec_gpu_ivf_add_with_lists(xvec_gpu_index* idx, cons
                                                        int64_t n) {
   if (!idx || n < 0 || (n > 0 && (!keys || !rows || !lists)))
     return set_error("invalid add arguments"), XVEC_GPU_INVALID_ARGUMENT;
-  if (idx->desc.kind != XVEC_INDEX_IVF_FLAT && idx->desc.kind != XVEC_INDEX_IVF_SQ8)
+  if (idx->desc.kind != XVEC_INDEX_IVF_FLAT && idx->desc.kind != XVEC_INDEX_IVF_SQ8 &&
+      idx->desc.kind != XVEC_INDEX_IVF_SQ4)
     return set_error("not an IVF index"), XVEC_GPU_INVALID_ARGUMENT;
   if (n == 0) return XVEC_GPU_OK;
   std::unique_lock<std::shared_mutex> lock(idx->mu);

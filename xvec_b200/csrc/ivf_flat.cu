@@ -406,7 +406,8 @@ using namespace xvec;
 extern "C" xvec_gpu_status xvec_gpu_ivf_set_model(xvec_gpu_index* idx, const float* centroids,
                                                   int32_t nlist) {
   if (!idx || !centroids) return set_error("nil argument"), XVEC_GPU_INVALID_ARGUMENT;
-  if (idx->desc.kind != XVEC_INDEX_IVF_FLAT && idx->desc.kind != XVEC_INDEX_IVF_SQ8)
+  if (idx->desc.kind != XVEC_INDEX_IVF_FLAT && idx->desc.kind != XVEC_INDEX_IVF_SQ8 &&
+      idx->desc.kind != XVEC_INDEX_IVF_SQ4)
     return set_error("not an IVF index"), XVEC_GPU_INVALID_ARGUMENT;
   if (nlist <= 0) return set_error("core: IVF NList must be positive"), XVEC_GPU_INVALID_ARGUMENT;
   const int d = idx->desc.dimension;

@@ -742,7 +742,8 @@ xvec_gpu_status rebuild_lists(xvec_gpu_index* idx, cudaStream_t s) {
     XVEC_LAUNCHED();
     XVEC_CUDA(cudaGetLastError());
   }
-  if (idx->desc.kind == XVEC_INDEX_IVF_SQ8 && idx->desc.dimension % 16 == 0) {
+  if ((idx->desc.kind == XVEC_INDEX_IVF_SQ8 || idx->desc.kind == XVEC_INDEX_IVF_SQ4) &&
+      idx->desc.dimension % 16 == 0) {
     const int d = idx->desc.dimension;
     const int64_t padded = (n + 31) / 32 * 32;
     if ((st = idx->list_sq_codes.reserve((size_t)padded * d, 0, s)) ||

@@ -449,7 +449,8 @@ xvec_gpu_status sq8_commit(xvec_gpu_index* idx, int64_t old_n, int64_t m, cudaSt
                          (long long)(old_n + i)),
                XVEC_GPU_NON_FINITE;
   }
-  const bool int4 = idx->desc.kind == XVEC_INDEX_SQ4_FLAT;
+  const bool int4 =
+      idx->desc.kind == XVEC_INDEX_SQ4_FLAT || idx->desc.kind == XVEC_INDEX_IVF_SQ4;
   if (int4 && (d & 1))
     return set_error("core: quantize vector %lld: core: INT4 quantization requires an even "
                      "dimension: got %d",
@@ -745,10 +746,16 @@ xvec_gpu_status ivf_sq8_search_impl(xvec_gpu_index* idx, const float* d_q, int n
     return st;
   XVEC_CUDA(cudaMemsetAsync(qflags.ptr, 0, (size_t)nq * 4, s));
   XVEC_CUDA(cudaMemsetAsync(qstatus.ptr, 0, (size_t)nq * 4, s));
-  sq8_prep_queries_kernel<8><<<blocks_of((int64_t)nq * 32), 256, 0, s>>>(
-      d_q, nq, d, metric, idx->sq_bounds.as<unsigned>(), qcodes.as<int8_t>(),
-      qparams.as<SQParams>(), qf.as<float>(), qinfo.as<float4>(), qeps.as<float>(),
-      qstatus.as<int>());
+  if (idx->desc.kind == XVEC_INDEX_IVF_SQ4)
+    sq8_prep_queries_kernel<4><<<blocks_of((int64_t)nq * 32), 256, 0, s>>>(
+        d_q, nq, d, metric, idx->sq_bounds.as<unsigned>(), qcodes.as<int8_t>(),
+        qparams.as<SQParams>(), qf.as<float>(), qinfo.as<float4>(), qeps.as<float>(),
+        qstatus.as<int>());
+  else
+    sq8_prep_queries_kernel<8><<<blocks_of((int64_t)nq * 32), 256, 0, s>>>(
+        d_q, nq, d, metric, idx->sq_bounds.as<unsigned>(), qcodes.as<int8_t>(),
+        qparams.as<SQParams>(), qf.as<float>(), qinfo.as<float4>(), qeps.as<float>(),
+        qstatus.as<int>());
   XVEC_LAUNCHED();
   launch_prep_queries<float>(d_q, nq, d, metric, pf.as<float>(), pn2.as<float>(),
                              paux.as<float>(), pstatus.as<int>(), s);
