@@ -45,7 +45,11 @@ def parse():
     p.add_argument("--nq", type=int, default=N_QUERIES)
     p.add_argument("--cpu-sample-rows", type=int, default=1_000_000)
     p.add_argument("--cpu-sample-queries", type=int, default=480)
+    p.add_argument("--ref-queries", type=int, default=0,
+                   help="--impl reference: queries per step (default: one per host thread)")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-parity", action="store_true",
+                   help="skip the check of sampled queries against the oracle over the full base")
     p.add_argument("--batch-sweep", default="",
                    help="comma-separated batch sizes (e.g. 1,8,64): after the main timing, "
                         "the median device latency of one search of each size is added to "
@@ -100,6 +104,17 @@ def mixture_chunk(torch, centers, chunk_index, rows, device, seed=99):
 
 def make_queries(torch, centers, nq, device):
     return mixture_chunk(torch, centers, 10**6, nq, device, seed=7)
+
+
+def host_chunks(torch, centers, n, device):
+    """The whole base again, chunk by chunk, as the float32 decoding of the
+    stored binary16 rows (what the reference scores for a VectorFP16 field),
+    with their keys: (rows [m, 768] float32, keys [m] uint64) on the host."""
+    import numpy as np
+    for c in range((n + CHUNK - 1) // CHUNK):
+        m = min(CHUNK, n - c * CHUNK)
+        rows = mixture_chunk(torch, centers, c, m, device).float().cpu().numpy()
+        yield rows, np.arange(c * CHUNK, c * CHUNK + m, dtype=np.uint64)
 
 
 # ---------------------------------------------------------------------------
@@ -170,66 +185,152 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------
-# CPU baseline: the oracle (reference C kernels when built) on a bounded sample.
+# The oracle over the full base: parity of sampled queries, the CPU baseline
+# and the reference arm.
 # ---------------------------------------------------------------------------
-def cpu_flat_cosine_qps(rows_f32, queries_f32, n_total, k):
-    import numpy as np
+PARITY_QUERIES = 32
 
-    from oracle.oracle import COSINE, Oracle, ReferenceFloats
+
+def oracle_with_kernels():
+    """The oracle, with the reference's own float kernels (floats_avx512.c,
+    compiled in place into oracle/_ref) when they are built and the host has
+    AVX-512; returns (oracle, kind)."""
+    from oracle.oracle import Oracle, ReferenceFloats
     ora = Oracle()
-    kind = "port"
     if ReferenceFloats.available():
         ora.use_reference_kernels(ReferenceFloats())
-        kind = "reference"
-    keys = np.arange(rows_f32.shape[0], dtype=np.uint64)
-    threads = os.cpu_count() or 1
+        return ora, "reference"
+    return ora, "port"
+
+
+def sample_query_ids(nq, count=PARITY_QUERIES):
+    import numpy as np
+    return np.unique(np.linspace(0, nq - 1, min(count, nq)).astype(np.int64))
+
+
+def oracle_flat_over_chunks(ora, metric, chunks, queries, k, threads):
+    """Flat top-k of `queries` over every row of `chunks` (an iterable of
+    (rows float32 [m, d], keys uint64 [m])) by the oracle: the top-k of each
+    chunk (topKPrevalidatedCandidatesWithOptions), then per query the
+    oracle's MergeSearchResults of those lists.  Exact: an entry of the top-k
+    over all rows is in the top-k of its own chunk under the same (score,
+    key) order.  Returns keys [nq, k], scores [nq, k], counts [nq] and the
+    seconds spent in the oracle (searches and merges)."""
+    import numpy as np
+    nq = queries.shape[0]
+    lk = [[] for _ in range(nq)]
+    ls = [[] for _ in range(nq)]
+    secs = 0.0
+    for rows, keys in chunks:
+        t0 = time.perf_counter()
+        st, ok, os_, oc, ost = ora.flat_search(metric, rows, keys, queries, k, threads=threads)
+        secs += time.perf_counter() - t0
+        if st != 0 or (ost != 0).any():
+            raise RuntimeError(f"oracle search status {st} / {ost[ost != 0][:4]}")
+        for q in range(nq):
+            lk[q].append(ok[q, :oc[q]])
+            ls[q].append(os_[q, :oc[q]])
+    out_k = np.zeros((nq, k), np.uint64)
+    out_s = np.zeros((nq, k), np.float32)
+    out_c = np.zeros(nq, np.int32)
     t0 = time.perf_counter()
-    st, _, _, _, _ = ora.flat_search(COSINE, rows_f32, keys, queries_f32, k, threads=threads)
-    dt = time.perf_counter() - t0
-    if st != 0:
-        raise RuntimeError(f"oracle status {st}")
-    qps_sample = queries_f32.shape[0] / dt
-    value = qps_sample * rows_f32.shape[0] / n_total
-    sample = (f"{queries_f32.shape[0]} queries x {rows_f32.shape[0]}-row prefix of the base, "
-              f"{dt:.1f} s on {threads} threads; QPS scaled by rows/{n_total} (work is linear "
-              f"in rows); distance kernels: "
-              + ("the reference's floats_avx512.c compiled in place" if kind == "reference"
-                 else "the oracle's restatement") + "; heap/top-k: ported Go rules")
-    return {"value": value, "unit": "queries/sec", "cores": threads, "kind": kind,
-            "sample": sample}
+    for q in range(nq):
+        mk, ms = ora.merge_results(metric, k, np.concatenate(lk[q]), np.concatenate(ls[q]))
+        out_c[q] = len(mk)
+        out_k[q, :len(mk)] = mk
+        out_s[q, :len(ms)] = ms
+    secs += time.perf_counter() - t0
+    return out_k, out_s, out_c, secs
+
+
+def parity_record(gpu, ref, qids, base_rows, kind, oracle_s, what):
+    """Compares the GPU's results of the sampled queries with the oracle's:
+    identical counts and keys, bit-identical float32 scores."""
+    import numpy as np
+    gk, gs, gc = gpu
+    rk, rs, rc = ref
+    bad = []
+    for i, q in enumerate(qids):
+        c = int(rc[i])
+        same = (int(gc[q]) == c and np.array_equal(gk[q, :c].view(np.uint64), rk[i, :c])
+                and np.array_equal(gs[q, :c].view(np.uint32), rs[i, :c].view(np.uint32)))
+        if not same:
+            bad.append(int(q))
+    return {"queries": int(len(qids)), "query_ids": f"{len(qids)} ids evenly spaced over the batch",
+            "base_rows": int(base_rows), "against": what, "oracle_kernels": kind,
+            "keys_identical": not bad, "scores_bitwise": not bad, "mismatched_queries": bad[:8],
+            "oracle_s": oracle_s}
+
+
+def gpu_results_host(search, queries, opts):
+    """One more search of the whole batch; its results on the host."""
+    import numpy as np
+    import torch
+    keys, scores, counts = search.search_device(queries, opts)
+    torch.cuda.synchronize()
+    return (keys.cpu().numpy().view(np.uint64), scores.cpu().numpy(), counts.cpu().numpy())
 
 
 def run_reference(args):
-    """--impl reference: the CPU path of the reference on the host cores."""
+    """--impl reference: the reference's CPU path for the default workload on
+    the host cores.  Each step is a bounded sample of the workload: a few of
+    the batch's queries, each scored against every one of the n rows with the
+    reference's own floats_avx512.c kernels (when built; the oracle's
+    restatement otherwise) and the ported heap/top-k and merge rules, on all
+    host threads.  The rows are the float32 decodings of the binary16 base,
+    generated once (on the GPU when there is one, which only makes the
+    synthetic data) and held in host memory; when the host cannot hold them
+    they are regenerated chunk by chunk every step, outside the timed part.
+    value = sampled queries / measured step time; nothing is scaled."""
     import numpy as np
     import torch
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    torch.manual_seed(0)
-    centers = mixture_centers(torch, "cpu")
-    n_rows = min(args.cpu_sample_rows, args.n)
-    rows = torch.cat([mixture_chunk(torch, centers, c, min(CHUNK, n_rows - c * CHUNK), "cpu")
-                      for c in range((n_rows + CHUNK - 1) // CHUNK)])
-    rows = rows.float().numpy()
-    queries = make_queries(torch, centers, max(args.cpu_sample_queries, 8), "cpu").float().numpy()
-    per = max(4, args.cpu_sample_queries // 2)
-    vals = []
+    from oracle.oracle import COSINE
+    dev = torch.device("cuda", 0) if torch.cuda.is_available() else torch.device("cpu")
+    n, k = args.n, TOP_K
+    centers = mixture_centers(torch, dev)
+    queries = make_queries(torch, centers, args.nq, dev)
+    threads = os.cpu_count() or 1
+    per = max(1, min(args.nq, args.ref_queries or threads))
+    ora, kind = oracle_with_kernels()
+    need = n * DIM * 4
+    try:
+        import psutil
+        avail = psutil.virtual_memory().available
+    except Exception:
+        avail = 0
+    held = need < 0.6 * avail
+    cache = list(host_chunks(torch, centers, n, dev)) if held else None
+    step_s = []
     for i in range(args.warmup + args.steps):
-        q = queries[(i * per) % queries.shape[0]:][:per]
-        r = cpu_flat_cosine_qps(rows, q, args.n, TOP_K)
+        ids = (np.arange(per) + i * per) % args.nq
+        q = queries[torch.as_tensor(ids, device=dev)].float().cpu().numpy()
+        chunks = cache if held else host_chunks(torch, centers, n, dev)
+        _, _, _, secs = oracle_flat_over_chunks(ora, COSINE, chunks, q, k, threads)
         if i >= args.warmup:
-            vals.append(r)
-    value = sum(v["value"] for v in vals) / len(vals)
+            step_s.append(secs)
+    ms = 1000.0 * sum(step_s) / len(step_s)
+    value = per / (ms / 1000.0)
+    sample = (f"{per} of the {args.nq} queries per step, each over all {n} rows (float32 "
+              f"decodings of the binary16 base, "
+              + ("held in host memory" if held else "regenerated per step outside the timing")
+              + f"); {args.steps} timed steps after {args.warmup} warm-up; {threads} threads; "
+              "distance kernels: "
+              + ("the reference's floats_avx512.c compiled in place" if kind == "reference"
+                 else "the oracle's restatement")
+              + "; per-chunk top-k merged by MergeSearchResults")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "queries/sec",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1000.0 * args.nq / value, "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "global_batch": args.nq, "top_k": TOP_K,
-                   "base_vectors": args.n, "dim": DIM, "metric": "cosine", "storage": "fp16",
-                   "parallelism": "host threads"},
-        "cpu_baseline": {**vals[-1], "value": value},
+        "ms_per_step": ms, "queries_per_step": per, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "global_batch": args.nq, "top_k": k,
+                   "base_vectors": n, "dim": DIM, "metric": "cosine", "storage": "fp16",
+                   "parallelism": "host threads (one query per task, as core.BatchTopK)"},
+        "cpu_baseline": {"value": value, "unit": "queries/sec", "cores": threads, "kind": kind,
+                         "sample": sample},
         "e2e": {"value": value, "unit": "queries/sec", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -1210,25 +1311,50 @@ def main():
         e2e_ms = float(t.item())
     e2e_value = nq / (e2e_ms / 1000.0)
 
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        m = min(args.cpu_sample_rows, n)
-        rows_s = torch.cat([mixture_chunk(torch, centers, c, min(CHUNK, m - c * CHUNK), dev)
-                            for c in range((m + CHUNK - 1) // CHUNK)])
-        cpu = cpu_flat_cosine_qps(rows_s.float().cpu().numpy(),
-                                  queries[:args.cpu_sample_queries].float().cpu().numpy(), n, k)
-        del rows_s
+    # --- parity on the full base (and, at N = 1, the CPU baseline) -----------
+    # Every rank takes the same collective step (the search), then rank 0
+    # checks the sampled queries against the oracle over all n rows, which it
+    # regenerates chunk by chunk; the others wait at the closing barrier.
+    gpu_res = gpu_results_host(search, queries, opts)
+    cpu, parity = None, None
+    if rank == 0 and not args.no_parity:
+        from oracle.oracle import COSINE
+        qids = sample_query_ids(nq)
+        ora, kind = oracle_with_kernels()
+        threads = os.cpu_count() or 1
+        qsel = queries[torch.as_tensor(qids, device=dev)].float().cpu().numpy()
+        rk, rs, rc, secs = oracle_flat_over_chunks(ora, COSINE, host_chunks(torch, centers, n, dev),
+                                                   qsel, k, threads)
+        parity = parity_record(gpu_res, (rk, rs, rc), qids, n, kind, secs,
+                               "oracle Flat cosine over all rows (per-chunk top-k merged by "
+                               "MergeSearchResults)")
+        if world == 1 and not args.no_cpu_baseline:
+            cpu = {"value": len(qids) / secs, "unit": "queries/sec", "cores": threads,
+                   "kind": kind,
+                   "sample": f"{len(qids)} of the {nq} queries over all {n} rows (float32 "
+                             f"decodings of the stored binary16 rows, held in host memory one "
+                             f"{CHUNK}-row chunk at a time), {secs:.1f} s of oracle time on "
+                             f"{threads} threads; no scaling; distance kernels: "
+                             + ("the reference's floats_avx512.c compiled in place"
+                                if kind == "reference" else "the oracle's restatement")
+                             + "; heap/top-k and merge: the ported Go rules"}
 
     if rank == 0:
         bf16_peak, hbm_peak, peak_kind = peaks()
         shard_rows = min(n, per_rank * CHUNK)
         flops = 2.0 * nq * shard_rows * DIM  # one launch of the scan on one shard
         achieved = flops / (scan_ms / 1000.0) / 1e12 if scan_ms > 0 else None
+        # DRAM traffic of the scan from the ncu capture of the one-GPU
+        # workload, scaled to this shard by its rows (the scan streams its
+        # shard's rows once per pass over the query blocks, so its traffic is
+        # proportional to the rows it holds).
         traffic = None
         tfile = os.path.join(ROOT, "profiles", "flat_scan_traffic.json")
         if os.path.exists(tfile):
             try:
-                traffic = json.load(open(tfile)).get("bytes_per_launch_full_workload")
+                tjs = json.load(open(tfile))
+                traffic = (tjs["bytes_per_launch_full_workload"] * shard_rows
+                           / tjs.get("rows_full_workload", N_BASE))
             except Exception:
                 traffic = None
         line = {
@@ -1250,6 +1376,7 @@ def main():
                          "kernel": "candidate scan", "kernel_ms": scan_ms,
                          "algorithmic_flops_per_launch": flops},
             "cpu_baseline": cpu,
+            "parity": parity,
             "clocks": clocks.summary(),
             "gpu_launches": launches,
             "exact_queries": int(st["exact_queries"]),

@@ -107,7 +107,14 @@ __device__ __forceinline__ float go_max_zero(float a, float b) {
 //   MODE 0: sum (x-q)^2                     (xvec_avx512_l2_squared)
 //   MODE 1: sum x*q                         (xvec_avx512_inner_product)
 //   MODE 2: sum x*q, sum x*x, sum q*q       (xvec_avx512_dot_norms)
+// For d >= 16 each half-warp evaluates the row its own lanes pass: the two
+// halves may pass two different rows (two candidates per warp) or the same
+// one.  Lane j of a half holds the AVX-512 accumulator lane j; its loads are
+// issued kRefBatch 16-element blocks at a time so that their latencies
+// overlap, and its fused multiply-adds keep the reference's order.
 // ---------------------------------------------------------------------------
+constexpr int kRefBatch = 8;
+
 template <int MODE, typename RowT>
 __device__ __forceinline__ void warp_reference_sums(const RowT* x, const float* q, int d,
                                                     float* s0, float* s1, float* s2) {
@@ -115,28 +122,38 @@ __device__ __forceinline__ void warp_reference_sums(const RowT* x, const float* 
   float r0 = 0.f, r1 = 0.f, r2 = 0.f;
   if (d >= 16) {
     const int blocks = d >> 4;
+    const int j = lane & 15;
     float a0 = 0.f, a1 = 0.f, a2 = 0.f;
-    if (lane < 16) {
-      for (int v = 0; v < blocks; ++v) {
-        const float xv = load_elem(x, v * 16 + lane), qv = q[v * 16 + lane];
+    for (int v0 = 0; v0 < blocks; v0 += kRefBatch) {
+      float xv[kRefBatch], qv[kRefBatch];
+#pragma unroll
+      for (int u = 0; u < kRefBatch; ++u) {
+        const bool in = v0 + u < blocks;
+        xv[u] = in ? load_elem(x, (int64_t)(v0 + u) * 16 + j) : 0.f;
+        qv[u] = in ? q[(int64_t)(v0 + u) * 16 + j] : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < kRefBatch; ++u) {
+        if (v0 + u >= blocks) break;
         if (MODE == 0) {
-          const float df = __fsub_rn(xv, qv);
+          const float df = __fsub_rn(xv[u], qv[u]);
           a0 = __fmaf_rn(df, df, a0);
         } else {
-          a0 = __fmaf_rn(xv, qv, a0);
+          a0 = __fmaf_rn(xv[u], qv[u], a0);
           if (MODE == 2) {
-            a1 = __fmaf_rn(xv, xv, a1);
-            a2 = __fmaf_rn(qv, qv, a2);
+            a1 = __fmaf_rn(xv[u], xv[u], a1);
+            a2 = __fmaf_rn(qv[u], qv[u], a2);
           }
         }
       }
     }
-    // reduce512: lanes added in index order to a zero start.
-    for (int j = 0; j < 16; ++j) {
-      r0 = __fadd_rn(r0, __shfl_sync(kFullMask, a0, j));
+    // reduce512: lanes added in index order to a zero start (within each
+    // half-warp).
+    for (int t = 0; t < 16; ++t) {
+      r0 = __fadd_rn(r0, __shfl_sync(kFullMask, a0, t, 16));
       if (MODE == 2) {
-        r1 = __fadd_rn(r1, __shfl_sync(kFullMask, a1, j));
-        r2 = __fadd_rn(r2, __shfl_sync(kFullMask, a2, j));
+        r1 = __fadd_rn(r1, __shfl_sync(kFullMask, a1, t, 16));
+        r2 = __fadd_rn(r2, __shfl_sync(kFullMask, a2, t, 16));
       }
     }
     // Fused scalar tail (the AVX-512 file is compiled with -mfma).

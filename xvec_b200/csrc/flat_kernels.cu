@@ -168,6 +168,7 @@ struct FlatScorer {
   __device__ float eps(int qi) const {
     return fast_eps(metric, d, q_n2[qi], ordered_to_float(*max_n2_ordered), split);
   }
+  __device__ bool half_warp() const { return d >= 16; }
   __device__ int error_flag(float) const { return 4; }
   __device__ float output(float r) const { return score_from_rank(metric, r); }
   __device__ bool keep(float out, float radius) const { return within_radius(metric, out, radius); }

@@ -81,6 +81,7 @@ struct IvfFlatScorer {
     return ivf_reference_score(metric, rows + pos * d, row_n2[pos], qf + (int64_t)qi * d,
                                q_n2[qi], d);
   }
+  __device__ bool half_warp() const { return d >= 16; }
   __device__ float eps(int qi) const {
     // The Flat bound covers the float32 dot against either cosine formula.
     const float u = 5.9604645e-8f, g = 4.f * (float)(d + 8) * u;
@@ -111,6 +112,7 @@ struct IvfProbeScorer {
     return ivf_reference_score(kMetricCosine, cents + c * d, cent_n2[c], qf + (int64_t)qi * d,
                                q_n2[qi], d);
   }
+  __device__ bool half_warp() const { return d >= 16; }
   __device__ float eps(int) const { return 0.f; }
   __device__ int error_flag(float) const { return 4; }
   __device__ float output(float r) const { return r; }

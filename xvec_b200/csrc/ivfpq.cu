@@ -484,6 +484,7 @@ struct PQScorer {
     return s;
   }
   __device__ float eps(int qi) const { return q_eps ? q_eps[qi] : 0.f; }
+  __device__ bool half_warp() const { return false; }
   __device__ int error_flag(float) const { return 8; }
   __device__ float output(float r) const { return score_from_rank(metric, r); }
   __device__ bool keep(float out, float radius) const { return within_radius(metric, out, radius); }

@@ -15,6 +15,9 @@
 //          float rank(float dot, const RowInfo&, const QueryInfo&);
 // Scorer:  int metric (ordering and radius rule);
 //          float score(int qi, int64_t row)  -- called by a whole warp;
+//          bool half_warp()                   -- true: score() evaluates the
+//                                                row of each half-warp apart,
+//                                                so a warp scores two rows;
 //          float eps(int qi)                  -- bound on |fast - reference|;
 //          int error_flag(float s)            -- flag bit for a non-finite score;
 //          float output(float rank)           -- the reported score of a rank;
@@ -175,12 +178,27 @@ __global__ void __launch_bounds__(256) scan_exact_kernel(
     st.thr = kEmptyKey;
   }
   __syncthreads();
+  const bool pairs = sc.half_warp();
+  const int half = lane >> 4;
   for (int64_t round = row_begin; round < row_end; round += kRowsPerRound) {
-    for (int j = 0; j < 16; ++j) {
-      const int64_t row = round + j * 8 + warp;
-      if (row >= row_end || !bitmap_pass(bitmap, row)) continue;
+    for (int j = 0; j < (pairs ? 8 : 16); ++j) {
+      int64_t row;
+      bool ok;
+      if (pairs) {
+        // Rows row0 and row0 + 1, one per half-warp; a half whose row is
+        // out of range or filtered out scores its partner's and drops it.
+        const int64_t row0 = round + (int64_t)(j * 8 + warp) * 2;
+        row = row0 + half;
+        ok = row < row_end && bitmap_pass(bitmap, row);
+        if (__ballot_sync(kFullMask, ok) == 0) continue;
+        if (!ok) row = half ? row0 : row0 + 1;
+      } else {
+        row = round + j * 8 + warp;
+        ok = row < row_end && bitmap_pass(bitmap, row);
+        if (!ok) continue;
+      }
       const float s = sc.score(qi, row);
-      if (lane == 0) {
+      if ((lane & (pairs ? 15 : 31)) == 0 && ok) {
         if (!finite_f(s)) {
           atomicOr(&q_flags[qi], sc.error_flag(s));
         } else {
@@ -339,15 +357,33 @@ __global__ void __launch_bounds__(256) merge_rescore_kernel(
     return;
   }
   const int ncand = s_ncand;
-  // Reference rescoring: one warp per candidate.
+  // Reference rescoring: one warp per candidate, or one half-warp per
+  // candidate when the scorer evaluates a row per half-warp.
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int c = warp; c < ncand; c += blockDim.x >> 5) {
-    const uint32_t kr = pos_of(cand[c]);
-    const uint32_t pos = pos_of_keyrank[kr];
-    const float s = sc.score(qi, pos);
-    if (lane == 0) {
-      if (!finite_f(s)) atomicOr(&q_flags[qi], sc.error_flag(s));
-      cand[c] = pack_rank(rank_from_score(metric, s), kr);
+  const int nwarps = blockDim.x >> 5;
+  if (sc.half_warp()) {
+    const int half = lane >> 4;
+    for (int c0 = warp * 2; c0 < ncand; c0 += nwarps * 2) {
+      // An odd last candidate is scored by both halves; one writes it.
+      const int c = min(c0 + half, ncand - 1);
+      const uint32_t kr = pos_of(cand[c]);
+      const uint32_t pos = pos_of_keyrank[kr];
+      const float s = sc.score(qi, pos);
+      __syncwarp();
+      if ((lane & 15) == 0 && c0 + half < ncand) {
+        if (!finite_f(s)) atomicOr(&q_flags[qi], sc.error_flag(s));
+        cand[c] = pack_rank(rank_from_score(metric, s), kr);
+      }
+    }
+  } else {
+    for (int c = warp; c < ncand; c += nwarps) {
+      const uint32_t kr = pos_of(cand[c]);
+      const uint32_t pos = pos_of_keyrank[kr];
+      const float s = sc.score(qi, pos);
+      if (lane == 0) {
+        if (!finite_f(s)) atomicOr(&q_flags[qi], sc.error_flag(s));
+        cand[c] = pack_rank(rank_from_score(metric, s), kr);
+      }
     }
   }
   __syncthreads();

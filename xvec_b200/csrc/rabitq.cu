@@ -686,6 +686,7 @@ struct RaBitQScorer {
   }
   __device__ float eps(int qi) const { return q_eps[qi]; }
   __device__ int error_flag(float s) const { return isnan(s) ? kRaBitQInvalid : kRaBitQOverflow; }
+  __device__ bool half_warp() const { return false; }
   // Without refinement the reported score is the public one
   // (publicRaBitQScore, hnsw_rabitq.go:746-751) and the radius applies to it
   // (acceptRaBitQNode, hnsw_rabitq.go:753-757).

@@ -45,10 +45,15 @@ __global__ void __launch_bounds__(256) refine_kernel(
   const int n = min(c, N);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float* q = queries + (int64_t)qi * d;
-  for (int i = warp; i < n; i += blockDim.x >> 5) {
+  // d >= 16: each half-warp scores its own candidate (an odd last one is
+  // scored by both halves and written by one).
+  const bool pairs = d >= 16;
+  const int step = pairs ? 2 : 1;
+  for (int i0 = warp * step; i0 < n; i0 += (blockDim.x >> 5) * step) {
+    const int i = pairs ? min(i0 + (lane >> 4), n - 1) : i0;
     const uint32_t pos = stage_pos[(int64_t)qi * stage_k + i];
     const float s = warp_reference_score(metric, rows + (int64_t)pos * d, q, d);
-    if (lane == 0) {
+    if ((lane & (pairs ? 15 : 31)) == 0 && (!pairs || i0 + (lane >> 4) < n)) {
       if (!finite_f(s)) atomicOr(&q_flags[qi], 4);
       cand[i] = pack_rank(rank_from_score(metric, s), keyrank[pos]);
     }
