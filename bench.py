@@ -428,7 +428,7 @@ def run_ivfpq(args):
     scanned = int(h_sizes[pr.keys.astype(np.int64)].sum())
     probe.close()
     opts = xb.SearchOptions(top_k=PQ_K, nprobe=PQ_NPROBE)
-    ms, scan_ms, e2e_ms, st, clocks = time_search(ShardedSearch(index), queries, opts, args, dev,
+    ms, scan_ms, e2e_ms, st, clocks = time_search(sharded(index, world, local), queries, opts, args, dev,
                                                   world, local)
 
     cpu = None
@@ -467,9 +467,28 @@ def run_ivfpq(args):
             "gpu_launches": int(st["kernel_launches"]),
         }
         print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    finish_ranks(world)
+
+
+_COMMS = []
+
+
+def sharded(index, world, local):
+    """The search every rank runs: the plain search at N = 1; above, the
+    library's sharded search over its own NCCL communicator (the id made by
+    rank 0 and sent over torch.distributed), one C-ABI call per step."""
+    from xvec_b200.sharded import ShardedSearch, library_comm
+    comm = library_comm(local) if world > 1 else None
+    if comm is not None:
+        _COMMS.append(comm)
+    return ShardedSearch(index, comm=comm)
+
+
+def close_comms():
+    """Frees the library's communicators (every rank, same order) before the
+    process group goes."""
+    while _COMMS:
+        _COMMS.pop().close()
 
 
 def time_search(search, queries, opts, args, dev, world, local):
@@ -583,6 +602,7 @@ def finish_ranks(world):
     import torch.distributed as dist
     if world > 1:
         dist.barrier()
+        close_comms()
         dist.destroy_process_group()
 
 
@@ -671,7 +691,7 @@ def run_ivf_flat(args, sq8=False):
     probe.close()
     opts = xb.SearchOptions(top_k=IVF_K, nprobe=IVF_NPROBE,
                             refine_scale=IVF_SQ_SCALE if sq8 else 0.0)
-    ms, scan_ms, e2e_ms, st, clocks = time_search(ShardedSearch(index), queries, opts, args, dev,
+    ms, scan_ms, e2e_ms, st, clocks = time_search(sharded(index, world, local), queries, opts, args, dev,
                                                   world, local)
     cpu = None
     if host_rows is not None:
@@ -761,7 +781,7 @@ def run_flat_fp32(args):
                           device=dev)
     torch.cuda.synchronize()
     opts = xb.SearchOptions(top_k=F32_K)
-    ms, scan_ms, e2e_ms, st, clocks = time_search(ShardedSearch(index), queries, opts, args, dev,
+    ms, scan_ms, e2e_ms, st, clocks = time_search(sharded(index, world, local), queries, opts, args, dev,
                                                   world, local)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -848,7 +868,7 @@ def run_sq8(args):
     queries = sq_rows(torch, scale, 10**6, nq, dev).contiguous()
     torch.cuda.synchronize()
     opts = xb.SearchOptions(top_k=SQ_K, refine_scale=SQ_SCALE)
-    ms, scan_ms, e2e_ms, st, clocks = time_search(ShardedSearch(index), queries, opts, args, dev,
+    ms, scan_ms, e2e_ms, st, clocks = time_search(sharded(index, world, local), queries, opts, args, dev,
                                                   world, local)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -909,7 +929,7 @@ def run_sq4(args):
     queries = sq_rows(torch, scale, 10**6, nq, dev).contiguous()
     torch.cuda.synchronize()
     opts = xb.SearchOptions(top_k=SQ4_K, refine_scale=SQ4_SCALE)
-    ms, scan_ms, e2e_ms, st, clocks = time_search(ShardedSearch(index), queries, opts, args, dev,
+    ms, scan_ms, e2e_ms, st, clocks = time_search(sharded(index, world, local), queries, opts, args, dev,
                                                   world, local)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -1095,11 +1115,11 @@ def run_rabitq(args, total_bits=1):
     queries = pq_mixture(torch, centers, 3 * 10**6, nq, dev).contiguous()
     torch.cuda.synchronize()
     opts = xb.SearchOptions(top_k=RQ_K, ef=RQ_EF, refine=True)
-    ms, scan_ms, e2e_ms, st, clocks = time_search(ShardedSearch(index), queries, opts, args, dev,
+    ms, scan_ms, e2e_ms, st, clocks = time_search(sharded(index, world, local), queries, opts, args, dev,
                                                   world, local)
     sweep = None
     if args.batch_sweep and world == 1:
-        sweep = batch_sweep(ShardedSearch(index), queries, opts,
+        sweep = batch_sweep(sharded(index, world, local), queries, opts,
                             [int(x) for x in args.batch_sweep.split(",")])
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -1255,7 +1275,7 @@ def main():
         del rows, keys
     queries = make_queries(torch, centers, nq, dev)
     torch.cuda.synchronize()
-    search = ShardedSearch(index)
+    search = sharded(index, world, local)
     opts = xb.SearchOptions(top_k=k)
 
     def barrier():
@@ -1382,9 +1402,7 @@ def main():
             "exact_queries": int(st["exact_queries"]),
         }
         print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    finish_ranks(world)
 
 
 if __name__ == "__main__":

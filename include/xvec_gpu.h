@@ -1,7 +1,7 @@
 /*
  * xvec_gpu.h — C ABI of the B200 (sm_100a) search library for xvec.
  *
- * This is the boundary a cgo shim binds (see INTEGRATION.md).  It takes plain
+ * This is the boundary a cgo shim binds.  It takes plain
  * pointers and sizes only.  Each entry point names the reference interface it
  * replaces, by file:line in the gorse-io/xvec module.
  *
@@ -337,6 +337,69 @@ xvec_gpu_status xvec_gpu_merge_results_device(int32_t device, int32_t metric, in
                                               uint64_t* d_out_keys, float* d_out_scores,
                                               int32_t* d_out_counts, void* stream);
 
+/* Multi-GPU search ------------------------------------------------------------
+ * The reference fans a query out over the segments of a collection and
+ * merges the per-segment top-k with MergeSearchResults (collection.go:
+ * 4040-4066, internal/core/query.go:154-191).  Here each GPU holds one shard
+ * of the rows in its own index (keys unique across shards) and the library
+ * exchanges the shards' lists with its own NCCL communicator: one all-gather
+ * of a packed buffer (keys, scores and counts of every query), then the
+ * MergeSearchResults order on every rank.  Refined searches (SQ8_FLAT,
+ * SQ4_FLAT, IVF_SQ8 and IVF_SQ4 with a refine scale, RABITQ with refine)
+ * exchange twice, so that the refined candidates are the whole index's
+ * (RefinedSearch, refiner.go:133-166).  NCCL is loaded at run time (the copy
+ * the process holds, else XVEC_GPU_NCCL_LIBRARY, else libnccl.so.2;
+ * XVEC_GPU_UNSUPPORTED without one).  Every wait on a communicator is bounded
+ * by its timeout: when it passes the communicator is aborted and the call
+ * returns XVEC_GPU_TIMEOUT (XVEC_GPU_NCCL_ERROR for an error NCCL reports);
+ * an aborted communicator fails every later call, so destroy it and make a
+ * new one.  A rank whose own search fails as a whole still takes part in the
+ * exchange, with every query failed by that status, so every rank reports it.
+ * The library's counterpart of the reference's in-process segment fan-out;
+ * no single reference call corresponds. */
+#define XVEC_GPU_COMM_ID_BYTES 128
+typedef struct xvec_gpu_comm xvec_gpu_comm;
+
+/* A new communicator id (ncclGetUniqueId): made by one rank, sent to the
+ * others by the caller (id_out: XVEC_GPU_COMM_ID_BYTES bytes). */
+xvec_gpu_status xvec_gpu_comm_unique_id(uint8_t* id_out);
+/* One process per GPU: this process's rank of nranks on `device`, joining
+ * the communicator `id`.  timeout_ms (<= 0: 60 s) bounds this call and every
+ * later wait on the communicator. */
+xvec_gpu_status xvec_gpu_comm_init_rank(int32_t device, const uint8_t* id, int32_t nranks,
+                                        int32_t rank, int32_t timeout_ms, xvec_gpu_comm** out);
+/* One process over several GPUs: ranks 0..ndev-1 on devices[0..ndev-1],
+ * written to out[0..ndev-1]. */
+xvec_gpu_status xvec_gpu_comm_init_all(const int32_t* devices, int32_t ndev, int32_t timeout_ms,
+                                       xvec_gpu_comm** out);
+/* Frees a communicator (a healthy one is flushed first, within its timeout). */
+xvec_gpu_status xvec_gpu_comm_destroy(xvec_gpu_comm* comm);
+/* Aborts a communicator's pending and future work (ncclCommAbort). */
+xvec_gpu_status xvec_gpu_comm_abort(xvec_gpu_comm* comm);
+int32_t xvec_gpu_comm_size(const xvec_gpu_comm* comm);
+int32_t xvec_gpu_comm_rank(const xvec_gpu_comm* comm);
+
+/* One rank's call of a sharded search (one process per GPU): every rank
+ * calls it with the same queries and options on its own shard's index (on
+ * the communicator's device) and receives the merged results of all shards
+ * in its device outputs (nq*top_k keys / scores, nq counts), enqueued on
+ * opts->stream.  filter_bitmap, if given, is this shard's (device memory).
+ * Returns like xvec_gpu_index_search_device. */
+xvec_gpu_status xvec_gpu_sharded_search_device(xvec_gpu_comm* comm, xvec_gpu_index* index,
+                                               const void* d_queries, int32_t nq,
+                                               const xvec_gpu_search_opts* opts,
+                                               uint64_t* d_out_keys, float* d_out_scores,
+                                               int32_t* d_out_counts);
+/* The same over ndev GPUs of one process (comms from xvec_gpu_comm_init_all,
+ * indexes[i] on comms[i]'s device): host queries in, the merged results in
+ * host outputs.  No filter bitmap (each shard has its own positions: filter
+ * through xvec_gpu_sharded_search_device). */
+xvec_gpu_status xvec_gpu_sharded_search(xvec_gpu_comm* const* comms,
+                                        xvec_gpu_index* const* indexes, int32_t ndev,
+                                        const void* queries, int32_t nq,
+                                        const xvec_gpu_search_opts* opts, uint64_t* out_keys,
+                                        float* out_scores, int32_t* out_counts);
+
 /* The two halves of a refined search, for a search whose rows are split
  * over several indexes (shards).  RefinedSearch (refiner.go:133-166) refines
  * the RefinementCandidateCount best approximate results of the whole index,
@@ -347,9 +410,9 @@ xvec_gpu_status xvec_gpu_merge_results_device(int32_t device, int32_t metric, in
  * better, ties by key); refine the merged list on every shard; merge those
  * results under the index metric.
  *
- * candidate_count: candidates per query for these options (SQ8_FLAT:
- * max(1, floor(top_k * refine_scale)); RABITQ with refine: max(top_k, ef));
- * 0 when the options ask for no refinement.
+ * candidate_count: candidates per query for these options (SQ8_FLAT,
+ * SQ4_FLAT, IVF_SQ8, IVF_SQ4: max(1, floor(top_k * refine_scale)); RABITQ
+ * with refine: max(top_k, ef)); 0 when the options ask for no refinement.
  * candidates_device: the approximate stage alone (no radius): per query up
  * to candidate_count keys with their ranks (the approximate distance, or the
  * negated inner product; for RaBitQ the estimate), best first, at stride
@@ -384,7 +447,9 @@ xvec_gpu_status xvec_gpu_index_refine_device(xvec_gpu_index* index, const float*
  * the scratch the batch needs must fit in 32 MiB (otherwise
  * XVEC_GPU_INVALID_ARGUMENT).  All calls share the array: calls whose GPU
  * work overlaps race (the library serialises calls from one process and each
- * call waits for its GPU work).  The first call on a device looks up the
+ * call waits for its GPU work, on its error paths too).  The cancel flag and
+ * the library's counters work as for the regular search.  The first call on a
+ * device looks up the
  * array's device address (which also makes the CUDA runtime load the
  * library's device code there, reserving the array); make that first call
  * before any stream capture. */
@@ -406,6 +471,15 @@ typedef struct {
   int64_t tensor_scans;    /* scans that ran on the tensor cores (tcgen05) */
 } xvec_gpu_stats;
 void xvec_gpu_stats_enable_timing(int32_t enabled);
+
+/* Bound of the device-side waits inside the tensor-core scans: 2 s by
+ * default, ns <= 0 restores it; returns the previous bound.  Applies to scans
+ * launched after the call, on every device.  A wait that runs out stops the
+ * scan (the kernel drains the copies it issued and frees its tensor memory)
+ * and the search returns XVEC_GPU_TIMEOUT; the device stays usable.  The
+ * reference's counterpart is the context check between candidates
+ * (ctx.Err(), internal/core/topk.go:130), which ends a search early. */
+int64_t xvec_gpu_set_wait_limit_ns(int64_t ns);
 void xvec_gpu_get_stats(xvec_gpu_stats* out);
 void xvec_gpu_reset_stats(void);
 

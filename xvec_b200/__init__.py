@@ -15,6 +15,7 @@ the search path so that tests read like the reference's own:
   core.Result {Key, Score}                       Result / ndarray pairs (topk.go:47-50)
   assignKMeans                                   kmeans_assign (kmeans.go:382-479)
   core.MergeSearchResults                        merge_results_device (query.go:154-191)
+  segment fan-out + merge (collection.go:4040-4066)  Comm, sharded_search(_device)
 
 There is no CPU fallback: importing this module fails if the shared library is
 missing, and every search runs on a CUDA device.
@@ -59,6 +60,10 @@ EXPORTED_SYMBOLS = (
     "xvec_gpu_ivf_set_model", "xvec_gpu_rabitq_set_model_bits", "xvec_gpu_ivf_add_with_lists",
     "xvec_gpu_ivf_file_info", "xvec_gpu_ivf_open", "xvec_gpu_kmeans_train_init_device",
     "xvec_gpu_pq_train", "xvec_gpu_pq_train_device",
+    "xvec_gpu_comm_unique_id", "xvec_gpu_comm_init_rank", "xvec_gpu_comm_init_all",
+    "xvec_gpu_comm_destroy", "xvec_gpu_comm_abort", "xvec_gpu_comm_size", "xvec_gpu_comm_rank",
+    "xvec_gpu_sharded_search_device", "xvec_gpu_sharded_search",
+    "xvec_gpu_set_wait_limit_ns",
 )
 
 
@@ -139,6 +144,21 @@ def _load() -> ctypes.CDLL:
                                                      vp, vp]
     lib.xvec_gpu_index_refine_device.argtypes = [vp, vp, i32, vp, i32, vp, i32, ctypes.c_float,
                                                  vp, vp, vp, vp]
+    lib.xvec_gpu_comm_unique_id.argtypes = [vp]
+    lib.xvec_gpu_comm_init_rank.argtypes = [i32, vp, i32, i32, i32, ctypes.POINTER(vp)]
+    lib.xvec_gpu_comm_init_all.argtypes = [vp, i32, i32, vp]
+    lib.xvec_gpu_comm_destroy.argtypes = [vp]
+    lib.xvec_gpu_comm_abort.argtypes = [vp]
+    lib.xvec_gpu_comm_size.restype = i32
+    lib.xvec_gpu_comm_size.argtypes = [vp]
+    lib.xvec_gpu_comm_rank.restype = i32
+    lib.xvec_gpu_comm_rank.argtypes = [vp]
+    lib.xvec_gpu_sharded_search_device.argtypes = [vp, vp, vp, i32, ctypes.POINTER(SearchOpts),
+                                                   vp, vp, vp]
+    lib.xvec_gpu_sharded_search.argtypes = [vp, vp, i32, vp, i32, ctypes.POINTER(SearchOpts), vp,
+                                            vp, vp]
+    lib.xvec_gpu_set_wait_limit_ns.restype = i64
+    lib.xvec_gpu_set_wait_limit_ns.argtypes = [i64]
     lib.xvec_gpu_stats_enable_timing.argtypes = [i32]
     lib.xvec_gpu_get_stats.argtypes = [ctypes.POINTER(Stats)]
     for name in EXPORTED_SYMBOLS:
@@ -178,6 +198,12 @@ def reset_stats() -> None:
 
 def enable_timing(on: bool = True) -> None:
     _lib.xvec_gpu_stats_enable_timing(1 if on else 0)
+
+
+def set_wait_limit_ns(ns: int) -> int:
+    """Bound of the tensor-core scans' device-side waits (xvec_gpu_set_wait_limit_ns):
+    2 s by default, ns <= 0 restores it; returns the previous bound."""
+    return int(_lib.xvec_gpu_set_wait_limit_ns(ns))
 
 
 def device_count() -> int:
@@ -651,3 +677,127 @@ def merge_results_device(device: int, metric: int, top_k: int, nq: int, parts: i
     _check(_lib.xvec_gpu_merge_results_device(device, metric, top_k, nq, parts, keys_ptr,
                                               scores_ptr, counts_ptr, out_keys_ptr,
                                               out_scores_ptr, out_counts_ptr, stream or None))
+
+
+# ---------------------------------------------------------------------------
+# Multi-GPU: the library's NCCL communicator and the sharded search.
+# ---------------------------------------------------------------------------
+COMM_ID_BYTES = 128
+
+
+def _use_pytorch_nccl() -> None:
+    """Points the library at the NCCL that PyTorch links (the nvidia.nccl
+    package), unless XVEC_GPU_NCCL_LIBRARY names one: a process holds one
+    library of that name, and the first to load decides which, so the two must
+    agree whichever loads first."""
+    if os.environ.get("XVEC_GPU_NCCL_LIBRARY"):
+        return
+    try:
+        import importlib.util
+        spec = importlib.util.find_spec("nvidia.nccl")
+    except (ImportError, ValueError):
+        return
+    for base in (spec.submodule_search_locations or []) if spec else []:
+        path = os.path.join(base, "lib", "libnccl.so.2")
+        if os.path.exists(path):
+            os.environ["XVEC_GPU_NCCL_LIBRARY"] = path
+            return
+
+
+class Comm:
+    """A communicator of the library (xvec_gpu_comm_*): one rank per GPU."""
+
+    def __init__(self, handle: ctypes.c_void_p, device: int):
+        self._h = handle
+        self.device = device
+
+    @staticmethod
+    def unique_id() -> bytes:
+        """A new communicator id (one rank makes it and sends it to the others)."""
+        _use_pytorch_nccl()
+        buf = (ctypes.c_uint8 * COMM_ID_BYTES)()
+        _check(_lib.xvec_gpu_comm_unique_id(buf))
+        return bytes(buf)
+
+    @classmethod
+    def init_rank(cls, device: int, comm_id: bytes, nranks: int, rank: int,
+                  timeout_ms: int = 60000) -> "Comm":
+        """This process's rank on `device` (one process per GPU)."""
+        if len(comm_id) != COMM_ID_BYTES:
+            raise XvecGPUError(INVALID_ARGUMENT, "communicator id must be 128 bytes")
+        _use_pytorch_nccl()
+        buf = (ctypes.c_uint8 * COMM_ID_BYTES).from_buffer_copy(comm_id)
+        h = ctypes.c_void_p()
+        _check(_lib.xvec_gpu_comm_init_rank(device, buf, nranks, rank, timeout_ms,
+                                            ctypes.byref(h)))
+        return cls(h, device)
+
+    @classmethod
+    def init_all(cls, devices: Sequence[int], timeout_ms: int = 60000) -> list:
+        """Ranks 0..len(devices)-1 of one process, one per device."""
+        _use_pytorch_nccl()
+        n = len(devices)
+        devs = (ctypes.c_int32 * n)(*devices)
+        hs = (ctypes.c_void_p * n)()
+        _check(_lib.xvec_gpu_comm_init_all(devs, n, timeout_ms, hs))
+        return [cls(ctypes.c_void_p(hs[i]), devices[i]) for i in range(n)]
+
+    @property
+    def size(self) -> int:
+        return int(_lib.xvec_gpu_comm_size(self._h))
+
+    @property
+    def rank(self) -> int:
+        return int(_lib.xvec_gpu_comm_rank(self._h))
+
+    def abort(self) -> None:
+        _check(_lib.xvec_gpu_comm_abort(self._h))
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            _lib.xvec_gpu_comm_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def sharded_search_device(comm: Comm, index: _Index, queries_ptr: int, nq: int,
+                          options: SearchOptions, out_keys_ptr: int, out_scores_ptr: int,
+                          out_counts_ptr: int, stream: int = 0,
+                          filter_ptr: Optional[int] = None) -> None:
+    """One rank's call of a sharded search (xvec_gpu_sharded_search_device):
+    the merged results of every rank's shard in this rank's device outputs."""
+    o = index._opts(options, stream=stream or None, device_filter_ptr=filter_ptr)
+    _check(_lib.xvec_gpu_sharded_search_device(comm._h, index._h, queries_ptr, nq,
+                                               ctypes.byref(o), out_keys_ptr, out_scores_ptr,
+                                               out_counts_ptr))
+
+
+def sharded_search(comms: Sequence[Comm], indexes: Sequence[_Index], queries,
+                   options: SearchOptions, raise_on_error: bool = True) -> SearchResults:
+    """A sharded search of one process over several GPUs
+    (xvec_gpu_sharded_search): host queries in, merged host results out."""
+    if options.filter is not None:
+        raise XvecGPUError(INVALID_ARGUMENT, "filter a sharded search per rank "
+                                             "(sharded_search_device)")
+    idx0 = indexes[0]
+    queries = np.ascontiguousarray(queries, idx0._row_dtype())
+    if queries.ndim == 1:
+        queries = queries[None, :]
+    nq, k = queries.shape[0], options.top_k
+    keys = np.zeros((nq, max(k, 1)), np.uint64)
+    scores = np.zeros((nq, max(k, 1)), np.float32)
+    counts = np.zeros(nq, np.int32)
+    n = len(comms)
+    ch = (ctypes.c_void_p * n)(*[c._h.value for c in comms])
+    ih = (ctypes.c_void_p * n)(*[i._h.value for i in indexes])
+    o = idx0._opts(options)
+    st = _lib.xvec_gpu_sharded_search(ch, ih, n, _ptr(queries), nq, ctypes.byref(o), _ptr(keys),
+                                      _ptr(scores), _ptr(counts))
+    if st != OK and (raise_on_error or not (counts < 0).any()):
+        raise XvecGPUError(st, last_error())
+    return SearchResults(keys[:, :k], scores[:, :k], counts)

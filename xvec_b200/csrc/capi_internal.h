@@ -124,6 +124,26 @@ xvec_gpu_status tc_seeded_scan(int device, int nq, int64_t n, int kp, cudaStream
                                const TcScanLaunch& scan, Scratch& pkeys, Scratch& pcounts,
                                Scratch& psat, int* lists_out);
 
+// MergeSearchResults of `parts` lists per query (merge.cu): part p's keys,
+// scores and counts start p * key_stride, p * score_stride and p *
+// count_stride elements in (query q's list at q * top_k inside a part).
+xvec_gpu_status launch_merge_results(int metric, int top_k, int nq, int parts,
+                                     const uint64_t* keys, int64_t key_stride,
+                                     const float* scores, int64_t score_stride,
+                                     const int* counts, int64_t count_stride,
+                                     uint64_t* out_keys, float* out_scores, int* out_counts,
+                                     cudaStream_t stream);
+
+// The search entry points' shared steps (capi.cu).
+xvec_gpu_status validate_search(xvec_gpu_index* idx, int nq, const xvec_gpu_search_opts* o);
+xvec_gpu_status search_device_locked(xvec_gpu_index* idx, const void* d_q, int nq,
+                                     const xvec_gpu_search_opts& o, const uint32_t* d_bitmap,
+                                     uint64_t* d_keys, float* d_scores, int* d_counts,
+                                     cudaStream_t s, std::vector<int>* statuses);
+size_t query_elem_bytes(const xvec_gpu_index* idx);
+// The caller's cancel flag (opts.cancel_flag) is set.
+bool is_cancelled(const xvec_gpu_search_opts& o);
+
 }  // namespace xvec
 
 struct xvec_gpu_index {

@@ -36,6 +36,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
+
 #include "capi_internal.h"
 #include "common.cuh"
 #include "flat_tc.cuh"
@@ -91,7 +93,7 @@ struct Shape {
   static constexpr uint32_t kSmemBytes = kStages * kStageBytes + kEpiBytes + 1024 + 512;
   static_assert(kStages >= 2, "shared memory too small for the stage ring");
 };
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // a wait gives up after 2 s
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // a wait gives up after 2 s (default)
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return (uint32_t)__cvta_generic_to_shared(p);
@@ -140,10 +142,11 @@ __device__ __forceinline__ uint64_t global_ns() {
   return t;
 }
 
-// Bounded parity wait: false once kWaitLimitNs passed or another role of
-// the CTA raised *abort.
+// Bounded parity wait: false once limit_ns passed or another role of the
+// CTA raised *abort.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
-                                          const volatile int* abort) {
+                                          const volatile int* abort,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   const uint32_t addr = smem_u32(bar);
   uint64_t start = 0;
   for (uint32_t i = 0;; ++i) {
@@ -160,7 +163,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
       if (abort && *abort) return false;
       const uint64_t now = global_ns();
       if (start == 0) start = now;
-      else if (now - start > kWaitLimitNs) return false;
+      else if (now - start > limit_ns) return false;
     }
   }
 }
@@ -418,7 +421,7 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
     unsigned long long* __restrict__ gthr, const uint32_t* __restrict__ bitmap,
     int64_t rows_per_part, int kp, int list_base, int num_lists, uint64_t* __restrict__ cand,
     int* __restrict__ part_counts, uint64_t* __restrict__ part_sat, int* __restrict__ q_flags,
-    int* __restrict__ status) {
+    int* __restrict__ status, uint64_t wait_ns) {
   constexpr bool RQ1 = MODE == kModeRaBitQ;   // RaBitQ code planes, integer queries
   constexpr bool RQF = MODE == kModeRaBitQFull;  // multi-bit values, bfloat16 query parts
   constexpr bool RQ = RQ1 || RQF;                // the RaBitQ epilogue
@@ -507,7 +510,7 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
       for (int t = 0; t < num_tiles && !*s_abort; ++t) {
         const int row0 = (int)(row_begin + (int64_t)t * kBN) + (int)rank * S::kRowsPerCta;
         for (int ks = 0; ks < ksteps; ++ks) {
-          if (!mbar_wait(&empty[stage], phase ^ 1, s_abort)) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, s_abort, wait_ns)) {
             atomicExch(status, 1);
             *s_abort = 1;
             break;
@@ -560,7 +563,7 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
       for (int t = 0; t < num_tiles && !*s_abort; ++t) {
         const int acc = t & 1;
         const uint32_t acc_phase = (t >> 1) & 1;
-        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, s_abort)) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, s_abort, wait_ns)) {
           atomicExch(status, 2);
           *s_abort = 1;
           break;
@@ -568,7 +571,7 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
         tmem_fence_after();
         const uint32_t d_tmem = tmem_base + acc * kBN;
         for (int ks = 0; ks < ksteps; ++ks) {
-          if (!mbar_wait(&full[stage], phase, s_abort)) {
+          if (!mbar_wait(&full[stage], phase, s_abort, wait_ns)) {
             atomicExch(status, 3);
             *s_abort = 1;
             break;
@@ -712,7 +715,7 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
       }
       if (qvalid) g_next = (uint64_t)*(volatile unsigned long long*)&gthr[qi];
       // Warp-uniform outcome: the tcgen05.ld below needs every lane.
-      if (!__all_sync(kFullMask, mbar_wait(&tfull[acc], acc_phase, s_abort))) {
+      if (!__all_sync(kFullMask, mbar_wait(&tfull[acc], acc_phase, s_abort, wait_ns))) {
         atomicExch(status, 4);
         *s_abort = 1;
         break;
@@ -940,6 +943,11 @@ int flat_tc_lists_per_part() { return 2; }
 bool flat_tc_pairs(int nq) { return nq > tc::kBM; }
 
 namespace {
+// Limit of the scan's main-loop waits (xvec_gpu_set_wait_limit_ns); the
+// teardown's waits for copies already issued keep the default.
+std::atomic<int64_t> g_tc_wait_ns{(int64_t)tc::kWaitLimitNs};
+uint64_t tc_wait_ns() { return (uint64_t)g_tc_wait_ns.load(std::memory_order_relaxed); }
+
 // Launches mode MODE (a Flat metric, or kModeSq8 + metric) on CTA pairs when
 // there are two query blocks, else on single CTAs.
 template <int MODE>
@@ -984,7 +992,7 @@ cudaError_t launch_tc(int nq, const void* queries, const void* queries2, int nc,
                          (int)tc::Shape<true, RQ, SPLIT, RQF>::kSmemBytes);
     err = cudaLaunchKernelEx(&cfg, kern, qmap, rmap, qmap2, rmap2, nc, nq, n, d, row_aux, keyrank, q_aux,
                              q_n2, gthr, bitmap, rows_per_part, kp, list_base, num_lists, cand,
-                             part_counts, part_sat, q_flags, status);
+                             part_counts, part_sat, q_flags, status, tc_wait_ns());
   } else {
     auto kern = tc::flat_scan_tc_kernel<MODE, false>;
     cfg.dynamicSmemBytes = tc::Shape<false, RQ, SPLIT, RQF>::kSmemBytes;
@@ -992,7 +1000,7 @@ cudaError_t launch_tc(int nq, const void* queries, const void* queries2, int nc,
                          (int)tc::Shape<false, RQ, SPLIT, RQF>::kSmemBytes);
     err = cudaLaunchKernelEx(&cfg, kern, qmap, rmap, qmap2, rmap2, nc, nq, n, d, row_aux, keyrank, q_aux,
                              q_n2, gthr, bitmap, rows_per_part, kp, list_base, num_lists, cand,
-                             part_counts, part_sat, q_flags, status);
+                             part_counts, part_sat, q_flags, status, tc_wait_ns());
   }
   if (err != cudaSuccess) return err;
   return cudaGetLastError();
@@ -1135,3 +1143,7 @@ bool sq8_tc_supported(int d, const void* codes, const void* qcodes) {
 }
 
 }  // namespace xvec
+
+extern "C" int64_t xvec_gpu_set_wait_limit_ns(int64_t ns) {
+  return xvec::g_tc_wait_ns.exchange(ns > 0 ? ns : (int64_t)xvec::tc::kWaitLimitNs);
+}

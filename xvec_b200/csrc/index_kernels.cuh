@@ -43,7 +43,8 @@ xvec_gpu_status ivf_flat_search_impl(xvec_gpu_index* idx, const float* d_q, int 
 xvec_gpu_status ivf_sq8_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
                                     const xvec_gpu_search_opts& o, const uint32_t* d_bitmap,
                                     uint64_t* d_keys, float* d_scores, int* d_counts,
-                                    cudaStream_t s, std::vector<int>* statuses);
+                                    cudaStream_t s, std::vector<int>* statuses,
+                                    bool candidates_only = false);
 
 xvec_gpu_status rabitq_reserve(xvec_gpu_index* idx, int64_t capacity, cudaStream_t s);
 xvec_gpu_status rabitq_commit(xvec_gpu_index* idx, int64_t old_n, int64_t m, cudaStream_t s);

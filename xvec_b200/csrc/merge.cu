@@ -38,11 +38,14 @@ void count_search(int64_t queries, int64_t exact_queries, double scan_ms, double
 bool timing_enabled() { return g_timing.load() != 0; }
 
 // One block per query: gather the valid entries of every part, bitonic-sort
-// them by (ordered rank, key) and keep the first top_k.
+// them by (ordered rank, key) and keep the first top_k.  Part p's lists start
+// p * key_stride / score_stride / count_stride elements into keys / scores /
+// counts (query q's list at q * k inside its part).
 __global__ void merge_results_kernel(int metric, int k, int nq, int parts, int n_pow2,
-                                     const uint64_t* __restrict__ keys,
-                                     const float* __restrict__ scores,
-                                     const int* __restrict__ counts, uint64_t* __restrict__ out_keys,
+                                     const uint64_t* __restrict__ keys, int64_t key_stride,
+                                     const float* __restrict__ scores, int64_t score_stride,
+                                     const int* __restrict__ counts, int64_t count_stride,
+                                     uint64_t* __restrict__ out_keys,
                                      float* __restrict__ out_scores, int* __restrict__ out_counts) {
   extern __shared__ __align__(16) unsigned char smem[];
   uint64_t* skey = reinterpret_cast<uint64_t*>(smem);
@@ -56,7 +59,7 @@ __global__ void merge_results_kernel(int metric, int k, int nq, int parts, int n
     // shards validate a query the same way, so the first one's status stands.
     s_err = 0;
     for (int p = 0; p < parts && s_err == 0; ++p) {
-      const int c = counts[(int64_t)p * nq + q];
+      const int c = counts[(int64_t)p * count_stride + q];
       if (c < 0) s_err = c;
     }
     if (s_err) out_counts[q] = s_err;
@@ -65,14 +68,15 @@ __global__ void merge_results_kernel(int metric, int k, int nq, int parts, int n
   if (s_err) return;
   for (int i = threadIdx.x; i < parts * k; i += blockDim.x) {
     const int p = i / k, j = i - p * k;
-    const int c = counts[(int64_t)p * nq + q];
+    const int c = counts[(int64_t)p * count_stride + q];
     if (j < c) {
-      const int64_t src = ((int64_t)p * nq + q) * k + j;
+      const int64_t src = (int64_t)q * k + j;
       const int slot = atomicAdd(&s_n, 1);
-      skey[slot] = keys[src];
-      sscore[slot] = scores[src];
+      const float sc = scores[(int64_t)p * score_stride + src];
+      skey[slot] = keys[(int64_t)p * key_stride + src];
+      sscore[slot] = sc;
       // + 0.f: -0 and +0 rank equal (the reference compares scores with ==).
-      srank[slot] = float_to_ordered(rank_from_score(metric, scores[src]) + 0.f);
+      srank[slot] = float_to_ordered(rank_from_score(metric, sc) + 0.f);
     }
   }
   __syncthreads();
@@ -106,6 +110,34 @@ __global__ void merge_results_kernel(int metric, int k, int nq, int parts, int n
     out_scores[(int64_t)q * k + i] = sscore[i];
   }
   if (threadIdx.x == 0) out_counts[q] = c;
+}
+
+xvec_gpu_status launch_merge_results(int metric, int top_k, int nq, int parts,
+                                     const uint64_t* keys, int64_t key_stride,
+                                     const float* scores, int64_t score_stride,
+                                     const int* counts, int64_t count_stride,
+                                     uint64_t* out_keys, float* out_scores, int* out_counts,
+                                     cudaStream_t stream) {
+  if (metric < XVEC_METRIC_L2 || metric > XVEC_METRIC_MIPSL2 || top_k <= 0 || nq < 0 ||
+      parts <= 0)
+    return set_error("invalid merge arguments"), XVEC_GPU_INVALID_ARGUMENT;
+  int64_t entries = (int64_t)parts * top_k;
+  int n_pow2 = 1;
+  while (n_pow2 < entries) n_pow2 <<= 1;
+  if (n_pow2 > 8192)
+    return set_error("merge of %lld entries per query exceeds 8192", (long long)entries),
+           XVEC_GPU_INVALID_ARGUMENT;
+  if (nq == 0) return XVEC_GPU_OK;
+  const size_t smem = (size_t)n_pow2 * 16;
+  cudaFuncSetAttribute(merge_results_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       (int)smem);
+  merge_results_kernel<<<nq, 256, smem, stream>>>(metric, top_k, nq, parts, n_pow2, keys,
+                                                  key_stride, scores, score_stride, counts,
+                                                  count_stride, out_keys, out_scores,
+                                                  out_counts);
+  XVEC_LAUNCHED();
+  XVEC_CUDA(cudaGetLastError());
+  return XVEC_GPU_OK;
 }
 
 }  // namespace xvec
@@ -144,24 +176,8 @@ extern "C" xvec_gpu_status xvec_gpu_merge_results_device(int32_t device, int32_t
                                                          const int32_t* d_counts,
                                                          uint64_t* d_out_keys, float* d_out_scores,
                                                          int32_t* d_out_counts, void* stream) {
-  if (metric < XVEC_METRIC_L2 || metric > XVEC_METRIC_MIPSL2 || top_k <= 0 || nq < 0 ||
-      parts <= 0)
-    return set_error("invalid merge arguments"), XVEC_GPU_INVALID_ARGUMENT;
-  int64_t entries = (int64_t)parts * top_k;
-  int n_pow2 = 1;
-  while (n_pow2 < entries) n_pow2 <<= 1;
-  if (n_pow2 > 8192)
-    return set_error("merge of %lld entries per query exceeds 8192", (long long)entries),
-           XVEC_GPU_INVALID_ARGUMENT;
-  if (nq == 0) return XVEC_GPU_OK;
-  cudaSetDevice(device);
-  const size_t smem = (size_t)n_pow2 * 16;
-  cudaFuncSetAttribute(merge_results_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       (int)smem);
-  merge_results_kernel<<<nq, 256, smem, static_cast<cudaStream_t>(stream)>>>(
-      metric, top_k, nq, parts, n_pow2, d_keys, d_scores, d_counts, d_out_keys, d_out_scores,
-      d_out_counts);
-  XVEC_LAUNCHED();
-  XVEC_CUDA(cudaGetLastError());
-  return XVEC_GPU_OK;
+  if (nq > 0 && parts > 0 && top_k > 0) cudaSetDevice(device);
+  return launch_merge_results(metric, top_k, nq, parts, d_keys, (int64_t)nq * top_k, d_scores,
+                              (int64_t)nq * top_k, d_counts, nq, d_out_keys, d_out_scores,
+                              d_out_counts, static_cast<cudaStream_t>(stream));
 }

@@ -17,7 +17,10 @@
 // parts that must start at zero are cleared on every call, and calls whose
 // GPU work overlaps (for example from two host threads on two streams of the
 // same device) race on it.  Calls are serialised on the host by a mutex, and
-// each call waits for its GPU work before returning.
+// each call waits for its GPU work before returning, on its error paths too,
+// so the array is idle whenever the mutex is released.  The caller's cancel
+// flag is polled between launches and the library's counters are updated,
+// as for the regular search.
 //
 // Set-up: the first call on a device looks up the device address of the
 // array with cudaGetSymbolAddress (with that device current) and keeps it;
@@ -139,16 +142,21 @@ xvec_gpu_status noalloc_search(xvec_gpu_index* idx, const void* d_q, int nq,
   XVEC_CUDA(cudaMemsetAsync(d_counts_out, 0, (size_t)nq * 4, s));
   launch_prep_queries<RowT>(static_cast<const RowT*>(d_q), nq, d, metric, qf, qn2, qaux, qstatus,
                             s);
+  XVEC_LAUNCHED();
   XVEC_CUDA(cudaGetLastError());
   if (n > 0) {
+    if (is_cancelled(o)) return set_error("cancelled"), XVEC_GPU_CANCELLED;
     XVEC_CUDA(launch_flat_scan_simt<RowT>(rows, n, d, idx->row_n2.as<float>(),
                                           idx->keyrank.as<uint32_t>(), qf, qn2, nq, nullptr,
                                           metric, parts, kp, pkeys, pcounts, psat, qflags, s));
+    XVEC_LAUNCHED();
+    if (is_cancelled(o)) return set_error("cancelled"), XVEC_GPU_CANCELLED;
     XVEC_CUDA(launch_flat_merge_rescore<RowT>(rows, d, idx->pos_of_kr.as<uint32_t>(),
                                               idx->keys.as<uint64_t>(), qf, qn2,
                                               idx->max_n2.as<unsigned>(), nullptr, nq, metric, k,
                                               o.radius, 0, pkeys, pcounts, psat, parts, kp,
                                               d_keys_out, d_scores_out, d_counts_out, qflags, s));
+    XVEC_LAUNCHED();
   }
   int h_status[kNoAllocMaxQueries], h_flags[kNoAllocMaxQueries], h_ids[kNoAllocMaxQueries];
   XVEC_CUDA(cudaMemcpyAsync(h_status, qstatus, (size_t)nq * 4, cudaMemcpyDeviceToHost, s));
@@ -159,12 +167,14 @@ xvec_gpu_status noalloc_search(xvec_gpu_index* idx, const void* d_q, int nq,
     for (int q = 0; q < nq; ++q)
       if (h_status[q] == 0 && (h_flags[q] & 3)) h_ids[nl++] = q;
   if (nl > 0) {
+    if (is_cancelled(o)) return set_error("cancelled"), XVEC_GPU_CANCELLED;
     int eparts = (int)std::max<int64_t>(1, std::min<int64_t>((592 + nl - 1) / nl, (n + 1023) / 1024));
     eparts = std::min(eparts, std::max(1, flat_merge_capacity() / kp));
     if ((size_t)nl * eparts > lists)
       eparts = std::max(1, (int)(lists / (size_t)nl));
     XVEC_CUDA(cudaMemcpyAsync(ids, h_ids, (size_t)nl * 4, cudaMemcpyHostToDevice, s));
     noalloc_clear_flags<<<(nl + 255) / 256, 256, 0, s>>>(ids, nl, qflags);
+    XVEC_LAUNCHED();
     XVEC_CUDA(launch_flat_scan_exact<RowT>(rows, n, d, idx->keyrank.as<uint32_t>(), qf, ids, nl,
                                            nullptr, metric, eparts, kp, pkeys, pcounts, psat,
                                            qflags, s));
@@ -173,6 +183,7 @@ xvec_gpu_status noalloc_search(xvec_gpu_index* idx, const void* d_q, int nq,
                                               idx->max_n2.as<unsigned>(), ids, nl, metric, k,
                                               o.radius, 1, pkeys, pcounts, psat, eparts, kp,
                                               d_keys_out, d_scores_out, d_counts_out, qflags, s));
+    count_launches(2);
     XVEC_CUDA(cudaMemcpyAsync(h_flags, qflags, (size_t)nq * 4, cudaMemcpyDeviceToHost, s));
     XVEC_CUDA(cudaStreamSynchronize(s));
     for (int i = 0; i < nl; ++i)
@@ -182,8 +193,10 @@ xvec_gpu_status noalloc_search(xvec_gpu_index* idx, const void* d_q, int nq,
       }
   }
   noalloc_apply_status<<<(nq + 255) / 256, 256, 0, s>>>(qstatus, qflags, nq, d_counts_out);
+  XVEC_LAUNCHED();
   XVEC_CUDA(cudaGetLastError());
   XVEC_CUDA(cudaStreamSynchronize(s));
+  count_search(nq, nl, 0.0, 0.0);
   for (int q = 0; q < nq; ++q) {
     int st = h_status[q];
     if (st == 0 && (h_flags[q] & 4)) st = XVEC_GPU_NON_FINITE;
@@ -233,7 +246,12 @@ extern "C" xvec_gpu_status xvec_gpu_index_search_noalloc(xvec_gpu_index* idx, co
   xvec_gpu_status st = noalloc_scratch(idx->device, &scratch);
   if (st) return st;
   cudaStream_t s = static_cast<cudaStream_t>(opts->stream);
-  if (idx->desc.storage == XVEC_STORAGE_FP16)
-    return noalloc_search<__half>(idx, d_q, nq, *opts, d_keys, d_scores, d_counts, scratch, s);
-  return noalloc_search<float>(idx, d_q, nq, *opts, d_keys, d_scores, d_counts, scratch, s);
+  if (is_cancelled(*opts)) return set_error("cancelled"), XVEC_GPU_CANCELLED;
+  st = idx->desc.storage == XVEC_STORAGE_FP16
+           ? noalloc_search<__half>(idx, d_q, nq, *opts, d_keys, d_scores, d_counts, scratch, s)
+           : noalloc_search<float>(idx, d_q, nq, *opts, d_keys, d_scores, d_counts, scratch, s);
+  // On an early return work may still be queued on the array: wait for it
+  // before the next call may take the array.
+  if (st != XVEC_GPU_OK) cudaStreamSynchronize(s);
+  return st;
 }

@@ -82,8 +82,15 @@ using namespace xvec;
 extern "C" int32_t xvec_gpu_index_candidate_count(const xvec_gpu_index* idx,
                                                   const xvec_gpu_search_opts* opts) {
   if (!idx || !opts) return 0;
-  if (idx->desc.kind == XVEC_INDEX_SQ8_FLAT || idx->desc.kind == XVEC_INDEX_SQ4_FLAT)
-    return sq8_candidate_count(*opts);
+  switch (idx->desc.kind) {
+    case XVEC_INDEX_SQ8_FLAT:
+    case XVEC_INDEX_SQ4_FLAT:
+    case XVEC_INDEX_IVF_SQ8:
+    case XVEC_INDEX_IVF_SQ4:
+      return sq8_candidate_count(*opts);
+    default:
+      break;
+  }
   if (idx->desc.kind == XVEC_INDEX_RABITQ) return rabitq_candidate_count(*opts);
   return 0;
 }
@@ -110,6 +117,9 @@ extern "C" xvec_gpu_status xvec_gpu_index_candidates_device(xvec_gpu_index* idx,
   if (idx->desc.kind == XVEC_INDEX_SQ8_FLAT || idx->desc.kind == XVEC_INDEX_SQ4_FLAT)
     return sq8_search_impl(idx, q, nq, *opts, opts->filter_bitmap, d_keys, d_ranks, d_counts, s,
                            &statuses, true);
+  if (idx->desc.kind == XVEC_INDEX_IVF_SQ8 || idx->desc.kind == XVEC_INDEX_IVF_SQ4)
+    return ivf_sq8_search_impl(idx, q, nq, *opts, opts->filter_bitmap, d_keys, d_ranks,
+                               d_counts, s, &statuses, true);
   return rabitq_search_impl(idx, q, nq, *opts, opts->filter_bitmap, d_keys, d_ranks, d_counts, s,
                             &statuses, true);
 }

@@ -709,7 +709,8 @@ xvec_gpu_status sq8_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
 xvec_gpu_status ivf_sq8_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
                                     const xvec_gpu_search_opts& o, const uint32_t* d_bitmap,
                                     uint64_t* d_keys, float* d_scores, int* d_counts,
-                                    cudaStream_t s, std::vector<int>* statuses) {
+                                    cudaStream_t s, std::vector<int>* statuses,
+                                    bool candidates_only) {
   if (!idx->has_model) return set_error("IVF index has no model"), XVEC_GPU_INVALID_ARGUMENT;
   if (o.nprobe <= 0) return set_error("core: IVF NProbe must be positive"), XVEC_GPU_INVALID_ARGUMENT;
   EventTimer timer(s);
@@ -717,6 +718,8 @@ xvec_gpu_status ivf_sq8_search_impl(xvec_gpu_index* idx, const float* d_q, int n
   const int d = idx->desc.dimension, metric = idx->desc.metric;
   const int64_t n = idx->n;
   const bool refine = o.refine_scale > 0;
+  if (candidates_only && !refine)
+    return set_error("candidates of a search without refinement"), XVEC_GPU_INVALID_ARGUMENT;
   int stage_k = o.top_k;
   if (refine) {
     if (std::isinf(o.refine_scale))
@@ -788,7 +791,7 @@ xvec_gpu_status ivf_sq8_search_impl(xvec_gpu_index* idx, const float* d_q, int n
   float* o_scores = d_scores;
   int* o_counts = d_counts;
   if ((st = spos.alloc((size_t)nq * stage_k * 4, s))) return st;
-  if (refine) {
+  if (refine && !candidates_only) {
     if ((st = skeys.alloc((size_t)nq * stage_k * 8, s)) ||
         (st = sscores.alloc((size_t)nq * stage_k * 4, s)) ||
         (st = scounts.alloc((size_t)nq * 4, s)))
@@ -881,7 +884,9 @@ xvec_gpu_status ivf_sq8_search_impl(xvec_gpu_index* idx, const float* d_q, int n
           return set_error("exact scan could not complete query %d", q), XVEC_GPU_CUDA_ERROR;
     }
   }
-  if (refine && n > 0) {
+  if (candidates_only) {
+    // The approximate stage's candidates are the output.
+  } else if (refine && n > 0) {
     // The approximate stage's failures are final; the refine stage sees
     // counts >= 0 only for healthy queries.
     sq8_status_kernel<<<blocks_of(nq), 256, 0, s>>>(qstatus.as<int>(), qflags.as<int>(), nq,
@@ -898,6 +903,11 @@ xvec_gpu_status ivf_sq8_search_impl(xvec_gpu_index* idx, const float* d_q, int n
   sq8_status_kernel<<<blocks_of(nq), 256, 0, s>>>(qstatus.as<int>(), qflags.as<int>(), nq,
                                                   d_counts);
   XVEC_LAUNCHED();
+  if (candidates_only && metric == XVEC_METRIC_IP) {
+    scores_to_ranks_kernel<<<blocks_of((int64_t)nq * stage_k), 256, 0, s>>>(
+        d_scores, d_counts, nq, stage_k, metric);
+    XVEC_LAUNCHED();
+  }
   XVEC_CUDA(cudaGetLastError());
   std::vector<int> h_flags(nq);
   XVEC_CUDA(cudaMemcpyAsync(h_flags.data(), qflags.ptr, (size_t)nq * 4, cudaMemcpyDeviceToHost, s));

@@ -3,10 +3,15 @@
 The reference fans a query out over segments and merges the per-segment
 top-k with MergeSearchResults (collection.go:4043-4066, query.go:154-191).
 Here each rank holds one shard of the rows (its own index on its own GPU,
-keys globally unique), searches it, the per-shard lists are exchanged with
-one NCCL all-gather, and every rank merges them on its GPU with the same
-ordering rule.  torch.distributed is the plumbing; the search and the merge
-are this library's kernels.
+keys globally unique), searches it, the per-shard lists are exchanged and
+every rank merges them on its GPU with the same ordering rule.
+
+With a library communicator (``library_comm``: the id made by rank 0 and
+sent over torch.distributed) the whole sharded search is one call of the C
+ABI, ``xvec_gpu_sharded_search_device``: the library's own NCCL all-gather of
+one packed buffer, bounded waits.  Without one, the exchange below runs over
+torch.distributed (any backend; gloo on the CPU) and the merge is the
+library's kernel.
 
 Refined searches (SQ8 with a refine scale, RaBitQ with Refine) take two
 exchanges, so that the refined candidates are the reference's: the
@@ -23,7 +28,8 @@ import numpy as np
 import torch
 import torch.distributed as dist
 
-from . import METRIC_L2, SearchOptions, SearchResults, _Index, merge_results_device
+from . import (METRIC_L2, Comm, SearchOptions, SearchResults, _Index, merge_results_device,
+               sharded_search_device)
 
 
 def shard_range(n_total: int, rank: int, world: int, align: int = 1):
@@ -35,6 +41,17 @@ def shard_range(n_total: int, rank: int, world: int, align: int = 1):
     begin = min(n_total, rank * per * align)
     end = min(n_total, (rank + 1) * per * align)
     return begin, end
+
+
+def library_comm(device: int, group=None, timeout_ms: int = 60000) -> Comm:
+    """The library's NCCL communicator over the ranks of a torch.distributed
+    job: rank 0 makes the id, broadcast_object_list sends it, every rank
+    joins on `device`."""
+    rank = dist.get_rank(group)
+    world = dist.get_world_size(group)
+    obj = [Comm.unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(obj, src=0, group=group)
+    return Comm.init_rank(device, obj[0], world, rank, timeout_ms)
 
 
 def exchange(keys: torch.Tensor, scores: torch.Tensor, counts: torch.Tensor, group=None):
@@ -73,9 +90,10 @@ def refined_search(candidates_fn, refine_fn, merge_fn, metric: int, k: int, c: i
 
 
 class ShardedSearch:
-    def __init__(self, index: _Index, group=None):
+    def __init__(self, index: _Index, group=None, comm: Comm | None = None):
         self.index = index
         self.group = group
+        self.comm = comm
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.device = torch.device("cuda", index.device)
 
@@ -84,6 +102,14 @@ class ShardedSearch:
         Returns merged (keys int64 [nq,k], scores float32 [nq,k], counts int32 [nq])."""
         nq, k = queries.shape[0], options.top_k
         stream = torch.cuda.current_stream(self.device).cuda_stream
+        if self.comm is not None:
+            keys = torch.empty((nq, k), dtype=torch.int64, device=self.device)
+            scores = torch.empty((nq, k), dtype=torch.float32, device=self.device)
+            counts = torch.empty((nq,), dtype=torch.int32, device=self.device)
+            sharded_search_device(self.comm, self.index, queries.data_ptr(), nq, options,
+                                  keys.data_ptr(), scores.data_ptr(), counts.data_ptr(),
+                                  stream=stream)
+            return keys, scores, counts
         c = self.index.candidate_count(options) if self.world > 1 else 0
         if c > 0:
             return self._refined(queries, options, c, stream)
