@@ -86,6 +86,67 @@ def peaks():
         return 1400.0, 6650.0, "fallback"
 
 
+def int8_peak(dev, seconds=3.0):
+    """Dense INT8 tensor throughput measured here, the denominator of the
+    INT8 scans' roofline: torch._int_mm (cuBLASLt, int8 x int8 -> int32)
+    on 8192^3, 2 * 8192^3 ops per call, best of 10 (burst) and back to back
+    for `seconds` (sustained), CUDA events; TOP/s."""
+    import torch
+    m = 8192
+    g = torch.Generator(device=dev).manual_seed(5)
+    a = torch.randint(-127, 128, (m, m), dtype=torch.int8, device=dev, generator=g)
+    b = torch.randint(-127, 128, (m, m), dtype=torch.int8, device=dev, generator=g)
+    for bt in (b, b.t().contiguous().t()):
+        try:
+            torch._int_mm(a, bt)
+            break
+        except RuntimeError:
+            continue
+    else:
+        return None
+    ops = 2.0 * m ** 3
+    burst = []
+    for _ in range(10):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        torch._int_mm(a, bt)
+        e1.record()
+        e1.synchronize()
+        burst.append(e0.elapsed_time(e1))
+    calls, t_ms = 0, 0.0
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    t_end = time.time() + seconds
+    while time.time() < t_end:
+        for _ in range(8):
+            torch._int_mm(a, bt)
+        calls += 8
+        torch.cuda.current_stream().synchronize()
+    e1.record()
+    e1.synchronize()
+    t_ms = e0.elapsed_time(e1)
+    return {"burst_tops": ops / (min(burst) / 1e3) / 1e12,
+            "sustained_tops": ops * calls / (t_ms / 1e3) / 1e12,
+            "how": "torch._int_mm int8 8192^3 (2 x 8192^3 ops): best of 10, and back to back "
+                   f"for {seconds:.0f} s; measured in this run on this GPU"}
+
+
+def int8_roofline(achieved, dev, kernel, note, ops):
+    """The INT8 scan's roofline object: against the sustained INT8 GEMM
+    figure measured in this run (the scan runs back to back in the timed
+    region), the nominal dense figure alongside."""
+    meas = int8_peak(dev)
+    peak = meas["sustained_tops"] if meas else 4500.0
+    return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOP/s",
+            "frac": (achieved / peak) if achieved else None, "traffic": None,
+            "peak_source": ("measured sustained dense INT8 GEMM (" + meas["how"] + ")"
+                            if meas else "nominal dense INT8 tensor (measurement failed)"),
+            "int8_gemm": meas, "nominal_tops": 4500.0,
+            "frac_of_nominal": (achieved / 4500.0) if achieved else None,
+            "kernel": kernel, "kernel_ms": None, "algorithmic_int_ops_per_launch": ops,
+            "note": note}
+
+
 # ---------------------------------------------------------------------------
 # Synthetic data (seeded, generated on the device where it is used).
 # ---------------------------------------------------------------------------
@@ -781,8 +842,23 @@ def run_flat_fp32(args):
                           device=dev)
     torch.cuda.synchronize()
     opts = xb.SearchOptions(top_k=F32_K)
-    ms, scan_ms, e2e_ms, st, clocks = time_search(sharded(index, world, local), queries, opts, args, dev,
-                                                  world, local)
+    search = sharded(index, world, local)
+    ms, scan_ms, e2e_ms, st, clocks = time_search(search, queries, opts, args, dev, world, local)
+    # Parity of sampled queries over all n rows (rank 0 regenerates them).
+    gpu_res = gpu_results_host(search, queries, opts)
+    parity = None
+    if rank == 0 and not args.no_parity:
+        from oracle.oracle import L2
+        allrows = torch.randn(n, F32_DIM, generator=torch.Generator(device=dev).manual_seed(101),
+                              device=dev).cpu().numpy()
+        qids = sample_query_ids(nq)
+        ora, kind = oracle_with_kernels()
+        rk, rs, rc, secs = oracle_flat_over_chunks(
+            ora, L2, [(allrows, np.arange(n, dtype=np.uint64))],
+            queries[torch.as_tensor(qids, device=dev)].cpu().numpy(), F32_K, os.cpu_count() or 1)
+        parity = parity_record(gpu_res, (rk, rs, rc), qids, n, kind, secs,
+                               "oracle Flat L2 over all rows")
+        del allrows
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_flat_l2_qps(rows.cpu().numpy(), queries[:max(8, args.cpu_sample_queries // 2)]
@@ -802,9 +878,10 @@ def run_flat_fp32(args):
                   "base_vectors": n, "dim": F32_DIM, "metric": "l2", "storage": "fp32",
                   "parallelism": f"rows sharded over {world} GPU(s), NCCL all-gather + merge",
                   "l2": "inputs larger than L2 (512 MB rows + 512 MB bf16 parts)"}
-        print(json.dumps(common_line(nq, ms, e2e_ms, args, world, "f32 rows, bf16x3 tensor ranks",
-                                     config, roof, cpu, clocks, st, F32_K, F32_DIM, 4)),
-              flush=True)
+        line = common_line(nq, ms, e2e_ms, args, world, "f32 rows, bf16x3 tensor ranks", config,
+                           roof, cpu, clocks, st, F32_K, F32_DIM, 4)
+        line["parity"] = parity
+        print(json.dumps(line), flush=True)
     finish_ranks(world)
 
 
@@ -879,13 +956,9 @@ def run_sq8(args):
         shard = e - b
         ops = 2.0 * nq * shard * SQ_DIM
         achieved = ops / (scan_ms / 1000.0) / 1e12 if scan_ms > 0 else None
-        peak = 4500.0
-        roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOP/s",
-                "frac": (achieved / peak) if achieved else None, "traffic": None,
-                "peak_source": "nominal dense INT8 tensor (no measured INT8 figure); the scan "
-                               "runs on tcgen05 kind::i8",
-                "kernel": "SQ8 code scan", "kernel_ms": scan_ms,
-                "algorithmic_int_ops_per_launch": ops}
+        roof = int8_roofline(achieved, dev, "SQ8 code scan",
+                             "the scan runs on tcgen05 kind::i8", ops)
+        roof["kernel_ms"] = scan_ms
         config = {"workload": SQ_WORKLOAD, "global_batch": nq, "top_k": SQ_K, "base_vectors": n,
                   "dim": SQ_DIM, "metric": "ip", "refine_scale": SQ_SCALE,
                   "parallelism": f"rows sharded over {world} GPU(s), NCCL all-gather + merge",
@@ -952,13 +1025,9 @@ def run_sq4(args):
         shard = e - b
         flops = 2.0 * nq * shard * SQ4_DIM
         achieved = flops / (scan_ms / 1000.0) / 1e12 if scan_ms > 0 else None
-        peak = 4500.0
-        roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOP/s",
-                "frac": (achieved / peak) if achieved else None, "traffic": None,
-                "peak_source": "nominal dense INT8 tensor (no measured INT8 figure); the INT4 "
-                               "codes are scanned by tcgen05 kind::i8",
-                "kernel": "INT4 code scan", "kernel_ms": scan_ms,
-                "algorithmic_int_ops_per_launch": flops}
+        roof = int8_roofline(achieved, dev, "INT4 code scan",
+                             "the INT4 codes are scanned by tcgen05 kind::i8", flops)
+        roof["kernel_ms"] = scan_ms
         config = {"workload": SQ4_WORKLOAD, "global_batch": nq, "top_k": SQ4_K,
                   "base_vectors": n, "dim": SQ4_DIM, "metric": "l2", "refine_scale": SQ4_SCALE,
                   "parallelism": f"rows sharded over {world} GPU(s), NCCL all-gather + merge",
@@ -1150,13 +1219,9 @@ def run_rabitq(args, total_bits=1):
             # query [h | l]: 2 x nq x n x (2 padded) integer ops.
             ops = 2.0 * nq * (e - b) * (2 * padded)
             achieved = ops / (scan_ms / 1000.0) / 1e12 if scan_ms > 0 else None
-            peak = 4500.0
-            roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOP/s",
-                    "frac": (achieved / peak) if achieved else None, "traffic": None,
-                    "peak_source": "nominal dense INT8 tensor (no measured INT8 figure); the "
-                                   "scan runs on tcgen05 kind::i8",
-                    "kernel": "RaBitQ code-plane scan", "kernel_ms": scan_ms,
-                    "algorithmic_int_ops_per_launch": ops}
+            roof = int8_roofline(achieved, dev, "RaBitQ code-plane scan",
+                                 "the scan runs on tcgen05 kind::i8", ops)
+            roof["kernel_ms"] = scan_ms
             workload, dtype = RQ_WORKLOAD, "1-bit codes as i8 planes, i32 dots, f32/f64 estimates"
             l2note = "inputs larger than L2 (19.2 GB code planes, 38 GB originals)"
         config = {"workload": workload, "global_batch": nq, "top_k": RQ_K, "base_vectors": n,

@@ -6,9 +6,9 @@ At n >= 2^20 rows the tensor-core scan runs two seeding launches (the
 first 1/256 and then 1/16 of the rows, each followed by the per-query
 threshold reduction) before the main launch over the rest, and the per-part
 candidate lists of the seeding launches saturate.  One query equals a row
-planted 300 times under different keys: its 100 best keys tie on the score,
-more than a candidate list holds, so the coverage check sends it to the
-exact (reference-order) scan.  Every query of the batch runs through the
+planted at 600 consecutive positions under different keys: its 100 best keys
+tie on the score and fall into one row part, more than its candidate lists
+hold, so the coverage check sends it to the exact (reference-order) scan.  Every query of the batch runs through the
 GPU; the oracle (a scalar restatement) checks a sample of 64 of them plus
 the planted one, since all 1,024 would take it minutes.  Keys identical,
 scores bit-identical (topk.go:105-166, query.go:154-191)."""
@@ -41,7 +41,9 @@ def mixture(rng, n, d, clusters=200, sigma=0.3, normalise=True):
 def base(seed, normalise):
     rng = np.random.default_rng(seed)
     rows = mixture(rng, N, D, normalise=normalise)
-    planted = rng.choice(N, 300, replace=False)
+    # 600 consecutive positions (at least 300 inside one row part of the main
+    # launch), so that a candidate list receives more tied keys than it holds.
+    planted = np.arange(700_000, 700_600)
     # Unnormalised bases plant a row of three times the norm, so that under
     # inner product too its copies are the query's best results.
     rows[planted] = rows[planted[0]] * (1.0 if normalise else 3.0)
@@ -61,7 +63,7 @@ def check(oracle, xb, res, metric, rows, keys, queries):
         assert int(res.counts[q]) == c, q
         assert np.array_equal(res.keys[q, :c], ok[i, :c]), q
         assert np.array_equal(res.scores[q, :c].view(np.uint32), os_[i, :c].view(np.uint32)), q
-    # The planted query's 100 results are 100 of the 300 identical rows.
+    # The planted query's 100 results are 100 of the 600 identical rows.
     assert len(np.unique(res.scores[517, :K])) == 1
 
 

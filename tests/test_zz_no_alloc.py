@@ -28,9 +28,10 @@ def _pool():
 
 
 def _reset_pool_high_water():
+    from cuda.bindings import driver
     cudart, pool = _pool()
     attr = cudart.cudaMemPoolAttr.cudaMemPoolAttrUsedMemHigh
-    (err,) = cudart.cudaMemPoolSetAttribute(pool, attr, cudart.cuuint64_t(0))
+    (err,) = cudart.cudaMemPoolSetAttribute(pool, attr, driver.cuuint64_t(0))
     assert err == cudart.cudaError_t.cudaSuccess
 
 
@@ -188,14 +189,15 @@ def test_noalloc_allocates_nothing_and_equals_the_oracle(oracle, xb):
 
 
 def test_noalloc_exact_pass_fallback(oracle, xb):
-    """A query equal to a row planted 300 times under different keys: its 100
-    best results tie, more than a candidate list holds, so the coverage
-    check sends it to the exact pass, which runs in the array too."""
+    """A query equal to a row planted at 600 consecutive positions under
+    different keys: its 100 best results tie and fall into one row part of
+    the scan, more than that part's candidate list holds, so the coverage
+    check sends the query to the exact pass, which runs in the array too."""
     import torch
     rng = np.random.default_rng(37)
     n, d, k = 9000, 64, 100
     rows = rng.standard_normal((n, d)).astype(np.float32)
-    planted = rng.choice(n, 300, replace=False)
+    planted = np.arange(3000, 3600)
     rows[planted] = rows[planted[0]]
     keys = rng.permutation(1 << 22)[:n].astype(np.uint64)
     queries = rng.standard_normal((40, d)).astype(np.float32)
