@@ -55,13 +55,13 @@ RABITQ_FACTORS_DTYPE = np.dtype([("cluster", "<i4"), ("pad_", "<i4"), ("coarse_a
                                  ("full_add", "<f8"), ("full_rescale", "<f8")])
 
 
-def build(reference: bool = True) -> None:
-    """Compile the restatement and, when the reference checkout exists, its C kernels."""
+def build(reference: str | None = None) -> None:
+    """Compile the restatement and, when `reference` (else the XVEC_REFERENCE
+    environment variable) names an existing reference checkout, its C kernels."""
     subprocess.run(["make", "-s", "-C", HERE], check=True)
-    if reference and os.path.isdir(os.environ.get("XVEC_REFERENCE", "/root/reference")):
-        subprocess.run(["make", "-s", "-C", HERE, "ref",
-                        "REFERENCE=" + os.environ.get("XVEC_REFERENCE", "/root/reference")],
-                       check=True)
+    reference = reference or os.environ.get("XVEC_REFERENCE")
+    if reference and os.path.isdir(reference):
+        subprocess.run(["make", "-s", "-C", HERE, "ref", "REFERENCE=" + reference], check=True)
 
 
 def _ptr(a: np.ndarray | None, typ):

@@ -98,15 +98,18 @@ def test_int4_odd_dimension(xb):
     idx.close()
 
 
-@pytest.mark.parametrize("metric", [L2, IP, COSINE])
-def test_int4_ivf_is_int4_over_the_probed_lists(oracle, xb, metric):
+@pytest.mark.parametrize("metric", [L2, IP, COSINE, MIPSL2])
+@pytest.mark.parametrize("d", [18, 64])
+def test_int4_ivf_is_int4_over_the_probed_lists(oracle, xb, metric, d):
     """ScalarQuantizedIVFIndex with QuantizationInt4 (ivf_quantized.go:135-192)
     is the INT4 SQ search restricted to the probed lists' positions: per
     query, the oracle's INT4 search with a filter holding exactly those
-    positions (the same composition the oracle pins for INT8)."""
+    positions (the same composition the oracle pins for INT8).  d = 64 runs
+    the list-major interleaved code copy (d a multiple of 16); d = 18 the
+    scan of the codes by position."""
     from oracle.zvecivf import csr_of
-    rng = np.random.default_rng(60 + metric)
-    n, d, nlist = 3000, 64, 16
+    rng = np.random.default_rng(60 + metric + 10 * d)
+    n, nlist = 3000, 16
     rows = scaled_gaussian(rng, n, d)
     keys = rng.permutation(1 << 20)[:n].astype(np.uint64)
     cents = rows[rng.choice(n, nlist, replace=False)].copy()
