@@ -239,22 +239,45 @@ def shard_data(seed, n, d, metric):
     return rows, keys, queries
 
 
-def test_two_gpus_one_process(oracle, xb):
+@pytest.mark.parametrize("case", ["fp16_cosine", "fp32_l2", "fp16_ip_small_shard",
+                                  "fp32_l2_planted"])
+def test_two_gpus_one_process(oracle, xb, case):
+    """Flat over two shards: each shard rescores only the candidates inside
+    the band that every shard's k best fast ranks give (one exchange before
+    the merge).  Cases: the tensor-core scans (FP16 cosine, FP32 split L2);
+    a shard with fewer rows than k (its ranks padded with +inf); a query
+    whose 100 best rows tie on one shard (600 copies of one row in one row
+    part: that shard's coverage check sends it to the exact scan)."""
     if xb.device_count() < 2:
         pytest.skip("needs two GPUs")
-    n, d = 30000, 128
-    rows, keys, queries = shard_data(21, n, d, COSINE)
-    r16, q16 = rows.astype(np.float16), queries.astype(np.float16)
+    n, d, k = 30000, 128, 100
+    metric = {"fp16_cosine": COSINE, "fp32_l2": L2, "fp16_ip_small_shard": IP,
+              "fp32_l2_planted": L2}[case]
+    fp16 = case.startswith("fp16")
+    rows, keys, queries = shard_data(21, n, d, metric)
+    split = 50 if case == "fp16_ip_small_shard" else 13000
+    if case == "fp32_l2_planted":
+        rows[20000:20600] = rows[20000]
+        queries[5] = rows[20000]
+    if fp16:
+        rows = rows.astype(np.float16).astype(np.float32)
+        queries = queries.astype(np.float16).astype(np.float32)
     shards = []
-    for dev, (b, e) in enumerate(((0, 13000), (13000, n))):
-        idx = xb.DenseFlatIndex(d, COSINE, xb.STORAGE_FP16, device=dev)
-        idx.add(keys[b:e], r16[b:e].view(np.uint16))
+    for dev, (b, e) in enumerate(((0, split), (split, n))):
+        if fp16:
+            idx = xb.DenseFlatIndex(d, metric, xb.STORAGE_FP16, device=dev)
+            idx.add(keys[b:e], rows[b:e].astype(np.float16).view(np.uint16))
+        else:
+            idx = xb.DenseFlatIndex(d, metric, device=dev)
+            idx.add(keys[b:e], rows[b:e])
         shards.append(idx)
     comms = xb.Comm.init_all([0, 1])
-    res = xb.sharded_search(comms, shards, q16.view(np.uint16), xb.SearchOptions(top_k=100))
-    _, ok, os_, oc, ost = oracle.flat_search(COSINE, r16.astype(np.float32), keys,
-                                             q16.astype(np.float32), 100)
+    q_in = queries.astype(np.float16).view(np.uint16) if fp16 else queries
+    res = xb.sharded_search(comms, shards, q_in, xb.SearchOptions(top_k=k))
+    _, ok, os_, oc, ost = oracle.flat_search(metric, rows, keys, queries, k)
     same((res.keys, res.scores, res.counts), (ok, os_, oracle_counts(oc, ost)))
+    if case == "fp32_l2_planted":
+        assert len(np.unique(res.scores[5, :k])) == 1
     for c in comms:
         c.close()
     for s in shards:

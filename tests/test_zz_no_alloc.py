@@ -179,7 +179,9 @@ def test_noalloc_allocates_nothing_and_equals_the_oracle(oracle, xb):
     _reset_pool_high_water()
     outs = [call(idx.search_device_noalloc), call(idx.search_device_noalloc)]
     assert _pool_high_water() == 0, "the no-allocation search used the stream-ordered pool"
-    assert torch.cuda.mem_get_info()[0] == free0
+    # Free device memory may grow (a pool trims what earlier tests left at a
+    # synchronisation) but never shrinks across the calls.
+    assert torch.cuda.mem_get_info()[0] >= free0
     for out in outs:
         _oracle_check(oracle, out, rows, keys, queries, L2, k)
     _reset_pool_high_water()

@@ -160,7 +160,7 @@ int choose_kp(int k) {
 // ---------------------------------------------------------------------------
 xvec_gpu_status tc_seeded_scan(int device, int nq, int64_t n, int kp, cudaStream_t s,
                                const TcScanLaunch& scan, Scratch& pkeys, Scratch& pcounts,
-                               Scratch& psat, int* lists_out) {
+                               Scratch& psat, int* lists_out, Scratch* gthr_out) {
   // Parts: pick the row split whose CTA count best fills whole waves of
   // one CTA per SM, keeping at least 16 tiles of 256 rows per part.
   int sms = 148;
@@ -211,7 +211,8 @@ xvec_gpu_status tc_seeded_scan(int device, int nq, int64_t n, int kp, cudaStream
       1, std::min<int64_t>(std::min<int64_t>(64, merge_lists / lpp - used), rest / 4096)));
   const int cap = flat_tc_cap();
   const int lists = (used + parts) * lpp;
-  Scratch gthr;
+  Scratch gthr_local;
+  Scratch& gthr = gthr_out ? *gthr_out : gthr_local;
   xvec_gpu_status st;
   if ((st = pkeys.alloc((size_t)nq * lists * cap * 8, s)) ||
       (st = pcounts.alloc((size_t)nq * lists * 4, s)) ||
@@ -242,7 +243,8 @@ template <typename RowT>
 xvec_gpu_status flat_search_impl(xvec_gpu_index* idx, const void* d_q, int nq,
                                  const xvec_gpu_search_opts& o, const uint32_t* d_bitmap,
                                  uint64_t* d_keys_out, float* d_scores_out, int* d_counts_out,
-                                 cudaStream_t s, std::vector<int>* statuses) {
+                                 cudaStream_t s, std::vector<int>* statuses,
+                                 BandExchange* band) {
   const int d = idx->desc.dimension;
   const int metric = idx->desc.metric;
   const int k = o.top_k;
@@ -263,6 +265,33 @@ xvec_gpu_status flat_search_impl(xvec_gpu_index* idx, const void* d_q, int nq,
   XVEC_LAUNCHED();
   XVEC_CUDA(cudaGetLastError());
   XVEC_CUDA(cudaMemsetAsync(d_counts_out, 0, (size_t)nq * 4, s));
+
+  // Sharded search: every shard's k best fast ranks and eps, exchanged once,
+  // give each query a rank limit that every row of the global top-k meets on
+  // its own shard, so a shard rescores about k / nranks candidates instead
+  // of all within its own F_k + 2 eps (pipeline.cuh, band_limit_kernel).
+  Scratch band_limit;
+  auto run_band = [&](const uint64_t* lkeys, const int* lcounts, int nlists, int stride,
+                      const unsigned long long* gthr, int split) -> xvec_gpu_status {
+    if (!band) return XVEC_GPU_OK;
+    band->used = true;
+    const size_t w = (size_t)nq * (k + 1);
+    Scratch bsend, brecv;
+    xvec_gpu_status bst;
+    if ((bst = bsend.alloc(w * 4, s)) || (bst = brecv.alloc(w * 4 * band->nranks, s)) ||
+        (bst = band_limit.alloc((size_t)nq * 4, s)))
+      return bst;
+    XVEC_CUDA(launch_flat_band_prepare<RowT>(rows, d, qf.as<float>(), qn2.as<float>(),
+                                             idx->max_n2.as<unsigned>(), nq, metric, k, lkeys,
+                                             lcounts, nlists, stride, gthr, bsend.as<float>(), s,
+                                             split));
+    XVEC_LAUNCHED();
+    if ((bst = band->allgather(bsend.as<float>(), brecv.as<float>(), w, s))) return bst;
+    XVEC_CUDA(launch_flat_band_limit(brecv.as<float>(), band->nranks, nq, k, bsend.as<float>(),
+                                     band_limit.as<float>(), s));
+    XVEC_LAUNCHED();
+    return XVEC_GPU_OK;
+  };
 
   std::vector<int> h_status(nq), h_flags(nq);
   const int kp = choose_kp(k);
@@ -290,7 +319,7 @@ xvec_gpu_status flat_search_impl(xvec_gpu_index* idx, const void* d_q, int nq,
     const float* row_aux =
         metric == XVEC_METRIC_COSINE ? idx->row_inv.as<float>() : idx->row_n2.as<float>();
     const __half* hrows = reinterpret_cast<const __half*>(rows);
-    Scratch pkeys, pcounts, psat;
+    Scratch pkeys, pcounts, psat, gthr_keep;
     int lists = 0;
     timer.mark(1);
     st = tc_seeded_scan(idx->device, nq, n, kp, s,
@@ -313,17 +342,22 @@ xvec_gpu_status flat_search_impl(xvec_gpu_index* idx, const void* d_q, int nq,
                               d_bitmap ? d_bitmap + b / 32 : nullptr, p, kp, list0, nlists, cand,
                               counts, sat, qflags.as<int>(), kstatus.as<int>(), s);
                         },
-                        pkeys, pcounts, psat, &lists);
+                        pkeys, pcounts, psat, &lists, &gthr_keep);
     if (st) return st;
     timer.mark(2);
     XVEC_LAUNCHED();
     count_tensor_scan();
     if (is_cancelled(o)) return set_error("cancelled"), XVEC_GPU_CANCELLED;
+    const unsigned long long* gthr = gthr_keep.as<unsigned long long>();
+    if ((st = run_band(pkeys.as<uint64_t>(), pcounts.as<int>(), lists, cap, gthr,
+                       kSplit ? 1 : 0)))
+      return st;
     XVEC_CUDA(launch_flat_merge_rescore<RowT>(
         rows, d, idx->pos_of_kr.as<uint32_t>(), idx->keys.as<uint64_t>(), qf.as<float>(),
         qn2.as<float>(), idx->max_n2.as<unsigned>(), nullptr, nq, metric, k, o.radius, 0,
         pkeys.as<uint64_t>(), pcounts.as<int>(), psat.as<uint64_t>(), lists, cap, d_keys_out,
-        d_scores_out, d_counts_out, qflags.as<int>(), s, kSplit ? 1 : 0));
+        d_scores_out, d_counts_out, qflags.as<int>(), s, kSplit ? 1 : 0, gthr,
+        band ? band_limit.as<float>() : nullptr));
     XVEC_LAUNCHED();
   } else if (fast) {
     if (is_cancelled(o)) return set_error("cancelled"), XVEC_GPU_CANCELLED;
@@ -346,11 +380,14 @@ xvec_gpu_status flat_search_impl(xvec_gpu_index* idx, const void* d_q, int nq,
     XVEC_LAUNCHED();
     count_tensor_scan();
     if (is_cancelled(o)) return set_error("cancelled"), XVEC_GPU_CANCELLED;
+    if ((st = run_band(pkeys.as<uint64_t>(), pcounts.as<int>(), parts, kp, nullptr, 0)))
+      return st;
     XVEC_CUDA(launch_flat_merge_rescore<RowT>(
         rows, d, idx->pos_of_kr.as<uint32_t>(), idx->keys.as<uint64_t>(), qf.as<float>(),
         qn2.as<float>(), idx->max_n2.as<unsigned>(), nullptr, nq, metric, k, o.radius, 0,
         pkeys.as<uint64_t>(), pcounts.as<int>(), psat.as<uint64_t>(), parts, kp, d_keys_out,
-        d_scores_out, d_counts_out, qflags.as<int>(), s));
+        d_scores_out, d_counts_out, qflags.as<int>(), s, 0, nullptr,
+        band ? band_limit.as<float>() : nullptr));
     XVEC_LAUNCHED();
   }
   XVEC_CUDA(cudaMemcpyAsync(h_status.data(), qstatus.ptr, (size_t)nq * 4, cudaMemcpyDeviceToHost,
@@ -446,14 +483,15 @@ xvec_gpu_status validate_search(xvec_gpu_index* idx, int nq, const xvec_gpu_sear
 xvec_gpu_status search_device_locked(xvec_gpu_index* idx, const void* d_q, int nq,
                                      const xvec_gpu_search_opts& o, const uint32_t* d_bitmap,
                                      uint64_t* d_keys, float* d_scores, int* d_counts,
-                                     cudaStream_t s, std::vector<int>* statuses) {
+                                     cudaStream_t s, std::vector<int>* statuses,
+                                     BandExchange* band) {
   switch (idx->desc.kind) {
     case XVEC_INDEX_FLAT:
       if (idx->desc.storage == XVEC_STORAGE_FP16)
         return flat_search_impl<__half>(idx, d_q, nq, o, d_bitmap, d_keys, d_scores, d_counts, s,
-                                        statuses);
+                                        statuses, band);
       return flat_search_impl<float>(idx, d_q, nq, o, d_bitmap, d_keys, d_scores, d_counts, s,
-                                     statuses);
+                                     statuses, band);
     case XVEC_INDEX_SQ8_FLAT:
     case XVEC_INDEX_SQ4_FLAT:
       return sq8_search_impl(idx, static_cast<const float*>(d_q), nq, o, d_bitmap, d_keys,

@@ -119,10 +119,24 @@ using TcScanLaunch = std::function<cudaError_t(int64_t b, int64_t e, int parts, 
                                                uint64_t* cand, int* counts, uint64_t* sat)>;
 // Runs the scan over all n rows as seeding launches over growing prefixes
 // (each followed by a threshold seeding) and one launch over the rest;
-// allocates the lists and reports their number per query.
+// allocates the lists and reports their number per query.  gthr_out
+// (optional) keeps the per-query shared thresholds for the merge's filter.
 xvec_gpu_status tc_seeded_scan(int device, int nq, int64_t n, int kp, cudaStream_t s,
                                const TcScanLaunch& scan, Scratch& pkeys, Scratch& pcounts,
-                               Scratch& psat, int* lists_out);
+                               Scratch& psat, int* lists_out, Scratch* gthr_out = nullptr);
+
+// A sharded search's exchange of per-query fast-rank bands (comm.cu): set by
+// the sharded search for one shard's Flat search, which calls it once
+// between its scan and its merge with `count` floats per rank (every rank
+// calls it exactly once per search, also when its own search failed).
+struct BandExchange {
+  int nranks = 1;
+  bool used = false;
+  // All-gathers count floats of send from every rank into recv
+  // [nranks][count]; bounded (XVEC_GPU_TIMEOUT / XVEC_GPU_NCCL_ERROR).
+  std::function<xvec_gpu_status(const float* send, float* recv, size_t count, cudaStream_t s)>
+      allgather;
+};
 
 // MergeSearchResults of `parts` lists per query (merge.cu): part p's keys,
 // scores and counts start p * key_stride, p * score_stride and p *
@@ -139,7 +153,8 @@ xvec_gpu_status validate_search(xvec_gpu_index* idx, int nq, const xvec_gpu_sear
 xvec_gpu_status search_device_locked(xvec_gpu_index* idx, const void* d_q, int nq,
                                      const xvec_gpu_search_opts& o, const uint32_t* d_bitmap,
                                      uint64_t* d_keys, float* d_scores, int* d_counts,
-                                     cudaStream_t s, std::vector<int>* statuses);
+                                     cudaStream_t s, std::vector<int>* statuses,
+                                     BandExchange* band = nullptr);
 size_t query_elem_bytes(const xvec_gpu_index* idx);
 // The caller's cancel flag (opts.cancel_flag) is set.
 bool is_cancelled(const xvec_gpu_search_opts& o);

@@ -35,6 +35,7 @@
 #include <vector>
 
 #include "capi_internal.h"
+#include "flat_kernels.cuh"
 #include "common.cuh"
 
 struct xvec_gpu_comm {
@@ -205,6 +206,55 @@ xvec_gpu_status fail_all(int* d_counts, int nq, xvec_gpu_status st, cudaStream_t
 
 bool whole_call_failure(xvec_gpu_status st) { return st != XVEC_GPU_OK; }
 
+__global__ void fill_float_kernel(float* p, size_t n, float v) {
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) p[i] = v;
+}
+
+// All-gathers count floats per rank (the Flat band exchange); bounded.
+xvec_gpu_status allgather_floats(xvec_gpu_comm* c, const float* send, float* recv, size_t count,
+                                 cudaStream_t s) {
+  const ncclResult_t r = nccl().AllGather(send, recv, count, ncclFloat32, c->comm, s);
+  xvec_gpu_status st;
+  if (r == ncclInProgress) {
+    if ((st = wait_ready(c, Clock::now(), "band all-gather enqueue"))) return st;
+  } else if (r != ncclSuccess) {
+    set_error("ncclAllGather: %s", nccl_msg(r));
+    abort_comm(c);
+    return XVEC_GPU_NCCL_ERROR;
+  }
+  return wait_stream(c, s, "all-gather of the fast-rank bands");
+}
+
+// The band exchange of a sharded Flat search: used by every rank exactly
+// once per search (a rank whose search ended before its band takes part
+// with an empty band, so that all ranks take the same collective steps).
+struct FlatBand {
+  BandExchange ex;
+  bool on = false;
+  FlatBand(xvec_gpu_comm* c, const xvec_gpu_index* idx, int k) {
+    on = c->nranks > 1 && idx->desc.kind == XVEC_INDEX_FLAT && flat_band_supported(c->nranks, k);
+    ex.nranks = c->nranks;
+    ex.allgather = [c](const float* send, float* recv, size_t count, cudaStream_t s) {
+      return allgather_floats(c, send, recv, count, s);
+    };
+  }
+  BandExchange* get() { return on ? &ex : nullptr; }
+  // Takes part with +inf ranks when the search did not reach its band.
+  xvec_gpu_status finish(int nq, int k, cudaStream_t s) {
+    if (!on || ex.used) return XVEC_GPU_OK;
+    ex.used = true;
+    const size_t w = (size_t)nq * (k + 1);
+    Scratch send, recv;
+    xvec_gpu_status st;
+    if ((st = send.alloc(w * 4, s)) || (st = recv.alloc(w * 4 * ex.nranks, s))) return st;
+    fill_float_kernel<<<(unsigned)((w + 255) / 256), 256, 0, s>>>(send.as<float>(), w, INFINITY);
+    XVEC_LAUNCHED();
+    XVEC_CUDA(cudaGetLastError());
+    return ex.allgather(send.as<float>(), recv.as<float>(), w, s);
+  }
+};
+
 // One rank's lists in the exchange: keys [nq kk] uint64, scores [nq kk]
 // float32, counts [nq] int32, padded to 16 bytes.
 struct Packed {
@@ -295,12 +345,17 @@ xvec_gpu_status rank_search(xvec_gpu_comm* c, xvec_gpu_index* idx, const void* d
   if ((st = lk.alloc((size_t)nq * k * 8, s)) || (st = ls.alloc((size_t)nq * k * 4, s)) ||
       (st = lc.alloc((size_t)nq * 4, s)))
     return st;
+  FlatBand band(c, idx, k);
   {
     std::shared_lock<std::shared_mutex> lock(idx->mu);
     std::vector<int> statuses;
     st = search_device_locked(idx, d_q, nq, opts, opts.filter_bitmap, lk.as<uint64_t>(),
-                              ls.as<float>(), lc.as<int>(), s, &statuses);
+                              ls.as<float>(), lc.as<int>(), s, &statuses, band.get());
   }
+  if (c->broken.load()) return st != XVEC_GPU_OK ? st : XVEC_GPU_NCCL_ERROR;
+  xvec_gpu_status bst = band.finish(nq, k, s);
+  if (bst == XVEC_GPU_TIMEOUT || bst == XVEC_GPU_NCCL_ERROR) return bst;
+  if (st == XVEC_GPU_OK) st = bst;
   if (whole_call_failure(st) && (st = fail_all(lc.as<int>(), nq, st, s))) return st;
   return exchange_merge(c, idx->desc.metric, k, nq, lk.as<uint64_t>(), ls.as<float>(),
                         lc.as<int>(), d_keys, d_scores, d_counts, h_counts, s);

@@ -211,29 +211,14 @@ __global__ void __launch_bounds__(256) seed_thresholds_kernel(
     const uint64_t* __restrict__ cand, const int* __restrict__ counts, int num_lists,
     int seed_lists, int cap, int kp, unsigned long long* __restrict__ gthr) {
   extern __shared__ __align__(16) unsigned char seed_smem[];
-  uint64_t* keys = reinterpret_cast<uint64_t*>(seed_smem);
+  uint64_t* keys = reinterpret_cast<uint64_t*>(seed_smem);  // [seed_lists * kp]
   __shared__ int hist[256];
-  __shared__ int offs[65];
   const int q = blockIdx.x;
-  if (threadIdx.x == 0) {
-    int total = 0;
-    for (int l = 0; l < seed_lists; ++l) {
-      offs[l] = total;
-      total += min(counts[(int64_t)q * num_lists + l], kp);
-    }
-    offs[seed_lists] = total;
-  }
-  __syncthreads();
-  const int total = offs[seed_lists];
+  // Published lists hold at most kp keys each, so the buffer holds them all.
+  const int total = gather_union(cand, counts, (int64_t)q * num_lists, seed_lists, cap,
+                                 kEmptyKey, keys, seed_lists * kp);
   if (total < kp) return;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int l = warp; l < seed_lists; l += blockDim.x >> 5) {
-    const uint64_t* src = cand + ((int64_t)q * num_lists + l) * cap;
-    const int c = offs[l + 1] - offs[l];
-    for (int j = lane; j < c; j += 32) keys[offs[l] + j] = src[j];
-  }
-  __syncthreads();
-  const uint64_t kth = smem_radix_select(keys, total, kp, 0, hist);
+  const uint64_t kth = smem_radix_select(keys, min(total, seed_lists * kp), kp, 0, hist);
   if (threadIdx.x == 0) atomicMin(&gthr[q], (unsigned long long)kth);
 }
 
@@ -310,24 +295,104 @@ cudaError_t launch_flat_merge_rescore(const RowT* rows, int d, const uint32_t* p
                                       const uint64_t* part_keys, const int* part_counts,
                                       const uint64_t* part_sat, int num_parts, int stride,
                                       uint64_t* out_keys, float* out_scores, int* out_counts,
-                                      int* q_flags, cudaStream_t stream, int split_eps) {
+                                      int* q_flags, cudaStream_t stream, int split_eps,
+                                      const unsigned long long* gthr, const float* band) {
   FlatScorer<RowT> sc{metric, rows, qf, d, q_n2, max_n2, split_eps};
   return launch_merge_rescore(sc, pos_of_keyrank, keys, query_ids, nlist, k, radius, exact_mode,
                               part_keys, part_counts, part_sat, num_parts, stride, out_keys,
-                              out_scores, out_counts, nullptr, q_flags, stream);
+                              out_scores, out_counts, nullptr, q_flags, stream, gthr, band);
 }
-template cudaError_t launch_flat_merge_rescore<float>(const float*, int, const uint32_t*,
-                                                      const uint64_t*, const float*, const float*,
-                                                      const unsigned*, const int*, int, int, int,
-                                                      float, int, const uint64_t*, const int*,
-                                                      const uint64_t*, int, int, uint64_t*, float*,
-                                                      int*, int*, cudaStream_t, int);
-template cudaError_t launch_flat_merge_rescore<__half>(const __half*, int, const uint32_t*,
-                                                       const uint64_t*, const float*,
-                                                       const float*, const unsigned*, const int*,
-                                                       int, int, int, float, int, const uint64_t*,
-                                                       const int*, const uint64_t*, int, int,
-                                                       uint64_t*, float*, int*, int*,
-                                                       cudaStream_t, int);
+#define XVEC_FLAT_MERGE_INST(T)                                                                 \
+  template cudaError_t launch_flat_merge_rescore<T>(                                            \
+      const T*, int, const uint32_t*, const uint64_t*, const float*, const float*,              \
+      const unsigned*, const int*, int, int, int, float, int, const uint64_t*, const int*,      \
+      const uint64_t*, int, int, uint64_t*, float*, int*, int*, cudaStream_t, int,               \
+      const unsigned long long*, const float*);
+XVEC_FLAT_MERGE_INST(float)
+XVEC_FLAT_MERGE_INST(__half)
+#undef XVEC_FLAT_MERGE_INST
+
+template <typename RowT>
+cudaError_t launch_flat_band_prepare(const RowT* rows, int d, const float* qf, const float* q_n2,
+                                     const unsigned* max_n2, int nq, int metric, int k,
+                                     const uint64_t* part_keys, const int* part_counts,
+                                     int num_parts, int stride, const unsigned long long* gthr,
+                                     float* out, cudaStream_t stream, int split_eps) {
+  FlatScorer<RowT> sc{metric, rows, qf, d, q_n2, max_n2, split_eps};
+  return launch_band_prepare(sc, nq, k, part_keys, part_counts, num_parts, stride, gthr, out,
+                             stream);
+}
+template cudaError_t launch_flat_band_prepare<float>(const float*, int, const float*,
+                                                     const float*, const unsigned*, int, int, int,
+                                                     const uint64_t*, const int*, int, int,
+                                                     const unsigned long long*, float*,
+                                                     cudaStream_t, int);
+template cudaError_t launch_flat_band_prepare<__half>(const __half*, int, const float*,
+                                                      const float*, const unsigned*, int, int, int,
+                                                      const uint64_t*, const int*, int, int,
+                                                      const unsigned long long*, float*,
+                                                      cudaStream_t, int);
+
+// Second half: from every shard's k best fast ranks and eps (recv [nranks]
+// blocks of nq * (k + 1) floats), the query's band limit on this shard:
+// F_k over all shards + the largest eps + this shard's eps (rounded up).
+// Any k rows with fast rank <= F_k have reference scores <= F_k + max eps,
+// so every row of the global top-k has a fast rank within the limit on its
+// own shard.  Fewer than k finite ranks in all: NaN (no band).
+__global__ void __launch_bounds__(256) band_limit_kernel(const float* __restrict__ recv,
+                                                         int nranks, int nq, int k,
+                                                         const float* __restrict__ own,
+                                                         float* __restrict__ band) {
+  extern __shared__ __align__(16) unsigned char limit_smem[];
+  uint64_t* keys = reinterpret_cast<uint64_t*>(limit_smem);  // [nranks * k]
+  __shared__ int hist[256];
+  __shared__ int s_n;
+  __shared__ unsigned s_eps;
+  const int q = blockIdx.x;
+  if (threadIdx.x == 0) {
+    s_n = 0;
+    s_eps = 0u;
+  }
+  __syncthreads();
+  for (int r = 0; r < nranks; ++r) {
+    const float* src = recv + ((int64_t)r * nq + q) * (k + 1);
+    for (int i = threadIdx.x; i < k; i += blockDim.x) {
+      const float v = src[i];
+      if (v < INFINITY) keys[atomicAdd(&s_n, 1)] = (uint64_t)float_to_ordered(v) << 32;
+    }
+    if (threadIdx.x == 0) atomicMax(&s_eps, float_to_ordered(src[k]));
+  }
+  __syncthreads();
+  const int m = s_n;
+  if (m < k) {
+    if (threadIdx.x == 0) band[q] = NAN;
+    return;
+  }
+  const uint64_t fk = smem_radix_select(keys, m, k, 32, hist);
+  if (threadIdx.x == 0) {
+    const float eps_max = ordered_to_float(s_eps);
+    const float eps_own = own[(int64_t)q * (k + 1) + k];
+    band[q] = __fadd_ru(ordered_to_float((unsigned)(fk >> 32)), __fadd_ru(eps_max, eps_own));
+  }
+}
+
+static cudaError_t launch_band_limit(const float* recv, int nranks, int nq, int k,
+                                     const float* own, float* band, cudaStream_t stream) {
+  if (nq <= 0) return cudaSuccess;
+  if (!flat_band_supported(nranks, k)) return cudaErrorInvalidValue;
+  const int smem = nranks * k * 8;
+  cudaFuncSetAttribute(band_limit_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  band_limit_kernel<<<nq, 256, smem, stream>>>(recv, nranks, nq, k, own, band);
+  return cudaGetLastError();
+}
+
+bool flat_band_supported(int nranks, int k) {
+  return nranks >= 1 && k >= 1 && (int64_t)nranks * k <= kMergeSmemEntries;
+}
+
+cudaError_t launch_flat_band_limit(const float* recv, int nranks, int nq, int k,
+                                   const float* own, float* band, cudaStream_t stream) {
+  return launch_band_limit(recv, nranks, nq, k, own, band, stream);
+}
 
 }  // namespace xvec

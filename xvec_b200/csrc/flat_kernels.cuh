@@ -52,6 +52,21 @@ cudaError_t launch_flat_merge_rescore(const RowT* rows, int d, const uint32_t* p
                                       const uint64_t* part_keys, const int* part_counts,
                                       const uint64_t* part_sat, int num_parts, int stride,
                                       uint64_t* out_keys, float* out_scores, int* out_counts,
-                                      int* q_flags, cudaStream_t stream, int split_eps = 0);
+                                      int* q_flags, cudaStream_t stream, int split_eps = 0,
+                                      const unsigned long long* gthr = nullptr,
+                                      const float* band = nullptr);
+
+// A sharded search's band (pipeline.cuh): this shard's k best fast ranks
+// and eps per query into out [nq][k + 1]; then, from every shard's, the
+// per-query rank limit (NaN: none).
+template <typename RowT>
+cudaError_t launch_flat_band_prepare(const RowT* rows, int d, const float* qf, const float* q_n2,
+                                     const unsigned* max_n2, int nq, int metric, int k,
+                                     const uint64_t* part_keys, const int* part_counts,
+                                     int num_parts, int stride, const unsigned long long* gthr,
+                                     float* out, cudaStream_t stream, int split_eps = 0);
+bool flat_band_supported(int nranks, int k);
+cudaError_t launch_flat_band_limit(const float* recv, int nranks, int nq, int k,
+                                   const float* own, float* band, cudaStream_t stream);
 
 }  // namespace xvec

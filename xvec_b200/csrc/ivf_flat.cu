@@ -35,10 +35,6 @@
 
 namespace xvec {
 
-xvec_gpu_status search_device_locked(xvec_gpu_index* idx, const void* d_q, int nq,
-                                     const xvec_gpu_search_opts& o, const uint32_t* d_bitmap,
-                                     uint64_t* d_keys, float* d_scores, int* d_counts,
-                                     cudaStream_t s, std::vector<int>* statuses);
 
 namespace {
 

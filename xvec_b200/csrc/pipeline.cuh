@@ -234,43 +234,135 @@ __global__ void __launch_bounds__(256) scan_exact_kernel(
 constexpr int kMaxCandidates = 1024;      // rescored candidates per query (k <= 1024)
 constexpr int kMaxCandidatesWide = 2048;  // the same for 1024 < k <= 2048
 constexpr int kMergeSmemEntries = 12288;  // union entries gathered in shared memory
+constexpr int kMergeFilteredEntries = 4096;  // the same when a threshold filters the union
 
 // Radix select over keys[0, m) in shared memory: the kth smallest (1-based)
 // considering bits [low_bit, 64) only; returns those high bits (low bits 0).
+// Every thread of the block calls it.  The histogram increments of a warp
+// that fall into one bin are combined (__match_any_sync) before the shared
+// atomic, and warp 0 finds the bin holding the kth key with a warp scan.
 static __device__ uint64_t smem_radix_select(const uint64_t* keys, int m, int kth, int low_bit,
-                                      int* hist) {
+                                             int* hist) {
   __shared__ uint64_t s_prefix;
   __shared__ int s_kth;
+  const int lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     s_prefix = 0;
     s_kth = kth;
   }
   __syncthreads();
+  const int mpad = (m + 31) & ~31;  // whole warps iterate together
 #pragma unroll 1
   for (int shift = 56; shift >= low_bit; shift -= 8) {
     for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
     __syncthreads();
     const uint64_t prefix = s_prefix;
     const uint64_t mask = (shift == 56) ? 0ull : (~0ull << (shift + 8));
-    for (int i = threadIdx.x; i < m; i += blockDim.x) {
-      const uint64_t key = keys[i];
-      if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 0xff], 1);
+    for (int i = threadIdx.x; i < mpad; i += blockDim.x) {
+      int bin = -1;
+      if (i < m) {
+        const uint64_t key = keys[i];
+        if ((key & mask) == prefix) bin = (int)((key >> shift) & 0xff);
+      }
+      const unsigned peers = __match_any_sync(kFullMask, bin);
+      if (bin >= 0 && lane == __ffs(peers) - 1) atomicAdd(&hist[bin], __popc(peers));
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-      int remaining = s_kth, digit = 0;
-      for (; digit < 255; ++digit) {
-        if (remaining <= hist[digit]) break;
-        remaining -= hist[digit];
+    if (threadIdx.x < 32) {
+      int local[8], sum = 0;
+#pragma unroll
+      for (int b = 0; b < 8; ++b) {
+        local[b] = hist[lane * 8 + b];
+        sum += local[b];
       }
-      s_kth = remaining;
-      s_prefix = prefix | ((uint64_t)digit << shift);
+      int incl = sum;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(kFullMask, incl, o);
+        if (lane >= o) incl += v;
+      }
+      const int excl = incl - sum;
+      const int want = s_kth;
+      const unsigned owner = __ballot_sync(kFullMask, excl < want && want <= incl);
+      if (owner != 0u) {
+        if (lane == __ffs(owner) - 1) {
+          int rem = want - excl, digit = 7;
+#pragma unroll
+          for (int b = 0; b < 8; ++b) {
+            if (rem <= local[b]) {
+              digit = b;
+              break;
+            }
+            rem -= local[b];
+          }
+          s_kth = rem;
+          s_prefix = prefix | ((uint64_t)(lane * 8 + digit) << shift);
+        }
+      } else if (lane == 31) {
+        // kth beyond the matching keys: the last bin, as a linear walk ends.
+        s_kth = want - (incl - local[7]);
+        s_prefix = prefix | (255ull << shift);
+      }
     }
     __syncthreads();
   }
   return s_prefix;
 }
 
+// Gathers the keys of one query's lists into ukeys (shared memory, any
+// order), keeping those <= filter: one warp per list, four loads per lane
+// in flight, appends combined per warp.  Returns the number of kept keys
+// (it may exceed cap; only the first cap are stored).  Every thread of the
+// block calls it.
+static __device__ int gather_union(const uint64_t* __restrict__ part_keys,
+                                   const int* __restrict__ part_counts, int64_t pbase,
+                                   int num_parts, int stride, uint64_t filter, uint64_t* ukeys,
+                                   int cap) {
+  __shared__ int s_total;
+  if (threadIdx.x == 0) s_total = 0;
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  for (int p = warp; p < num_parts; p += nwarps) {
+    const int c = part_counts[pbase + p];
+    const uint64_t* src = part_keys + (pbase + p) * stride;
+    for (int j0 = 0; j0 < c; j0 += 128) {
+      uint64_t kk[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int j = j0 + u * 32 + lane;
+        kk[u] = j < c ? src[j] : kEmptyKey;
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int j = j0 + u * 32 + lane;
+        const bool keep = j < c && kk[u] <= filter;
+        const unsigned m = __ballot_sync(kFullMask, keep);
+        if (m == 0u) continue;
+        int base = 0;
+        if (lane == 0) base = atomicAdd(&s_total, __popc(m));
+        base = __shfl_sync(kFullMask, base, 0);
+        const int slot = base + __popc(m & ((1u << lane) - 1));
+        if (keep && slot < cap) ukeys[slot] = kk[u];
+      }
+    }
+  }
+  __syncthreads();
+  return s_total;
+}
+
+// ---------------------------------------------------------------------------
+// Merge + reference rescoring.  One block (256 threads) per query.
+// exact_mode: the part keys already hold reference ranks; the candidates are
+// exactly the k best keys.
+// gthr (optional, fast mode): per query an upper bound on its kp-th best
+// fast key over all rows (the shared list threshold of the tensor-core
+// scan).  Keys above it are left out of the union, as if every list had
+// dropped them; the coverage check then also requires the bound to lie
+// above the candidate limit.
+// band (optional, fast mode): per query a rank limit computed over every
+// shard of a sharded search; the candidate limit is the lower of it and the
+// query's own F_k + 2 eps.
+// ---------------------------------------------------------------------------
 template <typename Scorer, int MAXC>
 __global__ void __launch_bounds__(256) merge_rescore_kernel(
     Scorer sc, const uint32_t* __restrict__ pos_of_keyrank, const uint64_t* __restrict__ keys,
@@ -278,54 +370,42 @@ __global__ void __launch_bounds__(256) merge_rescore_kernel(
     const uint64_t* __restrict__ part_keys, const int* __restrict__ part_counts,
     const uint64_t* __restrict__ part_sat, int num_parts, int stride,
     uint64_t* __restrict__ out_keys, float* __restrict__ out_scores, int* __restrict__ out_counts,
-    uint32_t* __restrict__ out_pos, int* __restrict__ q_flags) {
+    uint32_t* __restrict__ out_pos, int* __restrict__ q_flags,
+    const unsigned long long* __restrict__ gthr, const float* __restrict__ band,
+    int entries_cap) {
   const int metric = sc.metric;
   extern __shared__ __align__(16) unsigned char merge_smem[];
-  uint64_t* ukeys = reinterpret_cast<uint64_t*>(merge_smem);  // [kMergeSmemEntries]
+  uint64_t* ukeys = reinterpret_cast<uint64_t*>(merge_smem);  // [entries_cap]
   __shared__ int hist[256];
   __shared__ uint64_t cand[MAXC];
-  __shared__ int s_offsets[1025];
   __shared__ int s_ncand, s_fail;
   const int slot_q = blockIdx.x;
   const int qi = query_ids ? query_ids[blockIdx.x] : blockIdx.x;
   const int64_t pbase = (int64_t)slot_q * num_parts;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nwarps = blockDim.x >> 5;
 
-  // Prefix sums of the list counts (num_parts <= 1024).
   if (threadIdx.x == 0) {
-    int total = 0;
-    for (int p = 0; p < num_parts; ++p) {
-      s_offsets[p] = total;
-      total += part_counts[pbase + p];
-    }
-    s_offsets[num_parts] = total;
     s_ncand = 0;
     s_fail = 0;
   }
-  __syncthreads();
-  const int total = s_offsets[num_parts];
+  const uint64_t filter = (gthr && !exact_mode) ? (uint64_t)gthr[qi] : kEmptyKey;
+  const int total =
+      gather_union(part_keys, part_counts, pbase, num_parts, stride, filter, ukeys, entries_cap);
   if (total == 0) {
     if (threadIdx.x == 0) out_counts[qi] = 0;
     return;
   }
-  if (total > kMergeSmemEntries) {
-    // Cannot happen with the list sizes the scans produce; route to the
-    // exact path rather than read past the shared buffer.
+  if (total > entries_cap) {
+    // More keys than the shared buffer holds (the unfiltered union cannot
+    // reach it with the list sizes the scans produce): route the query to
+    // the exact path rather than read past the buffer.
     if (threadIdx.x == 0) {
       atomicOr(&q_flags[qi], 2);
       out_counts[qi] = 0;
     }
     return;
   }
-  // Gather the union (one warp per list).
-  {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int p = warp; p < num_parts; p += blockDim.x >> 5) {
-      const int off = s_offsets[p], c = s_offsets[p + 1] - off;
-      const uint64_t* src = part_keys + (pbase + p) * stride;
-      for (int j = lane; j < c; j += 32) ukeys[off + j] = src[j];
-    }
-  }
-  __syncthreads();
   const int kth = min(k, total);
   uint64_t limit;
   if (exact_mode) {
@@ -333,19 +413,32 @@ __global__ void __launch_bounds__(256) merge_rescore_kernel(
   } else {
     const uint64_t kr = smem_radix_select(ukeys, total, kth, 32, hist);
     const float eps = sc.eps(qi);
-    const float t = __fadd_ru(rank_of(kr), 2.f * eps);
+    float t = __fadd_ru(rank_of(kr), 2.f * eps);
+    if (band) {
+      const float b = band[qi];
+      if (b < t) t = b;  // NaN (no band) keeps the query's own limit
+    }
     limit = ((uint64_t)float_to_ordered(t) << 32) | 0xffffffffull;
-    // Coverage: a list dropped only keys above its saturation key.
+    // Coverage: a list dropped only keys above its saturation key, and the
+    // filter only keys above itself.
     for (int p = threadIdx.x; p < num_parts; p += blockDim.x) {
       const uint64_t sat = part_sat[pbase + p];
       if (sat != kEmptyKey && sat <= limit) atomicExch(&s_fail, 1);
     }
+    if (threadIdx.x == 0 && filter != kEmptyKey && filter <= limit) atomicExch(&s_fail, 1);
   }
-  for (int i = threadIdx.x; i < total; i += blockDim.x) {
-    const uint64_t key = ukeys[i];
-    if (key <= limit) {
-      const int slot = atomicAdd(&s_ncand, 1);
-      if (slot < MAXC) cand[slot] = key;
+  {
+    const int tpad = (total + 31) & ~31;
+    for (int i = threadIdx.x; i < tpad; i += blockDim.x) {
+      const uint64_t key = i < total ? ukeys[i] : kEmptyKey;
+      const bool in = i < total && key <= limit;
+      const unsigned m = __ballot_sync(kFullMask, in);
+      if (m == 0u) continue;
+      int base = 0;
+      if (lane == 0) base = atomicAdd(&s_ncand, __popc(m));
+      base = __shfl_sync(kFullMask, base, 0);
+      const int slot = base + __popc(m & ((1u << lane) - 1));
+      if (in && slot < MAXC) cand[slot] = key;
     }
   }
   __syncthreads();
@@ -359,8 +452,6 @@ __global__ void __launch_bounds__(256) merge_rescore_kernel(
   const int ncand = s_ncand;
   // Reference rescoring: one warp per candidate, or one half-warp per
   // candidate when the scorer evaluates a row per half-warp.
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nwarps = blockDim.x >> 5;
   if (sc.half_warp()) {
     const int half = lane >> 4;
     for (int c0 = warp * 2; c0 < ncand; c0 += nwarps * 2) {
@@ -415,6 +506,39 @@ __global__ void __launch_bounds__(256) merge_rescore_kernel(
   }
 }
 
+// First half of a sharded search's band: per query, the k best fast ranks
+// of this shard's lists (ascending is not required; +inf pads a shard with
+// fewer) and the shard's bound eps on |fast - reference|, written as k + 1
+// floats at out[q * (k + 1)].  The lists and the filter are those the merge
+// reads.
+template <typename Scorer>
+__global__ void __launch_bounds__(256) band_prepare_kernel(
+    Scorer sc, int k, const uint64_t* __restrict__ part_keys, const int* __restrict__ part_counts,
+    int num_parts, int stride, const unsigned long long* __restrict__ gthr, int entries_cap,
+    float* __restrict__ out) {
+  extern __shared__ __align__(16) unsigned char band_smem[];
+  uint64_t* ukeys = reinterpret_cast<uint64_t*>(band_smem);
+  __shared__ int hist[256];
+  __shared__ int s_n;
+  const int q = blockIdx.x;
+  float* dst = out + (int64_t)q * (k + 1);
+  const uint64_t filter = gthr ? (uint64_t)gthr[q] : kEmptyKey;
+  const int total = gather_union(part_keys, part_counts, (int64_t)q * num_parts, num_parts,
+                                 stride, filter, ukeys, entries_cap);
+  const int m = min(total, entries_cap);
+  // A truncated union gives a subset of real fast ranks: its k best are
+  // still ranks of real rows, so the band stays valid (only wider).
+  const int kth = min(k, m);
+  uint64_t kkey = 0;
+  if (kth > 0) kkey = smem_radix_select(ukeys, m, kth, 0, hist);
+  if (threadIdx.x == 0) s_n = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < m; i += blockDim.x)
+    if (kth > 0 && ukeys[i] <= kkey) dst[atomicAdd(&s_n, 1)] = rank_of(ukeys[i]);
+  __syncthreads();
+  for (int i = s_n + threadIdx.x; i < k; i += blockDim.x) dst[i] = INFINITY;
+  if (threadIdx.x == 0) dst[k] = sc.eps(q);
+}
 
 template <typename RowT, typename Ranker>
 cudaError_t launch_scan_simt(const RowT* rows, int64_t n, int d, const uint32_t* keyrank,
@@ -479,17 +603,39 @@ cudaError_t launch_merge_rescore(const Scorer& sc, const uint32_t* pos_of_keyran
                                  const int* part_counts, const uint64_t* part_sat, int num_parts,
                                  int stride, uint64_t* out_keys, float* out_scores,
                                  int* out_counts, uint32_t* out_pos, int* q_flags,
-                                 cudaStream_t stream) {
+                                 cudaStream_t stream, const unsigned long long* gthr = nullptr,
+                                 const float* band = nullptr) {
   if (nlist <= 0) return cudaSuccess;
   if (num_parts > 1024) return cudaErrorInvalidValue;
-  const int smem = kMergeSmemEntries * 8;
+  // A filtered union is small (a few kp): a smaller buffer lets more blocks
+  // share an SM; a query that overflows it takes the exact path.
+  const int cap = (gthr && !exact_mode) ? kMergeFilteredEntries : kMergeSmemEntries;
+  const int smem = cap * 8;
   if (k > kMaxCandidatesWide) return cudaErrorInvalidValue;
   auto kern = k > kMaxCandidates ? merge_rescore_kernel<Scorer, kMaxCandidatesWide>
                                  : merge_rescore_kernel<Scorer, kMaxCandidates>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   kern<<<nlist, 256, smem, stream>>>(sc, pos_of_keyrank, keys, query_ids, k, radius, exact_mode,
                                      part_keys, part_counts, part_sat, num_parts, stride,
-                                     out_keys, out_scores, out_counts, out_pos, q_flags);
+                                     out_keys, out_scores, out_counts, out_pos, q_flags, gthr,
+                                     band, cap);
+  return cudaGetLastError();
+}
+
+// The sharded band (band_prepare_kernel, band_limit_kernel) around one
+// exchange: `out` receives nq * (k + 1) floats.
+template <typename Scorer>
+cudaError_t launch_band_prepare(const Scorer& sc, int nq, int k, const uint64_t* part_keys,
+                                const int* part_counts, int num_parts, int stride,
+                                const unsigned long long* gthr, float* out, cudaStream_t stream) {
+  if (nq <= 0) return cudaSuccess;
+  if (num_parts > 1024) return cudaErrorInvalidValue;
+  const int cap = gthr ? kMergeFilteredEntries : kMergeSmemEntries;
+  const int smem = cap * 8;
+  cudaFuncSetAttribute(band_prepare_kernel<Scorer>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       smem);
+  band_prepare_kernel<Scorer><<<nq, 256, smem, stream>>>(sc, k, part_keys, part_counts, num_parts,
+                                                        stride, gthr, cap, out);
   return cudaGetLastError();
 }
 

@@ -41,10 +41,6 @@
 
 namespace xvec {
 
-xvec_gpu_status search_device_locked(xvec_gpu_index* idx, const void* d_q, int nq,
-                                     const xvec_gpu_search_opts& o, const uint32_t* d_bitmap,
-                                     uint64_t* d_keys, float* d_scores, int* d_counts,
-                                     cudaStream_t s, std::vector<int>* statuses);
 xvec_gpu_status add_device_locked(xvec_gpu_index* idx, const uint64_t* d_keys, const void* d_rows,
                                   int64_t m, cudaStream_t s);
 
