@@ -53,7 +53,8 @@ def parse():
     p.add_argument("--batch-sweep", default="",
                    help="comma-separated batch sizes (e.g. 1,8,64): after the main timing, "
                         "the median device latency of one search of each size is added to "
-                        "the JSON line as batch_sweep (rabitq_l2_refine, ivfpq_l2, sq8_ip_refine)")
+                        "the JSON line as batch_sweep (the default Flat workload, rabitq_l2_refine, ivfpq_l2, "
+                        "sq8_ip_refine)")
     p.add_argument("--workload",
                    choices=["flat_cosine_fp16", "ivfpq_l2", "sq8_ip_refine", "rabitq_l2_refine",
                             "flat_l2_fp32", "ivf_flat_l2", "ivf_sq8_l2_refine",
@@ -638,6 +639,7 @@ def batch_sweep(search, queries, opts, sizes, reps=15):
         med = times[len(times) // 2]
         out.append({"nq": b, "ms": med, "queries_per_sec": b / (med / 1000.0),
                     "tensor_scans_per_search": st["tensor_scans"] / reps,
+                    "stream_scans_per_search": st["stream_scans"] / reps,
                     "scan_ms": tst["scan_ms"] / reps, "search_device_ms": tst["search_ms"] / reps,
                     "exact_queries": st["exact_queries"]})
     return out
@@ -1199,21 +1201,16 @@ def run_rabitq(args, total_bits=1):
                              total_bits, extra_scale)
     if rank == 0:
         if total_bits > 1:
-            # BF16 MMAs of the code values against the query's high and low
-            # parts: 2 x nq x n x (2 padded) flops on the tensor pipe
-            # (2 x nq x n x padded algorithmic).
-            ops = 2.0 * nq * (e - b) * padded
+            # INT8 MMAs of the code plane v - 128 against the 16-bit integer
+            # query's two planes (h, l): 2 x nq x n x (2 padded) integer ops
+            # (2 x nq x n x padded algorithmic multiply-adds of the values).
+            ops = 2.0 * nq * (e - b) * (2 * padded)
             achieved = ops / (scan_ms / 1000.0) / 1e12 if scan_ms > 0 else None
-            bf16, _, peak_kind = peaks()
-            roof = {"bound": "tensor", "achieved": achieved, "peak": bf16, "unit": "TFLOP/s",
-                    "frac": (achieved / bf16) if achieved else None, "traffic": None,
-                    "peak_source": f"{peak_kind} sustained bf16 dense GEMM; the scan runs two "
-                                   "kind::f16 (BF16) MMAs per k-step, so the tensor pipe does "
-                                   "twice the algorithmic flops",
-                    "kernel": "RaBitQ full-code scan", "kernel_ms": scan_ms,
-                    "algorithmic_flops_per_launch": ops}
-            workload, dtype = RQ7_WORKLOAD, "7-bit codes as bf16, f32 dots, f32/f64 estimates"
-            l2note = "inputs larger than L2 (19.2 GB code values, 38 GB originals)"
+            roof = int8_roofline(achieved, dev, "RaBitQ multi-bit code-plane scan",
+                                 "the scan runs two tcgen05 kind::i8 MMAs per k-step", ops)
+            roof["kernel_ms"] = scan_ms
+            workload, dtype = RQ7_WORKLOAD, "7-bit codes as an i8 plane, i32 dots, f32/f64 estimates"
+            l2note = "inputs larger than L2 (9.6 GB code plane, 19.2 GB code values, 38 GB originals)"
         else:
             # INT8 MMAs over the code planes [127 b | b] against the integer
             # query [h | l]: 2 x nq x n x (2 padded) integer ops.
@@ -1231,6 +1228,7 @@ def run_rabitq(args, total_bits=1):
                   "l2": l2note}
         line = common_line(nq, ms, e2e_ms, args, world, dtype, config, roof, cpu, clocks, st,
                            RQ_K, RQ_DIM, 4)
+        line["exact_queries"] = int(st["exact_queries"])
         if sweep is not None:
             line["batch_sweep"] = sweep
         print(json.dumps(line), flush=True)
@@ -1424,6 +1422,20 @@ def main():
                                 if kind == "reference" else "the oracle's restatement")
                              + "; heap/top-k and merge: the ported Go rules"}
 
+    # Batch-size sweep (one GPU): device latency of one search per batch size;
+    # the streaming scan serves the smallest batches, the tensor cores the rest.
+    sweep = None
+    if args.batch_sweep and world == 1:
+        sweep = batch_sweep(search, queries, opts, [int(x) for x in args.batch_sweep.split(",")])
+        _, hbm, _ = peaks()
+        for e in sweep:
+            if e["stream_scans_per_search"] >= 1 and e["scan_ms"] > 0:
+                # The streaming scan reads every row once (plus a 1/64 sample).
+                gbs = n * DIM * 2 / (e["scan_ms"] / 1000.0) / 1e9
+                e["stream_scan_hbm"] = {"achieved_gbs": gbs, "peak_gbs": hbm,
+                                        "frac": gbs / hbm,
+                                        "bytes": "n x d x 2 (every row once)"}
+
     if rank == 0:
         bf16_peak, hbm_peak, peak_kind = peaks()
         shard_rows = min(n, per_rank * CHUNK)
@@ -1466,6 +1478,8 @@ def main():
             "gpu_launches": launches,
             "exact_queries": int(st["exact_queries"]),
         }
+        if sweep is not None:
+            line["batch_sweep"] = sweep
         print(json.dumps(line), flush=True)
     finish_ranks(world)
 

@@ -458,6 +458,39 @@ xvec_gpu_status xvec_gpu_index_search_noalloc(xvec_gpu_index* index, const void*
                                               uint64_t* d_out_keys, float* d_out_scores,
                                               int32_t* d_out_counts);
 
+/* ---- Rotation reformer -------------------------------------------------
+ * A collection whose vector index sets `rotate` rotates every stored and
+ * query vector with an FHT rotator before its scalar-quantized index sees it
+ * (collectionReformer, collection.go:1981-2000; RotationReformer,
+ * internal/core/rotation.go:248-280).  A caller of this library applies the
+ * same transform with these entry points before xvec_gpu_index_add* and
+ * xvec_gpu_index_search* (and Revert on vectors it returns).
+ *
+ * xvec_gpu_rotation_signs: the sign state collectionReformer derives for
+ * (schema name, field name, dimension, index type, quantize type): SHA-256 of
+ * "zvec-go-rotation-v1\0<schema>\0<field>\0<dimension>\0<index type>\0<quantize>"
+ * followed by a little-endian uint64 counter 0, 1, ..., the digests
+ * concatenated; out_len must be 4 * ((dimension + 7) / 8)
+ * (NewFHTRotatorFromSigns, rotation.go:87-104). */
+xvec_gpu_status xvec_gpu_rotation_signs(const char* schema_name, const char* field_name,
+                                        int32_t dimension, int32_t index_type, int32_t quantize,
+                                        uint8_t* out_signs, int64_t out_len);
+/* FHTRotator.Rotate (rotation.go:123-153; inverse = 0) or Unrotate
+ * (rotation.go:155-185; inverse = 1) of n vectors of `dimension` float32s,
+ * bit-identical to the reference.  signs: host memory, 4 * ((dimension + 7) /
+ * 8) bytes; dimension 1..65535 (MaxRotationDimension).  Host form: fails with
+ * XVEC_GPU_NON_FINITE naming the first vector whose input or result is not
+ * finite (RotateBatch, rotation.go:187-213).  Device form: in and out on
+ * `device`, enqueued on `stream`; d_failed (n int32) receives 1 for each such
+ * vector, 0 otherwise; the call does not wait. */
+xvec_gpu_status xvec_gpu_rotate(int32_t device, const uint8_t* signs, int64_t signs_len,
+                                int32_t dimension, const float* vectors, int64_t n, float* out,
+                                int32_t inverse);
+xvec_gpu_status xvec_gpu_rotate_device(int32_t device, const uint8_t* signs, int64_t signs_len,
+                                       int32_t dimension, const float* d_vectors, int64_t n,
+                                       float* d_out, int32_t inverse, int32_t* d_failed,
+                                       void* stream);
+
 /* Counters (the reference's RuntimeStats role, collection.go:5185-5315, for
  * the device path).  Device-time fields are filled only while timing is
  * enabled, because timing adds an event pair around each scan launch. */
@@ -469,6 +502,7 @@ typedef struct {
   double scan_ms;          /* device time of the candidate scan kernels */
   double search_ms;        /* device time of whole search calls */
   int64_t tensor_scans;    /* scans that ran on the tensor cores (tcgen05) */
+  int64_t stream_scans;    /* Flat scans of a few queries that streamed the rows once */
 } xvec_gpu_stats;
 void xvec_gpu_stats_enable_timing(int32_t enabled);
 

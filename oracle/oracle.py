@@ -55,6 +55,23 @@ RABITQ_FACTORS_DTYPE = np.dtype([("cluster", "<i4"), ("pad_", "<i4"), ("coarse_a
                                  ("full_add", "<f8"), ("full_rescale", "<f8")])
 
 
+def collection_rotation_signs(schema: str, field: str, dimension: int, index_type: int,
+                              quantize: int) -> np.ndarray:
+    """collectionReformer's sign state (collection.go:1981-2000): the bytes of
+    SHA-256 over the seed text followed by a little-endian uint64 counter,
+    counters 0, 1, ... concatenated until 4 ((dimension + 7) / 8) bytes."""
+    import hashlib
+    import struct
+    seed = ("zvec-go-rotation-v1\x00%s\x00%s\x00%d\x00%d\x00%d"
+            % (schema, field, dimension, index_type, quantize)).encode()
+    want = 4 * ((dimension + 7) // 8)
+    out, counter = b"", 0
+    while len(out) < want:
+        out += hashlib.sha256(seed + struct.pack("<Q", counter)).digest()
+        counter += 1
+    return np.frombuffer(out[:want], np.uint8).copy()
+
+
 def build(reference: str | None = None) -> None:
     """Compile the restatement and, when `reference` (else the XVEC_REFERENCE
     environment variable) names an existing reference checkout, its C kernels."""
@@ -160,6 +177,7 @@ class Oracle:
                                         ctypes.c_float, _u32p, ctypes.c_int32, _u64p, _f32p,
                                         _i32p, _i32p]
         lib.xo_fht_rotate.argtypes = [ctypes.c_int32, _u8p, _f32p, _f32p]
+        lib.xo_fht_unrotate.argtypes = [ctypes.c_int32, _u8p, _f32p, _f32p]
         lib.xo_rabitq_padded_dimension.restype = ctypes.c_int32
         lib.xo_rabitq_padded_dimension.argtypes = [ctypes.c_int32]
         lib.xo_rabitq_rotate.argtypes = [ctypes.c_int32, _u8p, _f32p, _f32p]
@@ -544,6 +562,14 @@ class Oracle:
         v = _c(v, np.float32)
         out = np.zeros_like(v)
         st = self.lib.xo_fht_rotate(v.size, _ptr(signs, _u8p), _ptr(v, _f32p), _ptr(out, _f32p))
+        return st, out
+
+    def fht_unrotate(self, signs, v):
+        signs = _c(signs, np.uint8)
+        v = _c(v, np.float32)
+        out = np.zeros_like(v)
+        st = self.lib.xo_fht_unrotate(v.size, _ptr(signs, _u8p), _ptr(v, _f32p),
+                                      _ptr(out, _f32p))
         return st, out
 
     def rabitq_padded_dimension(self, d):

@@ -1539,6 +1539,52 @@ extern "C" int xo_fht_rotate(int32_t dimension, const uint8_t* signs, const floa
   return rotate(dimension, floor_pow2(dimension), signs, in, out);
 }
 
+namespace {
+// FHTInverseKacWalk (fht.go:78-94).
+void fht_inverse_kac(float* data, int32_t n) {
+  int32_t half = n / 2, base = n % 2, off = base + half;
+  if (base != 0) data[half] *= (float)std::sqrt(0.5);
+  for (int32_t i = 0; i < half; ++i) {
+    float l = data[i], r = data[i + off];
+    data[i] = (l + r) * 0.5f;
+    data[i + off] = (l - r) * 0.5f;
+  }
+}
+}  // namespace
+
+// FHTRotator.Unrotate (rotation.go:155-185): the rounds of Rotate undone in
+// reverse order.
+extern "C" int xo_fht_unrotate(int32_t dimension, const uint8_t* signs, const float* in,
+                               float* out) {
+  if (dimension <= 0) return XO_INVALID_ARGUMENT;
+  const int32_t truncated = floor_pow2(dimension);
+  const int32_t bpr = (dimension + 7) / 8;
+  const float inv = 1.0f / (float)std::sqrt((double)(float)truncated);
+  for (int32_t i = 0; i < dimension; ++i)
+    if (!finite32(in[i])) return XO_NON_FINITE;
+  std::memcpy(out, in, sizeof(float) * dimension);
+  if (truncated == dimension) {
+    for (int r = 3; r >= 0; --r) {
+      fht_inplace(out, dimension);
+      scale(out, dimension, inv);
+      fht_flip(signs + r * bpr, out, dimension);
+    }
+  } else {
+    scale(out, dimension, 4.0f);
+    const int32_t start = dimension - truncated;
+    for (int r = 3; r >= 0; --r) {
+      fht_inverse_kac(out, dimension);
+      float* window = (r % 2 != 0) ? out + start : out;
+      fht_inplace(window, truncated);
+      scale(window, truncated, inv);
+      fht_flip(signs + r * bpr, out, dimension);
+    }
+  }
+  for (int32_t i = 0; i < dimension; ++i)
+    if (!finite32(out[i])) return XO_NON_FINITE;
+  return XO_OK;
+}
+
 // roundUpRaBitQDimension (rabitq.go:579-581).
 extern "C" int32_t xo_rabitq_padded_dimension(int32_t d) { return (d + 63) / 64 * 64; }
 

@@ -176,6 +176,8 @@ int xo_ivfpq_search(int metric, const float* centroids, int32_t nlist, int32_t d
 
 /* ---- RaBitQ (internal/core/rabitq*.go, rotation.go, ailego/math/fht.go) - */
 int xo_fht_rotate(int32_t dimension, const uint8_t* signs, const float* in, float* out);
+/* FHTRotator.Unrotate (rotation.go:155-185). */
+int xo_fht_unrotate(int32_t dimension, const uint8_t* signs, const float* in, float* out);
 int32_t xo_rabitq_padded_dimension(int32_t d);
 /* Padded rotation used by RaBitQModel (rabitq.go:555-577). */
 int xo_rabitq_rotate(int32_t d, const uint8_t* signs, const float* in, float* out);

@@ -84,7 +84,8 @@ def test_multibit_parity(oracle, xb, metric, total_bits):
 
 def test_multibit_960_tensor_core(oracle, xb):
     """d = 960 with 150 queries (CTA pairs) and 70,000 rows (the seeded
-    launches over row prefixes), TotalBits 7."""
+    launches over row prefixes), TotalBits 7: the INT8 tensor-core scan of
+    the code plane against the 16-bit integer query."""
     import xvec_b200
     rng = np.random.default_rng(960)
     d, n = 960, 70_000
@@ -100,6 +101,9 @@ def test_multibit_960_tensor_core(oracle, xb):
     case.check(xb, queries, 10, 100, refine=True)
     st1 = xvec_b200.stats()
     assert st1["tensor_scans"] > st0["tensor_scans"]
+    # The INT8 form's bound (exact integer dots, 16-bit query) is tight
+    # enough that no query needs the exact scan.
+    assert st1["exact_queries"] == st0["exact_queries"]
     case.check(xb, queries, 10, 50, refine=False)
     case.close()
 

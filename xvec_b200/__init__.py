@@ -64,6 +64,7 @@ EXPORTED_SYMBOLS = (
     "xvec_gpu_comm_destroy", "xvec_gpu_comm_abort", "xvec_gpu_comm_size", "xvec_gpu_comm_rank",
     "xvec_gpu_sharded_search_device", "xvec_gpu_sharded_search",
     "xvec_gpu_set_wait_limit_ns",
+    "xvec_gpu_rotation_signs", "xvec_gpu_rotate", "xvec_gpu_rotate_device",
 )
 
 
@@ -91,7 +92,7 @@ class Stats(ctypes.Structure):
     _fields_ = [("searches", ctypes.c_int64), ("queries", ctypes.c_int64),
                 ("kernel_launches", ctypes.c_int64), ("exact_queries", ctypes.c_int64),
                 ("scan_ms", ctypes.c_double), ("search_ms", ctypes.c_double),
-                ("tensor_scans", ctypes.c_int64)]
+                ("tensor_scans", ctypes.c_int64), ("stream_scans", ctypes.c_int64)]
 
 
 def _load() -> ctypes.CDLL:
@@ -157,6 +158,10 @@ def _load() -> ctypes.CDLL:
                                                    vp, vp, vp]
     lib.xvec_gpu_sharded_search.argtypes = [vp, vp, i32, vp, i32, ctypes.POINTER(SearchOpts), vp,
                                             vp, vp]
+    lib.xvec_gpu_rotation_signs.argtypes = [ctypes.c_char_p, ctypes.c_char_p, i32, i32, i32, vp,
+                                            i64]
+    lib.xvec_gpu_rotate.argtypes = [i32, vp, i64, i32, vp, i64, vp, i32]
+    lib.xvec_gpu_rotate_device.argtypes = [i32, vp, i64, i32, vp, i64, vp, i32, vp, vp]
     lib.xvec_gpu_set_wait_limit_ns.restype = i64
     lib.xvec_gpu_set_wait_limit_ns.argtypes = [i64]
     lib.xvec_gpu_stats_enable_timing.argtypes = [i32]
@@ -204,6 +209,50 @@ def set_wait_limit_ns(ns: int) -> int:
     """Bound of the tensor-core scans' device-side waits (xvec_gpu_set_wait_limit_ns):
     2 s by default, ns <= 0 restores it; returns the previous bound."""
     return int(_lib.xvec_gpu_set_wait_limit_ns(ns))
+
+
+def rotation_signs(schema_name: str, field_name: str, dimension: int, index_type: int,
+                   quantize: int) -> np.ndarray:
+    """collectionReformer's FHT sign state for a collection's vector field
+    (collection.go:1981-2000): 4 * ((dimension + 7) / 8) bytes."""
+    out = np.zeros(4 * ((dimension + 7) // 8), np.uint8)
+    _check(_lib.xvec_gpu_rotation_signs(schema_name.encode(), field_name.encode(), dimension,
+                                        index_type, quantize, out.ctypes.data, out.size))
+    return out
+
+
+class RotationReformer:
+    """RotationReformer (internal/core/rotation.go:248-280) over an FHT
+    rotator's sign state: transform() rotates vectors into index space,
+    revert() back, both on the GPU and bit-identical to FHTRotator."""
+
+    def __init__(self, dimension: int, signs, device: int = 0):
+        self.dimension, self.device = dimension, device
+        self.signs = np.ascontiguousarray(signs, np.uint8)
+
+    def _run(self, vectors, inverse: int) -> np.ndarray:
+        v = np.ascontiguousarray(vectors, np.float32)
+        one = v.ndim == 1
+        v = v.reshape(-1, self.dimension)
+        out = np.empty_like(v)
+        _check(_lib.xvec_gpu_rotate(self.device, self.signs.ctypes.data, self.signs.size,
+                                    self.dimension, v.ctypes.data, v.shape[0], out.ctypes.data,
+                                    inverse))
+        return out[0] if one else out
+
+    def transform(self, vectors) -> np.ndarray:
+        return self._run(vectors, 0)
+
+    def revert(self, vectors) -> np.ndarray:
+        return self._run(vectors, 1)
+
+    def transform_device(self, d_vectors: int, n: int, d_out: int, d_failed: int,
+                         inverse: bool = False, stream: int = 0) -> None:
+        """Device form (xvec_gpu_rotate_device): enqueued on `stream`;
+        d_failed (n int32) flags vectors whose input or result is not finite."""
+        _check(_lib.xvec_gpu_rotate_device(self.device, self.signs.ctypes.data, self.signs.size,
+                                           self.dimension, d_vectors, n, d_out, 1 if inverse else 0,
+                                           d_failed, stream or None))
 
 
 def device_count() -> int:

@@ -299,8 +299,10 @@ xvec_gpu_status flat_search_impl(xvec_gpu_index* idx, const void* d_q, int nq,
   // (kept beside them) and of the queries.
   constexpr bool kSplit = std::is_same<RowT, float>::value;
   Scratch qhi, qlo;
-  const bool tc_layout = n > 0 && n < (1ll << 31) - 256 && kp + 128 <= flat_tc_cap() &&
-                         d % 8 == 0 && d >= 64;
+  // A few queries: the streaming scan (one pass over the rows at HBM speed).
+  const bool use_stream = flat_stream_supported<RowT>(nq, n, d, kp, rows, d_q);
+  const bool tc_layout = !use_stream && n > 0 && n < (1ll << 31) - 256 &&
+                         kp + 128 <= flat_tc_cap() && d % 8 == 0 && d >= 64;
   if (kSplit && tc_layout) {
     if ((st = qhi.alloc((size_t)nq * d * 2, s)) || (st = qlo.alloc((size_t)nq * d * 2, s)))
       return st;
@@ -312,8 +314,30 @@ xvec_gpu_status flat_search_impl(xvec_gpu_index* idx, const void* d_q, int nq,
       tc_layout && (kSplit ? flat_tc_supported(d, idx->rows_bhi.ptr, qhi.ptr) &&
                                  flat_tc_supported(d, idx->rows_blo.ptr, qlo.ptr)
                            : flat_tc_supported(d, rows, d_q));
-  const bool fast = use_tc || (simt_cap_for(kp) <= 512 && n > 0);
-  if (use_tc) {
+  const bool fast = use_stream || use_tc || (simt_cap_for(kp) <= 512 && n > 0);
+  if (use_stream) {
+    if (is_cancelled(o)) return set_error("cancelled"), XVEC_GPU_CANCELLED;
+    Scratch lkeys, lcounts, lsat;
+    timer.mark(1);
+    if ((st = flat_stream_scan<RowT>(idx->device, rows, n, d, idx->row_n2.as<float>(),
+                                     idx->keyrank.as<uint32_t>(), qf.as<float>(), qn2.as<float>(),
+                                     nq, metric, d_bitmap, kp, s, lkeys, lcounts, lsat,
+                                     qflags.as<int>())))
+      return st;
+    timer.mark(2);
+    count_stream_scan();
+    if (is_cancelled(o)) return set_error("cancelled"), XVEC_GPU_CANCELLED;
+    const int lstride = flat_stream_list_stride(kp);
+    if ((st = run_band(lkeys.as<uint64_t>(), lcounts.as<int>(), 1, lstride, nullptr, 0)))
+      return st;
+    XVEC_CUDA(launch_flat_merge_rescore<RowT>(
+        rows, d, idx->pos_of_kr.as<uint32_t>(), idx->keys.as<uint64_t>(), qf.as<float>(),
+        qn2.as<float>(), idx->max_n2.as<unsigned>(), nullptr, nq, metric, k, o.radius, 0,
+        lkeys.as<uint64_t>(), lcounts.as<int>(), lsat.as<uint64_t>(), 1, lstride, d_keys_out,
+        d_scores_out, d_counts_out, qflags.as<int>(), s, 0, nullptr,
+        band ? band_limit.as<float>() : nullptr));
+    XVEC_LAUNCHED();
+  } else if (use_tc) {
     if (is_cancelled(o)) return set_error("cancelled"), XVEC_GPU_CANCELLED;
     const int cap = flat_tc_cap();
     const float* row_aux =

@@ -22,6 +22,7 @@ void set_error(const char* fmt, ...);
 // Library counters (xvec_gpu_get_stats).
 void count_launches(int64_t n);
 void count_tensor_scan();
+void count_stream_scan();
 void count_search(int64_t queries, int64_t exact_queries, double scan_ms, double search_ms);
 bool timing_enabled();
 #define XVEC_LAUNCHED() ::xvec::count_launches(1)
@@ -124,6 +125,21 @@ using TcScanLaunch = std::function<cudaError_t(int64_t b, int64_t e, int parts, 
 xvec_gpu_status tc_seeded_scan(int device, int nq, int64_t n, int kp, cudaStream_t s,
                                const TcScanLaunch& scan, Scratch& pkeys, Scratch& pcounts,
                                Scratch& psat, int* lists_out, Scratch* gthr_out = nullptr);
+
+// Streaming Flat candidate scan for a few queries (flat_stream.cu): a sample
+// pass over every 64th row for the starting thresholds, the pass over all
+// rows, and one candidate list per query (lkeys [nq][flat_stream_list_stride(kp)],
+// lcounts [nq], lsat [nq]) for the merge.
+int flat_stream_max_batch();
+int flat_stream_list_stride(int kp);
+template <typename RowT>
+bool flat_stream_supported(int nq, int64_t n, int d, int kp, const void* rows, const void* q);
+template <typename RowT>
+xvec_gpu_status flat_stream_scan(int device, const RowT* rows, int64_t n, int d,
+                                 const float* row_n2, const uint32_t* keyrank, const float* qf,
+                                 const float* q_n2, int nq, int metric, const uint32_t* bitmap,
+                                 int kp, cudaStream_t s, Scratch& lkeys, Scratch& lcounts,
+                                 Scratch& lsat, int* q_flags);
 
 // A sharded search's exchange of per-query fast-rank bands (comm.cu): set by
 // the sharded search for one shard's Flat search, which calls it once
@@ -234,6 +250,9 @@ struct xvec_gpu_index {
   int32_t rq_total_bits = 1;
   double rq_extra_scale = 0.0;
   xvec::DeviceBuffer rq_values;
+  // TotalBits 2..8: the code values again as int8 v - 128 [n][padded] (the
+  // INT8 tensor-core operand); rq_fast's w slot holds 128 sum(v - 128).
+  xvec::DeviceBuffer rq_vplane;
   // Flat FP32: the rows as bfloat16 high and low parts (the tensor-core
   // scan's operands; the float32 rows stay the reference data).
   xvec::DeviceBuffer rows_bhi;              // bf16 [n][d]

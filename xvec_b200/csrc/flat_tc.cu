@@ -69,6 +69,13 @@ constexpr int kModeSplit = 64;
 // exact up to 256) against the query's bfloat16 high and low parts, two MMAs
 // per k-step into one fp32 accumulator; the RaBitQ epilogue on the float dot.
 constexpr int kModeRaBitQFull = 128;
+// kModeRaBitQ8: multi-bit RaBitQ on kind::i8, the rows' code values as the
+// int8 plane v - 128 against the query as 16-bit integers w = round(q / s)
+// split into two int8 planes, w = 256 h + l + 128 (h, l signed): two MMAs per
+// k-step into two exact int32 accumulators of 128 columns (A_h, A_l), tiles
+// of 128 rows; the epilogue forms sum(v w) = 256 A_h + A_l + 128 sum(v - 128)
+// (a per-row term) + 128 sum(w) (folded into the query's terms).
+constexpr int kModeRaBitQ8 = 256;
 constexpr int kRaBitQMaxClusters = 16;
 // Per epilogue warp: radix histogram (1 KB) + the current tile's row
 // metadata for its 128 columns (aux floats + key ranks, 1 KB; SQ8/RaBitQ: the
@@ -79,10 +86,10 @@ constexpr uint32_t epi_smem_bytes(bool rq) {
 }
 constexpr uint32_t kSmemBudget = 232448 - 1024 - 1024 - 512;  // dynamic bytes for stages
 
-template <bool PAIR, bool RQ = false, bool SPLIT = false, bool SPLITA = false>
+template <bool PAIR, bool RQ = false, bool SPLIT = false, bool SPLITA = false, int BN = kBN>
 struct Shape {
-  static constexpr int kRowsPerCta = PAIR ? kBN / 2 : kBN;       // B rows loaded per CTA
-  static constexpr uint32_t kTileBBytes = kRowsPerCta * kBK * 2;  // 16 or 32 KB
+  static constexpr int kRowsPerCta = PAIR ? BN / 2 : BN;          // B rows loaded per CTA
+  static constexpr uint32_t kTileBBytes = kRowsPerCta * kBK * 2;  // 8, 16 or 32 KB
   static constexpr int kParts = SPLIT ? 2 : 1;                    // high (+ low) tiles
   // SPLITA: A high, B, A low.
   static constexpr uint32_t kStageBytes =
@@ -228,24 +235,24 @@ __device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b
   }
 }
 
-// kind::i8: A/B signed 8-bit, D = S32.
-template <int M>
+// kind::i8: A/B signed 8-bit, D = S32, N columns.
+template <int M, int N = kBN>
 constexpr uint32_t idesc_s8() {
-  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kBN >> 3) << 17) |
+  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) |
          ((uint32_t)(M >> 4) << 24);
 }
-template <bool PAIR>
+template <bool PAIR, int N = kBN>
 __device__ __forceinline__ void mma_s8(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t acc) {
   if constexpr (PAIR) {
     asm volatile(
         "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
         "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
-        "l"(a), "l"(b), "r"(idesc_s8<2 * kBM>()), "r"(acc));
+        "l"(a), "l"(b), "r"(idesc_s8<2 * kBM, N>()), "r"(acc));
   } else {
     asm volatile(
         "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
         "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
-        "l"(a), "l"(b), "r"(idesc_s8<kBM>()), "r"(acc));
+        "l"(a), "l"(b), "r"(idesc_s8<kBM, N>()), "r"(acc));
   }
 }
 
@@ -424,13 +431,19 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
     int* __restrict__ status, uint64_t wait_ns) {
   constexpr bool RQ1 = MODE == kModeRaBitQ;   // RaBitQ code planes, integer queries
   constexpr bool RQF = MODE == kModeRaBitQFull;  // multi-bit values, bfloat16 query parts
-  constexpr bool RQ = RQ1 || RQF;                // the RaBitQ epilogue
-  constexpr bool SQ = (MODE & kModeSq8) != 0;   // INT8 codes (SQ8) instead of FP16 rows
-  constexpr bool SPLIT = (MODE & kModeSplit) != 0;  // bfloat16 high/low parts of float32
-  constexpr bool I8 = SQ || RQ1;                // kind::i8 operands
-  constexpr int METRIC = MODE & 15;
+  constexpr bool RQ8 = MODE == kModeRaBitQ8;     // multi-bit values, 16-bit integer query
+  constexpr bool RQ = RQ1 || RQF || RQ8;         // the RaBitQ epilogue
+  constexpr bool SQ = (MODE & kModeSq8) != 0 && !RQ8;  // INT8 codes (SQ8) instead of FP16 rows
+  constexpr bool SPLIT = (MODE & kModeSplit) != 0 && !RQ8;  // bfloat16 high/low parts of float32
+  constexpr bool I8 = SQ || RQ1 || RQ8;         // kind::i8 operands
+  constexpr bool TWO_A = RQF || RQ8;            // stage: A, B, second A
+  constexpr int METRIC = RQ8 ? 0 : (MODE & 15);
   constexpr int kElemBytes = I8 ? 1 : 2;
-  using S = Shape<PAIR, RQ, SPLIT, RQF>;
+  // Rows per tile: RQ8 keeps two accumulators of BN columns per buffer.
+  constexpr int BN = RQ8 ? kBN / 2 : kBN;
+  constexpr int kHalfCols = BN / 2;         // columns per epilogue warp
+  constexpr int kChunks = kHalfCols / 32;   // 32-column chunks per epilogue warp
+  using S = Shape<PAIR, RQ, SPLIT, TWO_A, BN>;
   constexpr int kStages = S::kStages;
   constexpr uint32_t kStageBytes = S::kStageBytes;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -459,7 +472,7 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
   const int part = blockIdx.y;
   const int64_t row_begin = (int64_t)part * rows_per_part;
   const int64_t row_end = min(n, row_begin + rows_per_part);
-  const int num_tiles = row_end > row_begin ? (int)((row_end - row_begin + kBN - 1) / kBN) : 0;
+  const int num_tiles = row_end > row_begin ? (int)((row_end - row_begin + BN - 1) / BN) : 0;
   // k-steps of 128 bytes (kBK FP16 or 2 kBK INT8 elements).
   const int ksteps = (d * kElemBytes + 127) / 128;
   constexpr int kStepElems = 128 / kElemBytes;
@@ -508,7 +521,7 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
 #pragma unroll
       for (int s2 = 0; s2 < kStages; ++s2) count[s2] = 0;
       for (int t = 0; t < num_tiles && !*s_abort; ++t) {
-        const int row0 = (int)(row_begin + (int64_t)t * kBN) + (int)rank * S::kRowsPerCta;
+        const int row0 = (int)(row_begin + (int64_t)t * BN) + (int)rank * S::kRowsPerCta;
         for (int ks = 0; ks < ksteps; ++ks) {
           if (!mbar_wait(&empty[stage], phase ^ 1, s_abort, wait_ns)) {
             atomicExch(status, 1);
@@ -528,7 +541,7 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
               tma_load_2d_pair(&qmap2, full0 + stage * 8, a2_dst, ks * kStepElems, qblock * kBM);
               tma_load_2d_pair(&rmap2, full0 + stage * 8, b2_dst, ks * kStepElems, row0);
             }
-            if constexpr (RQF)
+            if constexpr (TWO_A)
               tma_load_2d_pair(&qmap2, full0 + stage * 8, a2_dst, ks * kStepElems, qblock * kBM);
           } else {
             tma_load_2d(&qmap, &full[stage], a_dst, ks * kStepElems, qblock * kBM);
@@ -537,7 +550,7 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
               tma_load_2d(&qmap2, &full[stage], a2_dst, ks * kStepElems, qblock * kBM);
               tma_load_2d(&rmap2, &full[stage], b2_dst, ks * kStepElems, row0);
             }
-            if constexpr (RQF)
+            if constexpr (TWO_A)
               tma_load_2d(&qmap2, &full[stage], a2_dst, ks * kStepElems, qblock * kBM);
           }
           ++count[stage];
@@ -582,7 +595,10 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
           const uint64_t bdesc = smem_desc_sw128(a_src + kTileABytes);
 #pragma unroll
           for (int k = 0; k < 4; ++k) {  // 32 bytes of K per MMA (16 FP16 or 32 INT8)
-            if constexpr (I8)
+            if constexpr (RQ8)
+              mma_s8<PAIR, BN>(d_tmem, adesc + (uint64_t)(k * 2), bdesc + (uint64_t)(k * 2),
+                               (ks > 0 || k > 0) ? 1u : 0u);
+            else if constexpr (I8)
               mma_s8<PAIR>(d_tmem, adesc + (uint64_t)(k * 2), bdesc + (uint64_t)(k * 2),
                            (ks > 0 || k > 0) ? 1u : 0u);
             else if constexpr (SPLIT || RQF)
@@ -591,6 +607,15 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
             else
               mma_f16<PAIR>(d_tmem, adesc + (uint64_t)(k * 2), bdesc + (uint64_t)(k * 2),
                             (ks > 0 || k > 0) ? 1u : 0u);
+          }
+          if constexpr (RQ8) {
+            // The low query plane against the same rows, into the second
+            // accumulator (BN columns further).
+            const uint64_t a2desc = smem_desc_sw128(a_src + kTileABytes + S::kTileBBytes);
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              mma_s8<PAIR, BN>(d_tmem + BN, a2desc + (uint64_t)(k * 2), bdesc + (uint64_t)(k * 2),
+                               (ks > 0 || k > 0) ? 1u : 0u);
           }
           if constexpr (RQF) {
             // The low query part against the same row values.
@@ -668,13 +693,13 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
     // Row metadata (aux, key rank, filter) of this warp's 128 columns is
     // loaded one tile ahead into registers and staged in shared memory, so
     // neither the scoring loop nor the append path waits on global memory.
-    float pf_aux[4];
-    float4 pf4[(SQ || RQ) ? 4 : 1];
-    uint32_t pf_kr[4], pf_vm[4];
+    float pf_aux[kChunks];
+    float4 pf4[(SQ || RQ) ? kChunks : 1];
+    uint32_t pf_kr[kChunks], pf_vm[kChunks];
     auto prefetch = [&](int t) {
-      const int64_t base = row_begin + (int64_t)t * kBN + half * 128;
+      const int64_t base = row_begin + (int64_t)t * BN + half * kHalfCols;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < kChunks; ++c) {
         const int64_t row = base + c * 32 + lane;
         const bool ok = t < num_tiles && row < row_end && bitmap_pass(bitmap, row);
         if constexpr (SQ || RQ) {
@@ -697,10 +722,10 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
     for (int t = 0; t < num_tiles; ++t) {
       const int acc = t & 1;
       const uint32_t acc_phase = (t >> 1) & 1;
-      uint32_t vm[4];
+      uint32_t vm[kChunks];
       __syncwarp();
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < kChunks; ++c) {
         meta_aux[c * 32 + lane] = pf_aux[c];
         if constexpr (SQ || RQ) meta4[c * 32 + lane] = pf4[c];
         meta_kr[c * 32 + lane] = pf_kr[c];
@@ -721,8 +746,39 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
         break;
       }
       tmem_fence_after();
-      const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * kBN + half * 128;
+      const uint32_t taddr =
+          tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * kBN + half * kHalfCols;
       uint32_t va[32], vb[32];
+      if constexpr (RQ8) {
+        // The 64 columns of this warp: A_h (va) and A_l (vb, BN columns on)
+        // of 32 rows at a time.
+#pragma unroll 1
+        for (int c = 0; c < kChunks; ++c) {
+          tmem_ld32(taddr + c * 32, va);
+          tmem_ld32(taddr + BN + c * 32, vb);
+          tmem_wait_ld();
+          const uint32_t vmask = qvalid ? vm[c] : 0u;
+          if (vmask != 0u) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float4 r = meta4[c * 32 + j];
+              const float g = gadd_tab[__float_as_int(r.z) * 32 + lane];
+              // sum(v' w) + 128 sum(v') of this row; the query's 128 sum(w)
+              // is folded into rq_q.x.
+              const float dp = fmaf(256.f, (float)(int)va[j], (float)(int)vb[j]) + r.w;
+              const float rank = fmaf(r.y, fmaf(rq_q.y, dp, -rq_q.x), r.x + g);
+              if (((vmask >> j) & 1u) && !(rank > thr_f)) {
+                if (!isfinite(rank)) {
+                  nonfinite = 1;
+                } else {
+                  const uint64_t key = pack_rank(rank, meta_kr[c * 32 + j]);
+                  if (key < thr) gbuf[cnt++] = key;
+                }
+              }
+            }
+          }
+        }
+      } else {
       tmem_ld32(taddr, va);
       tmem_wait_ld();
 #pragma unroll
@@ -815,6 +871,7 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
         }
         if (c + 1 < 4) tmem_wait_ld();
       }
+      }  // !RQ8
       // Release the accumulator to the MMA warp before any compaction (one
       // arrival per warp, on the issuing CTA's barrier).
       tmem_fence_before();
@@ -962,9 +1019,14 @@ cudaError_t launch_tc(int nq, const void* queries, const void* queries2, int nc,
   const int qblocks = (nq + tc::kBM - 1) / tc::kBM;
   const bool pair = flat_tc_pairs(nq);
   constexpr bool RQF = MODE == tc::kModeRaBitQFull;
-  constexpr bool RQ = MODE == tc::kModeRaBitQ || RQF;
-  constexpr bool SPLIT = (MODE & tc::kModeSplit) != 0;
-  const int box_rows = pair ? tc::Shape<true>::kRowsPerCta : tc::Shape<false>::kRowsPerCta;
+  constexpr bool RQ8 = MODE == tc::kModeRaBitQ8;
+  constexpr bool RQ = MODE == tc::kModeRaBitQ || RQF || RQ8;
+  constexpr bool SPLIT = (MODE & tc::kModeSplit) != 0 && !RQ8;
+  constexpr bool TWO_A = RQF || RQ8;
+  constexpr int BN = RQ8 ? tc::kBN / 2 : tc::kBN;
+  using SP = tc::Shape<true, RQ, SPLIT, TWO_A, BN>;
+  using SS = tc::Shape<false, RQ, SPLIT, TWO_A, BN>;
+  const int box_rows = pair ? SP::kRowsPerCta : SS::kRowsPerCta;
   // The low parts' maps (unused unless SPLIT) repeat the high parts'.
   CUtensorMap qmap, rmap, qmap2, rmap2;
   if (!make_map(&qmap, queries, nq, d, d, tc::kBM, elem_bytes) ||
@@ -987,17 +1049,15 @@ cudaError_t launch_tc(int nq, const void* queries, const void* queries2, int nc,
   cudaError_t err;
   if (pair) {
     auto kern = tc::flat_scan_tc_kernel<MODE, true>;
-    cfg.dynamicSmemBytes = tc::Shape<true, RQ, SPLIT, RQF>::kSmemBytes;
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)tc::Shape<true, RQ, SPLIT, RQF>::kSmemBytes);
+    cfg.dynamicSmemBytes = SP::kSmemBytes;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SP::kSmemBytes);
     err = cudaLaunchKernelEx(&cfg, kern, qmap, rmap, qmap2, rmap2, nc, nq, n, d, row_aux, keyrank, q_aux,
                              q_n2, gthr, bitmap, rows_per_part, kp, list_base, num_lists, cand,
                              part_counts, part_sat, q_flags, status, tc_wait_ns());
   } else {
     auto kern = tc::flat_scan_tc_kernel<MODE, false>;
-    cfg.dynamicSmemBytes = tc::Shape<false, RQ, SPLIT, RQF>::kSmemBytes;
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)tc::Shape<false, RQ, SPLIT, RQF>::kSmemBytes);
+    cfg.dynamicSmemBytes = SS::kSmemBytes;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SS::kSmemBytes);
     err = cudaLaunchKernelEx(&cfg, kern, qmap, rmap, qmap2, rmap2, nc, nq, n, d, row_aux, keyrank, q_aux,
                              q_n2, gthr, bitmap, rows_per_part, kp, list_base, num_lists, cand,
                              part_counts, part_sat, q_flags, status, tc_wait_ns());
@@ -1125,6 +1185,31 @@ cudaError_t launch_rabitq_full_scan_tc(const __nv_bfloat16* q_hi, const __nv_bfl
                                         reinterpret_cast<const float*>(q_terms), q_gadd, gthr,
                                         bitmap, num_parts, kp, list_base, num_lists, cand,
                                         part_counts, part_sat, q_flags, status, stream);
+}
+
+cudaError_t launch_rabitq8_scan_tc(const int8_t* q_planes, int nq, const int8_t* vplane,
+                                   int64_t n, int padded, const float4* row_info,
+                                   const uint32_t* keyrank, const float2* q_terms,
+                                   const float* q_gadd, int nc, unsigned long long* gthr,
+                                   const uint32_t* bitmap, int num_parts, int kp, int list_base,
+                                   int num_lists, uint64_t* cand, int* part_counts,
+                                   uint64_t* part_sat, int* q_flags, int* status,
+                                   cudaStream_t stream) {
+  if (nc > tc::kRaBitQMaxClusters || !rabitq8_tc_supported(padded, vplane, q_planes))
+    return cudaErrorInvalidValue;
+  return launch_tc<tc::kModeRaBitQ8>(nq, q_planes, q_planes + (int64_t)nq * padded, nc, vplane,
+                                     nullptr, n, padded, (int64_t)padded, 1,
+                                     reinterpret_cast<const float*>(row_info), keyrank,
+                                     reinterpret_cast<const float*>(q_terms), q_gadd, gthr,
+                                     bitmap, num_parts, kp, list_base, num_lists, cand,
+                                     part_counts, part_sat, q_flags, status, stream);
+}
+
+bool rabitq8_tc_supported(int padded, const void* vplane, const void* q_planes) {
+  // Rows of padded bytes in 128-byte k-steps; |A_h|, |A_l| <= 2^14 padded.
+  return padded % 64 == 0 && padded >= 64 && padded <= 65536 &&
+         ((uintptr_t)vplane % 16 == 0) && ((uintptr_t)q_planes % 16 == 0) &&
+         encode_fn() != nullptr;
 }
 
 int rabitq_tc_max_clusters() { return tc::kRaBitQMaxClusters; }

@@ -77,6 +77,23 @@ cudaError_t launch_rabitq_scan_tc(const int8_t* q_int, int nq, const int8_t* pla
                                   int num_parts, int kp, int list_base, int num_lists,
                                   uint64_t* cand, int* part_counts, uint64_t* part_sat,
                                   int* q_flags, int* status, cudaStream_t stream);
+// Multi-bit RaBitQ (TotalBits <= 8) on INT8 tensor cores: rows = the code
+// values as the int8 plane v - 128 [n][padded]; queries = 16-bit integers
+// w = round(rotated query / scale) as two int8 planes, q_planes [2][nq][padded]
+// (h, then l, w = 256 h + l + 128), so two exact int32 accumulators give
+// sum(v w) = 256 A_h + A_l + 128 sum(v - 128) + 128 sum(w).  row_info:
+// {full add, full rescale, cluster bits, 128 sum(v - 128)}; q_terms:
+// {-(center sum) - scale 128 sum(w), scale}; ranked with the multi-bit fast
+// estimate.  Lists, thresholds and status as for launch_flat_scan_tc.
+cudaError_t launch_rabitq8_scan_tc(const int8_t* q_planes, int nq, const int8_t* vplane,
+                                   int64_t n, int padded, const float4* row_info,
+                                   const uint32_t* keyrank, const float2* q_terms,
+                                   const float* q_gadd, int nc, unsigned long long* gthr,
+                                   const uint32_t* bitmap, int num_parts, int kp, int list_base,
+                                   int num_lists, uint64_t* cand, int* part_counts,
+                                   uint64_t* part_sat, int* q_flags, int* status,
+                                   cudaStream_t stream);
+bool rabitq8_tc_supported(int padded, const void* vplane, const void* q_planes);
 // Multi-bit RaBitQ: the rows' full code values as bfloat16 [n][padded]
 // against the query's bfloat16 high and low parts ([nq][padded] each);
 // q_terms[q].x = -(center sum) (float), the fast rank fmaf(rescale, dot -

@@ -12,7 +12,8 @@
 namespace xvec {
 
 namespace {
-std::atomic<int64_t> g_searches{0}, g_queries{0}, g_launches{0}, g_exact{0}, g_tensor{0};
+std::atomic<int64_t> g_searches{0}, g_queries{0}, g_launches{0}, g_exact{0}, g_tensor{0},
+    g_stream{0};
 std::mutex g_ms_mu;
 double g_scan_ms = 0, g_search_ms = 0;
 std::atomic<int> g_timing{0};
@@ -20,6 +21,7 @@ std::atomic<int> g_timing{0};
 
 void count_launches(int64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 void count_tensor_scan() { g_tensor.fetch_add(1); }
+void count_stream_scan() { g_stream.fetch_add(1); }
 thread_local int g_nested = 0;
 void nested_search_enter() { ++g_nested; }
 void nested_search_leave() { --g_nested; }
@@ -153,6 +155,7 @@ extern "C" void xvec_gpu_get_stats(xvec_gpu_stats* out) {
   out->kernel_launches = g_launches.load();
   out->exact_queries = g_exact.load();
   out->tensor_scans = g_tensor.load();
+  out->stream_scans = g_stream.load();
   std::lock_guard<std::mutex> lock(g_ms_mu);
   out->scan_ms = g_scan_ms;
   out->search_ms = g_search_ms;
@@ -164,6 +167,7 @@ extern "C" void xvec_gpu_reset_stats(void) {
   g_launches = 0;
   g_exact = 0;
   g_tensor = 0;
+  g_stream = 0;
   std::lock_guard<std::mutex> lock(g_ms_mu);
   g_scan_ms = 0;
   g_search_ms = 0;

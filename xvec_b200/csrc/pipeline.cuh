@@ -24,6 +24,8 @@
 //          bool keep(float out, float radius) -- the radius rule on that score.
 #pragma once
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "select.cuh"
 
@@ -538,6 +540,79 @@ __global__ void __launch_bounds__(256) band_prepare_kernel(
   __syncthreads();
   for (int i = s_n + threadIdx.x; i < k; i += blockDim.x) dst[i] = INFINITY;
   if (threadIdx.x == 0) dst[k] = sc.eps(q);
+}
+
+// Per query, the lists of one scan (num_parts lists of at most kp keys, as
+// the streaming scans write them): their union's best keys.
+// Threshold mode (gthr_out): the kp-th best key becomes the query's starting
+// threshold for a later pass (left at all-ones when the lists hold fewer
+// than kp keys).  List mode: the best out_cap keys (out_cap >= kp) become the
+// query's one candidate list (out_*, stride out_cap), its saturation the
+// lowest of the lists' and, when keys were left out here, the out_cap-th
+// key.  Keeping several kp keeps that saturation well above the candidate
+// limit F_k + 2 eps even where the distances of the nearest rows crowd
+// together.
+static __global__ void __launch_bounds__(1024) reduce_lists_kernel(
+    const uint64_t* __restrict__ keys, const int* __restrict__ counts,
+    const uint64_t* __restrict__ sats, int num_parts, int kp, int out_cap,
+    unsigned long long* __restrict__ gthr_out, uint64_t* __restrict__ out_keys,
+    int* __restrict__ out_counts, uint64_t* __restrict__ out_sat) {
+  extern __shared__ __align__(16) unsigned char reduce_smem[];
+  uint64_t* ukeys = reinterpret_cast<uint64_t*>(reduce_smem);  // [num_parts * kp]
+  __shared__ int hist[256];
+  __shared__ unsigned long long s_sat;
+  __shared__ int s_n;
+  const int q = blockIdx.x;
+  const int64_t pbase = (int64_t)q * num_parts;
+  if (threadIdx.x == 0) {
+    s_sat = kEmptyKey;
+    s_n = 0;
+  }
+  const int total =
+      gather_union(keys, counts, pbase, num_parts, kp, kEmptyKey, ukeys, num_parts * kp);
+  for (int p = threadIdx.x; p < num_parts; p += blockDim.x)
+    atomicMin(&s_sat, (unsigned long long)sats[pbase + p]);
+  __syncthreads();
+  const int m = min(total, num_parts * kp);
+  if (gthr_out) {
+    if (m >= kp) {
+      const uint64_t kth = smem_radix_select(ukeys, m, kp, 0, hist);
+      if (threadIdx.x == 0) gthr_out[q] = kth;
+    }
+    return;
+  }
+  uint64_t cut = kEmptyKey;
+  if (m > out_cap) cut = smem_radix_select(ukeys, m, out_cap, 0, hist);
+  for (int i = threadIdx.x; i < m; i += blockDim.x)
+    if (ukeys[i] <= cut) out_keys[(int64_t)q * out_cap + atomicAdd(&s_n, 1)] = ukeys[i];
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    out_counts[q] = s_n;
+    out_sat[q] = min((uint64_t)s_sat, cut);
+  }
+}
+
+static inline bool reduce_lists_supported(int num_parts, int kp) {
+  return (int64_t)num_parts * kp * 8 <= 200 * 1024;
+}
+
+// One block of 1024 threads per query (reduce_lists_kernel).
+// Candidate list length of the list mode: eight kp, within the merge's
+// shared buffer.
+static inline int reduce_lists_out_cap(int kp) { return std::min(8 * kp, kMergeSmemEntries); }
+
+static inline cudaError_t launch_reduce_lists(const uint64_t* keys, const int* counts,
+                                              const uint64_t* sats, int nq, int num_parts,
+                                              int kp, int out_cap, unsigned long long* gthr_out,
+                                              uint64_t* out_keys, int* out_counts,
+                                              uint64_t* out_sat, cudaStream_t stream) {
+  if (nq <= 0) return cudaSuccess;
+  if (!reduce_lists_supported(num_parts, kp) || out_cap < kp) return cudaErrorInvalidValue;
+  const int smem = num_parts * kp * 8;
+  cudaFuncSetAttribute(reduce_lists_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  reduce_lists_kernel<<<nq, 1024, smem, stream>>>(keys, counts, sats, num_parts, kp, out_cap,
+                                                  gthr_out, out_keys, out_counts, out_sat);
+  return cudaGetLastError();
 }
 
 template <typename RowT, typename Ranker>

@@ -34,6 +34,7 @@
 #include "capi_internal.h"
 #include "common.cuh"
 #include "flat_kernels.cuh"
+#include "fht.cuh"
 #include "flat_tc.cuh"
 #include "index_kernels.cuh"
 #include "pipeline.cuh"
@@ -108,64 +109,13 @@ __device__ void block_normalize(float* v, int d) {
   __syncthreads();
 }
 
-// FHTInPlace (fht.go:41-57) on data[0, n), n a power of two.
-__device__ void block_fht(float* data, int n) {
-  for (int w = 1; w < n; w <<= 1) {
-    for (int t = threadIdx.x; t < n / 2; t += blockDim.x) {
-      const int idx = (t / w) * 2 * w + (t % w);
-      const float l = data[idx], r = data[idx + w];
-      data[idx] = __fadd_rn(l, r);
-      data[idx + w] = __fsub_rn(l, r);
-    }
-    __syncthreads();
-  }
-}
-
-// FHTRotator.Rotate (rotation.go:123-153) of a padded vector in shared memory.
-__device__ void block_rotate(float* v, int padded, int truncated, const uint8_t* signs, float inv) {
-  const int bpr = padded / 8;
-  auto flip = [&](const uint8_t* sg) {
-    for (int i = threadIdx.x; i < padded; i += blockDim.x)
-      if (sg[i >> 3] & (1u << (i & 7))) v[i] = -v[i];
-    __syncthreads();
-  };
-  auto scale = [&](float* w, int n, float f) {
-    for (int i = threadIdx.x; i < n; i += blockDim.x) w[i] = __fmul_rn(w[i], f);
-    __syncthreads();
-  };
-  if (truncated == padded) {
-    for (int r = 0; r < 4; ++r) {
-      flip(signs + r * bpr);
-      block_fht(v, padded);
-      scale(v, padded, inv);
-    }
-    return;
-  }
-  const int start = padded - truncated;
-  for (int r = 0; r < 4; ++r) {
-    flip(signs + r * bpr);
-    float* window = (r % 2 != 0) ? v + start : v;
-    block_fht(window, truncated);
-    scale(window, truncated, inv);
-    // FHTKacWalk (fht.go:59-76); padded is even, so there is no middle term.
-    const int half = padded / 2;
-    for (int t = threadIdx.x; t < half; t += blockDim.x) {
-      const float l = v[t], rr = v[t + half];
-      v[t] = __fadd_rn(l, rr);
-      v[t + half] = __fsub_rn(l, rr);
-    }
-    __syncthreads();
-  }
-  scale(v, padded, 0.25f);
-}
-
 // Loads v (d floats) zero-padded to `padded`, optionally normalises, rotates.
 __device__ bool block_prepare_rotate(const float* src, int d, int padded, int truncated,
                                      const uint8_t* signs, float inv, bool normalize, float* v) {
   for (int i = threadIdx.x; i < padded; i += blockDim.x) v[i] = i < d ? src[i] : 0.f;
   __syncthreads();
   if (normalize) block_normalize(v, d);
-  block_rotate(v, padded, truncated, signs, inv);
+  block_fht_rotate(v, padded, truncated, signs, inv);  // FHTRotator.Rotate
   __shared__ int s_bad;
   if (threadIdx.x == 0) s_bad = 0;
   __syncthreads();
@@ -387,6 +337,34 @@ __global__ void rabitq_planes_kernel(const uint8_t* __restrict__ codes, int64_t 
   *reinterpret_cast<uint2*>(row + padded + col) = make_uint2(lo, hi);
 }
 
+// Multi-bit code values (TotalBits <= 8, bfloat16, exact) as the INT8
+// tensor-core operand v - 128, and the row's 128 sum(v - 128) into the w slot
+// of its fast terms (one warp per row).
+__global__ void rabitq_vplane_kernel(const uint16_t* __restrict__ values, int64_t m, int padded,
+                                     int8_t* __restrict__ plane, float4* __restrict__ fast) {
+  const int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (r >= m) return;
+  int sum = 0;
+  for (int i = lane; i < padded; i += 32) {
+    const int v = (int)__bfloat162float(__ushort_as_bfloat16(values[r * padded + i]));
+    plane[r * padded + i] = (int8_t)(v - 128);
+    sum += v - 128;
+  }
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(kFullMask, sum, o);
+  if (lane == 0) fast[r].w = 128.f * (float)sum;
+}
+
+// Estimate's center, -(2^(TotalBits-1) - 1/2).
+__device__ __forceinline__ double center_of(int total_bits) {
+  return -(ldexp(1.0, total_bits - 1) - 0.5);
+}
+
+// The query of the multi-bit INT8 scan: w = round(v / scale) with
+// |w| <= 32767 (scale = max |v| / 32767), as w = 256 h + l + 128 with h, l
+// signed bytes.
+constexpr int kRaBitQInt16Max = 32767;
+
 // The query as the integers of the tensor-core scan: w = round(v / scale)
 // with |w| <= kRaBitQIntMax, written as w = 127 h + l (|h| <= 127, |l| <= 63).
 constexpr int kRaBitQIntMax = 127 * 127 + 63;
@@ -405,11 +383,14 @@ __global__ void rabitq_prep_query_kernel(const float* queries, int nq, int d, in
                                          float* q_fast_sum, float* q_fast_gadd, float* q_eps,
                                          int* q_exact, int* q_status, int* q_flags,
                                          int8_t* q_int, float2* q_terms, int total_bits,
-                                         __nv_bfloat16* q_bf) {
+                                         __nv_bfloat16* q_bf, int8_t* q_planes8) {
   // total_bits > 1: q_bf holds the rotated queries' bfloat16 high parts
   // [nq][padded] followed by their low parts [nq][padded] (the multi-bit
-  // tensor-core operands) and q_int is unused.
+  // FFMA scan's input) and q_int is unused.  q_planes8 (optional, the
+  // multi-bit INT8 tensor-core scan): the 16-bit integer query as planes
+  // [2][nq][padded] (h, then l); q_terms and q_eps then follow that form.
   const bool multi = total_bits > 1;
+  const bool int8_form = multi && q_planes8 != nullptr;
   const double vmax = (double)((1 << total_bits) - 1);  // largest code value
   extern __shared__ float v[];
   __shared__ double s_sum;
@@ -429,6 +410,10 @@ __global__ void rabitq_prep_query_kernel(const float* queries, int nq, int d, in
       if (multi) {
         q_bf[(int64_t)q * padded + i] = __float2bfloat16_rn(0.f);
         q_bf[((int64_t)nq + q) * padded + i] = __float2bfloat16_rn(0.f);
+        if (int8_form) {
+          q_planes8[(int64_t)q * padded + i] = 0;
+          q_planes8[((int64_t)nq + q) * padded + i] = 0;
+        }
       } else {
         q_int[(int64_t)q * 2 * padded + i] = 0;
         q_int[(int64_t)q * 2 * padded + padded + i] = 0;
@@ -458,7 +443,7 @@ __global__ void rabitq_prep_query_kernel(const float* queries, int nq, int d, in
   }
   for (int i = threadIdx.x; i < padded; i += blockDim.x) q_rot[(int64_t)q * padded + i] = v[i];
   __shared__ float s_maxabs, s_scale;
-  __shared__ double s_resid;
+  __shared__ double s_resid, s_wsum, s_wabs;
   if (threadIdx.x == 0) {
     double s = 0.0, a = 0.0;
     float mx = 0.f;
@@ -479,10 +464,13 @@ __global__ void rabitq_prep_query_kernel(const float* queries, int nq, int d, in
     q_fast_sum[q] = __double2float_rn(s);
     // The scale of the tensor-core scan's integer query.
     const float scale = mx > 0.f ? mx / (float)kRaBitQIntMax : 0.f;
-    s_scale = scale;
+    s_scale = int8_form ? (mx > 0.f ? mx / (float)kRaBitQInt16Max : 0.f) : scale;
     s_resid = 0.0;
-    // Multi-bit: -(center sum), center = -(2^(TotalBits-1) - 1/2) (Estimate).
-    const double center = multi ? -(ldexp(1.0, total_bits - 1) - 0.5) : -0.5;
+    s_wsum = 0.0;
+    s_wabs = 0.0;
+    // Multi-bit: -(center sum), center = -(2^(TotalBits-1) - 1/2) (Estimate);
+    // the INT8 form's terms are set once sum(w) is known (below).
+    const double center = multi ? center_of(total_bits) : -0.5;
     q_terms[q] = multi ? make_float2(-__double2float_rn(__dmul_rn(center, s)), 0.f)
                        : make_float2(0.5f * __double2float_rn(s), scale);
     // Every value is a multiple of 2^g, so is every product with a code value
@@ -514,6 +502,37 @@ __global__ void rabitq_prep_query_kernel(const float* queries, int nq, int d, in
       const __nv_bfloat16 hi = __float2bfloat16_rn(v[i]);
       qhi[i] = hi;
       qlo[i] = __float2bfloat16_rn(v[i] - __bfloat162float(hi));
+    }
+    if (int8_form) {
+      // w = round(v / scale), |w| <= 32767, as h = floor(w / 256) and
+      // l = (w mod 256) - 128; sum w, sum |w| and the rounding bound
+      // sum |v - scale w| (each term exact in float64).
+      const float scale = s_scale;
+      int8_t* ph = q_planes8 + (int64_t)q * padded;
+      int8_t* pl = q_planes8 + ((int64_t)nq + q) * padded;
+      double resid = 0.0, wsum = 0.0, wabs = 0.0;
+      for (int i = threadIdx.x; i < padded; i += blockDim.x) {
+        int w = 0;
+        if (scale > 0.f) {
+          const double t = rint((double)v[i] / (double)scale);
+          w = (int)fmin(fmax(t, -(double)kRaBitQInt16Max), (double)kRaBitQInt16Max);
+        }
+        ph[i] = (int8_t)(w >> 8);
+        pl[i] = (int8_t)((w & 255) - 128);
+        resid += fabs((double)v[i] - (double)scale * (double)w);
+        wsum += (double)w;
+        wabs += fabs((double)w);
+      }
+      for (int o = 16; o > 0; o >>= 1) {
+        resid += __shfl_xor_sync(0xffffffffu, resid, o);
+        wsum += __shfl_xor_sync(0xffffffffu, wsum, o);
+        wabs += __shfl_xor_sync(0xffffffffu, wabs, o);
+      }
+      if ((threadIdx.x & 31) == 0) {
+        atomicAdd(&s_resid, resid);
+        atomicAdd(&s_wsum, wsum);
+        atomicAdd(&s_wabs, wabs);
+      }
     }
   } else {
     // The integer query and the bound on its rounding, sum |v_i - scale w_i|
@@ -554,7 +573,20 @@ __global__ void rabitq_prep_query_kernel(const float* queries, int nq, int d, in
     // (tensor-core scan), the float32 roundings of the inputs and of each
     // operation.
     double e;
-    if (multi) {
+    if (int8_form) {
+      // The exact integer dots leave the query's rounding, vmax sum |v - s w|,
+      // and the float32 evaluation of dp = 256 A_h + A_l + 128 sum(v - 128)
+      // (each |term| <= 128 (sum |w| + 384 padded), the row term <= 2^14
+      // padded; the int32-to-float conversions, the fma and the add) and of
+      // s dp - x (one fma).
+      const double scale = (double)s_scale;
+      const double dpmag = 128.0 * (s_wabs + 384.0 * padded) + 16384.0 * padded;
+      const double x = fabs(-__dmul_rn(center_of(total_bits), s_sum) -
+                            scale * 128.0 * s_wsum);
+      const double dot_err = vmax * s_resid * 1.0001 +
+                             kU * (5.0 * scale * dpmag + x) * 1.01;
+      e = maxR * (dot_err + kU * csum) + 6.0 * kU * (maxA + maxg + maxR * (vmax * S1 + csum));
+    } else if (multi) {
       // The bfloat16 split (|v - hi - lo| <= 2^-16 |v|, plus underflow) and
       // an fp32 accumulation of 2 padded exact products on the tensor cores
       // (the FFMA scan's float32 sum of padded terms is within the same
@@ -570,6 +602,14 @@ __global__ void rabitq_prep_query_kernel(const float* queries, int nq, int d, in
       e = maxR * dot_err + 6.0 * kU * (maxA + maxg + maxR * (S1 + 0.5 * sumd));
     }
     q_eps[q] = (float)(2.5 * e) + 1e-30f;
+    if (int8_form) {
+      // {-(center sum) - scale 128 sum(w), scale}: s dp - x = s sum(v w)
+      // + center sum (sum(v w) = dp + 128 sum(w)).
+      const double scale = (double)s_scale;
+      q_terms[q] = make_float2(
+          __double2float_rn(-__dmul_rn(center_of(total_bits), s_sum) - scale * 128.0 * s_wsum),
+          s_scale);
+    }
     // Magnitudes whose scale would lose precision go to the exact scan.
     if (!(s_maxabs < 1e30f) || (s_maxabs > 0.f && s_maxabs < 1e-30f)) q_flags[q] |= 1;
     q_status[q] = 0;
@@ -708,21 +748,23 @@ __global__ void rabitq_clear_flags(const int* ids, int n, int* q_flags) {
 }
 
 // Small batches: a scan of the sign bits (n x padded/8 bytes) instead of
-// the tensor-core operand planes (16 x larger).  One block per (row part,
-// query).  The block's query is a byte table in shared memory: entry (b,
-// pos) = the float32 sum of q[8 pos + i] over the set bits i of b, stored at
-// column (pos mod 4) * 32 + pos / 4 of row b (128 columns, zero past
-// padded/8).  Steps of 256 rows are staged in shared memory (coalesced
-// 8-byte loads, double-buffered, rows padded with zeros to 128 bytes); lane
-// l of a warp scores row l, reading its 32 code words in the rotated order
+// the tensor-core operand planes (16 x larger).  One block of 16 warps per
+// (row part, query), one part per SM.  The block's query is a byte table in
+// shared memory: entry (b, pos) = the float32 sum of q[8 pos + i] over the
+// set bits i of b, stored at column (pos mod 4) * 32 + pos / 4 of row b (128
+// columns, zero past padded/8).  Steps of 512 rows are staged in shared
+// memory (coalesced 8-byte loads held in registers while the block scores
+// the previous step, rows padded with zeros to 128 bytes); lane l of a warp
+// scores row l, reading its 32 code words in the rotated order
 // w = (g + l) mod 32, so the code reads (bank w) and the four table reads of
 // a word (column j * 32 + w, bank w) of the 32 lanes all hit different
 // banks.  A row's dot is a float32 sum of at most `padded` terms (within the
 // FFMA term of q_eps); ranks use the RaBitQRanker formula; keys below the
 // block's threshold go to one block list, compacted to the KP best by a
-// block sort when full.
-constexpr int kLutThreads = 256;
-constexpr int kLutCap = 1024;       // block list entries
+// block sort when full.  The parts' lists are then reduced to one list per
+// query (reduce_lists_kernel) for the merge.
+constexpr int kLutThreads = 512;
+constexpr int kLutCap = 2048;       // block list entries (kp + one step's appends)
 constexpr int kLutMaxBytes = 128;   // padded / 8 (padded <= 1024)
 
 __global__ void __launch_bounds__(kLutThreads, 1) rabitq_lut_scan_kernel(
@@ -734,8 +776,8 @@ __global__ void __launch_bounds__(kLutThreads, 1) rabitq_lut_scan_kernel(
     uint64_t* __restrict__ part_sat, int* __restrict__ q_flags) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   float* lut = reinterpret_cast<float*>(smem_raw);                          // [256][128]
-  uint32_t* stage = reinterpret_cast<uint32_t*>(lut + 256 * kLutMaxBytes);  // [2][256][32]
-  uint64_t* list = reinterpret_cast<uint64_t*>(stage + 2 * kLutThreads * 32);  // [kLutCap]
+  uint32_t* stage = reinterpret_cast<uint32_t*>(lut + 256 * kLutMaxBytes);  // [512][32]
+  uint64_t* list = reinterpret_cast<uint64_t*>(stage + kLutThreads * 32);   // [kLutCap]
   float* gadd = reinterpret_cast<float*>(list + kLutCap);                   // [nc]
   __shared__ int s_count, s_bad;
   __shared__ unsigned long long s_thr;
@@ -755,7 +797,7 @@ __global__ void __launch_bounds__(kLutThreads, 1) rabitq_lut_scan_kernel(
       lut[b * kLutMaxBytes + col] = lut[(b & (b - 1)) * kLutMaxBytes + col] + v[__ffs(b) - 1];
   }
   // Zero padding of the staged rows (bytes past padded/8, never overwritten).
-  for (int i = tid; i < 2 * kLutThreads * 32; i += kLutThreads)
+  for (int i = tid; i < kLutThreads * 32; i += kLutThreads)
     if ((i & 31) >= bytes / 4) stage[i] = 0u;
   for (int c = tid; c < nc; c += kLutThreads) gadd[c] = q_fast_gadd[(int64_t)q * nc + c];
   if (tid == 0) {
@@ -766,9 +808,9 @@ __global__ void __launch_bounds__(kLutThreads, 1) rabitq_lut_scan_kernel(
   const float half_sum = 0.5f * q_fast_sum[q];
   const int64_t begin = (int64_t)part * rows_per_part;
   const int64_t end = min(n, begin + rows_per_part);
-  const int steps = (int)((end - begin + kLutThreads - 1) / kLutThreads);
-  // Step i's rows [begin + 256 i, ...) as 8-byte words: thread t takes words
-  // t, t + 256, ... of the step's contiguous bytes.
+  const int steps = end > begin ? (int)((end - begin + kLutThreads - 1) / kLutThreads) : 0;
+  // Step i's rows [begin + 512 i, ...) as 8-byte words: thread t takes words
+  // t, t + 512, ... of the step's contiguous bytes.
   const int per_step = kLutThreads * words8;
   constexpr int kMaxLoads = kLutMaxBytes / 8;  // words per thread per step
   uint2 pre[kMaxLoads];
@@ -782,28 +824,46 @@ __global__ void __launch_bounds__(kLutThreads, 1) rabitq_lut_scan_kernel(
       pre[k] = (u < per_step && u < words_avail) ? __ldg(src + u) : make_uint2(0u, 0u);
     }
   };
-  auto store_step = [&](int buf) {
-    uint32_t* dst = stage + buf * kLutThreads * 32;
+  auto store_step = [&]() {
 #pragma unroll
     for (int k = 0; k < kMaxLoads; ++k) {
       const int u = tid + k * kLutThreads;
       if (u < per_step) {
         const int r = u / words8, w = u - r * words8;
-        *reinterpret_cast<uint2*>(dst + r * 32 + w * 2) = pre[k];
+        *reinterpret_cast<uint2*>(stage + r * 32 + w * 2) = pre[k];
       }
+    }
+  };
+  // The row terms of this thread's row in a step, loaded a step ahead.
+  float4 nf = make_float4(0.f, 0.f, 0.f, 0.f);
+  uint32_t nkr = 0;
+  bool nok = false;
+  auto load_terms = [&](int i) {
+    const int64_t row = begin + (int64_t)i * kLutThreads + tid;
+    nok = row < end && bitmap_pass(bitmap, row);
+    if (nok) {
+      nf = fast[row];
+      nkr = keyrank[row];
     }
   };
   if (steps > 0) {
     load_step(0);
-    store_step(0);
+    load_terms(0);
+    store_step();
   }
   __syncthreads();
   bool saturated = false;
   for (int i = 0; i < steps; ++i) {
-    if (i + 1 < steps) load_step(i + 1);
-    const int64_t row = begin + (int64_t)i * kLutThreads + tid;
-    const bool ok = row < end && bitmap_pass(bitmap, row);
-    const uint32_t* mine = stage + (i & 1) * kLutThreads * 32 + tid * 32;
+    const bool ok = nok;
+    const float4 f = nf;
+    const uint32_t kr = nkr;
+    // The next step's codes and row terms stay in flight (in registers)
+    // while this step is scored from the stage.
+    if (i + 1 < steps) {
+      load_step(i + 1);
+      load_terms(i + 1);
+    }
+    const uint32_t* mine = stage + tid * 32;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 4
     for (int g = 0; g < 32; ++g) {
@@ -815,20 +875,19 @@ __global__ void __launch_bounds__(kLutThreads, 1) rabitq_lut_scan_kernel(
     }
     const float dot = (acc[0] + acc[1]) + (acc[2] + acc[3]);
     if (ok) {
-      const float4 f = fast[row];
       const float rank = fmaf(f.y, dot - half_sum, f.x + gadd[__float_as_int(f.z)]);
       if (!finite_f(rank)) {
         s_bad = 1;
       } else {
-        const uint64_t key = pack_rank(rank, keyrank[row]);
+        const uint64_t key = pack_rank(rank, kr);
         if (key < *(volatile unsigned long long*)&s_thr) {
           const int slot = atomicAdd(&s_count, 1);
           list[slot] = key;
         }
       }
     }
-    if (i + 1 < steps) store_step((i + 1) & 1);
-    __syncthreads();
+    __syncthreads();  // the stage is read and the appends are in
+    if (i + 1 < steps) store_step();
     // Room for the next step's appends: compact to the KP best.
     if (s_count > kLutCap - kLutThreads) {
       const int cnt = s_count;
@@ -839,12 +898,12 @@ __global__ void __launch_bounds__(kLutThreads, 1) rabitq_lut_scan_kernel(
         s_thr = list[kp - 1];
         s_count = kp;
       }
-      __syncthreads();
     }
+    __syncthreads();
   }
   __syncthreads();
   const int cnt = s_count;
-  block_sort_u64<kLutCap>(list, cnt);
+  block_sort_u64_fit<kLutCap>(list, cnt);
   __syncthreads();
   const int out = min(cnt, kp);
   const int64_t slot = (int64_t)q * parts + part;
@@ -889,6 +948,9 @@ xvec_gpu_status rabitq_reserve(xvec_gpu_index* idx, int64_t cap, cudaStream_t s)
       (st = idx->rq_fast.reserve((size_t)cap * 16, (size_t)n * 16, s)) ||
       (st = plane.reserve((size_t)cap * idx->padded * 2, (size_t)n * idx->padded * 2, s)))
     return st;
+  if (idx->rq_total_bits > 1 && idx->rq_total_bits <= 8 &&
+      (st = idx->rq_vplane.reserve((size_t)cap * idx->padded, (size_t)n * idx->padded, s)))
+    return st;
   if (!idx->rq_bounds.ptr) {
     if ((st = idx->rq_bounds.reserve(16, 0, s))) return st;
     XVEC_CUDA(cudaMemsetAsync(idx->rq_bounds.ptr, 0, 16, s));
@@ -928,6 +990,13 @@ xvec_gpu_status rabitq_commit(xvec_gpu_index* idx, int64_t old_n, int64_t m, cud
   XVEC_CUDA(cudaMemcpyAsync(&h, err.ptr, 4, cudaMemcpyDeviceToHost, s));
   XVEC_CUDA(cudaStreamSynchronize(s));
   if (h) return set_error("core: invalid RaBitQ code (status %d)", h), (xvec_gpu_status)h;
+  if (idx->rq_total_bits > 1 && idx->rq_total_bits <= 8) {
+    rabitq_vplane_kernel<<<blocks_of(m * 32), 256, 0, s>>>(
+        idx->rq_values.as<uint16_t>() + old_n * padded, m, padded,
+        idx->rq_vplane.as<int8_t>() + old_n * padded, idx->rq_fast.as<float4>() + old_n);
+    XVEC_LAUNCHED();
+    XVEC_CUDA(cudaGetLastError());
+  }
   if (idx->rq_total_bits == 1) {
   const int64_t code_bytes = m * (padded / 8);
   rabitq_planes_kernel<<<blocks_of(code_bytes), 256, 0, s>>>(
@@ -1005,10 +1074,21 @@ xvec_gpu_status rabitq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq
   xvec_gpu_status st;
   const int total_bits = idx->rq_total_bits;
   const bool multi = total_bits > 1;
-  Scratch qrot, qsum, gadd, gerr, qfs, qfg, qeps, qexact, qstatus, qflags, qint, qterms, qbf;
+  Scratch qrot, qsum, gadd, gerr, qfs, qfg, qeps, qexact, qstatus, qflags, qint, qterms, qbf,
+      q8;
+  // Multi-bit with TotalBits <= 8: the INT8 tensor-core scan on the int8
+  // code plane and the 16-bit integer query (its eps is that form's).
+  const bool want8 = multi && total_bits <= 8 && idx->rq_vplane.ptr != nullptr;
   if ((st = qint.alloc((size_t)nq * padded * 2, s)) || (st = qterms.alloc((size_t)nq * 8, s)) ||
-      (multi && (st = qbf.alloc((size_t)nq * padded * 4, s))))
+      (multi && (st = qbf.alloc((size_t)nq * padded * 4, s))) ||
+      (want8 && (st = q8.alloc((size_t)nq * padded * 2, s))))
     return st;
+  const int64_t n_all = idx->n;
+  const bool small_batch = !multi && n_all > 0 && nq <= 8 && padded <= 8 * kLutMaxBytes &&
+                           kp <= 256 && nc <= 4096;
+  const bool tc8 = want8 && !small_batch && n_all > 0 && nc <= rabitq_tc_max_clusters() &&
+                   kp + 128 <= flat_tc_cap() && n_all < (1ll << 31) - 256 &&
+                   rabitq8_tc_supported(padded, idx->rq_vplane.ptr, q8.ptr);
   if ((st = qrot.alloc((size_t)nq * padded * 4, s)) || (st = qsum.alloc((size_t)nq * 8, s)) ||
       (st = gadd.alloc((size_t)nq * nc * 8, s)) || (st = gerr.alloc((size_t)nq * nc * 8, s)) ||
       (st = qfs.alloc((size_t)nq * 4, s)) || (st = qfg.alloc((size_t)nq * nc * 4, s)) ||
@@ -1022,7 +1102,7 @@ xvec_gpu_status rabitq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq
       idx->rq_bounds.as<unsigned>(), qrot.as<float>(), qsum.as<double>(), gadd.as<double>(),
       gerr.as<double>(), qfs.as<float>(), qfg.as<float>(), qeps.as<float>(), qexact.as<int>(),
       qstatus.as<int>(), qflags.as<int>(), qint.as<int8_t>(), qterms.as<float2>(), total_bits,
-      multi ? qbf.as<__nv_bfloat16>() : nullptr);
+      multi ? qbf.as<__nv_bfloat16>() : nullptr, tc8 ? q8.as<int8_t>() : nullptr);
   XVEC_LAUNCHED();
   // The approximate stage writes the final results, or the candidates of the
   // refine stage (no radius there: hnsw_rabitq.go:584).
@@ -1044,27 +1124,32 @@ xvec_gpu_status rabitq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq
   const float stage_radius = refine ? 0.f : o.radius;
   // Small batches: the sign bits through a byte table (the tensor-core scan
   // streams 16x more bytes and fills few SMs at this size).
-  const bool small = !multi && n > 0 && nq <= 8 && padded <= 8 * kLutMaxBytes && kp <= 256;
+  const bool small = small_batch;
   // INT8 tensor cores on the code planes (one bit), or BF16 tensor cores on
   // the full code values (up to 8 bits), when the layout allows, else FFMA.
   const bool use_tc = !small && n > 0 && nc <= rabitq_tc_max_clusters() &&
                       kp + 128 <= flat_tc_cap() && n < (1ll << 31) - 256 &&
-                      (multi ? total_bits <= 8 && (uintptr_t)idx->rq_values.ptr % 16 == 0 &&
-                                   (uintptr_t)qbf.ptr % 16 == 0
-                             : rabitq_tc_supported(padded, idx->rq_planes.ptr, qint.ptr));
+                      (multi ? tc8 : rabitq_tc_supported(padded, idx->rq_planes.ptr, qint.ptr));
   const bool fast = small || use_tc || (n > 0 && simt_cap_for(kp) <= 512);
   if (small) {
-    int parts = (int)std::max<int64_t>(
-        1, std::min<int64_t>(flat_merge_capacity() / kp, (n + 4095) / 4096));
+    // One part per SM (each block keeps its kp best), then one list per
+    // query for the merge.
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, idx->device);
+    int parts = (int)std::max<int64_t>(1, std::min<int64_t>(sms, (n + 4095) / 4096));
+    while (parts > 1 && !reduce_lists_supported(parts, kp)) --parts;
     const int64_t rows_per_part = ((n + parts - 1) / parts + kLutThreads - 1) / kLutThreads *
                                   kLutThreads;
     parts = (int)((n + rows_per_part - 1) / rows_per_part);
-    Scratch pkeys, pcounts, psat;
+    const int lstride = reduce_lists_out_cap(kp);
+    Scratch pkeys, pcounts, psat, lkeys, lcounts, lsat;
     if ((st = pkeys.alloc((size_t)nq * parts * kp * 8, s)) ||
         (st = pcounts.alloc((size_t)nq * parts * 4, s)) ||
-        (st = psat.alloc((size_t)nq * parts * 8, s)))
+        (st = psat.alloc((size_t)nq * parts * 8, s)) ||
+        (st = lkeys.alloc((size_t)nq * lstride * 8, s)) ||
+        (st = lcounts.alloc((size_t)nq * 4, s)) || (st = lsat.alloc((size_t)nq * 8, s)))
       return st;
-    const int smem = kLutMaxBytes * 256 * 4 + 2 * kLutThreads * 128 + kLutCap * 8 + nc * 4;
+    const int smem = kLutMaxBytes * 256 * 4 + kLutThreads * 128 + kLutCap * 8 + nc * 4;
     cudaFuncSetAttribute(rabitq_lut_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          smem);
     timer.mark(1);
@@ -1075,14 +1160,18 @@ xvec_gpu_status rabitq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq
         psat.as<uint64_t>(), qflags.as<int>());
     XVEC_LAUNCHED();
     XVEC_CUDA(cudaGetLastError());
+    XVEC_CUDA(launch_reduce_lists(pkeys.as<uint64_t>(), pcounts.as<int>(), psat.as<uint64_t>(),
+                                  nq, parts, kp, lstride, nullptr, lkeys.as<uint64_t>(),
+                                  lcounts.as<int>(), lsat.as<uint64_t>(), s));
+    XVEC_LAUNCHED();
     timer.mark(2);
     XVEC_CUDA(launch_merge_rescore(sc, idx->pos_of_kr.as<uint32_t>(), idx->keys.as<uint64_t>(),
-                                   nullptr, nq, cc, stage_radius, 0, pkeys.as<uint64_t>(),
-                                   pcounts.as<int>(), psat.as<uint64_t>(), parts, kp, o_keys,
+                                   nullptr, nq, cc, stage_radius, 0, lkeys.as<uint64_t>(),
+                                   lcounts.as<int>(), lsat.as<uint64_t>(), 1, lstride, o_keys,
                                    o_scores, o_counts, spos.as<uint32_t>(), qflags.as<int>(), s));
     XVEC_LAUNCHED();
   } else if (use_tc) {
-    Scratch pkeys, pcounts, psat, kstatus;
+    Scratch pkeys, pcounts, psat, kstatus, gthr_keep;
     int lists = 0;
     if ((st = kstatus.alloc(4, s))) return st;
     XVEC_CUDA(cudaMemsetAsync(kstatus.ptr, 0, 4, s));
@@ -1092,9 +1181,8 @@ xvec_gpu_status rabitq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq
         [&](int64_t b, int64_t e, int p, int list0, int nlists, unsigned long long* gthr,
             uint64_t* cand, int* counts, uint64_t* sat) {
           if (multi)
-            return launch_rabitq_full_scan_tc(
-                qbf.as<__nv_bfloat16>(), qbf.as<__nv_bfloat16>() + (int64_t)nq * padded, nq,
-                idx->rq_values.as<__nv_bfloat16>() + b * padded, e - b, padded,
+            return launch_rabitq8_scan_tc(
+                q8.as<int8_t>(), nq, idx->rq_vplane.as<int8_t>() + b * padded, e - b, padded,
                 idx->rq_fast.as<float4>() + b, idx->keyrank.as<uint32_t>() + b,
                 qterms.as<float2>(), qfg.as<float>(), nc, gthr,
                 d_bitmap ? d_bitmap + b / 32 : nullptr, p, kp, list0, nlists, cand, counts, sat,
@@ -1105,7 +1193,7 @@ xvec_gpu_status rabitq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq
               qterms.as<float2>(), qfg.as<float>(), nc, gthr, d_bitmap ? d_bitmap + b / 32 : nullptr,
               p, kp, list0, nlists, cand, counts, sat, qflags.as<int>(), kstatus.as<int>(), s);
         },
-        pkeys, pcounts, psat, &lists);
+        pkeys, pcounts, psat, &lists, &gthr_keep);
     if (st) return st;
     timer.mark(2);
     XVEC_LAUNCHED();
@@ -1114,7 +1202,8 @@ xvec_gpu_status rabitq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq
                                    nullptr, nq, cc, stage_radius, 0, pkeys.as<uint64_t>(),
                                    pcounts.as<int>(), psat.as<uint64_t>(), lists, flat_tc_cap(),
                                    o_keys, o_scores, o_counts, spos.as<uint32_t>(),
-                                   qflags.as<int>(), s));
+                                   qflags.as<int>(), s,
+                                   gthr_keep.as<unsigned long long>()));
     XVEC_LAUNCHED();
     int h_kstatus = 0;
     XVEC_CUDA(cudaMemcpyAsync(&h_kstatus, kstatus.ptr, 4, cudaMemcpyDeviceToHost, s));

@@ -569,7 +569,7 @@ xvec_gpu_status sq8_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
                       sq8_tc_supported(d, idx->sq_codes.ptr, qcodes.ptr);
   const bool fast = use_tc || (ranked && simt_cap_for(kp) <= 512);
   if (use_tc) {
-    Scratch pkeys, pcounts, psat, kstatus;
+    Scratch pkeys, pcounts, psat, kstatus, gthr_keep;
     int lists = 0;
     if ((st = kstatus.alloc(4, s))) return st;
     XVEC_CUDA(cudaMemsetAsync(kstatus.ptr, 0, 4, s));
@@ -585,7 +585,7 @@ xvec_gpu_status sq8_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
                                     d_bitmap ? d_bitmap + b / 32 : nullptr, p, kp, list0, nlists,
                                     cand, counts, sat, qflags.as<int>(), kstatus.as<int>(), s);
         },
-        pkeys, pcounts, psat, &lists);
+        pkeys, pcounts, psat, &lists, &gthr_keep);
     if (st) return st;
     timer.mark(2);
     XVEC_LAUNCHED();
@@ -594,7 +594,8 @@ xvec_gpu_status sq8_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
                                    nullptr, nq, stage_k, stage_radius, 0, pkeys.as<uint64_t>(),
                                    pcounts.as<int>(), psat.as<uint64_t>(), lists, flat_tc_cap(),
                                    o_keys, o_scores, o_counts, spos.as<uint32_t>(),
-                                   qflags.as<int>(), s));
+                                   qflags.as<int>(), s,
+                                   gthr_keep.as<unsigned long long>()));
     XVEC_LAUNCHED();
     int h_kstatus = 0;
     XVEC_CUDA(cudaMemcpyAsync(&h_kstatus, kstatus.ptr, 4, cudaMemcpyDeviceToHost, s));
