@@ -58,7 +58,8 @@ def parse():
     p.add_argument("--workload",
                    choices=["flat_cosine_fp16", "ivfpq_l2", "sq8_ip_refine", "rabitq_l2_refine",
                             "flat_l2_fp32", "ivf_flat_l2", "ivf_sq8_l2_refine",
-                            "rabitq7_l2_refine", "sq4_l2_refine", "pq_train_l2"],
+                            "rabitq7_l2_refine", "sq4_l2_refine", "pq_train_l2",
+                            "rabitq_hnsw_l2_refine"],
                    default="flat_cosine_fp16",
                    help="flat_cosine_fp16: the Flat configuration above (default); ivfpq_l2: "
                         "IVF-PQ L2, 1e8 x 128, nlist 16384, 32 x 256 PQ, nprobe 64, k=10; "
@@ -70,7 +71,9 @@ def parse():
                         "INT8 list scoring and ScaleFactor 4; rabitq7_l2_refine: the RaBitQ "
                         "data with TotalBits 7; sq4_l2_refine: INT4 SQ Flat L2, 4e6 x 128, "
                         "10,000 queries, k=10, ScaleFactor 4; pq_train_l2: TrainPQ (32 chunks, "
-                        "200,000-row sample, 12 iterations) on 1e6 x 128, one training per step")
+                        "200,000-row sample, 12 iterations) on 1e6 x 128, one training per step; "
+                        "rabitq_hnsw_l2_refine: the HNSW-RaBitQ graph walk, 1e6 x 960, degree-32 "
+                        "proximity graph built on the GPU, EF 100, k=10, beside the linear scan")
     return p.parse_args()
 
 
@@ -411,7 +414,10 @@ def run_reference(args):
 PQ_N, PQ_DIM, PQ_CLUSTERS, PQ_NLIST, PQ_CHUNKS, PQ_NPROBE, PQ_K = (
     100_000_000, 128, 10_000, 16_384, 32, 64, 10)
 PQ_CHUNK_ROWS = 1_000_000
-PQ_TRAIN_ROWS, PQ_TRAIN_ITERS, PQ_TRAIN_SEED = 4_000_000, 10, 16_384
+PQ_TRAIN_ITERS, PQ_TRAIN_SEED = 10, 16_384
+# TrainPQ (pq.go:107-179) for the codebook: 32 chunks, a 200,000-row sample
+# drawn by TrainPQ from the first 4,000,000 rows, 12 Lloyd iterations.
+PQ_CODEBOOK_ROWS, PQ_CODEBOOK_SAMPLE, PQ_CODEBOOK_ITERS = 4_000_000, 200_000, 12
 PQ_WORKLOAD = ("IVF-PQ L2 search, 100,000,000 x 128 float32 (10,000-cluster mixture), "
                "nlist 16,384, PQ 32 x 256 (8-bit codes), nprobe 64, 10,000 queries, top-k=10")
 
@@ -444,12 +450,13 @@ def run_ivfpq(args):
     nq = args.nq
     g = torch.Generator(device=dev).manual_seed(4321)
     centers = torch.randn(PQ_CLUSTERS, PQ_DIM, generator=g, device=dev)
-    # Coarse centroids: GPU k-means on the first rows (every rank trains the
-    # same model).
-    train_n = min(n, PQ_TRAIN_ROWS)
-    train = torch.cat([pq_mixture(torch, centers, c, min(PQ_CHUNK_ROWS, train_n - c * PQ_CHUNK_ROWS),
-                                  dev)
-                       for c in range((train_n + PQ_CHUNK_ROWS - 1) // PQ_CHUNK_ROWS)]).contiguous()
+    # Coarse centroids: GPU k-means on every row, as IVFBuilder.Build trains
+    # (ivf.go:144-212); every rank trains the same model.
+    train_n = n
+    train = torch.empty(train_n, PQ_DIM, device=dev)
+    for c in range((train_n + PQ_CHUNK_ROWS - 1) // PQ_CHUNK_ROWS):
+        m = min(PQ_CHUNK_ROWS, train_n - c * PQ_CHUNK_ROWS)
+        train[c * PQ_CHUNK_ROWS:c * PQ_CHUNK_ROWS + m] = pq_mixture(torch, centers, c, m, dev)
     cents = torch.empty(PQ_NLIST, PQ_DIM, device=dev)
     train_labels = torch.empty(train_n, dtype=torch.int32, device=dev)
     torch.cuda.synchronize()
@@ -461,10 +468,17 @@ def run_ivfpq(args):
     torch.cuda.synchronize()
     t_train = time.perf_counter() - t_train
     cents = cents[:kc].contiguous()
+    # The PQ codebook: TrainPQ on the GPU (KMC2 seeding per chunk, Lloyd).
+    t_pq = time.perf_counter()
+    book_rows = train[:min(train_n, PQ_CODEBOOK_ROWS)].cpu().numpy()
     del train, train_labels
-    pivots = pq_mixture(torch, centers, 10**6 + 2, 256, dev).contiguous()
+    _, pivots = xb.pq_train(xb.METRIC_L2, book_rows, chunks=PQ_CHUNKS,
+                            max_train_samples=PQ_CODEBOOK_SAMPLE,
+                            max_iterations=PQ_CODEBOOK_ITERS, seed=PQ_TRAIN_SEED, device=local)
+    t_pq = time.perf_counter() - t_pq
+    del book_rows
     index = xb.IVFPQIndex(PQ_DIM, xb.METRIC_L2, device=local)
-    index.set_model(cents.cpu().numpy(), pivots.cpu().numpy(), PQ_CHUNKS)
+    index.set_model(cents.cpu().numpy(), pivots, PQ_CHUNKS)
     b, e = shard_range(n, rank, world, align=PQ_CHUNK_ROWS)
     index.reserve(e - b)
     sizes = torch.zeros(PQ_NLIST, dtype=torch.int64, device=dev)
@@ -511,8 +525,11 @@ def run_ivfpq(args):
                        "pq_chunks": PQ_CHUNKS, "nprobe": PQ_NPROBE,
                        "model": f"coarse centroids: GPU k-means (xvec_gpu_kmeans_train, "
                                 f"reservoir seed {PQ_TRAIN_SEED}, {train_iters} Lloyd "
-                                f"iterations) on the first {train_n} rows in {t_train:.1f} s; "
-                                "PQ codebook: seeded mixture draws",
+                                f"iterations) on all {train_n} rows in {t_train:.1f} s; "
+                                f"PQ codebook: TrainPQ on the GPU (xvec_gpu_pq_train: "
+                                f"{PQ_CHUNKS} chunks, a {PQ_CODEBOOK_SAMPLE}-row sample of the "
+                                f"first {min(train_n, PQ_CODEBOOK_ROWS)} rows, "
+                                f"{PQ_CODEBOOK_ITERS} iterations) in {t_pq:.1f} s",
                        "parallelism": f"rows sharded over {world} GPU(s), NCCL all-gather + merge",
                        "l2": "inputs larger than L2 (3.2 GB codes, 51 GB originals)"},
             "e2e": {"value": nq / (e2e_ms / 1000.0), "unit": "queries/sec",
@@ -1235,6 +1252,125 @@ def run_rabitq(args, total_bits=1):
     finish_ranks(world)
 
 
+# HNSW-RaBitQ: the graph walk over a proximity graph built here (level 0: each
+# row's 24 nearest rows by the library's FP16 Flat search plus 8 random rows,
+# the long links that make a small-world graph navigable; levels drawn as HNSW
+# draws them, each upper level's nodes linked to their 32 nearest nodes of that
+# level); the same index searched linearly beside it.
+RH_N, RH_DEGREE, RH_RANDOM = 1_000_000, 32, 8
+RH_WORKLOAD = ("HNSW-RaBitQ 1-bit L2 graph search with exact FP32 refinement, 1,000,000 x 960 "
+               "(1,000-cluster mixture), degree-32 proximity graph (24 nearest + 8 random links), "
+               "16 clusters, 10,000 queries, top-k=10, EF 100")
+
+
+def knn_graph_level(xb, torch, vecs, degree, dev):
+    """Each row's `degree` nearest other rows (L2) by the library's Flat
+    search over FP16 copies, as int32 positions [n][degree]."""
+    n, d = vecs.shape
+    idx = xb.DenseFlatIndex(d, xb.METRIC_L2, xb.STORAGE_FP16, device=dev.index or 0)
+    h = vecs.half().contiguous()
+    keys = torch.arange(n, dtype=torch.int64, device=dev)
+    idx.add_device(keys.data_ptr(), h.data_ptr(), n)
+    k = min(degree + 1, n)
+    out = torch.empty((n, k), dtype=torch.int64, device=dev)
+    sc = torch.empty((n, k), dtype=torch.float32, device=dev)
+    cnt = torch.empty(n, dtype=torch.int32, device=dev)
+    for b in range(0, n, 8192):
+        e = min(n, b + 8192)
+        idx.search_device(h[b:e].data_ptr(), e - b, xb.SearchOptions(top_k=k),
+                          out[b:e].data_ptr(), sc[b:e].data_ptr(), cnt[b:e].data_ptr())
+    torch.cuda.synchronize()
+    idx.close()
+    # Drop the row itself (first, at distance 0, for rows without an equal
+    # row of a lower key; otherwise the last neighbour goes).
+    own = torch.arange(n, device=dev).unsqueeze(1)
+    sel = torch.where(out[:, :1] == own, out[:, 1:], out[:, :-1])[:, :degree]
+    return sel.to(torch.int32).cpu().numpy()
+
+
+def run_rabitq_hnsw(args):
+    import numpy as np
+    import torch
+
+    import xvec_b200 as xb
+    world, rank, local, dev = init_ranks(args)
+    if world != 1:
+        raise SystemExit("rabitq_hnsw_l2_refine runs on one GPU (the graph is not sharded)")
+    n = args.n if args.n != N_BASE else RH_N
+    nq = args.nq
+    g = torch.Generator(device=dev).manual_seed(960)
+    centers = torch.randn(CLUSTERS, RQ_DIM, generator=g, device=dev)
+    cents = pq_mixture(torch, centers, 10**6 + 11, RQ_NC, dev).contiguous()
+    padded = (RQ_DIM + 63) // 64 * 64
+    signs = np.random.default_rng(961).integers(0, 256, 4 * padded // 8, dtype=np.uint8)
+    rows = torch.cat([pq_mixture(torch, centers, 2 * 10**6 + c, min(RQ_CHUNK_ROWS, n - c * RQ_CHUNK_ROWS), dev)
+                      for c in range((n + RQ_CHUNK_ROWS - 1) // RQ_CHUNK_ROWS)]).contiguous()
+    index = xb.RaBitQIndex(RQ_DIM, xb.METRIC_L2, device=local)
+    index.set_model(cents.cpu().numpy(), signs)
+    keys = torch.arange(n, dtype=torch.int64, device=dev)
+    index.add_device(keys.data_ptr(), rows.data_ptr(), n, torch.cuda.current_stream().cuda_stream)
+    # The graph: HNSW levels, each level's kNN lists.
+    t0 = time.perf_counter()
+    rng = np.random.default_rng(7)
+    levels = np.floor(-np.log(rng.random(n) + 1e-12) / np.log(RH_DEGREE)).astype(np.int64)
+    max_level = int(levels.max())
+    offsets = np.zeros((max_level + 1, n + 1), np.int64)
+    flat, base = [], 0
+    for level in range(max_level + 1):
+        nodes = np.nonzero(levels >= level)[0]
+        counts = np.zeros(n, np.int64)
+        if nodes.size > 1:
+            sub = rows[torch.as_tensor(nodes, device=dev)]
+            near = RH_DEGREE - RH_RANDOM if level == 0 else RH_DEGREE
+            nb = knn_graph_level(xb, torch, sub, min(near, nodes.size - 1), dev)
+            lists = nodes[nb]                       # positions
+            if level == 0:
+                lists = np.concatenate(
+                    [lists, rng.integers(0, n, (n, RH_RANDOM)).astype(lists.dtype)], axis=1)
+            counts[nodes] = lists.shape[1]
+            order = np.zeros((n, lists.shape[1]), np.int32)
+            order[nodes] = lists
+            flat.append(order[counts > 0].reshape(-1) if lists.shape[1] else np.zeros(0, np.int32))
+        else:
+            flat.append(np.zeros(0, np.int32))
+        offsets[level, 1:] = np.cumsum(counts)
+        offsets[level] += base
+        base += int(counts.sum())
+    entry = int(np.nonzero(levels == max_level)[0][0])
+    neighbors = np.concatenate(flat).astype(np.int32)
+    index.set_graph(max_level, entry, offsets.reshape(-1), neighbors)
+    graph_s = time.perf_counter() - t0
+    del rows
+    queries = pq_mixture(torch, centers, 3 * 10**6, nq, dev).contiguous()
+    torch.cuda.synchronize()
+    opts = xb.SearchOptions(top_k=RQ_K, ef=RQ_EF, refine=True)
+    search = sharded(index, world, local)
+    ms, walk_ms, e2e_ms, st, clocks = time_search(search, queries, opts, args, dev, world, local)
+    lin_opts = xb.SearchOptions(top_k=RQ_K, ef=RQ_EF, refine=True, linear=True)
+    lin_ms, _, _, _, _ = time_search(search, queries, lin_opts, args, dev, world, local)
+    # Agreement of the walk with the linear scan (recall of the walk's top-10).
+    gw = gpu_results_host(search, queries, opts)
+    gl = gpu_results_host(search, queries, lin_opts)
+    hit = sum(len(set(gw[0][q, :int(gw[2][q])].tolist()) & set(gl[0][q, :int(gl[2][q])].tolist()))
+              for q in range(nq))
+    recall = hit / float(max(1, int(gl[2].sum())))
+    # Bytes the walk reads per query: codes (padded / 8) + factors (48) per
+    # estimate; the walk is latency-bound, so no roofline fraction is claimed.
+    roof = {"bound": "latency", "achieved": None, "peak": None, "unit": None, "frac": None,
+            "traffic": None, "kernel": "hnsw_rabitq_walk_kernel", "kernel_ms": walk_ms,
+            "note": "one warp per query; sequential heap decisions per visited node"}
+    config = {"workload": RH_WORKLOAD, "global_batch": nq, "top_k": RQ_K, "base_vectors": n,
+              "dim": RQ_DIM, "metric": "l2", "clusters": RQ_NC, "ef": RQ_EF, "degree": RH_DEGREE,
+              "graph_levels": max_level + 1, "graph_build_s": graph_s,
+              "parallelism": "one GPU", "l2": "inputs larger than L2 (3.8 GB originals)"}
+    line = common_line(nq, ms, e2e_ms, args, world, "1-bit codes, f64 estimates", config, roof,
+                       None, clocks, st, RQ_K, RQ_DIM, 4)
+    line["linear_scan"] = {"ms_per_step": lin_ms, "queries_per_sec": nq / (lin_ms / 1000.0)}
+    line["walk_recall_vs_linear"] = recall
+    print(json.dumps(line), flush=True)
+    finish_ranks(world)
+
+
 def cpu_rabitq_qps(cents, signs, sample, queries, n_total, total_bits=1, extra_scale=0.0):
     import numpy as np
 
@@ -1304,6 +1440,8 @@ def main():
         return run_sq4(args)
     if args.workload == "pq_train_l2":
         return run_pq_train(args)
+    if args.workload == "rabitq_hnsw_l2_refine":
+        return run_rabitq_hnsw(args)
 
     import numpy as np
     import torch

@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define XVEC_GPU_ABI_VERSION 2
+#define XVEC_GPU_ABI_VERSION 3
 
 typedef enum {
   XVEC_GPU_OK = 0,
@@ -137,6 +137,9 @@ typedef struct {
                                legacy default stream */
   const volatile int32_t* cancel_flag; /* optional host flag, polled between kernel
                                           launches; non-zero => XVEC_GPU_CANCELLED */
+  int32_t linear;           /* HNSWRaBitQSearchOptions.Linear (hnsw_rabitq.go:589-591),
+                               RABITQ with a graph only: non-zero = the linear scan of
+                               every code instead of the graph walk */
 } xvec_gpu_search_opts;
 
 /* Library ------------------------------------------------------------------ */
@@ -457,6 +460,24 @@ xvec_gpu_status xvec_gpu_index_search_noalloc(xvec_gpu_index* index, const void*
                                               int32_t nq, const xvec_gpu_search_opts* opts,
                                               uint64_t* d_out_keys, float* d_out_scores,
                                               int32_t* d_out_counts);
+
+/* HNSW-RaBitQ graph (HNSWRaBitQIndex, hnsw_rabitq.go): the graph the Go
+ * side built over the index's insertion positions, for the graph walk of
+ * searchPrepared (hnsw_rabitq.go:589-612: descent through the upper levels on
+ * coarse estimates, :644-671; the base-layer search, :673-737).  Node p's
+ * level-L neighbours (positions, in the reference's list order) are
+ * neighbors[offsets[L (n + 1) + p] .. offsets[L (n + 1) + p + 1]) for L in
+ * 0..max_level; offsets is (max_level + 1) (n + 1) int64 in host memory,
+ * each level's run non-decreasing; entry is the entry point
+ * (hnswIndex.entryPoint); n must equal the index's row count.  With a graph,
+ * searches of more than 1000 rows (DefaultHNSWBruteForceThreshold,
+ * hnsw.go:592) walk it unless opts.linear is set; results equal the
+ * reference's walk (keys identical, scores bit-identical).  Adding rows
+ * invalidates the graph (searches then fail until it is set again);
+ * max_level = -1 removes it. */
+xvec_gpu_status xvec_gpu_rabitq_set_graph(xvec_gpu_index* index, int32_t max_level, int64_t entry,
+                                          const int64_t* offsets, const int32_t* neighbors,
+                                          int64_t total_neighbors);
 
 /* ---- Rotation reformer -------------------------------------------------
  * A collection whose vector index sets `rotate` rotates every stored and

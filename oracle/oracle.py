@@ -198,6 +198,13 @@ class Oracle:
                                               _f32p, ctypes.c_int32, ctypes.c_int32,
                                               ctypes.c_int32, ctypes.c_int32, ctypes.c_float,
                                               _u32p, ctypes.c_int32, _u64p, _f32p, _i32p, _i32p]
+        lib.xo_hnsw_rabitq_search.argtypes = [ctypes.c_int, ctypes.c_int32, _f32p,
+                                              ctypes.c_int32, _u8p, ctypes.c_int32, _u8p, _u8p,
+                                              ctypes.c_void_p, _f32p, _u64p, ctypes.c_int64,
+                                              ctypes.c_int32, ctypes.c_int64, _i64p, _i32p,
+                                              _f32p, ctypes.c_int32, ctypes.c_int32,
+                                              ctypes.c_int32, ctypes.c_int32, ctypes.c_float,
+                                              _u32p, ctypes.c_int32, _u64p, _f32p, _i32p, _i32p]
         lib.xo_rabitq_prepare_query.argtypes = [ctypes.c_int, ctypes.c_int32, _f32p,
                                                 ctypes.c_int32, _u8p, _f32p, _f32p, _f64p, _f64p,
                                                 _f64p]
@@ -743,6 +750,87 @@ class Oracle:
                                             threads or os.cpu_count(), _ptr(ok, _u64p),
                                             _ptr(os_, _f32p), _ptr(oc, _i32p), _ptr(ost, _i32p))
         return st, ok.reshape(nq, k), os_.reshape(nq, k), oc, ost
+
+
+    def hnsw_rabitq_search(self, metric, centroids, signs, codes, factors, originals, keys,
+                           graph, queries, k, ef, radius=0.0, bitmap=None, refine=True,
+                           total_bits=1, extra=None, threads=0):
+        """HNSW-RaBitQ search (hnsw_rabitq.go:589-801) over `graph` =
+        (max_level, entry, offsets [(max_level + 1) (n + 1)] int64, neighbors
+        int32): node p's level-L neighbours at neighbors[offsets[L (n + 1) + p]
+        .. offsets[L (n + 1) + p + 1])."""
+        max_level, entry, offsets, nbrs = graph
+        centroids = _c(centroids, np.float32)
+        signs = _c(signs, np.uint8)
+        codes = _c(codes, np.uint8)
+        factors = np.ascontiguousarray(factors, RABITQ_FACTORS_DTYPE)
+        originals = _c(originals, np.float32)
+        keys = _c(keys, np.uint64)
+        queries = _c(queries, np.float32)
+        offsets = _c(offsets, np.int64)
+        nbrs = _c(nbrs, np.int32)
+        n, d = originals.shape
+        if total_bits > 1:
+            extra = _c(extra, np.uint8)
+            assert extra.shape == (n, self.rabitq_extra_bytes(d, total_bits))
+        nq = queries.shape[0]
+        ok, os_, oc, ost = self._outs(nq, k)
+        bm = None if bitmap is None else _c(bitmap, np.uint32)
+        st = self.lib.xo_hnsw_rabitq_search(
+            metric, d, _ptr(centroids, _f32p), centroids.shape[0], _ptr(signs, _u8p), total_bits,
+            _ptr(codes, _u8p), _ptr(extra, _u8p) if total_bits > 1 else None, factors.ctypes.data,
+            _ptr(originals, _f32p), _ptr(keys, _u64p), n, max_level, entry,
+            _ptr(offsets, _i64p), _ptr(nbrs, _i32p), _ptr(queries, _f32p), nq, k, ef,
+            1 if refine else 0, radius, _ptr(bm, _u32p), threads or os.cpu_count(),
+            _ptr(ok, _u64p), _ptr(os_, _f32p), _ptr(oc, _i32p), _ptr(ost, _i32p))
+        return st, ok.reshape(nq, k), os_.reshape(nq, k), oc, ost
+
+
+def hnsw_test_graph(vectors, degree=12, seed=0, ml=None):
+    """A layered proximity graph for the graph-search tests (any graph
+    defines the search): node levels drawn as HNSW draws them (floor of
+    -ln(U) / ln(degree)), on each level every node linked to its `degree`
+    nearest nodes of that level (L2, ties to the lower position) plus two
+    random ones, and on level 0 also to the next position (so every node is
+    reachable), the entry the first node of the top level.  Returns
+    (max_level, entry, offsets, neighbors) in the layout of
+    hnsw_rabitq_search."""
+    rng = np.random.default_rng(seed)
+    n = vectors.shape[0]
+    ml = ml if ml is not None else 1.0 / np.log(max(degree, 2))
+    levels = np.floor(-np.log(rng.random(n) + 1e-12) * ml).astype(np.int64)
+    max_level = int(levels.max())
+    v = vectors.astype(np.float64)
+    sq = (v * v).sum(axis=1)
+    offsets = np.zeros((max_level + 1, n + 1), np.int64)
+    lists = []
+    for level in range(max_level + 1):
+        nodes = np.nonzero(levels >= level)[0]
+        adj = [np.zeros(0, np.int32) for _ in range(n)]
+        if nodes.size > 1:
+            for start in range(0, nodes.size, 2048):
+                blk = nodes[start:start + 2048]
+                dist = sq[blk][:, None] + sq[nodes][None, :] - 2.0 * v[blk] @ v[nodes].T
+                for i, p in enumerate(blk):
+                    dist[i, start + i] = np.inf
+                    take = min(degree, nodes.size - 1)
+                    near = nodes[np.lexsort((nodes, dist[i]))[:take]]
+                    extra = rng.choice(nodes, size=min(2, nodes.size), replace=False)
+                    if level == 0:
+                        extra = np.append(extra, (p + 1) % n)
+                    extra = extra[(extra != p) & ~np.isin(extra, near)]
+                    adj[p] = np.concatenate([near, extra]).astype(np.int32)
+        counts = np.array([a.size for a in adj], np.int64)
+        offsets[level, 1:] = np.cumsum(counts)
+        lists.append(np.concatenate(adj) if counts.sum() else np.zeros(0, np.int32))
+    base = 0
+    flat = []
+    for level in range(max_level + 1):
+        offsets[level] += base
+        base += lists[level].size
+        flat.append(lists[level])
+    entry = int(np.nonzero(levels == max_level)[0][0])
+    return max_level, entry, offsets.reshape(-1), np.concatenate(flat).astype(np.int32)
 
 
 class ReferenceFloats:

@@ -16,6 +16,7 @@
 #include "xvec_oracle.h"
 
 #include <algorithm>
+#include <queue>
 #include <atomic>
 #include <cmath>
 #include <cstring>
@@ -1941,4 +1942,200 @@ extern "C" int xo_rabitq_search(int metric, int32_t d, const float* centroids, i
                                originals, keys, n, queries, nq, k, candidate_count, refine,
                                radius, bitmap, threads, out_keys, out_scores, out_counts,
                                out_status);
+}
+
+// ---------------------------------------------------------------------------
+// HNSW-RaBitQ graph search (hnsw_rabitq.go:589-612 searchPrepared, :644-671
+// searchRaBitQLayer, :673-737 searchRaBitQBase, :739-757 node order and
+// acceptance, :780-801 refinePrepared) over a given graph.  The graph: levels
+// 0..max_level, node p's level-L neighbours at
+// neighbors[offsets[L (n + 1) + p] .. offsets[L (n + 1) + p + 1]).
+// ---------------------------------------------------------------------------
+namespace {
+struct GraphNode {
+  float score;
+  uint64_t key;
+  int64_t pos;
+};
+// raBitQNodeBetter (:739-744): lower estimate, ties to the lower key.
+inline bool node_better(const GraphNode& a, const GraphNode& b) {
+  if (a.score == b.score) return a.key < b.key;
+  return a.score < b.score;
+}
+struct BestOnTop {
+  bool operator()(const GraphNode& a, const GraphNode& b) const { return node_better(b, a); }
+};
+struct WorstOnTop {
+  bool operator()(const GraphNode& a, const GraphNode& b) const { return node_better(a, b); }
+};
+// EstimateCoarse with its lower bound (rabitq.go:421-430, 464-476).
+int coarse_with_lower(const float* rot, int32_t padded, double sum, const double* gadd,
+                      const double* gerr, const uint8_t* bits, const xo_rabitq_factors* f,
+                      float* dist, float* lower) {
+  double dot = 0;
+  for (int32_t i = 0; i < padded; ++i)
+    if (bits[i / 8] & (1u << (i % 8))) dot += (double)rot[i];
+  const double centered = dot - .5 * sum;
+  const double d = f->coarse_add + gadd[f->cluster] + f->coarse_rescale * centered;
+  const double eb = f->coarse_error * gerr[f->cluster];
+  const double maxf = 3.40282346638528859811704183484516925440e+38;
+  if (std::isnan(d) || std::isinf(d) || std::isnan(eb) || std::isinf(eb) || eb < 0)
+    return XO_INVALID_ARGUMENT;
+  if (std::fabs(d) > maxf || eb > maxf) return XO_OVERFLOW;
+  if (d - eb < -maxf || d + eb > maxf) return XO_OVERFLOW;
+  *dist = (float)d;
+  *lower = (float)(d - eb);
+  return XO_OK;
+}
+}  // namespace
+
+extern "C" int xo_hnsw_rabitq_search(
+    int metric, int32_t d, const float* centroids, int32_t nc, const uint8_t* signs,
+    int32_t total_bits, const uint8_t* binary_codes, const uint8_t* extra_codes,
+    const xo_rabitq_factors* factors, const float* originals, const uint64_t* keys, int64_t n,
+    int32_t max_level, int64_t entry, const int64_t* offsets, const int32_t* neighbors,
+    const float* queries, int32_t nq, int32_t k, int32_t ef, int32_t refine, float radius,
+    const uint32_t* bitmap, int32_t threads, uint64_t* out_keys, float* out_scores,
+    int32_t* out_counts, int32_t* out_status) {
+  int st0 = validate_options(k, radius);
+  if (st0 != XO_OK) return st0;
+  if (ef <= 0 || ef > 2048) return XO_INVALID_ARGUMENT;
+  const int32_t padded = xo_rabitq_padded_dimension(d);
+  const int32_t bytes = padded / 8;
+  const int64_t xbytes = ((int64_t)padded * (total_bits - 1) + 7) / 8;
+  std::vector<int32_t> status(nq, XO_OK);
+  auto public_score = [&](float dist) { return metric == XO_IP ? 1.0f - dist : dist; };
+  parallel_for(nq, threads, [&](int64_t q) {
+    const float* query = queries + q * d;
+    std::vector<float> rot(padded);
+    std::vector<double> gadd(nc), gerr(nc);
+    double sum;
+    int st = xo_rabitq_prepare_query(metric, d, centroids, nc, signs, query, rot.data(), &sum,
+                                     gadd.data(), gerr.data());
+    std::vector<Result> res;
+    auto full = [&](int64_t p, float* dist) {
+      return xo_rabitq_estimate(rot.data(), padded, sum, gadd.data(), gerr.data(), total_bits,
+                                binary_codes + p * bytes,
+                                total_bits > 1 ? extra_codes + p * xbytes : nullptr,
+                                &factors[p], dist);
+    };
+    auto coarse = [&](int64_t p, float* dist, float* lower) {
+      return coarse_with_lower(rot.data(), padded, sum, gadd.data(), gerr.data(),
+                               binary_codes + p * bytes, &factors[p], dist, lower);
+    };
+    if (st == XO_OK && n > 0) {
+      // The approximate stage's size: candidateCount with refine (:579),
+      // else TopK; the base layer keeps max(ef, that).
+      const int64_t top = refine ? std::min<int64_t>(n, std::max(k, ef)) : k;
+      const int64_t capacity = std::max<int64_t>(ef, top);
+      // acceptRaBitQNode (:753-757): the filter, and without refine the radius
+      // on the public score.
+      auto accept = [&](const GraphNode& v) {
+        if (!filter_pass(bitmap, v.pos)) return false;
+        return refine ? true : within_radius(metric, public_score(v.score), radius);
+      };
+      // searchRaBitQLayer on levels max_level .. 1 (coarse estimates).
+      int64_t cur = entry;
+      float cur_dist = 0, lo = 0;
+      for (int32_t level = max_level; level > 0 && st == XO_OK; --level) {
+        st = coarse(cur, &cur_dist, &lo);
+        bool changed = true;
+        while (st == XO_OK && changed) {
+          changed = false;
+          // Go's range takes the list of the node the pass starts from, even
+          // when the pass moves on to a neighbour.
+          const int64_t* off = offsets + (int64_t)level * (n + 1);
+          const int64_t first = off[cur], last = off[cur + 1];
+          for (int64_t e = first; e < last && st == XO_OK; ++e) {
+            const int64_t nb = neighbors[e];
+            float cd, cl;
+            st = coarse(nb, &cd, &cl);
+            if (st != XO_OK) break;
+            if (cd < cur_dist || (cd == cur_dist && nb < cur)) {
+              cur = nb;
+              cur_dist = cd;
+              changed = true;
+            }
+          }
+        }
+      }
+      std::vector<GraphNode> nodes;
+      if (st == XO_OK) {
+        // searchRaBitQBase (:673-737).
+        std::vector<uint8_t> visited((size_t)n, 0);
+        std::priority_queue<GraphNode, std::vector<GraphNode>, BestOnTop> frontier;
+        std::priority_queue<GraphNode, std::vector<GraphNode>, WorstOnTop> accepted;
+        float sd;
+        st = full(cur, &sd);
+        if (st == XO_OK) {
+          GraphNode start{sd, keys[cur], cur};
+          visited[cur] = 1;
+          frontier.push(start);
+          if (accept(start)) accepted.push(start);
+          const int64_t* off0 = offsets;
+          while (!frontier.empty() && st == XO_OK) {
+            GraphNode c = frontier.top();
+            frontier.pop();
+            if ((int64_t)accepted.size() >= capacity && !accepted.empty() &&
+                node_better(accepted.top(), c))
+              break;
+            for (int64_t e = off0[c.pos]; e < off0[c.pos + 1]; ++e) {
+              const int64_t nb = neighbors[e];
+              if (visited[nb]) continue;
+              visited[nb] = 1;
+              float cd, cl;
+              st = coarse(nb, &cd, &cl);
+              if (st != XO_OK) break;
+              if ((int64_t)accepted.size() >= capacity && !accepted.empty() &&
+                  cl >= accepted.top().score)
+                continue;
+              float fd;
+              st = full(nb, &fd);
+              if (st != XO_OK) break;
+              GraphNode v{fd, keys[nb], nb};
+              if ((int64_t)accepted.size() < capacity || accepted.empty() ||
+                  node_better(v, accepted.top())) {
+                frontier.push(v);
+                if (accept(v)) {
+                  accepted.push(v);
+                  if ((int64_t)accepted.size() > capacity) accepted.pop();
+                }
+              }
+            }
+          }
+        }
+        while (!accepted.empty()) {
+          nodes.push_back(accepted.top());
+          accepted.pop();
+        }
+        std::reverse(nodes.begin(), nodes.end());  // best first
+        if ((int64_t)nodes.size() > top) nodes.resize((size_t)top);
+      }
+      if (st == XO_OK) {
+        if (!refine) {
+          for (auto& v : nodes) res.push_back(Result{v.key, public_score(v.score)});
+        } else {
+          // refinePrepared: exact fp32 top-k of the candidates' originals.
+          std::vector<int64_t> cpos;
+          for (auto& v : nodes) cpos.push_back(v.pos);
+          st = validate_query(metric, query, d);
+          if (st == XO_OK)
+            st = topk_scan(metric, (int64_t)cpos.size(), k, radius, nullptr, keys, cpos.data(),
+                           [&](int64_t pos, float* s) {
+                             return prevalidated(metric, originals + pos * d, query, d, s);
+                           },
+                           &res);
+        }
+      }
+    }
+    status[q] = st;
+    if (st != XO_OK) res.clear();
+    write_results(res, k, (int32_t)q, out_keys, out_scores, out_counts);
+  });
+  int first = XO_OK;
+  for (int32_t q = 0; q < nq; ++q) {
+    if (out_status) out_status[q] = status[q];
+    if (first == XO_OK) first = status[q];
+  }
+  return first;
 }

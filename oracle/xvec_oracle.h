@@ -239,6 +239,20 @@ int xo_rabitq_search(int metric, int32_t d, const float* centroids, int32_t nc,
                      const uint32_t* filter_bitmap, int32_t threads, uint64_t* out_keys,
                      float* out_scores, int32_t* out_counts, int32_t* out_status);
 
+
+/* HNSW-RaBitQ graph search (hnsw_rabitq.go:589-801) over a given graph: node
+ * p's level-L neighbours at neighbors[offsets[L (n+1) + p] .. offsets[L (n+1) + p + 1]).
+ * Results as xo_rabitq_search_bits. */
+int xo_hnsw_rabitq_search(int metric, int32_t d, const float* centroids, int32_t nc,
+                          const uint8_t* signs, int32_t total_bits, const uint8_t* binary_codes,
+                          const uint8_t* extra_codes, const xo_rabitq_factors* factors,
+                          const float* originals, const uint64_t* keys, int64_t n,
+                          int32_t max_level, int64_t entry, const int64_t* offsets,
+                          const int32_t* neighbors, const float* queries, int32_t nq, int32_t k,
+                          int32_t ef, int32_t refine, float radius, const uint32_t* bitmap,
+                          int32_t threads, uint64_t* out_keys, float* out_scores,
+                          int32_t* out_counts, int32_t* out_status);
+
 #ifdef __cplusplus
 }
 #endif

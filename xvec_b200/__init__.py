@@ -65,6 +65,7 @@ EXPORTED_SYMBOLS = (
     "xvec_gpu_sharded_search_device", "xvec_gpu_sharded_search",
     "xvec_gpu_set_wait_limit_ns",
     "xvec_gpu_rotation_signs", "xvec_gpu_rotate", "xvec_gpu_rotate_device",
+    "xvec_gpu_rabitq_set_graph",
 )
 
 
@@ -85,7 +86,8 @@ class SearchOpts(ctypes.Structure):
                 ("nprobe", ctypes.c_int32), ("refine_scale", ctypes.c_float),
                 ("ef", ctypes.c_int32), ("refine", ctypes.c_int32),
                 ("filter_bitmap", ctypes.c_void_p), ("filter_words", ctypes.c_int64),
-                ("stream", ctypes.c_void_p), ("cancel_flag", ctypes.c_void_p)]
+                ("stream", ctypes.c_void_p), ("cancel_flag", ctypes.c_void_p),
+                ("linear", ctypes.c_int32)]
 
 
 class Stats(ctypes.Structure):
@@ -158,6 +160,7 @@ def _load() -> ctypes.CDLL:
                                                    vp, vp, vp]
     lib.xvec_gpu_sharded_search.argtypes = [vp, vp, i32, vp, i32, ctypes.POINTER(SearchOpts), vp,
                                             vp, vp]
+    lib.xvec_gpu_rabitq_set_graph.argtypes = [vp, i32, i64, vp, vp, i64]
     lib.xvec_gpu_rotation_signs.argtypes = [ctypes.c_char_p, ctypes.c_char_p, i32, i32, i32, vp,
                                             i64]
     lib.xvec_gpu_rotate.argtypes = [i32, vp, i64, i32, vp, i64, vp, i32]
@@ -273,6 +276,7 @@ class SearchOptions:
     refine_scale: float = 0.0            # > 0: UseRefiner with this ScaleFactor (SQ8)
     ef: int = 300                        # HNSWRaBitQSearchOptions.EF (DefaultHNSWEFSearch)
     refine: bool = True                  # HNSWRaBitQSearchOptions.Refine
+    linear: bool = False                 # HNSWRaBitQSearchOptions.Linear (with a graph)
 
 
 def bitmap_from_predicate(n: int, keys: Sequence[int], predicate: Callable[[int], bool]) -> np.ndarray:
@@ -349,6 +353,7 @@ class _Index:
         o.refine_scale = options.refine_scale
         o.ef = options.ef
         o.refine = 1 if options.refine else 0
+        o.linear = 1 if options.linear else 0
         if device_filter_ptr is not None:
             o.filter_bitmap = device_filter_ptr
             o.filter_words = (len(self) + 31) // 32
@@ -603,10 +608,26 @@ class Int4QuantizedIVFIndex(IVFIndex):
 
 
 class RaBitQIndex(_Index):
-    """RaBitQ linear scan with exact refinement (hnsw_rabitq.go:539-642, 780-801)
-    over codes of RaBitQModelState.TotalBits bits (one bit: EstimateCoarse;
-    more: Estimate on the full codes, rabitq.go:421-446)."""
+    """HNSWRaBitQIndex search with exact refinement (hnsw_rabitq.go:539-642,
+    780-801) over codes of RaBitQModelState.TotalBits bits (one bit:
+    EstimateCoarse; more: Estimate on the full codes, rabitq.go:421-446): the
+    linear scan, or with a graph (set_graph) the graph walk of
+    searchPrepared (hnsw_rabitq.go:589-737)."""
     kind = INDEX_RABITQ
+
+    def set_graph(self, max_level: int, entry: int, offsets, neighbors) -> None:
+        """The HNSW graph over the insertion positions (xvec_gpu_rabitq_set_graph):
+        node p's level-L neighbours at neighbors[offsets[L (n + 1) + p] ..
+        offsets[L (n + 1) + p + 1]); max_level = -1 removes the graph."""
+        if max_level < 0:
+            _check(_lib.xvec_gpu_rabitq_set_graph(self._h, -1, 0, None, None, 0))
+            return
+        offsets = np.ascontiguousarray(offsets, np.int64)
+        neighbors = np.ascontiguousarray(neighbors, np.int32)
+        self._graph = (offsets, neighbors)
+        _check(_lib.xvec_gpu_rabitq_set_graph(self._h, max_level, entry, offsets.ctypes.data,
+                                              neighbors.ctypes.data if neighbors.size else None,
+                                              neighbors.size))
 
     def set_model(self, centroids, rotation_signs, total_bits: int = 1,
                   extra_scale: float = 0.0) -> None:

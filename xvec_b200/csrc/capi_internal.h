@@ -250,6 +250,13 @@ struct xvec_gpu_index {
   int32_t rq_total_bits = 1;
   double rq_extra_scale = 0.0;
   xvec::DeviceBuffer rq_values;
+  // HNSW-RaBitQ graph (xvec_gpu_rabitq_set_graph) over hnsw_n positions:
+  // levels 0..hnsw_max_level (-1: none), node p's level-L neighbours at
+  // hnsw_nbrs[hnsw_offsets[L (hnsw_n + 1) + p] .. hnsw_offsets[L (hnsw_n + 1) + p + 1]).
+  int32_t hnsw_max_level = -1;
+  int64_t hnsw_entry = 0, hnsw_n = 0;
+  xvec::DeviceBuffer hnsw_offsets;          // int64
+  xvec::DeviceBuffer hnsw_nbrs;             // int32
   // TotalBits 2..8: the code values again as int8 v - 128 [n][padded] (the
   // INT8 tensor-core operand); rq_fast's w slot holds 128 sum(v - 128).
   xvec::DeviceBuffer rq_vplane;

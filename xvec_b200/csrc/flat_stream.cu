@@ -47,6 +47,13 @@ constexpr int kStreamMaxKp = 128;   // candidate list length (kp) the scan serve
 constexpr int kStreamSlack = 32;    // list entries beyond kp before a compaction
 constexpr int kSampleStep = 64;     // the sample pass reads every 64th row
 
+// The queries in shared memory with 4 floats of padding after every 32: the
+// 16-byte chunk loads of a lane group (chunks j, j + 1, ... of one query)
+// then fall on distinct banks.  A chunk (8 FP16 or 4 FP32 elements) never
+// straddles the padding.
+__host__ __device__ __forceinline__ int qpad(int i) { return i + (i >> 5) * 4; }
+__host__ __device__ __forceinline__ int qstride(int d) { return qpad(d) + 4; }
+
 // 16 bytes of a row as floats.
 __device__ __forceinline__ void unpack16(const uint4& v, float* x, const __half*) {
   const __half2* h = reinterpret_cast<const __half2*>(&v);
@@ -147,8 +154,9 @@ __global__ void __launch_bounds__(kStreamThreads, 1) flat_stream_kernel(
     uint64_t* __restrict__ out_sat, int* __restrict__ q_flags) {
   extern __shared__ __align__(16) unsigned char stream_smem[];
   const int lcap = kp + kStreamSlack;
-  float* qs = reinterpret_cast<float*>(stream_smem);                        // [nq][d]
-  uint64_t* lists = reinterpret_cast<uint64_t*>(qs + (size_t)kStreamMaxQ * d);  // [W][nq][lcap]
+  const int qst = qstride(d);
+  float* qs = reinterpret_cast<float*>(stream_smem);                     // [nq][qst], padded
+  uint64_t* lists = reinterpret_cast<uint64_t*>(qs + (size_t)kStreamMaxQ * qst);  // [W][nq][lcap]
   uint64_t* mbuf = lists + (size_t)kStreamWarps * kStreamMaxQ * lcap;         // [W * lcap]
   int* hists = reinterpret_cast<int*>(mbuf + (size_t)kStreamWarps * lcap);   // [W][256]
   __shared__ int s_cnt[kStreamWarps][kStreamMaxQ];
@@ -164,7 +172,10 @@ __global__ void __launch_bounds__(kStreamThreads, 1) flat_stream_kernel(
   const int elems = 16 / (int)sizeof(RowT);
   const int nchunks = d / elems;
 
-  for (int i = threadIdx.x; i < nq * d; i += kStreamThreads) qs[i] = qf[i];
+  for (int i = threadIdx.x; i < nq * d; i += kStreamThreads) {
+    const int q = i / d, e = i - q * d;
+    qs[q * qst + qpad(e)] = qf[i];
+  }
   if (threadIdx.x < kStreamMaxQ) s_nonfinite[threadIdx.x] = 0;
   __syncthreads();
 
@@ -206,9 +217,9 @@ __global__ void __launch_bounds__(kStreamThreads, 1) flat_stream_kernel(
 #pragma unroll
           for (int q = 0; q < kStreamMaxQ; ++q) {
             if (q < nq) {
-              // 16-byte aligned: d is a multiple of the chunk's elements.
+              // 16-byte aligned: d and qpad keep multiples of 4 floats.
               const float4* qq =
-                  reinterpret_cast<const float4*>(qs + (size_t)q * d + (size_t)c * elems);
+                  reinterpret_cast<const float4*>(qs + (size_t)q * qst + qpad(c * elems));
 #pragma unroll
               for (int e4 = 0; e4 < 4 / (int)sizeof(RowT); ++e4) {  // float4s per chunk
                 const float4 w = qq[e4];
@@ -316,7 +327,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) flat_stream_kernel(
 template <typename RowT>
 size_t stream_smem_bytes(int d, int kp) {
   const int lcap = kp + kStreamSlack;
-  return (size_t)kStreamMaxQ * d * 4 + (size_t)kStreamWarps * kStreamMaxQ * lcap * 8 +
+  return (size_t)kStreamMaxQ * qstride(d) * 4 + (size_t)kStreamWarps * kStreamMaxQ * lcap * 8 +
          (size_t)kStreamWarps * lcap * 8 + (size_t)kStreamWarps * 256 * 4;
 }
 

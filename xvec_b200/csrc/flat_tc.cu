@@ -65,10 +65,6 @@ constexpr uint32_t kTileABytes = kBM * kBK * 2;  // 16 KB
 constexpr int kModeSq8 = 16;
 constexpr int kModeRaBitQ = 32;
 constexpr int kModeSplit = 64;
-// kModeRaBitQFull: multi-bit RaBitQ, the rows' full code values (bfloat16,
-// exact up to 256) against the query's bfloat16 high and low parts, two MMAs
-// per k-step into one fp32 accumulator; the RaBitQ epilogue on the float dot.
-constexpr int kModeRaBitQFull = 128;
 // kModeRaBitQ8: multi-bit RaBitQ on kind::i8, the rows' code values as the
 // int8 plane v - 128 against the query as 16-bit integers w = round(q / s)
 // split into two int8 planes, w = 256 h + l + 128 (h, l signed): two MMAs per
@@ -430,13 +426,12 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
     int* __restrict__ part_counts, uint64_t* __restrict__ part_sat, int* __restrict__ q_flags,
     int* __restrict__ status, uint64_t wait_ns) {
   constexpr bool RQ1 = MODE == kModeRaBitQ;   // RaBitQ code planes, integer queries
-  constexpr bool RQF = MODE == kModeRaBitQFull;  // multi-bit values, bfloat16 query parts
   constexpr bool RQ8 = MODE == kModeRaBitQ8;     // multi-bit values, 16-bit integer query
-  constexpr bool RQ = RQ1 || RQF || RQ8;         // the RaBitQ epilogue
+  constexpr bool RQ = RQ1 || RQ8;                // the RaBitQ epilogue
   constexpr bool SQ = (MODE & kModeSq8) != 0 && !RQ8;  // INT8 codes (SQ8) instead of FP16 rows
   constexpr bool SPLIT = (MODE & kModeSplit) != 0 && !RQ8;  // bfloat16 high/low parts of float32
   constexpr bool I8 = SQ || RQ1 || RQ8;         // kind::i8 operands
-  constexpr bool TWO_A = RQF || RQ8;            // stage: A, B, second A
+  constexpr bool TWO_A = RQ8;                   // stage: A, B, second A
   constexpr int METRIC = RQ8 ? 0 : (MODE & 15);
   constexpr int kElemBytes = I8 ? 1 : 2;
   // Rows per tile: RQ8 keeps two accumulators of BN columns per buffer.
@@ -601,7 +596,7 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
             else if constexpr (I8)
               mma_s8<PAIR>(d_tmem, adesc + (uint64_t)(k * 2), bdesc + (uint64_t)(k * 2),
                            (ks > 0 || k > 0) ? 1u : 0u);
-            else if constexpr (SPLIT || RQF)
+            else if constexpr (SPLIT)
               mma_bf16<PAIR>(d_tmem, adesc + (uint64_t)(k * 2), bdesc + (uint64_t)(k * 2),
                              (ks > 0 || k > 0) ? 1u : 0u);
             else
@@ -616,13 +611,6 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
             for (int k = 0; k < 4; ++k)
               mma_s8<PAIR, BN>(d_tmem + BN, a2desc + (uint64_t)(k * 2), bdesc + (uint64_t)(k * 2),
                                (ks > 0 || k > 0) ? 1u : 0u);
-          }
-          if constexpr (RQF) {
-            // The low query part against the same row values.
-            const uint64_t a2desc = smem_desc_sw128(a_src + kTileABytes + S::kTileBBytes);
-#pragma unroll
-            for (int k = 0; k < 4; ++k)
-              mma_bf16<PAIR>(d_tmem, a2desc + (uint64_t)(k * 2), bdesc + (uint64_t)(k * 2), 1u);
           }
           if constexpr (SPLIT) {
             // The high query part against the low row part, and the low
@@ -808,15 +796,14 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
         };
         const float4* a4 = reinterpret_cast<const float4*>(meta_aux + c * 32);
         if constexpr (RQ) {
-          // RaBitQRanker (rabitq.cu): add + gAdd[cluster] + rescale (dot - sum/2);
-          // multi-bit: full add + gAdd[cluster] + full rescale (dot + center sum)
-          // with rq_q.x = -(center sum).
+          // RaBitQRanker (rabitq.cu): add + gAdd[cluster] + rescale (dot - sum/2)
+          // with dot = scale * the exact integer dot.
           if (vmask != 0u) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
               const float4 r = meta4[c * 32 + j];
               const float g = gadd_tab[__float_as_int(r.z) * 32 + lane];
-              const float dot = RQF ? __uint_as_float(cur[j]) : (float)(int)cur[j] * rq_q.y;
+              const float dot = (float)(int)cur[j] * rq_q.y;
               const float rank = fmaf(r.y, dot - rq_q.x, r.x + g);
               if (((vmask >> j) & 1u) && !(rank > thr_f)) {
                 if (!isfinite(rank)) {
@@ -1018,11 +1005,10 @@ cudaError_t launch_tc(int nq, const void* queries, const void* queries2, int nc,
                       uint64_t* part_sat, int* q_flags, int* status, cudaStream_t stream) {
   const int qblocks = (nq + tc::kBM - 1) / tc::kBM;
   const bool pair = flat_tc_pairs(nq);
-  constexpr bool RQF = MODE == tc::kModeRaBitQFull;
   constexpr bool RQ8 = MODE == tc::kModeRaBitQ8;
-  constexpr bool RQ = MODE == tc::kModeRaBitQ || RQF || RQ8;
+  constexpr bool RQ = MODE == tc::kModeRaBitQ || RQ8;
   constexpr bool SPLIT = (MODE & tc::kModeSplit) != 0 && !RQ8;
-  constexpr bool TWO_A = RQF || RQ8;
+  constexpr bool TWO_A = RQ8;
   constexpr int BN = RQ8 ? tc::kBN / 2 : tc::kBN;
   using SP = tc::Shape<true, RQ, SPLIT, TWO_A, BN>;
   using SS = tc::Shape<false, RQ, SPLIT, TWO_A, BN>;
@@ -1165,26 +1151,6 @@ cudaError_t launch_rabitq_scan_tc(const int8_t* q_int, int nq, const int8_t* pla
                                     reinterpret_cast<const float*>(q_terms), q_gadd, gthr, bitmap, num_parts, kp, list_base,
                                     num_lists, cand, part_counts, part_sat, q_flags, status,
                                     stream);
-}
-
-cudaError_t launch_rabitq_full_scan_tc(const __nv_bfloat16* q_hi, const __nv_bfloat16* q_lo,
-                                       int nq, const __nv_bfloat16* values, int64_t n,
-                                       int padded, const float4* row_info,
-                                       const uint32_t* keyrank, const float2* q_terms,
-                                       const float* q_gadd, int nc, unsigned long long* gthr,
-                                       const uint32_t* bitmap, int num_parts, int kp,
-                                       int list_base, int num_lists, uint64_t* cand,
-                                       int* part_counts, uint64_t* part_sat, int* q_flags,
-                                       int* status, cudaStream_t stream) {
-  if (nc > tc::kRaBitQMaxClusters || !flat_tc_supported(padded, values, q_hi) ||
-      (uintptr_t)q_lo % 16 != 0)
-    return cudaErrorInvalidValue;
-  return launch_tc<tc::kModeRaBitQFull>(nq, q_hi, q_lo, nc, values, nullptr, n, padded,
-                                        (int64_t)padded, 2,
-                                        reinterpret_cast<const float*>(row_info), keyrank,
-                                        reinterpret_cast<const float*>(q_terms), q_gadd, gthr,
-                                        bitmap, num_parts, kp, list_base, num_lists, cand,
-                                        part_counts, part_sat, q_flags, status, stream);
 }
 
 cudaError_t launch_rabitq8_scan_tc(const int8_t* q_planes, int nq, const int8_t* vplane,

@@ -94,19 +94,6 @@ cudaError_t launch_rabitq8_scan_tc(const int8_t* q_planes, int nq, const int8_t*
                                    uint64_t* part_sat, int* q_flags, int* status,
                                    cudaStream_t stream);
 bool rabitq8_tc_supported(int padded, const void* vplane, const void* q_planes);
-// Multi-bit RaBitQ: the rows' full code values as bfloat16 [n][padded]
-// against the query's bfloat16 high and low parts ([nq][padded] each);
-// q_terms[q].x = -(center sum) (float), the fast rank fmaf(rescale, dot -
-// q_terms.x, add + gAdd).
-cudaError_t launch_rabitq_full_scan_tc(const __nv_bfloat16* q_hi, const __nv_bfloat16* q_lo,
-                                       int nq, const __nv_bfloat16* values, int64_t n,
-                                       int padded, const float4* row_info,
-                                       const uint32_t* keyrank, const float2* q_terms,
-                                       const float* q_gadd, int nc, unsigned long long* gthr,
-                                       const uint32_t* bitmap, int num_parts, int kp,
-                                       int list_base, int num_lists, uint64_t* cand,
-                                       int* part_counts, uint64_t* part_sat, int* q_flags,
-                                       int* status, cudaStream_t stream);
 // Most clusters the RaBitQ tensor-core epilogue takes.
 int rabitq_tc_max_clusters();
 // True when the RaBitQ tensor-core scan can take this layout.

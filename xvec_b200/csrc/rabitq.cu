@@ -91,6 +91,10 @@ constexpr double kU = 5.9604644775390625e-8;  // 2^-24
 constexpr int kRaBitQInvalid = 8;      // ErrInvalidRaBitQCode
 constexpr int kRaBitQOverflow = 16;    // ErrQuantizationOverflow
 constexpr int kRaBitQFullCheck = 32;   // estimates may fail: check every row
+constexpr int kRaBitQGraphFull = 64;   // the graph walk's frontier outgrew its buffer
+// DefaultHNSWBruteForceThreshold (hnsw.go:592): indexes of at most this many
+// rows are scanned linearly even with a graph.
+constexpr int64_t kHNSWBruteForce = 1000;
 inline unsigned blocks_of(int64_t n, int t = 256) { return (unsigned)((n + t - 1) / t); }
 
 // normalizeRaBitQVector (rabitq.go:514-526) of v[0, d) in shared memory.
@@ -383,12 +387,11 @@ __global__ void rabitq_prep_query_kernel(const float* queries, int nq, int d, in
                                          float* q_fast_sum, float* q_fast_gadd, float* q_eps,
                                          int* q_exact, int* q_status, int* q_flags,
                                          int8_t* q_int, float2* q_terms, int total_bits,
-                                         __nv_bfloat16* q_bf, int8_t* q_planes8) {
-  // total_bits > 1: q_bf holds the rotated queries' bfloat16 high parts
-  // [nq][padded] followed by their low parts [nq][padded] (the multi-bit
-  // FFMA scan's input) and q_int is unused.  q_planes8 (optional, the
-  // multi-bit INT8 tensor-core scan): the 16-bit integer query as planes
-  // [2][nq][padded] (h, then l); q_terms and q_eps then follow that form.
+                                         int8_t* q_planes8) {
+  // total_bits > 1: q_int is unused; q_planes8 (optional, the multi-bit INT8
+  // tensor-core scan): the 16-bit integer query as planes [2][nq][padded]
+  // (h, then l); q_terms and q_eps then follow that form, else the FFMA
+  // scan's.
   const bool multi = total_bits > 1;
   const bool int8_form = multi && q_planes8 != nullptr;
   const double vmax = (double)((1 << total_bits) - 1);  // largest code value
@@ -408,8 +411,6 @@ __global__ void rabitq_prep_query_kernel(const float* queries, int nq, int d, in
     for (int i = threadIdx.x; i < padded; i += blockDim.x) {
       q_rot[(int64_t)q * padded + i] = 0.f;
       if (multi) {
-        q_bf[(int64_t)q * padded + i] = __float2bfloat16_rn(0.f);
-        q_bf[((int64_t)nq + q) * padded + i] = __float2bfloat16_rn(0.f);
         if (int8_form) {
           q_planes8[(int64_t)q * padded + i] = 0;
           q_planes8[((int64_t)nq + q) * padded + i] = 0;
@@ -494,15 +495,6 @@ __global__ void rabitq_prep_query_kernel(const float* queries, int nq, int d, in
   }
   __syncthreads();
   if (multi) {
-    // bfloat16 high and low parts: hi = bf16(v), lo = bf16(v - hi) (v - hi is
-    // exact in float32).
-    __nv_bfloat16* qhi = q_bf + (int64_t)q * padded;
-    __nv_bfloat16* qlo = q_bf + ((int64_t)nq + q) * padded;
-    for (int i = threadIdx.x; i < padded; i += blockDim.x) {
-      const __nv_bfloat16 hi = __float2bfloat16_rn(v[i]);
-      qhi[i] = hi;
-      qlo[i] = __float2bfloat16_rn(v[i] - __bfloat162float(hi));
-    }
     if (int8_form) {
       // w = round(v / scale), |w| <= 32767, as h = floor(w / 256) and
       // l = (w mod 256) - 128; sum w, sum |w| and the rounding bound
@@ -587,10 +579,12 @@ __global__ void rabitq_prep_query_kernel(const float* queries, int nq, int d, in
                              kU * (5.0 * scale * dpmag + x) * 1.01;
       e = maxR * (dot_err + kU * csum) + 6.0 * kU * (maxA + maxg + maxR * (vmax * S1 + csum));
     } else if (multi) {
-      // The bfloat16 split (|v - hi - lo| <= 2^-16 |v|, plus underflow) and
-      // an fp32 accumulation of 2 padded exact products on the tensor cores
-      // (the FFMA scan's float32 sum of padded terms is within the same
-      // bound), the float32 roundings of the terms and of the formula.
+      // The FFMA scan (TotalBits 9, or clusters beyond the tensor-core
+      // epilogue's table): a float32 sum of padded products of exact 16-bit
+      // code values with the float32 query, bounded here with a margin for
+      // any accumulation order (2 padded + 8 roundings, plus 2^-16 relative
+      // and the underflow of each term), then the float32 roundings of the
+      // terms and of the formula.
       const double dot_err =
           vmax * (S1 * (ldexp(1.0, -16) + (2.0 * padded + 8.0) * ldexp(1.0, -23) * 1.01) +
                   (double)padded * ldexp(1.0, -126));
@@ -620,6 +614,7 @@ __host__ __device__ inline int rabitq_query_status(int prep, int flags, int refi
   if (prep) return prep;
   if (flags & kRaBitQInvalid) return XVEC_GPU_INVALID_ARGUMENT;
   if (flags & kRaBitQOverflow) return XVEC_GPU_OVERFLOW;
+  if (flags & kRaBitQGraphFull) return XVEC_GPU_UNSUPPORTED;
   if (refine_status) return refine_status;
   if (flags & 4) return XVEC_GPU_NON_FINITE;
   return 0;
@@ -733,6 +728,491 @@ struct RaBitQScorer {
     return within_radius(public_metric, out, radius);
   }
 };
+
+// ---------------------------------------------------------------------------
+// HNSW-RaBitQ graph walk (HNSWRaBitQIndex.searchPrepared,
+// hnsw_rabitq.go:589-612): the descent through the upper levels
+// (searchRaBitQLayer, :644-671, coarse estimates) and the base-layer search
+// (searchRaBitQBase, :673-737) over a graph the caller uploaded
+// (xvec_gpu_rabitq_set_graph).  One warp per query: the warp computes the
+// estimates of a neighbour list 32 at a time (each estimate a warp-wide
+// float64 sum, as the linear scan's exact scorer takes it), and lane 0 then
+// applies the reference's decisions to the neighbours in list order, with
+// the frontier (best first) and the accepted set (worst first) as binary
+// heaps in shared memory.  A node is the packed key (order-preserving
+// estimate << 32 | key rank), so the heaps' order is raBitQNodeBetter
+// (:739-744).  Full estimates are computed ahead for every unvisited
+// neighbour (they are pure functions), but a failure counts only where the
+// reference computes that estimate.
+// ---------------------------------------------------------------------------
+
+struct WalkArgs {
+  const uint8_t* codes;
+  const RaBitQFactors* factors;
+  const float* q_rot;
+  const double* q_sum;
+  const double* g_add;
+  const double* g_error;
+  const int* q_exact;
+  int padded, nc, total_bits;
+  const uint16_t* values;
+  int64_t n;
+  int max_level;
+  int64_t entry;
+  const int64_t* offsets;  // [(max_level + 1) (n + 1)]
+  const int32_t* nbrs;
+  const uint64_t* keys;
+  const uint32_t* keyrank;
+  const uint32_t* pos_of_kr;
+  const uint32_t* bitmap;
+  int capacity, top, refine, public_metric;
+  float radius;
+  int fcap;                 // frontier entries per warp
+  uint32_t* visited;        // [slots][words]
+  int64_t words;
+  int32_t* vlist;           // [slots][vcap]
+  int vcap;
+  int nq;
+  int stride;               // output entries per query
+  uint64_t* o_keys;
+  float* o_scores;
+  int* o_counts;
+  uint32_t* o_pos;
+  int* q_flags;
+};
+
+// EstimateCoarse (full = false) or Estimate (rabitq.go:421-446) of `row`
+// for query qi with makeRaBitQEstimate's checks (:464-476): 0, or the
+// failure flag.  Every lane gets the result.
+__device__ int walk_estimate(const WalkArgs& a, int qi, int64_t row, bool full, float* dist,
+                             float* lower) {
+  const int lane = threadIdx.x & 31;
+  const uint8_t* b = a.codes + row * (a.padded / 8);
+  const float* q = a.q_rot + (int64_t)qi * a.padded;
+  const bool multi = full && a.total_bits > 1, half = a.total_bits > 8;
+  const uint16_t* vrow = multi ? a.values + row * a.padded : nullptr;
+  auto term = [&](int i) -> double {
+    if (multi) return __dmul_rn(rabitq_value(vrow, i, half), (double)q[i]);
+    return (b[i >> 3] & (1u << (i & 7))) ? (double)q[i] : 0.0;
+  };
+  double dot = 0.0;
+  if (a.q_exact[qi]) {
+    for (int i = lane; i < a.padded; i += 32) dot = __dadd_rn(dot, term(i));
+    for (int o = 16; o > 0; o >>= 1) dot = __dadd_rn(dot, __shfl_xor_sync(kFullMask, dot, o));
+  } else {
+    if (lane == 0)
+      for (int i = 0; i < a.padded; ++i) {
+        const double t = term(i);
+        if (multi || t != 0.0 || (b[i >> 3] & (1u << (i & 7)))) dot = __dadd_rn(dot, t);
+      }
+    dot = __shfl_sync(kFullMask, dot, 0);
+  }
+  const RaBitQFactors f = a.factors[row];
+  const int64_t gi = (int64_t)qi * a.nc + f.cluster;
+  double d, eb;
+  if (multi) {
+    const double center = -(ldexp(1.0, a.total_bits - 1) - 0.5);
+    d = __dadd_rn(__dadd_rn(f.full_add, a.g_add[gi]),
+                  __dmul_rn(f.full_rescale, __dadd_rn(dot, __dmul_rn(center, a.q_sum[qi]))));
+    eb = __ddiv_rn(__dmul_rn(f.error, a.g_error[gi]), ldexp(1.0, a.total_bits - 1));
+  } else {
+    const double centered = __dsub_rn(dot, __dmul_rn(0.5, a.q_sum[qi]));
+    d = __dadd_rn(__dadd_rn(f.add, a.g_add[gi]), __dmul_rn(f.rescale, centered));
+    eb = __dmul_rn(f.error, a.g_error[gi]);
+  }
+  constexpr double kMaxF = 3.40282346638528859811704183484516925440e+38;
+  if (isnan(d) || isinf(d) || isnan(eb) || isinf(eb) || eb < 0) return kRaBitQInvalid;
+  if (fabs(d) > kMaxF || eb > kMaxF) return kRaBitQOverflow;
+  const double lo = __dsub_rn(d, eb), hi = __dadd_rn(d, eb);
+  if (lo < -kMaxF || hi > kMaxF) return kRaBitQOverflow;
+  *dist = __double2float_rn(d);
+  *lower = __double2float_rn(lo);
+  return 0;
+}
+
+__device__ __forceinline__ uint64_t walk_key(float score, uint32_t kr) {
+  return ((uint64_t)float_to_ordered(score) << 32) | kr;
+}
+
+// Binary heaps of packed keys in shared memory (lane 0 only): MIN = true
+// keeps the smallest key on top (the frontier), false the largest (the
+// accepted set).
+template <bool MIN>
+__device__ __forceinline__ bool heap_before(uint64_t a, uint64_t b) {
+  return MIN ? a < b : a > b;
+}
+template <bool MIN>
+__device__ void heap_push(uint64_t* h, int& size, uint64_t v) {
+  int i = size++;
+  while (i > 0) {
+    const int p = (i - 1) >> 1;
+    if (!heap_before<MIN>(v, h[p])) break;
+    h[i] = h[p];
+    i = p;
+  }
+  h[i] = v;
+}
+template <bool MIN>
+__device__ uint64_t heap_pop(uint64_t* h, int& size) {
+  const uint64_t top = h[0];
+  const uint64_t v = h[--size];
+  int i = 0;
+  for (;;) {
+    const int l = 2 * i + 1;
+    if (l >= size) break;
+    int c = l;
+    if (l + 1 < size && heap_before<MIN>(h[l + 1], h[l])) c = l + 1;
+    if (!heap_before<MIN>(h[c], v)) break;
+    h[i] = h[c];
+    i = c;
+  }
+  if (size > 0) h[i] = v;
+  return top;
+}
+template <bool MIN>
+__device__ void heap_build(uint64_t* h, int size) {
+  for (int s = size / 2 - 1; s >= 0; --s) {
+    const uint64_t v = h[s];
+    int i = s;
+    for (;;) {
+      const int l = 2 * i + 1;
+      if (l >= size) break;
+      int c = l;
+      if (l + 1 < size && heap_before<MIN>(h[l + 1], h[l])) c = l + 1;
+      if (!heap_before<MIN>(h[c], v)) break;
+      h[i] = h[c];
+      i = c;
+    }
+    h[i] = v;
+  }
+}
+
+// Sorts a[0, m) ascending with the warp (bitonic over the next power of two,
+// padded with all-ones keys; a has room for it).
+__device__ void warp_sort_keys(uint64_t* a, int m) {
+  const int lane = threadIdx.x & 31;
+  int p = 1;
+  while (p < m) p <<= 1;
+  for (int i = m + lane; i < p; i += 32) a[i] = kEmptyKey;
+  __syncwarp();
+  for (int k = 2; k <= p; k <<= 1)
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = lane; i < p; i += 32) {
+        const int x = i ^ j;
+        if (x > i) {
+          const uint64_t u = a[i], w = a[x];
+          const bool up = (i & k) == 0;
+          if ((u > w) == up) {
+            a[i] = w;
+            a[x] = u;
+          }
+        }
+      }
+      __syncwarp();
+    }
+}
+
+__global__ void __launch_bounds__(256) hnsw_rabitq_walk_kernel(WalkArgs a) {
+  extern __shared__ __align__(16) unsigned char walk_smem[];
+  const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5, wpb = blockDim.x >> 5;
+  // Per warp: frontier [fcap], accepted [pow2 >= capacity].
+  int acap2 = 1;
+  while (acap2 < a.capacity + 1) acap2 <<= 1;
+  uint64_t* frontier = reinterpret_cast<uint64_t*>(walk_smem) + (size_t)wib * (a.fcap + acap2);
+  uint64_t* accepted = frontier + a.fcap;
+  const int slot = blockIdx.x * wpb + wib, slots = gridDim.x * wpb;
+  uint32_t* vis = a.visited + (int64_t)slot * a.words;
+  int32_t* vl = a.vlist + (int64_t)slot * a.vcap;
+  for (int qi = slot; qi < a.nq; qi += slots) {
+    int fail = 0;
+    int nvis = 0;  // visited nodes recorded (lane 0's count is the truth)
+    // Marks node p visited; true when it was not yet (every lane calls it
+    // with its own p or -1).
+    auto mark = [&](int64_t p) -> bool {
+      bool fresh = false;
+      if (p >= 0) {
+        const uint32_t bit = 1u << (p & 31);
+        fresh = !(atomicOr(&vis[p >> 5], bit) & bit);
+      }
+      const unsigned m = __ballot_sync(kFullMask, fresh);
+      if (fresh) {
+        const int at = nvis + __popc(m & ((1u << lane) - 1));
+        if (at < a.vcap) vl[at] = (int32_t)p;
+      }
+      nvis += __popc(m);
+      return fresh;
+    };
+    // ---- upper levels: greedy descent on coarse estimates ----
+    int64_t cur = a.entry;
+    float cur_d = 0.f, lo = 0.f;
+    for (int level = a.max_level; level > 0 && !fail; --level) {
+      fail = walk_estimate(a, qi, cur, false, &cur_d, &lo);
+      bool changed = !fail;
+      while (changed && !fail) {
+        changed = false;
+        const int64_t* off = a.offsets + (int64_t)level * (a.n + 1);
+        const int64_t first = off[cur], last = off[cur + 1];
+        for (int64_t e0 = first; e0 < last && !fail; e0 += 32) {
+          const int cnt = (int)min((int64_t)32, last - e0);
+          const int64_t nb = lane < cnt ? (int64_t)a.nbrs[e0 + lane] : -1;
+          float nd = 0.f, nl = 0.f;
+          int nst = 0;
+          for (int j = 0; j < cnt; ++j) {
+            const int64_t p = __shfl_sync(kFullMask, nb, j);
+            float dj, lj;
+            const int sj = walk_estimate(a, qi, p, false, &dj, &lj);
+            if (lane == j) {
+              nd = dj;
+              nst = sj;
+            }
+          }
+          for (int j = 0; j < cnt; ++j) {
+            const int64_t p = __shfl_sync(kFullMask, nb, j);
+            const float dj = __shfl_sync(kFullMask, nd, j);
+            const int sj = __shfl_sync(kFullMask, nst, j);
+            if (sj) {
+              fail = sj;
+              break;
+            }
+            if (dj < cur_d || (dj == cur_d && p < cur)) {
+              cur = p;
+              cur_d = dj;
+              changed = true;
+            }
+          }
+        }
+      }
+    }
+    // ---- base layer ----
+    int fsize = 0, asize = 0;
+    auto accept = [&](int64_t p, float score) {
+      if (!bitmap_pass(a.bitmap, p)) return false;
+      if (a.refine) return true;
+      const float pub = a.public_metric == kMetricIP ? __fsub_rn(1.f, score) : score;
+      return within_radius(a.public_metric, pub, a.radius);
+    };
+    if (!fail) {
+      float sd, sl;
+      fail = walk_estimate(a, qi, cur, true, &sd, &sl);
+      mark(cur);
+      if (!fail && lane == 0) {
+        const uint64_t s = walk_key(sd, a.keyrank[cur]);
+        heap_push<true>(frontier, fsize, s);
+        if (accept(cur, sd)) heap_push<false>(accepted, asize, s);
+      }
+    }
+    fsize = __shfl_sync(kFullMask, fsize, 0);
+    asize = __shfl_sync(kFullMask, asize, 0);
+    __syncwarp();
+    while (fsize > 0 && !fail) {
+      uint64_t c = 0;
+      if (lane == 0) c = heap_pop<true>(frontier, fsize);
+      c = __shfl_sync(kFullMask, c, 0);
+      fsize = __shfl_sync(kFullMask, fsize, 0);
+      const uint64_t worst0 = __shfl_sync(kFullMask, asize > 0 ? accepted[0] : 0ull, 0);
+      if (asize >= a.capacity && asize > 0 && worst0 < c) break;
+      const int64_t cpos = a.pos_of_kr[(uint32_t)c];
+      const int64_t first = a.offsets[cpos], last = a.offsets[cpos + 1];
+      for (int64_t e0 = first; e0 < last && !fail; e0 += 32) {
+        const int cnt = (int)min((int64_t)32, last - e0);
+        int64_t nb = lane < cnt ? (int64_t)a.nbrs[e0 + lane] : -1;
+        // A node listed twice is taken at its first place (the reference's
+        // later occurrence finds it visited).
+        const unsigned same = __match_any_sync(kFullMask, nb);
+        if (nb >= 0 && lane != __ffs(same) - 1) nb = -2;  // a repeat within the chunk
+        const bool fresh = mark(nb >= 0 ? nb : -1);
+        float cd = 0.f, cl = 0.f, fd = 0.f;
+        int cst = 0, fst = 0;
+        const unsigned fm = __ballot_sync(kFullMask, fresh);
+        for (unsigned m = fm; m; m &= m - 1) {
+          const int j = __ffs(m) - 1;
+          const int64_t p = __shfl_sync(kFullMask, nb, j);
+          float dj, lj, fj, unused;
+          const int s1 = walk_estimate(a, qi, p, false, &dj, &lj);
+          int s2 = 0;
+          if (a.total_bits > 1)
+            s2 = walk_estimate(a, qi, p, true, &fj, &unused);
+          else
+            fj = dj;
+          if (lane == j) {
+            cd = dj;
+            cl = lj;
+            cst = s1;
+            fd = fj;
+            fst = s2;
+          }
+        }
+        (void)cd;
+        // The reference's decisions, in list order (lane 0 holds the heaps).
+        for (unsigned m = fm; m; m &= m - 1) {
+          const int j = __ffs(m) - 1;
+          const int64_t p = __shfl_sync(kFullMask, nb, j);
+          const float lj = __shfl_sync(kFullMask, cl, j);
+          const float fj = __shfl_sync(kFullMask, fd, j);
+          const int c1 = __shfl_sync(kFullMask, cst, j);
+          const int c2 = __shfl_sync(kFullMask, fst, j);
+          if (c1) {
+            fail = c1;
+            break;
+          }
+          int verdict = 0;  // 0 pruned / skipped, 1 continue, -1 failed
+          if (lane == 0) {
+            const bool full_set = asize >= a.capacity && asize > 0;
+            if (full_set && lj >= rank_of(accepted[0])) {
+              verdict = 0;
+            } else if (c2) {
+              verdict = -1;
+            } else {
+              verdict = 1;
+              const uint64_t v = walk_key(fj, a.keyrank[p]);
+              if (asize < a.capacity || asize == 0 || v < accepted[0]) {
+                if (fsize == a.fcap && asize >= a.capacity && asize > 0) {
+                  // Frontier entries worse than the worst accepted node only
+                  // end the walk when popped: drop them.
+                  int keep = 0;
+                  for (int i = 0; i < fsize; ++i)
+                    if (frontier[i] < accepted[0]) frontier[keep++] = frontier[i];
+                  fsize = keep;
+                  heap_build<true>(frontier, fsize);
+                }
+                if (fsize == a.fcap) {
+                  verdict = -2;
+                } else {
+                  heap_push<true>(frontier, fsize, v);
+                  if (accept(p, fj)) {
+                    heap_push<false>(accepted, asize, v);
+                    if (asize > a.capacity) heap_pop<false>(accepted, asize);
+                  }
+                }
+              }
+            }
+          }
+          verdict = __shfl_sync(kFullMask, verdict, 0);
+          if (verdict == -1) {
+            fail = c2;
+            break;
+          }
+          if (verdict == -2) {
+            fail = kRaBitQGraphFull;
+            break;
+          }
+        }
+        fsize = __shfl_sync(kFullMask, fsize, 0);
+        asize = __shfl_sync(kFullMask, asize, 0);
+        __syncwarp();
+      }
+    }
+    // ---- results: the accepted nodes best first, the first `top` of them ----
+    __syncwarp();
+    int count = 0;
+    if (!fail) {
+      warp_sort_keys(accepted, asize);
+      count = min(asize, a.top);
+      for (int i = lane; i < count; i += 32) {
+        const uint64_t v = accepted[i];
+        const uint32_t pos = a.pos_of_kr[(uint32_t)v];
+        const float est = rank_of(v);
+        a.o_keys[(int64_t)qi * a.stride + i] = a.keys[pos];
+        a.o_scores[(int64_t)qi * a.stride + i] =
+            (!a.refine && a.public_metric == kMetricIP) ? __fsub_rn(1.f, est) : est;
+        if (a.o_pos) a.o_pos[(int64_t)qi * a.stride + i] = pos;
+      }
+    }
+    if (lane == 0) {
+      a.o_counts[qi] = count;
+      if (fail) atomicOr(&a.q_flags[qi], fail);
+    }
+    // Clear this query's visited marks (the whole bitmap when the record
+    // overflowed).
+    __syncwarp();
+    if (nvis <= a.vcap) {
+      for (int i = lane; i < nvis; i += 32) {
+        const int32_t p = vl[i];
+        atomicAnd(&vis[p >> 5], ~(1u << (p & 31)));
+      }
+    } else {
+      for (int64_t w = lane; w < a.words; w += 32) vis[w] = 0u;
+    }
+    __syncwarp();
+  }
+}
+
+// Launches the walk for nq queries: the approximate stage's `top` nodes
+// (refine: the candidate count cc, else k) per query into o_* (stride cc).
+xvec_gpu_status rabitq_graph_walk(xvec_gpu_index* idx, int nq, int k, int ef, int cc,
+                                  bool refine, float radius, const uint32_t* d_bitmap,
+                                  const RaBitQScorer& sc, uint64_t* o_keys, float* o_scores,
+                                  int* o_counts, uint32_t* o_pos, int* q_flags, cudaStream_t s) {
+  const int64_t n = idx->n;
+  const int top = refine ? cc : k;
+  const int capacity = std::max(ef, top);
+  const int warps = capacity <= 256 ? 8 : capacity <= 1024 ? 4 : 2;
+  int acap2 = 1;
+  while (acap2 < capacity + 1) acap2 <<= 1;
+  const int per_warp = (200 * 1024 / 8) / warps;
+  const int fcap = per_warp - acap2;
+  if (fcap < 2 * capacity)
+    return set_error("HNSW-RaBitQ walk: capacity %d is beyond the supported maximum", capacity),
+           XVEC_GPU_INVALID_ARGUMENT;
+  const size_t smem = (size_t)warps * (fcap + acap2) * 8;
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, idx->device);
+  const int64_t words = (n + 31) / 32;
+  int64_t slots = std::min<int64_t>((int64_t)sms * warps, ((int64_t)nq + warps - 1) / warps * warps);
+  // The per-warp visited bitmaps stay within 2 GB.
+  while (slots > warps && slots * words * 4 > (2ll << 30)) slots -= warps;
+  const int vcap = 65536;
+  Scratch vis, vlist;
+  xvec_gpu_status st;
+  if ((st = vis.alloc((size_t)slots * words * 4, s)) ||
+      (st = vlist.alloc((size_t)slots * vcap * 4, s)))
+    return st;
+  XVEC_CUDA(cudaMemsetAsync(vis.ptr, 0, (size_t)slots * words * 4, s));
+  WalkArgs a{};
+  a.codes = sc.codes;
+  a.factors = sc.factors;
+  a.q_rot = sc.q_rot;
+  a.q_sum = sc.q_sum;
+  a.g_add = sc.g_add;
+  a.g_error = sc.g_error;
+  a.q_exact = sc.q_exact;
+  a.padded = sc.padded;
+  a.nc = sc.nc;
+  a.total_bits = sc.total_bits;
+  a.values = sc.values;
+  a.n = n;
+  a.max_level = idx->hnsw_max_level;
+  a.entry = idx->hnsw_entry;
+  a.offsets = idx->hnsw_offsets.as<int64_t>();
+  a.nbrs = idx->hnsw_nbrs.as<int32_t>();
+  a.keys = idx->keys.as<uint64_t>();
+  a.keyrank = idx->keyrank.as<uint32_t>();
+  a.pos_of_kr = idx->pos_of_kr.as<uint32_t>();
+  a.bitmap = d_bitmap;
+  a.capacity = capacity;
+  a.top = top;
+  a.refine = refine ? 1 : 0;
+  a.public_metric = idx->desc.metric;
+  a.radius = radius;
+  a.fcap = fcap;
+  a.visited = vis.as<uint32_t>();
+  a.words = words;
+  a.vlist = vlist.as<int32_t>();
+  a.vcap = vcap;
+  a.nq = nq;
+  a.stride = cc;
+  a.o_keys = o_keys;
+  a.o_scores = o_scores;
+  a.o_counts = o_counts;
+  a.o_pos = o_pos;
+  a.q_flags = q_flags;
+  XVEC_CUDA(cudaFuncSetAttribute(hnsw_rabitq_walk_kernel,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  hnsw_rabitq_walk_kernel<<<(unsigned)(slots / warps), warps * 32, smem, s>>>(a);
+  XVEC_LAUNCHED();
+  XVEC_CUDA(cudaGetLastError());
+  return XVEC_GPU_OK;
+}
 
 // Per-query status: PrepareQuery's, then the scan's, then the refine's.
 __global__ void rabitq_status_kernel(const int* q_status, const int* q_flags,
@@ -864,16 +1344,20 @@ __global__ void __launch_bounds__(kLutThreads, 1) rabitq_lut_scan_kernel(
       load_terms(i + 1);
     }
     const uint32_t* mine = stage + tid * 32;
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 4
+    float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
+    // Byte j of a word selects row (byte) of column j * 32 + w: the float
+    // offset byte * 128 is the byte shifted into bits 7..14.
+#pragma unroll 8
     for (int g = 0; g < 32; ++g) {
       const int w = (g + lane) & 31;
       const uint32_t word = mine[w];
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        acc[j] += lut[((word >> (8 * j)) & 0xffu) * kLutMaxBytes + j * 32 + w];
+      const float* col = lut + w;
+      acc0 += col[(word << 7) & 0x7f80u];
+      acc1 += col[32 + ((word >> 1) & 0x7f80u)];
+      acc2 += col[64 + ((word >> 9) & 0x7f80u)];
+      acc3 += col[96 + ((word >> 17) & 0x7f80u)];
     }
-    const float dot = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+    const float dot = (acc0 + acc1) + (acc2 + acc3);
     if (ok) {
       const float rank = fmaf(f.y, dot - half_sum, f.x + gadd[__float_as_int(f.z)]);
       if (!finite_f(rank)) {
@@ -1074,19 +1558,24 @@ xvec_gpu_status rabitq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq
   xvec_gpu_status st;
   const int total_bits = idx->rq_total_bits;
   const bool multi = total_bits > 1;
-  Scratch qrot, qsum, gadd, gerr, qfs, qfg, qeps, qexact, qstatus, qflags, qint, qterms, qbf,
-      q8;
+  Scratch qrot, qsum, gadd, gerr, qfs, qfg, qeps, qexact, qstatus, qflags, qint, qterms, q8;
   // Multi-bit with TotalBits <= 8: the INT8 tensor-core scan on the int8
   // code plane and the 16-bit integer query (its eps is that form's).
   const bool want8 = multi && total_bits <= 8 && idx->rq_vplane.ptr != nullptr;
   if ((st = qint.alloc((size_t)nq * padded * 2, s)) || (st = qterms.alloc((size_t)nq * 8, s)) ||
-      (multi && (st = qbf.alloc((size_t)nq * padded * 4, s))) ||
       (want8 && (st = q8.alloc((size_t)nq * padded * 2, s))))
     return st;
   const int64_t n_all = idx->n;
   const bool small_batch = !multi && n_all > 0 && nq <= 8 && padded <= 8 * kLutMaxBytes &&
                            kp <= 256 && nc <= 4096;
-  const bool tc8 = want8 && !small_batch && n_all > 0 && nc <= rabitq_tc_max_clusters() &&
+  const bool graph_walk = idx->hnsw_max_level >= 0 && !o.linear && n_all > kHNSWBruteForce;
+  if (graph_walk && idx->hnsw_n != n_all)
+    return set_error("the HNSW graph covers %lld rows, the index holds %lld: set the graph "
+                     "again after adding rows",
+                     (long long)idx->hnsw_n, (long long)n_all),
+           XVEC_GPU_INVALID_ARGUMENT;
+  const bool tc8 = !graph_walk && want8 && !small_batch && n_all > 0 &&
+                   nc <= rabitq_tc_max_clusters() &&
                    kp + 128 <= flat_tc_cap() && n_all < (1ll << 31) - 256 &&
                    rabitq8_tc_supported(padded, idx->rq_vplane.ptr, q8.ptr);
   if ((st = qrot.alloc((size_t)nq * padded * 4, s)) || (st = qsum.alloc((size_t)nq * 8, s)) ||
@@ -1102,7 +1591,7 @@ xvec_gpu_status rabitq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq
       idx->rq_bounds.as<unsigned>(), qrot.as<float>(), qsum.as<double>(), gadd.as<double>(),
       gerr.as<double>(), qfs.as<float>(), qfg.as<float>(), qeps.as<float>(), qexact.as<int>(),
       qstatus.as<int>(), qflags.as<int>(), qint.as<int8_t>(), qterms.as<float2>(), total_bits,
-      multi ? qbf.as<__nv_bfloat16>() : nullptr, tc8 ? q8.as<int8_t>() : nullptr);
+      tc8 ? q8.as<int8_t>() : nullptr);
   XVEC_LAUNCHED();
   // The approximate stage writes the final results, or the candidates of the
   // refine stage (no radius there: hnsw_rabitq.go:584).
@@ -1124,14 +1613,23 @@ xvec_gpu_status rabitq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq
   const float stage_radius = refine ? 0.f : o.radius;
   // Small batches: the sign bits through a byte table (the tensor-core scan
   // streams 16x more bytes and fills few SMs at this size).
-  const bool small = small_batch;
-  // INT8 tensor cores on the code planes (one bit), or BF16 tensor cores on
-  // the full code values (up to 8 bits), when the layout allows, else FFMA.
-  const bool use_tc = !small && n > 0 && nc <= rabitq_tc_max_clusters() &&
+  // An uploaded graph: the HNSW-RaBitQ walk unless the caller asks for the
+  // linear scan or the index is small (searchPrepared, hnsw_rabitq.go:589-591).
+  const bool walk = graph_walk;
+  const bool small = !walk && small_batch;
+  // INT8 tensor cores on the code planes (one bit) or on the int8 code-value
+  // plane (up to 8 bits), when the layout allows, else FFMA.
+  const bool use_tc = !walk && !small && n > 0 && nc <= rabitq_tc_max_clusters() &&
                       kp + 128 <= flat_tc_cap() && n < (1ll << 31) - 256 &&
                       (multi ? tc8 : rabitq_tc_supported(padded, idx->rq_planes.ptr, qint.ptr));
-  const bool fast = small || use_tc || (n > 0 && simt_cap_for(kp) <= 512);
-  if (small) {
+  const bool fast = walk || small || use_tc || (n > 0 && simt_cap_for(kp) <= 512);
+  if (walk) {
+    timer.mark(1);
+    if ((st = rabitq_graph_walk(idx, nq, k, o.ef, cc, refine, o.radius, d_bitmap, sc, o_keys,
+                                o_scores, o_counts, spos.as<uint32_t>(), qflags.as<int>(), s)))
+      return st;
+    timer.mark(2);
+  } else if (small) {
     // One part per SM (each block keeps its kp best), then one list per
     // query for the merge.
     int sms = 148;
@@ -1261,7 +1759,8 @@ xvec_gpu_status rabitq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq
     for (int q = 0; q < nq; ++q) {
       if (h_status[q] != 0) continue;
       if (!fast || (h_flags[q] & 3)) exact_list.push_back(q);
-      if ((h_flags[q] & kRaBitQFullCheck) && d_bitmap) check_list.push_back(q);
+      // (The graph walk meets failing estimates where the reference does.)
+      if ((h_flags[q] & kRaBitQFullCheck) && d_bitmap && !walk) check_list.push_back(q);
     }
   auto exact_pass = [&](const std::vector<int>& list, const uint32_t* bitmap,
                         bool write) -> xvec_gpu_status {
@@ -1350,6 +1849,59 @@ xvec_gpu_status rabitq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq
 }  // namespace xvec
 
 using namespace xvec;
+
+extern "C" xvec_gpu_status xvec_gpu_rabitq_set_graph(xvec_gpu_index* idx, int32_t max_level,
+                                                     int64_t entry, const int64_t* offsets,
+                                                     const int32_t* neighbors,
+                                                     int64_t total_neighbors) {
+  if (!idx) return set_error("nil index"), XVEC_GPU_INVALID_ARGUMENT;
+  if (idx->desc.kind != XVEC_INDEX_RABITQ)
+    return set_error("a graph belongs to a RaBitQ index"), XVEC_GPU_INVALID_ARGUMENT;
+  std::unique_lock<std::shared_mutex> lock(idx->mu);
+  if (max_level < 0) {
+    idx->hnsw_max_level = -1;
+    idx->hnsw_n = 0;
+    return XVEC_GPU_OK;
+  }
+  const int64_t n = idx->n;
+  if (max_level > 64) return set_error("graph level %d out of range", max_level), XVEC_GPU_INVALID_ARGUMENT;
+  if (n <= 0 || entry < 0 || entry >= n)
+    return set_error("graph entry %lld outside the index's %lld rows", (long long)entry,
+                     (long long)n),
+           XVEC_GPU_INVALID_ARGUMENT;
+  if (!offsets || total_neighbors < 0 || (total_neighbors > 0 && !neighbors))
+    return set_error("nil graph arrays"), XVEC_GPU_INVALID_ARGUMENT;
+  const int64_t levels = (int64_t)max_level + 1;
+  for (int64_t l = 0; l < levels; ++l) {
+    const int64_t* off = offsets + l * (n + 1);
+    if (off[0] < 0 || off[n] > total_neighbors)
+      return set_error("graph level %lld: offsets outside the neighbour array", (long long)l),
+             XVEC_GPU_INVALID_ARGUMENT;
+    for (int64_t p = 0; p < n; ++p)
+      if (off[p + 1] < off[p])
+        return set_error("graph level %lld: offsets decrease at node %lld", (long long)l,
+                         (long long)p),
+               XVEC_GPU_INVALID_ARGUMENT;
+  }
+  for (int64_t e = 0; e < total_neighbors; ++e)
+    if (neighbors[e] < 0 || neighbors[e] >= n)
+      return set_error("graph neighbour %lld: position %d outside the index", (long long)e,
+                       neighbors[e]),
+             XVEC_GPU_INVALID_ARGUMENT;
+  XVEC_CUDA(cudaSetDevice(idx->device));
+  cudaStream_t s = nullptr;
+  xvec_gpu_status st;
+  const size_t obytes = (size_t)levels * (n + 1) * 8, nbytes = (size_t)total_neighbors * 4;
+  if ((st = idx->hnsw_offsets.reserve(obytes, 0, s)) ||
+      (st = idx->hnsw_nbrs.reserve(std::max<size_t>(nbytes, 4), 0, s)))
+    return st;
+  XVEC_CUDA(cudaMemcpy(idx->hnsw_offsets.ptr, offsets, obytes, cudaMemcpyHostToDevice));
+  if (nbytes) XVEC_CUDA(cudaMemcpy(idx->hnsw_nbrs.ptr, neighbors, nbytes, cudaMemcpyHostToDevice));
+  idx->hnsw_max_level = max_level;
+  idx->hnsw_entry = entry;
+  idx->hnsw_n = n;
+  return XVEC_GPU_OK;
+}
 
 extern "C" xvec_gpu_status xvec_gpu_rabitq_set_model(xvec_gpu_index* idx, const float* centroids,
                                                      int32_t nclusters,
