@@ -407,9 +407,8 @@ def run_reference(args):
 # N(0,1), sigma 0.3); nlist 16,384; PQ 32 chunks x 256 codewords; nprobe 64;
 # 10,000 queries; top-k 10.  The 16,384 coarse centroids are trained on the
 # GPU with the IVF builder's k-means (xvec_gpu_kmeans_train: reservoir seeding,
-# 10 Lloyd iterations) on the first 4,000,000 rows, standing in for the
-# builder's training on every row; the PQ codebook is a seeded draw of 256
-# vectors from the mixture (PQ training is not part of this path).
+# 10 Lloyd iterations) on every row, as the builder trains; the PQ codebook is
+# TrainPQ's on the GPU (xvec_gpu_pq_train).
 # ---------------------------------------------------------------------------
 PQ_N, PQ_DIM, PQ_CLUSTERS, PQ_NLIST, PQ_CHUNKS, PQ_NPROBE, PQ_K = (
     100_000_000, 128, 10_000, 16_384, 32, 64, 10)
@@ -509,7 +508,7 @@ def run_ivfpq(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_ivfpq_qps(cents.cpu().numpy(), pivots.cpu().numpy(), h_sizes,
+        cpu = cpu_ivfpq_qps(cents.cpu().numpy(), np.asarray(pivots), h_sizes,
                             queries[:args.cpu_sample_queries].cpu().numpy())
     if rank == 0:
         _, hbm_peak, peak_kind = peaks()

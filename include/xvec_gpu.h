@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define XVEC_GPU_ABI_VERSION 3
+#define XVEC_GPU_ABI_VERSION 4
 
 typedef enum {
   XVEC_GPU_OK = 0,
@@ -89,7 +89,15 @@ typedef enum {
   /* IVF with INT4 scalar-quantized scoring of the probed lists' rows:
    * ScalarQuantizedIVFIndex with QuantizationInt4 (ivf_quantized.go:31-54),
    * the IVF_SQ8 kind with INT4 codes (kept one per byte, as SQ4_FLAT). */
-  XVEC_INDEX_IVF_SQ4 = 8
+  XVEC_INDEX_IVF_SQ4 = 8,
+  /* DiskANN graph search with the PQ frontier: DiskANNIndex
+   * (internal/core/diskann.go:343-367; SearchDiskANN :472-525,
+   * searchDiskANNGraph :559-651) over the float32 node vectors (the rows), their
+   * PQ codes (encoded at insertion from the prepared rows: cosine rows
+   * normalised, diskann.go:258-274, under the traversal metric, L2 for cosine
+   * and MIPSL2, :276-281) and a graph the caller uploads
+   * (xvec_gpu_diskann_set_graph).  Every metric; storage FP32. */
+  XVEC_INDEX_DISKANN = 9
 } xvec_gpu_index_kind;
 
 typedef enum {
@@ -120,9 +128,13 @@ typedef struct {
                                SQ8_FLAT only: exact fp32 rerank of floor(top_k*scale)
                                codes. */
   int32_t ef;               /* HNSWRaBitQSearchOptions.EF (hnsw_rabitq.go:548-550),
-                               RABITQ only: in [1, 2048] (ErrInvalidHNSWEF); with
+                               RABITQ: in [1, 2048] (ErrInvalidHNSWEF); with
                                refine, min(len, max(top_k, ef)) estimates are refined
-                               (hnsw_rabitq.go:579) */
+                               (hnsw_rabitq.go:579).  DISKANN: DiskANNSearchOptions.
+                               ListSize (diskann.go:326-333); 0 = DefaultDiskANNQueryList
+                               (300), negative = ErrInvalidDiskANNListSize; the
+                               traversal keeps min(len, max(top_k, ListSize)) <= 2048
+                               nodes */
   int32_t refine;           /* HNSWRaBitQSearchOptions.Refine, RABITQ only: non-zero =
                                exact fp32 rerank of the best estimates; zero = the
                                estimates themselves with the public score (IP:
@@ -138,8 +150,10 @@ typedef struct {
   const volatile int32_t* cancel_flag; /* optional host flag, polled between kernel
                                           launches; non-zero => XVEC_GPU_CANCELLED */
   int32_t linear;           /* HNSWRaBitQSearchOptions.Linear (hnsw_rabitq.go:589-591),
-                               RABITQ with a graph only: non-zero = the linear scan of
-                               every code instead of the graph walk */
+                               RABITQ with a graph: non-zero = the linear scan of
+                               every code instead of the graph walk.
+                               DiskANNSearchOptions.Linear (diskann.go:521-523),
+                               DISKANN: the exact scan of every node */
 } xvec_gpu_search_opts;
 
 /* Library ------------------------------------------------------------------ */
@@ -478,6 +492,29 @@ xvec_gpu_status xvec_gpu_index_search_noalloc(xvec_gpu_index* index, const void*
 xvec_gpu_status xvec_gpu_rabitq_set_graph(xvec_gpu_index* index, int32_t max_level, int64_t entry,
                                           const int64_t* offsets, const int32_t* neighbors,
                                           int64_t total_neighbors);
+
+/* ---- DiskANN ------------------------------------------------------------
+ * xvec_gpu_diskann_set_model: the PQ model of the traversal encoding
+ * (PQModelState, pq.go:86-94: pivots [256*dimension], centroid-major, split into
+ * `chunks` contiguous chunks by pqChunkOffsets, pq.go:395-406), trained on the
+ * prepared rows under the traversal metric as the DiskANN builder trains it
+ * (diskann.go:224-233); before rows are added.
+ *
+ * xvec_gpu_diskann_set_graph: the graph over the index's rows (positions
+ * 0..n-1, n = the index's row count): node p's neighbours at
+ * neighbors[offsets[p] .. offsets[p + 1]) (offsets: n + 1 int64 in host
+ * memory; at most max_degree each, max_degree in [1, 2048]); entry is the
+ * graph's entry point (DiskANNIndex.entryPoint); max_degree is the node
+ * layout's MaxDegree (NewDiskANNLayout, diskann_storage.go:61-100), which
+ * sets the traversal's read batch (diskANNReadBatchSize, diskann.go:685-691).
+ * Results equal the reference's traversal (keys identical, scores
+ * bit-identical).  Adding rows invalidates the graph (searches then fail
+ * until it is set again); offsets = NULL removes it. */
+xvec_gpu_status xvec_gpu_diskann_set_model(xvec_gpu_index* index, const float* pivots,
+                                           int32_t chunks);
+xvec_gpu_status xvec_gpu_diskann_set_graph(xvec_gpu_index* index, int64_t entry,
+                                           int32_t max_degree, const int64_t* offsets,
+                                           const int32_t* neighbors, int64_t total_neighbors);
 
 /* ---- Rotation reformer -------------------------------------------------
  * A collection whose vector index sets `rotate` rotates every stored and

@@ -205,6 +205,15 @@ class Oracle:
                                               _f32p, ctypes.c_int32, ctypes.c_int32,
                                               ctypes.c_int32, ctypes.c_int32, ctypes.c_float,
                                               _u32p, ctypes.c_int32, _u64p, _f32p, _i32p, _i32p]
+        lib.xo_diskann_code_norms.argtypes = [_f32p, _i32p, ctypes.c_int32, ctypes.c_int32,
+                                              _u8p, ctypes.c_int64, _f32p]
+        lib.xo_diskann_code_norms.restype = None
+        lib.xo_diskann_search.argtypes = [ctypes.c_int, ctypes.c_int32, _f32p, _i32p,
+                                          ctypes.c_int32, _u8p, _f32p, _f32p, _u64p,
+                                          ctypes.c_int64, ctypes.c_int64, _i64p, _i32p,
+                                          ctypes.c_int32, _f32p, ctypes.c_int32, ctypes.c_int32,
+                                          ctypes.c_int32, ctypes.c_float, _u32p, ctypes.c_int32,
+                                          _u64p, _f32p, _i32p, _i32p]
         lib.xo_rabitq_prepare_query.argtypes = [ctypes.c_int, ctypes.c_int32, _f32p,
                                                 ctypes.c_int32, _u8p, _f32p, _f32p, _f64p, _f64p,
                                                 _f64p]
@@ -784,6 +793,127 @@ class Oracle:
             1 if refine else 0, radius, _ptr(bm, _u32p), threads or os.cpu_count(),
             _ptr(ok, _u64p), _ptr(os_, _f32p), _ptr(oc, _i32p), _ptr(ost, _i32p))
         return st, ok.reshape(nq, k), os_.reshape(nq, k), oc, ost
+
+    # DiskANN ----------------------------------------------------------------
+    @staticmethod
+    def diskann_traversal_metric(metric):
+        """diskANNTraversalMetric (diskann.go:276-281)."""
+        return L2 if metric in (COSINE, MIPSL2) else metric
+
+    @staticmethod
+    def diskann_read_batch(d, max_degree):
+        """diskANNReadBatchSize (diskann.go:685-691) for the node layout of
+        NewDiskANNLayout (diskann_storage.go:61-100): 128 sectors per read,
+        ceil(record / 4096) sectors per node when a record exceeds a
+        sector."""
+        record = 4 * d + 4 + 4 * max_degree + 4
+        sectors = 1 if record <= 4096 else (record + 4095) // 4096
+        return max(1, 128 // sectors)
+
+    def diskann_prepare(self, metric, rows):
+        """prepareDiskANNPQVectors (diskann.go:258-274): cosine rows
+        normalised as normalizeRaBitQVector (rabitq.go:514-526)."""
+        rows = _c(rows, np.float32)
+        if metric != COSINE:
+            return rows.copy()
+        out = rows.copy()
+        for i in range(rows.shape[0]):
+            ns = 0.0
+            for x in rows[i].astype(np.float64):
+                ns += x * x
+            if ns != 0:
+                out[i] = rows[i] * np.float32(1.0 / np.sqrt(ns))
+        return out
+
+    def diskann_encode(self, metric, pivots, offsets, rows):
+        """The DiskANN build's PQ codes (diskann.go:224-243): EncodeBatch of
+        the prepared rows under the traversal metric, and for MIPSL2 the code
+        norms."""
+        tm = self.diskann_traversal_metric(metric)
+        prepared = self.diskann_prepare(metric, rows)
+        offsets = _c(offsets, np.int32)
+        chunks = offsets.size - 1
+        codes = np.zeros((rows.shape[0], chunks), np.uint8)
+        for i in range(rows.shape[0]):
+            st, codes[i] = self.pq_encode(tm, pivots, offsets, prepared[i])
+            assert st == OK
+        norms = np.zeros(rows.shape[0], np.float32)
+        if metric == MIPSL2:
+            pivots = _c(pivots, np.float32)
+            self.lib.xo_diskann_code_norms(_ptr(pivots, _f32p), _ptr(offsets, _i32p), chunks,
+                                           rows.shape[1], _ptr(codes, _u8p), rows.shape[0],
+                                           _ptr(norms, _f32p))
+        return codes, norms
+
+    def diskann_search(self, metric, pivots, offsets, codes, code_norms, vectors, keys, graph,
+                       beam, queries, k, list_size, radius=0.0, bitmap=None, threads=0):
+        """DiskANNIndex.SearchDiskANN (diskann.go:472-525, 559-683) with
+        Linear false over `graph` = (entry, offsets [n + 1] int64, neighbors
+        int32)."""
+        entry, goff, nbrs = graph
+        pivots = _c(pivots, np.float32)
+        offsets = _c(offsets, np.int32)
+        codes = _c(codes, np.uint8)
+        code_norms = _c(code_norms, np.float32)
+        vectors = _c(vectors, np.float32)
+        keys = _c(keys, np.uint64)
+        queries = _c(queries, np.float32)
+        goff = _c(goff, np.int64)
+        nbrs = _c(nbrs, np.int32)
+        n, d = vectors.shape
+        nq = queries.shape[0]
+        ok, os_, oc, ost = self._outs(nq, k)
+        bm = None if bitmap is None else _c(bitmap, np.uint32)
+        st = self.lib.xo_diskann_search(
+            metric, d, _ptr(pivots, _f32p), _ptr(offsets, _i32p), offsets.size - 1,
+            _ptr(codes, _u8p), _ptr(code_norms, _f32p), _ptr(vectors, _f32p), _ptr(keys, _u64p),
+            n, entry, _ptr(goff, _i64p), _ptr(nbrs, _i32p), beam, _ptr(queries, _f32p), nq, k,
+            list_size, radius, _ptr(bm, _u32p), threads or os.cpu_count(), _ptr(ok, _u64p),
+            _ptr(os_, _f32p), _ptr(oc, _i32p), _ptr(ost, _i32p))
+        return st, ok.reshape(nq, k), os_.reshape(nq, k), oc, ost
+
+
+def diskann_test_graph(vectors, degree=16, seed=0):
+    """A single-level proximity graph for the DiskANN tests (any graph
+    defines the search): every node linked to its `degree` - 3 nearest nodes
+    (L2, ties to the lower position), two random ones and the next position
+    (so every node is reachable), at most `degree` in all; the entry the node
+    nearest the mean.  Returns (entry, offsets [n + 1], neighbors) in the
+    layout of diskann_search."""
+    rng = np.random.default_rng(seed)
+    n = vectors.shape[0]
+    v = vectors.astype(np.float64)
+    sq = (v * v).sum(axis=1)
+    near = max(0, min(degree - 3, n - 1))
+    adj = []
+    for start in range(0, n, 512):
+        blk = v[start:start + 512]
+        m = blk.shape[0]
+        dist = sq[start:start + m, None] + sq[None, :] - 2.0 * blk @ v.T
+        dist[np.arange(m), start + np.arange(m)] = np.inf
+        if near > 0:
+            part = np.argpartition(dist, near - 1, axis=1)[:, :near] if near < n else \
+                np.tile(np.arange(n), (m, 1))
+        for i in range(m):
+            p = start + i
+            if near > 0:
+                cand = part[i]
+                cand = cand[np.lexsort((cand, dist[i, cand]))]
+                cand = [int(c) for c in cand if c != p]
+            else:
+                cand = []
+            extra = [int(x) for x in rng.integers(0, n, 2)] if n > 1 else []
+            seen, row = set(), []
+            for c in cand + extra + ([(p + 1) % n] if n > 1 else []):
+                if c != p and c not in seen:
+                    seen.add(c)
+                    row.append(c)
+            adj.append(np.asarray(row[:degree], np.int32))
+    offsets = np.zeros(n + 1, np.int64)
+    offsets[1:] = np.cumsum([a.size for a in adj])
+    nbrs = np.concatenate(adj) if n else np.zeros(0, np.int32)
+    entry = int(np.argmin(((v - v.mean(axis=0)) ** 2).sum(axis=1))) if n else 0
+    return entry, offsets, nbrs.astype(np.int32)
 
 
 def hnsw_test_graph(vectors, degree=12, seed=0, ml=None):

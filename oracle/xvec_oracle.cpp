@@ -2139,3 +2139,176 @@ extern "C" int xo_hnsw_rabitq_search(
   }
   return first;
 }
+
+// ---------------------------------------------------------------------------
+// DiskANN graph search with the PQ frontier (DiskANNIndex.searchDiskANNGraph,
+// diskann.go:559-651; diskANNApproximateScore :653-683) over a given graph:
+// node p's neighbours at neighbors[offsets[p] .. offsets[p + 1]), node p's
+// vector at vectors[p d], its PQ code (of the prepared vector, under the
+// traversal metric) at codes[p chunks].
+// ---------------------------------------------------------------------------
+namespace {
+struct DiskNode {
+  float score;
+  uint32_t id;
+};
+// diskANNTraversalMetric (diskann.go:276-281).
+inline int diskann_traversal(int metric) {
+  return (metric == XO_COSINE || metric == XO_MIPSL2) ? XO_L2 : metric;
+}
+// The queue order of searchDiskANNGraph (:571-576): the traversal metric's
+// Better, ties to the lower node id.
+struct DiskBetter {
+  int traversal;
+  bool operator()(const DiskNode& a, const DiskNode& b) const {
+    if (a.score == b.score) return a.id < b.id;
+    return better(traversal, a.score, b.score);
+  }
+};
+}  // namespace
+
+// diskANNPQCodeNorms (diskann.go:292-323): per code, the float64 sum of the
+// squares of its pivots' chunk components in chunk order, as float32.
+extern "C" void xo_diskann_code_norms(const float* pivots, const int32_t* offsets, int32_t chunks,
+                                      int32_t d, const uint8_t* codes, int64_t n, float* norms) {
+  for (int64_t p = 0; p < n; ++p) {
+    double norm = 0;
+    for (int32_t c = 0; c < chunks; ++c) {
+      const float* pv = pivots + (int64_t)codes[p * chunks + c] * d;
+      for (int32_t i = offsets[c]; i < offsets[c + 1]; ++i) norm += (double)pv[i] * (double)pv[i];
+    }
+    norms[p] = (float)norm;
+  }
+}
+
+// diskANNApproximateScore (diskann.go:653-676).
+static int diskann_approx(int metric, const float* table, int32_t chunks, const uint8_t* codes,
+                          const float* code_norms, uint32_t id, double query_norm, float* out) {
+  float score;
+  int st = xo_pq_lookup(table, chunks, codes + (int64_t)id * chunks, &score);
+  if (st != XO_OK) return st;
+  if (metric != XO_MIPSL2) {
+    *out = score;
+    return XO_OK;
+  }
+  const double cn = (double)code_norms[id];
+  const double inner = (query_norm + cn - (double)score) / 2;
+  const double den = go_maxd(query_norm, cn);
+  if (den == 0) {
+    *out = 0;
+    return XO_OK;
+  }
+  const double converted = 2 - 2 * inner / den;
+  if (std::isnan(converted) || std::isinf(converted) || converted > 3.4028234663852886e38 ||
+      converted < -3.4028234663852886e38)
+    return XO_OVERFLOW;
+  *out = (float)converted;
+  return XO_OK;
+}
+
+// DiskANNIndex.SearchDiskANN (diskann.go:472-525) with Linear = false:
+// validation, then searchDiskANNGraph; `beam` is diskANNReadBatchSize
+// (:685-691).
+extern "C" int xo_diskann_search(int metric, int32_t d, const float* pivots,
+                                 const int32_t* offsets, int32_t chunks, const uint8_t* codes,
+                                 const float* code_norms, const float* vectors,
+                                 const uint64_t* keys, int64_t n, int64_t entry,
+                                 const int64_t* graph_offsets, const int32_t* neighbors,
+                                 int32_t beam, const float* queries, int32_t nq, int32_t k,
+                                 int32_t list_size, float radius, const uint32_t* bitmap,
+                                 int32_t threads, uint64_t* out_keys, float* out_scores,
+                                 int32_t* out_counts, int32_t* out_status) {
+  if (list_size <= 0) return XO_INVALID_ARGUMENT;  // ErrInvalidDiskANNListSize
+  int st0 = validate_options(k, radius);
+  if (st0 != XO_OK) return st0;
+  if (beam <= 0) return XO_INVALID_ARGUMENT;
+  const int traversal = diskann_traversal(metric);
+  const DiskBetter node_better{traversal};
+  std::vector<int32_t> status(nq, XO_OK);
+  parallel_for(nq, threads, [&](int64_t q) {
+    const float* query = queries + q * d;
+    std::vector<Result> res;
+    int st = validate_query(metric, query, d);
+    if (st == XO_OK && n > 0) {
+      // prepareDiskANNPQQuery (:283-289), the table, diskANNVectorNormSquared.
+      std::vector<float> prepared = prepare_vector(query, d, metric);
+      std::vector<float> table((size_t)chunks * 256);
+      st = xo_pq_distance_table(traversal, pivots, offsets, chunks, d, prepared.data(),
+                                table.data());
+      double qnorm = 0;
+      for (int32_t i = 0; i < d; ++i) qnorm += (double)prepared[i] * (double)prepared[i];
+      const int64_t capacity = std::min<int64_t>(n, std::max(k, list_size));
+      auto approx = [&](uint32_t id, float* s) {
+        return diskann_approx(metric, table.data(), chunks, codes, code_norms, id, qnorm, s);
+      };
+      // frontier: best on top; retained: worst on top.
+      auto best_top = [&](const DiskNode& a, const DiskNode& b) { return node_better(b, a); };
+      auto worst_top = [&](const DiskNode& a, const DiskNode& b) { return node_better(a, b); };
+      std::priority_queue<DiskNode, std::vector<DiskNode>, decltype(best_top)> frontier(best_top);
+      std::priority_queue<DiskNode, std::vector<DiskNode>, decltype(worst_top)> retained(
+          worst_top);
+      std::vector<uint8_t> visited((size_t)n, 0), member((size_t)n, 0), expanded((size_t)n, 0);
+      WorstFirstHeap collector{metric, {}};
+      float es = 0;
+      if (st == XO_OK) st = approx((uint32_t)entry, &es);
+      if (st == XO_OK) {
+        const DiskNode start{es, (uint32_t)entry};
+        frontier.push(start);
+        retained.push(start);
+        visited[entry] = member[entry] = 1;
+      }
+      while (st == XO_OK && !frontier.empty()) {
+        std::vector<DiskNode> batch;
+        while (!frontier.empty() && (int32_t)batch.size() < beam) {
+          const DiskNode c = frontier.top();
+          frontier.pop();
+          if (!member[c.id] || expanded[c.id]) continue;
+          expanded[c.id] = 1;
+          batch.push_back(c);
+        }
+        if (batch.empty()) break;
+        for (const DiskNode& node : batch) {
+          float exact;
+          st = xo_metric_compute(metric, query, vectors + (int64_t)node.id * d, d, &exact);
+          if (st != XO_OK) break;
+          // diskANNResultCollector.Add (:709-721): filter, radius, top-k.
+          if (filter_pass(bitmap, node.id) && within_radius(metric, exact, radius))
+            collector.offer(Result{keys[node.id], exact}, (size_t)k);
+          for (int64_t e = graph_offsets[node.id]; e < graph_offsets[node.id + 1]; ++e) {
+            const uint32_t nb = (uint32_t)neighbors[e];
+            if (visited[nb]) continue;
+            visited[nb] = 1;
+            float s;
+            st = approx(nb, &s);
+            if (st != XO_OK) break;
+            const DiskNode cand{s, nb};
+            if ((int64_t)retained.size() < capacity) {
+              retained.push(cand);
+              member[nb] = 1;
+              frontier.push(cand);
+              continue;
+            }
+            if (node_better(cand, retained.top())) {
+              member[retained.top().id] = 0;
+              retained.pop();
+              retained.push(cand);
+              member[nb] = 1;
+              frontier.push(cand);
+            }
+          }
+          if (st != XO_OK) break;
+        }
+      }
+      if (st == XO_OK) res = collector.sorted();
+    }
+    status[q] = st;
+    if (st != XO_OK) res.clear();
+    write_results(res, k, (int32_t)q, out_keys, out_scores, out_counts);
+  });
+  int first = XO_OK;
+  for (int32_t q = 0; q < nq; ++q) {
+    if (out_status) out_status[q] = status[q];
+    if (first == XO_OK) first = status[q];
+  }
+  return first;
+}

@@ -253,6 +253,25 @@ int xo_hnsw_rabitq_search(int metric, int32_t d, const float* centroids, int32_t
                           int32_t threads, uint64_t* out_keys, float* out_scores,
                           int32_t* out_counts, int32_t* out_status);
 
+/* diskANNPQCodeNorms (diskann.go:292-323): float32 of the float64 sum of the
+ * squared pivot components of each code, chunk by chunk. */
+void xo_diskann_code_norms(const float* pivots, const int32_t* offsets, int32_t chunks, int32_t d,
+                           const uint8_t* codes, int64_t n, float* norms);
+
+/* DiskANN graph search with the PQ frontier (diskann.go:472-525, 559-683)
+ * over a given graph: node p's neighbours at neighbors[graph_offsets[p] ..
+ * graph_offsets[p + 1]), its vector at vectors[p d], its PQ code (of the
+ * prepared vector under the traversal metric) at codes[p chunks], code_norms
+ * for MIPSL2 (else unused).  beam = diskANNReadBatchSize.  Results as
+ * xo_flat_search. */
+int xo_diskann_search(int metric, int32_t d, const float* pivots, const int32_t* offsets,
+                      int32_t chunks, const uint8_t* codes, const float* code_norms,
+                      const float* vectors, const uint64_t* keys, int64_t n, int64_t entry,
+                      const int64_t* graph_offsets, const int32_t* neighbors, int32_t beam,
+                      const float* queries, int32_t nq, int32_t k, int32_t list_size,
+                      float radius, const uint32_t* bitmap, int32_t threads, uint64_t* out_keys,
+                      float* out_scores, int32_t* out_counts, int32_t* out_status);
+
 #ifdef __cplusplus
 }
 #endif

@@ -30,7 +30,7 @@ def test_abi_version_and_errors_without_gpu():
     import ctypes
     import xvec_b200
     lib = xvec_b200.library()
-    assert lib.xvec_gpu_abi_version() == 3
+    assert lib.xvec_gpu_abi_version() == 4
     # Invalid descriptors fail before any device work.
     desc = xvec_b200.IndexDesc(xvec_b200.INDEX_FLAT, 0, 1, 1, 0)
     h = ctypes.c_void_p()

@@ -35,7 +35,7 @@ LIB_PATH = os.path.join(HERE, "libxvec_gpu.so")
 METRIC_L2, METRIC_IP, METRIC_COSINE, METRIC_MIPSL2 = 1, 2, 3, 4
 INDEX_FLAT, INDEX_SQ8_FLAT, INDEX_IVF_PQ, INDEX_RABITQ, INDEX_IVF_FLAT, INDEX_IVF_SQ8 = (
     1, 2, 3, 4, 5, 6)
-INDEX_SQ4_FLAT, INDEX_IVF_SQ4 = 7, 8
+INDEX_SQ4_FLAT, INDEX_IVF_SQ4, INDEX_DISKANN = 7, 8, 9
 STORAGE_FP32, STORAGE_FP16 = 1, 2
 
 STATUS_NAMES = {
@@ -65,7 +65,7 @@ EXPORTED_SYMBOLS = (
     "xvec_gpu_sharded_search_device", "xvec_gpu_sharded_search",
     "xvec_gpu_set_wait_limit_ns",
     "xvec_gpu_rotation_signs", "xvec_gpu_rotate", "xvec_gpu_rotate_device",
-    "xvec_gpu_rabitq_set_graph",
+    "xvec_gpu_rabitq_set_graph", "xvec_gpu_diskann_set_model", "xvec_gpu_diskann_set_graph",
 )
 
 
@@ -161,6 +161,8 @@ def _load() -> ctypes.CDLL:
     lib.xvec_gpu_sharded_search.argtypes = [vp, vp, i32, vp, i32, ctypes.POINTER(SearchOpts), vp,
                                             vp, vp]
     lib.xvec_gpu_rabitq_set_graph.argtypes = [vp, i32, i64, vp, vp, i64]
+    lib.xvec_gpu_diskann_set_model.argtypes = [vp, vp, i32]
+    lib.xvec_gpu_diskann_set_graph.argtypes = [vp, i64, i32, vp, vp, i64]
     lib.xvec_gpu_rotation_signs.argtypes = [ctypes.c_char_p, ctypes.c_char_p, i32, i32, i32, vp,
                                             i64]
     lib.xvec_gpu_rotate.argtypes = [i32, vp, i64, i32, vp, i64, vp, i32]
@@ -640,6 +642,31 @@ class RaBitQIndex(_Index):
             _check(_lib.xvec_gpu_rabitq_set_model_bits(self._h, _ptr(centroids),
                                                        centroids.shape[0], _ptr(signs),
                                                        total_bits, float(extra_scale)))
+
+
+class DiskANNIndex(_Index):
+    """DiskANNIndex graph search with the PQ frontier (diskann.go:472-683):
+    set_model (the traversal PQ model) before adding rows, set_graph after.
+    SearchOptions.ef is DiskANNSearchOptions.ListSize (0: the default 300),
+    SearchOptions.linear its Linear flag."""
+    kind = INDEX_DISKANN
+
+    def set_model(self, pivots, chunks: int) -> None:
+        pivots = np.ascontiguousarray(pivots, np.float32)
+        _check(_lib.xvec_gpu_diskann_set_model(self._h, _ptr(pivots), chunks))
+
+    def set_graph(self, entry: int, max_degree: int, offsets, neighbors) -> None:
+        """The graph over the insertion positions: node p's neighbours at
+        neighbors[offsets[p] .. offsets[p + 1]); offsets None removes it."""
+        if offsets is None:
+            _check(_lib.xvec_gpu_diskann_set_graph(self._h, 0, 0, None, None, 0))
+            return
+        offsets = np.ascontiguousarray(offsets, np.int64)
+        neighbors = np.ascontiguousarray(neighbors, np.int32)
+        self._graph = (offsets, neighbors)
+        _check(_lib.xvec_gpu_diskann_set_graph(self._h, entry, max_degree, offsets.ctypes.data,
+                                               neighbors.ctypes.data if neighbors.size else None,
+                                               neighbors.size))
 
 
 def kmeans_assign(metric: int, vectors, centroids, device: int = 0):

@@ -9,7 +9,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libxvec_gpu.so")
-SOURCES = ["capi.cu", "flat_kernels.cu", "flat_tc.cu", "index_quantized.cu", "merge.cu", "noalloc.cu", "sq8.cu", "ivfpq.cu", "rabitq.cu", "refine_api.cu", "kmeans.cu", "ivf_flat.cu", "ivf_file.cu", "pq_train.cu", "comm.cu", "flat_stream.cu", "rotation.cu"]
+SOURCES = ["capi.cu", "flat_kernels.cu", "flat_tc.cu", "index_quantized.cu", "merge.cu", "noalloc.cu", "sq8.cu", "ivfpq.cu", "rabitq.cu", "refine_api.cu", "kmeans.cu", "ivf_flat.cu", "ivf_file.cu", "pq_train.cu", "comm.cu", "flat_stream.cu", "rotation.cu", "diskann.cu"]
 NVCC = os.environ.get("NVCC", "nvcc")
 FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
          "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr", "-Xptxas", "-warn-spills"]

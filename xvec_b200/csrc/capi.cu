@@ -533,6 +533,17 @@ xvec_gpu_status search_device_locked(xvec_gpu_index* idx, const void* d_q, int n
     case XVEC_INDEX_IVF_SQ4:
       return ivf_sq8_search_impl(idx, static_cast<const float*>(d_q), nq, o, d_bitmap, d_keys,
                                  d_scores, d_counts, s, statuses);
+    case XVEC_INDEX_DISKANN:
+      // searchDiskANN (diskann.go:476-525): ListSize (opts.ef; 0 =
+      // DefaultDiskANNQueryList) must be positive; Linear scans every node
+      // exactly (searchDiskANNLinear :527-557, the Flat search's result).
+      if (o.ef < 0)
+        return set_error("core: invalid DiskANN list size"), XVEC_GPU_INVALID_ARGUMENT;
+      if (o.linear)
+        return flat_search_impl<float>(idx, d_q, nq, o, d_bitmap, d_keys, d_scores, d_counts, s,
+                                       statuses, band);
+      return diskann_search_impl(idx, static_cast<const float*>(d_q), nq, o, d_bitmap, d_keys,
+                                 d_scores, d_counts, s, statuses);
     default: return set_error("invalid index kind"), XVEC_GPU_INVALID_ARGUMENT;
   }
 }
@@ -690,6 +701,14 @@ extern "C" xvec_gpu_status xvec_gpu_index_create(const xvec_gpu_index_desc* desc
                XVEC_GPU_INVALID_ARGUMENT;
       break;
     case XVEC_INDEX_IVF_FLAT:
+      break;
+    case XVEC_INDEX_DISKANN:
+      // NewDiskANNLayout (diskann_storage.go:68-70).
+      if (desc->dimension > 65535)
+        return set_error("core: invalid DiskANN layout: dimension must be in [1,65535]"),
+               XVEC_GPU_INVALID_ARGUMENT;
+      if (desc->storage != XVEC_STORAGE_FP32)
+        return set_error("DiskANN node vectors are float32"), XVEC_GPU_INVALID_ARGUMENT;
       break;
     default: return set_error("invalid index kind %d", desc->kind), XVEC_GPU_INVALID_ARGUMENT;
   }

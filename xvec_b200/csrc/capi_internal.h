@@ -257,6 +257,16 @@ struct xvec_gpu_index {
   int64_t hnsw_entry = 0, hnsw_n = 0;
   xvec::DeviceBuffer hnsw_offsets;          // int64
   xvec::DeviceBuffer hnsw_nbrs;             // int32
+  // DiskANN: the PQ model in pivots / chunk_offsets / chunks (has_model),
+  // the codes of the prepared rows in pq_codes, their MIPSL2 norms, and the
+  // graph (xvec_gpu_diskann_set_graph): node p's neighbours at
+  // dk_nbrs[dk_offsets[p] .. dk_offsets[p + 1]); dk_entry -1: no graph over
+  // the current rows.
+  int64_t dk_entry = -1;
+  int32_t dk_beam = 1, dk_max_degree = 0;
+  xvec::DeviceBuffer dk_norms;              // float [n]
+  xvec::DeviceBuffer dk_offsets;            // int64 [n + 1]
+  xvec::DeviceBuffer dk_nbrs;               // int32
   // TotalBits 2..8: the code values again as int8 v - 128 [n][padded] (the
   // INT8 tensor-core operand); rq_fast's w slot holds 128 sum(v - 128).
   xvec::DeviceBuffer rq_vplane;

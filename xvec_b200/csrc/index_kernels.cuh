@@ -46,6 +46,23 @@ xvec_gpu_status ivf_sq8_search_impl(xvec_gpu_index* idx, const float* d_q, int n
                                     cudaStream_t s, std::vector<int>* statuses,
                                     bool candidates_only = false);
 
+// PQModel.Encode of n rows (block per row; err receives a status when a
+// chunk score is not finite) and PQModel.DistanceTable of nq queries
+// (q_flags |= 4 when a table entry is not finite), in ivfpq.cu.
+cudaError_t launch_pq_encode(const float* rows, int64_t n, int d, int metric, const float* pivots,
+                             const int* offsets, int chunks, uint8_t* codes, int* err,
+                             cudaStream_t s);
+cudaError_t launch_pq_table(const float* queries, int nq, int d, int metric, const float* pivots,
+                            const int* offsets, int chunks, float* table, int* q_flags,
+                            cudaStream_t s);
+
+xvec_gpu_status diskann_reserve(xvec_gpu_index* idx, int64_t capacity, cudaStream_t s);
+xvec_gpu_status diskann_commit(xvec_gpu_index* idx, int64_t old_n, int64_t m, cudaStream_t s);
+xvec_gpu_status diskann_search_impl(xvec_gpu_index* idx, const float* d_q, int nq,
+                                    const xvec_gpu_search_opts& o, const uint32_t* d_bitmap,
+                                    uint64_t* d_keys, float* d_scores, int* d_counts,
+                                    cudaStream_t s, std::vector<int>* statuses);
+
 xvec_gpu_status rabitq_reserve(xvec_gpu_index* idx, int64_t capacity, cudaStream_t s);
 xvec_gpu_status rabitq_commit(xvec_gpu_index* idx, int64_t old_n, int64_t m, cudaStream_t s);
 

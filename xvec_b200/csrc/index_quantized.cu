@@ -1,5 +1,6 @@
 // index_quantized.cu — dispatch of the per-kind insertion hooks: the
-// quantized kinds (SQ8: sq8.cu, IVF-PQ: ivfpq.cu, RaBitQ: rabitq.cu), the IVF
+// quantized kinds (SQ8: sq8.cu, IVF-PQ: ivfpq.cu, RaBitQ: rabitq.cu, DiskANN:
+// diskann.cu), the IVF
 // list assignment (IVF-Flat and IVF-SQ8: ivf_flat.cu) and the
 // bfloat16 split of Flat FP32 rows (the tensor-core scan's operands).
 #include "flat_tc.cuh"
@@ -29,6 +30,7 @@ xvec_gpu_status extra_reserve(xvec_gpu_index* idx, int64_t cap, cudaStream_t s) 
     const xvec_gpu_status st = sq8_reserve(idx, cap, s);
     return st ? st : ivf_flat_reserve(idx, cap, s);
   }
+  if (idx->desc.kind == XVEC_INDEX_DISKANN) return diskann_reserve(idx, cap, s);
   return XVEC_GPU_OK;
 }
 xvec_gpu_status extra_validate(xvec_gpu_index* idx, int64_t, int64_t, cudaStream_t) {
@@ -40,6 +42,8 @@ xvec_gpu_status extra_validate(xvec_gpu_index* idx, int64_t, int64_t, cudaStream
        idx->desc.kind == XVEC_INDEX_IVF_SQ4) &&
       !idx->has_model)
     return set_error("set the IVF model before adding rows"), XVEC_GPU_INVALID_ARGUMENT;
+  if (idx->desc.kind == XVEC_INDEX_DISKANN && !idx->has_model)
+    return set_error("set the DiskANN PQ model before adding rows"), XVEC_GPU_INVALID_ARGUMENT;
   return XVEC_GPU_OK;
 }
 xvec_gpu_status extra_commit(xvec_gpu_index* idx, int64_t old_n, int64_t m, cudaStream_t s) {
@@ -60,6 +64,7 @@ xvec_gpu_status extra_commit(xvec_gpu_index* idx, int64_t old_n, int64_t m, cuda
     const xvec_gpu_status st = sq8_commit(idx, old_n, m, s);
     return st ? st : ivf_flat_commit(idx, old_n, m, s);
   }
+  if (idx->desc.kind == XVEC_INDEX_DISKANN) return diskann_commit(idx, old_n, m, s);
   return XVEC_GPU_OK;
 }
 

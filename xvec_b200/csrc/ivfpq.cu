@@ -512,6 +512,27 @@ __global__ void iota32_kernel(uint32_t* out, int64_t n) {
 
 }  // namespace
 
+cudaError_t launch_pq_encode(const float* rows, int64_t n, int d, int metric, const float* pivots,
+                             const int* offsets, int chunks, uint8_t* codes, int* err,
+                             cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  pq_encode_kernel<<<(unsigned)n, 256, 0, s>>>(rows, n, d, metric, pivots, offsets, chunks, codes,
+                                                err);
+  XVEC_LAUNCHED();
+  return cudaGetLastError();
+}
+
+cudaError_t launch_pq_table(const float* queries, int nq, int d, int metric, const float* pivots,
+                            const int* offsets, int chunks, float* table, int* q_flags,
+                            cudaStream_t s) {
+  if (nq <= 0) return cudaSuccess;
+  pq_table_kernel<<<nq, 256, 0, s>>>(queries, nq, d, metric, pivots, offsets, chunks, table,
+                                     q_flags);
+  XVEC_LAUNCHED();
+  return cudaGetLastError();
+}
+
+
 // Nearest centroid of each row through a Flat index over the centroids
 // (keys = centroid index): top-1 under the metric, ties to the lower index.
 xvec_gpu_status assign_rows(xvec_gpu_index* probe, const float* d_rows, int64_t n, int d,

@@ -1304,12 +1304,16 @@ __global__ void __launch_bounds__(kLutThreads, 1) rabitq_lut_scan_kernel(
       pre[k] = (u < per_step && u < words_avail) ? __ldg(src + u) : make_uint2(0u, 0u);
     }
   };
+  // Row of word u: u / words8 through a float reciprocal (u < 2^13, so
+  // (u + 0.5) / words8 is at least 1/32 away from an integer and the product
+  // rounds to the right side).
+  const float inv_words8 = 1.0f / (float)words8;
   auto store_step = [&]() {
 #pragma unroll
     for (int k = 0; k < kMaxLoads; ++k) {
       const int u = tid + k * kLutThreads;
       if (u < per_step) {
-        const int r = u / words8, w = u - r * words8;
+        const int r = (int)(((float)u + 0.5f) * inv_words8), w = u - r * words8;
         *reinterpret_cast<uint2*>(stage + r * 32 + w * 2) = pre[k];
       }
     }
@@ -1345,17 +1349,27 @@ __global__ void __launch_bounds__(kLutThreads, 1) rabitq_lut_scan_kernel(
     }
     const uint32_t* mine = stage + tid * 32;
     float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
-    // Byte j of a word selects row (byte) of column j * 32 + w: the float
-    // offset byte * 128 is the byte shifted into bits 7..14.
+    // Byte j of a word selects row (byte) of column j * 32 + w: the byte
+    // offset byte * 512 is the byte shifted into bits 9..16, and column j
+    // adds 128 j bytes (the load's immediate).  32-bit shared addresses;
+    // volatile keeps the loads on this side of the step's barriers.
+    const uint32_t lut_s = (uint32_t)__cvta_generic_to_shared(lut);
+    const uint32_t mine_s = (uint32_t)__cvta_generic_to_shared(mine);
 #pragma unroll 8
     for (int g = 0; g < 32; ++g) {
-      const int w = (g + lane) & 31;
-      const uint32_t word = mine[w];
-      const float* col = lut + w;
-      acc0 += col[(word << 7) & 0x7f80u];
-      acc1 += col[32 + ((word >> 1) & 0x7f80u)];
-      acc2 += col[64 + ((word >> 9) & 0x7f80u)];
-      acc3 += col[96 + ((word >> 17) & 0x7f80u)];
+      const uint32_t w = (uint32_t)(g + lane) & 31u;
+      uint32_t word;
+      asm volatile("ld.shared.u32 %0, [%1];" : "=r"(word) : "r"(mine_s + w * 4));
+      const uint32_t col = lut_s + w * 4;
+      float t0, t1, t2, t3;
+      asm volatile("ld.shared.f32 %0, [%1];" : "=f"(t0) : "r"(col + ((word << 9) & 0x1fe00u)));
+      asm volatile("ld.shared.f32 %0, [%1+128];" : "=f"(t1) : "r"(col + ((word << 1) & 0x1fe00u)));
+      asm volatile("ld.shared.f32 %0, [%1+256];" : "=f"(t2) : "r"(col + ((word >> 7) & 0x1fe00u)));
+      asm volatile("ld.shared.f32 %0, [%1+384];" : "=f"(t3) : "r"(col + ((word >> 15) & 0x1fe00u)));
+      acc0 += t0;
+      acc1 += t1;
+      acc2 += t2;
+      acc3 += t3;
     }
     const float dot = (acc0 + acc1) + (acc2 + acc3);
     if (ok) {
