@@ -57,6 +57,7 @@ def parse():
                         "sq8_ip_refine)")
     p.add_argument("--workload",
                    choices=["flat_cosine_fp16", "ivfpq_l2", "sq8_ip_refine", "rabitq_l2_refine",
+                            "diskann_l2",
                             "flat_l2_fp32", "ivf_flat_l2", "ivf_sq8_l2_refine",
                             "rabitq7_l2_refine", "sq4_l2_refine", "pq_train_l2",
                             "rabitq_hnsw_l2_refine"],
@@ -308,7 +309,7 @@ def oracle_flat_over_chunks(ora, metric, chunks, queries, k, threads):
     return out_k, out_s, out_c, secs
 
 
-def parity_record(gpu, ref, qids, base_rows, kind, oracle_s, what):
+def parity_record(gpu, ref, qids, base_rows, kind, oracle_s, what, how="evenly spaced over the batch"):
     """Compares the GPU's results of the sampled queries with the oracle's:
     identical counts and keys, bit-identical float32 scores."""
     import numpy as np
@@ -321,10 +322,40 @@ def parity_record(gpu, ref, qids, base_rows, kind, oracle_s, what):
                 and np.array_equal(gs[q, :c].view(np.uint32), rs[i, :c].view(np.uint32)))
         if not same:
             bad.append(int(q))
-    return {"queries": int(len(qids)), "query_ids": f"{len(qids)} ids evenly spaced over the batch",
+    return {"queries": int(len(qids)), "query_ids": f"{len(qids)} ids {how}",
             "base_rows": int(base_rows), "against": what, "oracle_kernels": kind,
             "keys_identical": not bad, "scores_bitwise": not bad, "mismatched_queries": bad[:8],
             "oracle_s": oracle_s}
+
+
+def merged_refine(ora, metric, cand, k, lists, queries):
+    """The refined search over chunked candidates (RefinedSearch,
+    refiner.go:133-166): per query, the `cand` best of every chunk's
+    approximate candidates (MergeSearchResults of the per-chunk lists, which
+    hold each chunk's `cand` best under the same (score, key) order), the exact
+    metric.Compute of their originals, and the top k (MergeSearchResults).
+    lists[q] = [(keys, approximate scores, originals [m, d])]."""
+    import numpy as np
+    nq = len(lists)
+    out_k = np.zeros((nq, k), np.uint64)
+    out_s = np.zeros((nq, k), np.float32)
+    out_c = np.zeros(nq, np.int32)
+    for q in range(nq):
+        keys = np.concatenate([x[0] for x in lists[q]])
+        scores = np.concatenate([x[1] for x in lists[q]])
+        rows = np.concatenate([x[2] for x in lists[q]])
+        ck, _ = ora.merge_results(metric, cand, keys, scores)
+        where = {int(kk): i for i, kk in enumerate(keys)}
+        exact = np.zeros(len(ck), np.float32)
+        for i, kk in enumerate(ck):
+            st, exact[i] = ora.metric_compute(metric, queries[q], rows[where[int(kk)]])
+            if st != 0:
+                raise RuntimeError(f"oracle exact score status {st}")
+        mk, ms = ora.merge_results(metric, k, ck, exact)
+        out_c[q] = len(mk)
+        out_k[q, :len(mk)] = mk
+        out_s[q, :len(ms)] = ms
+    return out_k, out_s, out_c
 
 
 def gpu_results_host(search, queries, opts):
@@ -483,6 +514,8 @@ def run_ivfpq(args):
     sizes = torch.zeros(PQ_NLIST, dtype=torch.int64, device=dev)
     labels = torch.empty(PQ_CHUNK_ROWS, dtype=torch.int32, device=dev)
     stream = torch.cuda.current_stream().cuda_stream
+    check = rank == 0 and world == 1 and not args.no_parity
+    host_labels = np.empty(e - b, np.int32) if check else None
     for c0 in range(b, e, PQ_CHUNK_ROWS):
         m = min(PQ_CHUNK_ROWS, e - c0)
         rows = pq_mixture(torch, centers, c0 // PQ_CHUNK_ROWS, m, dev).contiguous()
@@ -491,6 +524,8 @@ def run_ivfpq(args):
         xb.kmeans_assign_device(local, xb.METRIC_L2, rows.data_ptr(), m, cents.data_ptr(),
                                 cents.shape[0], PQ_DIM, labels.data_ptr(), 0, stream)
         sizes += torch.bincount(labels[:m].long(), minlength=PQ_NLIST)
+        if check:
+            host_labels[c0 - b:c0 - b + m] = labels[:m].cpu().numpy()
         del rows, keys
     queries = pq_mixture(torch, centers, 10**6 + 3, nq, dev).contiguous()
     torch.cuda.synchronize()
@@ -503,8 +538,17 @@ def run_ivfpq(args):
     scanned = int(h_sizes[pr.keys.astype(np.int64)].sum())
     probe.close()
     opts = xb.SearchOptions(top_k=PQ_K, nprobe=PQ_NPROBE)
-    ms, scan_ms, e2e_ms, st, clocks = time_search(sharded(index, world, local), queries, opts, args, dev,
-                                                  world, local)
+    search = sharded(index, world, local)
+    ms, scan_ms, e2e_ms, st, clocks = time_search(search, queries, opts, args, dev, world, local)
+    # Parity of sampled queries (one GPU): the oracle's IVF-PQ search over the
+    # lists its own probe picks, with every row of those lists regenerated and
+    # PQ-encoded by the oracle (the rows' lists are the GPU assignment's).
+    parity = None
+    if check:
+        gpu_res = gpu_results_host(search, queries, opts)
+        parity = ivfpq_parity(torch, centers, cents.cpu().numpy(), np.asarray(pivots), host_labels,
+                              queries, gpu_res, n, dev)
+        del host_labels
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -543,6 +587,7 @@ def run_ivfpq(args):
             "cpu_baseline": cpu,
             "clocks": clocks,
             "gpu_launches": int(st["kernel_launches"]),
+            "parity": parity,
         }
         print(json.dumps(line), flush=True)
     finish_ranks(world)
@@ -746,7 +791,8 @@ def run_ivf_flat(args, sq8=False):
     index.reserve(e - b)
     sizes = torch.zeros(kc, dtype=torch.int64, device=dev)
     lab = torch.empty(PQ_CHUNK_ROWS, dtype=torch.int32, device=dev)
-    host_rows = [] if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
+    host_rows = ([] if (rank == 0 and world == 1 and not (args.no_cpu_baseline and args.no_parity))
+                 else None)
     host_labels = []
     for c0 in range(b, e, PQ_CHUNK_ROWS):
         m = min(PQ_CHUNK_ROWS, e - c0)
@@ -770,9 +816,10 @@ def run_ivf_flat(args, sq8=False):
     probe.close()
     opts = xb.SearchOptions(top_k=IVF_K, nprobe=IVF_NPROBE,
                             refine_scale=IVF_SQ_SCALE if sq8 else 0.0)
-    ms, scan_ms, e2e_ms, st, clocks = time_search(sharded(index, world, local), queries, opts, args, dev,
-                                                  world, local)
-    cpu = None
+    search = sharded(index, world, local)
+    ms, scan_ms, e2e_ms, st, clocks = time_search(search, queries, opts, args, dev, world, local)
+    gpu_res = gpu_results_host(search, queries, opts) if host_rows is not None else None
+    cpu, parity = None, None
     if host_rows is not None:
         from oracle.oracle import L2 as OL2, Oracle
         allrows = np.concatenate(host_rows)
@@ -789,19 +836,30 @@ def run_ivf_flat(args, sq8=False):
         if sq8:
             codes, params = ora.quantize_int8_batch(allrows)
             t0 = time.perf_counter()
-            ora.ivf_sq8_search(OL2, codes, params, allrows, all_keys, cents.cpu().numpy(),
-                               offsets, positions, qs, IVF_K, IVF_NPROBE,
-                               refine_scale=IVF_SQ_SCALE, threads=threads)
+            ost, rk, rs, rc, _ = ora.ivf_sq8_search(OL2, codes, params, allrows, all_keys,
+                                                    cents.cpu().numpy(), offsets, positions, qs,
+                                                    IVF_K, IVF_NPROBE, refine_scale=IVF_SQ_SCALE,
+                                                    threads=threads)
         else:
             t0 = time.perf_counter()
-            ora.ivf_flat_search(OL2, allrows, all_keys, cents.cpu().numpy(), offsets, positions,
-                                qs, IVF_K, IVF_NPROBE, threads=threads)
+            ost, rk, rs, rc, _ = ora.ivf_flat_search(OL2, allrows, all_keys, cents.cpu().numpy(),
+                                                     offsets, positions, qs, IVF_K, IVF_NPROBE,
+                                                     threads=threads)
         dt = time.perf_counter() - t0
-        cpu = {"value": qs.shape[0] / dt, "unit": "queries/sec", "cores": threads, "kind": "port",
-               "sample": f"{qs.shape[0]} queries over the full index, {dt:.1f} s on {threads} "
-                         "threads (lists from the GPU assignment"
-                         + (", codes from the oracle's quantizer" if sq8 else "")
-                         + ", not timed)"}
+        if not args.no_cpu_baseline:
+            cpu = {"value": qs.shape[0] / dt, "unit": "queries/sec", "cores": threads,
+                   "kind": "port",
+                   "sample": f"{qs.shape[0]} queries over the full index, {dt:.1f} s on "
+                             f"{threads} threads (lists from the GPU assignment"
+                             + (", codes from the oracle's quantizer" if sq8 else "")
+                             + ", not timed)"}
+        if not args.no_parity and ost == 0:
+            # The same oracle run is the parity check of those queries.
+            parity = parity_record(gpu_res, (rk, rs, rc), np.arange(qs.shape[0]), n, "port", dt,
+                                   ("oracle SQ-IVF search + refine" if sq8 else
+                                    "oracle IVF exact search")
+                                   + " over the full index (lists from the GPU assignment)",
+                                   how="first of the batch")
     if rank == 0:
         _, hbm_peak, peak_kind = peaks()
         # Per scanned row: the float32 row, or the INT8 codes and the row's
@@ -824,8 +882,10 @@ def run_ivf_flat(args, sq8=False):
         if sq8:
             config["refine_scale"] = IVF_SQ_SCALE
         dtype = "i8 codes, f32/f64 scores" if sq8 else "f32"
-        print(json.dumps(common_line(nq, ms, e2e_ms, args, world, dtype, config, roof, cpu, clocks,
-                                     st, IVF_K, PQ_DIM, 4)), flush=True)
+        line = common_line(nq, ms, e2e_ms, args, world, dtype, config, roof, cpu, clocks, st,
+                           IVF_K, PQ_DIM, 4)
+        line["parity"] = parity
+        print(json.dumps(line), flush=True)
     finish_ranks(world)
 
 
@@ -930,6 +990,7 @@ def cpu_flat_l2_qps(rows, queries):
 # codes; 10,000 queries; top-k 10 with ScaleFactor 4 (40 codes refined).
 # ---------------------------------------------------------------------------
 SQ_N, SQ_DIM, SQ_K, SQ_SCALE, SQ_CHUNK_ROWS = 20_000_000, 1024, 10, 4.0, 500_000
+SQ_PARITY_QUERIES = 16
 SQ_WORKLOAD = ("INT8 scalar-quantized Flat IP search with FP32 refinement, 20,000,000 x 1024 "
                "(N(0,1) x per-dimension U(0.5,2)), 10,000 queries, top-k=10, ScaleFactor 4")
 
@@ -963,8 +1024,39 @@ def run_sq8(args):
     queries = sq_rows(torch, scale, 10**6, nq, dev).contiguous()
     torch.cuda.synchronize()
     opts = xb.SearchOptions(top_k=SQ_K, refine_scale=SQ_SCALE)
-    ms, scan_ms, e2e_ms, st, clocks = time_search(sharded(index, world, local), queries, opts, args, dev,
-                                                  world, local)
+    search = sharded(index, world, local)
+    ms, scan_ms, e2e_ms, st, clocks = time_search(search, queries, opts, args, dev, world, local)
+    # Parity of sampled queries over all n rows: the oracle quantizes every
+    # row (regenerated chunk by chunk on rank 0), keeps each chunk's 40 best
+    # codes per query, merges them and refines the 40 with the originals.
+    gpu_res = gpu_results_host(search, queries, opts)
+    parity = None
+    if rank == 0 and not args.no_parity:
+        from oracle.oracle import IP as OIP
+        qids = sample_query_ids(nq, SQ_PARITY_QUERIES)
+        qs = queries[torch.as_tensor(qids, device=dev)].cpu().numpy()
+        ora, kind = oracle_with_kernels()
+        threads = os.cpu_count() or 1
+        cand = max(1, int(SQ_K * SQ_SCALE))
+        lists = [[] for _ in qids]
+        t0 = time.perf_counter()
+        for c0 in range(0, n, SQ_CHUNK_ROWS):
+            m = min(SQ_CHUNK_ROWS, n - c0)
+            rows = sq_rows(torch, scale, c0 // SQ_CHUNK_ROWS, m, dev).cpu().numpy()
+            codes, params = ora.quantize_int8_batch(rows, threads)
+            keys = np.arange(c0, c0 + m, dtype=np.uint64)
+            st_, ok, os_, oc, ost = ora.sq8_search(OIP, codes, params, rows, keys, qs, cand,
+                                                   threads=threads)
+            if st_ != 0:
+                raise RuntimeError(f"oracle SQ8 status {st_}")
+            for i in range(len(qids)):
+                kk = ok[i, :oc[i]]
+                lists[i].append((kk, os_[i, :oc[i]], rows[(kk - c0).astype(np.int64)]))
+            del rows, codes, params
+        rk, rs, rc = merged_refine(ora, OIP, cand, SQ_K, lists, qs)
+        parity = parity_record(gpu_res, (rk, rs, rc), qids, n, kind, time.perf_counter() - t0,
+                               "oracle SQ8 Flat IP + refine over all rows (each chunk's 40 best "
+                               "codes merged, then the exact refine)")
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         m = min(args.cpu_sample_rows // 10, n)
@@ -981,8 +1073,10 @@ def run_sq8(args):
                   "dim": SQ_DIM, "metric": "ip", "refine_scale": SQ_SCALE,
                   "parallelism": f"rows sharded over {world} GPU(s), NCCL all-gather + merge",
                   "l2": "inputs larger than L2 (20 GB codes)"}
-        print(json.dumps(common_line(nq, ms, e2e_ms, args, world, "i8 codes, f32/f64 scores",
-                                     config, roof, cpu, clocks, st, SQ_K, SQ_DIM, 4)), flush=True)
+        line = common_line(nq, ms, e2e_ms, args, world, "i8 codes, f32/f64 scores", config, roof,
+                           cpu, clocks, st, SQ_K, SQ_DIM, 4)
+        line["parity"] = parity
+        print(json.dumps(line), flush=True)
     finish_ranks(world)
 
 
@@ -1162,6 +1256,7 @@ def cpu_sq8_qps(sample, queries, n_total):
 # signs; 10,000 queries; top-k 10 with EF 100 (10x over-fetch) and Refine.
 # ---------------------------------------------------------------------------
 RQ_N, RQ_DIM, RQ_NC, RQ_K, RQ_EF, RQ_CHUNK_ROWS = 10_000_000, 960, 16, 10, 100, 500_000
+RQ_PARITY_QUERIES = 16
 RQ_WORKLOAD = ("RaBitQ 1-bit L2 search with exact FP32 refinement, 10,000,000 x 960 "
                "(1,000-cluster mixture), 16 clusters, 10,000 queries, top-k=10, EF 100")
 # The same data with the reference's default TotalBits 7 (6 extra bits); the
@@ -1202,12 +1297,47 @@ def run_rabitq(args, total_bits=1):
     queries = pq_mixture(torch, centers, 3 * 10**6, nq, dev).contiguous()
     torch.cuda.synchronize()
     opts = xb.SearchOptions(top_k=RQ_K, ef=RQ_EF, refine=True)
-    ms, scan_ms, e2e_ms, st, clocks = time_search(sharded(index, world, local), queries, opts, args, dev,
-                                                  world, local)
+    search = sharded(index, world, local)
+    ms, scan_ms, e2e_ms, st, clocks = time_search(search, queries, opts, args, dev, world, local)
     sweep = None
     if args.batch_sweep and world == 1:
-        sweep = batch_sweep(sharded(index, world, local), queries, opts,
-                            [int(x) for x in args.batch_sweep.split(",")])
+        sweep = batch_sweep(search, queries, opts, [int(x) for x in args.batch_sweep.split(",")])
+    # Parity of sampled queries over all n rows: the oracle encodes every row
+    # (regenerated chunk by chunk on rank 0), keeps each chunk's EF best
+    # estimates per query, merges them and refines the EF with the originals.
+    gpu_res = gpu_results_host(search, queries, opts)
+    parity = None
+    if rank == 0 and not args.no_parity:
+        from oracle.oracle import L2 as OL2
+        qids = sample_query_ids(nq, RQ_PARITY_QUERIES)
+        qs = queries[torch.as_tensor(qids, device=dev)].cpu().numpy()
+        ora, kind = oracle_with_kernels()
+        threads = os.cpu_count() or 1
+        cents_h = cents.cpu().numpy()
+        lists = [[] for _ in qids]
+        t0 = time.perf_counter()
+        for c0 in range(0, n, RQ_CHUNK_ROWS):
+            m = min(RQ_CHUNK_ROWS, n - c0)
+            rows = pq_mixture(torch, centers, 2 * 10**6 + c0 // RQ_CHUNK_ROWS, m,
+                              dev).cpu().numpy()
+            codes, extra, factors = ora.rabitq_encode_rows(OL2, cents_h, signs, rows, total_bits,
+                                                           extra_scale, threads)
+            keys = np.arange(c0, c0 + m, dtype=np.uint64)
+            st_, ok, os_, oc, ost = ora.rabitq_search(OL2, cents_h, signs, codes, factors, rows,
+                                                      keys, qs, RQ_EF, RQ_EF, threads=threads,
+                                                      refine=False, total_bits=total_bits,
+                                                      extra=extra)
+            if st_ != 0:
+                raise RuntimeError(f"oracle RaBitQ status {st_}")
+            for i in range(len(qids)):
+                kk = ok[i, :oc[i]]
+                lists[i].append((kk, os_[i, :oc[i]], rows[(kk - c0).astype(np.int64)]))
+            del rows, codes, extra, factors
+        rk, rs, rc = merged_refine(ora, OL2, min(n, max(RQ_K, RQ_EF)), RQ_K, lists, qs)
+        parity = parity_record(gpu_res, (rk, rs, rc), qids, n, kind, time.perf_counter() - t0,
+                               f"oracle RaBitQ ({total_bits}-bit) linear search + refine over "
+                               "all rows (each chunk's EF best estimates merged, then the exact "
+                               "refine)")
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         m = min(args.cpu_sample_rows // 50, n)
@@ -1245,6 +1375,7 @@ def run_rabitq(args, total_bits=1):
         line = common_line(nq, ms, e2e_ms, args, world, dtype, config, roof, cpu, clocks, st,
                            RQ_K, RQ_DIM, 4)
         line["exact_queries"] = int(st["exact_queries"])
+        line["parity"] = parity
         if sweep is not None:
             line["batch_sweep"] = sweep
         print(json.dumps(line), flush=True)
@@ -1353,6 +1484,29 @@ def run_rabitq_hnsw(args):
     hit = sum(len(set(gw[0][q, :int(gw[2][q])].tolist()) & set(gl[0][q, :int(gl[2][q])].tolist()))
               for q in range(nq))
     recall = hit / float(max(1, int(gl[2].sum())))
+    # Parity of sampled queries: the oracle's walk over the same graph, every
+    # row regenerated and encoded by the oracle.
+    parity = None
+    if not args.no_parity:
+        from oracle.oracle import L2 as OL2
+        qids = sample_query_ids(nq, RQ_PARITY_QUERIES)
+        qs = queries[torch.as_tensor(qids, device=dev)].cpu().numpy()
+        ora, kind = oracle_with_kernels()
+        t0 = time.perf_counter()
+        host = np.concatenate([
+            pq_mixture(torch, centers, 2 * 10**6 + c, min(RQ_CHUNK_ROWS, n - c * RQ_CHUNK_ROWS),
+                       dev).cpu().numpy()
+            for c in range((n + RQ_CHUNK_ROWS - 1) // RQ_CHUNK_ROWS)])
+        cents_h = cents.cpu().numpy()
+        codes, _, factors = ora.rabitq_encode_rows(OL2, cents_h, signs, host)
+        ost, rk, rs, rc, _ = ora.hnsw_rabitq_search(
+            OL2, cents_h, signs, codes, factors, host, np.arange(n, dtype=np.uint64),
+            (max_level, entry, offsets.reshape(-1), neighbors), qs, RQ_K, RQ_EF)
+        if ost != 0:
+            raise RuntimeError(f"oracle HNSW-RaBitQ status {ost}")
+        parity = parity_record(gw, (rk, rs, rc), qids, n, kind, time.perf_counter() - t0,
+                               "oracle HNSW-RaBitQ walk + refine over the same graph")
+        del host, codes, factors
     # Bytes the walk reads per query: codes (padded / 8) + factors (48) per
     # estimate; the walk is latency-bound, so no roofline fraction is claimed.
     roof = {"bound": "latency", "achieved": None, "peak": None, "unit": None, "frac": None,
@@ -1366,6 +1520,114 @@ def run_rabitq_hnsw(args):
                        None, clocks, st, RQ_K, RQ_DIM, 4)
     line["linear_scan"] = {"ms_per_step": lin_ms, "queries_per_sec": nq / (lin_ms / 1000.0)}
     line["walk_recall_vs_linear"] = recall
+    line["parity"] = parity
+    print(json.dumps(line), flush=True)
+    finish_ranks(world)
+
+
+# DiskANN with the PQ frontier: 1,000,000 x 128 float32 from the 10,000-cluster
+# mixture; a degree-32 graph built here (each row's 24 nearest rows by the
+# library's FP16 Flat search plus 8 random rows, the entry the row nearest the
+# mean); the traversal PQ model TrainPQ's on the GPU (32 chunks); ListSize 100,
+# MaxDegree 32 (1 sector per node: read batches of 128 nodes); 10,000 queries,
+# top-k 10.
+DK_N, DK_DIM, DK_DEGREE, DK_RANDOM, DK_CHUNKS, DK_LIST, DK_K = (
+    1_000_000, 128, 32, 8, 32, 100, 10)
+DK_PARITY_QUERIES, DK_CPU_QUERIES = 16, 2000
+DK_WORKLOAD = ("DiskANN L2 graph search with the PQ frontier, 1,000,000 x 128 float32 "
+               "(10,000-cluster mixture), degree-32 graph (24 nearest + 8 random links), PQ 32 "
+               "x 256, ListSize 100, 10,000 queries, top-k=10")
+
+
+def run_diskann(args):
+    import numpy as np
+    import torch
+
+    import xvec_b200 as xb
+    world, rank, local, dev = init_ranks(args)
+    if world != 1:
+        raise SystemExit("diskann_l2 runs on one GPU (the graph is not sharded)")
+    n = args.n if args.n != N_BASE else DK_N
+    nq = args.nq
+    g = torch.Generator(device=dev).manual_seed(4321)
+    centers = torch.randn(PQ_CLUSTERS, DK_DIM, generator=g, device=dev)
+    rows = torch.cat([pq_mixture(torch, centers, 5 * 10**6 + c,
+                                 min(PQ_CHUNK_ROWS, n - c * PQ_CHUNK_ROWS), dev)
+                      for c in range((n + PQ_CHUNK_ROWS - 1) // PQ_CHUNK_ROWS)]).contiguous()
+    host = rows.cpu().numpy()
+    t0 = time.perf_counter()
+    chunk_offsets, pivots = xb.pq_train(xb.METRIC_L2, host, chunks=DK_CHUNKS, seed=DK_CHUNKS,
+                                        device=local)
+    pq_s = time.perf_counter() - t0
+    index = xb.DiskANNIndex(DK_DIM, xb.METRIC_L2, device=local)
+    index.set_model(pivots, DK_CHUNKS)
+    keys = torch.arange(n, dtype=torch.int64, device=dev)
+    index.add_device(keys.data_ptr(), rows.data_ptr(), n, torch.cuda.current_stream().cuda_stream)
+    t0 = time.perf_counter()
+    near = knn_graph_level(xb, torch, rows, DK_DEGREE - DK_RANDOM, dev)
+    rng = np.random.default_rng(17)
+    nbrs = np.concatenate([near, rng.integers(0, n, (n, DK_RANDOM)).astype(np.int32)], axis=1)
+    offsets = np.arange(0, n * DK_DEGREE + 1, DK_DEGREE, dtype=np.int64)
+    entry = int(torch.argmin(((rows - rows.mean(dim=0)) ** 2).sum(dim=1)).item())
+    index.set_graph(entry, DK_DEGREE, offsets, nbrs.reshape(-1))
+    graph_s = time.perf_counter() - t0
+    del rows
+    queries = pq_mixture(torch, centers, 6 * 10**6, nq, dev).contiguous()
+    torch.cuda.synchronize()
+    opts = xb.SearchOptions(top_k=DK_K, ef=DK_LIST)
+    search = sharded(index, world, local)
+    ms, walk_ms, e2e_ms, st, clocks = time_search(search, queries, opts, args, dev, world, local)
+    lin_opts = xb.SearchOptions(top_k=DK_K, linear=True)
+    lin_ms, _, _, _, _ = time_search(search, queries, lin_opts, args, dev, world, local)
+    gw = gpu_results_host(search, queries, opts)
+    gl = gpu_results_host(search, queries, lin_opts)
+    hit = sum(len(set(gw[0][q, :int(gw[2][q])].tolist()) & set(gl[0][q, :int(gl[2][q])].tolist()))
+              for q in range(nq))
+    recall = hit / float(max(1, int(gl[2].sum())))
+    parity, cpu = None, None
+    if not (args.no_parity and args.no_cpu_baseline):
+        from oracle.oracle import L2 as OL2
+        ora, kind = oracle_with_kernels()
+        threads = os.cpu_count() or 1
+        codes = ora.pq_encode_rows(OL2, pivots, chunk_offsets, host, threads)
+        norms = np.zeros(n, np.float32)
+        beam = 128  # diskANNReadBatchSize of 648-byte node records
+        graph = (entry, offsets, nbrs.reshape(-1))
+        all_keys = np.arange(n, dtype=np.uint64)
+        if not args.no_parity:
+            qids = sample_query_ids(nq, DK_PARITY_QUERIES)
+            qs = queries[torch.as_tensor(qids, device=dev)].cpu().numpy()
+            t0 = time.perf_counter()
+            ost, rk, rs, rc, _ = ora.diskann_search(OL2, pivots, chunk_offsets, codes, norms, host,
+                                                    all_keys, graph, beam, qs, DK_K, DK_LIST,
+                                                    threads=threads)
+            if ost != 0:
+                raise RuntimeError(f"oracle DiskANN status {ost}")
+            parity = parity_record(gw, (rk, rs, rc), qids, n, kind, time.perf_counter() - t0,
+                                   "oracle DiskANN traversal over the same graph and PQ model")
+        if not args.no_cpu_baseline:
+            qs = queries[:min(nq, DK_CPU_QUERIES)].cpu().numpy()
+            t0 = time.perf_counter()
+            ora.diskann_search(OL2, pivots, chunk_offsets, codes, norms, host, all_keys, graph,
+                               beam, qs, DK_K, DK_LIST, threads=threads)
+            dt = time.perf_counter() - t0
+            cpu = {"value": qs.shape[0] / dt, "unit": "queries/sec", "cores": threads,
+                   "kind": "port",
+                   "sample": f"{qs.shape[0]} queries over the full index, {dt:.2f} s on "
+                             f"{threads} threads (one query per thread)"}
+    roof = {"bound": "latency", "achieved": None, "peak": None, "unit": None, "frac": None,
+            "traffic": None, "kernel": "diskann_search_kernel", "kernel_ms": walk_ms,
+            "note": "one block per query; rounds of up to 128 expansions with a sorted merge"}
+    config = {"workload": DK_WORKLOAD, "global_batch": nq, "top_k": DK_K, "base_vectors": n,
+              "dim": DK_DIM, "metric": "l2", "pq_chunks": DK_CHUNKS, "list_size": DK_LIST,
+              "degree": DK_DEGREE, "read_batch": 128,  # 648-byte node records: 1 sector
+              "graph_build_s": graph_s, "pq_train_s": pq_s, "parallelism": "one GPU",
+              "l2": "inputs smaller than L2 (512 MB rows, 32 MB codes): a graph walk"}
+    line = common_line(nq, ms, e2e_ms, args, world, "f32 rows, u8 PQ codes, f64 sums", config,
+                       roof, cpu, clocks, st, DK_K, DK_DIM, 4)
+    line["linear_scan"] = {"ms_per_step": lin_ms, "queries_per_sec": nq / (lin_ms / 1000.0)}
+    line["recall_vs_exact"] = recall
+    line["parity"] = parity
     print(json.dumps(line), flush=True)
     finish_ranks(world)
 
@@ -1387,6 +1649,47 @@ def cpu_rabitq_qps(cents, signs, sample, queries, n_total, total_bits=1, extra_s
             "cores": threads, "kind": "port",
             "sample": f"{queries.shape[0]} queries x {sample.shape[0]}-row sample, {dt:.1f} s on "
                       f"{threads} threads; QPS scaled by rows/{n_total}"}
+
+
+PQ_PARITY_QUERIES = 8
+
+
+def ivfpq_parity(torch, centers, cents, pivots, labels, queries, gpu_res, n, dev):
+    import numpy as np
+
+    from oracle.oracle import L2 as OL2
+    ora, kind = oracle_with_kernels()
+    threads = os.cpu_count() or 1
+    qids = sample_query_ids(queries.shape[0], PQ_PARITY_QUERIES)
+    qs = queries[torch.as_tensor(qids, device=dev)].cpu().numpy()
+    t0 = time.perf_counter()
+    probed = np.unique(np.concatenate([ora.ivf_probe(OL2, cents, q, PQ_NPROBE) for q in qs]))
+    pos = np.nonzero(np.isin(labels, probed))[0]
+    rows = np.empty((pos.size, PQ_DIM), np.float32)
+    for c0 in range(0, n, PQ_CHUNK_ROWS):
+        m = min(PQ_CHUNK_ROWS, n - c0)
+        lo, hi = np.searchsorted(pos, [c0, c0 + m])
+        if hi == lo:
+            continue
+        chunk = pq_mixture(torch, centers, c0 // PQ_CHUNK_ROWS, m, dev)
+        sel = torch.as_tensor(pos[lo:hi] - c0, device=dev)
+        rows[lo:hi] = chunk[sel].cpu().numpy()
+        del chunk
+    offsets = ora.pq_chunk_offsets(PQ_DIM, PQ_CHUNKS)
+    codes = ora.pq_encode_rows(OL2, pivots, offsets, rows, threads)
+    lab = labels[pos]
+    list_offsets = np.zeros(cents.shape[0] + 1, np.int64)
+    list_offsets[1:] = np.cumsum(np.bincount(lab, minlength=cents.shape[0]))
+    list_positions = np.argsort(lab, kind="stable").astype(np.int64)
+    st, rk, rs, rc, ost = ora.ivfpq_search(OL2, cents, pivots, offsets, codes,
+                                           pos.astype(np.uint64), list_offsets, list_positions,
+                                           qs, PQ_K, PQ_NPROBE, threads=threads)
+    if st != 0:
+        raise RuntimeError(f"oracle IVF-PQ status {st}")
+    return parity_record(gpu_res, (rk, rs, rc), qids, n, kind, time.perf_counter() - t0,
+                         f"oracle IVF-PQ search (its own probe of the {cents.shape[0]} centroids, "
+                         f"the {pos.size} rows of the probed lists PQ-encoded by the oracle; "
+                         "lists from the GPU assignment)")
 
 
 def cpu_ivfpq_qps(cents, pivots, list_sizes, queries):
@@ -1439,6 +1742,8 @@ def main():
         return run_sq4(args)
     if args.workload == "pq_train_l2":
         return run_pq_train(args)
+    if args.workload == "diskann_l2":
+        return run_diskann(args)
     if args.workload == "rabitq_hnsw_l2_refine":
         return run_rabitq_hnsw(args)
 

@@ -205,6 +205,13 @@ class Oracle:
                                               _f32p, ctypes.c_int32, ctypes.c_int32,
                                               ctypes.c_int32, ctypes.c_int32, ctypes.c_float,
                                               _u32p, ctypes.c_int32, _u64p, _f32p, _i32p, _i32p]
+        lib.xo_pq_encode_rows.argtypes = [ctypes.c_int, _f32p, _i32p, ctypes.c_int32,
+                                          ctypes.c_int32, _f32p, ctypes.c_int64, ctypes.c_int32,
+                                          _u8p]
+        lib.xo_rabitq_encode_rows.argtypes = [ctypes.c_int, ctypes.c_int32, _f32p, ctypes.c_int32,
+                                              _u8p, ctypes.c_int32, ctypes.c_double, _f32p,
+                                              ctypes.c_int64, ctypes.c_int32, _u8p, _u8p,
+                                              ctypes.c_int64, ctypes.c_void_p]
         lib.xo_diskann_code_norms.argtypes = [_f32p, _i32p, ctypes.c_int32, ctypes.c_int32,
                                               _u8p, ctypes.c_int64, _f32p]
         lib.xo_diskann_code_norms.restype = None
@@ -656,6 +663,43 @@ class Oracle:
             factors[i] = (f.cluster, 0, f.coarse_add, f.coarse_rescale, f.coarse_error,
                           f.full_add, f.full_rescale)
         return codes, extra[:, :self.rabitq_extra_bytes(d, total_bits)].copy(), factors
+
+    def pq_encode_rows(self, metric, pivots, offsets, rows, threads=0):
+        """PQModel.EncodeBatch (pq.go:303-330) of every row, threaded."""
+        pivots = _c(pivots, np.float32)
+        offsets = _c(offsets, np.int32)
+        rows = _c(rows, np.float32)
+        n, d = rows.shape
+        chunks = offsets.size - 1
+        codes = np.zeros((n, chunks), np.uint8)
+        st = self.lib.xo_pq_encode_rows(metric, _ptr(pivots, _f32p), _ptr(offsets, _i32p), chunks,
+                                        d, _ptr(rows, _f32p), n, threads or os.cpu_count(),
+                                        _ptr(codes, _u8p))
+        if st != OK:
+            raise ValueError(f"encode rows: status {st}")
+        return codes
+
+    def rabitq_encode_rows(self, metric, centroids, signs, rows, total_bits=1, extra_scale=0.0,
+                           threads=0):
+        """rabitq_encode_batch over `threads` workers."""
+        centroids = _c(centroids, np.float32)
+        signs = _c(signs, np.uint8)
+        rows = _c(rows, np.float32)
+        n, d = rows.shape
+        padded = self.rabitq_padded_dimension(d)
+        xbytes = self.rabitq_extra_bytes(d, total_bits)
+        stride = max(1, xbytes)
+        codes = np.zeros((n, padded // 8), np.uint8)
+        extra = np.zeros((n, stride), np.uint8)
+        factors = np.zeros(n, RABITQ_FACTORS_DTYPE)
+        st = self.lib.xo_rabitq_encode_rows(metric, d, _ptr(centroids, _f32p), centroids.shape[0],
+                                            _ptr(signs, _u8p), total_bits, extra_scale,
+                                            _ptr(rows, _f32p), n, threads or os.cpu_count(),
+                                            _ptr(codes, _u8p), _ptr(extra, _u8p), stride,
+                                            factors.ctypes.data)
+        if st != OK:
+            raise ValueError(f"encode rows: status {st}")
+        return codes, extra[:, :xbytes].copy(), factors
 
     def rabitq_estimate(self, rotated, qsum, gadd, gerr, total_bits, code, extra, factors_row):
         rotated = _c(rotated, np.float32)

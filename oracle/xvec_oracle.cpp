@@ -2312,3 +2312,38 @@ extern "C" int xo_diskann_search(int metric, int32_t d, const float* pivots,
   }
   return first;
 }
+
+// ---------------------------------------------------------------------------
+// Batch encoders for the full-size checks: PQModel.EncodeBatch (pq.go:303-330)
+// and RaBitQModel.Encode (rabitq.go:297-327) of n rows over `threads`
+// workers; a row's code does not depend on the split.  The first failing
+// row's status is returned.
+// ---------------------------------------------------------------------------
+extern "C" int xo_pq_encode_rows(int metric, const float* pivots, const int32_t* offsets,
+                                 int32_t chunks, int32_t d, const float* rows, int64_t n,
+                                 int32_t threads, uint8_t* codes) {
+  std::vector<int> st(n > 0 ? (size_t)n : 1, XO_OK);
+  parallel_for(n, threads, [&](int64_t i) {
+    st[i] = xo_pq_encode(metric, pivots, offsets, chunks, d, rows + i * d, codes + i * chunks);
+  });
+  for (int64_t i = 0; i < n; ++i)
+    if (st[i] != XO_OK) return st[i];
+  return XO_OK;
+}
+
+extern "C" int xo_rabitq_encode_rows(int metric, int32_t d, const float* centroids, int32_t nc,
+                                     const uint8_t* signs, int32_t total_bits, double extra_scale,
+                                     const float* rows, int64_t n, int32_t threads,
+                                     uint8_t* binary_codes, uint8_t* extra_codes,
+                                     int64_t extra_stride, xo_rabitq_factors* factors) {
+  const int32_t bytes = xo_rabitq_padded_dimension(d) / 8;
+  std::vector<int> st(n > 0 ? (size_t)n : 1, XO_OK);
+  parallel_for(n, threads, [&](int64_t i) {
+    st[i] = xo_rabitq_encode(metric, d, centroids, nc, signs, total_bits, extra_scale,
+                             rows + i * d, binary_codes + i * bytes,
+                             extra_codes + i * extra_stride, &factors[i]);
+  });
+  for (int64_t i = 0; i < n; ++i)
+    if (st[i] != XO_OK) return st[i];
+  return XO_OK;
+}

@@ -253,6 +253,16 @@ int xo_hnsw_rabitq_search(int metric, int32_t d, const float* centroids, int32_t
                           int32_t threads, uint64_t* out_keys, float* out_scores,
                           int32_t* out_counts, int32_t* out_status);
 
+/* Threaded batch forms of xo_pq_encode and xo_rabitq_encode (codes [n][chunks];
+ * sign bits [n][padded/8], extra codes [n][extra_stride] with extra_stride >= 1,
+ * factors [n]); the first failing row's status. */
+int xo_pq_encode_rows(int metric, const float* pivots, const int32_t* offsets, int32_t chunks,
+                      int32_t d, const float* rows, int64_t n, int32_t threads, uint8_t* codes);
+int xo_rabitq_encode_rows(int metric, int32_t d, const float* centroids, int32_t nc,
+                          const uint8_t* signs, int32_t total_bits, double extra_scale,
+                          const float* rows, int64_t n, int32_t threads, uint8_t* binary_codes,
+                          uint8_t* extra_codes, int64_t extra_stride, xo_rabitq_factors* factors);
+
 /* diskANNPQCodeNorms (diskann.go:292-323): float32 of the float64 sum of the
  * squared pivot components of each code, chunk by chunk. */
 void xo_diskann_code_norms(const float* pivots, const int32_t* offsets, int32_t chunks, int32_t d,

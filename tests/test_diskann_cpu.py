@@ -125,3 +125,21 @@ def test_read_batch_follows_the_layout():
     assert Oracle.diskann_read_batch(128, 64) == 128
     assert Oracle.diskann_read_batch(960, 64) == 64  # 4104-byte records: 2 sectors
     assert Oracle.diskann_read_batch(128, 2048) == 42  # 8712 bytes: 3 sectors
+
+
+def test_batch_encoders_equal_the_row_encoders(oracle):
+    rng = np.random.default_rng(4)
+    rows = rng.standard_normal((300, 70)).astype(np.float32)
+    offsets = oracle.pq_chunk_offsets(70, 9)
+    pivots = rng.standard_normal((256, 70)).astype(np.float32)
+    codes = oracle.pq_encode_rows(L2, pivots, offsets, rows)
+    for i in range(0, 300, 37):
+        st, c = oracle.pq_encode(L2, pivots, offsets, rows[i])
+        assert st == OK and np.array_equal(c, codes[i])
+    cents = rows[:5].copy()
+    signs = rng.integers(0, 256, 4 * oracle.rabitq_padded_dimension(70) // 8, dtype=np.uint8)
+    for bits, scale in [(1, 0.0), (4, 24.0)]:
+        a = oracle.rabitq_encode_rows(L2, cents, signs, rows, bits, scale)
+        b = oracle.rabitq_encode_batch(L2, cents, signs, rows, bits, scale)
+        assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1])
+        assert a[2].tobytes() == b[2].tobytes()

@@ -1349,27 +1349,18 @@ __global__ void __launch_bounds__(kLutThreads, 1) rabitq_lut_scan_kernel(
     }
     const uint32_t* mine = stage + tid * 32;
     float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
-    // Byte j of a word selects row (byte) of column j * 32 + w: the byte
-    // offset byte * 512 is the byte shifted into bits 9..16, and column j
-    // adds 128 j bytes (the load's immediate).  32-bit shared addresses;
-    // volatile keeps the loads on this side of the step's barriers.
-    const uint32_t lut_s = (uint32_t)__cvta_generic_to_shared(lut);
-    const uint32_t mine_s = (uint32_t)__cvta_generic_to_shared(mine);
+    // Byte j of word w selects row (byte) of column j * 32 + w: the float
+    // offset byte * 128 is the byte shifted into bits 7..14.  Plain shared
+    // loads, so that the compiler overlaps the words of several iterations.
 #pragma unroll 8
     for (int g = 0; g < 32; ++g) {
       const uint32_t w = (uint32_t)(g + lane) & 31u;
-      uint32_t word;
-      asm volatile("ld.shared.u32 %0, [%1];" : "=r"(word) : "r"(mine_s + w * 4));
-      const uint32_t col = lut_s + w * 4;
-      float t0, t1, t2, t3;
-      asm volatile("ld.shared.f32 %0, [%1];" : "=f"(t0) : "r"(col + ((word << 9) & 0x1fe00u)));
-      asm volatile("ld.shared.f32 %0, [%1+128];" : "=f"(t1) : "r"(col + ((word << 1) & 0x1fe00u)));
-      asm volatile("ld.shared.f32 %0, [%1+256];" : "=f"(t2) : "r"(col + ((word >> 7) & 0x1fe00u)));
-      asm volatile("ld.shared.f32 %0, [%1+384];" : "=f"(t3) : "r"(col + ((word >> 15) & 0x1fe00u)));
-      acc0 += t0;
-      acc1 += t1;
-      acc2 += t2;
-      acc3 += t3;
+      const uint32_t word = mine[w];
+      const float* col = lut + w;
+      acc0 += col[(word << 7) & 0x7f80u];
+      acc1 += col[((word >> 1) & 0x7f80u) + 32];
+      acc2 += col[((word >> 9) & 0x7f80u) + 64];
+      acc3 += col[((word >> 17) & 0x7f80u) + 96];
     }
     const float dot = (acc0 + acc1) + (acc2 + acc3);
     if (ok) {
