@@ -1525,18 +1525,30 @@ def run_rabitq_hnsw(args):
     finish_ranks(world)
 
 
-# DiskANN with the PQ frontier: 1,000,000 x 128 float32 from the 10,000-cluster
-# mixture; a degree-32 graph built here (each row's 24 nearest rows by the
-# library's FP16 Flat search plus 8 random rows, the entry the row nearest the
-# mean); the traversal PQ model TrainPQ's on the GPU (32 chunks); ListSize 100,
-# MaxDegree 32 (1 sector per node: read batches of 128 nodes); 10,000 queries,
-# top-k 10.
+# DiskANN with the PQ frontier: 1,000,000 x 128 float32 of low intrinsic
+# dimension (a 1,000-cluster mixture in 16 latent dimensions, sigma 0.5,
+# projected to 128 by a fixed Gaussian matrix, plus N(0, 0.05^2) noise: the
+# shape of descriptor data, on which a nearest-neighbour graph is navigable);
+# a degree-32 graph built here (each row's 24 nearest rows by the library's
+# FP16 Flat search plus 8 random rows, the entry the row nearest the mean);
+# the traversal PQ model TrainPQ's on the GPU (32 chunks); ListSize 100,
+# MaxDegree 32 (1 sector per node: read batches of 128 nodes); 10,000
+# queries from the same distribution, top-k 10.
 DK_N, DK_DIM, DK_DEGREE, DK_RANDOM, DK_CHUNKS, DK_LIST, DK_K = (
     1_000_000, 128, 32, 8, 32, 100, 10)
 DK_PARITY_QUERIES, DK_CPU_QUERIES = 16, 2000
+DK_LATENT, DK_CLUSTERS, DK_SIGMA, DK_NOISE = 16, 1000, 0.5, 0.05
 DK_WORKLOAD = ("DiskANN L2 graph search with the PQ frontier, 1,000,000 x 128 float32 "
-               "(10,000-cluster mixture), degree-32 graph (24 nearest + 8 random links), PQ 32 "
-               "x 256, ListSize 100, 10,000 queries, top-k=10")
+               "(1,000-cluster mixture in 16 latent dimensions projected to 128, plus noise), "
+               "degree-32 graph (24 nearest + 8 random links), PQ 32 x 256, ListSize 100, "
+               "10,000 queries, top-k=10")
+
+
+def dk_rows(torch, proj, centers, tag, rows, device):
+    g = torch.Generator(device=device).manual_seed(11_000_003 + tag)
+    idx = torch.randint(0, centers.shape[0], (rows,), generator=g, device=device)
+    z = centers[idx] + DK_SIGMA * torch.randn(rows, centers.shape[1], generator=g, device=device)
+    return z @ proj + DK_NOISE * torch.randn(rows, proj.shape[1], generator=g, device=device)
 
 
 def run_diskann(args):
@@ -1549,10 +1561,11 @@ def run_diskann(args):
         raise SystemExit("diskann_l2 runs on one GPU (the graph is not sharded)")
     n = args.n if args.n != N_BASE else DK_N
     nq = args.nq
-    g = torch.Generator(device=dev).manual_seed(4321)
-    centers = torch.randn(PQ_CLUSTERS, DK_DIM, generator=g, device=dev)
-    rows = torch.cat([pq_mixture(torch, centers, 5 * 10**6 + c,
-                                 min(PQ_CHUNK_ROWS, n - c * PQ_CHUNK_ROWS), dev)
+    g = torch.Generator(device=dev).manual_seed(1616)
+    proj = torch.randn(DK_LATENT, DK_DIM, generator=g, device=dev) / DK_LATENT ** 0.5
+    centers = torch.randn(DK_CLUSTERS, DK_LATENT, generator=g, device=dev)
+    rows = torch.cat([dk_rows(torch, proj, centers, c, min(PQ_CHUNK_ROWS, n - c * PQ_CHUNK_ROWS),
+                              dev)
                       for c in range((n + PQ_CHUNK_ROWS - 1) // PQ_CHUNK_ROWS)]).contiguous()
     host = rows.cpu().numpy()
     t0 = time.perf_counter()
@@ -1572,7 +1585,7 @@ def run_diskann(args):
     index.set_graph(entry, DK_DEGREE, offsets, nbrs.reshape(-1))
     graph_s = time.perf_counter() - t0
     del rows
-    queries = pq_mixture(torch, centers, 6 * 10**6, nq, dev).contiguous()
+    queries = dk_rows(torch, proj, centers, 10**6, nq, dev).contiguous()
     torch.cuda.synchronize()
     opts = xb.SearchOptions(top_k=DK_K, ef=DK_LIST)
     search = sharded(index, world, local)

@@ -38,6 +38,7 @@
 #include "flat_kernels.cuh"
 #include "flat_tc.cuh"
 #include "index_kernels.cuh"
+#include "pipeline.cuh"
 #include "select.cuh"
 
 namespace xvec {
@@ -49,6 +50,8 @@ constexpr int kDiskMaxCap = 2048;     // capacity = min(n, max(TopK, ListSize))
 constexpr int kDiskCand = 2048;       // neighbour slots per merge step (also the degree bound)
 constexpr int kDiskMaxBeam = 128;     // MaxDiskANNReadSectors (diskann_storage.go:31)
 constexpr int kDiskVisitCap = 16384;  // visited nodes recorded per slot for the reset
+constexpr int kDiskSmemChunks = 64;   // PQ tables up to 64 KB go to shared memory
+constexpr int kDiskPerThread = kDiskCand / kDiskThreads;  // slots per thread in a step
 constexpr int kDefaultListSize = 300; // DefaultDiskANNQueryList (diskann.go:36)
 constexpr unsigned kNoError = 0xffffffffu;
 
@@ -82,12 +85,71 @@ struct DiskArgs {
 // diskANNApproximateScore (diskann.go:653-676): the table lookup summed in
 // float64 in chunk order (PQDistanceTable.Lookup, pq.go:574-595), and for
 // MIPSL2 the conversion through the code and query norms.  0, or the
-// failing status.
+// failing status.  `table` is the query's [chunks][256] table in shared or
+// global memory; codes of 16-byte multiples are read as 16-byte vectors.
 __device__ __forceinline__ int disk_pq_score(const DiskArgs& a, const float* table, double qn,
                                              uint32_t id, float* out) {
   const uint8_t* code = a.codes + (int64_t)id * a.chunks;
   double s = 0.0;
-  for (int c = 0; c < a.chunks; ++c) s = __dadd_rn(s, (double)__ldg(table + c * 256 + code[c]));
+  if ((a.chunks & 15) == 0) {
+    const uint4* cv = reinterpret_cast<const uint4*>(code);
+    for (int c0 = 0; c0 < a.chunks; c0 += 16) {
+      const uint4 v = __ldg(cv + (c0 >> 4));
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const uint32_t b = (w[j >> 2] >> (8 * (j & 3))) & 0xffu;
+        s = __dadd_rn(s, (double)table[(c0 + j) * 256 + b]);
+      }
+    }
+  } else {
+    for (int c = 0; c < a.chunks; ++c) s = __dadd_rn(s, (double)table[c * 256 + code[c]]);
+  }
+  if (isnan(s) || isinf(s) || s > (double)FLT_MAX || s < -(double)FLT_MAX) return XVEC_GPU_OVERFLOW;
+  const float score = __double2float_rn(s);
+  if (a.metric != kMetricMIPS) {
+    *out = score;
+    return 0;
+  }
+  const double cn = (double)a.code_norms[id];
+  const double inner = __ddiv_rn(__dsub_rn(__dadd_rn(qn, cn), (double)score), 2.0);
+  const double den = go_maxd(qn, cn);
+  if (den == 0.0) {
+    *out = 0.f;
+    return 0;
+  }
+  const double conv = __dsub_rn(2.0, __ddiv_rn(__dmul_rn(2.0, inner), den));
+  if (isnan(conv) || isinf(conv) || conv > (double)FLT_MAX || conv < -(double)FLT_MAX)
+    return XVEC_GPU_OVERFLOW;
+  *out = __double2float_rn(conv);
+  return 0;
+}
+
+// The float64 chunk-order sum of a code held in registers (16 or 32 bytes).
+// TREE: the query's table makes every partial sum exact in float64 (see
+// the kernel), so four interleaved accumulators give the same bits as the
+// chunk-order chain with a quarter of its latency.
+template <bool TREE>
+__device__ __forceinline__ double pq_sum_codes(const float* table, const uint4 (&cv)[2], int vec) {
+  double s[4] = {0.0, 0.0, 0.0, 0.0};
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    if (h >= vec) break;
+    const uint32_t w[4] = {cv[h].x, cv[h].y, cv[h].z, cv[h].w};
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const uint32_t b = (w[j >> 2] >> (8 * (j & 3))) & 0xffu;
+      const int acc = TREE ? (j & 3) : 0;
+      s[acc] = __dadd_rn(s[acc], (double)table[(h * 16 + j) * 256 + b]);
+    }
+  }
+  return TREE ? __dadd_rn(__dadd_rn(s[0], s[1]), __dadd_rn(s[2], s[3])) : s[0];
+}
+
+// diskANNApproximateScore after the lookup sum: the overflow check of
+// Lookup and the MIPSL2 conversion.
+__device__ __forceinline__ int disk_pq_finish(const DiskArgs& a, const float* table, double qn,
+                                              uint32_t id, double s, float* out) {
   if (isnan(s) || isinf(s) || s > (double)FLT_MAX || s < -(double)FLT_MAX) return XVEC_GPU_OVERFLOW;
   const float score = __double2float_rn(s);
   if (a.metric != kMetricMIPS) {
@@ -171,21 +233,44 @@ __device__ __forceinline__ int block_exclusive_sum(int v, int* total) {
   return base + incl - v;
 }
 
+// Sorts the n (<= kDiskThreads) distinct keys of a into out by rank: each
+// key's position is the number of keys below it (one pass, no stages).
+__device__ __forceinline__ void block_rank_sort(const uint64_t* a, int n, uint64_t* out) {
+  const int t = threadIdx.x;
+  if (t < n) {
+    const uint64_t x = a[t];
+    int r = 0;
+    for (int j = 0; j < n; ++j) r += a[j] < x;
+    out[r] = x;
+  }
+}
+
 // Shared-memory layout of the search block (bytes).
 struct DiskSmem {
   int capA, k;
-  size_t r0, r1, e0, e1, k0, k1, x, bk, bid, bdeg, gb, fresh, total;
-  __host__ __device__ DiskSmem(int cap_alloc, int k_alloc) : capA(cap_alloc), k(k_alloc) {
+  size_t tbl, r0, r1, e0, e1, k0, k1, x, x2, hist, bk, bk2, boff, bid, bdeg, gb, nbs, work, fresh,
+      total;
+  __host__ __device__ DiskSmem(int cap_alloc, int k_alloc, int table_floats)
+      : capA(cap_alloc), k(k_alloc) {
     size_t o = 0;
+    tbl = o; o += (size_t)table_floats * 4;
     r0 = o; o += (size_t)capA * 8;
     r1 = o; o += (size_t)capA * 8;
     k0 = o; o += (size_t)k * 8;
     k1 = o; o += (size_t)k * 8;
     x = o; o += (size_t)kDiskCand * 8;
+    hist = o; o += 256 * 4;
     bk = o; o += (size_t)kDiskMaxBeam * 8;
+    bk2 = o; o += (size_t)kDiskMaxBeam * 8;
+    boff = o; o += (size_t)kDiskMaxBeam * 8;
     bid = o; o += (size_t)kDiskMaxBeam * 4;
     bdeg = o; o += (size_t)(kDiskMaxBeam + 1) * 4;
     gb = o; o += (size_t)(kDiskMaxBeam + 1) * 4;
+    // The step's neighbour ids and claimed nodes, dead once the step's
+    // candidates are scored, share their 16 KB with the sorted candidates.
+    nbs = o; o += (size_t)kDiskCand * 4;
+    work = o; o += (size_t)kDiskCand * 4;
+    x2 = nbs;
     e0 = o; o += (size_t)capA;
     e1 = o; o += (size_t)capA;
     fresh = o; o += (size_t)kDiskCand;
@@ -194,31 +279,42 @@ struct DiskSmem {
 };
 
 // One block per query slot; the slot's blocks take queries blockIdx.x,
-// blockIdx.x + gridDim.x, ...
-__global__ void __launch_bounds__(kDiskThreads) diskann_search_kernel(DiskArgs a, int capA) {
+// blockIdx.x + gridDim.x, ...  SMEM_TABLE: the query's PQ table is copied
+// into shared memory (chunks <= kDiskSmemChunks).
+template <bool SMEM_TABLE>
+__global__ void __launch_bounds__(kDiskThreads, 3) diskann_search_kernel(DiskArgs a, int capA) {
   extern __shared__ __align__(16) unsigned char smem[];
-  const DiskSmem L(capA, a.k);
+  const DiskSmem L(capA, a.k, SMEM_TABLE ? a.chunks * 256 : 0);
+  float* T = reinterpret_cast<float*>(smem + L.tbl);
   uint64_t* R[2] = {reinterpret_cast<uint64_t*>(smem + L.r0),
                     reinterpret_cast<uint64_t*>(smem + L.r1)};
   uint8_t* E[2] = {smem + L.e0, smem + L.e1};
   uint64_t* K[2] = {reinterpret_cast<uint64_t*>(smem + L.k0),
                     reinterpret_cast<uint64_t*>(smem + L.k1)};
   uint64_t* X = reinterpret_cast<uint64_t*>(smem + L.x);
+  uint64_t* X2 = reinterpret_cast<uint64_t*>(smem + L.x2);
+  int* HIST = reinterpret_cast<int*>(smem + L.hist);
   uint64_t* BK = reinterpret_cast<uint64_t*>(smem + L.bk);
+  uint64_t* BK2 = reinterpret_cast<uint64_t*>(smem + L.bk2);
+  int64_t* BOFF = reinterpret_cast<int64_t*>(smem + L.boff);
   uint32_t* BID = reinterpret_cast<uint32_t*>(smem + L.bid);
   int* BDEG = reinterpret_cast<int*>(smem + L.bdeg);
   int* GB = reinterpret_cast<int*>(smem + L.gb);
+  uint32_t* NB = reinterpret_cast<uint32_t*>(smem + L.nbs);
+  uint32_t* WORK = reinterpret_cast<uint32_t*>(smem + L.work);
   uint8_t* FRESH = smem + L.fresh;
-  __shared__ int s_r, s_cur, s_kc, s_kcur, s_xc, s_ngroups, s_vcount, s_pq_fail, s_status;
-  __shared__ unsigned s_err_pos;
+  __shared__ int s_r, s_cur, s_kc, s_kcur, s_xc, s_ngroups, s_vcount, s_pq_fail, s_status, s_wc;
+  __shared__ int s_safe, s_valid, s_emax, s_emin, s_xn;
+  __shared__ unsigned s_err_pos, s_maxabs;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   uint32_t* vis = a.visited + (int64_t)blockIdx.x * a.words;
   uint32_t* vrec = a.vrec + (int64_t)blockIdx.x * kDiskVisitCap;
   const unsigned stride = (unsigned)a.max_degree + 1;  // error positions: node j, slot 0..degree
+  const int tsize = a.chunks * 256;
 
   for (int q = blockIdx.x; q < a.nq; q += gridDim.x) {
     const float* qv = a.qf + (int64_t)q * a.d;
-    const float* table = a.table + (int64_t)q * a.chunks * 256;
+    const float* gtable = a.table + (int64_t)q * tsize;
     const double qn = a.qnorm[q];
     int status = a.q_status[q];
     if (status == 0 && (a.q_flags[q] & 4)) status = XVEC_GPU_NON_FINITE;
@@ -226,9 +322,49 @@ __global__ void __launch_bounds__(kDiskThreads) diskann_search_kernel(DiskArgs a
       if (tid == 0) a.out_counts[q] = status ? -status : 0;
       continue;
     }
+    // The table (copied when in shared memory) and its largest magnitude:
+    // while chunks x that stays below MaxFloat32 no lookup can overflow, and
+    // the claims need not remember which slots saw a node unvisited.
+    // Also the span of its non-zero entries' exponents: every entry is a
+    // multiple of 2^(e_min - 150) and a sum of at most 32 of them is below
+    // 2^(e_max - 121), so with e_max - e_min <= 24 every partial sum is exact
+    // in float64 and the lookup may add in any order.
+    if (tid == 0) {
+      s_maxabs = 0u;
+      s_emax = 0;
+      s_emin = 255;
+    }
+    __syncthreads();
+    float mx = 0.f;
+    int emax = 0, emin = 255;
+    for (int i = tid; i < tsize; i += kDiskThreads) {
+      const float v = gtable[i];
+      if (SMEM_TABLE) T[i] = v;
+      mx = fmaxf(mx, fabsf(v));
+      const uint32_t bits = __float_as_uint(v) & 0x7fffffffu;
+      if (bits != 0u) {
+        const int e = max(1, (int)(bits >> 23));
+        emax = max(emax, e);
+        emin = min(emin, e);
+      }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+      mx = fmaxf(mx, __shfl_xor_sync(kFullMask, mx, o));
+      emax = max(emax, __shfl_xor_sync(kFullMask, emax, o));
+      emin = min(emin, __shfl_xor_sync(kFullMask, emin, o));
+    }
+    if (lane == 0) {
+      atomicMax(&s_maxabs, __float_as_uint(mx));  // non-negative floats order as ints
+      atomicMax(&s_emax, emax);
+      atomicMin(&s_emin, emin);
+    }
+    __syncthreads();
+    const float* table = SMEM_TABLE ? T : gtable;
     // The entry point (diskann.go:588-597).
     if (tid == 0) {
       const uint32_t entry = (uint32_t)a.entry;
+      s_safe = a.metric != kMetricMIPS &&
+               (double)__uint_as_float(s_maxabs) * (double)a.chunks < 1e38;
       float es = 0.f;
       s_status = disk_pq_score(a, table, qn, entry, &es);
       R[0][0] = disk_node_key(a.traversal, es, entry);
@@ -243,6 +379,8 @@ __global__ void __launch_bounds__(kDiskThreads) diskann_search_kernel(DiskArgs a
       atomicOr(vis + (entry >> 5), 1u << (entry & 31));
     }
     __syncthreads();
+    const bool safe = s_safe != 0;
+    const bool tree = s_emax - s_emin <= 24;
     // Rounds (diskann.go:600-649); each expands at least one node, so there
     // are at most n of them.
     while (s_status == 0) {
@@ -263,33 +401,69 @@ __global__ void __launch_bounds__(kDiskThreads) diskann_search_kernel(DiskArgs a
       if (nb == 0) break;
       __syncthreads();
       // Exact scores (metric.Compute(query, node.Vector)), one warp per node,
-      // into the round's collector keys (filter, radius: :709-721).
-      for (int j = warp; j < nb; j += kDiskWarps) {
-        const uint32_t id = BID[j];
-        const float s = warp_reference_score<float>(a.metric, a.rows + (int64_t)id * a.d, qv, a.d);
-        if (lane == 0) {
+      // into the round's collector keys (filter, radius: :709-721).  The
+      // warp's rows are prefetched first, so their loads overlap.
+      {
+        const int row_bytes = a.d * 4;
+        for (int j = warp; j < nb; j += kDiskWarps) {
+          const char* rp = reinterpret_cast<const char*>(a.rows + (int64_t)BID[j] * a.d);
+          for (int off = lane * 128; off < row_bytes; off += 32 * 128)
+            asm volatile("prefetch.global.L1 [%0];" ::"l"(rp + off));
+        }
+      }
+      // From d = 16 on the two half-warps score two nodes at once.
+      const int per_warp = a.d >= 16 ? 2 : 1;
+      for (int j0 = warp * per_warp; j0 < nb; j0 += kDiskWarps * per_warp) {
+        const int j = per_warp == 2 ? j0 + (lane >> 4) : j0;
+        const bool has = j < nb;
+        const uint32_t id = BID[has ? j : j0];
+        const float sc = warp_reference_score<float>(a.metric, a.rows + (int64_t)id * a.d, qv, a.d);
+        if ((lane & 15) == 0 && has && (per_warp == 2 || lane == 0)) {
           uint64_t key = kEmptyKey;
-          if (!finite_f(s)) atomicMin(&s_err_pos, (unsigned)j * stride);
-          else if (bitmap_pass(a.bitmap, id) && within_radius(a.metric, s, a.radius))
-            key = pack_rank(rank_from_score(a.metric, s) + 0.f, a.keyrank[id]);
+          if (!finite_f(sc)) atomicMin(&s_err_pos, (unsigned)j * stride);
+          else if (bitmap_pass(a.bitmap, id) && within_radius(a.metric, sc, a.radius))
+            key = pack_rank(rank_from_score(a.metric, sc) + 0.f, a.keyrank[id]);
           BK[j] = key;
         }
       }
-      for (int j = nb + tid; j < kDiskMaxBeam; j += kDiskThreads) BK[j] = kEmptyKey;
-      // Neighbour slots of the batch, in merge steps of at most kDiskCand.
-      if (tid == 0) {
-        int acc = 0, g = 0;
-        GB[0] = 0;
-        BDEG[0] = 0;
-        for (int j = 0; j < nb; ++j) {
-          const int dg = (int)(a.goff[BID[j] + 1] - a.goff[BID[j]]);
-          if (acc + dg > kDiskCand && j > GB[g]) {
-            GB[++g] = j;
-            acc = 0;
-          }
-          BDEG[j + 1] = BDEG[j] + dg;
-          acc += dg;
+      // Neighbour slots of the batch, in merge steps of at most kDiskCand:
+      // the nodes' list offsets and degrees (one thread per node), their
+      // prefix sums (warp 0), the steps (thread 0, from shared memory).
+      if (tid < nb) {
+        const int64_t o0 = a.goff[BID[tid]];
+        BOFF[tid] = o0;
+        BDEG[tid + 1] = (int)(a.goff[BID[tid] + 1] - o0);
+      }
+      __syncthreads();
+      if (warp == 0) {
+        constexpr int kPer = kDiskMaxBeam / 32;
+        int v[kPer], run = 0;
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) {
+          const int j = lane * kPer + i;
+          run += j < nb ? BDEG[j + 1] : 0;
+          v[i] = run;
         }
+        int incl = run;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int t = __shfl_up_sync(kFullMask, incl, o);
+          if (lane >= o) incl += t;
+        }
+        const int before = incl - run;
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) {
+          const int j = lane * kPer + i;
+          if (j < nb) BDEG[j + 1] = before + v[i];
+        }
+        if (lane == 0) BDEG[0] = 0;
+      }
+      __syncthreads();
+      if (tid == 0) {
+        int g = 0;
+        GB[0] = 0;
+        for (int j = 1; j < nb; ++j)
+          if (BDEG[j + 1] - BDEG[GB[g]] > kDiskCand) GB[++g] = j;
         GB[++g] = nb;
         s_ngroups = g;
       }
@@ -297,65 +471,199 @@ __global__ void __launch_bounds__(kDiskThreads) diskann_search_kernel(DiskArgs a
       const int ngroups = s_ngroups;
       for (int g = 0; g < ngroups; ++g) {
         const int j0 = GB[g], j1 = GB[g + 1], base = BDEG[j0];
-        // Which slots saw an unvisited node before this step (L2 reads: the
-        // bitmap changes through atomics).
-        for (int j = j0 + warp; j < j1; j += kDiskWarps) {
-          const int64_t o = a.goff[BID[j]];
-          const int dg = BDEG[j + 1] - BDEG[j];
-          for (int e = lane; e < dg; e += 32) {
-            const uint32_t nbid = (uint32_t)a.nbrs[o + e];
-            FRESH[BDEG[j] - base + e] = ((__ldcg(vis + (nbid >> 5)) >> (nbid & 31)) & 1u) == 0;
+        const int slots = BDEG[j1] - base;
+        // The step's neighbour ids (node of a slot by a binary search of the
+        // prefix sums), and which of them were unvisited before the step (L2
+        // reads: the bitmap changes through atomics; kept only when a lookup
+        // can fail).  A thread takes slots tid + 256 i (at most 8), its loads
+        // issued together.
+        {
+          uint32_t nbv[kDiskPerThread];
+#pragma unroll
+          for (int i = 0; i < kDiskPerThread; ++i) {
+            const int sl = tid + i * kDiskThreads;
+            nbv[i] = 0;
+            if (sl < slots) {
+              int lo = j0, hi = j1 - 1;
+              while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (BDEG[mid] - base <= sl) lo = mid;
+                else hi = mid - 1;
+              }
+              nbv[i] = (uint32_t)__ldg(a.nbrs + BOFF[lo] + (sl + base - BDEG[lo]));
+            }
+          }
+          uint32_t vw[kDiskPerThread];
+#pragma unroll
+          for (int i = 0; i < kDiskPerThread; ++i) {
+            const int sl = tid + i * kDiskThreads;
+            if (sl < slots) {
+              NB[sl] = nbv[i];
+              if (!safe) vw[i] = __ldcg(vis + (nbv[i] >> 5));
+            }
+          }
+          if (!safe) {
+#pragma unroll
+            for (int i = 0; i < kDiskPerThread; ++i) {
+              const int sl = tid + i * kDiskThreads;
+              if (sl < slots) FRESH[sl] = ((vw[i] >> (nbv[i] & 31)) & 1u) == 0;
+            }
           }
         }
         if (tid == 0) {
           s_xc = 0;
+          s_wc = 0;
           s_pq_fail = 0;
         }
         __syncthreads();
-        const int rr = s_r, rc = s_cur;
+        // Claims: the first slot to set a node's bit queues it for scoring
+        // (a warp's winners take their queue places with one atomic).
+        {
+          uint32_t old[kDiskPerThread];
+#pragma unroll
+          for (int i = 0; i < kDiskPerThread; ++i) {
+            const int sl = tid + i * kDiskThreads;
+            old[i] = 0xffffffffu;
+            if (sl < slots && (safe || FRESH[sl]))
+              old[i] = atomicOr(vis + (NB[sl] >> 5), 1u << (NB[sl] & 31));
+          }
+#pragma unroll
+          for (int i = 0; i < kDiskPerThread; ++i) {
+            const int sl = tid + i * kDiskThreads;
+            const uint32_t nbid = sl < slots ? NB[sl] : 0u;
+            const bool won = sl < slots && ((old[i] >> (nbid & 31)) & 1u) == 0;
+            const unsigned m = __ballot_sync(kFullMask, won);
+            if (m == 0u) continue;
+            const int leader = __ffs(m) - 1;
+            int wbase = 0, vbase = 0;
+            if (lane == leader) {
+              wbase = atomicAdd(&s_wc, __popc(m));
+              vbase = atomicAdd(&s_vcount, __popc(m));
+            }
+            wbase = __shfl_sync(kFullMask, wbase, leader);
+            vbase = __shfl_sync(kFullMask, vbase, leader);
+            if (won) {
+              const int r = __popc(m & ((1u << lane) - 1u));
+              WORK[wbase + r] = nbid;
+              if (vbase + r < kDiskVisitCap) vrec[vbase + r] = nbid;
+            }
+          }
+        }
+        __syncthreads();
+        const int rr = s_r, rc = s_cur, wc = s_wc;
         const uint64_t worst = rr >= a.cap ? R[rc][rr - 1] : kEmptyKey;
-        // Claims: the first slot to set a node's bit scores it.
-        for (int j = j0 + warp; j < j1; j += kDiskWarps) {
-          const int64_t o = a.goff[BID[j]];
-          const int dg = BDEG[j + 1] - BDEG[j];
-          for (int e = lane; e < dg; e += 32) {
-            if (!FRESH[BDEG[j] - base + e]) continue;
-            const uint32_t nbid = (uint32_t)a.nbrs[o + e];
-            const uint32_t bit = 1u << (nbid & 31);
-            if (atomicOr(vis + (nbid >> 5), bit) & bit) continue;
-            const int vi = atomicAdd(&s_vcount, 1);
-            if (vi < kDiskVisitCap) vrec[vi] = nbid;
+        // PQ scores of the claimed nodes; those that beat a full retained
+        // set's worst join the step's candidates.  Codes of 16 or 32 bytes:
+        // two items per thread at a time, their code loads issued together.
+        if (a.chunks == 16 || a.chunks == 32) {
+          const int vec = a.chunks >> 4;
+          for (int c0 = 0; c0 < wc; c0 += 2 * kDiskThreads) {
+            uint4 cv[2][2];
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+              const int c = c0 + tid + i * kDiskThreads;
+              if (c < wc) {
+                const uint4* src = reinterpret_cast<const uint4*>(a.codes + (int64_t)WORK[c] * a.chunks);
+                cv[i][0] = __ldg(src);
+                cv[i][1] = vec > 1 ? __ldg(src + 1) : make_uint4(0u, 0u, 0u, 0u);
+              }
+            }
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+              const int c = c0 + tid + i * kDiskThreads;
+              bool keep = false;
+              uint64_t key = 0;
+              if (c < wc) {
+                const uint32_t nbid = WORK[c];
+                const double sum = tree ? pq_sum_codes<true>(table, cv[i], vec)
+                                        : pq_sum_codes<false>(table, cv[i], vec);
+                float ps;
+                if (disk_pq_finish(a, table, qn, nbid, sum, &ps)) {
+                  s_pq_fail = 1;
+                } else {
+                  key = disk_node_key(a.traversal, ps, nbid);
+                  keep = key < worst;
+                }
+              }
+              const unsigned m = __ballot_sync(kFullMask, keep);
+              if (m == 0u) continue;
+              const int leader = __ffs(m) - 1;
+              int xbase = 0;
+              if (lane == leader) xbase = atomicAdd(&s_xc, __popc(m));
+              xbase = __shfl_sync(kFullMask, xbase, leader);
+              if (keep) X[xbase + __popc(m & ((1u << lane) - 1u))] = key;
+            }
+          }
+        } else {
+          for (int c = tid; c < wc; c += kDiskThreads) {
+            const uint32_t nbid = WORK[c];
             float ps;
             if (disk_pq_score(a, table, qn, nbid, &ps)) {
               s_pq_fail = 1;
               continue;
             }
             const uint64_t key = disk_node_key(a.traversal, ps, nbid);
-            if (key >= worst) continue;  // cannot enter a full retained
-            X[atomicAdd(&s_xc, 1)] = key;
+            if (key < worst) X[atomicAdd(&s_xc, 1)] = key;
           }
         }
         __syncthreads();
         if (s_pq_fail) {
           // A node's score fails wherever it is scored, so the sequential
           // loop fails at the node's first slot: the least failing slot
-          // among those that saw it unvisited.
-          for (int j = j0 + warp; j < j1; j += kDiskWarps) {
-            const int64_t o = a.goff[BID[j]];
-            const int dg = BDEG[j + 1] - BDEG[j];
-            for (int e = lane; e < dg; e += 32) {
-              if (!FRESH[BDEG[j] - base + e]) continue;
-              float ps;
-              if (disk_pq_score(a, table, qn, (uint32_t)a.nbrs[o + e], &ps))
-                atomicMin(&s_err_pos, (unsigned)j * stride + 1u + (unsigned)e);
+          // among those that saw it unvisited (lookups that can fail are
+          // never `safe`, so FRESH is set).
+          for (int sl = tid; sl < slots; sl += kDiskThreads) {
+            if (!FRESH[sl]) continue;
+            float ps;
+            if (!disk_pq_score(a, table, qn, NB[sl], &ps)) continue;
+            int lo = j0, hi = j1 - 1;
+            while (lo < hi) {
+              const int mid = (lo + hi + 1) >> 1;
+              if (BDEG[mid] - base <= sl) lo = mid;
+              else hi = mid - 1;
             }
+            atomicMin(&s_err_pos, (unsigned)lo * stride + 1u + (unsigned)(sl + base - BDEG[lo]));
           }
+          __syncthreads();  // NB is read here; the sorted candidates reuse it
         }
-        const int xc = s_xc;
+        int xc = s_xc;
         if (xc > 0) {
-          block_sort_u64_fit<kDiskCand>(X, xc);
+          const uint64_t* xs = X;
+          if (xc > kDiskThreads && xc > a.cap) {
+            // Only the step's `capacity` best can enter: keep the keys whose
+            // rank is at most that of the capacity-th best (a radix select
+            // on the rank bits), then order the few that remain.
+            const uint64_t lim = smem_radix_select(X, xc, a.cap, 32, HIST) | 0xffffffffull;
+            if (tid == 0) s_xn = 0;
+            __syncthreads();
+            for (int i0 = warp * 32; i0 < xc; i0 += kDiskThreads) {
+              const int i = i0 + lane;
+              const bool keep = i < xc && X[i] <= lim;
+              const unsigned m = __ballot_sync(kFullMask, keep);
+              if (m == 0u) continue;
+              const int leader = __ffs(m) - 1;
+              int base = 0;
+              if (lane == leader) base = atomicAdd(&s_xn, __popc(m));
+              base = __shfl_sync(kFullMask, base, leader);
+              if (keep) X2[base + __popc(m & ((1u << lane) - 1u))] = X[i];
+            }
+            __syncthreads();
+            xc = s_xn;
+            if (xc <= kDiskThreads) {
+              block_rank_sort(X2, xc, X);
+            } else {
+              block_sort_u64_fit<kDiskCand>(X2, xc);
+              xs = X2;
+            }
+          } else if (xc <= kDiskThreads) {
+            block_rank_sort(X, xc, X2);
+            xs = X2;
+          } else {
+            block_sort_u64_fit<kDiskCand>(X, xc);
+          }
+          __syncthreads();
           const int rn = min(a.cap, rr + xc);
-          merge_runs(R[rc], E[rc], rr, X, xc, R[1 - rc], E[1 - rc], rn);
+          merge_runs(R[rc], E[rc], rr, xs, xc, R[1 - rc], E[1 - rc], rn);
           __syncthreads();
           if (tid == 0) {
             s_r = rn;
@@ -367,12 +675,16 @@ __global__ void __launch_bounds__(kDiskThreads) diskann_search_kernel(DiskArgs a
       if (s_err_pos != kNoError) break;
       // The collector (:709-721): the round's accepted nodes merged into the
       // top-k.
-      block_sort_u64_fit<kDiskMaxBeam>(BK, nb);
-      const int valid = count_less(BK, nb, kEmptyKey);
+      if (tid == 0) s_valid = 0;
+      __syncthreads();
+      if (tid < nb && BK[tid] != kEmptyKey) atomicAdd(&s_valid, 1);
+      block_rank_sort(BK, nb, BK2);  // rejected nodes (kEmptyKey) rank last
+      __syncthreads();
+      const int valid = s_valid;
       const int kc = s_kc, kcur = s_kcur;
       if (valid > 0) {
         const int kn = min(a.k, kc + valid);
-        merge_runs(K[kcur], nullptr, kc, BK, valid, K[1 - kcur], nullptr, kn);
+        merge_runs(K[kcur], nullptr, kc, BK2, valid, K[1 - kcur], nullptr, kn);
         __syncthreads();
         if (tid == 0) {
           s_kc = kn;
@@ -393,10 +705,10 @@ __global__ void __launch_bounds__(kDiskThreads) diskann_search_kernel(DiskArgs a
       const uint64_t* kk = K[s_kcur];
       for (int i = warp; i < kc; i += kDiskWarps) {
         const uint32_t pos = a.pos_of_kr[(uint32_t)kk[i]];
-        const float s = warp_reference_score<float>(a.metric, a.rows + (int64_t)pos * a.d, qv, a.d);
+        const float sc = warp_reference_score<float>(a.metric, a.rows + (int64_t)pos * a.d, qv, a.d);
         if (lane == 0) {
           a.out_keys[(int64_t)q * a.k + i] = a.keys[pos];
-          a.out_scores[(int64_t)q * a.k + i] = s;
+          a.out_scores[(int64_t)q * a.k + i] = sc;
         }
       }
       if (tid == 0) a.out_counts[q] = kc;
@@ -588,13 +900,15 @@ xvec_gpu_status diskann_search_impl(xvec_gpu_index* idx, const float* d_q, int n
   const int wave = (int)std::max<int64_t>(1, std::min<int64_t>(nq, (1ll << 30) / (1024ll * chunks)));
   Scratch table, visited, vrec;
   if ((st = table.alloc((size_t)wave * chunks * 1024, s))) return st;
-  const size_t smem = DiskSmem(cap, k).total;
-  if (smem > 48 * 1024)
-    XVEC_CUDA(cudaFuncSetAttribute(diskann_search_kernel,
-                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  // The query's table in shared memory when it is at most 64 KB.
+  const bool smem_table = chunks <= kDiskSmemChunks;
+  auto kernel = smem_table ? diskann_search_kernel<true> : diskann_search_kernel<false>;
+  const size_t smem = DiskSmem(cap, k, smem_table ? chunks * 256 : 0).total;
+  XVEC_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  XVEC_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 cudaSharedmemCarveoutMaxShared));
   int per_sm = 0, sms = 0;
-  XVEC_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, diskann_search_kernel,
-                                                          kDiskThreads, smem));
+  XVEC_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kDiskThreads, smem));
   XVEC_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, idx->device));
   const int64_t words = std::max<int64_t>(1, (n + 31) / 32);
   // Visited bitmaps of at most 1 GiB in total.
@@ -645,7 +959,7 @@ xvec_gpu_status diskann_search_impl(xvec_gpu_index* idx, const float* d_q, int n
     a.out_keys = d_keys + (int64_t)q0 * k;
     a.out_scores = d_scores + (int64_t)q0 * k;
     a.out_counts = d_counts + q0;
-    diskann_search_kernel<<<std::min(slots, w), kDiskThreads, smem, s>>>(a, cap);
+    kernel<<<std::min(slots, w), kDiskThreads, smem, s>>>(a, cap);
     XVEC_LAUNCHED();
     XVEC_CUDA(cudaGetLastError());
   }

@@ -1228,22 +1228,22 @@ __global__ void rabitq_clear_flags(const int* ids, int n, int* q_flags) {
 }
 
 // Small batches: a scan of the sign bits (n x padded/8 bytes) instead of
-// the tensor-core operand planes (16 x larger).  One block of 16 warps per
+// the tensor-core operand planes (16 x larger).  One block of 32 warps per
 // (row part, query), one part per SM.  The block's query is a byte table in
 // shared memory: entry (b, pos) = the float32 sum of q[8 pos + i] over the
 // set bits i of b, stored at column (pos mod 4) * 32 + pos / 4 of row b (128
 // columns, zero past padded/8).  Steps of 512 rows are staged in shared
 // memory (coalesced 8-byte loads held in registers while the block scores
-// the previous step, rows padded with zeros to 128 bytes); lane l of a warp
-// scores row l, reading its 32 code words in the rotated order
-// w = (g + l) mod 32, so the code reads (bank w) and the four table reads of
-// a word (column j * 32 + w, bank w) of the 32 lanes all hit different
-// banks.  A row's dot is a float32 sum of at most `padded` terms (within the
+// the previous step, rows padded with zeros to 128 bytes); two lanes score a
+// row, each over 16 of its 32 code words read in a rotated order, so the
+// code reads (bank w) and the four table reads of a word (column j * 32 + w,
+// bank w) of the 32 lanes all hit different banks.  A row's dot is a float32 sum of at most `padded` terms (within the
 // FFMA term of q_eps); ranks use the RaBitQRanker formula; keys below the
 // block's threshold go to one block list, compacted to the KP best by a
 // block sort when full.  The parts' lists are then reduced to one list per
 // query (reduce_lists_kernel) for the merge.
-constexpr int kLutThreads = 512;
+constexpr int kLutThreads = 1024;
+constexpr int kLutRows = 512;       // rows per step (two threads per row)
 constexpr int kLutCap = 2048;       // block list entries (kp + one step's appends)
 constexpr int kLutMaxBytes = 128;   // padded / 8 (padded <= 1024)
 
@@ -1257,7 +1257,7 @@ __global__ void __launch_bounds__(kLutThreads, 1) rabitq_lut_scan_kernel(
   extern __shared__ __align__(16) unsigned char smem_raw[];
   float* lut = reinterpret_cast<float*>(smem_raw);                          // [256][128]
   uint32_t* stage = reinterpret_cast<uint32_t*>(lut + 256 * kLutMaxBytes);  // [512][32]
-  uint64_t* list = reinterpret_cast<uint64_t*>(stage + kLutThreads * 32);   // [kLutCap]
+  uint64_t* list = reinterpret_cast<uint64_t*>(stage + kLutRows * 32);      // [kLutCap]
   float* gadd = reinterpret_cast<float*>(list + kLutCap);                   // [nc]
   __shared__ int s_count, s_bad;
   __shared__ unsigned long long s_thr;
@@ -1277,7 +1277,7 @@ __global__ void __launch_bounds__(kLutThreads, 1) rabitq_lut_scan_kernel(
       lut[b * kLutMaxBytes + col] = lut[(b & (b - 1)) * kLutMaxBytes + col] + v[__ffs(b) - 1];
   }
   // Zero padding of the staged rows (bytes past padded/8, never overwritten).
-  for (int i = tid; i < kLutThreads * 32; i += kLutThreads)
+  for (int i = tid; i < kLutRows * 32; i += kLutThreads)
     if ((i & 31) >= bytes / 4) stage[i] = 0u;
   for (int c = tid; c < nc; c += kLutThreads) gadd[c] = q_fast_gadd[(int64_t)q * nc + c];
   if (tid == 0) {
@@ -1288,15 +1288,15 @@ __global__ void __launch_bounds__(kLutThreads, 1) rabitq_lut_scan_kernel(
   const float half_sum = 0.5f * q_fast_sum[q];
   const int64_t begin = (int64_t)part * rows_per_part;
   const int64_t end = min(n, begin + rows_per_part);
-  const int steps = end > begin ? (int)((end - begin + kLutThreads - 1) / kLutThreads) : 0;
+  const int steps = end > begin ? (int)((end - begin + kLutRows - 1) / kLutRows) : 0;
   // Step i's rows [begin + 512 i, ...) as 8-byte words: thread t takes words
-  // t, t + 512, ... of the step's contiguous bytes.
-  const int per_step = kLutThreads * words8;
-  constexpr int kMaxLoads = kLutMaxBytes / 8;  // words per thread per step
+  // t, t + 1024, ... of the step's contiguous bytes.
+  const int per_step = kLutRows * words8;
+  constexpr int kMaxLoads = kLutRows * (kLutMaxBytes / 8) / kLutThreads;  // per thread
   uint2 pre[kMaxLoads];
   auto load_step = [&](int i) {
-    const int64_t r0 = begin + (int64_t)i * kLutThreads;
-    const int64_t words_avail = (min(end, r0 + kLutThreads) - r0) * words8;
+    const int64_t r0 = begin + (int64_t)i * kLutRows;
+    const int64_t words_avail = (min(end, r0 + kLutRows) - r0) * words8;
     const uint2* src = reinterpret_cast<const uint2*>(codes + r0 * bytes);
 #pragma unroll
     for (int k = 0; k < kMaxLoads; ++k) {
@@ -1318,13 +1318,17 @@ __global__ void __launch_bounds__(kLutThreads, 1) rabitq_lut_scan_kernel(
       }
     }
   };
+  // Warp w scores rows 16 w .. 16 w + 15 of a step: lane l takes row
+  // 16 w + (l mod 16) and its words 16 (l / 16) .. 16 (l / 16) + 15; the two
+  // halves are added by a shuffle and the lower half ranks the row.
+  const int row_local = (tid >> 5) * 16 + (lane & 15), half = lane >> 4;
   // The row terms of this thread's row in a step, loaded a step ahead.
   float4 nf = make_float4(0.f, 0.f, 0.f, 0.f);
   uint32_t nkr = 0;
   bool nok = false;
   auto load_terms = [&](int i) {
-    const int64_t row = begin + (int64_t)i * kLutThreads + tid;
-    nok = row < end && bitmap_pass(bitmap, row);
+    const int64_t row = begin + (int64_t)i * kLutRows + row_local;
+    nok = half == 0 && row < end && bitmap_pass(bitmap, row);
     if (nok) {
       nf = fast[row];
       nkr = keyrank[row];
@@ -1347,22 +1351,25 @@ __global__ void __launch_bounds__(kLutThreads, 1) rabitq_lut_scan_kernel(
       load_step(i + 1);
       load_terms(i + 1);
     }
-    const uint32_t* mine = stage + tid * 32;
+    const uint32_t* mine = stage + row_local * 32 + half * 16;
+    const float* lut_h = lut + half * 16;
     float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
     // Byte j of word w selects row (byte) of column j * 32 + w: the float
-    // offset byte * 128 is the byte shifted into bits 7..14.  Plain shared
-    // loads, so that the compiler overlaps the words of several iterations.
+    // offset byte * 128 is the byte shifted into bits 7..14.  The words of a
+    // half are read in the order (g + l) mod 16, so the 32 lanes' code and
+    // table reads hit 32 different banks.
 #pragma unroll 8
-    for (int g = 0; g < 32; ++g) {
-      const uint32_t w = (uint32_t)(g + lane) & 31u;
+    for (int g = 0; g < 16; ++g) {
+      const uint32_t w = (uint32_t)(g + lane) & 15u;
       const uint32_t word = mine[w];
-      const float* col = lut + w;
+      const float* col = lut_h + w;
       acc0 += col[(word << 7) & 0x7f80u];
       acc1 += col[((word >> 1) & 0x7f80u) + 32];
       acc2 += col[((word >> 9) & 0x7f80u) + 64];
       acc3 += col[((word >> 17) & 0x7f80u) + 96];
     }
-    const float dot = (acc0 + acc1) + (acc2 + acc3);
+    float dot = (acc0 + acc1) + (acc2 + acc3);
+    dot += __shfl_xor_sync(kFullMask, dot, 16);
     if (ok) {
       const float rank = fmaf(f.y, dot - half_sum, f.x + gadd[__float_as_int(f.z)]);
       if (!finite_f(rank)) {
@@ -1378,7 +1385,7 @@ __global__ void __launch_bounds__(kLutThreads, 1) rabitq_lut_scan_kernel(
     __syncthreads();  // the stage is read and the appends are in
     if (i + 1 < steps) store_step();
     // Room for the next step's appends: compact to the KP best.
-    if (s_count > kLutCap - kLutThreads) {
+    if (s_count > kLutCap - kLutRows) {
       const int cnt = s_count;
       block_sort_u64<kLutCap>(list, cnt);
       __syncthreads();
@@ -1641,8 +1648,7 @@ xvec_gpu_status rabitq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, idx->device);
     int parts = (int)std::max<int64_t>(1, std::min<int64_t>(sms, (n + 4095) / 4096));
     while (parts > 1 && !reduce_lists_supported(parts, kp)) --parts;
-    const int64_t rows_per_part = ((n + parts - 1) / parts + kLutThreads - 1) / kLutThreads *
-                                  kLutThreads;
+    const int64_t rows_per_part = ((n + parts - 1) / parts + kLutRows - 1) / kLutRows * kLutRows;
     parts = (int)((n + rows_per_part - 1) / rows_per_part);
     const int lstride = reduce_lists_out_cap(kp);
     Scratch pkeys, pcounts, psat, lkeys, lcounts, lsat;
@@ -1652,7 +1658,7 @@ xvec_gpu_status rabitq_search_impl(xvec_gpu_index* idx, const float* d_q, int nq
         (st = lkeys.alloc((size_t)nq * lstride * 8, s)) ||
         (st = lcounts.alloc((size_t)nq * 4, s)) || (st = lsat.alloc((size_t)nq * 8, s)))
       return st;
-    const int smem = kLutMaxBytes * 256 * 4 + kLutThreads * 128 + kLutCap * 8 + nc * 4;
+    const int smem = kLutMaxBytes * 256 * 4 + kLutRows * 128 + kLutCap * 8 + nc * 4;
     cudaFuncSetAttribute(rabitq_lut_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          smem);
     timer.mark(1);
