@@ -1386,11 +1386,14 @@ def run_rabitq(args, total_bits=1):
 # row's 24 nearest rows by the library's FP16 Flat search plus 8 random rows,
 # the long links that make a small-world graph navigable; levels drawn as HNSW
 # draws them, each upper level's nodes linked to their 32 nearest nodes of that
-# level); the same index searched linearly beside it.
+# level); the same index searched linearly beside it.  The rows have low
+# intrinsic dimension (a 1,000-cluster mixture in 16 latent dimensions
+# projected to 960, plus noise), on which such a graph is navigable.
 RH_N, RH_DEGREE, RH_RANDOM = 1_000_000, 32, 8
 RH_WORKLOAD = ("HNSW-RaBitQ 1-bit L2 graph search with exact FP32 refinement, 1,000,000 x 960 "
-               "(1,000-cluster mixture), degree-32 proximity graph (24 nearest + 8 random links), "
-               "16 clusters, 10,000 queries, top-k=10, EF 100")
+               "(1,000-cluster mixture in 16 latent dimensions projected to 960, plus noise), "
+               "degree-32 proximity graph (24 nearest + 8 random links), 16 clusters, 10,000 "
+               "queries, top-k=10, EF 100")
 
 
 def knn_graph_level(xb, torch, vecs, degree, dev):
@@ -1429,11 +1432,16 @@ def run_rabitq_hnsw(args):
     n = args.n if args.n != N_BASE else RH_N
     nq = args.nq
     g = torch.Generator(device=dev).manual_seed(960)
-    centers = torch.randn(CLUSTERS, RQ_DIM, generator=g, device=dev)
-    cents = pq_mixture(torch, centers, 10**6 + 11, RQ_NC, dev).contiguous()
+    proj = torch.randn(DK_LATENT, RQ_DIM, generator=g, device=dev) / DK_LATENT ** 0.5
+    latent = torch.randn(DK_CLUSTERS, DK_LATENT, generator=g, device=dev)
+
+    def gen(tag, m):
+        return dk_rows(torch, proj, latent, tag, m, dev)
+
+    cents = gen(10**6 + 11, RQ_NC).contiguous()
     padded = (RQ_DIM + 63) // 64 * 64
     signs = np.random.default_rng(961).integers(0, 256, 4 * padded // 8, dtype=np.uint8)
-    rows = torch.cat([pq_mixture(torch, centers, 2 * 10**6 + c, min(RQ_CHUNK_ROWS, n - c * RQ_CHUNK_ROWS), dev)
+    rows = torch.cat([gen(2 * 10**6 + c, min(RQ_CHUNK_ROWS, n - c * RQ_CHUNK_ROWS))
                       for c in range((n + RQ_CHUNK_ROWS - 1) // RQ_CHUNK_ROWS)]).contiguous()
     index = xb.RaBitQIndex(RQ_DIM, xb.METRIC_L2, device=local)
     index.set_model(cents.cpu().numpy(), signs)
@@ -1471,7 +1479,7 @@ def run_rabitq_hnsw(args):
     index.set_graph(max_level, entry, offsets.reshape(-1), neighbors)
     graph_s = time.perf_counter() - t0
     del rows
-    queries = pq_mixture(torch, centers, 3 * 10**6, nq, dev).contiguous()
+    queries = gen(3 * 10**6, nq).contiguous()
     torch.cuda.synchronize()
     opts = xb.SearchOptions(top_k=RQ_K, ef=RQ_EF, refine=True)
     search = sharded(index, world, local)
@@ -1494,8 +1502,7 @@ def run_rabitq_hnsw(args):
         ora, kind = oracle_with_kernels()
         t0 = time.perf_counter()
         host = np.concatenate([
-            pq_mixture(torch, centers, 2 * 10**6 + c, min(RQ_CHUNK_ROWS, n - c * RQ_CHUNK_ROWS),
-                       dev).cpu().numpy()
+            gen(2 * 10**6 + c, min(RQ_CHUNK_ROWS, n - c * RQ_CHUNK_ROWS)).cpu().numpy()
             for c in range((n + RQ_CHUNK_ROWS - 1) // RQ_CHUNK_ROWS)])
         cents_h = cents.cpu().numpy()
         codes, _, factors = ora.rabitq_encode_rows(OL2, cents_h, signs, host)

@@ -95,6 +95,20 @@ def test_walk_filter_radius_linear(oracle, xb):
     c["idx"].close()
 
 
+def test_walk_frontier_outgrows_the_first_buffer(oracle, xb):
+    # A filter that passes one row in a hundred keeps the accepted set from
+    # filling, so the frontier holds most visited nodes: more than the first
+    # launch's buffer of 1024 entries, fewer than the second's.
+    c = build(oracle, xb, L2, 1, seed=41)
+    n = c["rows"].shape[0]
+    bitmap = np.zeros((n + 31) // 32, np.uint32)
+    for p in range(0, n, 100):
+        bitmap[p >> 5] |= np.uint32(1 << (p & 31))
+    compare(oracle, xb, c, 10, 50, refine=True, bitmap=bitmap)
+    compare(oracle, xb, c, 10, 50, refine=False, bitmap=bitmap)
+    c["idx"].close()
+
+
 def test_walk_with_repeated_neighbours(oracle, xb):
     """Lists that name a neighbour twice: the reference takes it at its first
     place (the second finds it visited)."""

@@ -735,8 +735,9 @@ struct RaBitQScorer {
 // (searchRaBitQLayer, :644-671, coarse estimates) and the base-layer search
 // (searchRaBitQBase, :673-737) over a graph the caller uploaded
 // (xvec_gpu_rabitq_set_graph).  One warp per query: the warp computes the
-// estimates of a neighbour list 32 at a time (each estimate a warp-wide
-// float64 sum, as the linear scan's exact scorer takes it), and lane 0 then
+// estimates of a neighbour list 32 at a time (lane j the j-th neighbour's,
+// a float64 sum in index order, or in four interleaved parts when the
+// query's sums are exact), and lane 0 then
 // applies the reference's decisions to the neighbours in list order, with
 // the frontier (best first) and the accepted set (worst first) as binary
 // heaps in shared memory.  A node is the packed key (order-preserving
@@ -773,6 +774,7 @@ struct WalkArgs {
   int32_t* vlist;           // [slots][vcap]
   int vcap;
   int nq;
+  const int* qids;          // the queries to walk (null: 0 .. nq - 1)
   int stride;               // output entries per query
   uint64_t* o_keys;
   float* o_scores;
@@ -780,6 +782,9 @@ struct WalkArgs {
   uint32_t* o_pos;
   int* q_flags;
 };
+
+__device__ int walk_finish(const WalkArgs& a, int qi, int64_t row, bool multi, double dot,
+                           float* dist, float* lower);
 
 // EstimateCoarse (full = false) or Estimate (rabitq.go:421-446) of `row`
 // for query qi with makeRaBitQEstimate's checks (:464-476): 0, or the
@@ -807,6 +812,54 @@ __device__ int walk_estimate(const WalkArgs& a, int qi, int64_t row, bool full, 
       }
     dot = __shfl_sync(kFullMask, dot, 0);
   }
+  return walk_finish(a, qi, row, multi, dot, dist, lower);
+}
+
+// One lane's estimate of `row` (the other lanes take other rows): the dot
+// in index order (any order when the query's sums are exact), then
+// walk_finish.
+__device__ int walk_estimate_lane(const WalkArgs& a, int qi, int64_t row, bool full, float* dist,
+                                  float* lower) {
+  const float* q = a.q_rot + (int64_t)qi * a.padded;
+  const bool multi = full && a.total_bits > 1, half = a.total_bits > 8;
+  const bool any_order = a.q_exact[qi] != 0;
+  double acc[4] = {0.0, 0.0, 0.0, 0.0};
+  if (multi) {
+    const uint16_t* vrow = a.values + row * a.padded;
+    for (int i = 0; i < a.padded; i += 8) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(vrow + i);
+      const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const uint16_t v16 = (uint16_t)(w[j >> 1] >> (16 * (j & 1)));
+        const double v = half ? (double)__half2float(__ushort_as_half(v16))
+                              : (double)__bfloat162float(__ushort_as_bfloat16(v16));
+        const int k = any_order ? (j & 3) : 0;
+        acc[k] = __dadd_rn(acc[k], __dmul_rn(v, (double)q[i + j]));
+      }
+    }
+  } else {
+    const uint32_t* words = reinterpret_cast<const uint32_t*>(a.codes + row * (a.padded / 8));
+    for (int wi = 0; wi < a.padded / 32; ++wi) {
+      const uint32_t word = words[wi];
+#pragma unroll 8
+      for (int j = 0; j < 32; ++j) {
+        // An unset bit adds +0, which leaves the sum unchanged (it is never
+        // -0: it starts at +0).
+        const double t = ((word >> j) & 1u) ? (double)q[wi * 32 + j] : 0.0;
+        const int k = any_order ? (j & 3) : 0;
+        acc[k] = __dadd_rn(acc[k], t);
+      }
+    }
+  }
+  const double dot = any_order ? __dadd_rn(__dadd_rn(acc[0], acc[1]), __dadd_rn(acc[2], acc[3]))
+                               : acc[0];
+  return walk_finish(a, qi, row, multi, dot, dist, lower);
+}
+
+// makeRaBitQEstimate's formula and checks (rabitq.go:434-476) given the dot.
+__device__ int walk_finish(const WalkArgs& a, int qi, int64_t row, bool multi, double dot,
+                           float* dist, float* lower) {
   const RaBitQFactors f = a.factors[row];
   const int64_t gi = (int64_t)qi * a.nc + f.cluster;
   double d, eb;
@@ -923,7 +976,8 @@ __global__ void __launch_bounds__(256) hnsw_rabitq_walk_kernel(WalkArgs a) {
   const int slot = blockIdx.x * wpb + wib, slots = gridDim.x * wpb;
   uint32_t* vis = a.visited + (int64_t)slot * a.words;
   int32_t* vl = a.vlist + (int64_t)slot * a.vcap;
-  for (int qi = slot; qi < a.nq; qi += slots) {
+  for (int t = slot; t < a.nq; t += slots) {
+    const int qi = a.qids ? a.qids[t] : t;
     int fail = 0;
     int nvis = 0;  // visited nodes recorded (lane 0's count is the truth)
     // Marks node p visited; true when it was not yet (every lane calls it
@@ -957,15 +1011,8 @@ __global__ void __launch_bounds__(256) hnsw_rabitq_walk_kernel(WalkArgs a) {
           const int64_t nb = lane < cnt ? (int64_t)a.nbrs[e0 + lane] : -1;
           float nd = 0.f, nl = 0.f;
           int nst = 0;
-          for (int j = 0; j < cnt; ++j) {
-            const int64_t p = __shfl_sync(kFullMask, nb, j);
-            float dj, lj;
-            const int sj = walk_estimate(a, qi, p, false, &dj, &lj);
-            if (lane == j) {
-              nd = dj;
-              nst = sj;
-            }
-          }
+          if (lane < cnt) nst = walk_estimate_lane(a, qi, nb, false, &nd, &nl);
+          __syncwarp();
           for (int j = 0; j < cnt; ++j) {
             const int64_t p = __shfl_sync(kFullMask, nb, j);
             const float dj = __shfl_sync(kFullMask, nd, j);
@@ -1024,25 +1071,17 @@ __global__ void __launch_bounds__(256) hnsw_rabitq_walk_kernel(WalkArgs a) {
         float cd = 0.f, cl = 0.f, fd = 0.f;
         int cst = 0, fst = 0;
         const unsigned fm = __ballot_sync(kFullMask, fresh);
-        for (unsigned m = fm; m; m &= m - 1) {
-          const int j = __ffs(m) - 1;
-          const int64_t p = __shfl_sync(kFullMask, nb, j);
-          float dj, lj, fj, unused;
-          const int s1 = walk_estimate(a, qi, p, false, &dj, &lj);
-          int s2 = 0;
-          if (a.total_bits > 1)
-            s2 = walk_estimate(a, qi, p, true, &fj, &unused);
-          else
-            fj = dj;
-          if (lane == j) {
-            cd = dj;
-            cl = lj;
-            cst = s1;
-            fd = fj;
-            fst = s2;
+        // Each unvisited neighbour's estimates by its own lane.
+        if (fresh) {
+          cst = walk_estimate_lane(a, qi, nb, false, &cd, &cl);
+          if (a.total_bits > 1) {
+            float unused;
+            fst = walk_estimate_lane(a, qi, nb, true, &fd, &unused);
+          } else {
+            fd = cd;
           }
         }
-        (void)cd;
+        __syncwarp();
         // The reference's decisions, in list order (lane 0 holds the heaps).
         for (unsigned m = fm; m; m &= m - 1) {
           const int j = __ffs(m) - 1;
@@ -1137,6 +1176,11 @@ __global__ void __launch_bounds__(256) hnsw_rabitq_walk_kernel(WalkArgs a) {
   }
 }
 
+__global__ void clear_flag_bits_kernel(const int* ids, int n, int bit, int* q_flags) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) q_flags[ids[i]] &= ~bit;
+}
+
 // Launches the walk for nq queries: the approximate stage's `top` nodes
 // (refine: the candidate count cc, else k) per query into o_* (stride cc).
 xvec_gpu_status rabitq_graph_walk(xvec_gpu_index* idx, int nq, int k, int ef, int cc,
@@ -1146,28 +1190,12 @@ xvec_gpu_status rabitq_graph_walk(xvec_gpu_index* idx, int nq, int k, int ef, in
   const int64_t n = idx->n;
   const int top = refine ? cc : k;
   const int capacity = std::max(ef, top);
-  const int warps = capacity <= 256 ? 8 : capacity <= 1024 ? 4 : 2;
   int acap2 = 1;
   while (acap2 < capacity + 1) acap2 <<= 1;
-  const int per_warp = (200 * 1024 / 8) / warps;
-  const int fcap = per_warp - acap2;
-  if (fcap < 2 * capacity)
-    return set_error("HNSW-RaBitQ walk: capacity %d is beyond the supported maximum", capacity),
-           XVEC_GPU_INVALID_ARGUMENT;
-  const size_t smem = (size_t)warps * (fcap + acap2) * 8;
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, idx->device);
   const int64_t words = (n + 31) / 32;
-  int64_t slots = std::min<int64_t>((int64_t)sms * warps, ((int64_t)nq + warps - 1) / warps * warps);
-  // The per-warp visited bitmaps stay within 2 GB.
-  while (slots > warps && slots * words * 4 > (2ll << 30)) slots -= warps;
   const int vcap = 65536;
-  Scratch vis, vlist;
-  xvec_gpu_status st;
-  if ((st = vis.alloc((size_t)slots * words * 4, s)) ||
-      (st = vlist.alloc((size_t)slots * vcap * 4, s)))
-    return st;
-  XVEC_CUDA(cudaMemsetAsync(vis.ptr, 0, (size_t)slots * words * 4, s));
   WalkArgs a{};
   a.codes = sc.codes;
   a.factors = sc.factors;
@@ -1194,23 +1222,78 @@ xvec_gpu_status rabitq_graph_walk(xvec_gpu_index* idx, int nq, int k, int ef, in
   a.refine = refine ? 1 : 0;
   a.public_metric = idx->desc.metric;
   a.radius = radius;
-  a.fcap = fcap;
-  a.visited = vis.as<uint32_t>();
-  a.words = words;
-  a.vlist = vlist.as<int32_t>();
   a.vcap = vcap;
-  a.nq = nq;
   a.stride = cc;
   a.o_keys = o_keys;
   a.o_scores = o_scores;
   a.o_counts = o_counts;
   a.o_pos = o_pos;
   a.q_flags = q_flags;
-  XVEC_CUDA(cudaFuncSetAttribute(hnsw_rabitq_walk_kernel,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  hnsw_rabitq_walk_kernel<<<(unsigned)(slots / warps), warps * 32, smem, s>>>(a);
+  // One launch over `count` queries (qids: their ids, or null for all) with
+  // `warps` warps per block and a frontier of fcap entries per warp; the
+  // blocks fill the SMs (several per SM when the frontier is small).
+  auto launch = [&](int count, const int* qids, int warps, int fcap) -> xvec_gpu_status {
+    const size_t smem = (size_t)warps * (fcap + acap2) * 8;
+    XVEC_CUDA(cudaFuncSetAttribute(hnsw_rabitq_walk_kernel,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    int per_sm = 0;
+    XVEC_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, hnsw_rabitq_walk_kernel,
+                                                            warps * 32, smem));
+    int64_t slots = std::min<int64_t>((int64_t)sms * std::max(1, per_sm) * warps,
+                                      ((int64_t)count + warps - 1) / warps * warps);
+    // The per-warp visited bitmaps stay within 2 GB.
+    while (slots > warps && slots * words * 4 > (2ll << 30)) slots -= warps;
+    Scratch vis, vlist;
+    xvec_gpu_status st;
+    if ((st = vis.alloc((size_t)slots * words * 4, s)) ||
+        (st = vlist.alloc((size_t)slots * vcap * 4, s)))
+      return st;
+    XVEC_CUDA(cudaMemsetAsync(vis.ptr, 0, (size_t)slots * words * 4, s));
+    a.fcap = fcap;
+    a.visited = vis.as<uint32_t>();
+    a.words = words;
+    a.vlist = vlist.as<int32_t>();
+    a.nq = count;
+    a.qids = qids;
+    hnsw_rabitq_walk_kernel<<<(unsigned)(slots / warps), warps * 32, smem, s>>>(a);
+    XVEC_LAUNCHED();
+    XVEC_CUDA(cudaGetLastError());
+    return XVEC_GPU_OK;
+  };
+  // The large frontier: 200 KB of shared memory per SM.
+  const int big_warps = capacity <= 256 ? 8 : capacity <= 1024 ? 4 : 2;
+  const int big_fcap = (200 * 1024 / 8) / big_warps - acap2;
+  if (big_fcap < 2 * capacity)
+    return set_error("HNSW-RaBitQ walk: capacity %d is beyond the supported maximum", capacity),
+           XVEC_GPU_INVALID_ARGUMENT;
+  // First a frontier of max(1024, 4 capacity) entries, so that several
+  // blocks share an SM; the queries whose frontier outgrew it walk again with
+  // the large one (a walk's result does not depend on the buffer it used).
+  const int small_fcap = std::max(1024, 4 * capacity);
+  int small_warps = 8;
+  while (small_warps > 1 && (size_t)small_warps * (small_fcap + acap2) * 8 > 72 * 1024)
+    small_warps >>= 1;
+  const bool small_fits = (size_t)small_warps * (small_fcap + acap2) * 8 <= 72 * 1024;
+  if (!small_fits || small_fcap >= big_fcap || nq == 0)
+    return launch(nq, nullptr, big_warps, big_fcap);
+  xvec_gpu_status st = launch(nq, nullptr, small_warps, small_fcap);
+  if (st) return st;
+  std::vector<int> flags(nq);
+  XVEC_CUDA(cudaMemcpyAsync(flags.data(), q_flags, (size_t)nq * 4, cudaMemcpyDeviceToHost, s));
+  XVEC_CUDA(cudaStreamSynchronize(s));
+  std::vector<int> again;
+  for (int q = 0; q < nq; ++q)
+    if (flags[q] & kRaBitQGraphFull) again.push_back(q);
+  if (again.empty()) return XVEC_GPU_OK;
+  Scratch dq;
+  if ((st = dq.alloc(again.size() * 4, s))) return st;
+  XVEC_CUDA(cudaMemcpyAsync(dq.ptr, again.data(), again.size() * 4, cudaMemcpyHostToDevice, s));
+  clear_flag_bits_kernel<<<(unsigned)((again.size() + 255) / 256), 256, 0, s>>>(
+      dq.as<int>(), (int)again.size(), kRaBitQGraphFull, q_flags);
   XVEC_LAUNCHED();
-  XVEC_CUDA(cudaGetLastError());
+  st = launch((int)again.size(), dq.as<int>(), big_warps, big_fcap);
+  if (st) return st;
+  XVEC_CUDA(cudaStreamSynchronize(s));
   return XVEC_GPU_OK;
 }
 
