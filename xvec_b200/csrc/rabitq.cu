@@ -824,10 +824,26 @@ __device__ int walk_estimate_lane(const WalkArgs& a, int qi, int64_t row, bool f
   const bool multi = full && a.total_bits > 1, half = a.total_bits > 8;
   const bool any_order = a.q_exact[qi] != 0;
   double acc[4] = {0.0, 0.0, 0.0, 0.0};
+  // The row's lines are requested up front (each lane reads its own row, so
+  // the loads below would otherwise wait on L2 one after another).
+  {
+    const char* rb = multi ? reinterpret_cast<const char*>(a.values + row * a.padded)
+                           : reinterpret_cast<const char*>(a.codes + row * (a.padded / 8));
+    const int bytes = multi ? a.padded * 2 : a.padded / 8;
+    const uintptr_t first = reinterpret_cast<uintptr_t>(rb) & ~(uintptr_t)127;
+    for (uintptr_t l = first; l < reinterpret_cast<uintptr_t>(rb) + bytes; l += 128)
+      asm volatile("prefetch.global.L1 [%0];" ::"l"(l));
+    asm volatile("prefetch.global.L1 [%0];" ::"l"(a.factors + row));
+  }
+  // The query is read four floats at a time (every lane reads the same
+  // address: one broadcast per warp).
+  const float4* q4 = reinterpret_cast<const float4*>(q);
   if (multi) {
     const uint16_t* vrow = a.values + row * a.padded;
     for (int i = 0; i < a.padded; i += 8) {
       const uint4 raw = *reinterpret_cast<const uint4*>(vrow + i);
+      const float4 qa = __ldg(q4 + (i >> 2)), qb = __ldg(q4 + (i >> 2) + 1);
+      const float qv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
       const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
@@ -835,20 +851,27 @@ __device__ int walk_estimate_lane(const WalkArgs& a, int qi, int64_t row, bool f
         const double v = half ? (double)__half2float(__ushort_as_half(v16))
                               : (double)__bfloat162float(__ushort_as_bfloat16(v16));
         const int k = any_order ? (j & 3) : 0;
-        acc[k] = __dadd_rn(acc[k], __dmul_rn(v, (double)q[i + j]));
+        acc[k] = __dadd_rn(acc[k], __dmul_rn(v, (double)qv[j]));
       }
     }
   } else {
-    const uint32_t* words = reinterpret_cast<const uint32_t*>(a.codes + row * (a.padded / 8));
+    const uint2* pairs = reinterpret_cast<const uint2*>(a.codes + row * (a.padded / 8));
     for (int wi = 0; wi < a.padded / 32; ++wi) {
-      const uint32_t word = words[wi];
-#pragma unroll 8
-      for (int j = 0; j < 32; ++j) {
-        // An unset bit adds +0, which leaves the sum unchanged (it is never
-        // -0: it starts at +0).
-        const double t = ((word >> j) & 1u) ? (double)q[wi * 32 + j] : 0.0;
-        const int k = any_order ? (j & 3) : 0;
-        acc[k] = __dadd_rn(acc[k], t);
+      const uint2 pw = pairs[wi >> 1];
+      const uint32_t word = (wi & 1) ? pw.y : pw.x;
+#pragma unroll
+      for (int g = 0; g < 8; ++g) {
+        const float4 v = __ldg(q4 + wi * 8 + g);
+        const float qv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int j = g * 4 + u;
+          // An unset bit adds +0, which leaves the sum unchanged (it is
+          // never -0: it starts at +0).
+          const double t = ((word >> j) & 1u) ? (double)qv[u] : 0.0;
+          const int k = any_order ? u : 0;
+          acc[k] = __dadd_rn(acc[k], t);
+        }
       }
     }
   }
@@ -965,14 +988,24 @@ __device__ void warp_sort_keys(uint64_t* a, int m) {
     }
 }
 
+constexpr int kWalkStage = 96;  // uint64 slots per warp for the staged neighbour values
+
 __global__ void __launch_bounds__(256) hnsw_rabitq_walk_kernel(WalkArgs a) {
   extern __shared__ __align__(16) unsigned char walk_smem[];
   const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5, wpb = blockDim.x >> 5;
   // Per warp: frontier [fcap], accepted [pow2 >= capacity].
   int acap2 = 1;
   while (acap2 < a.capacity + 1) acap2 <<= 1;
-  uint64_t* frontier = reinterpret_cast<uint64_t*>(walk_smem) + (size_t)wib * (a.fcap + acap2);
+  uint64_t* frontier =
+      reinterpret_cast<uint64_t*>(walk_smem) + (size_t)wib * (a.fcap + acap2 + kWalkStage);
   uint64_t* accepted = frontier + a.fcap;
+  // A neighbour list's values for lane 0's decisions (lane j's in slot j).
+  uint32_t* st_kr = reinterpret_cast<uint32_t*>(accepted + acap2);
+  float* st_l = reinterpret_cast<float*>(st_kr + 32);
+  float* st_f = st_l + 32;
+  int* st_c1 = reinterpret_cast<int*>(st_f + 32);
+  int* st_c2 = st_c1 + 32;
+  int* st_acc = st_c2 + 32;
   const int slot = blockIdx.x * wpb + wib, slots = gridDim.x * wpb;
   uint32_t* vis = a.visited + (int64_t)slot * a.words;
   int32_t* vl = a.vlist + (int64_t)slot * a.vcap;
@@ -1082,60 +1115,55 @@ __global__ void __launch_bounds__(256) hnsw_rabitq_walk_kernel(WalkArgs a) {
           }
         }
         __syncwarp();
-        // The reference's decisions, in list order (lane 0 holds the heaps).
-        for (unsigned m = fm; m; m &= m - 1) {
-          const int j = __ffs(m) - 1;
-          const int64_t p = __shfl_sync(kFullMask, nb, j);
-          const float lj = __shfl_sync(kFullMask, cl, j);
-          const float fj = __shfl_sync(kFullMask, fd, j);
-          const int c1 = __shfl_sync(kFullMask, cst, j);
-          const int c2 = __shfl_sync(kFullMask, fst, j);
-          if (c1) {
-            fail = c1;
-            break;
-          }
-          int verdict = 0;  // 0 pruned / skipped, 1 continue, -1 failed
-          if (lane == 0) {
+        // The reference's decisions, in list order, by lane 0 (which holds
+        // the heaps) from the values each lane staged for its neighbour.
+        if (fresh) {
+          st_kr[lane] = a.keyrank[nb];
+          st_l[lane] = cl;
+          st_f[lane] = fd;
+          st_c1[lane] = cst;
+          st_c2[lane] = fst;
+          st_acc[lane] = accept(nb, fd) ? 1 : 0;
+        }
+        __syncwarp();
+        int lfail = 0;
+        if (lane == 0) {
+          for (unsigned m = fm; m; m &= m - 1) {
+            const int j = __ffs(m) - 1;
+            if (st_c1[j]) {
+              lfail = st_c1[j];
+              break;
+            }
             const bool full_set = asize >= a.capacity && asize > 0;
-            if (full_set && lj >= rank_of(accepted[0])) {
-              verdict = 0;
-            } else if (c2) {
-              verdict = -1;
-            } else {
-              verdict = 1;
-              const uint64_t v = walk_key(fj, a.keyrank[p]);
-              if (asize < a.capacity || asize == 0 || v < accepted[0]) {
-                if (fsize == a.fcap && asize >= a.capacity && asize > 0) {
-                  // Frontier entries worse than the worst accepted node only
-                  // end the walk when popped: drop them.
-                  int keep = 0;
-                  for (int i = 0; i < fsize; ++i)
-                    if (frontier[i] < accepted[0]) frontier[keep++] = frontier[i];
-                  fsize = keep;
-                  heap_build<true>(frontier, fsize);
-                }
-                if (fsize == a.fcap) {
-                  verdict = -2;
-                } else {
-                  heap_push<true>(frontier, fsize, v);
-                  if (accept(p, fj)) {
-                    heap_push<false>(accepted, asize, v);
-                    if (asize > a.capacity) heap_pop<false>(accepted, asize);
-                  }
-                }
+            if (full_set && st_l[j] >= rank_of(accepted[0])) continue;  // pruned
+            if (st_c2[j]) {
+              lfail = st_c2[j];
+              break;
+            }
+            const uint64_t v = walk_key(st_f[j], st_kr[j]);
+            if (asize < a.capacity || asize == 0 || v < accepted[0]) {
+              if (fsize == a.fcap && asize >= a.capacity && asize > 0) {
+                // Frontier entries worse than the worst accepted node only
+                // end the walk when popped: drop them.
+                int keep = 0;
+                for (int i = 0; i < fsize; ++i)
+                  if (frontier[i] < accepted[0]) frontier[keep++] = frontier[i];
+                fsize = keep;
+                heap_build<true>(frontier, fsize);
+              }
+              if (fsize == a.fcap) {
+                lfail = kRaBitQGraphFull;
+                break;
+              }
+              heap_push<true>(frontier, fsize, v);
+              if (st_acc[j]) {
+                heap_push<false>(accepted, asize, v);
+                if (asize > a.capacity) heap_pop<false>(accepted, asize);
               }
             }
           }
-          verdict = __shfl_sync(kFullMask, verdict, 0);
-          if (verdict == -1) {
-            fail = c2;
-            break;
-          }
-          if (verdict == -2) {
-            fail = kRaBitQGraphFull;
-            break;
-          }
         }
+        fail = __shfl_sync(kFullMask, lfail, 0);
         fsize = __shfl_sync(kFullMask, fsize, 0);
         asize = __shfl_sync(kFullMask, asize, 0);
         __syncwarp();
@@ -1233,7 +1261,7 @@ xvec_gpu_status rabitq_graph_walk(xvec_gpu_index* idx, int nq, int k, int ef, in
   // `warps` warps per block and a frontier of fcap entries per warp; the
   // blocks fill the SMs (several per SM when the frontier is small).
   auto launch = [&](int count, const int* qids, int warps, int fcap) -> xvec_gpu_status {
-    const size_t smem = (size_t)warps * (fcap + acap2) * 8;
+    const size_t smem = (size_t)warps * (fcap + acap2 + kWalkStage) * 8;
     XVEC_CUDA(cudaFuncSetAttribute(hnsw_rabitq_walk_kernel,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     int per_sm = 0;
@@ -1262,7 +1290,7 @@ xvec_gpu_status rabitq_graph_walk(xvec_gpu_index* idx, int nq, int k, int ef, in
   };
   // The large frontier: 200 KB of shared memory per SM.
   const int big_warps = capacity <= 256 ? 8 : capacity <= 1024 ? 4 : 2;
-  const int big_fcap = (200 * 1024 / 8) / big_warps - acap2;
+  const int big_fcap = (200 * 1024 / 8) / big_warps - acap2 - kWalkStage;
   if (big_fcap < 2 * capacity)
     return set_error("HNSW-RaBitQ walk: capacity %d is beyond the supported maximum", capacity),
            XVEC_GPU_INVALID_ARGUMENT;
@@ -1271,9 +1299,11 @@ xvec_gpu_status rabitq_graph_walk(xvec_gpu_index* idx, int nq, int k, int ef, in
   // the large one (a walk's result does not depend on the buffer it used).
   const int small_fcap = std::max(1024, 4 * capacity);
   int small_warps = 8;
-  while (small_warps > 1 && (size_t)small_warps * (small_fcap + acap2) * 8 > 72 * 1024)
+  while (small_warps > 1 &&
+         (size_t)small_warps * (small_fcap + acap2 + kWalkStage) * 8 > 75 * 1024)
     small_warps >>= 1;
-  const bool small_fits = (size_t)small_warps * (small_fcap + acap2) * 8 <= 72 * 1024;
+  const bool small_fits =
+      (size_t)small_warps * (small_fcap + acap2 + kWalkStage) * 8 <= 75 * 1024;
   if (!small_fits || small_fcap >= big_fcap || nq == 0)
     return launch(nq, nullptr, big_warps, big_fcap);
   xvec_gpu_status st = launch(nq, nullptr, small_warps, small_fcap);
