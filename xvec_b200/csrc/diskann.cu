@@ -286,11 +286,17 @@ __global__ void __launch_bounds__(kDiskThreads, 3) diskann_search_kernel(DiskArg
   extern __shared__ __align__(16) unsigned char smem[];
   const DiskSmem L(capA, a.k, SMEM_TABLE ? a.chunks * 256 : 0);
   float* T = reinterpret_cast<float*>(smem + L.tbl);
-  uint64_t* R[2] = {reinterpret_cast<uint64_t*>(smem + L.r0),
-                    reinterpret_cast<uint64_t*>(smem + L.r1)};
-  uint8_t* E[2] = {smem + L.e0, smem + L.e1};
-  uint64_t* K[2] = {reinterpret_cast<uint64_t*>(smem + L.k0),
-                    reinterpret_cast<uint64_t*>(smem + L.k1)};
+  // The double buffers chosen by a select, not an indexed array (which
+  // would live in local memory).
+  uint64_t* const R0 = reinterpret_cast<uint64_t*>(smem + L.r0);
+  uint64_t* const R1 = reinterpret_cast<uint64_t*>(smem + L.r1);
+  uint8_t* const E0 = smem + L.e0;
+  uint8_t* const E1 = smem + L.e1;
+  uint64_t* const K0 = reinterpret_cast<uint64_t*>(smem + L.k0);
+  uint64_t* const K1 = reinterpret_cast<uint64_t*>(smem + L.k1);
+  auto R = [&](int c) { return c ? R1 : R0; };
+  auto E = [&](int c) { return c ? E1 : E0; };
+  auto K = [&](int c) { return c ? K1 : K0; };
   uint64_t* X = reinterpret_cast<uint64_t*>(smem + L.x);
   uint64_t* X2 = reinterpret_cast<uint64_t*>(smem + L.x2);
   int* HIST = reinterpret_cast<int*>(smem + L.hist);
@@ -367,8 +373,8 @@ __global__ void __launch_bounds__(kDiskThreads, 3) diskann_search_kernel(DiskArg
                (double)__uint_as_float(s_maxabs) * (double)a.chunks < 1e38;
       float es = 0.f;
       s_status = disk_pq_score(a, table, qn, entry, &es);
-      R[0][0] = disk_node_key(a.traversal, es, entry);
-      E[0][0] = 0;
+      R(0)[0] = disk_node_key(a.traversal, es, entry);
+      E(0)[0] = 0;
       s_r = 1;
       s_cur = 0;
       s_kc = 0;
@@ -389,13 +395,13 @@ __global__ void __launch_bounds__(kDiskThreads, 3) diskann_search_kernel(DiskArg
       const int per = (r + kDiskThreads - 1) / kDiskThreads;
       const int i0 = min(r, tid * per), i1 = min(r, i0 + per);
       int cnt = 0;
-      for (int i = i0; i < i1; ++i) cnt += E[cur][i] == 0;
+      for (int i = i0; i < i1; ++i) cnt += E(cur)[i] == 0;
       int total;
       int idx = block_exclusive_sum(cnt, &total);
       for (int i = i0; i < i1 && idx < a.beam; ++i)
-        if (E[cur][i] == 0) {
-          BID[idx++] = (uint32_t)R[cur][i];
-          E[cur][i] = 1;
+        if (E(cur)[i] == 0) {
+          BID[idx++] = (uint32_t)R(cur)[i];
+          E(cur)[i] = 1;
         }
       const int nb = min(total, a.beam);
       if (nb == 0) break;
@@ -551,7 +557,7 @@ __global__ void __launch_bounds__(kDiskThreads, 3) diskann_search_kernel(DiskArg
         }
         __syncthreads();
         const int rr = s_r, rc = s_cur, wc = s_wc;
-        const uint64_t worst = rr >= a.cap ? R[rc][rr - 1] : kEmptyKey;
+        const uint64_t worst = rr >= a.cap ? R(rc)[rr - 1] : kEmptyKey;
         // PQ scores of the claimed nodes; those that beat a full retained
         // set's worst join the step's candidates.  Codes of 16 or 32 bytes:
         // two items per thread at a time, their code loads issued together.
@@ -663,7 +669,7 @@ __global__ void __launch_bounds__(kDiskThreads, 3) diskann_search_kernel(DiskArg
           }
           __syncthreads();
           const int rn = min(a.cap, rr + xc);
-          merge_runs(R[rc], E[rc], rr, xs, xc, R[1 - rc], E[1 - rc], rn);
+          merge_runs(R(rc), E(rc), rr, xs, xc, R(1 - rc), E(1 - rc), rn);
           __syncthreads();
           if (tid == 0) {
             s_r = rn;
@@ -684,7 +690,7 @@ __global__ void __launch_bounds__(kDiskThreads, 3) diskann_search_kernel(DiskArg
       const int kc = s_kc, kcur = s_kcur;
       if (valid > 0) {
         const int kn = min(a.k, kc + valid);
-        merge_runs(K[kcur], nullptr, kc, BK2, valid, K[1 - kcur], nullptr, kn);
+        merge_runs(K(kcur), nullptr, kc, BK2, valid, K(1 - kcur), nullptr, kn);
         __syncthreads();
         if (tid == 0) {
           s_kc = kn;
@@ -702,7 +708,7 @@ __global__ void __launch_bounds__(kDiskThreads, 3) diskann_search_kernel(DiskArg
       if (tid == 0) a.out_counts[q] = -s_status;
     } else {
       const int kc = s_kc;
-      const uint64_t* kk = K[s_kcur];
+      const uint64_t* kk = K(s_kcur);
       for (int i = warp; i < kc; i += kDiskWarps) {
         const uint32_t pos = a.pos_of_kr[(uint32_t)kk[i]];
         const float sc = warp_reference_score<float>(a.metric, a.rows + (int64_t)pos * a.d, qv, a.d);

@@ -815,26 +815,20 @@ __device__ int walk_estimate(const WalkArgs& a, int qi, int64_t row, bool full, 
   return walk_finish(a, qi, row, multi, dot, dist, lower);
 }
 
-// One lane's estimate of `row` (the other lanes take other rows): the dot
-// in index order (any order when the query's sums are exact), then
-// walk_finish.
-__device__ int walk_estimate_lane(const WalkArgs& a, int qi, int64_t row, bool full, float* dist,
-                                  float* lower) {
-  const float* q = a.q_rot + (int64_t)qi * a.padded;
-  const bool multi = full && a.total_bits > 1, half = a.total_bits > 8;
-  const bool any_order = a.q_exact[qi] != 0;
-  double acc[4] = {0.0, 0.0, 0.0, 0.0};
-  // The row's lines are requested up front (each lane reads its own row, so
-  // the loads below would otherwise wait on L2 one after another).
-  {
-    const char* rb = multi ? reinterpret_cast<const char*>(a.values + row * a.padded)
-                           : reinterpret_cast<const char*>(a.codes + row * (a.padded / 8));
-    const int bytes = multi ? a.padded * 2 : a.padded / 8;
-    const uintptr_t first = reinterpret_cast<uintptr_t>(rb) & ~(uintptr_t)127;
-    for (uintptr_t l = first; l < reinterpret_cast<uintptr_t>(rb) + bytes; l += 128)
-      asm volatile("prefetch.global.L1 [%0];" ::"l"(l));
-    asm volatile("prefetch.global.L1 [%0];" ::"l"(a.factors + row));
-  }
+// One lane's dot of `row` with the query (the other lanes take other rows):
+// the float64 sum in index order, or (ANY_ORDER: the query's sums are exact)
+// in four interleaved parts.  ANY_ORDER is a template parameter so that the
+// four parts stay in registers.
+template <bool ANY_ORDER>
+__device__ __noinline__ double walk_dot_lane(const WalkArgs& a, const float* q, int64_t row, bool multi,
+                                bool half) {
+  double acc0 = 0.0, acc1 = 0.0, acc2 = 0.0, acc3 = 0.0;
+  auto add = [&](int part, double t) {
+    if (!ANY_ORDER || part == 0) acc0 = __dadd_rn(acc0, t);
+    else if (part == 1) acc1 = __dadd_rn(acc1, t);
+    else if (part == 2) acc2 = __dadd_rn(acc2, t);
+    else acc3 = __dadd_rn(acc3, t);
+  };
   // The query is read four floats at a time (every lane reads the same
   // address: one broadcast per warp).
   const float4* q4 = reinterpret_cast<const float4*>(q);
@@ -850,8 +844,7 @@ __device__ int walk_estimate_lane(const WalkArgs& a, int qi, int64_t row, bool f
         const uint16_t v16 = (uint16_t)(w[j >> 1] >> (16 * (j & 1)));
         const double v = half ? (double)__half2float(__ushort_as_half(v16))
                               : (double)__bfloat162float(__ushort_as_bfloat16(v16));
-        const int k = any_order ? (j & 3) : 0;
-        acc[k] = __dadd_rn(acc[k], __dmul_rn(v, (double)qv[j]));
+        add(j & 3, __dmul_rn(v, (double)qv[j]));
       }
     }
   } else {
@@ -865,18 +858,34 @@ __device__ int walk_estimate_lane(const WalkArgs& a, int qi, int64_t row, bool f
         const float qv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          const int j = g * 4 + u;
           // An unset bit adds +0, which leaves the sum unchanged (it is
           // never -0: it starts at +0).
-          const double t = ((word >> j) & 1u) ? (double)qv[u] : 0.0;
-          const int k = any_order ? u : 0;
-          acc[k] = __dadd_rn(acc[k], t);
+          add(u, ((word >> (g * 4 + u)) & 1u) ? (double)qv[u] : 0.0);
         }
       }
     }
   }
-  const double dot = any_order ? __dadd_rn(__dadd_rn(acc[0], acc[1]), __dadd_rn(acc[2], acc[3]))
-                               : acc[0];
+  return ANY_ORDER ? __dadd_rn(__dadd_rn(acc0, acc1), __dadd_rn(acc2, acc3)) : acc0;
+}
+
+// One lane's estimate of `row`: the dot (walk_dot_lane), then walk_finish.
+__device__ int walk_estimate_lane(const WalkArgs& a, int qi, int64_t row, bool full, float* dist,
+                                  float* lower) {
+  const float* q = a.q_rot + (int64_t)qi * a.padded;
+  const bool multi = full && a.total_bits > 1, half = a.total_bits > 8;
+  // The row's lines are requested up front (each lane reads its own row, so
+  // the loads below would otherwise wait on L2 one after another).
+  {
+    const char* rb = multi ? reinterpret_cast<const char*>(a.values + row * a.padded)
+                           : reinterpret_cast<const char*>(a.codes + row * (a.padded / 8));
+    const int bytes = multi ? a.padded * 2 : a.padded / 8;
+    const uintptr_t first = reinterpret_cast<uintptr_t>(rb) & ~(uintptr_t)127;
+    for (uintptr_t l = first; l < reinterpret_cast<uintptr_t>(rb) + bytes; l += 128)
+      asm volatile("prefetch.global.L1 [%0];" ::"l"(l));
+    asm volatile("prefetch.global.L1 [%0];" ::"l"(a.factors + row));
+  }
+  const double dot = a.q_exact[qi] ? walk_dot_lane<true>(a, q, row, multi, half)
+                                   : walk_dot_lane<false>(a, q, row, multi, half);
   return walk_finish(a, qi, row, multi, dot, dist, lower);
 }
 
@@ -1379,15 +1388,19 @@ __global__ void __launch_bounds__(kLutThreads, 1) rabitq_lut_scan_kernel(
   const int bytes = padded / 8, words8 = bytes / 8;  // 8-byte words per row
   const float* qr = q_rot + (int64_t)q * padded;
   // Table: thread pos < 128 fills column col(pos) for every byte value b,
-  // entry b = entry (b with its lowest set bit cleared) + that bit's value.
+  // entry b = entry (b without its highest set bit) + that bit's value.
   if (tid < kLutMaxBytes) {
     const int pos = tid, col = (pos & 3) * 32 + (pos >> 2);
     float v[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) v[i] = pos < bytes ? qr[pos * 8 + i] : 0.f;
+    // Entry 2^i + j is entry j plus bit i's value (i unrolled, so v stays in
+    // registers).
     lut[col] = 0.f;
-    for (int b = 1; b < 256; ++b)
-      lut[b * kLutMaxBytes + col] = lut[(b & (b - 1)) * kLutMaxBytes + col] + v[__ffs(b) - 1];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      for (int j = 0; j < (1 << i); ++j)
+        lut[((1 << i) + j) * kLutMaxBytes + col] = lut[j * kLutMaxBytes + col] + v[i];
   }
   // Zero padding of the staged rows (bytes past padded/8, never overwritten).
   for (int i = tid; i < kLutRows * 32; i += kLutThreads)
