@@ -160,7 +160,8 @@ int choose_kp(int k) {
 // ---------------------------------------------------------------------------
 xvec_gpu_status tc_seeded_scan(int device, int nq, int64_t n, int kp, cudaStream_t s,
                                const TcScanLaunch& scan, Scratch& pkeys, Scratch& pcounts,
-                               Scratch& psat, int* lists_out, Scratch* gthr_out) {
+                               Scratch& psat, int* lists_out, Scratch* gthr_out,
+                               const TcPreseed& preseed) {
   // Parts: pick the row split whose CTA count best fills whole waves of
   // one CTA per SM, keeping at least 16 tiles of 256 rows per part.
   int sms = 148;
@@ -219,6 +220,10 @@ xvec_gpu_status tc_seeded_scan(int device, int nq, int64_t n, int kp, cudaStream
       (st = psat.alloc((size_t)nq * lists * 8, s)) || (st = gthr.alloc((size_t)nq * 8, s)))
     return st;
   XVEC_CUDA(cudaMemsetAsync(gthr.ptr, 0xff, (size_t)nq * 8, s));
+  if (preseed && !ends.empty()) {
+    XVEC_CUDA(preseed(gthr.as<unsigned long long>()));
+    count_launches(2);
+  }
   prev = 0;
   int list0 = 0;
   for (size_t i = 0; i < ends.size(); ++i) {
@@ -343,7 +348,7 @@ xvec_gpu_status flat_search_impl(xvec_gpu_index* idx, const void* d_q, int nq,
     const float* row_aux =
         metric == XVEC_METRIC_COSINE ? idx->row_inv.as<float>() : idx->row_n2.as<float>();
     const __half* hrows = reinterpret_cast<const __half*>(rows);
-    Scratch pkeys, pcounts, psat, gthr_keep;
+    Scratch pkeys, pcounts, psat, gthr_keep, seed_ranks;
     int lists = 0;
     timer.mark(1);
     st = tc_seeded_scan(idx->device, nq, n, kp, s,
@@ -366,7 +371,17 @@ xvec_gpu_status flat_search_impl(xvec_gpu_index* idx, const void* d_q, int nq,
                               d_bitmap ? d_bitmap + b / 32 : nullptr, p, kp, list0, nlists, cand,
                               counts, sat, qflags.as<int>(), kstatus.as<int>(), s);
                         },
-                        pkeys, pcounts, psat, &lists, &gthr_keep);
+                        pkeys, pcounts, psat, &lists, &gthr_keep,
+                        [&](unsigned long long* gthr) -> cudaError_t {
+                          const int samples = flat_sample_seed_rows(n, kp);
+                          if (samples == 0) return cudaSuccess;
+                          if (seed_ranks.alloc((size_t)nq * samples * 4, s) != XVEC_GPU_OK)
+                            return cudaErrorMemoryAllocation;
+                          return launch_flat_sample_seed<RowT>(
+                              rows, n, d, idx->row_n2.as<float>(), d_bitmap, qf.as<float>(),
+                              qn2.as<float>(), nq, metric, kp, idx->max_n2.as<unsigned>(),
+                              kSplit ? 1 : 0, samples, seed_ranks.as<uint32_t>(), gthr, s);
+                        });
     if (st) return st;
     timer.mark(2);
     XVEC_LAUNCHED();

@@ -122,9 +122,14 @@ using TcScanLaunch = std::function<cudaError_t(int64_t b, int64_t e, int parts, 
 // (each followed by a threshold seeding) and one launch over the rest;
 // allocates the lists and reports their number per query.  gthr_out
 // (optional) keeps the per-query shared thresholds for the merge's filter.
+// preseed (optional): lowers the fresh thresholds before the first launch
+// (flat_kernels.cuh, launch_flat_sample_seed); it runs only when the scan
+// has seeding launches, whose lists would otherwise start empty.
+using TcPreseed = std::function<cudaError_t(unsigned long long* gthr)>;
 xvec_gpu_status tc_seeded_scan(int device, int nq, int64_t n, int kp, cudaStream_t s,
                                const TcScanLaunch& scan, Scratch& pkeys, Scratch& pcounts,
-                               Scratch& psat, int* lists_out, Scratch* gthr_out = nullptr);
+                               Scratch& psat, int* lists_out, Scratch* gthr_out = nullptr,
+                               const TcPreseed& preseed = TcPreseed());
 
 // Streaming Flat candidate scan for a few queries (flat_stream.cu): a sample
 // pass over every 64th row for the starting thresholds, the pass over all

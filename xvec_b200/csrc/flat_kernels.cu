@@ -16,6 +16,8 @@
 //      radius (query.go:193-201) and top-k.
 //   4. scan (exact) + merge in exact mode for the rare query whose candidate
 //      set cannot be proven complete, and for large k.
+#include <algorithm>
+
 #include "flat_kernels.cuh"
 #include "pipeline.cuh"
 
@@ -233,6 +235,196 @@ cudaError_t launch_seed_thresholds(const uint64_t* cand, const int* counts, int 
                                                     gthr);
   return cudaGetLastError();
 }
+
+// ---------------------------------------------------------------------------
+// Sample seeding of the tensor-core scan's shared thresholds.
+//
+// Before its first launch the scan's candidate lists have no threshold, so
+// each list accepts every row of its first tiles and then compacts them, a
+// cost per (query, list) that dominates a launch over few rows.  Instead,
+// for every query: the FP32 Flat fast ranks (fast_rank, the SIMT scan's) of
+// `samples` rows evenly spaced over the base, their kp-th best R, and the
+// bound t = R + eps_sample + eps_scan rounded up.  The kp sample rows ranked
+// at or below R have reference ranks within eps_sample of their sample ranks
+// (the fast_eps bound holds for any float32 accumulation order) and scan
+// ranks within eps_scan of their reference ranks, so at least kp rows have
+// scan keys at or below pack(t, max key rank): an upper bound on the query's
+// kp-th best scan key over all rows, which is all that the scan (a list
+// drops only keys above it) and the merge's coverage check ask of gthr.
+// Rows the filter excludes are not sampled.
+// ---------------------------------------------------------------------------
+constexpr int kSmpTile = 64;  // queries and sample rows per block
+constexpr int kSmpK = 32;     // dimensions per shared-memory chunk
+constexpr uint32_t kSmpNone = 0xffffffffu;
+
+// ranks[q][s]: the ordered fast rank of query q against sample row s
+// (kSmpNone: filtered out or not finite).  Block: a 64 x 64 tile, each
+// thread 4 queries x 4 sample rows accumulated with FFMA over 32-dimension
+// chunks staged in shared memory.
+template <typename RowT>
+__global__ void __launch_bounds__(256) sample_rank_kernel(
+    const RowT* __restrict__ rows, int64_t n, int d, const float* __restrict__ row_n2,
+    const uint32_t* __restrict__ bitmap, const float* __restrict__ qf,
+    const float* __restrict__ q_n2, int nq, int metric, int samples,
+    uint32_t* __restrict__ ranks) {
+  __shared__ __align__(16) float qs[kSmpK][kSmpTile + 4];
+  __shared__ __align__(16) float xs[kSmpK][kSmpTile + 4];
+  __shared__ int64_t srow[kSmpTile];
+  const int tid = threadIdx.x;
+  const int q0 = blockIdx.x * kSmpTile, s0 = blockIdx.y * kSmpTile;
+  if (tid < kSmpTile) srow[tid] = s0 + tid < samples ? (int64_t)(s0 + tid) * n / samples : -1;
+  __syncthreads();
+  const int tq = (tid >> 4) * 4, ts = (tid & 15) * 4;
+  const int kk = tid & 31, rr = tid >> 5;  // loader: dimension kk of tile rows rr + 8 i
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+  for (int k0 = 0; k0 < d; k0 += kSmpK) {
+    const int k = k0 + kk;
+#pragma unroll
+    for (int i = 0; i < kSmpTile / 8; ++i) {
+      const int r = rr + 8 * i;
+      const int q = q0 + r;
+      qs[kk][r] = (q < nq && k < d) ? qf[(int64_t)q * d + k] : 0.f;
+      const int64_t row = srow[r];
+      xs[kk][r] = (row >= 0 && k < d) ? load_elem(rows, row * d + k) : 0.f;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int c = 0; c < kSmpK; ++c) {
+      const float4 a = *reinterpret_cast<const float4*>(&qs[c][tq]);
+      const float4 b = *reinterpret_cast<const float4*>(&xs[c][ts]);
+      const float av[4] = {a.x, a.y, a.z, a.w};
+      const float bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int q = q0 + tq + i;
+    if (q >= nq) continue;
+    const float qn2 = q_n2[q];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int s = s0 + ts + j;
+      if (s >= samples) continue;
+      const int64_t row = srow[ts + j];
+      uint32_t o = kSmpNone;
+      if (bitmap_pass(bitmap, row)) {
+        const float r = fast_rank(metric, acc[i][j], row_n2[row], qn2);
+        if (finite_f(r)) o = float_to_ordered(r);
+      }
+      ranks[(int64_t)q * samples + s] = o;
+    }
+  }
+}
+
+// One warp per query: the kp-th smallest of its sample ranks (a radix
+// select over the 32-bit ordered ranks, 8 bits per pass), then gthr[q] =
+// min(gthr[q], pack(t, max key rank)) with t the bound above.
+__global__ void __launch_bounds__(256) sample_seed_select_kernel(
+    const uint32_t* __restrict__ ranks, int nq, int samples, int kp, int metric, int d,
+    const float* __restrict__ q_n2, const unsigned* __restrict__ max_n2, int split,
+    unsigned long long* __restrict__ gthr) {
+  __shared__ int hist_all[8][256];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int q = blockIdx.x * 8 + warp;
+  if (q >= nq) return;  // whole warps; nothing below synchronises the block
+  int* hist = hist_all[warp];
+  const uint32_t* v = ranks + (int64_t)q * samples;
+  int cnt = 0;
+  for (int i = lane; i < samples; i += 32) cnt += v[i] != kSmpNone;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(kFullMask, cnt, o);
+  if (cnt < kp) return;  // too few finite sample ranks: no seed
+  uint32_t prefix = 0;
+  int kth = kp;
+#pragma unroll 1
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int b = lane; b < 256; b += 32) hist[b] = 0;
+    __syncwarp();
+    const uint32_t mask = shift == 24 ? 0u : (~0u << (shift + 8));
+    for (int i = lane; i < samples; i += 32) {
+      const uint32_t x = v[i];
+      if ((x & mask) == prefix) atomicAdd(&hist[(x >> shift) & 0xff], 1);
+    }
+    __syncwarp();
+    // Lane l owns bins 8 l .. 8 l + 7: the bin where the running count
+    // reaches kth holds the next digit.
+    int local[8], sum = 0;
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+      local[b] = hist[lane * 8 + b];
+      sum += local[b];
+    }
+    int incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(kFullMask, incl, o);
+      if (lane >= o) incl += t;
+    }
+    const int excl = incl - sum;
+    const unsigned owner = __ballot_sync(kFullMask, excl < kth && kth <= incl);
+    const int src = __ffs(owner) - 1;
+    int digit = 0, rem = kth - excl;
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+      if (rem > 0 && rem <= local[b]) {
+        digit = lane * 8 + b;
+        rem = -rem;  // found: later bins leave it alone
+      } else if (rem > 0) {
+        rem -= local[b];
+      }
+    }
+    digit = __shfl_sync(kFullMask, digit, src);
+    kth = -__shfl_sync(kFullMask, rem, src);
+    prefix |= (uint32_t)digit << shift;
+    __syncwarp();
+  }
+  // prefix is the kp-th smallest rank; kp <= cnt finite ranks sort before
+  // every kSmpNone, so it is finite.
+  if (lane == 0) {
+    const float qn2 = q_n2[q], xn2 = ordered_to_float(*max_n2);
+    const float e = __fadd_ru(fast_eps(metric, d, qn2, xn2, 0), fast_eps(metric, d, qn2, xn2, split));
+    const float t = __fadd_ru(ordered_to_float(prefix), e);
+    if (finite_f(t)) atomicMin(&gthr[q], (unsigned long long)pack_rank(t, 0xffffffffu));
+  }
+}
+
+int flat_sample_seed_rows(int64_t n, int kp) {
+  const int s = std::min(2048, std::max(1024, 8 * kp));
+  return n >= 16 * (int64_t)s ? s : 0;
+}
+
+template <typename RowT>
+cudaError_t launch_flat_sample_seed(const RowT* rows, int64_t n, int d, const float* row_n2,
+                                    const uint32_t* bitmap, const float* qf, const float* q_n2,
+                                    int nq, int metric, int kp, const unsigned* max_n2, int split,
+                                    int samples, uint32_t* ranks, unsigned long long* gthr,
+                                    cudaStream_t stream) {
+  if (nq <= 0 || samples <= 0 || kp > samples) return cudaSuccess;
+  const dim3 grid((unsigned)((nq + kSmpTile - 1) / kSmpTile),
+                  (unsigned)((samples + kSmpTile - 1) / kSmpTile));
+  sample_rank_kernel<RowT><<<grid, 256, 0, stream>>>(rows, n, d, row_n2, bitmap, qf, q_n2, nq,
+                                                     metric, samples, ranks);
+  sample_seed_select_kernel<<<(unsigned)((nq + 7) / 8), 256, 0, stream>>>(
+      ranks, nq, samples, kp, metric, d, q_n2, max_n2, split, gthr);
+  return cudaGetLastError();
+}
+template cudaError_t launch_flat_sample_seed<float>(const float*, int64_t, int, const float*,
+                                                    const uint32_t*, const float*, const float*,
+                                                    int, int, int, const unsigned*, int, int,
+                                                    uint32_t*, unsigned long long*, cudaStream_t);
+template cudaError_t launch_flat_sample_seed<__half>(const __half*, int64_t, int, const float*,
+                                                     const uint32_t*, const float*, const float*,
+                                                     int, int, int, const unsigned*, int, int,
+                                                     uint32_t*, unsigned long long*, cudaStream_t);
 
 int simt_cap_for(int kp) {
   // CAP must hold KP retained entries plus two tiles of appends.

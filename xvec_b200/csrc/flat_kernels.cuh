@@ -30,6 +30,21 @@ cudaError_t launch_seed_thresholds(const uint64_t* cand, const int* counts, int 
                                    cudaStream_t stream);
 int exact_cap_for(int kp);
 
+// Sample seeding of the tensor-core scan's shared thresholds (before its
+// first launch): per query, the kp-th best FP32 fast rank over `samples` rows
+// evenly spaced over the base (filtered rows left out), plus the sample's and
+// the scan's error bounds (split: the scan ranks bfloat16 high/low parts),
+// lowers gthr[q] to a bound on its kp-th best scan key over all rows.
+// ranks: nq x samples uint32 of scratch.  flat_sample_seed_rows gives the
+// sample size for n rows and kp (0: the base is too small to seed this way).
+int flat_sample_seed_rows(int64_t n, int kp);
+template <typename RowT>
+cudaError_t launch_flat_sample_seed(const RowT* rows, int64_t n, int d, const float* row_n2,
+                                    const uint32_t* bitmap, const float* qf, const float* q_n2,
+                                    int nq, int metric, int kp, const unsigned* max_n2, int split,
+                                    int samples, uint32_t* ranks, unsigned long long* gthr,
+                                    cudaStream_t stream);
+
 template <typename RowT>
 cudaError_t launch_flat_scan_simt(const RowT* rows, int64_t n, int d, const float* row_n2,
                                   const uint32_t* keyrank, const float* qf, const float* q_n2,
