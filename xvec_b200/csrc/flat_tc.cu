@@ -301,6 +301,21 @@ __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// v[j] for a warp-uniform j: a tree of selects on the bits of j, so the
+// array stays in registers (a run-time index would move it to local memory).
+__device__ __forceinline__ uint32_t pick32(const uint32_t (&v)[32], int j) {
+  uint32_t a[16], b[8], c[4], d[2];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) a[i] = (j & 16) ? v[i + 16] : v[i];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) b[i] = (j & 8) ? a[i + 8] : a[i];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) c[i] = (j & 4) ? b[i + 4] : b[i];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) d[i] = (j & 2) ? c[i + 2] : c[i];
+  return (j & 1) ? d[1] : d[0];
+}
+
 // Fast rank from the tensor-core dot product.  aux: 1/||x|| (cosine) or
 // ||x||^2 (L2, MIPS); qa: 1/||q|| (cosine) or ||q||^2.
 template <int METRIC>
@@ -775,11 +790,11 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
         uint32_t(&nxt)[32] = (c & 1) ? va : vb;
         if (c + 1 < 4) tmem_ld32(taddr + (c + 1) * 32, nxt);
         const uint32_t vmask = qvalid ? vm[c] : 0u;
-        // Rare path: the exact fast rank and key of column j, appended when
-        // below the list threshold.
-        auto rare = [&](int j, float a) {
+        // Rare path: the exact fast rank and key of column j (its dot v),
+        // appended when below the list threshold.
+        auto rare_v = [&](int j, uint32_t v, float a) {
           const float ra = METRIC == kMetricL2 ? -2.f * a : a;
-          const float r = tc_rank<METRIC>(__uint_as_float(cur[j]), ra, qa, qn2);
+          const float r = tc_rank<METRIC>(__uint_as_float(v), ra, qa, qn2);
           if (!isfinite(r)) {
             nonfinite = 1;
           } else {
@@ -836,24 +851,29 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
               }
             }
           }
-        } else if (vmask == kFullMask) {
+        } else {
+          // Flat metrics: the chunk's pass mask without branches, then one
+          // loop over the columns that pass for some lane of the warp (few
+          // once the thresholds are set), each column's dot picked from the
+          // registers by its warp-uniform index.  The per-column test stays
+          // free of the append path's code, which keeps the unrolled loop
+          // small.
+          uint32_t pass = 0u;
 #pragma unroll
           for (int g = 0; g < 8; ++g) {
             const float4 av = a4[g];
             const float aa[4] = {av.x, av.y, av.z, av.w};
 #pragma unroll
             for (int e = 0; e < 4; ++e)
-              if (score(g * 4 + e, aa[e]) >= tq) rare(g * 4 + e, aa[e]);
+              if (score(g * 4 + e, aa[e]) >= tq) pass |= 1u << (g * 4 + e);
           }
-        } else if (vmask != 0u) {
-#pragma unroll
-          for (int g = 0; g < 8; ++g) {
-            const float4 av = a4[g];
-            const float aa[4] = {av.x, av.y, av.z, av.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-              if (((vmask >> (g * 4 + e)) & 1u) && score(g * 4 + e, aa[e]) >= tq)
-                rare(g * 4 + e, aa[e]);
+          pass &= vmask;
+          uint32_t any = __reduce_or_sync(kFullMask, pass);
+          while (any) {
+            const int j = __ffs(any) - 1;
+            any &= any - 1;
+            const uint32_t v = pick32(cur, j);
+            if ((pass >> j) & 1u) rare_v(j, v, meta_aux[c * 32 + j]);
           }
         }
         if (c + 1 < 4) tmem_wait_ld();
