@@ -752,6 +752,17 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
       const uint32_t taddr =
           tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * kBN + half * kHalfCols;
       uint32_t va[32], vb[32];
+      // Rare path of the quantized modes: the fast rank of column j of
+      // chunk c, appended when below the list threshold (a non-finite rank
+      // marks the query for the exact scan).
+      auto append = [&](int c, int j, float rank) {
+        if (!isfinite(rank)) {
+          nonfinite = 1;
+        } else {
+          const uint64_t key = pack_rank(rank, meta_kr[c * 32 + j]);
+          if (key < thr) gbuf[cnt++] = key;
+        }
+      };
       if constexpr (RQ8) {
         // The 64 columns of this warp: A_h (va) and A_l (vb, BN columns on)
         // of 32 rows at a time.
@@ -761,24 +772,29 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
           tmem_ld32(taddr + BN + c * 32, vb);
           tmem_wait_ld();
           const uint32_t vmask = qvalid ? vm[c] : 0u;
+          auto rq8_rank = [&](int j, uint32_t h, uint32_t l) -> float {
+            const float4 r = meta4[c * 32 + j];
+            const float g = gadd_tab[__float_as_int(r.z) * 32 + lane];
+            // sum(v' w) + 128 sum(v') of this row; the query's 128 sum(w)
+            // is folded into rq_q.x.
+            const float dp = fmaf(256.f, (float)(int)h, (float)(int)l) + r.w;
+            return fmaf(r.y, fmaf(rq_q.y, dp, -rq_q.x), r.x + g);
+          };
+          // The pass mask, then the passing columns one at a time (as for
+          // the Flat metrics below).
+          uint32_t pass = 0u;
           if (vmask != 0u) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const float4 r = meta4[c * 32 + j];
-              const float g = gadd_tab[__float_as_int(r.z) * 32 + lane];
-              // sum(v' w) + 128 sum(v') of this row; the query's 128 sum(w)
-              // is folded into rq_q.x.
-              const float dp = fmaf(256.f, (float)(int)va[j], (float)(int)vb[j]) + r.w;
-              const float rank = fmaf(r.y, fmaf(rq_q.y, dp, -rq_q.x), r.x + g);
-              if (((vmask >> j) & 1u) && !(rank > thr_f)) {
-                if (!isfinite(rank)) {
-                  nonfinite = 1;
-                } else {
-                  const uint64_t key = pack_rank(rank, meta_kr[c * 32 + j]);
-                  if (key < thr) gbuf[cnt++] = key;
-                }
-              }
-            }
+            for (int j = 0; j < 32; ++j)
+              if (!(rq8_rank(j, va[j], vb[j]) > thr_f)) pass |= 1u << j;
+          }
+          pass &= vmask;
+          uint32_t any = __reduce_or_sync(kFullMask, pass);
+          while (any) {
+            const int j = __ffs(any) - 1;
+            any &= any - 1;
+            const uint32_t h = pick32(va, j), l = pick32(vb, j);
+            if ((pass >> j) & 1u) append(c, j, rq8_rank(j, h, l));
           }
         }
       } else {
@@ -813,42 +829,59 @@ __global__ void __launch_bounds__(kThreads, 1) flat_scan_tc_kernel(
         if constexpr (RQ) {
           // RaBitQRanker (rabitq.cu): add + gAdd[cluster] + rescale (dot - sum/2)
           // with dot = scale * the exact integer dot.
+          auto rq_rank = [&](int j, uint32_t v) -> float {
+            const float4 r = meta4[c * 32 + j];
+            const float g = gadd_tab[__float_as_int(r.z) * 32 + lane];
+            const float dot = (float)(int)v * rq_q.y;
+            return fmaf(r.y, dot - rq_q.x, r.x + g);
+          };
+          uint32_t pass = 0u;
           if (vmask != 0u) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const float4 r = meta4[c * 32 + j];
-              const float g = gadd_tab[__float_as_int(r.z) * 32 + lane];
-              const float dot = (float)(int)cur[j] * rq_q.y;
-              const float rank = fmaf(r.y, dot - rq_q.x, r.x + g);
-              if (((vmask >> j) & 1u) && !(rank > thr_f)) {
-                if (!isfinite(rank)) {
-                  nonfinite = 1;
-                } else {
-                  const uint64_t key = pack_rank(rank, meta_kr[c * 32 + j]);
-                  if (key < thr) gbuf[cnt++] = key;
-                }
-              }
-            }
+            for (int j = 0; j < 32; ++j)
+              if (!(rq_rank(j, cur[j]) > thr_f)) pass |= 1u << j;
+          }
+          pass &= vmask;
+          uint32_t any = __reduce_or_sync(kFullMask, pass);
+          while (any) {
+            const int j = __ffs(any) - 1;
+            any &= any - 1;
+            const uint32_t v = pick32(cur, j);
+            if ((pass >> j) & 1u) append(c, j, rq_rank(j, v));
           }
         } else if constexpr (SQ) {
           // SQ8Ranker (sq8.cu) on the exact integer dot product.
-          if (vmask != 0u) {
+          auto sq_rank = [&](int j, uint32_t v) -> float {
+            const float4 r = meta4[c * 32 + j];
+            const float dot = (float)(int)v;
+            const float tt = fmaf(qinfo.x, dot, qinfo.y * r.z);
+            const float inner = fmaf(r.x, tt, r.y * qinfo.z);
+            return METRIC == kMetricIP ? -inner : (r.w + qinfo.w) - 2.f * inner;
+          };
+          if constexpr (METRIC == kMetricL2) {
+            // Per column: with the pass mask below, this mode's rank terms
+            // and the live chunk exceed the register budget and spill.
+            if (vmask != 0u) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const float4 r = meta4[c * 32 + j];
-              const float dot = (float)(int)cur[j];
-              const float tt = fmaf(qinfo.x, dot, qinfo.y * r.z);
-              const float inner = fmaf(r.x, tt, r.y * qinfo.z);
-              const float rank =
-                  METRIC == kMetricIP ? -inner : (r.w + qinfo.w) - 2.f * inner;
-              if (((vmask >> j) & 1u) && !(rank > thr_f)) {
-                if (!isfinite(rank)) {
-                  nonfinite = 1;
-                } else {
-                  const uint64_t key = pack_rank(rank, meta_kr[c * 32 + j]);
-                  if (key < thr) gbuf[cnt++] = key;
-                }
+              for (int j = 0; j < 32; ++j) {
+                const float rank = sq_rank(j, cur[j]);
+                if (((vmask >> j) & 1u) && !(rank > thr_f)) append(c, j, rank);
               }
+            }
+          } else {
+            uint32_t pass = 0u;
+            if (vmask != 0u) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (!(sq_rank(j, cur[j]) > thr_f)) pass |= 1u << j;
+            }
+            pass &= vmask;
+            uint32_t any = __reduce_or_sync(kFullMask, pass);
+            while (any) {
+              const int j = __ffs(any) - 1;
+              any &= any - 1;
+              const uint32_t v = pick32(cur, j);
+              if ((pass >> j) & 1u) append(c, j, sq_rank(j, v));
             }
           }
         } else {
