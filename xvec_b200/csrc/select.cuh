@@ -99,43 +99,4 @@ __device__ __forceinline__ void block_sort_u64_fit(uint64_t* a, int n) {
   block_sort_u64<N>(a, n);
 }
 
-// Block-wide radix select: the kth smallest (1-based) of the keys produced by
-// `get(i)` for i in [0, m).  Requires 1 <= kth <= m.  Uses 256 ints of shared
-// scratch `hist` and two shared ints.
-template <typename Get>
-__device__ uint64_t block_radix_select(Get get, int m, int kth, int* hist, uint64_t* prefix_out) {
-  __shared__ uint64_t s_prefix;
-  __shared__ int s_kth;
-  if (threadIdx.x == 0) {
-    s_prefix = 0;
-    s_kth = kth;
-  }
-  __syncthreads();
-#pragma unroll 1
-  for (int shift = 56; shift >= 0; shift -= 8) {
-    for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
-    __syncthreads();
-    const uint64_t prefix = s_prefix;
-    const uint64_t mask = (shift == 56) ? 0ull : (~0ull << (shift + 8));
-    for (int i = threadIdx.x; i < m; i += blockDim.x) {
-      const uint64_t key = get(i);
-      if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 0xff], 1);
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      int remaining = s_kth;
-      int digit = 0;
-      for (; digit < 256; ++digit) {
-        if (remaining <= hist[digit]) break;
-        remaining -= hist[digit];
-      }
-      s_kth = remaining;
-      s_prefix = prefix | ((uint64_t)digit << shift);
-    }
-    __syncthreads();
-  }
-  if (prefix_out) *prefix_out = s_prefix;
-  return s_prefix;
-}
-
 }  // namespace xvec
